@@ -1,0 +1,380 @@
+"""Benchmark: fused KL-GEMM distillation loss, forward + backward, loss-rows/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c2]
+
+One step = the full loss path over one batch of rows: valid-row count, pass 1
+(both views' logits over all vocab tiles with online max/sum-exp/KL), merge,
+finalize (loss), pass 2 (logit recompute -> dZ chunks -> dH and dW GEMMs).
+Workload at N=1 is the 16,384-row SmolLM2-135M training shape (H=576,
+V=49,152, bf16, block-32 mask with ratio U(0,1)); synthetic seeded inputs.
+At N>1 each rank runs its own 16,384 rows (weak scaling, row sharded): the
+valid count and loss are all-reduced and dW is all-reduced over NCCL.
+
+``value``  device-timed throughput with inputs resident (CUDA events per step,
+           L2 flushed between steps by writing a 256 MiB buffer), max over ranks.
+``e2e``    the same metric through the public autograd API with the step's
+           inputs copied host->device (pinned) and the loss read back each step.
+``--impl reference`` times the CPU restatement of the reference's loss (its
+           own op sequence in fp32 torch, all host threads) on a bounded row
+           sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CONFIGS = {
+    # name: rows, hidden, vocab, description
+    "c2": (16384, 576, 49152, "SmolLM2-135M training shape, [8,2048,576] per view, V=49152, bf16, "
+                              "block-32 mask ratio U(0,1)"),
+    "c5": (12288, 576, 49152, "ragged/edge: 12288 rows, ~25% valid, teacher x4, T=2, bf16"),
+    "c3": (65536, 2048, 49152, "SmolLM2-1.7B shape, [32,2048,2048] per view, V=49152, bf16"),
+}
+METRIC = "KL-GEMM fwd+bwd loss-rows/sec"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="time budget of the CPU baseline sample")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("bf16_tflops", 1590.0), d.get("bf16_tflops_sustained", 1400.0), "measured"
+    return 1590.0, 1400.0, "fallback"
+
+
+def load_traffic(kernel: str, config: str):
+    """Bytes per launch from a committed ncu summary (profiles/traffic.json), else None."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    try:
+        return json.loads(p.read_text()).get(config, {}).get(kernel)
+    except Exception:
+        return None
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons of one GPU while running."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 7:
+                self.rows.append(parts)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        if not self.rows:
+            return None
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[3 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def cpu_baseline(config: str, seconds: float):
+    """Reference loss (its op sequence, fp32 torch on the host cores) on a row sample."""
+    import torch
+    from oracle import klgemm_oracle as O
+
+    N, H, V, _ = CONFIGS[config]
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    sample = 256
+    p = O.make_problem(config, n_rows=sample, seed=7)
+    hs, ht, W, m, T = p["h_s"].float(), p["h_t"].float(), p["W"].float(), p["mask"], p["T"]
+    times = []
+    t_end = time.perf_counter() + seconds
+    while True:
+        t0 = time.perf_counter()
+        O.aligned_kl_torch_with_grads(hs, ht, W, m, T)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_end and len(times) >= 2:
+            break
+    t = statistics.median(times[1:]) if len(times) > 1 else times[0]
+    return {"value": sample / t, "unit": "rows/s", "cores": threads, "kind": "port",
+            "sample": f"{sample} of {N} rows x full V={V}, H={H}, fp32 torch (reference op sequence, "
+                      f"train.py:142-210) fwd+bwd incl. dW; median of {len(times) - 1} runs"}
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    N, H, V, desc = CONFIGS[args.config]
+    import torch
+    from oracle import klgemm_oracle as O
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    sample = 128
+    p = O.make_problem(args.config, n_rows=sample, seed=7)
+    hs, ht, W, m, T = p["h_s"].float(), p["h_t"].float(), p["W"].float(), p["mask"], p["T"]
+    for _ in range(max(1, args.warmup)):
+        O.aligned_kl_torch_with_grads(hs, ht, W, m, T)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        O.aligned_kl_torch_with_grads(hs, ht, W, m, T)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = sample * args.steps / total
+    line = {
+        "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded)",
+        "impl": "reference",
+        "config": {"workload": f"{args.config}: {desc}", "rows": N, "hidden": H, "vocab": V,
+                   "rows_per_step_sample": sample, "parallelism": "host CPU"},
+        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "port",
+                         "sample": f"{sample} of {N} rows per step, full V, fp32 fwd+bwd incl. dW"},
+        "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- our arm
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from oracle import klgemm_oracle as O  # input generator only (seeded workload shapes)
+    from orthrus_training_test_b200 import _lib, ops
+    from orthrus_training_test_b200.parallel import row_sharded_kl_loss
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        if world == 1 and args.gpus > 1:
+            raise SystemExit("--gpus N > 1 must be launched with torch.distributed.run (one process per GPU)")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    _lib.lib()
+
+    N, H, V, desc = CONFIGS[args.config]
+    p = O.make_problem(args.config, seed=42 + rank)       # this rank's rows
+    pw = O.make_problem(args.config, n_rows=1, seed=42)   # shared lm_head
+    T = p["T"]
+    hs = p["h_s"].to(dev)
+    ht = p["h_t"].to(dev)
+    W = pw["W"].to(dev)
+    m = ops.mask_u8(p["mask"].to(dev))
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def step():
+        cnt = ops.count_valid(m)
+        if world > 1:
+            dist.all_reduce(cnt)
+        loss, lse, _, _ = ops.kl_forward(hs, ht, W, m, T, count=cnt)
+        if world > 1:
+            dist.all_reduce(loss)
+        dh, dw = ops.kl_backward(hs, ht, W, m, lse, cnt, temperature=T)
+        if world > 1:
+            dist.all_reduce(dw)
+        return loss
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+
+    # ---------------------------------------------------------------- device-timed steps
+    sampler = ClockSampler(local) if rank == 0 else None
+    barrier()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    launches0 = _lib.launch_count()
+    _lib.trace_begin(8192)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush.zero_()                                  # evict inputs from L2 (outside the timed events)
+        ev[i][0].record()
+        step()
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    trace = _lib.trace_end(8192)
+    launches = _lib.launch_count() - launches0
+    clocks = sampler.stop() if sampler else None
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    total_ms = torch.tensor([sum(step_ms)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
+    total_ms = float(total_ms.item())
+    assert _lib.device_status() == 0
+
+    rows_total = N * world * args.steps
+    value = rows_total / (total_ms / 1e3)
+
+    # ---------------------------------------------------------------- per-kernel roofline
+    peak_burst, peak_sust, peak_src = load_peaks()
+    by_kind = {}
+    for kind, ms in trace:
+        t = by_kind.setdefault(kind, [0.0, 0])
+        t[0] += ms
+        t[1] += 1
+    flops_per_step = {"stats": 4.0 * N * H * V, "dz": 4.0 * N * H * V, "gemm_dh": 2.0 * N * H * V,
+                      "gemm_dw": 2.0 * N * H * V}
+    dom = max((k for k in by_kind if k in flops_per_step), key=lambda k: by_kind[k][0])
+    dom_ms, dom_n = by_kind[dom]
+    dom_flops_per_launch = flops_per_step[dom] * args.steps / dom_n
+    dom_avg_ms = dom_ms / dom_n
+    achieved = dom_flops_per_launch / (dom_avg_ms / 1e3) / 1e12
+    traffic = load_traffic(dom, args.config)
+    roofline = {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": peak_sust, "unit": "TFLOP/s",
+                "frac": achieved / peak_sust, "traffic": traffic,
+                "peak_kind": f"{peak_src} sustained bf16 (kernel timed inside back-to-back steps)",
+                "frac_of_burst_peak": achieved / peak_burst,
+                "algorithmic_flops_per_launch": dom_flops_per_launch}
+    step_flops = 8.0 * N * H * V
+    kernels = {k: {"launches": n, "total_ms": t, "share": t / sum(x[0] for x in by_kind.values())}
+               for k, (t, n) in sorted(by_kind.items(), key=lambda kv: -kv[1][0])}
+
+    # ---------------------------------------------------------------- end-to-end (public API)
+    e2e = None
+    if not args.no_e2e:
+        hs_h = p["h_s"].pin_memory()
+        ht_h = p["h_t"].pin_memory()
+        m_h = p["mask"].to(torch.uint8).pin_memory()
+        Wp = W.clone().requires_grad_(True)
+        h2d = hs_h.numel() * hs_h.element_size() + ht_h.numel() * ht_h.element_size() + m_h.numel()
+
+        def e2e_step():
+            hs_d = hs_h.to(dev, non_blocking=True).requires_grad_(True)
+            ht_d = ht_h.to(dev, non_blocking=True)
+            m_d = m_h.to(dev, non_blocking=True)
+            if world > 1:
+                loss = row_sharded_kl_loss(hs_d, ht_d, Wp, m_d, T)
+            else:
+                loss = ops.kl_gemm_loss(hs_d, ht_d, Wp, m_d, T)
+            loss.backward()
+            Wp.grad = None
+            return float(loss.item())                # device -> host read of the step's result
+
+        for _ in range(max(2, args.warmup // 2)):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e_ms = []
+        for _ in range(args.steps):
+            flush.zero_()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            e2e_step()
+            b.record()
+            torch.cuda.synchronize()
+            e_ms.append(a.elapsed_time(b))
+        et = torch.tensor([sum(e_ms)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(et, op=dist.ReduceOp.MAX)
+        e2e = {"value": rows_total / (float(et.item()) / 1e3), "unit": "rows/s", "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": 4, "ms_per_step": float(et.item()) / args.steps,
+               "api": "row_sharded_kl_loss" if world > 1 else "kl_gemm_loss (KLGemmFn autograd)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.config, args.cpu_seconds)
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) hidden, "
+            "N(0,0.02) lm_head)",
+            "config": {"workload": f"{args.config}: {desc}", "rows_per_gpu": N, "hidden": H, "vocab": V,
+                       "temperature": T, "parallelism": f"row-sharded dp{world}" if world > 1 else "single GPU",
+                       "l2": "flushed between steps (256 MiB write)"},
+            "tensor_peak_frac": {"algorithmic_flops_per_step": step_flops,
+                                 "achieved_tflops": step_flops / (total_ms / args.steps / 1e3) / 1e12,
+                                 "frac_of_sustained": step_flops / (total_ms / args.steps / 1e3) / 1e12 / peak_sust,
+                                 "frac_of_burst": step_flops / (total_ms / args.steps / 1e3) / 1e12 / peak_burst,
+                                 "note": "8*N*H*V per fwd+bwd; executed work is 12*N*H*V (logits recomputed)"},
+            "roofline": roofline,
+            "kernels": kernels,
+            "gpu_launches": int(launches),
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,142 @@
+/*
+ * klgemm.h -- C-ABI of the fused KL-GEMM distillation loss for B200 (sm_100a).
+ *
+ * Replaces the reference's loss path, which has no native FFI of its own:
+ * the Python entry point is compute_kl_loss (train.py:142-195), its compiled
+ * chunk body _kl_chunk_body (train.py:198-210), and the teacher-probability
+ * precompute it consumes (train.py:549-567).  The binding a Python caller
+ * uses (ctypes) is orthrus_training_test_b200/_lib.py; INTEGRATION.md shows
+ * how the reference's call site reaches it.
+ *
+ * Math (natural log, z = h W^T / T, W = lm_head weight [V, H]):
+ *   KL_i  = sum_v p_v (z_t - z_s) - lse(z_t) + lse(z_s),  p = softmax(z_t)
+ *   loss  = sum_i valid_i KL_i / count,   count = sum_i valid_i
+ *   dZ_s  = g * valid_i / count * (softmax(z_s) - p) / T
+ *   dH_s  = dZ_s W,   dW = dZ_s^T h_s   (teacher detached, as in train.py:183)
+ *
+ * Conventions
+ *   - Inputs h_s, h_t [N, H] and W [V, H] are bf16, row-major, 16-byte aligned,
+ *     H a multiple of 8.  (fp32 callers convert with klg_cast_f32_bf16.)
+ *   - mask [N] is uint8 (nonzero = row carries loss), the reference's
+ *     target != pad_token_id (train.py:163-164).
+ *   - Every pointer is device memory owned by the caller; the library holds no
+ *     device allocation across calls.  `stream` is a cudaStream_t; work is only
+ *     enqueued on it (no host synchronisation).
+ *   - Return value: KLG_OK or a KLG_ERR_* code; klg_last_error gives the text
+ *     (per host thread).  Device-side pipeline timeouts are reported through
+ *     klg_device_status.
+ */
+#ifndef KLGEMM_H_
+#define KLGEMM_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KLG_VERSION 100
+
+#define KLG_OK 0
+#define KLG_ERR_ARG 1        /* bad shape, null pointer, inconsistent sizes      */
+#define KLG_ERR_ALIGN 2      /* pointer / stride alignment                        */
+#define KLG_ERR_CUDA 3       /* CUDA runtime or driver error at launch            */
+#define KLG_ERR_WORKSPACE 4  /* workspace missing or too small                    */
+
+/* Library version (KLG_VERSION). */
+int klg_version(void);
+
+/* Copies the calling thread's last error message into buf. */
+int klg_last_error(char* buf, int len);
+
+/* Reads (and optionally clears) the device status word: 0 = no device-side
+ * error; otherwise bits of the pipeline waits that ran out of their time
+ * bound (the kernel then ended early).  Synchronises the device. */
+int klg_device_status(int* status, int reset);
+
+/* Number of kernels this library has launched in this process. */
+long long klg_launch_count(void);
+
+/* ---------------------------------------------------------------- forward
+ * Replaces: the teacher lm_head + softmax + entropy precompute
+ * (train.py:549-567 and train.py:188-191), the student lm_head + soft-target
+ * cross_entropy + masked sum (train.py:198-210) and the final division
+ * (train.py:195).  No [N, V] tensor is formed. */
+
+/* Number of vocab-range partial records klg_fwd_stats writes per row on the
+ * current device. */
+int klg_num_partials(int64_t n_rows, int64_t vocab, int* n_part);
+
+/* Pass 1: per row, online softmax statistics of both views over W's rows,
+ * written as n_part records partials[n_part][5][n_rows] =
+ * (m_s, S_s, m_t, S_t, A) in the log2 domain (u = z log2(e)):
+ * S = sum 2^(u - m), A = sum_v 2^(u_t - m_t) (u_t - u_s). */
+int klg_fwd_stats(const void* h_s, const void* h_t, const void* w, int64_t n_rows, int64_t hidden,
+                  int64_t vocab, float inv_temp, float* partials, int n_part, void* stream);
+
+/* Online-softmax merge of partial records [n_part][5][n_rows] -> stats [5][n_rows].
+ * Also merges records gathered from ranks holding different vocab shards. */
+int klg_merge_stats(const float* partials, int n_part, int64_t n_rows, float* stats, void* stream);
+
+/* count = sum(mask) as a float device scalar (train.py:165). */
+int klg_count_valid(const uint8_t* mask, int64_t n_rows, float* count, void* stream);
+
+/* loss = sum(mask * KL) / count (0 when count == 0, train.py:166-167 and 195);
+ * lse [2][n_rows] = log2-domain log-sum-exp of (student, teacher) for the
+ * backward; row_kl [n_rows] (nats, may be NULL). */
+int klg_finalize(const float* stats, const uint8_t* mask, int64_t n_rows, const float* count, float* loss,
+                 float* lse, float* row_kl, void* stream);
+
+/* Bytes of forward workspace klg_fwd needs. */
+int64_t klg_fwd_workspace_bytes(int64_t n_rows, int64_t vocab);
+
+/* Whole forward on one device: [count] -> stats -> merge -> finalize.
+ * count_given = 0: count is computed from mask into *count;
+ * count_given = 1: *count already holds the (e.g. all-reduced) normaliser. */
+int klg_fwd(const void* h_s, const void* h_t, const void* w, const uint8_t* mask, int64_t n_rows, int64_t hidden,
+            int64_t vocab, float inv_temp, int count_given, float* count, float* loss, float* lse, float* row_kl,
+            void* workspace, int64_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- backward
+ * Replaces: autograd of train.py:202-210 (which stores bf16 [chunk, V] logits)
+ * and, with the lm_head trainable, its weight gradient. */
+
+/* Recommended workspace bytes for klg_bwd (a [n_rows, C] bf16 dZ chunk). */
+int64_t klg_bwd_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t vocab);
+
+/* Vocab columns per backward chunk for a given workspace size (-1 if < 128). */
+int64_t klg_bwd_chunk_cols(int64_t n_rows, int64_t vocab, int64_t workspace_bytes);
+
+/* Pass 2: recomputes the logits chunk by chunk (never storing them) and
+ * writes d_h_s [n_rows, H] fp32 (overwritten) and d_w [V, H] fp32 (overwritten).
+ * grad = device scalar upstream gradient (NULL = 1).  Either output may be NULL
+ * to skip it (the reference's lm_head is frozen: model.py:323-324). */
+int klg_bwd(const void* h_s, const void* h_t, const void* w, const uint8_t* mask, const float* lse,
+            const float* count, const float* grad, int64_t n_rows, int64_t hidden, int64_t vocab, float inv_temp,
+            float* d_h_s, float* d_w, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* fp32 -> bf16 conversion (round to nearest even) for fp32 callers. */
+int klg_cast_f32_bf16(const float* in, void* out, int64_t n, void* stream);
+
+/* ---------------------------------------------------------------- timing
+ * Per-launch timing for benchmarks (the reference's counterpart is the manual
+ * synchronize + perf_counter breakdown of train.py:541-547 and 676-685).
+ * Between klg_trace_begin and klg_trace_end every kernel the library launches
+ * (up to `capacity`) is bracketed by two CUDA events on its stream;
+ * klg_trace_end waits for them and returns each launch's kind and duration. */
+#define KLG_KIND_STATS 1
+#define KLG_KIND_DZ 2
+#define KLG_KIND_GEMM_DH 3
+#define KLG_KIND_GEMM_DW 4
+#define KLG_KIND_MERGE 5
+#define KLG_KIND_FINALIZE 6
+#define KLG_KIND_COUNT 7
+#define KLG_KIND_CAST 8
+int klg_trace_begin(int capacity);
+int klg_trace_end(int* kinds, float* ms, int capacity, int* n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KLGEMM_H_ */

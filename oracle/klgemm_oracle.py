@@ -1,0 +1,423 @@
+"""Oracle: a CPU restatement of the reference's KL distillation loss.
+
+TEST INFRASTRUCTURE ONLY.  The product (``orthrus_training_test_b200``) never
+imports this module; ``tests/``, ``__graft_entry__.smoke()`` and the
+CPU-baseline leg of ``bench.py`` use it as the checker / CPU baseline.
+
+Parity pin: every function here is checked against golden vectors produced by
+running the reference's own ``train.compute_kl_loss`` (reference
+``train.py:142-195`` + ``train.py:198-210``) in the build container; the
+generator is ``tests/golden/make_golden.py`` and the check is
+``tests/test_oracle.py``.
+
+Reference algorithm (``train.py``):
+
+* ``_get_kl_indices`` (train.py:124-139): student rows are the diffusion
+  positions ``blk*K + k`` for ``k = 1..K-1`` (the anchor, offset 0, is
+  excluded); teacher offsets are ``0..K-2``.
+* ``compute_kl_loss`` (train.py:142-195): teacher row ``anchor + k - 1``
+  clamped to ``[0, L-1]`` (train.py:161); ``valid = target != pad``
+  (train.py:163-164); early return of ``0.0`` when no row is valid
+  (train.py:166-167); 2048-row chunks (train.py:170-173); teacher softmax and
+  entropy in fp32 under ``no_grad`` (train.py:188-191); result
+  ``sum(valid * KL) / sum(valid)`` (train.py:195).
+* ``_kl_chunk_body`` (train.py:198-210): student logits through the shared
+  ``lm_head``; soft-target ``cross_entropy`` against the teacher probabilities;
+  ``KL = CE - entropy``; masked sum.
+
+Temperature: the reference has none (T = 1).  For T != 1 both logit tensors
+are divided by T before the softmax, with no T^2 factor; at T = 1 this is the
+reference formula unchanged.
+
+Three restatements live here:
+
+``kl_loss_reference_ops``   torch fp32, the reference's own op sequence and
+                            signature (device agnostic; autograd for grads).
+``aligned_kl_loss_torch``   torch fp32, the same ops on pre-aligned rows
+                            ``(h_s, h_t, mask)`` -- the fused op's contract.
+``aligned_kl_loss_np``      float64 numpy with closed-form gradients, an
+                            independent derivation used to cross-check both.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import numpy as np
+
+CHUNK = 2048  # train.py:170
+
+
+# --------------------------------------------------------------------------
+# Row selection (reference train.py:124-139, train.py:160-164)
+# --------------------------------------------------------------------------
+
+def kl_indices(B: int, B_blocks: int, K: int):
+    """Restates ``_get_kl_indices`` (train.py:124-139) in numpy.
+
+    Returns ``(diff_pos [B, N], batch_idx [B, N], offsets [K-1])`` with
+    ``N = B_blocks * (K - 1)``.
+    """
+    N = B_blocks * (K - 1)
+    diff_pos = np.arange(B_blocks * K).reshape(B_blocks, K)[:, 1:].reshape(-1)
+    diff_pos = np.broadcast_to(diff_pos[None, :], (B, N)).copy()
+    batch_idx = np.broadcast_to(np.arange(B)[:, None], (B, N)).copy()
+    offsets = np.arange(0, K - 1)
+    return diff_pos, batch_idx, offsets
+
+
+def select_rows_np(diff_hidden, ar_hidden, anchor_positions, K, target_ids, pad_token_id):
+    """Gathers aligned student/teacher rows and the validity mask.
+
+    Restates train.py:156-164: ``ar_pos = clamp(anchor + offsets, 0, L-1)``,
+    ``tgt = target_ids[batch_idx, diff_pos]``, ``valid = tgt != pad``.
+    Returns ``(h_s [B*N, H], h_t [B*N, H], valid [B*N] bool, diff_pos, ar_pos)``.
+    """
+    B, B_blocks = anchor_positions.shape
+    L = ar_hidden.shape[1]
+    N = B_blocks * (K - 1)
+    diff_pos, batch_idx, offsets = kl_indices(B, B_blocks, K)
+    ar_pos = np.clip((anchor_positions[:, :, None] + offsets[None, None, :]).reshape(B, N), 0, L - 1)
+    tgt = target_ids[batch_idx, diff_pos]
+    valid = tgt != pad_token_id
+    h_s = diff_hidden[batch_idx, diff_pos].reshape(B * N, -1)
+    h_t = ar_hidden[batch_idx, ar_pos].reshape(B * N, -1)
+    return h_s, h_t, valid.reshape(-1), diff_pos, ar_pos
+
+
+# --------------------------------------------------------------------------
+# torch fp32 restatement of the reference op sequence
+# --------------------------------------------------------------------------
+
+def _torch():
+    import torch
+    return torch
+
+
+def fp32_strict():
+    """Context for an fp32 reference: TF32 off and "highest" matmul precision.
+
+    The reference module flips both on import (train.py:47-50); an fp32
+    oracle must undo that or it is not fp32.
+    """
+    torch = _torch()
+
+    class _Ctx:
+        def __enter__(self):
+            self.prev = (torch.backends.cuda.matmul.allow_tf32,
+                         torch.backends.cudnn.allow_tf32,
+                         torch.get_float32_matmul_precision())
+            torch.backends.cuda.matmul.allow_tf32 = False
+            torch.backends.cudnn.allow_tf32 = False
+            torch.set_float32_matmul_precision("highest")
+            return self
+
+        def __exit__(self, *exc):
+            torch.backends.cuda.matmul.allow_tf32 = self.prev[0]
+            torch.backends.cudnn.allow_tf32 = self.prev[1]
+            torch.set_float32_matmul_precision(self.prev[2])
+            return False
+
+    return _Ctx()
+
+
+def kl_loss_reference_ops(diff_hidden, ar_hidden_states, weight, anchor_positions, K,
+                          target_ids, pad_token_id, temperature: float = 1.0,
+                          chunk: int = CHUNK):
+    """Restates ``compute_kl_loss`` (train.py:142-195) with the fp32 teacher path.
+
+    Same op order as the reference: gather -> teacher ``linear`` ->
+    ``softmax``/``log_softmax``/entropy under ``no_grad`` (train.py:188-191)
+    -> student ``linear`` -> soft-target ``cross_entropy`` (train.py:202-208)
+    -> ``CE - ent`` -> masked sum (train.py:209-210) -> ``/ total``
+    (train.py:195).  ``weight`` is the lm_head matrix ``[V, H]``; set
+    ``weight.requires_grad_(True)`` to obtain dW (the reference trains with a
+    frozen lm_head, so it never computes dW itself).
+    """
+    torch = _torch()
+    F = torch.nn.functional
+    B, B_blocks = anchor_positions.shape
+    device = diff_hidden.device
+    L = ar_hidden_states.shape[1]
+    N = B_blocks * (K - 1)
+    dp, bi, off = kl_indices(B, B_blocks, K)
+    diff_pos = torch.as_tensor(dp, device=device)
+    batch_idx = torch.as_tensor(bi, device=device)
+    offsets = torch.as_tensor(off, device=device)
+    ar_pos = (anchor_positions.unsqueeze(-1) + offsets).view(B, N).clamp(0, L - 1)
+    tgt = target_ids[batch_idx, diff_pos]
+    valid = tgt != pad_token_id
+    total_tokens = valid.sum().float()
+    if total_tokens == 0:                                   # train.py:166-167
+        return torch.tensor(0.0, device=device, requires_grad=True)
+    inv_t = 1.0 / float(temperature)
+    total_kl = 0.0
+    for c in range(0, N, chunk):                            # train.py:173
+        c_end = min(c + chunk, N)
+        chunk_valid = valid[:, c:c_end].float()
+        if not chunk_valid.any():                           # train.py:176-177
+            continue
+        b_idx = batch_idx[:, c:c_end]
+        d_idx = diff_pos[:, c:c_end]
+        a_idx = ar_pos[:, c:c_end]
+        with torch.no_grad():                               # train.py:183-191
+            t_logits = F.linear(ar_hidden_states[b_idx, a_idx], weight).float() * inv_t
+            p_t = F.softmax(t_logits, dim=-1)
+            ent = -(p_t * F.log_softmax(t_logits, dim=-1)).sum(dim=-1)
+        s_logits = F.linear(diff_hidden[b_idx, d_idx], weight) * inv_t   # train.py:201-202
+        ce = F.cross_entropy(s_logits.view(-1, s_logits.size(-1)),
+                             p_t.view(-1, p_t.size(-1)), reduction="none").view(B, -1)
+        kl = ce.float() - ent.float()                       # train.py:209
+        total_kl = total_kl + (kl * chunk_valid).sum()      # train.py:210
+    return total_kl / total_tokens
+
+
+def aligned_kl_loss_torch(h_s, h_t, weight, mask, temperature: float = 1.0,
+                          chunk: int = CHUNK, normaliser=None):
+    """The reference op sequence on pre-aligned rows (the fused op's contract).
+
+    ``h_s, h_t [N, H]``, ``weight [V, H]``, ``mask [N]`` (bool).  Equivalent to
+    ``kl_loss_reference_ops`` after its gather step.  ``normaliser`` overrides
+    ``sum(mask)`` (used for row-sharded checks where the count is global).
+    Returns a scalar tensor that is differentiable w.r.t. ``h_s`` and
+    ``weight``.  Rows are processed in ``chunk``-row blocks so that only
+    ``chunk x V`` logits exist at a time.
+    """
+    torch = _torch()
+    F = torch.nn.functional
+    valid = mask.bool()
+    total = valid.sum().float() if normaliser is None else torch.as_tensor(float(normaliser))
+    if float(total) == 0.0:
+        return torch.tensor(0.0, device=h_s.device, requires_grad=True)
+    inv_t = 1.0 / float(temperature)
+    N = h_s.shape[0]
+    total_kl = 0.0
+    for c in range(0, N, chunk):
+        c_end = min(c + chunk, N)
+        cv = valid[c:c_end].float()
+        if not cv.any():
+            continue
+        with torch.no_grad():
+            t_logits = F.linear(h_t[c:c_end].float(), weight.float()).float() * inv_t
+            p_t = F.softmax(t_logits, dim=-1)
+            ent = -(p_t * F.log_softmax(t_logits, dim=-1)).sum(dim=-1)
+            del t_logits
+        s_logits = F.linear(h_s[c:c_end].float(), weight.float()) * inv_t
+        ce = F.cross_entropy(s_logits, p_t, reduction="none")
+        total_kl = total_kl + ((ce.float() - ent) * cv).sum()
+    return total_kl / total.to(h_s.device)
+
+
+def aligned_kl_torch_with_grads(h_s, h_t, weight, mask, temperature: float = 1.0,
+                                chunk: int = CHUNK, normaliser=None, want_dw: bool = True):
+    """Loss, dH_s and dW of ``aligned_kl_loss_torch`` via autograd, in fp32.
+
+    Inputs of any float dtype are upcast to fp32 first (so a bf16 problem is
+    checked against fp32 arithmetic on the same bf16 values).
+    """
+    torch = _torch()
+    with fp32_strict():
+        hs = h_s.detach().float().requires_grad_(True)
+        w = weight.detach().float().requires_grad_(want_dw)
+        loss = aligned_kl_loss_torch(hs, h_t.detach().float(), w, mask, temperature,
+                                     chunk=chunk, normaliser=normaliser)
+        if loss.grad_fn is None:
+            dh = torch.zeros_like(hs)
+            dw = torch.zeros_like(w) if want_dw else None
+        else:
+            loss.backward()
+            dh = hs.grad if hs.grad is not None else torch.zeros_like(hs)
+            dw = (w.grad if w.grad is not None else torch.zeros_like(w)) if want_dw else None
+    return loss.detach(), dh, dw
+
+
+# --------------------------------------------------------------------------
+# float64 numpy restatement with closed-form gradients
+# --------------------------------------------------------------------------
+
+def _lse(z):
+    m = z.max(axis=-1, keepdims=True)
+    return (m + np.log(np.exp(z - m).sum(axis=-1, keepdims=True)))[..., 0]
+
+
+def aligned_kl_loss_np(h_s, h_t, W, mask, temperature: float = 1.0, chunk: int = 512,
+                       normaliser: Optional[float] = None, want_grads: bool = True):
+    """float64 restatement: ``loss, dH_s, dW, row_kl, lse_s, lse_t``.
+
+    Per row ``i`` (natural log, ``z = h W^T / T``):
+    ``KL_i = sum_v p_v (z_t - z_s) - lse_t + lse_s`` with ``p = softmax(z_t)``
+    -- algebraically ``CE(z_s, p) - H(p)`` of train.py:204-209.
+    Gradient of ``loss = sum valid_i KL_i / n`` (soft-target CE rule, teacher
+    detached as in train.py:183): ``dZ_s = valid_i/n * (softmax(z_s) - p) / T``,
+    ``dH_s = dZ_s W``, ``dW = dZ_s^T h_s``.
+    """
+    h_s = np.asarray(h_s, dtype=np.float64)
+    h_t = np.asarray(h_t, dtype=np.float64)
+    W = np.asarray(W, dtype=np.float64)
+    valid = np.asarray(mask).astype(bool)
+    n = float(valid.sum()) if normaliser is None else float(normaliser)
+    N = h_s.shape[0]
+    inv_t = 1.0 / float(temperature)
+    row_kl = np.zeros(N)
+    lse_s = np.zeros(N)
+    lse_t = np.zeros(N)
+    dH = np.zeros_like(h_s) if want_grads else None
+    dW = np.zeros_like(W) if want_grads else None
+    for c in range(0, N, chunk):
+        e = min(c + chunk, N)
+        zs = (h_s[c:e] @ W.T) * inv_t
+        zt = (h_t[c:e] @ W.T) * inv_t
+        ls = _lse(zs)
+        lt = _lse(zt)
+        p = np.exp(zt - lt[:, None])
+        q = np.exp(zs - ls[:, None])
+        row_kl[c:e] = (p * (zt - zs)).sum(axis=1) - lt + ls
+        lse_s[c:e] = ls
+        lse_t[c:e] = lt
+        if want_grads and n > 0:
+            coef = valid[c:e].astype(np.float64) / n * inv_t
+            dz = coef[:, None] * (q - p)
+            dH[c:e] = dz @ W
+            dW += dz.T @ h_s[c:e]
+    loss = float((row_kl * valid).sum() / n) if n > 0 else 0.0
+    return loss, dH, dW, row_kl, lse_s, lse_t
+
+
+# --------------------------------------------------------------------------
+# Vocab-range partial statistics (shard-combine reference for multi-rank tests)
+# --------------------------------------------------------------------------
+
+def partial_stats_np(h_s, h_t, W_range, temperature: float = 1.0):
+    """Per-row partial record over one vocab range, natural-log domain.
+
+    Returns ``[5, N]``: ``(m_s, S_s, m_t, S_t, A)`` with ``S = sum exp(z - m)``
+    and ``A = sum exp(z_t - m_t) (z_t - z_s)`` over the range.
+    """
+    inv_t = 1.0 / float(temperature)
+    zs = (np.asarray(h_s, np.float64) @ np.asarray(W_range, np.float64).T) * inv_t
+    zt = (np.asarray(h_t, np.float64) @ np.asarray(W_range, np.float64).T) * inv_t
+    ms = zs.max(axis=1)
+    mt = zt.max(axis=1)
+    es = np.exp(zs - ms[:, None])
+    et = np.exp(zt - mt[:, None])
+    return np.stack([ms, es.sum(1), mt, et.sum(1), (et * (zt - zs)).sum(1)])
+
+
+def merge_partials_np(parts):
+    """Online-softmax merge of ``[P, 5, N]`` partial records into ``[5, N]``."""
+    parts = np.asarray(parts, np.float64)
+    ms = parts[:, 0].max(axis=0)
+    mt = parts[:, 2].max(axis=0)
+    ws = np.exp(parts[:, 0] - ms)
+    wt = np.exp(parts[:, 2] - mt)
+    return np.stack([ms, (parts[:, 1] * ws).sum(0), mt, (parts[:, 3] * wt).sum(0),
+                     (parts[:, 4] * wt).sum(0)])
+
+
+def finalize_np(stats, mask, normaliser: Optional[float] = None):
+    """Loss, per-row KL and log-sum-exps from a merged ``[5, N]`` record."""
+    ms, Ss, mt, St, A = stats
+    lse_s = ms + np.log(Ss)
+    lse_t = mt + np.log(St)
+    row_kl = A / St - lse_t + lse_s
+    valid = np.asarray(mask).astype(bool)
+    n = float(valid.sum()) if normaliser is None else float(normaliser)
+    loss = float((row_kl * valid).sum() / n) if n > 0 else 0.0
+    return loss, row_kl, lse_s, lse_t
+
+
+def range_grads_np(h_s, h_t, W_range, lse_s, lse_t, mask, normaliser, temperature=1.0, g=1.0):
+    """dZ over one vocab range given global log-sum-exps: ``(dH partial, dW range)``."""
+    inv_t = 1.0 / float(temperature)
+    hs = np.asarray(h_s, np.float64)
+    Wr = np.asarray(W_range, np.float64)
+    zs = (hs @ Wr.T) * inv_t
+    zt = (np.asarray(h_t, np.float64) @ Wr.T) * inv_t
+    q = np.exp(zs - np.asarray(lse_s)[:, None])
+    p = np.exp(zt - np.asarray(lse_t)[:, None])
+    n = float(normaliser)
+    coef = (np.asarray(mask).astype(np.float64) / n * inv_t * g) if n > 0 else np.zeros(hs.shape[0])
+    dz = coef[:, None] * (q - p)
+    return dz @ Wr, dz.T @ hs
+
+
+# --------------------------------------------------------------------------
+# Seeded workloads (shapes and distributions of the benchmark configurations)
+# --------------------------------------------------------------------------
+
+def block_mask(n_rows: int, block: int, lo: float, hi: float, gen) -> "object":
+    """Per block of ``block`` positions draw ``r ~ U(lo, hi)``; each row valid with prob ``r``."""
+    torch = _torch()
+    n_blk = (n_rows + block - 1) // block
+    r = torch.rand(n_blk, generator=gen) * (hi - lo) + lo
+    r = r.repeat_interleave(block)[:n_rows]
+    return torch.rand(n_rows, generator=gen) < r
+
+
+def make_problem(name: str, n_rows: Optional[int] = None, seed: int = 42):
+    """Seeded synthetic inputs with a benchmark configuration's shapes.
+
+    Returns a dict with ``h_s, h_t [N, H]``, ``W [V, H]``, ``mask [N]`` (bool),
+    ``T`` and ``dtype`` (all CPU tensors; bf16 configurations are returned
+    already rounded to bf16).  ``n_rows`` subsamples the row count.
+
+    Configurations (rows x hidden x vocab):
+      c1  1024 x 576 x 49152   fp32, N(0,1) hidden, N(0,0.02) weight, Bernoulli(0.5) mask, T=1
+      c2  16384 x 576 x 49152  bf16, mask ratio U(0,1) per block of 32, T=1
+      c3  65536 x 2048 x 49152 bf16, Bernoulli(0.5), T=1
+      c4  32768 x 1024 x 248320 bf16, Bernoulli(0.5), T=1 (vocab split in 8 shards)
+      c5  12288 x 576 x 49152  bf16, mask ratio U(0,0.5) per block of 32, teacher x4, T=2,
+          >= 8 rows forced all-masked
+    """
+    torch = _torch()
+    cfg = {
+        "c1": (1024, 576, 49152, torch.float32),
+        "c2": (16384, 576, 49152, torch.bfloat16),
+        "c3": (65536, 2048, 49152, torch.bfloat16),
+        "c4": (32768, 1024, 248320, torch.bfloat16),
+        "c5": (12288, 576, 49152, torch.bfloat16),
+    }[name]
+    N, H, V, dt = cfg
+    if n_rows is not None:
+        N = int(n_rows)
+    g = torch.Generator().manual_seed(seed)
+    h_s = torch.randn(N, H, generator=g)
+    h_t = torch.randn(N, H, generator=g)
+    W = torch.randn(V, H, generator=g) * 0.02
+    T = 1.0
+    if name == "c2":
+        mask = block_mask(N, 32, 0.0, 1.0, g)
+    elif name == "c5":
+        mask = block_mask(N, 32, 0.0, 0.5, g)
+        h_t = h_t * 4.0
+        T = 2.0
+        mask[: min(8, N)] = False
+        mask[N // 2: N // 2 + 8] = False
+    else:
+        mask = torch.rand(N, generator=g) < 0.5
+    return {"h_s": h_s.to(dt), "h_t": h_t.to(dt), "W": W.to(dt), "mask": mask,
+            "T": T, "dtype": dt, "name": name}
+
+
+def grad_metrics(ours, ref) -> Tuple[float, float]:
+    """``(max_rel, cosine)`` of a gradient against its reference.
+
+    ``max_rel = max|ours - ref| / max|ref|`` (normalised max error) and the
+    cosine similarity of the flattened tensors, both in float64.
+    """
+    a = np.asarray(ours, np.float64).ravel()
+    b = np.asarray(ref, np.float64).ravel()
+    denom = np.abs(b).max()
+    max_rel = float(np.abs(a - b).max() / denom) if denom > 0 else float(np.abs(a).max())
+    na = np.linalg.norm(a)
+    nb = np.linalg.norm(b)
+    if na == 0 and nb == 0:
+        cos = 1.0
+    elif na == 0 or nb == 0:
+        cos = 0.0
+    else:
+        cos = float(a @ b / (na * nb))
+    return max_rel, cos
+
+
+LN2 = math.log(2.0)

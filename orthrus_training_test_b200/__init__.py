@@ -1,0 +1,12 @@
+"""Fused KL-GEMM distillation loss for B200 (sm_100a).
+
+Public API
+  compute_kl_loss   drop-in for the reference's ``train.compute_kl_loss``
+  kl_gemm_loss      the fused loss on aligned rows (``KLGemmFn.apply``)
+  KLGemmFn          the ``torch.autograd.Function``
+  parallel          row-sharded and vocab-sharded multi-GPU variants
+"""
+from .ops import KLGemmFn, kl_gemm_loss, kl_forward, kl_backward  # noqa: F401
+from .loss import compute_kl_loss, select_rows  # noqa: F401
+
+__all__ = ["KLGemmFn", "kl_gemm_loss", "kl_forward", "kl_backward", "compute_kl_loss", "select_rows"]

@@ -1,0 +1,463 @@
+// C-ABI of the fused KL-GEMM distillation loss (see include/klgemm.h).
+//
+// Host side: argument checks, tensor-map construction, work planning and the
+// launch sequence.  All device memory is owned by the caller; every entry
+// point only enqueues work on the caller's stream and never synchronises
+// (except klg_device_status, which reads the device status word).
+#include <cuda_runtime.h>
+#include <cuda.h>
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "klg_kernels.cuh"
+#include "../../include/klgemm.h"
+
+namespace {
+
+thread_local char g_err[512] = "";
+std::atomic<long long> g_launches{0};
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(KLG_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map, 128-byte swizzle, zero fill out of bounds.
+// inner = contiguous extent (elements), outer = row count, ld = row stride (elements).
+bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
+              uint32_t box_outer) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Per-launch timing trace (klg_trace_begin / klg_trace_end).
+struct Trace {
+  std::mutex mu;
+  bool on = false;
+  int cap = 0;
+  int used = 0;
+  std::vector<cudaEvent_t> ev;  // 2 per launch
+  std::vector<int> kind;
+};
+Trace g_trace;
+
+// Records the "before" event of the next traced launch; returns its slot or -1.
+int trace_pre(cudaStream_t s) {
+  std::lock_guard<std::mutex> lk(g_trace.mu);
+  if (!g_trace.on || g_trace.used >= g_trace.cap) return -1;
+  const int i = g_trace.used++;
+  cudaEventRecord(g_trace.ev[2 * i], s);
+  return i;
+}
+void trace_post(int slot, cudaStream_t s, int kind) {
+  if (slot < 0) return;
+  std::lock_guard<std::mutex> lk(g_trace.mu);
+  cudaEventRecord(g_trace.ev[2 * slot + 1], s);
+  g_trace.kind[slot] = kind;
+}
+
+int num_sms() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+  return n;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline int cdiv(long long a, long long b) { return (int)((a + b - 1) / b); }
+
+// Work split of a dual-view launch: n_rt row tiles x n_vt vocab tiles are cut
+// into units of vpu vocab tiles.  Picks vpu (>= 4 where possible) so the unit
+// count fills the SMs in whole waves as closely as possible, preferring the
+// largest vpu among near-ties.
+void plan_dual(int n_rt, int n_vt, int n_sm, int& vpu, int& n_uv) {
+  const int vmin = n_vt < 4 ? n_vt : 4;
+  double best = -1.0;
+  vpu = n_vt;
+  for (int v = n_vt; v >= vmin; --v) {
+    const int uv = cdiv(n_vt, v);
+    if (uv > 64) break;
+    const long long units = (long long)n_rt * uv;
+    const long long waves = (units + n_sm - 1) / n_sm;
+    // balance of tile work across SMs (tiles per unit vary only in the last uv)
+    const double eff = (double)n_rt * n_vt / ((double)waves * n_sm * v);
+    if (eff > best + 0.005) {
+      best = eff;
+      vpu = v;
+    }
+  }
+  n_uv = cdiv(n_vt, vpu);
+}
+
+int gemm_bn(long long hidden) {
+  if (hidden % 256 == 0) return 256;
+  if (hidden % 192 == 0) return 192;
+  if (hidden % 128 == 0) return 128;
+  return 256;
+}
+
+template <typename Kern>
+cudaError_t set_smem(Kern k, int bytes) {
+  return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+template <int MODE>
+int launch_dual(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMap& mw, const klg::DualArgs& a,
+                cudaStream_t s) {
+  auto k = klg::dual_kernel<MODE>;
+  cudaError_t e = set_smem(k, klg::DUAL_SMEM);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dual_kernel)");
+  const int grid = a.n_units < num_sms() ? a.n_units : num_sms();
+  const int slot = trace_pre(s);
+  k<<<grid, klg::NUM_THREADS, klg::DUAL_SMEM, s>>>(mhs, mht, mw, a);
+  e = cudaGetLastError();
+  trace_post(slot, s, MODE == klg::MODE_STATS ? KLG_KIND_STATS : KLG_KIND_DZ);
+  if (e != cudaSuccess) return cuda_fail(e, "launch dual_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
+template <bool A_MN, bool B_MN, int BN>
+int launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const klg::GemmArgs& a, cudaStream_t s, int kind) {
+  auto k = klg::gemm_kernel<A_MN, B_MN, BN>;
+  constexpr int smem = klg::GemmCfg<BN>::SMEM;
+  cudaError_t e = set_smem(k, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm_kernel)");
+  const int grid = a.n_tiles < num_sms() ? a.n_tiles : num_sms();
+  const int slot = trace_pre(s);
+  k<<<grid, klg::NUM_THREADS, smem, s>>>(ma, mb, a);
+  e = cudaGetLastError();
+  trace_post(slot, s, kind);
+  if (e != cudaSuccess) return cuda_fail(e, "launch gemm_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
+template <bool A_MN, bool B_MN>
+int launch_gemm(int bn, const CUtensorMap& ma, const CUtensorMap& mb, const klg::GemmArgs& a, cudaStream_t s,
+                int kind) {
+  switch (bn) {
+    case 128: return launch_gemm_t<A_MN, B_MN, 128>(ma, mb, a, s, kind);
+    case 192: return launch_gemm_t<A_MN, B_MN, 192>(ma, mb, a, s, kind);
+    default: return launch_gemm_t<A_MN, B_MN, 256>(ma, mb, a, s, kind);
+  }
+}
+
+klg::GemmArgs gemm_args(int M, int Ncol, int K, int bn, float* C, int ldc, int accumulate, int a_k0, int b_k0) {
+  klg::GemmArgs g;
+  g.M = M;
+  g.Ncol = Ncol;
+  g.K = K;
+  g.n_mt = cdiv(M, klg::BM);
+  g.n_nt = cdiv(Ncol, bn);
+  g.n_tiles = g.n_mt * g.n_nt;
+  g.n_kb = cdiv(K, klg::BK);
+  g.C = C;
+  g.ldc = ldc;
+  g.accumulate = accumulate;
+  g.a_k0 = a_k0;
+  g.b_k0 = b_k0;
+  return g;
+}
+
+int check_problem(const void* hs, const void* ht, const void* w, int64_t n_rows, int64_t hidden, int64_t vocab,
+                  float inv_temp) {
+  if (!hs || !ht || !w) return fail(KLG_ERR_ARG, "null input pointer");
+  if (n_rows < 1 || hidden < 8 || vocab < 1) return fail(KLG_ERR_ARG, "bad shape N=%lld H=%lld V=%lld",
+                                                          (long long)n_rows, (long long)hidden, (long long)vocab);
+  if (n_rows > (1ll << 30) || hidden > (1ll << 20) || vocab > (1ll << 30))
+    return fail(KLG_ERR_ARG, "shape too large N=%lld H=%lld V=%lld", (long long)n_rows, (long long)hidden,
+                (long long)vocab);
+  if (hidden % 8 != 0) return fail(KLG_ERR_ALIGN, "hidden=%lld must be a multiple of 8", (long long)hidden);
+  if (!aligned16(hs) || !aligned16(ht) || !aligned16(w)) return fail(KLG_ERR_ALIGN, "inputs must be 16-byte aligned");
+  if (!(inv_temp > 0.f) || !std::isfinite(inv_temp)) return fail(KLG_ERR_ARG, "inv_temp must be finite and > 0");
+  return KLG_OK;
+}
+
+}  // namespace
+
+// ======================================================================= C-ABI
+extern "C" {
+
+int klg_version(void) { return KLG_VERSION; }
+
+int klg_last_error(char* buf, int len) {
+  if (!buf || len <= 0) return KLG_ERR_ARG;
+  std::snprintf(buf, (size_t)len, "%s", g_err);
+  return KLG_OK;
+}
+
+int klg_device_status(int* status, int reset) {
+  if (!status) return fail(KLG_ERR_ARG, "null status pointer");
+  cudaError_t e = cudaMemcpyFromSymbol(status, klg::g_status, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "read device status");
+  if (reset) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(klg::g_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e, "reset device status");
+  }
+  return KLG_OK;
+}
+
+long long klg_launch_count(void) { return g_launches.load(); }
+
+int klg_num_partials(int64_t n_rows, int64_t vocab, int* n_part) {
+  if (!n_part || n_rows < 1 || vocab < 1) return fail(KLG_ERR_ARG, "bad arguments to klg_num_partials");
+  int vpu, n_uv;
+  plan_dual(cdiv(n_rows, klg::BM), cdiv(vocab, klg::DUAL_BN), num_sms(), vpu, n_uv);
+  *n_part = n_uv;
+  return KLG_OK;
+}
+
+int klg_fwd_stats(const void* hs, const void* ht, const void* w, int64_t n_rows, int64_t hidden, int64_t vocab,
+                  float inv_temp, float* partials, int n_part, void* stream) {
+  int rc = check_problem(hs, ht, w, n_rows, hidden, vocab, inv_temp);
+  if (rc) return rc;
+  if (!partials || !aligned16(partials)) return fail(KLG_ERR_ARG, "partials must be non-null and 16-byte aligned");
+  klg::DualArgs a{};
+  a.n_rows = (int)n_rows;
+  a.v_begin = 0;
+  a.v_count = (int)vocab;
+  a.n_rt = cdiv(n_rows, klg::BM);
+  a.n_vt = cdiv(vocab, klg::DUAL_BN);
+  int n_uv;
+  plan_dual(a.n_rt, a.n_vt, num_sms(), a.vt_per_unit, n_uv);
+  if (n_part != n_uv) return fail(KLG_ERR_ARG, "n_part=%d but this device plans %d (use klg_num_partials)", n_part, n_uv);
+  a.n_units = a.n_rt * n_uv;
+  a.n_kb = cdiv(hidden, klg::BK);
+  a.scale_log2 = inv_temp * 1.4426950408889634f;
+  a.partials = partials;
+  alignas(64) CUtensorMap mhs, mht, mw;
+  if (!make_map(&mhs, hs, hidden, n_rows, hidden, klg::BK, klg::BM) ||
+      !make_map(&mht, ht, hidden, n_rows, hidden, klg::BK, klg::BM) ||
+      !make_map(&mw, w, hidden, vocab, hidden, klg::BK, klg::DUAL_BN))
+    return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+  return launch_dual<klg::MODE_STATS>(mhs, mht, mw, a, (cudaStream_t)stream);
+}
+
+int klg_merge_stats(const float* partials, int n_part, int64_t n_rows, float* stats, void* stream) {
+  if (!partials || !stats || n_part < 1 || n_rows < 1) return fail(KLG_ERR_ARG, "bad arguments to klg_merge_stats");
+  const int slot = trace_pre((cudaStream_t)stream);
+  klg::merge_kernel<<<cdiv(n_rows, 256), 256, 0, (cudaStream_t)stream>>>(partials, n_part, (int)n_rows, stats);
+  cudaError_t e = cudaGetLastError();
+  trace_post(slot, (cudaStream_t)stream, KLG_KIND_MERGE);
+  if (e != cudaSuccess) return cuda_fail(e, "launch merge_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
+int klg_count_valid(const uint8_t* mask, int64_t n_rows, float* count, void* stream) {
+  if (!mask || !count || n_rows < 1 || n_rows > (1ll << 30)) return fail(KLG_ERR_ARG, "bad arguments to klg_count_valid");
+  const int slot = trace_pre((cudaStream_t)stream);
+  klg::count_valid_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(mask, (int)n_rows, count);
+  cudaError_t e = cudaGetLastError();
+  trace_post(slot, (cudaStream_t)stream, KLG_KIND_COUNT);
+  if (e != cudaSuccess) return cuda_fail(e, "launch count_valid_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
+int klg_finalize(const float* stats, const uint8_t* mask, int64_t n_rows, const float* count, float* loss, float* lse,
+                 float* row_kl, void* stream) {
+  if (!stats || !mask || !count || !loss || n_rows < 1 || n_rows > (1ll << 30))
+    return fail(KLG_ERR_ARG, "bad arguments to klg_finalize");
+  const int slot = trace_pre((cudaStream_t)stream);
+  klg::finalize_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(stats, mask, (int)n_rows, count, loss, lse, row_kl);
+  cudaError_t e = cudaGetLastError();
+  trace_post(slot, (cudaStream_t)stream, KLG_KIND_FINALIZE);
+  if (e != cudaSuccess) return cuda_fail(e, "launch finalize_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
+int64_t klg_fwd_workspace_bytes(int64_t n_rows, int64_t vocab) {
+  int n_part = 0;
+  if (klg_num_partials(n_rows, vocab, &n_part) != KLG_OK) return -1;
+  return (int64_t)(n_part + 1) * 5 * n_rows * 4 + 256;
+}
+
+int klg_fwd(const void* hs, const void* ht, const void* w, const uint8_t* mask, int64_t n_rows, int64_t hidden,
+            int64_t vocab, float inv_temp, int count_given, float* count, float* loss, float* lse, float* row_kl,
+            void* workspace, int64_t workspace_bytes, void* stream) {
+  int rc = check_problem(hs, ht, w, n_rows, hidden, vocab, inv_temp);
+  if (rc) return rc;
+  if (!mask || !count || !loss || !lse) return fail(KLG_ERR_ARG, "null output pointer");
+  int n_part = 0;
+  if ((rc = klg_num_partials(n_rows, vocab, &n_part))) return rc;
+  const int64_t need = (int64_t)(n_part + 1) * 5 * n_rows * 4;
+  if (!workspace || workspace_bytes < need || !aligned16(workspace))
+    return fail(KLG_ERR_WORKSPACE, "forward workspace needs %lld bytes (16-byte aligned)", (long long)need);
+  float* parts = static_cast<float*>(workspace);
+  float* stats = parts + (size_t)n_part * 5 * n_rows;
+  if (!count_given && (rc = klg_count_valid(mask, n_rows, count, stream))) return rc;
+  if ((rc = klg_fwd_stats(hs, ht, w, n_rows, hidden, vocab, inv_temp, parts, n_part, stream))) return rc;
+  if ((rc = klg_merge_stats(parts, n_part, n_rows, stats, stream))) return rc;
+  return klg_finalize(stats, mask, n_rows, count, loss, lse, row_kl, stream);
+}
+
+int64_t klg_bwd_chunk_cols(int64_t n_rows, int64_t vocab, int64_t workspace_bytes) {
+  if (n_rows < 1 || vocab < 1) return -1;
+  const int64_t full = (int64_t)cdiv(vocab, 128) * 128;
+  int64_t c = workspace_bytes / (n_rows * 2);
+  c = (c / 128) * 128;
+  if (c > full) c = full;
+  return c >= 128 ? c : -1;
+}
+
+int64_t klg_bwd_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t vocab) {
+  (void)hidden;
+  if (n_rows < 1 || vocab < 1) return -1;
+  const int64_t full = (int64_t)cdiv(vocab, 128) * 128;
+  int64_t cols = (256ll << 20) / (n_rows * 2);
+  cols = (cols / 128) * 128;
+  if (cols < 2048) cols = 2048;
+  if (cols > full) cols = full;
+  return n_rows * cols * 2;
+}
+
+int klg_bwd(const void* hs, const void* ht, const void* w, const uint8_t* mask, const float* lse, const float* count,
+            const float* grad, int64_t n_rows, int64_t hidden, int64_t vocab, float inv_temp, float* d_hs, float* d_w,
+            void* workspace, int64_t workspace_bytes, void* stream) {
+  int rc = check_problem(hs, ht, w, n_rows, hidden, vocab, inv_temp);
+  if (rc) return rc;
+  if (!mask || !lse || !count) return fail(KLG_ERR_ARG, "null mask/lse/count");
+  if (!d_hs && !d_w) return KLG_OK;
+  if ((d_hs && !aligned16(d_hs)) || (d_w && !aligned16(d_w))) return fail(KLG_ERR_ALIGN, "outputs must be 16-byte aligned");
+  const int64_t cols = klg_bwd_chunk_cols(n_rows, vocab, workspace_bytes);
+  if (!workspace || cols < 0 || !aligned16(workspace))
+    return fail(KLG_ERR_WORKSPACE, "backward workspace too small: needs >= %lld bytes", (long long)(n_rows * 256));
+  cudaStream_t s = (cudaStream_t)stream;
+  __nv_bfloat16* dz = static_cast<__nv_bfloat16*>(workspace);
+  const int bn = gemm_bn(hidden);
+
+  alignas(64) CUtensorMap mhs, mht, mw, mw_mn, mhs_mn;
+  if (!make_map(&mhs, hs, hidden, n_rows, hidden, klg::BK, klg::BM) ||
+      !make_map(&mht, ht, hidden, n_rows, hidden, klg::BK, klg::BM) ||
+      !make_map(&mw, w, hidden, vocab, hidden, klg::BK, klg::DUAL_BN) ||
+      !make_map(&mw_mn, w, hidden, vocab, hidden, 64, klg::BK) ||
+      !make_map(&mhs_mn, hs, hidden, n_rows, hidden, 64, klg::BK))
+    return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+
+  klg::DualArgs a{};
+  a.n_rows = (int)n_rows;
+  a.n_rt = cdiv(n_rows, klg::BM);
+  a.n_kb = cdiv(hidden, klg::BK);
+  a.scale_log2 = inv_temp * 1.4426950408889634f;
+  a.lse = lse;
+  a.mask = mask;
+  a.count = count;
+  a.grad = grad;
+  a.inv_temp = inv_temp;
+  a.dz = dz;
+  a.ld_dz = (int)cols;
+
+  for (int64_t v0 = 0; v0 < vocab; v0 += cols) {
+    const int64_t wv = (vocab - v0) < cols ? (vocab - v0) : cols;
+    a.v_begin = (int)v0;
+    a.v_count = (int)wv;
+    a.n_vt = cdiv(wv, klg::DUAL_BN);
+    int n_uv;
+    plan_dual(a.n_rt, a.n_vt, num_sms(), a.vt_per_unit, n_uv);
+    a.n_units = a.n_rt * n_uv;
+    if ((rc = launch_dual<klg::MODE_DZ>(mhs, mht, mw, a, s))) return rc;
+    if (d_hs) {
+      alignas(64) CUtensorMap mdz;
+      if (!make_map(&mdz, dz, wv, n_rows, cols, klg::BK, klg::BM)) return fail(KLG_ERR_CUDA, "tensor map (dz)");
+      klg::GemmArgs g = gemm_args((int)n_rows, (int)hidden, (int)wv, bn, d_hs, (int)hidden, v0 > 0, 0, (int)v0);
+      if ((rc = launch_gemm<false, true>(bn, mdz, mw_mn, g, s, KLG_KIND_GEMM_DH))) return rc;
+    }
+    if (d_w) {
+      alignas(64) CUtensorMap mdz_mn;
+      if (!make_map(&mdz_mn, dz, wv, n_rows, cols, 64, klg::BK)) return fail(KLG_ERR_CUDA, "tensor map (dz^T)");
+      klg::GemmArgs g = gemm_args((int)wv, (int)hidden, (int)n_rows, bn, d_w + v0 * hidden, (int)hidden, 0, 0, 0);
+      if ((rc = launch_gemm<true, true>(bn, mdz_mn, mhs_mn, g, s, KLG_KIND_GEMM_DW))) return rc;
+    }
+  }
+  return KLG_OK;
+}
+
+int klg_cast_f32_bf16(const float* in, void* out, int64_t n, void* stream) {
+  if (!in || !out || n < 0) return fail(KLG_ERR_ARG, "bad arguments to klg_cast_f32_bf16");
+  if (n == 0) return KLG_OK;
+  long long blocks = (n + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  const int slot = trace_pre((cudaStream_t)stream);
+  klg::cast_f32_bf16_kernel<<<(int)blocks, 256, 0, (cudaStream_t)stream>>>(in, static_cast<__nv_bfloat16*>(out), n);
+  cudaError_t e = cudaGetLastError();
+  trace_post(slot, (cudaStream_t)stream, KLG_KIND_CAST);
+  if (e != cudaSuccess) return cuda_fail(e, "launch cast_f32_bf16_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
+int klg_trace_begin(int capacity) {
+  if (capacity < 1 || capacity > (1 << 20)) return fail(KLG_ERR_ARG, "trace capacity out of range");
+  std::lock_guard<std::mutex> lk(g_trace.mu);
+  while ((int)g_trace.ev.size() < 2 * capacity) {
+    cudaEvent_t e;
+    cudaError_t err = cudaEventCreate(&e);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaEventCreate");
+    g_trace.ev.push_back(e);
+  }
+  g_trace.kind.assign(capacity, 0);
+  g_trace.cap = capacity;
+  g_trace.used = 0;
+  g_trace.on = true;
+  return KLG_OK;
+}
+
+int klg_trace_end(int* kinds, float* ms, int capacity, int* n) {
+  std::lock_guard<std::mutex> lk(g_trace.mu);
+  g_trace.on = false;
+  const int used = g_trace.used;
+  if (n) *n = used;
+  for (int i = 0; i < used && i < capacity; ++i) {
+    cudaError_t err = cudaEventSynchronize(g_trace.ev[2 * i + 1]);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaEventSynchronize");
+    float t = 0.f;
+    err = cudaEventElapsedTime(&t, g_trace.ev[2 * i], g_trace.ev[2 * i + 1]);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaEventElapsedTime");
+    if (kinds) kinds[i] = g_trace.kind[i];
+    if (ms) ms[i] = t;
+  }
+  g_trace.used = 0;
+  return used > capacity ? fail(KLG_ERR_ARG, "trace holds %d launches, buffer %d", used, capacity) : KLG_OK;
+}
+
+}  // extern "C"

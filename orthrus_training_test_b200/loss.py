@@ -1,0 +1,71 @@
+"""Drop-in for the reference's ``compute_kl_loss`` (train.py:142-195).
+
+Same signature and semantics; the arithmetic runs in the fused sm_100a op
+(:class:`~orthrus_training_test_b200.ops.KLGemmFn`).  ``teacher_probs`` and
+``teacher_ent`` are accepted and ignored: the fused op recomputes the teacher
+logits tile by tile, so the caller can drop the ``[B, L, V]`` precompute of
+train.py:549-567.
+"""
+from __future__ import annotations
+
+from typing import Tuple
+
+import torch
+
+from .ops import KLGemmFn
+
+_index_cache: dict = {}
+
+
+def kl_indices(B: int, B_blocks: int, K: int, device) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """``(diff_pos [B,N], batch_idx [B,N], offsets [K-1])`` as in train.py:124-139.
+
+    Student rows are the diffusion positions ``blk*K + k`` for k = 1..K-1 (the
+    anchor at offset 0 carries no loss); teacher offsets are 0..K-2.
+    """
+    key = (B, B_blocks, K, str(device))
+    hit = _index_cache.get(key)
+    if hit is None:
+        N = B_blocks * (K - 1)
+        diff_pos = torch.arange(B_blocks * K, device=device).view(B_blocks, K)[:, 1:].reshape(-1)
+        diff_pos = diff_pos.unsqueeze(0).expand(B, N)
+        batch_idx = torch.arange(B, device=device).unsqueeze(1).expand(B, N)
+        offsets = torch.arange(0, K - 1, device=device)
+        hit = (diff_pos, batch_idx, offsets)
+        _index_cache[key] = hit
+    return hit
+
+
+def select_rows(diff_hidden, ar_hidden_states, anchor_positions, K, target_ids, pad_token_id):
+    """Aligned ``(h_s [B*N, H], h_t [B*N, H], valid [B*N])`` of train.py:156-164.
+
+    Teacher row = ``anchor + k - 1`` clamped to ``[0, L-1]`` (train.py:161);
+    valid = ``target != pad_token_id`` (train.py:163-164).  The student gather
+    is differentiable (its backward scatters dH_s into ``diff_hidden.grad``).
+    """
+    B, B_blocks = anchor_positions.shape
+    L = ar_hidden_states.shape[1]
+    N = B_blocks * (K - 1)
+    diff_pos, batch_idx, offsets = kl_indices(B, B_blocks, K, diff_hidden.device)
+    ar_pos = (anchor_positions.unsqueeze(-1) + offsets).view(B, N).clamp(0, L - 1)
+    valid = target_ids[batch_idx, diff_pos] != pad_token_id
+    h_s = diff_hidden[batch_idx, diff_pos].reshape(B * N, -1)
+    h_t = ar_hidden_states[batch_idx, ar_pos].reshape(B * N, -1)
+    return h_s, h_t, valid.reshape(-1)
+
+
+def compute_kl_loss(diff_hidden: torch.Tensor, ar_hidden_states: torch.Tensor, lm_head: torch.nn.Module,
+                    anchor_positions: torch.Tensor, K: int, target_ids: torch.Tensor, pad_token_id: int,
+                    teacher_probs=None, teacher_ent=None, temperature: float = 1.0) -> torch.Tensor:
+    """Forward KL(teacher || student) averaged over valid diffusion positions.
+
+    Signature of train.py:142-152 (plus an optional ``temperature``, default 1
+    = the reference).  Returns a 0-d fp32 tensor; ``0.0`` with
+    ``requires_grad`` when no position is valid (train.py:166-167).
+    """
+    if getattr(lm_head, "bias", None) is not None:
+        raise ValueError("lm_head with a bias is not supported (the reference's tied lm_head has none)")
+    h_s, h_t, valid = select_rows(diff_hidden, ar_hidden_states, anchor_positions, K, target_ids, pad_token_id)
+    if not bool(valid.any()):
+        return torch.tensor(0.0, device=diff_hidden.device, requires_grad=True)
+    return KLGemmFn.apply(h_s, h_t.detach(), lm_head.weight, valid, float(temperature), None)

@@ -1,0 +1,205 @@
+"""PyTorch binding of the fused KL-GEMM distillation loss.
+
+``KLGemmFn`` is the ``torch.autograd.Function`` that replaces the reference's
+loss arithmetic (``train.py:142-210``): its forward runs pass 1 (both views'
+logits over vocab tiles with online max / sum-exp / KL, never storing an
+``[N, V]`` tensor) and returns the scalar loss; its backward runs pass 2
+(recompute the logits chunk by chunk, form dZ, then dH_s = dZ W and
+dW = dZ^T h_s).  Saved for backward: the inputs and two log-sum-exps per row.
+
+Every function here calls the CUDA library; there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import call
+
+_vp = ctypes.c_void_p
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return _vp(t.data_ptr()) if t is not None else _vp(0)
+
+
+def _stream(device: torch.device):
+    return _vp(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _require_cuda(*ts):
+    dev = ts[0].device
+    if dev.type != "cuda":
+        raise RuntimeError("the fused KL-GEMM loss runs on CUDA tensors only (no CPU path)")
+    for t in ts:
+        if t.device != dev:
+            raise RuntimeError(f"all tensors must be on {dev}, got {t.device}")
+    return dev
+
+
+def to_compute_dtype(x: torch.Tensor) -> torch.Tensor:
+    """bf16, contiguous.  fp32 inputs are rounded to bf16 by the library's cast kernel."""
+    x = x.detach()
+    if x.dtype == torch.bfloat16:
+        return x.contiguous()
+    if x.dtype == torch.float32:
+        x = x.contiguous()
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+        call("klg_cast_f32_bf16", _ptr(x), _ptr(out), x.numel(), _stream(x.device))
+        return out
+    raise TypeError(f"unsupported dtype {x.dtype} (bf16 or fp32)")
+
+
+def mask_u8(mask: torch.Tensor) -> torch.Tensor:
+    if mask.dtype == torch.uint8:
+        return mask.contiguous()
+    return (mask != 0).to(torch.uint8).contiguous()
+
+
+def num_partials(n_rows: int, vocab: int) -> int:
+    n = ctypes.c_int(0)
+    call("klg_num_partials", n_rows, vocab, ctypes.byref(n))
+    return n.value
+
+
+# ----------------------------------------------------------------- pass pieces
+
+def count_valid(mask: torch.Tensor) -> torch.Tensor:
+    """``sum(mask)`` as a float32 ``[1]`` device tensor (train.py:165)."""
+    m = mask_u8(mask)
+    dev = _require_cuda(m)
+    out = torch.empty(1, dtype=torch.float32, device=dev)
+    call("klg_count_valid", _ptr(m), m.numel(), _ptr(out), _stream(dev))
+    return out
+
+
+def fwd_stats(h_s: torch.Tensor, h_t: torch.Tensor, weight: torch.Tensor, temperature: float = 1.0) -> torch.Tensor:
+    """Pass 1 partial records ``[n_part, 5, N]`` (log2 domain) over ``weight``'s rows."""
+    dev = _require_cuda(h_s, h_t, weight)
+    N, H = h_s.shape
+    V = weight.shape[0]
+    n_part = num_partials(N, V)
+    parts = torch.empty(n_part, 5, N, dtype=torch.float32, device=dev)
+    call("klg_fwd_stats", _ptr(h_s), _ptr(h_t), _ptr(weight), N, H, V, 1.0 / float(temperature), _ptr(parts), n_part,
+         _stream(dev))
+    return parts
+
+
+def merge_stats(parts: torch.Tensor) -> torch.Tensor:
+    """Online-softmax merge ``[P, 5, N] -> [5, N]``."""
+    parts = parts.contiguous()
+    dev = _require_cuda(parts)
+    P, _, N = parts.shape
+    out = torch.empty(5, N, dtype=torch.float32, device=dev)
+    call("klg_merge_stats", _ptr(parts), P, N, _ptr(out), _stream(dev))
+    return out
+
+
+def finalize(stats: torch.Tensor, mask: torch.Tensor, count: torch.Tensor,
+             want_row_kl: bool = False) -> Tuple[torch.Tensor, torch.Tensor, Optional[torch.Tensor]]:
+    """``(loss [] fp32, lse [2, N] log2 domain, row_kl [N] or None)``."""
+    m = mask_u8(mask)
+    dev = _require_cuda(stats, m, count)
+    N = stats.shape[1]
+    loss = torch.empty((), dtype=torch.float32, device=dev)
+    lse = torch.empty(2, N, dtype=torch.float32, device=dev)
+    row_kl = torch.empty(N, dtype=torch.float32, device=dev) if want_row_kl else None
+    call("klg_finalize", _ptr(stats), _ptr(m), N, _ptr(count), _ptr(loss), _ptr(lse), _ptr(row_kl), _stream(dev))
+    return loss, lse, row_kl
+
+
+def kl_forward(h_s: torch.Tensor, h_t: torch.Tensor, weight: torch.Tensor, mask: torch.Tensor,
+               temperature: float = 1.0, count: Optional[torch.Tensor] = None, want_row_kl: bool = False):
+    """Whole forward on one device.  ``count`` (a ``[1]`` fp32 device tensor)
+    overrides the normaliser (e.g. an all-reduced global count).
+
+    Returns ``(loss, lse, count, row_kl)``.
+    """
+    m = mask_u8(mask)
+    dev = _require_cuda(h_s, h_t, weight, m)
+    N, H = h_s.shape
+    V = weight.shape[0]
+    if h_t.shape != h_s.shape or weight.shape[1] != H or m.numel() != N:
+        raise ValueError(f"shape mismatch: h_s {tuple(h_s.shape)} h_t {tuple(h_t.shape)} "
+                         f"weight {tuple(weight.shape)} mask {tuple(m.shape)}")
+    ws_bytes = int(_lib.lib().klg_fwd_workspace_bytes(N, V))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    given = count is not None
+    cnt = count if given else torch.empty(1, dtype=torch.float32, device=dev)
+    loss = torch.empty((), dtype=torch.float32, device=dev)
+    lse = torch.empty(2, N, dtype=torch.float32, device=dev)
+    row_kl = torch.empty(N, dtype=torch.float32, device=dev) if want_row_kl else None
+    call("klg_fwd", _ptr(h_s), _ptr(h_t), _ptr(weight), _ptr(m), N, H, V, 1.0 / float(temperature), int(given),
+         _ptr(cnt), _ptr(loss), _ptr(lse), _ptr(row_kl), _ptr(ws), ws_bytes, _stream(dev))
+    return loss, lse, cnt, row_kl
+
+
+def kl_backward(h_s, h_t, weight, mask, lse, count, grad: Optional[torch.Tensor] = None, temperature: float = 1.0,
+                need_dh: bool = True, need_dw: bool = True, workspace_bytes: Optional[int] = None):
+    """Pass 2: ``(dH_s [N, H] fp32 or None, dW [V, H] fp32 or None)``.
+
+    ``grad`` is the upstream gradient as a device scalar (None = 1).
+    ``workspace_bytes`` sizes the dZ chunk (default: the library's choice).
+    """
+    m = mask_u8(mask)
+    dev = _require_cuda(h_s, h_t, weight, m, lse, count)
+    N, H = h_s.shape
+    V = weight.shape[0]
+    if workspace_bytes is None:
+        workspace_bytes = int(_lib.lib().klg_bwd_workspace_bytes(N, H, V))
+    ws = torch.empty(int(workspace_bytes), dtype=torch.uint8, device=dev)
+    dh = torch.empty(N, H, dtype=torch.float32, device=dev) if need_dh else None
+    dw = torch.empty(V, H, dtype=torch.float32, device=dev) if need_dw else None
+    g = None
+    if grad is not None:
+        g = grad.detach().to(device=dev, dtype=torch.float32).reshape(1).contiguous()
+    call("klg_bwd", _ptr(h_s), _ptr(h_t), _ptr(weight), _ptr(m), _ptr(lse), _ptr(count), _ptr(g), N, H, V,
+         1.0 / float(temperature), _ptr(dh), _ptr(dw), _ptr(ws), int(workspace_bytes), _stream(dev))
+    return dh, dw
+
+
+# ----------------------------------------------------------------- autograd op
+
+class KLGemmFn(torch.autograd.Function):
+    """``loss = sum_i mask_i KL(softmax(h_t W^T / T) || softmax(h_s W^T / T)) / sum(mask)``.
+
+    Arguments: ``h_s [N, H]`` (student rows, differentiable), ``h_t [N, H]``
+    (teacher rows, treated as detached like train.py:183), ``weight [V, H]``
+    (lm_head, differentiable if it requires grad), ``mask [N]``, ``temperature``
+    (float), ``count`` (optional ``[1]`` device tensor overriding sum(mask)).
+    bf16 or fp32 inputs; compute is bf16 on the tensor cores with fp32
+    accumulation and fp32 softmax arithmetic.
+    """
+
+    @staticmethod
+    def forward(ctx, h_s, h_t, weight, mask, temperature=1.0, count=None):
+        hs = to_compute_dtype(h_s)
+        ht = to_compute_dtype(h_t)
+        w = to_compute_dtype(weight)
+        m = mask_u8(mask)
+        loss, lse, cnt, _ = kl_forward(hs, ht, w, m, temperature, count=count)
+        ctx.save_for_backward(hs, ht, w, m, lse, cnt)
+        ctx.temperature = float(temperature)
+        ctx.dtypes = (h_s.dtype, weight.dtype)
+        return loss
+
+    @staticmethod
+    def backward(ctx, g):
+        hs, ht, w, m, lse, cnt = ctx.saved_tensors
+        need_dh = ctx.needs_input_grad[0]
+        need_dw = ctx.needs_input_grad[2]
+        if not (need_dh or need_dw):
+            return None, None, None, None, None, None
+        dh, dw = kl_backward(hs, ht, w, m, lse, cnt, grad=g, temperature=ctx.temperature,
+                             need_dh=need_dh, need_dw=need_dw)
+        return (dh.to(ctx.dtypes[0]) if need_dh else None, None,
+                dw.to(ctx.dtypes[1]) if need_dw else None, None, None, None)
+
+
+def kl_gemm_loss(h_s: torch.Tensor, h_t: torch.Tensor, weight: torch.Tensor, mask: torch.Tensor,
+                 temperature: float = 1.0, count: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Fused forward-KL distillation loss on aligned rows (see :class:`KLGemmFn`)."""
+    return KLGemmFn.apply(h_s, h_t, weight, mask, temperature, count)

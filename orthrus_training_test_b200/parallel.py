@@ -1,0 +1,157 @@
+"""Multi-GPU variants of the fused KL-GEMM loss (one process per GPU).
+
+The reference is single-GPU (train.py:254); these are the two ways the loss
+shards across an 8-GPU NVLink box:
+
+Row sharding (``row_sharded_kl_loss``): each rank owns different token rows
+and a full replica of the lm_head.  Rows are independent, so the only
+exchanges are the global valid-row count (normaliser, one float), the loss
+(one float) and the lm_head gradient dW ``[V, H]`` (all-reduce, the
+data-parallel gradient exchange).  dH stays local.
+
+Vocab sharding (``vocab_sharded_kl_loss``): each rank owns all rows and one
+contiguous slice of the lm_head's rows (vocab entries).  Pass 1 yields per-row
+partial records ``(m_s, S_s, m_t, S_t, A)`` over the local slice; one
+all-gather plus the online-softmax merge gives every rank the global loss and
+log-sum-exps.  Pass 2 yields the local dW slice (complete, no exchange) and a
+partial dH that is all-reduced.
+
+The per-device arithmetic comes from an *engine*.  The product engine is
+:class:`CudaEngine` (the sm_100a library).  Tests substitute a CPU engine
+with the same interface to exercise this host logic on ``gloo`` ranks.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+
+class CudaEngine:
+    """Per-device arithmetic through the CUDA library."""
+
+    def prepare(self, x: torch.Tensor) -> torch.Tensor:
+        from .ops import to_compute_dtype
+        return to_compute_dtype(x)
+
+    def mask(self, m: torch.Tensor) -> torch.Tensor:
+        from .ops import mask_u8
+        return mask_u8(m)
+
+    def count(self, mask: torch.Tensor) -> torch.Tensor:
+        from .ops import count_valid
+        return count_valid(mask)
+
+    def forward(self, h_s, h_t, w, mask, temperature, count):
+        """Full-vocab forward with a given normaliser: ``(loss, lse)``."""
+        from .ops import kl_forward
+        loss, lse, _, _ = kl_forward(h_s, h_t, w, mask, temperature, count=count)
+        return loss, lse
+
+    def partial_stats(self, h_s, h_t, w, temperature):
+        """Merged per-row record ``[5, N]`` over ``w``'s rows."""
+        from .ops import fwd_stats, merge_stats
+        return merge_stats(fwd_stats(h_s, h_t, w, temperature))
+
+    def merge(self, parts):
+        from .ops import merge_stats
+        return merge_stats(parts)
+
+    def finalize(self, stats, mask, count):
+        from .ops import finalize
+        loss, lse, _ = finalize(stats, mask, count)
+        return loss, lse
+
+    def backward(self, h_s, h_t, w, mask, lse, count, grad, temperature, need_dh, need_dw):
+        from .ops import kl_backward
+        return kl_backward(h_s, h_t, w, mask, lse, count, grad=grad, temperature=temperature, need_dh=need_dh,
+                           need_dw=need_dw)
+
+
+def _engine(engine):
+    return engine if engine is not None else CudaEngine()
+
+
+class _RowShardedFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, h_s, h_t, weight, mask, temperature, group, engine):
+        eng = _engine(engine)
+        hs, ht, w, m = eng.prepare(h_s), eng.prepare(h_t), eng.prepare(weight), eng.mask(mask)
+        count = eng.count(m)
+        dist.all_reduce(count, op=dist.ReduceOp.SUM, group=group)      # global normaliser
+        loss, lse = eng.forward(hs, ht, w, m, temperature, count)     # sum_local valid*KL / global count
+        loss = loss.reshape(1).clone()
+        dist.all_reduce(loss, op=dist.ReduceOp.SUM, group=group)
+        ctx.save_for_backward(hs, ht, w, m, lse, count)
+        ctx.temperature, ctx.group, ctx.eng = float(temperature), group, eng
+        ctx.dtypes = (h_s.dtype, weight.dtype)
+        return loss.reshape(())
+
+    @staticmethod
+    def backward(ctx, g):
+        hs, ht, w, m, lse, count = ctx.saved_tensors
+        need_dh, need_dw = ctx.needs_input_grad[0], ctx.needs_input_grad[2]
+        dh, dw = ctx.eng.backward(hs, ht, w, m, lse, count, g, ctx.temperature, need_dh, need_dw)
+        if need_dw:
+            dist.all_reduce(dw, op=dist.ReduceOp.SUM, group=ctx.group)  # data-parallel dW exchange
+        return (dh.to(ctx.dtypes[0]) if need_dh else None, None, dw.to(ctx.dtypes[1]) if need_dw else None,
+                None, None, None, None)
+
+
+def row_sharded_kl_loss(h_s: torch.Tensor, h_t: torch.Tensor, weight: torch.Tensor, mask: torch.Tensor,
+                        temperature: float = 1.0, group: Optional[dist.ProcessGroup] = None,
+                        engine=None) -> torch.Tensor:
+    """Global loss over all ranks' rows; every rank gets the same value.
+
+    ``h_s, h_t, mask``: this rank's rows.  ``weight``: the full lm_head
+    (replicated).  Gradients: dH for the local rows; dW summed over ranks.
+    Equals the single-device loss on the concatenated rows.
+    """
+    return _RowShardedFn.apply(h_s, h_t, weight, mask, float(temperature), group, engine)
+
+
+class _VocabShardedFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, h_s, h_t, w_shard, mask, temperature, group, engine):
+        eng = _engine(engine)
+        hs, ht, w, m = eng.prepare(h_s), eng.prepare(h_t), eng.prepare(w_shard), eng.mask(mask)
+        count = eng.count(m)                                          # identical rows on every rank
+        local = eng.partial_stats(hs, ht, w, temperature).contiguous()
+        world = dist.get_world_size(group)
+        gathered = torch.empty((world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
+        dist.all_gather_into_tensor(gathered, local, group=group)     # per-row (m, S, m, S, A) partials
+        stats = eng.merge(gathered)
+        loss, lse = eng.finalize(stats, m, count)
+        ctx.save_for_backward(hs, ht, w, m, lse, count)
+        ctx.temperature, ctx.group, ctx.eng = float(temperature), group, eng
+        ctx.dtypes = (h_s.dtype, w_shard.dtype)
+        return loss
+
+    @staticmethod
+    def backward(ctx, g):
+        hs, ht, w, m, lse, count = ctx.saved_tensors
+        need_dh, need_dw = ctx.needs_input_grad[0], ctx.needs_input_grad[2]
+        dh, dw = ctx.eng.backward(hs, ht, w, m, lse, count, g, ctx.temperature, True, need_dw)
+        dist.all_reduce(dh, op=dist.ReduceOp.SUM, group=ctx.group)     # partial dH over vocab slices
+        return (dh.to(ctx.dtypes[0]) if need_dh else None, None, dw.to(ctx.dtypes[1]) if need_dw else None,
+                None, None, None, None)
+
+
+def vocab_sharded_kl_loss(h_s: torch.Tensor, h_t: torch.Tensor, weight_shard: torch.Tensor, mask: torch.Tensor,
+                          temperature: float = 1.0, group: Optional[dist.ProcessGroup] = None,
+                          engine=None) -> torch.Tensor:
+    """Loss with the lm_head split by vocab rows across ranks.
+
+    ``h_s, h_t, mask``: all rows (identical on every rank).  ``weight_shard``:
+    this rank's contiguous slice of lm_head rows.  Returns the global loss on
+    every rank; gradients: the full dH (all-reduced) and this rank's dW slice.
+    """
+    return _VocabShardedFn.apply(h_s, h_t, weight_shard, mask, float(temperature), group, engine)
+
+
+def shard_bounds(vocab: int, world: int, rank: int):
+    """Contiguous vocab slice ``[lo, hi)`` of ``rank`` (sizes differ by at most one row)."""
+    base, rem = divmod(vocab, world)
+    lo = rank * base + min(rank, rem)
+    return lo, lo + base + (1 if rank < rem else 0)
