@@ -100,6 +100,25 @@ int num_sms() {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Makes the device that owns `p` current on this host thread (binding its
+// primary context).  Callers may run on threads that never touched the CUDA
+// runtime (e.g. the autograd engine's device thread), where the driver-level
+// calls below (tensor-map encoding) would otherwise find no context.  Also
+// rejects pointers that are not device memory.
+int bind_device(const void* p) {
+  cudaPointerAttributes at;
+  cudaError_t e = cudaPointerGetAttributes(&at, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return cuda_fail(e, "cudaPointerGetAttributes");
+  }
+  if (at.type != cudaMemoryTypeDevice && at.type != cudaMemoryTypeManaged)
+    return fail(KLG_ERR_ARG, "pointer %p is not device memory", p);
+  e = cudaSetDevice(at.device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  return KLG_OK;
+}
+
 inline int cdiv(long long a, long long b) { return (int)((a + b - 1) / b); }
 
 // Work split of a dual-view launch: n_rt row tiles x n_vt vocab tiles are cut
@@ -259,6 +278,7 @@ int klg_fwd_stats(const void* hs, const void* ht, const void* w, int64_t n_rows,
   int n_uv;
   plan_dual(a.n_rt, a.n_vt, num_sms(), a.vt_per_unit, n_uv);
   if (n_part != n_uv) return fail(KLG_ERR_ARG, "n_part=%d but this device plans %d (use klg_num_partials)", n_part, n_uv);
+  if ((rc = bind_device(hs))) return rc;
   a.n_units = a.n_rt * n_uv;
   a.n_kb = cdiv(hidden, klg::BK);
   a.scale_log2 = inv_temp * 1.4426950408889634f;
@@ -273,6 +293,7 @@ int klg_fwd_stats(const void* hs, const void* ht, const void* w, int64_t n_rows,
 
 int klg_merge_stats(const float* partials, int n_part, int64_t n_rows, float* stats, void* stream) {
   if (!partials || !stats || n_part < 1 || n_rows < 1) return fail(KLG_ERR_ARG, "bad arguments to klg_merge_stats");
+  if (int rc = bind_device(partials)) return rc;
   const int slot = trace_pre((cudaStream_t)stream);
   klg::merge_kernel<<<cdiv(n_rows, 256), 256, 0, (cudaStream_t)stream>>>(partials, n_part, (int)n_rows, stats);
   cudaError_t e = cudaGetLastError();
@@ -284,6 +305,7 @@ int klg_merge_stats(const float* partials, int n_part, int64_t n_rows, float* st
 
 int klg_count_valid(const uint8_t* mask, int64_t n_rows, float* count, void* stream) {
   if (!mask || !count || n_rows < 1 || n_rows > (1ll << 30)) return fail(KLG_ERR_ARG, "bad arguments to klg_count_valid");
+  if (int rc = bind_device(mask)) return rc;
   const int slot = trace_pre((cudaStream_t)stream);
   klg::count_valid_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(mask, (int)n_rows, count);
   cudaError_t e = cudaGetLastError();
@@ -297,6 +319,7 @@ int klg_finalize(const float* stats, const uint8_t* mask, int64_t n_rows, const 
                  float* row_kl, void* stream) {
   if (!stats || !mask || !count || !loss || n_rows < 1 || n_rows > (1ll << 30))
     return fail(KLG_ERR_ARG, "bad arguments to klg_finalize");
+  if (int rc = bind_device(stats)) return rc;
   const int slot = trace_pre((cudaStream_t)stream);
   klg::finalize_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(stats, mask, (int)n_rows, count, loss, lse, row_kl);
   cudaError_t e = cudaGetLastError();
@@ -362,6 +385,7 @@ int klg_bwd(const void* hs, const void* ht, const void* w, const uint8_t* mask, 
   const int64_t cols = klg_bwd_chunk_cols(n_rows, vocab, workspace_bytes);
   if (!workspace || cols < 0 || !aligned16(workspace))
     return fail(KLG_ERR_WORKSPACE, "backward workspace too small: needs >= %lld bytes", (long long)(n_rows * 256));
+  if ((rc = bind_device(hs))) return rc;
   cudaStream_t s = (cudaStream_t)stream;
   __nv_bfloat16* dz = static_cast<__nv_bfloat16*>(workspace);
   const int bn = gemm_bn(hidden);
@@ -415,6 +439,7 @@ int klg_bwd(const void* hs, const void* ht, const void* w, const uint8_t* mask, 
 int klg_cast_f32_bf16(const float* in, void* out, int64_t n, void* stream) {
   if (!in || !out || n < 0) return fail(KLG_ERR_ARG, "bad arguments to klg_cast_f32_bf16");
   if (n == 0) return KLG_OK;
+  if (int rc = bind_device(in)) return rc;
   long long blocks = (n + 255) / 256;
   if (blocks > 148 * 32) blocks = 148 * 32;
   const int slot = trace_pre((cudaStream_t)stream);

@@ -43,6 +43,7 @@ def _require_cuda(*ts):
 def to_compute_dtype(x: torch.Tensor) -> torch.Tensor:
     """bf16, contiguous.  fp32 inputs are rounded to bf16 by the library's cast kernel."""
     x = x.detach()
+    _require_cuda(x)
     if x.dtype == torch.bfloat16:
         return x.contiguous()
     if x.dtype == torch.float32:

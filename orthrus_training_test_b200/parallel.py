@@ -119,9 +119,10 @@ class _VocabShardedFn(torch.autograd.Function):
         count = eng.count(m)                                          # identical rows on every rank
         local = eng.partial_stats(hs, ht, w, temperature).contiguous()
         world = dist.get_world_size(group)
-        gathered = torch.empty((world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
+        gathered = torch.empty((world * local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype,
+                               device=local.device)
         dist.all_gather_into_tensor(gathered, local, group=group)     # per-row (m, S, m, S, A) partials
-        stats = eng.merge(gathered)
+        stats = eng.merge(gathered.view((world,) + tuple(local.shape)))
         loss, lse = eng.finalize(stats, m, count)
         ctx.save_for_backward(hs, ht, w, m, lse, count)
         ctx.temperature, ctx.group, ctx.eng = float(temperature), group, eng

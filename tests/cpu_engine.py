@@ -1,0 +1,50 @@
+"""CPU stand-in for the CUDA engine, built on the oracle (tests only).
+
+Implements the engine interface that ``orthrus_training_test_b200.parallel``
+drives, so the multi-rank host logic (normaliser all-reduce, partial-record
+all-gather and merge, dW / dH exchanges) can run on ``gloo`` CPU ranks.
+Records are in the natural-log domain here; the product engine uses log2 --
+the format is private to each engine.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from oracle import klgemm_oracle as O
+
+
+def _np(t):
+    return t.detach().cpu().double().numpy()
+
+
+class CpuOracleEngine:
+    def prepare(self, x):
+        return x.detach().double()
+
+    def mask(self, m):
+        return (m != 0).to(torch.uint8)
+
+    def count(self, mask):
+        return mask.double().sum().reshape(1)
+
+    def forward(self, h_s, h_t, w, mask, temperature, count):
+        stats = self.partial_stats(h_s, h_t, w, temperature)
+        return self.finalize(stats, mask, count)
+
+    def partial_stats(self, h_s, h_t, w, temperature):
+        return torch.from_numpy(O.partial_stats_np(_np(h_s), _np(h_t), _np(w), temperature))
+
+    def merge(self, parts):
+        return torch.from_numpy(O.merge_partials_np(_np(parts)))
+
+    def finalize(self, stats, mask, count):
+        loss, _, ls, lt = O.finalize_np(_np(stats), _np(mask).astype(bool), float(count.item()))
+        return torch.tensor(loss, dtype=torch.float64), torch.from_numpy(np.stack([ls, lt]))
+
+    def backward(self, h_s, h_t, w, mask, lse, count, grad, temperature, need_dh, need_dw):
+        g = 1.0 if grad is None else float(grad.item())
+        L = _np(lse)
+        dh, dw = O.range_grads_np(_np(h_s), _np(h_t), _np(w), L[0], L[1], _np(mask).astype(bool),
+                                  float(count.item()), temperature, g)
+        return (torch.from_numpy(dh) if need_dh else None), (torch.from_numpy(dw) if need_dw else None)

@@ -1,0 +1,87 @@
+"""The C-ABI library loads, exports everything include/klgemm.h declares, and
+rejects bad arguments with the documented status codes (no GPU needed: every
+call here fails validation before any device work)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from orthrus_training_test_b200 import _lib
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared_functions():
+    text = (ROOT / "include" / "klgemm.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(klg_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_every_declared_symbol_is_exported():
+    L = _lib.lib()
+    names = declared_functions()
+    assert len(names) >= 15
+    for n in names:
+        assert hasattr(L, n), f"{n} declared in include/klgemm.h but not exported"
+    assert set(names) == set(_lib.SIGNATURES), "ctypes signatures out of sync with the header"
+
+
+def test_version_and_error_text():
+    L = _lib.lib()
+    assert L.klg_version() == 100
+    rc = L.klg_fwd_stats(None, None, None, 10, 64, 10, 1.0, None, 1, None)
+    assert rc == _lib.KLG_ERR_ARG
+    assert "null" in _lib.last_error()
+
+
+def _buf(nbytes, offset=0):
+    raw = ctypes.create_string_buffer(nbytes + 64)
+    base = (ctypes.addressof(raw) + 15) & ~15
+    return raw, ctypes.c_void_p(base + offset)
+
+
+def test_argument_validation_codes():
+    L = _lib.lib()
+    keep, p = _buf(1 << 16)
+    _, odd = _buf(1 << 16, offset=4)
+    # hidden not a multiple of 8 -> alignment error
+    assert L.klg_fwd_stats(p, p, p, 4, 12, 4, 1.0, p, 1, None) == _lib.KLG_ERR_ALIGN
+    # misaligned input pointer
+    assert L.klg_fwd_stats(odd, p, p, 4, 64, 4, 1.0, p, 1, None) == _lib.KLG_ERR_ALIGN
+    # bad shapes / temperature
+    assert L.klg_fwd_stats(p, p, p, 0, 64, 4, 1.0, p, 1, None) == _lib.KLG_ERR_ARG
+    assert L.klg_fwd_stats(p, p, p, 4, 64, 0, 1.0, p, 1, None) == _lib.KLG_ERR_ARG
+    assert L.klg_fwd_stats(p, p, p, 4, 64, 4, 0.0, p, 1, None) == _lib.KLG_ERR_ARG
+    assert L.klg_fwd_stats(p, p, p, 4, 64, 4, float("inf"), p, 1, None) == _lib.KLG_ERR_ARG
+    # wrong partial-record count for this problem
+    n = ctypes.c_int(0)
+    assert L.klg_num_partials(4, 4, ctypes.byref(n)) == 0 and n.value == 1
+    assert L.klg_fwd_stats(p, p, p, 4, 64, 4, 1.0, p, 7, None) == _lib.KLG_ERR_ARG
+    # workspace too small
+    assert L.klg_fwd(p, p, p, p, 4, 64, 4, 1.0, 0, p, p, p, None, p, 8, None) == _lib.KLG_ERR_WORKSPACE
+    assert L.klg_bwd(p, p, p, p, p, p, None, 4, 64, 4, 1.0, p, p, p, 100, None) == _lib.KLG_ERR_WORKSPACE
+    # null outputs
+    assert L.klg_finalize(None, p, 4, p, p, p, None, None) == _lib.KLG_ERR_ARG
+    assert L.klg_merge_stats(p, 0, 4, p, None) == _lib.KLG_ERR_ARG
+    assert L.klg_count_valid(None, 4, p, None) == _lib.KLG_ERR_ARG
+    assert L.klg_trace_begin(0) == _lib.KLG_ERR_ARG
+    # both outputs NULL: nothing to do, succeeds without touching the device
+    assert L.klg_bwd(p, p, p, p, p, p, None, 4, 64, 4, 1.0, None, None, p, 1 << 16, None) == 0
+    del keep
+
+
+@pytest.mark.parametrize("n,v,ws,expect", [(16384, 49152, 256 << 20, 8192), (1, 1, 256, 128), (300, 1500, 300 * 256, 128),
+                                           (100, 50000, 100 * 2 * 200, 128), (100, 50000, 100, -1),
+                                           (10, 1000, 1 << 30, 1024)])
+def test_backward_chunk_plan(n, v, ws, expect):
+    assert _lib.lib().klg_bwd_chunk_cols(n, v, ws) == expect
+
+
+def test_workspace_sizes_bounded():
+    L = _lib.lib()
+    # the dZ chunk stays far below a full [N, V] tensor at the benchmark sizes
+    for n, h, v in [(16384, 576, 49152), (65536, 2048, 49152), (32768, 1024, 31040), (12251, 576, 49152)]:
+        ws = L.klg_bwd_workspace_bytes(n, h, v)
+        assert 0 < ws <= 256 << 20
+        assert ws < n * v * 2 / 4

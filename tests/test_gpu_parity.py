@@ -137,8 +137,10 @@ def test_upstream_grad_scales_linearly():
     h_s, h_t, W, mask, T = rand_problem(200, 128, 600, seed=7)
     a = run_ours(h_s, h_t, W, mask, T)
     b = run_ours(h_s, h_t, W, mask, T, grad=3.0)
-    np.testing.assert_allclose(b["dh"], 3.0 * a["dh"], rtol=1e-2, atol=1e-9)
-    np.testing.assert_allclose(b["dw"], 3.0 * a["dw"], rtol=1e-2, atol=1e-9)
+    # dZ is stored in bf16, so 3*round(dz) and round(3*dz) differ by one rounding
+    for k in ("dh", "dw"):
+        mr, cos = O.grad_metrics(b[k], 3.0 * a[k])
+        assert mr < 1e-2 and cos > 0.99999, (k, mr, cos)
 
 
 def test_autograd_function_matches_oracle():

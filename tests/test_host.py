@@ -1,0 +1,49 @@
+"""Host-side logic of the drop-in shim (CPU): the row selection of
+train.py:124-139 / 156-164 that feeds the fused op."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import klgemm_oracle as O
+from orthrus_training_test_b200.loss import kl_indices, select_rows
+from tests.conftest import GOLDEN, golden_cases
+
+
+@pytest.mark.parametrize("name", golden_cases())
+def test_select_rows_matches_oracle(name):
+    g = dict(np.load(GOLDEN / f"{name}.npz"))
+    h_s, h_t, valid = select_rows(torch.tensor(g["diff_hidden"]), torch.tensor(g["ar_hidden"]),
+                                  torch.tensor(g["anchor_positions"]), int(g["K"]), torch.tensor(g["target_ids"]),
+                                  int(g["pad"]))
+    rs, rt, rv, _, _ = O.select_rows_np(g["diff_hidden"], g["ar_hidden"], g["anchor_positions"], int(g["K"]),
+                                        g["target_ids"], int(g["pad"]))
+    np.testing.assert_array_equal(h_s.numpy(), rs)
+    np.testing.assert_array_equal(h_t.numpy(), rt)
+    np.testing.assert_array_equal(valid.numpy(), rv)
+
+
+def test_indices_match_reference_layout():
+    dp, bi, off = kl_indices(3, 4, 5, "cpu")
+    rdp, rbi, roff = O.kl_indices(3, 4, 5)
+    np.testing.assert_array_equal(dp.numpy(), rdp)
+    np.testing.assert_array_equal(bi.numpy(), rbi)
+    np.testing.assert_array_equal(off.numpy(), roff)
+    # anchors (offset 0 of each block) never appear among student rows
+    assert not np.any(dp.numpy() % 5 == 0)
+
+
+def test_student_gather_is_differentiable():
+    g = dict(np.load(GOLDEN / "anchors_clamp.npz"))
+    diff = torch.tensor(g["diff_hidden"], requires_grad=True)
+    h_s, _, _ = select_rows(diff, torch.tensor(g["ar_hidden"]), torch.tensor(g["anchor_positions"]), int(g["K"]),
+                            torch.tensor(g["target_ids"]), int(g["pad"]))
+    h_s.sum().backward()
+    assert diff.grad is not None and diff.grad.sum().item() == h_s.numel()
+
+
+def test_shim_rejects_cpu_tensors():
+    """No CPU fallback: the op refuses host tensors loudly."""
+    from orthrus_training_test_b200 import kl_gemm_loss
+    x = torch.zeros(4, 64)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        kl_gemm_loss(x, x, torch.zeros(10, 64), torch.ones(4, dtype=torch.bool))
