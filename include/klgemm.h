@@ -97,6 +97,24 @@ int klg_fwd(const void* h_s, const void* h_t, const void* w, const uint8_t* mask
             int64_t vocab, float inv_temp, int count_given, float* count, float* loss, float* lse, float* row_kl,
             void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of klg_fwd (no counterpart in the reference), for
+ * callers that cannot allocate device memory: e.g. a runtime whose device
+ * memory is all reserved up front by its own allocator, or a latency-critical
+ * loop where cudaMalloc's implicit device-wide synchronisation is not allowed.
+ * Same arguments and results as klg_fwd minus the workspace: its scratch is a
+ * fixed 16 MiB array inside the library (klg_fwd_noalloc_max_floats() floats)
+ * that each GPU loading the library holds until exit; problems needing more,
+ * (n_part + 1) * 5 * n_rows floats, are rejected with KLG_ERR_WORKSPACE.  The
+ * first call on a device looks up the array's address; make it before any
+ * stream capture.  Calls share the array: calls that overlap on the GPU race.
+ * Allocates nothing. */
+int klg_fwd_noalloc(const void* h_s, const void* h_t, const void* w, const uint8_t* mask, int64_t n_rows,
+                    int64_t hidden, int64_t vocab, float inv_temp, int count_given, float* count, float* loss,
+                    float* lse, float* row_kl, void* stream);
+
+/* Scratch capacity of klg_fwd_noalloc, in floats. */
+long long klg_fwd_noalloc_max_floats(void);
+
 /* ---------------------------------------------------------------- backward
  * Replaces: autograd of train.py:202-210 (which stores bf16 [chunk, V] logits)
  * and, with the lm_head trainable, its weight gradient. */

@@ -486,3 +486,81 @@ int klg_trace_end(int* kinds, float* ms, int capacity, int* n) {
 }
 
 }  // extern "C"
+
+// ============================================================ allocation-free forward
+//
+// klg_fwd_noalloc: the forward of klg_fwd for callers that cannot allocate device
+// memory -- for example a host runtime whose device memory is entirely reserved
+// up front by its own allocator (so there is nowhere to put a workspace), or a
+// call site on a latency-critical loop where cudaMalloc's implicit device-wide
+// synchronisation is not acceptable.  Instead of a caller-provided workspace the
+// pass-1 partial records and the merged row statistics live in the file-scope
+// array below, which every GPU that loads this library keeps for the life of the
+// process (KLG_NOALLOC_SCRATCH_FLOATS floats = 16 MiB).
+//
+// Host code never uses `klg_noalloc_scratch` as an address: on the host that name
+// only stands for the device variable.  The device address is looked up once per
+// device with cudaGetSymbolAddress (with that device current) on the first call
+// made on that device, so make that first call before any stream capture.  All
+// calls share the one array and it keeps the last call's contents; nothing in it
+// needs to start at zero (every call overwrites what it reads).  Calls whose work
+// overlaps on the GPU (different streams, or several host threads) race on it.
+
+#define KLG_NOALLOC_SCRATCH_FLOATS (4ll << 20)
+
+static __device__ __align__(256) float klg_noalloc_scratch[KLG_NOALLOC_SCRATCH_FLOATS];
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device (set up on first use).
+int noalloc_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(KLG_ERR_ARG, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, klg_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(klg_noalloc_scratch)");
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return KLG_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+long long klg_fwd_noalloc_max_floats(void) { return KLG_NOALLOC_SCRATCH_FLOATS; }
+
+int klg_fwd_noalloc(const void* hs, const void* ht, const void* w, const uint8_t* mask, int64_t n_rows, int64_t hidden,
+                    int64_t vocab, float inv_temp, int count_given, float* count, float* loss, float* lse,
+                    float* row_kl, void* stream) {
+  int rc = check_problem(hs, ht, w, n_rows, hidden, vocab, inv_temp);
+  if (rc) return rc;
+  if (!mask || !count || !loss || !lse) return fail(KLG_ERR_ARG, "null output pointer");
+  int n_part = 0;
+  if ((rc = klg_num_partials(n_rows, vocab, &n_part))) return rc;
+  const long long need = (long long)(n_part + 1) * 5 * n_rows;
+  if (need > KLG_NOALLOC_SCRATCH_FLOATS)
+    return fail(KLG_ERR_WORKSPACE,
+                "klg_fwd_noalloc: %lld rows x %lld vocab needs %lld scratch floats, above its fixed %lld "
+                "(use klg_fwd with a workspace)",
+                (long long)n_rows, (long long)vocab, need, (long long)KLG_NOALLOC_SCRATCH_FLOATS);
+  if ((rc = bind_device(hs))) return rc;
+  float* parts = nullptr;
+  if ((rc = noalloc_scratch(&parts))) return rc;
+  float* stats = parts + (size_t)n_part * 5 * n_rows;
+  if (!count_given && (rc = klg_count_valid(mask, n_rows, count, stream))) return rc;
+  if ((rc = klg_fwd_stats(hs, ht, w, n_rows, hidden, vocab, inv_temp, parts, n_part, stream))) return rc;
+  if ((rc = klg_merge_stats(parts, n_part, n_rows, stats, stream))) return rc;
+  return klg_finalize(stats, mask, n_rows, count, loss, lse, row_kl, stream);
+}
+
+}  // extern "C"
