@@ -15,7 +15,7 @@
 #include <vector>
 
 #include "klg_kernels.cuh"
-#include "../../include/klgemm.h"
+#include "klgemm.h"
 
 namespace {
 
