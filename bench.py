@@ -285,8 +285,7 @@ def main():
         t = by_kind.setdefault(kind, [0.0, 0])
         t[0] += ms
         t[1] += 1
-    flops_per_step = {"stats": 4.0 * N * H * V, "dz": 4.0 * N * H * V, "gemm_dh": 2.0 * N * H * V,
-                      "gemm_dw": 2.0 * N * H * V}
+    flops_per_step = {"stats": 4.0 * N * H * V, "dz": 4.0 * N * H * V, "gemm": 4.0 * N * H * V}
     dom = max((k for k in by_kind if k in flops_per_step), key=lambda k: by_kind[k][0])
     dom_ms, dom_n = by_kind[dom]
     dom_flops_per_launch = flops_per_step[dom] * args.steps / dom_n

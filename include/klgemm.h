@@ -119,7 +119,8 @@ long long klg_fwd_noalloc_max_floats(void);
  * Replaces: autograd of train.py:202-210 (which stores bf16 [chunk, V] logits)
  * and, with the lm_head trainable, its weight gradient. */
 
-/* Recommended workspace bytes for klg_bwd (a [n_rows, C] bf16 dZ chunk). */
+/* Recommended workspace bytes for klg_bwd (4 KiB of tile counters + a [n_rows, C]
+ * bf16 dZ chunk). */
 int64_t klg_bwd_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t vocab);
 
 /* Vocab columns per backward chunk for a given workspace size (-1 if < 128). */
@@ -142,14 +143,13 @@ int klg_cast_f32_bf16(const float* in, void* out, int64_t n, void* stream);
  * Between klg_trace_begin and klg_trace_end every kernel the library launches
  * (up to `capacity`) is bracketed by two CUDA events on its stream;
  * klg_trace_end waits for them and returns each launch's kind and duration. */
-#define KLG_KIND_STATS 1
-#define KLG_KIND_DZ 2
-#define KLG_KIND_GEMM_DH 3
-#define KLG_KIND_GEMM_DW 4
-#define KLG_KIND_MERGE 5
-#define KLG_KIND_FINALIZE 6
-#define KLG_KIND_COUNT 7
-#define KLG_KIND_CAST 8
+#define KLG_KIND_STATS 1     /* pass 1: both views' logits -> per-row partial records  */
+#define KLG_KIND_DZ 2        /* pass 2: logit recompute -> dZ chunk                     */
+#define KLG_KIND_GEMM 3      /* pass 2: dW chunk = dZ^T h_s and dH += dZ W_chunk        */
+#define KLG_KIND_MERGE 4
+#define KLG_KIND_FINALIZE 5
+#define KLG_KIND_COUNT 6
+#define KLG_KIND_CAST 7
 int klg_trace_begin(int capacity);
 int klg_trace_end(int* kinds, float* ms, int capacity, int* n);
 

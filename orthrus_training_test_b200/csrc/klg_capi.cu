@@ -157,14 +157,15 @@ cudaError_t set_smem(Kern k, int bytes) {
 }
 
 template <int MODE>
-int launch_dual(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMap& mw, const klg::DualArgs& a,
-                cudaStream_t s) {
+int launch_dual(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMap& mw, const CUtensorMap& mout,
+                const klg::DualArgs& a, cudaStream_t s) {
   auto k = klg::dual_kernel<MODE>;
-  cudaError_t e = set_smem(k, klg::DUAL_SMEM);
+  constexpr int smem = klg::dual_smem(MODE);
+  cudaError_t e = set_smem(k, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dual_kernel)");
   const int grid = a.n_units < num_sms() ? a.n_units : num_sms();
   const int slot = trace_pre(s);
-  k<<<grid, klg::NUM_THREADS, klg::DUAL_SMEM, s>>>(mhs, mht, mw, a);
+  k<<<grid, klg::NUM_THREADS, smem, s>>>(mhs, mht, mw, mout, a);
   e = cudaGetLastError();
   trace_post(slot, s, MODE == klg::MODE_STATS ? KLG_KIND_STATS : KLG_KIND_DZ);
   if (e != cudaSuccess) return cuda_fail(e, "launch dual_kernel");
@@ -172,46 +173,48 @@ int launch_dual(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMa
   return KLG_OK;
 }
 
-template <bool A_MN, bool B_MN, int BN>
-int launch_gemm_t(const CUtensorMap& ma, const CUtensorMap& mb, const klg::GemmArgs& a, cudaStream_t s, int kind) {
-  auto k = klg::gemm_kernel<A_MN, B_MN, BN>;
+template <int BN>
+int launch_grouped_t(const CUtensorMap& a0, const CUtensorMap& b0, const CUtensorMap& a1, const CUtensorMap& b1,
+                     const klg::GroupedArgs& g, cudaStream_t s) {
+  auto k = klg::gemm_grouped_kernel<BN>;
   constexpr int smem = klg::GemmCfg<BN>::SMEM;
   cudaError_t e = set_smem(k, smem);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm_kernel)");
-  const int grid = a.n_tiles < num_sms() ? a.n_tiles : num_sms();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm_grouped_kernel)");
+  const int grid = g.n_tiles < num_sms() ? g.n_tiles : num_sms();
   const int slot = trace_pre(s);
-  k<<<grid, klg::NUM_THREADS, smem, s>>>(ma, mb, a);
+  k<<<grid, klg::NUM_THREADS, smem, s>>>(a0, b0, a1, b1, g);
   e = cudaGetLastError();
-  trace_post(slot, s, kind);
-  if (e != cudaSuccess) return cuda_fail(e, "launch gemm_kernel");
+  trace_post(slot, s, KLG_KIND_GEMM);
+  if (e != cudaSuccess) return cuda_fail(e, "launch gemm_grouped_kernel");
   ++g_launches;
   return KLG_OK;
 }
 
-template <bool A_MN, bool B_MN>
-int launch_gemm(int bn, const CUtensorMap& ma, const CUtensorMap& mb, const klg::GemmArgs& a, cudaStream_t s,
-                int kind) {
+int launch_grouped(int bn, const CUtensorMap& a0, const CUtensorMap& b0, const CUtensorMap& a1, const CUtensorMap& b1,
+                   const klg::GroupedArgs& g, cudaStream_t s) {
   switch (bn) {
-    case 128: return launch_gemm_t<A_MN, B_MN, 128>(ma, mb, a, s, kind);
-    case 192: return launch_gemm_t<A_MN, B_MN, 192>(ma, mb, a, s, kind);
-    default: return launch_gemm_t<A_MN, B_MN, 256>(ma, mb, a, s, kind);
+    case 128: return launch_grouped_t<128>(a0, b0, a1, b1, g, s);
+    case 192: return launch_grouped_t<192>(a0, b0, a1, b1, g, s);
+    default: return launch_grouped_t<256>(a0, b0, a1, b1, g, s);
   }
 }
 
-klg::GemmArgs gemm_args(int M, int Ncol, int K, int bn, float* C, int ldc, int accumulate, int a_k0, int b_k0) {
-  klg::GemmArgs g;
+klg::GemmProblem gemm_problem(bool on, int M, int Ncol, int K, int bn, float* C, int ldc, int accumulate, int a_k0,
+                              int b_k0, int a_mn) {
+  klg::GemmProblem g{};
   g.M = M;
   g.Ncol = Ncol;
   g.K = K;
   g.n_mt = cdiv(M, klg::BM);
   g.n_nt = cdiv(Ncol, bn);
-  g.n_tiles = g.n_mt * g.n_nt;
+  g.n_tiles = on ? g.n_mt * g.n_nt : 0;
   g.n_kb = cdiv(K, klg::BK);
   g.C = C;
   g.ldc = ldc;
   g.accumulate = accumulate;
   g.a_k0 = a_k0;
   g.b_k0 = b_k0;
+  g.a_mn = a_mn;
   return g;
 }
 
@@ -288,7 +291,7 @@ int klg_fwd_stats(const void* hs, const void* ht, const void* w, int64_t n_rows,
       !make_map(&mht, ht, hidden, n_rows, hidden, klg::BK, klg::BM) ||
       !make_map(&mw, w, hidden, vocab, hidden, klg::BK, klg::DUAL_BN))
     return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
-  return launch_dual<klg::MODE_STATS>(mhs, mht, mw, a, (cudaStream_t)stream);
+  return launch_dual<klg::MODE_STATS>(mhs, mht, mw, mw, a, (cudaStream_t)stream);
 }
 
 int klg_merge_stats(const float* partials, int n_part, int64_t n_rows, float* stats, void* stream) {
@@ -354,13 +357,17 @@ int klg_fwd(const void* hs, const void* ht, const void* w, const uint8_t* mask, 
   return klg_finalize(stats, mask, n_rows, count, loss, lse, row_kl, stream);
 }
 
+// Backward workspace: [KLG_BWD_HEADER bytes: one tile counter per chunk][dZ chunk N x C bf16].
+#define KLG_BWD_HEADER 4096
+
 int64_t klg_bwd_chunk_cols(int64_t n_rows, int64_t vocab, int64_t workspace_bytes) {
   if (n_rows < 1 || vocab < 1) return -1;
   const int64_t full = (int64_t)cdiv(vocab, 128) * 128;
-  int64_t c = workspace_bytes / (n_rows * 2);
+  int64_t c = (workspace_bytes - KLG_BWD_HEADER) / (n_rows * 2);
   c = (c / 128) * 128;
   if (c > full) c = full;
-  return c >= 128 ? c : -1;
+  if (c < 128 || cdiv(vocab, c) > KLG_BWD_HEADER / 4) return -1;
+  return c;
 }
 
 int64_t klg_bwd_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t vocab) {
@@ -371,7 +378,7 @@ int64_t klg_bwd_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t vocab) {
   cols = (cols / 128) * 128;
   if (cols < 2048) cols = 2048;
   if (cols > full) cols = full;
-  return n_rows * cols * 2;
+  return KLG_BWD_HEADER + n_rows * cols * 2;
 }
 
 int klg_bwd(const void* hs, const void* ht, const void* w, const uint8_t* mask, const float* lse, const float* count,
@@ -384,10 +391,12 @@ int klg_bwd(const void* hs, const void* ht, const void* w, const uint8_t* mask, 
   if ((d_hs && !aligned16(d_hs)) || (d_w && !aligned16(d_w))) return fail(KLG_ERR_ALIGN, "outputs must be 16-byte aligned");
   const int64_t cols = klg_bwd_chunk_cols(n_rows, vocab, workspace_bytes);
   if (!workspace || cols < 0 || !aligned16(workspace))
-    return fail(KLG_ERR_WORKSPACE, "backward workspace too small: needs >= %lld bytes", (long long)(n_rows * 256));
+    return fail(KLG_ERR_WORKSPACE, "backward workspace too small: needs >= %lld bytes",
+                (long long)(KLG_BWD_HEADER + n_rows * 256));
   if ((rc = bind_device(hs))) return rc;
   cudaStream_t s = (cudaStream_t)stream;
-  __nv_bfloat16* dz = static_cast<__nv_bfloat16*>(workspace);
+  int* counters = static_cast<int*>(workspace);
+  __nv_bfloat16* dz = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(workspace) + KLG_BWD_HEADER);
   const int bn = gemm_bn(hidden);
 
   alignas(64) CUtensorMap mhs, mht, mw, mw_mn, mhs_mn;
@@ -410,8 +419,11 @@ int klg_bwd(const void* hs, const void* ht, const void* w, const uint8_t* mask, 
   a.inv_temp = inv_temp;
   a.dz = dz;
   a.ld_dz = (int)cols;
+  const int n_chunks = cdiv(vocab, cols);
+  cudaError_t ce = cudaMemsetAsync(counters, 0, sizeof(int) * n_chunks, s);
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaMemsetAsync(tile counters)");
 
-  for (int64_t v0 = 0; v0 < vocab; v0 += cols) {
+  for (int64_t v0 = 0, ci = 0; v0 < vocab; v0 += cols, ++ci) {
     const int64_t wv = (vocab - v0) < cols ? (vocab - v0) : cols;
     a.v_begin = (int)v0;
     a.v_count = (int)wv;
@@ -419,19 +431,21 @@ int klg_bwd(const void* hs, const void* ht, const void* w, const uint8_t* mask, 
     int n_uv;
     plan_dual(a.n_rt, a.n_vt, num_sms(), a.vt_per_unit, n_uv);
     a.n_units = a.n_rt * n_uv;
-    if ((rc = launch_dual<klg::MODE_DZ>(mhs, mht, mw, a, s))) return rc;
-    if (d_hs) {
-      alignas(64) CUtensorMap mdz;
-      if (!make_map(&mdz, dz, wv, n_rows, cols, klg::BK, klg::BM)) return fail(KLG_ERR_CUDA, "tensor map (dz)");
-      klg::GemmArgs g = gemm_args((int)n_rows, (int)hidden, (int)wv, bn, d_hs, (int)hidden, v0 > 0, 0, (int)v0);
-      if ((rc = launch_gemm<false, true>(bn, mdz, mw_mn, g, s, KLG_KIND_GEMM_DH))) return rc;
-    }
-    if (d_w) {
-      alignas(64) CUtensorMap mdz_mn;
-      if (!make_map(&mdz_mn, dz, wv, n_rows, cols, 64, klg::BK)) return fail(KLG_ERR_CUDA, "tensor map (dz^T)");
-      klg::GemmArgs g = gemm_args((int)wv, (int)hidden, (int)n_rows, bn, d_w + v0 * hidden, (int)hidden, 0, 0, 0);
-      if ((rc = launch_gemm<true, true>(bn, mdz_mn, mhs_mn, g, s, KLG_KIND_GEMM_DW))) return rc;
-    }
+    alignas(64) CUtensorMap mdz_out;
+    if (!make_map(&mdz_out, dz, wv, n_rows, cols, 64, 32)) return fail(KLG_ERR_CUDA, "tensor map (dz store)");
+    if ((rc = launch_dual<klg::MODE_DZ>(mhs, mht, mw, mdz_out, a, s))) return rc;
+    // one grouped launch: problem 0 = dW chunk (longer tiles first), problem 1 = dH += dZ W_chunk
+    alignas(64) CUtensorMap mdz_k, mdz_mn;
+    if (!make_map(&mdz_k, dz, wv, n_rows, cols, klg::BK, klg::BM) || !make_map(&mdz_mn, dz, wv, n_rows, cols, 64, klg::BK))
+      return fail(KLG_ERR_CUDA, "tensor map (dz operand)");
+    klg::GroupedArgs g{};
+    g.p[0] = gemm_problem(d_w != nullptr, (int)wv, (int)hidden, (int)n_rows, bn, d_w ? d_w + v0 * hidden : nullptr,
+                          (int)hidden, 0, 0, 0, 1);
+    g.p[1] = gemm_problem(d_hs != nullptr, (int)n_rows, (int)hidden, (int)wv, bn, d_hs, (int)hidden, v0 > 0, 0,
+                          (int)v0, 0);
+    g.n_tiles = g.p[0].n_tiles + g.p[1].n_tiles;
+    g.counter = counters + ci;
+    if ((rc = launch_grouped(bn, mdz_mn, mhs_mn, mdz_k, mw_mn, g, s))) return rc;
   }
   return KLG_OK;
 }

@@ -37,7 +37,10 @@ constexpr int DUAL_BN = 128;
 constexpr int DUAL_STAGES = 4;
 constexpr int DUAL_STAGE_BYTES = 3 * TILE_128x64;  // A_s | A_t | B
 constexpr int DUAL_TMEM_COLS = 512;                // 2 buffers x (Z_s 128 | Z_t 128)
-constexpr int DUAL_SMEM = 1024 + DUAL_STAGES * DUAL_STAGE_BYTES + 256;
+constexpr int DUAL_STAGING_BYTES = 4 * 8192;          // MODE_DZ: per epilogue warp 32 rows x 128 bf16
+constexpr int dual_smem(int mode) {
+  return 1024 + DUAL_STAGES * DUAL_STAGE_BYTES + (mode == 1 ? DUAL_STAGING_BYTES : 0) + 256;
+}
 
 enum { MODE_STATS = 0, MODE_DZ = 1 };
 
@@ -94,16 +97,72 @@ __device__ __forceinline__ void drain_loads(uint32_t full0, int stage, uint32_t 
   }
 }
 
+// One 32-column chunk of the pass-1 statistics update (online max / sum-exp / KL).
+__device__ __forceinline__ void stats_chunk(const uint32_t (&bs)[32], const uint32_t (&bt)[32], int nvalid, float sl2,
+                                            float& ms, float& Ss, float& mt, float& St, float& A) {
+  float zs[32], zt[32];
+  float cms = -INFINITY, cmt = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const bool v = j < nvalid;
+    zs[j] = v ? __uint_as_float(bs[j]) * sl2 : -INFINITY;
+    zt[j] = v ? __uint_as_float(bt[j]) * sl2 : -INFINITY;
+    cms = fmaxf(cms, zs[j]);
+    cmt = fmaxf(cmt, zt[j]);
+  }
+  const float nms = fmaxf(ms, cms);
+  const float nmt = fmaxf(mt, cmt);
+  const float rs = ex2(ms - nms);
+  const float rt = ex2(mt - nmt);
+  ms = nms;
+  mt = nmt;
+  float s0 = 0.f, s1 = 0.f, t0 = 0.f, t1 = 0.f, a0 = 0.f, a1 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) {
+    s0 += ex2(zs[j] - ms);
+    s1 += ex2(zs[j + 1] - ms);
+    const float e0 = ex2(zt[j] - mt);
+    const float e1 = ex2(zt[j + 1] - mt);
+    t0 += e0;
+    t1 += e1;
+    a0 = fmaf(e0, (j < nvalid) ? zt[j] - zs[j] : 0.f, a0);
+    a1 = fmaf(e1, (j + 1 < nvalid) ? zt[j + 1] - zs[j + 1] : 0.f, a1);
+  }
+  Ss = fmaf(Ss, rs, s0 + s1);
+  St = fmaf(St, rt, t0 + t1);
+  A = fmaf(A, rt, a0 + a1);
+}
+
+// One 32-column chunk of dZ = coef * (2^(u_s - L_s) - 2^(u_t - L_t)) as 16 bf16 pairs.
+__device__ __forceinline__ void dz_chunk(const uint32_t (&bs)[32], const uint32_t (&bt)[32], float sl2, float Ls,
+                                         float Lt, float coef, uint32_t (&pk)[16]) {
+  if (coef == 0.f) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) pk[j] = 0u;
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) {
+    const float q0 = ex2(fmaf(__uint_as_float(bs[j]), sl2, -Ls));
+    const float q1 = ex2(fmaf(__uint_as_float(bs[j + 1]), sl2, -Ls));
+    const float p0 = ex2(fmaf(__uint_as_float(bt[j]), sl2, -Lt));
+    const float p1 = ex2(fmaf(__uint_as_float(bt[j + 1]), sl2, -Lt));
+    pk[j / 2] = pack_bf16x2(coef * (q0 - p0), coef * (q1 - p1));
+  }
+}
+
+// map_out (MODE_DZ only): the dZ chunk [N][v_count] with row stride ld_dz, box 64 x 32.
 template <int MODE>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ CUtensorMap map_ht,
-            const __grid_constant__ CUtensorMap map_w, const DualArgs a) {
+            const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_out, const DualArgs a) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t bar0 = sbase + DUAL_STAGES * DUAL_STAGE_BYTES;
+  const uint32_t stg0 = sbase + DUAL_STAGES * DUAL_STAGE_BYTES;  // MODE_DZ staging (1024-aligned)
+  const uint32_t bar0 = stg0 + (MODE == MODE_DZ ? DUAL_STAGING_BYTES : 0);
   const uint32_t full0 = bar0;                          // [STAGES]
   const uint32_t empty0 = bar0 + 8u * DUAL_STAGES;      // [STAGES]
   const uint32_t tfull0 = bar0 + 16u * DUAL_STAGES;     // [2]
@@ -206,6 +265,7 @@ dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ 
     const int q = warp & 3;                 // TMEM lane quarter of this warp
     const int r_in_tile = q * 32 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+    const uint32_t stg = stg0 + (uint32_t)(warp - EPI_WARP0) * 8192u;  // this warp's dZ staging (2 x 4 KB)
     int tcount = 0;
     bool ok = true;
     for (int u = blockIdx.x; ok && u < a.n_units; u += gridDim.x) {
@@ -228,75 +288,62 @@ dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ 
         const uint32_t tph = (tcount >> 1) & 1;
         if (!mbar_wait(tfull0 + 8u * buf, tph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) { ok = false; break; }
         tc_fence_after();
+        if (MODE == MODE_DZ) {
+          if (lane == 0) bulk_wait_read0();   // staging free: previous tile's stores have read it
+          __syncwarp();
+        }
+        const uint32_t tbase = lane_addr + buf * 256;
+        if (MODE == MODE_STATS) {
+          // load -> wait -> update per 32-column chunk
 #pragma unroll 1
-        for (int c = 0; c < DUAL_BN / 32; ++c) {
-          float zs[32], zt[32];
-          tmem_ld32(lane_addr + buf * 256 + c * 32, zs);
-          tmem_ld32(lane_addr + buf * 256 + 128 + c * 32, zt);
-          tmem_wait_ld();
-          const int col0 = vt * DUAL_BN + c * 32;      // relative to v_begin
-          const int nvalid = min(32, a.v_count - col0);
-          if (nvalid <= 0) continue;
-          if (MODE == MODE_STATS) {
-            float cms = -INFINITY, cmt = -INFINITY;
+          for (int c = 0; c < DUAL_BN / 32; ++c) {
+            uint32_t bs[32], bt[32];
+            tmem_ld32_raw(tbase + c * 32, bs);
+            tmem_ld32_raw(tbase + 128 + c * 32, bt);
+            tmem_wait_ld_regs(bs, bt);
+            const int nvalid = min(32, a.v_count - (vt * DUAL_BN + c * 32));
+            if (nvalid > 0) stats_chunk(bs, bt, nvalid, a.scale_log2, ms, Ss, mt, St, A);
+          }
+        } else {
+          // TMEM reads software-pipelined: chunk c+1 is in flight while chunk c is processed.
+          uint32_t bs[2][32], bt[2][32];
+          tmem_ld32_raw(tbase, bs[0]);
+          tmem_ld32_raw(tbase + 128, bt[0]);
+          tmem_wait_ld_regs(bs[0], bt[0]);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const bool v = j < nvalid;
-              zs[j] = v ? zs[j] * a.scale_log2 : -INFINITY;
-              zt[j] = v ? zt[j] * a.scale_log2 : -INFINITY;
-              cms = fmaxf(cms, zs[j]);
-              cmt = fmaxf(cmt, zt[j]);
+          for (int c = 0; c < DUAL_BN / 32; ++c) {
+            const int cur = c & 1;
+            if (c + 1 < DUAL_BN / 32) {
+              tmem_ld32_raw(tbase + (c + 1) * 32, bs[cur ^ 1]);
+              tmem_ld32_raw(tbase + 128 + (c + 1) * 32, bt[cur ^ 1]);
             }
-            const float nms = fmaxf(ms, cms);
-            const float nmt = fmaxf(mt, cmt);
-            const float rs = ex2(ms - nms);
-            const float rt_ = ex2(mt - nmt);
-            ms = nms;
-            mt = nmt;
-            float s0 = 0.f, s1 = 0.f, t0 = 0.f, t1 = 0.f, a0 = 0.f, a1 = 0.f;
+            if (vt * DUAL_BN + c * 32 < a.v_count) {
+              uint32_t pk[16];
+              dz_chunk(bs[cur], bt[cur], a.scale_log2, Ls, Lt, coef, pk);
+              // 128-byte-swizzled staging row: 16-byte chunk j of row r lives at chunk j ^ (r % 8)
+              const uint32_t rowp = stg + (uint32_t)(c >> 1) * 4096u + (uint32_t)lane * 128u;
 #pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-              s0 += ex2(zs[j] - ms);
-              s1 += ex2(zs[j + 1] - ms);
-              const float e0 = ex2(zt[j] - mt);
-              const float e1 = ex2(zt[j + 1] - mt);
-              t0 += e0;
-              t1 += e1;
-              a0 = fmaf(e0, (j < nvalid) ? zt[j] - zs[j] : 0.f, a0);
-              a1 = fmaf(e1, (j + 1 < nvalid) ? zt[j + 1] - zs[j + 1] : 0.f, a1);
-            }
-            Ss = fmaf(Ss, rs, s0 + s1);
-            St = fmaf(St, rt_, t0 + t1);
-            A = fmaf(A, rt_, a0 + a1);
-          } else {
-            if (!row_ok) continue;
-            __nv_bfloat16* dst = a.dz + (size_t)row * a.ld_dz + col0;
-            uint32_t pk[16];
-            if (coef == 0.f) {
-#pragma unroll
-              for (int j = 0; j < 16; ++j) pk[j] = 0u;
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; j += 2) {
-                const float q0 = ex2(fmaf(zs[j], a.scale_log2, -Ls));
-                const float q1 = ex2(fmaf(zs[j + 1], a.scale_log2, -Ls));
-                const float p0 = ex2(fmaf(zt[j], a.scale_log2, -Lt));
-                const float p1 = ex2(fmaf(zt[j + 1], a.scale_log2, -Lt));
-                pk[j / 2] = pack_bf16x2(coef * (q0 - p0), coef * (q1 - p1));
+              for (int k = 0; k < 4; ++k) {
+                const uint32_t j = (uint32_t)((c & 1) * 4 + k);
+                st_shared_v4(rowp + ((j ^ (uint32_t)(lane & 7)) << 4), pk[4 * k], pk[4 * k + 1], pk[4 * k + 2],
+                             pk[4 * k + 3]);
               }
             }
-            if (nvalid == 32) {
-              uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-              for (int j = 0; j < 4; ++j) d4[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-            } else {
-              unsigned short* d2 = reinterpret_cast<unsigned short*>(dst);
-              for (int j = 0; j < nvalid; ++j) d2[j] = (unsigned short)((pk[j >> 1] >> ((j & 1) * 16)) & 0xFFFFu);
-            }
+            if (c + 1 < DUAL_BN / 32) tmem_wait_ld_regs(bs[cur ^ 1], bt[cur ^ 1]);
           }
         }
         tc_fence_before();
         mbar_arrive(tempty0 + 8u * buf);
+        if (MODE == MODE_DZ) {
+          fence_async_shared();
+          __syncwarp();
+          const int x0 = vt * DUAL_BN, y0 = rt * BM + q * 32;
+          if (lane == 0 && y0 < a.n_rows) {
+            tma_store_2d(&map_out, stg, x0, y0);
+            if (x0 + 64 < a.v_count) tma_store_2d(&map_out, stg + 4096, x0 + 64, y0);
+            bulk_commit();
+          }
+        }
       }
       if (MODE == MODE_STATS && ok && row_ok) {
         float* p = a.partials + (size_t)uv * 5 * a.n_rows + row;
@@ -307,6 +354,7 @@ dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ 
         p[(size_t)4 * a.n_rows] = A;
       }
     }
+    if (MODE == MODE_DZ && lane == 0) bulk_wait0();   // dZ stores complete before exit
   }
   tc_fence_before();
   __syncthreads();
@@ -315,15 +363,248 @@ dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ 
 }
 
 // =====================================================================================
-// generic GEMM: C[M][Ncol] (+)= A[M][K] * B[K][Ncol], bf16 in, fp32 out
+// pass-1 log-sum-exp on CTA pairs (training path)
+//
+// One view at a time (student rows, then teacher rows): per unit (view, 256-row pair
+// tile, vocab range) the pair computes 256 x 256 logit tiles with
+// tcgen05.mma.cta_group::2 (each CTA: its own 128 rows as A, its half of the W tile as
+// B) into double-buffered TMEM, and 8 epilogue warps per CTA (two per TMEM lane
+// quarter, one per 128-column half) keep online (m, S) per row.  Output: partial
+// records parts[n_uv * 2 halves][2][2N] = (m, S) in log2 units, row index view*N + row.
+// The KL cross term is accumulated by the dZ pass, which has both views' values.
 // =====================================================================================
-struct GemmArgs {
+constexpr int LSE_BN = 256;                                // vocab rows per pair tile
+constexpr int LSE_STAGES = 6;
+constexpr int LSE_A_BYTES = TILE_128x64;                   // this CTA's 128 rows x 64
+constexpr int LSE_B_BYTES = (LSE_BN / 2) * BK * 2;         // this CTA's half of the W tile
+constexpr int LSE_STAGE_BYTES = LSE_A_BYTES + LSE_B_BYTES; // 32 KB
+constexpr int LSE_EPI_WARPS = 8;
+constexpr int LSE_THREADS = 64 + 32 * LSE_EPI_WARPS;
+constexpr int LSE_TMEM_COLS = 512;                         // 2 buffers x 256 columns
+constexpr int LSE_SMEM = 1024 + LSE_STAGES * LSE_STAGE_BYTES + 256;
+
+struct LseArgs {
+  int n_rows;       // N rows per view
+  int vocab;        // V
+  int n_rp;         // ceil(N / 256)
+  int n_vt;         // ceil(V / 256)
+  int vt_per_unit;
+  int n_uv;         // ceil(n_vt / vt_per_unit)
+  int n_units;      // 2 * n_rp * n_uv
+  int n_kb;         // ceil(H / 64)
+  float scale_log2; // log2(e) / T
+  float* parts;     // [n_uv * 2][2][2N]
+};
+
+__device__ __forceinline__ void lse_unit(const LseArgs& a, int u, int& view, int& rp, int& uv, int& vt0, int& vt1) {
+  const int per_uv = 2 * a.n_rp;
+  uv = u / per_uv;
+  const int r = u % per_uv;
+  view = r / a.n_rp;
+  rp = r % a.n_rp;
+  vt0 = uv * a.vt_per_unit;
+  vt1 = min(vt0 + a.vt_per_unit, a.n_vt);
+}
+
+// Online (m, S) update of one 32-column chunk, log2 units.
+__device__ __forceinline__ void lse_chunk(const uint32_t (&b)[32], int nvalid, float sl2, float& m, float& S) {
+  float cm = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) cm = fmaxf(cm, j < nvalid ? __uint_as_float(b[j]) : -INFINITY);
+  const float nm = fmaxf(m, cm * sl2);
+  const float r = ex2(m - nm);
+  m = nm;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    s0 += j < nvalid ? ex2(fmaf(__uint_as_float(b[j]), sl2, -m)) : 0.f;
+    s1 += j + 1 < nvalid ? ex2(fmaf(__uint_as_float(b[j + 1]), sl2, -m)) : 0.f;
+    s2 += j + 2 < nvalid ? ex2(fmaf(__uint_as_float(b[j + 2]), sl2, -m)) : 0.f;
+    s3 += j + 3 < nvalid ? ex2(fmaf(__uint_as_float(b[j + 3]), sl2, -m)) : 0.f;
+  }
+  S = fmaf(S, r, (s0 + s1) + (s2 + s3));
+}
+
+__global__ void __launch_bounds__(LSE_THREADS, 1)
+lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ CUtensorMap map_ht,
+                const __grid_constant__ CUtensorMap map_w, const LseArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + LSE_STAGES * LSE_STAGE_BYTES;
+  const uint32_t full0 = bar0;                         // [STAGES] leader only: both CTAs' bytes
+  const uint32_t empty0 = bar0 + 8u * LSE_STAGES;      // [STAGES] each CTA
+  const uint32_t tfull0 = bar0 + 16u * LSE_STAGES;     // [2] each CTA
+  const uint32_t tempty0 = tfull0 + 16u;               // [2] leader only: 16 warp arrivals
+  const uint32_t done_bar = tempty0 + 16u;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int cid = blockIdx.x >> 1;
+  const int n_clusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < LSE_STAGES; ++s) {
+      mbar_init(full0 + 8u * s, 2);
+      mbar_init(empty0 + 8u * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull0 + 8u * b, 1);
+      mbar_init(tempty0 + 8u * b, 2 * LSE_EPI_WARPS);
+    }
+    mbar_init(done_bar, 1);
+    fence_mbar_init();
+    tma_prefetch(&map_hs);
+    tma_prefetch(&map_ht);
+    tma_prefetch(&map_w);
+  }
+  if (warp == 1) tmem_alloc_pair(smem_u32(&tmem_slot), LSE_TMEM_COLS);
+  tc_fence_before();
+  cluster_sync();   // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  volatile int* abort_p = &abort_flag;
+  const uint32_t lead_full0 = mapa_shared(full0, 0);
+  const uint32_t lead_tempty0 = mapa_shared(tempty0, 0);
+  const uint32_t peer_empty0 = mapa_shared(empty0, 1);
+  const uint32_t peer_tfull0 = mapa_shared(tfull0, 1);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA producer (both CTAs)
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      for (int u = cid; ok && u < a.n_units; u += n_clusters) {
+        int view, rp, uv, vt0, vt1;
+        lse_unit(a, u, view, rp, uv, vt0, vt1);
+        const CUtensorMap* ma = view ? &map_ht : &map_hs;
+        const int row0 = rp * 256 + (int)rank * 128;
+        for (int vt = vt0; ok && vt < vt1; ++vt) {
+          for (int kb = 0; kb < a.n_kb; ++kb) {
+            if (!mbar_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
+            const uint32_t sa = sbase + stage * LSE_STAGE_BYTES;
+            const uint32_t fb = lead_full0 + 8u * stage;
+            if (leader) mbar_arrive_expect_tx(full0 + 8u * stage, 2 * LSE_STAGE_BYTES);
+            tma_load_2d_pair(sa, ma, fb, kb * BK, row0);
+            tma_load_2d_pair(sa + LSE_A_BYTES, &map_w, fb, kb * BK, vt * LSE_BN + (int)rank * (LSE_BN / 2));
+            if (!leader) mbar_arrive_cluster(fb);
+            ++issued;
+            if (++stage == LSE_STAGES) { stage = 0; phase ^= 1; }
+          }
+        }
+      }
+      if (leader) drain_loads<LSE_STAGES>(full0, stage, phase, issued);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ------------------------------------------------------------ pair MMA issuer (leader)
+      constexpr uint32_t idesc = make_idesc_bf16(2 * BM, LSE_BN, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      int tcount = 0;
+      bool ok = true;
+      for (int u = cid; ok && u < a.n_units; u += n_clusters) {
+        int view, rp, uv, vt0, vt1;
+        lse_unit(a, u, view, rp, uv, vt0, vt1);
+        for (int vt = vt0; ok && vt < vt1; ++vt, ++tcount) {
+          const int buf = tcount & 1;
+          const uint32_t tph = (tcount >> 1) & 1;
+          if (!mbar_wait(tempty0 + 8u * buf, tph ^ 1, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d = tmem + buf * LSE_BN;
+          for (int kb = 0; kb < a.n_kb; ++kb) {
+            if (!mbar_wait(full0 + 8u * stage, phase, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t sa = sbase + stage * LSE_STAGE_BYTES;
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)
+              mma_bf16_pair(d, desc_kmajor(sa, k), desc_kmajor(sa + LSE_A_BYTES, k), idesc, (kb | k) != 0);
+            mma_commit_pair(empty0 + 8u * stage);
+            mma_commit_pair(peer_empty0 + 8u * stage);
+            if (++stage == LSE_STAGES) { stage = 0; phase ^= 1; }
+          }
+          if (ok) {
+            mma_commit_pair(tfull0 + 8u * buf);
+            mma_commit_pair(peer_tfull0 + 8u * buf);
+          }
+        }
+      }
+      mma_commit_pair(done_bar);
+      mbar_wait_drain(done_bar, 0);
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue (both CTAs)
+    const int q = warp & 3;
+    const int h = (warp - EPI_WARP0) >> 2;        // 128-column half of the 256-column tile
+    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 128);
+    int tcount = 0;
+    bool ok = true;
+    for (int u = cid; ok && u < a.n_units; u += n_clusters) {
+      int view, rp, uv, vt0, vt1;
+      lse_unit(a, u, view, rp, uv, vt0, vt1);
+      const int row = rp * 256 + (int)rank * 128 + q * 32 + lane;
+      float m = NEG_BIG, S = 0.f;
+      for (int vt = vt0; ok && vt < vt1; ++vt, ++tcount) {
+        const int buf = tcount & 1;
+        const uint32_t tph = (tcount >> 1) & 1;
+        if (!mbar_wait(tfull0 + 8u * buf, tph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) { ok = false; break; }
+        tc_fence_after();
+        const int col_base = vt * LSE_BN + h * 128;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t b0[32];
+          tmem_ld32_raw(lane_addr + buf * LSE_BN + c * 32, b0);
+          tmem_wait_ld_regs(b0);
+          const int nvalid = min(32, a.vocab - (col_base + c * 32));
+          if (nvalid > 0) lse_chunk(b0, nvalid, a.scale_log2, m, S);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (leader) mbar_arrive(tempty0 + 8u * buf);
+          else mbar_arrive_cluster(lead_tempty0 + 8u * buf);
+        }
+      }
+      if (ok && row < a.n_rows) {
+        const size_t n2 = 2 * (size_t)a.n_rows;
+        float* p = a.parts + ((size_t)(uv * 2 + h) * 2) * n2 + (size_t)view * a.n_rows + row;
+        p[0] = m;
+        p[n2] = S;
+      }
+    }
+  }
+  tc_fence_before();
+  cluster_sync();   // all pair MMAs retired and both epilogues done before TMEM is released
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem, LSE_TMEM_COLS);
+}
+
+// =====================================================================================
+// grouped GEMM for the backward chunk: dW_chunk = dZ^T h_s and dH (+)= dZ W_chunk in one
+// persistent launch.  C[M][Ncol] (+)= A[M][K] * B[K][Ncol], bf16 in, fp32 out; B is
+// MN-major for both problems; A is MN-major for dW (dZ^T) and K-major for dH (dZ).
+// Tiles are handed out dynamically (global atomic counter) with the longer dW tiles first,
+// so SMs that finish early pick up the remaining work (greedy longest-first).
+// =====================================================================================
+struct GemmProblem {
   int M, Ncol, K;
   int n_mt, n_nt, n_tiles, n_kb;
   float* C;
   int ldc;
   int accumulate;   // 1: C += A*B, 0: C = A*B
   int a_k0, b_k0;   // K coordinate of the first k-block in A's and B's tensor maps
+  int a_mn;         // A stored [K][M] (M contiguous) instead of [M][K]
+};
+struct GroupedArgs {
+  GemmProblem p[2];
+  int n_tiles;      // p[0].n_tiles + p[1].n_tiles
+  int* counter;     // zero before the launch
 };
 
 template <int BN>
@@ -333,20 +614,29 @@ struct GemmCfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (BN >= 192) ? 4 : 6;
   static constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
-  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 256;
+  static constexpr int SCHED = 4;   // tile-index ring depth
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 512;
 };
 
-// A_MN: A stored [K][M] (M contiguous), loaded as two 64-wide boxes.
-// B_MN: B stored [K][Ncol] (Ncol contiguous), loaded as BN/64 boxes; otherwise
-//       B stored [Ncol][K] (K contiguous) and loaded as one 64 x BN box.
-template <bool A_MN, bool B_MN, int BN>
+__device__ __forceinline__ void grouped_tile(const GroupedArgs& g, int t, int& pi, int& mt, int& nt) {
+  pi = t < g.p[0].n_tiles ? 0 : 1;
+  const int lt = pi ? t - g.p[0].n_tiles : t;
+  mt = lt / g.p[pi].n_nt;
+  nt = lt % g.p[pi].n_nt;
+}
+
+template <int BN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, const GemmArgs a) {
+gemm_grouped_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_b0,
+                    const __grid_constant__ CUtensorMap map_a1, const __grid_constant__ CUtensorMap map_b1,
+                    const GroupedArgs g) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
+  constexpr int SCHED = Cfg::SCHED;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
+  __shared__ int tile_ring[SCHED];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + STAGES * Cfg::STAGE_BYTES;
@@ -355,6 +645,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ C
   const uint32_t tfull0 = bar0 + 16u * STAGES;
   const uint32_t tempty0 = tfull0 + 16u;
   const uint32_t done_bar = tempty0 + 16u;
+  const uint32_t sfull0 = done_bar + 8u;               // [SCHED] tile index published
+  const uint32_t sempty0 = sfull0 + 8u * SCHED;        // [SCHED] tile index consumed (MMA + 4 epilogue warps)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
@@ -369,9 +661,15 @@ gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ C
       mbar_init(tempty0 + 8u * b, 4 * 32);
     }
     mbar_init(done_bar, 1);
+    for (int s = 0; s < SCHED; ++s) {
+      mbar_init(sfull0 + 8u * s, 1);
+      mbar_init(sempty0 + 8u * s, 1 + 4);
+    }
     fence_mbar_init();
-    tma_prefetch(&map_a);
-    tma_prefetch(&map_b);
+    tma_prefetch(&map_a0);
+    tma_prefetch(&map_b0);
+    tma_prefetch(&map_a1);
+    tma_prefetch(&map_b1);
   }
   if (warp == 1) tmem_alloc(smem_u32(&tmem_slot), Cfg::TMEM_COLS);
   tc_fence_before();
@@ -379,34 +677,43 @@ gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ C
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
   volatile int* abort_p = &abort_flag;
+  volatile int* ring = tile_ring;
 
   if (warp == 0) {
     if (lane == 0) {
+      // ------------------------------------------------------------ scheduler + TMA producer
       int stage = 0;
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < a.n_tiles; t += gridDim.x) {
-        const int mt = t / a.n_nt, nt = t % a.n_nt;
-        for (int kb = 0; kb < a.n_kb; ++kb) {
+      for (int k = 0; ok; ++k) {
+        const int slot = k % SCHED;
+        const uint32_t sph = (uint32_t)(k / SCHED) & 1u;
+        if (!mbar_wait(sempty0 + 8u * slot, sph ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) break;
+        const int t = atomicAdd(g.counter, 1);
+        ring[slot] = t;
+        mbar_arrive(sfull0 + 8u * slot);
+        if (t >= g.n_tiles) break;
+        int pi, mt, nt;
+        grouped_tile(g, t, pi, mt, nt);
+        const GemmProblem& P = g.p[pi];
+        const CUtensorMap* ma = pi ? &map_a1 : &map_a0;
+        const CUtensorMap* mb = pi ? &map_b1 : &map_b0;
+        for (int kb = 0; kb < P.n_kb; ++kb) {
           if (!mbar_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
           const uint32_t sa = sbase + stage * Cfg::STAGE_BYTES;
           const uint32_t sb = sa + Cfg::A_BYTES;
           const uint32_t fb = full0 + 8u * stage;
           mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
-          const int ka = a.a_k0 + kb * BK, kbb = a.b_k0 + kb * BK;
-          if (A_MN) {
-            tma_load_2d(sa, &map_a, fb, mt * BM, ka);
-            tma_load_2d(sa + 8192, &map_a, fb, mt * BM + 64, ka);
+          const int ka = P.a_k0 + kb * BK, kbb = P.b_k0 + kb * BK;
+          if (P.a_mn) {
+            tma_load_2d(sa, ma, fb, mt * BM, ka);
+            tma_load_2d(sa + 8192, ma, fb, mt * BM + 64, ka);
           } else {
-            tma_load_2d(sa, &map_a, fb, ka, mt * BM);
+            tma_load_2d(sa, ma, fb, ka, mt * BM);
           }
-          if (B_MN) {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + 8192 * j, &map_b, fb, nt * BN + 64 * j, kbb);
-          } else {
-            tma_load_2d(sb, &map_b, fb, kbb, nt * BN);
-          }
+          for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + 8192 * j, mb, fb, nt * BN + 64 * j, kbb);
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -415,27 +722,38 @@ gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ C
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16(BM, BN, A_MN, B_MN);
+      // ------------------------------------------------------------ MMA issuer
+      constexpr uint32_t idesc_kmaj = make_idesc_bf16(BM, BN, false, true);
+      constexpr uint32_t idesc_mnmaj = make_idesc_bf16(BM, BN, true, true);
       int stage = 0;
       uint32_t phase = 0;
-      int tcount = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < a.n_tiles; t += gridDim.x, ++tcount) {
-        const int buf = tcount & 1;
-        const uint32_t tph = (tcount >> 1) & 1;
-        if (!mbar_wait(tempty0 + 8u * buf, tph ^ 1, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
+      for (int k = 0; ok; ++k) {
+        const int slot = k % SCHED;
+        const uint32_t sph = (uint32_t)(k / SCHED) & 1u;
+        if (!mbar_wait(sfull0 + 8u * slot, sph, abort_p, KLG_STATUS_TIMEOUT_MMA)) break;
+        const int t = ring[slot];
+        mbar_arrive(sempty0 + 8u * slot);
+        if (t >= g.n_tiles) break;
+        int pi, mt, nt;
+        grouped_tile(g, t, pi, mt, nt);
+        const GemmProblem& P = g.p[pi];
+        const bool amn = P.a_mn != 0;
+        const uint32_t idesc = amn ? idesc_mnmaj : idesc_kmaj;
+        const int buf = k & 1;
+        const uint32_t tph = (uint32_t)(k >> 1) & 1u;
+        if (!mbar_wait(tempty0 + 8u * buf, tph ^ 1, abort_p, KLG_STATUS_TIMEOUT_MMA)) break;
         tc_fence_after();
         const uint32_t d = tmem + buf * BN;
-        for (int kb = 0; kb < a.n_kb; ++kb) {
+        for (int kb = 0; kb < P.n_kb; ++kb) {
           if (!mbar_wait(full0 + 8u * stage, phase, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = sbase + stage * Cfg::STAGE_BYTES;
           const uint32_t sb = sa + Cfg::A_BYTES;
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t ad = A_MN ? desc_mnmajor(sa, k) : desc_kmajor(sa, k);
-            const uint64_t bd = B_MN ? desc_mnmajor(sb, k) : desc_kmajor(sb, k);
-            mma_bf16(d, ad, bd, idesc, (kb | k) != 0);
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = amn ? desc_mnmajor(sa, kk) : desc_kmajor(sa, kk);
+            mma_bf16(d, ad, desc_mnmajor(sb, kk), idesc, (kb | kk) != 0);
           }
           mma_commit(empty0 + 8u * stage);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -446,38 +764,54 @@ gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ C
       mbar_wait_drain(done_bar, 0);
     }
   } else {
+    // -------------------------------------------------------------- epilogue
     const int q = warp & 3;
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
-    int tcount = 0;
-    for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x, ++tcount) {
-      const int mt = t / a.n_nt, nt = t % a.n_nt;
-      const int buf = tcount & 1;
-      const uint32_t tph = (tcount >> 1) & 1;
+    for (int k = 0;; ++k) {
+      const int slot = k % SCHED;
+      const uint32_t sph = (uint32_t)(k / SCHED) & 1u;
+      int t = 0;
+      if (lane == 0) {
+        if (!mbar_wait(sfull0 + 8u * slot, sph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) t = -1;
+        else {
+          t = ring[slot];
+          mbar_arrive(sempty0 + 8u * slot);
+        }
+      }
+      t = __shfl_sync(0xffffffffu, t, 0);
+      if (t < 0 || t >= g.n_tiles) break;
+      int pi, mt, nt;
+      grouped_tile(g, t, pi, mt, nt);
+      const GemmProblem& P = g.p[pi];
+      const int buf = k & 1;
+      const uint32_t tph = (uint32_t)(k >> 1) & 1u;
       if (!mbar_wait(tfull0 + 8u * buf, tph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const int row = mt * BM + q * 32 + lane;
-      const bool row_ok = row < a.M;
-      float* crow = a.C + (size_t)row * a.ldc;
+      const bool row_ok = row < P.M;
+      float* crow = P.C + (size_t)(row_ok ? row : 0) * P.ldc;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         float v[32];
         tmem_ld32(lane_addr + buf * BN + c * 32, v);
         tmem_wait_ld();
         const int col0 = nt * BN + c * 32;
-        if (!row_ok || col0 >= a.Ncol) continue;
-        if (col0 + 32 <= a.Ncol) {
+        if (!row_ok || col0 >= P.Ncol) continue;
+        if (col0 + 32 <= P.Ncol) {
           float4* d4 = reinterpret_cast<float4*>(crow + col0);
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-            if (a.accumulate) {
+            if (P.accumulate) {
               const float4 old = d4[j];
               o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
             }
             d4[j] = o;
           }
         } else {
-          for (int j = 0; j < a.Ncol - col0; ++j) crow[col0 + j] = a.accumulate ? crow[col0 + j] + v[j] : v[j];
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < P.Ncol) crow[col0 + j] = P.accumulate ? crow[col0 + j] + v[j] : v[j];
         }
       }
       tc_fence_before();

@@ -71,9 +71,13 @@ def test_argument_validation_codes():
     del keep
 
 
-@pytest.mark.parametrize("n,v,ws,expect", [(16384, 49152, 256 << 20, 8192), (1, 1, 256, 128), (300, 1500, 300 * 256, 128),
-                                           (100, 50000, 100 * 2 * 200, 128), (100, 50000, 100, -1),
-                                           (10, 1000, 1 << 30, 1024)])
+HDR = 4096  # tile counters ahead of the dZ chunk
+
+
+@pytest.mark.parametrize("n,v,ws,expect", [(16384, 49152, HDR + 16384 * 8192 * 2, 8192), (1, 1, HDR + 256, 128),
+                                           (300, 1500, HDR + 300 * 256, 128), (100, 50000, HDR + 100 * 2 * 200, 128),
+                                           (100, 50000, 100, -1), (10, 1000, 1 << 30, 1024),
+                                           (10, 128 * 2000, HDR + 10 * 256, -1)])  # > 1024 chunks
 def test_backward_chunk_plan(n, v, ws, expect):
     assert _lib.lib().klg_bwd_chunk_cols(n, v, ws) == expect
 
@@ -83,5 +87,6 @@ def test_workspace_sizes_bounded():
     # the dZ chunk stays far below a full [N, V] tensor at the benchmark sizes
     for n, h, v in [(16384, 576, 49152), (65536, 2048, 49152), (32768, 1024, 31040), (12251, 576, 49152)]:
         ws = L.klg_bwd_workspace_bytes(n, h, v)
-        assert 0 < ws <= 256 << 20
+        assert 0 < ws <= (256 << 20) + HDR
+        assert _lib.lib().klg_bwd_chunk_cols(n, v, ws) >= 2048
         assert ws < n * v * 2 / 4
