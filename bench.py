@@ -2,9 +2,10 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c2]
 
-One step = the full loss path over one batch of rows: valid-row count, pass 1
-(both views' logits over all vocab tiles with online max/sum-exp/KL), merge,
-finalize (loss), pass 2 (logit recompute -> dZ chunks -> dH and dW GEMMs).
+One step = the full training-path loss over one batch of rows (klg_fwd_bwd):
+valid-row count, pass 1 (both views' log-sum-exps over all vocab tiles on CTA
+pairs), pass 2 (logit recompute -> dZ chunks with the KL cross term -> dW and
+dH GEMMs), loss.
 Workload at N=1 is the 16,384-row SmolLM2-135M training shape (H=576,
 V=49,152, bf16, block-32 mask with ratio U(0,1)); synthetic seeded inputs.
 At N>1 each rank runs its own 16,384 rows (weak scaling, row sharded): the
@@ -230,15 +231,16 @@ def main():
         if world > 1:
             dist.barrier()
 
+    fb_ws = int(_lib.lib().klg_fwd_bwd_workspace_bytes(N, H, V))
+
     def step():
+        # the training step: count (all-reduced across ranks) -> loss + dH + dW -> loss and dW all-reduced
         cnt = ops.count_valid(m)
         if world > 1:
             dist.all_reduce(cnt)
-        loss, lse, _, _ = ops.kl_forward(hs, ht, W, m, T, count=cnt)
+        loss, _, _, _, dh, dw = ops.kl_fwd_bwd(hs, ht, W, m, T, count=cnt, workspace_bytes=fb_ws)
         if world > 1:
             dist.all_reduce(loss)
-        dh, dw = ops.kl_backward(hs, ht, W, m, lse, cnt, temperature=T)
-        if world > 1:
             dist.all_reduce(dw)
         return loss
 

@@ -134,6 +134,26 @@ int klg_bwd(const void* h_s, const void* h_t, const void* w, const uint8_t* mask
             const float* count, const float* grad, int64_t n_rows, int64_t hidden, int64_t vocab, float inv_temp,
             float* d_h_s, float* d_w, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------- training step
+ * Forward and backward in one call (what the trainer does per diffusion chunk,
+ * train.py:614-639: loss then backward).  Pass 1 computes only the two views'
+ * log-sum-exps, on CTA pairs (tcgen05.mma.cta_group::2, 256 x 256 tiles); pass 2
+ * recomputes the logits per vocab chunk, writes dZ, accumulates the KL cross term
+ * sum_v p_v (z_t - z_s) per row on the way, and runs the dW / dH GEMMs; the loss is
+ * formed at the end.  Gradients are for an upstream gradient *grad (NULL = 1).
+ * row_kl (optional) holds KL for rows with mask set and 0 elsewhere. */
+
+/* Recommended workspace bytes for klg_fwd_bwd. */
+int64_t klg_fwd_bwd_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t vocab);
+
+/* dZ chunk width klg_fwd_bwd uses for a workspace of this size (-1 if too small). */
+int64_t klg_fwd_bwd_chunk_cols(int64_t n_rows, int64_t vocab, int64_t workspace_bytes);
+
+int klg_fwd_bwd(const void* h_s, const void* h_t, const void* w, const uint8_t* mask, int64_t n_rows, int64_t hidden,
+                int64_t vocab, float inv_temp, int count_given, float* count, const float* grad, float* loss,
+                float* lse, float* row_kl, float* d_h_s, float* d_w, void* workspace, int64_t workspace_bytes,
+                void* stream);
+
 /* fp32 -> bf16 conversion (round to nearest even) for fp32 callers. */
 int klg_cast_f32_bf16(const float* in, void* out, int64_t n, void* stream);
 

@@ -41,6 +41,10 @@ SIGNATURES = {
     "klg_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64,
                         c_int64, c_float, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
     "klg_cast_f32_bf16": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
+    "klg_fwd_bwd_workspace_bytes": (c_int64, [c_int64, c_int64, c_int64]),
+    "klg_fwd_bwd_chunk_cols": (c_int64, [c_int64, c_int64, c_int64]),
+    "klg_fwd_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_float, c_int, c_void_p,
+                            c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
     "klg_fwd_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_float, c_int,
                                 c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "klg_fwd_noalloc_max_floats": (c_longlong, []),

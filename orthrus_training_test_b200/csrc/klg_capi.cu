@@ -11,7 +11,10 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <algorithm>
+#include <functional>
 #include <mutex>
+#include <queue>
 #include <vector>
 
 #include "klg_kernels.cuh"
@@ -50,10 +53,10 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 2-D bf16 tensor map, 128-byte swizzle, zero fill out of bounds.
+// 2-D bf16 tensor map, 128-byte (default) or 64-byte swizzle, zero fill out of bounds.
 // inner = contiguous extent (elements), outer = row count, ld = row stride (elements).
 bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
-              uint32_t box_outer) {
+              uint32_t box_outer, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {inner, outer};
@@ -61,7 +64,7 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, 
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t es[2] = {1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -125,13 +128,13 @@ inline int cdiv(long long a, long long b) { return (int)((a + b - 1) / b); }
 // into units of vpu vocab tiles.  Picks vpu (>= 4 where possible) so the unit
 // count fills the SMs in whole waves as closely as possible, preferring the
 // largest vpu among near-ties.
-void plan_dual(int n_rt, int n_vt, int n_sm, int& vpu, int& n_uv) {
+void plan_dual(int n_rt, int n_vt, int n_sm, int& vpu, int& n_uv, int max_uv = 64) {
   const int vmin = n_vt < 4 ? n_vt : 4;
   double best = -1.0;
   vpu = n_vt;
   for (int v = n_vt; v >= vmin; --v) {
     const int uv = cdiv(n_vt, v);
-    if (uv > 64) break;
+    if (uv > max_uv) break;
     const long long units = (long long)n_rt * uv;
     const long long waves = (units + n_sm - 1) / n_sm;
     // balance of tile work across SMs (tiles per unit vary only in the last uv)
@@ -173,6 +176,126 @@ int launch_dual(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMa
   return KLG_OK;
 }
 
+int launch_lse_pair(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMap& mw, const klg::LseArgs& a,
+                    cudaStream_t s) {
+  cudaError_t e = set_smem(klg::lse_pair_kernel, klg::LSE_SMEM);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(lse_pair_kernel)");
+  const int pairs = a.n_units < num_sms() / 2 ? a.n_units : num_sms() / 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(klg::LSE_THREADS);
+  cfg.dynamicSmemBytes = klg::LSE_SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const int slot = trace_pre(s);
+  e = cudaLaunchKernelEx(&cfg, klg::lse_pair_kernel, mhs, mht, mw, a);
+  trace_post(slot, s, KLG_KIND_STATS);
+  if (e != cudaSuccess) return cuda_fail(e, "launch lse_pair_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
+int launch_dz_pair(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMap& mw, const CUtensorMap& mout,
+                   const klg::DualArgs& a, cudaStream_t s) {
+  cudaError_t e = set_smem(klg::dz_pair_kernel, klg::DZP_SMEM);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dz_pair_kernel)");
+  const int pairs = a.n_units < num_sms() / 2 ? a.n_units : num_sms() / 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(klg::DZP_THREADS);
+  cfg.dynamicSmemBytes = klg::DZP_SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const int slot = trace_pre(s);
+  e = cudaLaunchKernelEx(&cfg, klg::dz_pair_kernel, mhs, mht, mw, mout, a);
+  trace_post(slot, s, KLG_KIND_DZ);
+  if (e != cudaSuccess) return cuda_fail(e, "launch dz_pair_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
+// Longest-first greedy assignment of tiles [t_begin, t_end) to `pairs` CTA pairs.
+void build_schedule(const klg::PairGemmArgs& g, int t_begin, int t_end, int pairs, klg::PairSchedule& sc) {
+  std::vector<std::vector<uint32_t>> lists(pairs);
+  typedef std::pair<long long, int> Load;   // (assigned k-blocks, pair)
+  std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
+  for (int c = 0; c < pairs; ++c) heap.push(Load(0, c));
+  // problem 0 tiles first when they are the longer ones (equal costs within a problem)
+  const int first = g.p[0].n_kb >= g.p[1].n_kb ? 0 : 1;
+  for (int pass = 0; pass < 2; ++pass) {
+    const int pi = pass == 0 ? first : 1 - first;
+    const int lo = pi == 0 ? 0 : g.p[0].n_tiles, hi = pi == 0 ? g.p[0].n_tiles : g.n_tiles;
+    for (int t = std::max(lo, t_begin); t < std::min(hi, t_end); ++t) {
+      Load l = heap.top();
+      heap.pop();
+      lists[l.second].push_back((uint32_t)t);
+      l.first += g.p[pi].n_kb;
+      heap.push(l);
+    }
+  }
+  int n = 0;
+  for (int c = 0; c < pairs; ++c) {
+    sc.start[c] = (uint16_t)n;
+    for (uint32_t t : lists[c]) sc.tile[n++] = t;
+  }
+  sc.start[pairs] = (uint16_t)n;
+}
+
+template <int BN>
+int launch_gemm_pair_t(const CUtensorMap& a0, const CUtensorMap& b0, const CUtensorMap& a1, const CUtensorMap& b1,
+                       const klg::PairGemmArgs& g, cudaStream_t s) {
+  using Cfg = klg::PairGemmCfg<BN>;
+  auto k = klg::gemm_pair_kernel<BN>;
+  cudaError_t e = set_smem(k, Cfg::SMEM);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm_pair_kernel)");
+  const int max_pairs = std::min(num_sms() / 2, klg::PAIR_MAX_CLUSTERS);
+  static thread_local klg::PairSchedule sc;   // 25 KB: kept off the stack
+  for (int t0 = 0; t0 < g.n_tiles; t0 += klg::PAIR_MAX_TILES) {
+    const int t1 = std::min(g.n_tiles, t0 + klg::PAIR_MAX_TILES);
+    const int pairs = std::min(max_pairs, t1 - t0);
+    build_schedule(g, t0, t1, pairs, sc);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(Cfg::THREADS);
+    cfg.dynamicSmemBytes = Cfg::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const int slot = trace_pre(s);
+    e = cudaLaunchKernelEx(&cfg, k, a0, b0, a1, b1, g, sc);
+    trace_post(slot, s, KLG_KIND_GEMM);
+    if (e != cudaSuccess) return cuda_fail(e, "launch gemm_pair_kernel");
+    ++g_launches;
+  }
+  return KLG_OK;
+}
+
+int launch_gemm_pair(int bn, const CUtensorMap& a0, const CUtensorMap& b0, const CUtensorMap& a1, const CUtensorMap& b1,
+                     const klg::PairGemmArgs& g, cudaStream_t s) {
+  switch (bn) {
+    case 128: return launch_gemm_pair_t<128>(a0, b0, a1, b1, g, s);
+    case 192: return launch_gemm_pair_t<192>(a0, b0, a1, b1, g, s);
+    default: return launch_gemm_pair_t<256>(a0, b0, a1, b1, g, s);
+  }
+}
+
 template <int BN>
 int launch_grouped_t(const CUtensorMap& a0, const CUtensorMap& b0, const CUtensorMap& a1, const CUtensorMap& b1,
                      const klg::GroupedArgs& g, cudaStream_t s) {
@@ -200,12 +323,12 @@ int launch_grouped(int bn, const CUtensorMap& a0, const CUtensorMap& b0, const C
 }
 
 klg::GemmProblem gemm_problem(bool on, int M, int Ncol, int K, int bn, float* C, int ldc, int accumulate, int a_k0,
-                              int b_k0, int a_mn) {
+                              int b_k0, int a_mn, int bm = klg::BM) {
   klg::GemmProblem g{};
   g.M = M;
   g.Ncol = Ncol;
   g.K = K;
-  g.n_mt = cdiv(M, klg::BM);
+  g.n_mt = cdiv(M, bm);
   g.n_nt = cdiv(Ncol, bn);
   g.n_tiles = on ? g.n_mt * g.n_nt : 0;
   g.n_kb = cdiv(K, klg::BK);
@@ -381,6 +504,120 @@ int64_t klg_bwd_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t vocab) {
   return KLG_BWD_HEADER + n_rows * cols * 2;
 }
 
+}  // extern "C"
+
+namespace {
+
+// Pass 2 over vocab chunks of `cols` columns: dZ chunk (dual_kernel<MODE_DZ>) then one
+// grouped GEMM launch for dW_chunk and dH.  With a_parts set, the dZ pass also writes the
+// per-unit KL cross-term partials (at most 8 units per chunk), returning their count.
+int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask, const float* lse, const float* count,
+              const float* grad, int64_t n_rows, int64_t hidden, int64_t vocab, float inv_temp, float* d_hs, float* d_w,
+              int* counters, __nv_bfloat16* dz, int64_t cols, float* a_parts, int* n_ap_out, cudaStream_t s) {
+  int rc;
+  const int bn = gemm_bn(hidden);
+  alignas(64) CUtensorMap mhs, mht, mw, mw_mn, mhs_mn;
+  if (!make_map(&mhs, hs, hidden, n_rows, hidden, klg::BK, klg::BM) ||
+      !make_map(&mht, ht, hidden, n_rows, hidden, klg::BK, klg::BM) ||
+      !make_map(&mw, w, hidden, vocab, hidden, klg::BK, klg::DZP_BN / 2) ||
+      !make_map(&mw_mn, w, hidden, vocab, hidden, 32, klg::BK, CU_TENSOR_MAP_SWIZZLE_64B) ||
+      !make_map(&mhs_mn, hs, hidden, n_rows, hidden, 32, klg::BK, CU_TENSOR_MAP_SWIZZLE_64B))
+    return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+
+  klg::DualArgs a{};
+  a.n_rows = (int)n_rows;
+  a.n_rt = cdiv(n_rows, 256);   // pair tiles
+  a.n_kb = cdiv(hidden, klg::BK);
+  a.scale_log2 = inv_temp * 1.4426950408889634f;
+  a.lse = lse;
+  a.mask = mask;
+  a.count = count;
+  a.grad = grad;
+  a.inv_temp = inv_temp;
+  a.dz = dz;
+  a.ld_dz = (int)cols;
+  a.a_parts = a_parts;
+  const int n_chunks = cdiv(vocab, cols);
+  cudaError_t ce = cudaMemsetAsync(counters, 0, sizeof(int) * n_chunks, s);
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaMemsetAsync(tile counters)");
+  int n_ap = 0;
+  for (int64_t v0 = 0, ci = 0; v0 < vocab; v0 += cols, ++ci) {
+    const int64_t wv = (vocab - v0) < cols ? (vocab - v0) : cols;
+    a.v_begin = (int)v0;
+    a.v_count = (int)wv;
+    a.n_vt = cdiv(wv, klg::DZP_BN);
+    int n_uv;
+    plan_dual(a.n_rt, a.n_vt, num_sms() / 2, a.vt_per_unit, n_uv, a_parts ? 8 : 64);
+    a.n_units = a.n_rt * n_uv;
+    a.a_part_base = n_ap;
+    n_ap += 2 * n_uv;   // one cross-term partial per unit and 64-column half
+    alignas(64) CUtensorMap mdz_out;
+    if (!make_map(&mdz_out, dz, wv, n_rows, cols, 64, 32)) return fail(KLG_ERR_CUDA, "tensor map (dz store)");
+    if ((rc = launch_dz_pair(mhs, mht, mw, mdz_out, a, s))) return rc;
+    if (!d_hs && !d_w) continue;
+    // one grouped launch: problem 0 = dW chunk (longer tiles first), problem 1 = dH += dZ W_chunk
+    alignas(64) CUtensorMap mdz_k, mdz_mn;
+    if (!make_map(&mdz_k, dz, wv, n_rows, cols, klg::BK, klg::BM) || !make_map(&mdz_mn, dz, wv, n_rows, cols, 64, klg::BK))
+      return fail(KLG_ERR_CUDA, "tensor map (dz operand)");
+    klg::PairGemmArgs g{};
+    g.p[0] = gemm_problem(d_w != nullptr, (int)wv, (int)hidden, (int)n_rows, bn, d_w ? d_w + v0 * hidden : nullptr,
+                          (int)hidden, 0, 0, 0, 1, 256);
+    g.p[1] = gemm_problem(d_hs != nullptr, (int)n_rows, (int)hidden, (int)wv, bn, d_hs, (int)hidden, v0 > 0, 0,
+                          (int)v0, 0, 256);
+    g.n_tiles = g.p[0].n_tiles + g.p[1].n_tiles;
+    (void)ci;
+    if ((rc = launch_gemm_pair(bn, mdz_mn, mhs_mn, mdz_k, mw_mn, g, s))) return rc;
+  }
+  if (n_ap_out) *n_ap_out = n_ap;
+  return KLG_OK;
+}
+
+// Number of cross-term partial rows pass 2 writes for chunks of `cols` columns.
+int pass2_parts(int64_t n_rows, int64_t vocab, int64_t cols) {
+  int n_ap = 0;
+  const int n_rt = cdiv(n_rows, 256);
+  for (int64_t v0 = 0; v0 < vocab; v0 += cols) {
+    const int64_t wv = (vocab - v0) < cols ? (vocab - v0) : cols;
+    int vpu, n_uv;
+    plan_dual(n_rt, cdiv(wv, klg::DZP_BN), num_sms() / 2, vpu, n_uv, 8);
+    n_ap += 2 * n_uv;
+  }
+  return n_ap;
+}
+
+// Training-path workspace layout for a given total size: returns the dZ chunk width (or -1).
+struct FwdBwdLayout {
+  int64_t lse_parts_off, a_parts_off, dz_off, cols;
+  int n_lp, n_ap;
+};
+int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
+FwdBwdLayout fwd_bwd_layout(int64_t n_rows, int64_t vocab, int64_t workspace_bytes) {
+  FwdBwdLayout L{};
+  int vpu, n_uv;
+  plan_dual(2 * cdiv(n_rows, 256), cdiv(vocab, klg::LSE_BN), num_sms() / 2, vpu, n_uv);
+  L.n_lp = 2 * n_uv;
+  L.lse_parts_off = KLG_BWD_HEADER;
+  L.a_parts_off = align256(L.lse_parts_off + (int64_t)L.n_lp * 2 * 2 * n_rows * 4);
+  L.cols = -1;
+  const int64_t full = (int64_t)cdiv(vocab, 128) * 128;
+  for (int64_t c = full; c >= 128; c -= 128) {
+    if (cdiv(vocab, c) > KLG_BWD_HEADER / 4) break;
+    const int n_ap = pass2_parts(n_rows, vocab, c);
+    const int64_t dz_off = align256(L.a_parts_off + (int64_t)n_ap * n_rows * 4);
+    if (dz_off + n_rows * c * 2 <= workspace_bytes) {
+      L.cols = c;
+      L.n_ap = n_ap;
+      L.dz_off = dz_off;
+      break;
+    }
+  }
+  return L;
+}
+
+}  // namespace
+
+extern "C" {
+
 int klg_bwd(const void* hs, const void* ht, const void* w, const uint8_t* mask, const float* lse, const float* count,
             const float* grad, int64_t n_rows, int64_t hidden, int64_t vocab, float inv_temp, float* d_hs, float* d_w,
             void* workspace, int64_t workspace_bytes, void* stream) {
@@ -394,58 +631,97 @@ int klg_bwd(const void* hs, const void* ht, const void* w, const uint8_t* mask, 
     return fail(KLG_ERR_WORKSPACE, "backward workspace too small: needs >= %lld bytes",
                 (long long)(KLG_BWD_HEADER + n_rows * 256));
   if ((rc = bind_device(hs))) return rc;
-  cudaStream_t s = (cudaStream_t)stream;
   int* counters = static_cast<int*>(workspace);
   __nv_bfloat16* dz = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(workspace) + KLG_BWD_HEADER);
-  const int bn = gemm_bn(hidden);
+  return run_pass2(hs, ht, w, mask, lse, count, grad, n_rows, hidden, vocab, inv_temp, d_hs, d_w, counters, dz, cols,
+                   nullptr, nullptr, (cudaStream_t)stream);
+}
 
-  alignas(64) CUtensorMap mhs, mht, mw, mw_mn, mhs_mn;
+int64_t klg_fwd_bwd_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t vocab) {
+  if (n_rows < 1 || vocab < 1) return -1;
+  const int64_t dz_bytes = klg_bwd_workspace_bytes(n_rows, hidden, vocab) - KLG_BWD_HEADER;
+  const int64_t cols = dz_bytes / (n_rows * 2);
+  FwdBwdLayout L = fwd_bwd_layout(n_rows, vocab, INT64_MAX / 4);
+  const int n_ap = pass2_parts(n_rows, vocab, cols);
+  return align256(L.a_parts_off + (int64_t)n_ap * n_rows * 4) + dz_bytes;
+}
+
+int64_t klg_fwd_bwd_chunk_cols(int64_t n_rows, int64_t vocab, int64_t workspace_bytes) {
+  if (n_rows < 1 || vocab < 1) return -1;
+  return fwd_bwd_layout(n_rows, vocab, workspace_bytes).cols;
+}
+
+int klg_fwd_bwd(const void* hs, const void* ht, const void* w, const uint8_t* mask, int64_t n_rows, int64_t hidden,
+                int64_t vocab, float inv_temp, int count_given, float* count, const float* grad, float* loss,
+                float* lse, float* row_kl, float* d_hs, float* d_w, void* workspace, int64_t workspace_bytes,
+                void* stream) {
+  int rc = check_problem(hs, ht, w, n_rows, hidden, vocab, inv_temp);
+  if (rc) return rc;
+  if (!mask || !count || !loss || !lse) return fail(KLG_ERR_ARG, "null mask/count/loss/lse");
+  if ((d_hs && !aligned16(d_hs)) || (d_w && !aligned16(d_w))) return fail(KLG_ERR_ALIGN, "outputs must be 16-byte aligned");
+  if (!workspace || !aligned16(workspace)) return fail(KLG_ERR_WORKSPACE, "null or misaligned workspace");
+  const FwdBwdLayout L = fwd_bwd_layout(n_rows, vocab, workspace_bytes);
+  if (L.cols < 0)
+    return fail(KLG_ERR_WORKSPACE, "workspace of %lld bytes too small (see klg_fwd_bwd_workspace_bytes)",
+                (long long)workspace_bytes);
+  if ((rc = bind_device(hs))) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* lse_parts = reinterpret_cast<float*>(ws + L.lse_parts_off);
+  float* a_parts = reinterpret_cast<float*>(ws + L.a_parts_off);
+  if (!count_given && (rc = klg_count_valid(mask, n_rows, count, stream))) return rc;
+
+  // pass 1: log-sum-exp of both views on CTA pairs
+  alignas(64) CUtensorMap mhs, mht, mw;
   if (!make_map(&mhs, hs, hidden, n_rows, hidden, klg::BK, klg::BM) ||
       !make_map(&mht, ht, hidden, n_rows, hidden, klg::BK, klg::BM) ||
-      !make_map(&mw, w, hidden, vocab, hidden, klg::BK, klg::DUAL_BN) ||
-      !make_map(&mw_mn, w, hidden, vocab, hidden, 64, klg::BK) ||
-      !make_map(&mhs_mn, hs, hidden, n_rows, hidden, 64, klg::BK))
+      !make_map(&mw, w, hidden, vocab, hidden, klg::BK, klg::LSE_BN / 2))
     return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
-
-  klg::DualArgs a{};
-  a.n_rows = (int)n_rows;
-  a.n_rt = cdiv(n_rows, klg::BM);
-  a.n_kb = cdiv(hidden, klg::BK);
-  a.scale_log2 = inv_temp * 1.4426950408889634f;
-  a.lse = lse;
-  a.mask = mask;
-  a.count = count;
-  a.grad = grad;
-  a.inv_temp = inv_temp;
-  a.dz = dz;
-  a.ld_dz = (int)cols;
-  const int n_chunks = cdiv(vocab, cols);
-  cudaError_t ce = cudaMemsetAsync(counters, 0, sizeof(int) * n_chunks, s);
-  if (ce != cudaSuccess) return cuda_fail(ce, "cudaMemsetAsync(tile counters)");
-
-  for (int64_t v0 = 0, ci = 0; v0 < vocab; v0 += cols, ++ci) {
-    const int64_t wv = (vocab - v0) < cols ? (vocab - v0) : cols;
-    a.v_begin = (int)v0;
-    a.v_count = (int)wv;
-    a.n_vt = cdiv(wv, klg::DUAL_BN);
-    int n_uv;
-    plan_dual(a.n_rt, a.n_vt, num_sms(), a.vt_per_unit, n_uv);
-    a.n_units = a.n_rt * n_uv;
-    alignas(64) CUtensorMap mdz_out;
-    if (!make_map(&mdz_out, dz, wv, n_rows, cols, 64, 32)) return fail(KLG_ERR_CUDA, "tensor map (dz store)");
-    if ((rc = launch_dual<klg::MODE_DZ>(mhs, mht, mw, mdz_out, a, s))) return rc;
-    // one grouped launch: problem 0 = dW chunk (longer tiles first), problem 1 = dH += dZ W_chunk
-    alignas(64) CUtensorMap mdz_k, mdz_mn;
-    if (!make_map(&mdz_k, dz, wv, n_rows, cols, klg::BK, klg::BM) || !make_map(&mdz_mn, dz, wv, n_rows, cols, 64, klg::BK))
-      return fail(KLG_ERR_CUDA, "tensor map (dz operand)");
-    klg::GroupedArgs g{};
-    g.p[0] = gemm_problem(d_w != nullptr, (int)wv, (int)hidden, (int)n_rows, bn, d_w ? d_w + v0 * hidden : nullptr,
-                          (int)hidden, 0, 0, 0, 1);
-    g.p[1] = gemm_problem(d_hs != nullptr, (int)n_rows, (int)hidden, (int)wv, bn, d_hs, (int)hidden, v0 > 0, 0,
-                          (int)v0, 0);
-    g.n_tiles = g.p[0].n_tiles + g.p[1].n_tiles;
-    g.counter = counters + ci;
-    if ((rc = launch_grouped(bn, mdz_mn, mhs_mn, mdz_k, mw_mn, g, s))) return rc;
+  klg::LseArgs la{};
+  la.n_rows = (int)n_rows;
+  la.vocab = (int)vocab;
+  la.n_rp = cdiv(n_rows, 256);
+  la.n_vt = cdiv(vocab, klg::LSE_BN);
+  plan_dual(2 * la.n_rp, la.n_vt, num_sms() / 2, la.vt_per_unit, la.n_uv);
+  la.n_units = 2 * la.n_rp * la.n_uv;
+  la.n_kb = cdiv(hidden, klg::BK);
+  la.scale_log2 = inv_temp * 1.4426950408889634f;
+  la.parts = lse_parts;
+  if (2 * la.n_uv != L.n_lp) return fail(KLG_ERR_ARG, "internal plan mismatch");
+  if ((rc = launch_lse_pair(mhs, mht, mw, la, s))) return rc;
+  {
+    const int n2 = (int)(2 * n_rows);
+    const int slot = trace_pre(s);
+    klg::lse_merge_kernel<<<cdiv(n2, 256), 256, 0, s>>>(lse_parts, L.n_lp, n2, lse);
+    cudaError_t e = cudaGetLastError();
+    trace_post(slot, s, KLG_KIND_MERGE);
+    if (e != cudaSuccess) return cuda_fail(e, "launch lse_merge_kernel");
+    ++g_launches;
+  }
+  // pass 2: dZ chunks (+ KL cross-term partials) and the dW / dH GEMMs
+  int n_ap = 0;
+  int* counters = reinterpret_cast<int*>(ws);
+  __nv_bfloat16* dz = reinterpret_cast<__nv_bfloat16*>(ws + L.dz_off);
+  if ((rc = run_pass2(hs, ht, w, mask, lse, count, grad, n_rows, hidden, vocab, inv_temp, d_hs, d_w, counters, dz,
+                      L.cols, a_parts, &n_ap, s)))
+    return rc;
+  if (n_ap != L.n_ap) return fail(KLG_ERR_ARG, "internal plan mismatch (cross-term partials)");
+  {
+    // per-row KL in 256-row blocks (block sums reuse the pass-1 partial area), then the loss
+    const int nb = cdiv(n_rows, 256);
+    float* block_sums = lse_parts;
+    int slot = trace_pre(s);
+    klg::row_kl_pair_kernel<<<nb, 256, 0, s>>>(lse, a_parts, n_ap, mask, (int)n_rows, row_kl, block_sums);
+    cudaError_t e = cudaGetLastError();
+    trace_post(slot, s, KLG_KIND_FINALIZE);
+    if (e != cudaSuccess) return cuda_fail(e, "launch row_kl_pair_kernel");
+    ++g_launches;
+    slot = trace_pre(s);
+    klg::loss_from_sums_kernel<<<1, 1024, 0, s>>>(block_sums, nb, count, loss);
+    e = cudaGetLastError();
+    trace_post(slot, s, KLG_KIND_FINALIZE);
+    if (e != cudaSuccess) return cuda_fail(e, "launch loss_from_sums_kernel");
+    ++g_launches;
   }
   return KLG_OK;
 }

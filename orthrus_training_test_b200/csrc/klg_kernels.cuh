@@ -64,6 +64,8 @@ struct DualArgs {
   float inv_temp;
   __nv_bfloat16* dz;     // [N][ld_dz], column j = W row v_begin + j
   int ld_dz;
+  float* a_parts;        // optional [.][N]: per unit sum_v p_v (u_t - u_s) (log2 units), row a_part_base + uv
+  int a_part_base;
 };
 
 __device__ __forceinline__ void dual_unit(const DualArgs& a, int u, int& rt, int& uv, int& vt0, int& vt1) {
@@ -133,22 +135,29 @@ __device__ __forceinline__ void stats_chunk(const uint32_t (&bs)[32], const uint
   A = fmaf(A, rt, a0 + a1);
 }
 
-// One 32-column chunk of dZ = coef * (2^(u_s - L_s) - 2^(u_t - L_t)) as 16 bf16 pairs.
-__device__ __forceinline__ void dz_chunk(const uint32_t (&bs)[32], const uint32_t (&bt)[32], float sl2, float Ls,
-                                         float Lt, float coef, uint32_t (&pk)[16]) {
+// One 32-column chunk of dZ = coef * (2^(u_s - L_s) - 2^(u_t - L_t)) as 16 bf16 pairs,
+// and acc += sum_{j < nvalid} p_j (z_t - z_s) (raw logits; scaled by log2(e)/T later).
+__device__ __forceinline__ void dz_chunk(const uint32_t (&bs)[32], const uint32_t (&bt)[32], int nvalid, float sl2,
+                                         float Ls, float Lt, float coef, uint32_t (&pk)[16], float& acc) {
   if (coef == 0.f) {
 #pragma unroll
     for (int j = 0; j < 16; ++j) pk[j] = 0u;
     return;
   }
+  float a0 = 0.f, a1 = 0.f;
 #pragma unroll
   for (int j = 0; j < 32; j += 2) {
-    const float q0 = ex2(fmaf(__uint_as_float(bs[j]), sl2, -Ls));
-    const float q1 = ex2(fmaf(__uint_as_float(bs[j + 1]), sl2, -Ls));
-    const float p0 = ex2(fmaf(__uint_as_float(bt[j]), sl2, -Lt));
-    const float p1 = ex2(fmaf(__uint_as_float(bt[j + 1]), sl2, -Lt));
+    const float zs0 = __uint_as_float(bs[j]), zs1 = __uint_as_float(bs[j + 1]);
+    const float zt0 = __uint_as_float(bt[j]), zt1 = __uint_as_float(bt[j + 1]);
+    const float q0 = ex2(fmaf(zs0, sl2, -Ls));
+    const float q1 = ex2(fmaf(zs1, sl2, -Ls));
+    const float p0 = ex2(fmaf(zt0, sl2, -Lt));
+    const float p1 = ex2(fmaf(zt1, sl2, -Lt));
     pk[j / 2] = pack_bf16x2(coef * (q0 - p0), coef * (q1 - p1));
+    a0 = fmaf(j < nvalid ? p0 : 0.f, zt0 - zs0, a0);
+    a1 = fmaf(j + 1 < nvalid ? p1 : 0.f, zt1 - zs1, a1);
   }
+  acc += a0 + a1;
 }
 
 // map_out (MODE_DZ only): the dZ chunk [N][v_count] with row stride ld_dz, box 64 x 32.
@@ -275,7 +284,7 @@ dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ 
       const bool row_ok = row < a.n_rows;
       // per-row state
       float ms = NEG_BIG, Ss = 0.f, mt = NEG_BIG, St = 0.f, A = 0.f;  // STATS
-      float Ls = 0.f, Lt = 0.f, coef = 0.f;                            // DZ
+      float Ls = 0.f, Lt = 0.f, coef = 0.f, acc = 0.f;                 // DZ
       if (MODE == MODE_DZ && row_ok) {
         Ls = a.lse[row];
         Lt = a.lse[a.n_rows + row];
@@ -317,9 +326,10 @@ dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ 
               tmem_ld32_raw(tbase + (c + 1) * 32, bs[cur ^ 1]);
               tmem_ld32_raw(tbase + 128 + (c + 1) * 32, bt[cur ^ 1]);
             }
-            if (vt * DUAL_BN + c * 32 < a.v_count) {
+            const int nvalid = a.v_count - (vt * DUAL_BN + c * 32);
+            if (nvalid > 0) {
               uint32_t pk[16];
-              dz_chunk(bs[cur], bt[cur], a.scale_log2, Ls, Lt, coef, pk);
+              dz_chunk(bs[cur], bt[cur], nvalid, a.scale_log2, Ls, Lt, coef, pk, acc);
               // 128-byte-swizzled staging row: 16-byte chunk j of row r lives at chunk j ^ (r % 8)
               const uint32_t rowp = stg + (uint32_t)(c >> 1) * 4096u + (uint32_t)lane * 128u;
 #pragma unroll
@@ -345,6 +355,8 @@ dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ 
           }
         }
       }
+      if (MODE == MODE_DZ && ok && row_ok && a.a_parts)
+        a.a_parts[(size_t)(a.a_part_base + uv) * a.n_rows + row] = acc * a.scale_log2;
       if (MODE == MODE_STATS && ok && row_ok) {
         float* p = a.partials + (size_t)uv * 5 * a.n_rows + row;
         p[0] = ms;
@@ -583,6 +595,223 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
   cluster_sync();   // all pair MMAs retired and both epilogues done before TMEM is released
   tc_fence_after();
   if (warp == 1) tmem_dealloc_pair(tmem, LSE_TMEM_COLS);
+}
+
+// =====================================================================================
+// pass-2 dZ on CTA pairs
+//
+// Per unit (256-row pair tile, vocab range of the chunk) the pair recomputes both views'
+// logit tiles (M = 256 rows: 128 per CTA, N = 128 vocab: each CTA loads a 64-row half of
+// the W tile) into double-buffered TMEM.  8 epilogue warps per CTA (lane quarter x
+// 64-column half) form dZ = coef (q - p) as bf16, stage it in shared memory and write it
+// with TMA tensor stores; each also accumulates its half of the KL cross term.
+// =====================================================================================
+constexpr int DZP_BN = 128;
+constexpr int DZP_STAGES = 4;
+constexpr int DZP_B_BYTES = (DZP_BN / 2) * BK * 2;                        // 8 KB
+constexpr int DZP_STAGE_BYTES = 2 * TILE_128x64 + DZP_B_BYTES;            // 40 KB
+constexpr int DZP_EPI_WARPS = 8;
+constexpr int DZP_THREADS = 64 + 32 * DZP_EPI_WARPS;
+constexpr int DZP_STAGING_BYTES = DZP_EPI_WARPS * 4096;                   // 32 rows x 64 bf16 per warp
+constexpr int DZP_SMEM = 1024 + DZP_STAGES * DZP_STAGE_BYTES + DZP_STAGING_BYTES + 256;
+
+// Units: n_rt counts 256-row pair tiles; a_parts rows: a_part_base + uv * 2 + column half.
+__global__ void __launch_bounds__(DZP_THREADS, 1)
+dz_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ CUtensorMap map_ht,
+               const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_out,
+               const DualArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t stg0 = sbase + DZP_STAGES * DZP_STAGE_BYTES;
+  const uint32_t bar0 = stg0 + DZP_STAGING_BYTES;
+  const uint32_t full0 = bar0;
+  const uint32_t empty0 = bar0 + 8u * DZP_STAGES;
+  const uint32_t tfull0 = bar0 + 16u * DZP_STAGES;
+  const uint32_t tempty0 = tfull0 + 16u;
+  const uint32_t done_bar = tempty0 + 16u;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int cid = blockIdx.x >> 1;
+  const int n_clusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < DZP_STAGES; ++s) {
+      mbar_init(full0 + 8u * s, 2);
+      mbar_init(empty0 + 8u * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull0 + 8u * b, 1);
+      mbar_init(tempty0 + 8u * b, 2 * DZP_EPI_WARPS);
+    }
+    mbar_init(done_bar, 1);
+    fence_mbar_init();
+    tma_prefetch(&map_hs);
+    tma_prefetch(&map_ht);
+    tma_prefetch(&map_w);
+    tma_prefetch(&map_out);
+  }
+  if (warp == 1) tmem_alloc_pair(smem_u32(&tmem_slot), DUAL_TMEM_COLS);
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  volatile int* abort_p = &abort_flag;
+  const uint32_t lead_full0 = mapa_shared(full0, 0);
+  const uint32_t lead_tempty0 = mapa_shared(tempty0, 0);
+  const uint32_t peer_empty0 = mapa_shared(empty0, 1);
+  const uint32_t peer_tfull0 = mapa_shared(tfull0, 1);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      for (int u = cid; ok && u < a.n_units; u += n_clusters) {
+        int rt, uv, vt0, vt1;
+        dual_unit(a, u, rt, uv, vt0, vt1);
+        const int row0 = rt * 256 + (int)rank * 128;
+        for (int vt = vt0; ok && vt < vt1; ++vt) {
+          for (int kb = 0; kb < a.n_kb; ++kb) {
+            if (!mbar_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
+            const uint32_t sa = sbase + stage * DZP_STAGE_BYTES;
+            const uint32_t fb = lead_full0 + 8u * stage;
+            if (leader) mbar_arrive_expect_tx(full0 + 8u * stage, 2 * DZP_STAGE_BYTES);
+            tma_load_2d_pair(sa, &map_hs, fb, kb * BK, row0);
+            tma_load_2d_pair(sa + TILE_128x64, &map_ht, fb, kb * BK, row0);
+            tma_load_2d_pair(sa + 2 * TILE_128x64, &map_w, fb, kb * BK,
+                             a.v_begin + vt * DZP_BN + (int)rank * (DZP_BN / 2));
+            if (!leader) mbar_arrive_cluster(fb);
+            ++issued;
+            if (++stage == DZP_STAGES) { stage = 0; phase ^= 1; }
+          }
+        }
+      }
+      if (leader) drain_loads<DZP_STAGES>(full0, stage, phase, issued);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = make_idesc_bf16(2 * BM, DZP_BN, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      int tcount = 0;
+      bool ok = true;
+      for (int u = cid; ok && u < a.n_units; u += n_clusters) {
+        int rt, uv, vt0, vt1;
+        dual_unit(a, u, rt, uv, vt0, vt1);
+        for (int vt = vt0; ok && vt < vt1; ++vt, ++tcount) {
+          const int buf = tcount & 1;
+          const uint32_t tph = (tcount >> 1) & 1;
+          if (!mbar_wait(tempty0 + 8u * buf, tph ^ 1, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d_s = tmem + buf * 256;
+          const uint32_t d_t = d_s + 128;
+          for (int kb = 0; kb < a.n_kb; ++kb) {
+            if (!mbar_wait(full0 + 8u * stage, phase, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t sa = sbase + stage * DZP_STAGE_BYTES;
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) {
+              const uint64_t bdesc = desc_kmajor(sa + 2 * TILE_128x64, k);
+              const uint32_t acc = (kb | k) != 0;
+              mma_bf16_pair(d_s, desc_kmajor(sa, k), bdesc, idesc, acc);
+              mma_bf16_pair(d_t, desc_kmajor(sa + TILE_128x64, k), bdesc, idesc, acc);
+            }
+            mma_commit_pair(empty0 + 8u * stage);
+            mma_commit_pair(peer_empty0 + 8u * stage);
+            if (++stage == DZP_STAGES) { stage = 0; phase ^= 1; }
+          }
+          if (ok) {
+            mma_commit_pair(tfull0 + 8u * buf);
+            mma_commit_pair(peer_tfull0 + 8u * buf);
+          }
+        }
+      }
+      mma_commit_pair(done_bar);
+      mbar_wait_drain(done_bar, 0);
+    }
+  } else {
+    const int q = warp & 3;
+    const int h = (warp - EPI_WARP0) >> 2;   // 64-column half of the 128-column tile
+    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 64);
+    const uint32_t stg = stg0 + (uint32_t)(warp - EPI_WARP0) * 4096u;
+    int tcount = 0;
+    bool ok = true;
+    for (int u = cid; ok && u < a.n_units; u += n_clusters) {
+      int rt, uv, vt0, vt1;
+      dual_unit(a, u, rt, uv, vt0, vt1);
+      const int row = rt * 256 + (int)rank * 128 + q * 32 + lane;
+      const bool row_ok = row < a.n_rows;
+      float Ls = 0.f, Lt = 0.f, coef = 0.f, acc = 0.f;
+      if (row_ok) {
+        Ls = a.lse[row];
+        Lt = a.lse[a.n_rows + row];
+        const float cnt = *a.count;
+        const float g = a.grad ? *a.grad : 1.0f;
+        coef = (a.mask[row] && cnt > 0.f) ? g / cnt * a.inv_temp : 0.f;
+      }
+      for (int vt = vt0; ok && vt < vt1; ++vt, ++tcount) {
+        const int buf = tcount & 1;
+        const uint32_t tph = (tcount >> 1) & 1;
+        if (!mbar_wait(tfull0 + 8u * buf, tph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) { ok = false; break; }
+        tc_fence_after();
+        if (lane == 0) bulk_wait_read0();   // staging free: previous tile's store has read it
+        __syncwarp();
+        const uint32_t tbase = lane_addr + buf * 256;
+        uint32_t bs[2][32], bt[2][32];
+        tmem_ld32_raw(tbase, bs[0]);
+        tmem_ld32_raw(tbase + 128, bt[0]);
+        tmem_wait_ld_regs(bs[0], bt[0]);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int cur = c & 1;
+          if (c == 0) {
+            tmem_ld32_raw(tbase + 32, bs[1]);
+            tmem_ld32_raw(tbase + 128 + 32, bt[1]);
+          }
+          const int nvalid = a.v_count - (vt * DZP_BN + h * 64 + c * 32);
+          if (nvalid > 0) {
+            uint32_t pk[16];
+            dz_chunk(bs[cur], bt[cur], nvalid, a.scale_log2, Ls, Lt, coef, pk, acc);
+            const uint32_t rowp = stg + (uint32_t)lane * 128u;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint32_t j = (uint32_t)(c * 4 + k);
+              st_shared_v4(rowp + ((j ^ (uint32_t)(lane & 7)) << 4), pk[4 * k], pk[4 * k + 1], pk[4 * k + 2],
+                           pk[4 * k + 3]);
+            }
+          }
+          if (c == 0) tmem_wait_ld_regs(bs[1], bt[1]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (leader) mbar_arrive(tempty0 + 8u * buf);
+          else mbar_arrive_cluster(lead_tempty0 + 8u * buf);
+        }
+        fence_async_shared();
+        __syncwarp();
+        const int x0 = vt * DZP_BN + h * 64, y0 = rt * 256 + (int)rank * 128 + q * 32;
+        if (lane == 0 && y0 < a.n_rows && x0 < a.v_count) {
+          tma_store_2d(&map_out, stg, x0, y0);
+          bulk_commit();
+        }
+      }
+      if (ok && row_ok && a.a_parts)
+        a.a_parts[(size_t)(a.a_part_base + uv * 2 + h) * a.n_rows + row] = acc * a.scale_log2;
+    }
+    if (lane == 0) bulk_wait0();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem, DUAL_TMEM_COLS);
 }
 
 // =====================================================================================
@@ -825,6 +1054,228 @@ gemm_grouped_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_con
 }
 
 // =====================================================================================
+// grouped GEMM on CTA pairs: the backward chunk's dW = dZ^T h_s and dH (+)= dZ W_chunk.
+// Tile = (problem, 256-row pair tile, BN-column tile); each CTA holds 128 rows of A and
+// one BN/2-column half of B (MN-major, 64-byte swizzle: 32-column boxes).  Tiles are
+// assigned to pairs by a longest-first greedy schedule built on the host and passed in
+// the launch parameters (deterministic; dW tiles are the long ones).
+// =====================================================================================
+constexpr int PAIR_MAX_TILES = 6144;
+constexpr int PAIR_MAX_CLUSTERS = 128;
+struct PairSchedule {
+  uint32_t tile[PAIR_MAX_TILES];           // tile ids, grouped by pair
+  uint16_t start[PAIR_MAX_CLUSTERS + 1];   // pair c runs tile[start[c] .. start[c+1])
+};
+struct PairGemmArgs {
+  GemmProblem p[2];   // n_mt counts 256-row pair tiles
+  int n_tiles;
+};
+
+template <int BN>
+struct PairGemmCfg {
+  static constexpr int A_BYTES = TILE_128x64;          // this CTA's 128 rows x 64 K
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;    // this CTA's BN/2 columns x 64 K
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (227 * 1024 - 2048) / STAGE_BYTES > 8 ? 8 : (227 * 1024 - 2048) / STAGE_BYTES;
+  static constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
+  static constexpr int EPI_WARPS = 4;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 256;
+};
+
+__device__ __forceinline__ void pair_tile(const PairGemmArgs& g, int t, int& pi, int& mt, int& nt) {
+  pi = t < g.p[0].n_tiles ? 0 : 1;
+  const int lt = pi ? t - g.p[0].n_tiles : t;
+  mt = lt / g.p[pi].n_nt;
+  nt = lt % g.p[pi].n_nt;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(PairGemmCfg<BN>::THREADS, 1)
+gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_b0,
+                 const __grid_constant__ CUtensorMap map_a1, const __grid_constant__ CUtensorMap map_b1,
+                 const PairGemmArgs g, const __grid_constant__ PairSchedule sched) {
+  using Cfg = PairGemmCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr int EPI = Cfg::EPI_WARPS;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + STAGES * Cfg::STAGE_BYTES;
+  const uint32_t full0 = bar0;
+  const uint32_t empty0 = bar0 + 8u * STAGES;
+  const uint32_t tfull0 = bar0 + 16u * STAGES;
+  const uint32_t tempty0 = tfull0 + 16u;
+  const uint32_t done_bar = tempty0 + 16u;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int cid = blockIdx.x >> 1;
+  const int i0 = sched.start[cid], i1 = sched.start[cid + 1];
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full0 + 8u * s, 2);
+      mbar_init(empty0 + 8u * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull0 + 8u * b, 1);
+      mbar_init(tempty0 + 8u * b, 2 * EPI);
+    }
+    mbar_init(done_bar, 1);
+    fence_mbar_init();
+    tma_prefetch(&map_a0);
+    tma_prefetch(&map_b0);
+    tma_prefetch(&map_a1);
+    tma_prefetch(&map_b1);
+  }
+  if (warp == 1) tmem_alloc_pair(smem_u32(&tmem_slot), Cfg::TMEM_COLS);
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  volatile int* abort_p = &abort_flag;
+  const uint32_t lead_full0 = mapa_shared(full0, 0);
+  const uint32_t lead_tempty0 = mapa_shared(tempty0, 0);
+  const uint32_t peer_empty0 = mapa_shared(empty0, 1);
+  const uint32_t peer_tfull0 = mapa_shared(tfull0, 1);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA producer (both CTAs)
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      for (int i = i0; ok && i < i1; ++i) {
+        int pi, mt, nt;
+        pair_tile(g, sched.tile[i], pi, mt, nt);
+        const GemmProblem& P = g.p[pi];
+        const CUtensorMap* ma = pi ? &map_a1 : &map_a0;
+        const CUtensorMap* mb = pi ? &map_b1 : &map_b0;
+        const int row0 = mt * 256 + (int)rank * 128;
+        const int col0 = nt * BN + (int)rank * (BN / 2);
+        for (int kb = 0; kb < P.n_kb; ++kb) {
+          if (!mbar_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
+          const uint32_t sa = sbase + stage * Cfg::STAGE_BYTES;
+          const uint32_t sb = sa + Cfg::A_BYTES;
+          const uint32_t fb = lead_full0 + 8u * stage;
+          if (leader) mbar_arrive_expect_tx(full0 + 8u * stage, 2 * Cfg::STAGE_BYTES);
+          const int ka = P.a_k0 + kb * BK, kbb = P.b_k0 + kb * BK;
+          if (P.a_mn) {
+            tma_load_2d_pair(sa, ma, fb, row0, ka);
+            tma_load_2d_pair(sa + 8192, ma, fb, row0 + 64, ka);
+          } else {
+            tma_load_2d_pair(sa, ma, fb, ka, row0);
+          }
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j) tma_load_2d_pair(sb + 4096 * j, mb, fb, col0 + 32 * j, kbb);
+          if (!leader) mbar_arrive_cluster(fb);
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (leader) drain_loads<STAGES>(full0, stage, phase, issued);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ------------------------------------------------------------ pair MMA issuer (leader)
+      constexpr uint32_t idesc_kmaj = make_idesc_bf16(2 * BM, BN, false, true);
+      constexpr uint32_t idesc_mnmaj = make_idesc_bf16(2 * BM, BN, true, true);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int i = i0, k = 0; ok && i < i1; ++i, ++k) {
+        int pi, mt, nt;
+        pair_tile(g, sched.tile[i], pi, mt, nt);
+        const GemmProblem& P = g.p[pi];
+        const bool amn = P.a_mn != 0;
+        const uint32_t idesc = amn ? idesc_mnmaj : idesc_kmaj;
+        const int buf = k & 1;
+        const uint32_t tph = (uint32_t)(k >> 1) & 1u;
+        if (!mbar_wait(tempty0 + 8u * buf, tph ^ 1, abort_p, KLG_STATUS_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + buf * BN;
+        for (int kb = 0; kb < P.n_kb; ++kb) {
+          if (!mbar_wait(full0 + 8u * stage, phase, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = sbase + stage * Cfg::STAGE_BYTES;
+          const uint32_t sb = sa + Cfg::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = amn ? desc_mnmajor(sa, kk) : desc_kmajor(sa, kk);
+            mma_bf16_pair(d, ad, desc_mnmajor_sw64(sb, kk), idesc, (kb | kk) != 0);
+          }
+          mma_commit_pair(empty0 + 8u * stage);
+          mma_commit_pair(peer_empty0 + 8u * stage);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (ok) {
+          mma_commit_pair(tfull0 + 8u * buf);
+          mma_commit_pair(peer_tfull0 + 8u * buf);
+        }
+      }
+      mma_commit_pair(done_bar);
+      mbar_wait_drain(done_bar, 0);
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue (both CTAs)
+    const int q = warp & 3;
+    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+    for (int i = i0, k = 0; i < i1; ++i, ++k) {
+      int pi, mt, nt;
+      pair_tile(g, sched.tile[i], pi, mt, nt);
+      const GemmProblem& P = g.p[pi];
+      const int buf = k & 1;
+      const uint32_t tph = (uint32_t)(k >> 1) & 1u;
+      if (!mbar_wait(tfull0 + 8u * buf, tph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) break;
+      tc_fence_after();
+      const int row = mt * 256 + (int)rank * 128 + q * 32 + lane;
+      const bool row_ok = row < P.M;
+      float* crow = P.C + (size_t)(row_ok ? row : 0) * P.ldc;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        tmem_ld32(lane_addr + buf * BN + c * 32, v);
+        tmem_wait_ld();
+        const int col0 = nt * BN + c * 32;
+        if (!row_ok || col0 >= P.Ncol) continue;
+        if (col0 + 32 <= P.Ncol) {
+          float4* d4 = reinterpret_cast<float4*>(crow + col0);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            if (P.accumulate) {
+              const float4 old = d4[j];
+              o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+            }
+            d4[j] = o;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < P.Ncol) crow[col0 + j] = P.accumulate ? crow[col0 + j] + v[j] : v[j];
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader) mbar_arrive(tempty0 + 8u * buf);
+        else mbar_arrive_cluster(lead_tempty0 + 8u * buf);
+      }
+    }
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem, Cfg::TMEM_COLS);
+}
+
+// =====================================================================================
 // small kernels
 // =====================================================================================
 
@@ -892,6 +1343,67 @@ __global__ void finalize_kernel(const float* __restrict__ stats, const uint8_t* 
     if (row_kl) row_kl[i] = kl;
     if (mask[i]) acc += kl;
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    acc = (threadIdx.x < (blockDim.x >> 5)) ? part[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (threadIdx.x == 0) {
+      const float c = *count;
+      *loss = c > 0.f ? acc / c : 0.f;
+    }
+  }
+}
+
+// lse[i] = log2-domain log-sum-exp of row i from n_part (m, S) records parts[n_part][2][n2].
+__global__ void lse_merge_kernel(const float* __restrict__ parts, int n_part, int n2, float* __restrict__ lse) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n2) return;
+  const size_t st = (size_t)n2;
+  float M = NEG_BIG;
+  for (int p = 0; p < n_part; ++p) M = fmaxf(M, parts[(size_t)p * 2 * st + i]);
+  float S = 0.f;
+  for (int p = 0; p < n_part; ++p) S = fmaf(parts[(size_t)p * 2 * st + st + i], ex2(parts[(size_t)p * 2 * st + i] - M), S);
+  lse[i] = M + __log2f(S);
+}
+
+// Training-path per-row KL: KL_i = ln2 * (sum_p a_parts[p][i] + L_s,i - L_t,i) for rows
+// carrying loss (0 elsewhere: the cross term is only formed for them).  Each block
+// writes the sum of its rows' masked KL to block_sums[blockIdx.x] (fixed order).
+__global__ void row_kl_pair_kernel(const float* __restrict__ lse, const float* __restrict__ a_parts, int n_ap,
+                                   const uint8_t* __restrict__ mask, int n, float* __restrict__ row_kl,
+                                   float* __restrict__ block_sums) {
+  __shared__ float part[8];
+  const float ln2 = 0.69314718055994530942f;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  float kl = 0.f;
+  if (i < n && mask[i]) {
+    float A = 0.f;
+    for (int p = 0; p < n_ap; ++p) A += a_parts[(size_t)p * n + i];
+    kl = ln2 * (A + lse[i] - lse[(size_t)n + i]);
+  }
+  if (row_kl && i < n) row_kl[i] = kl;
+  float acc = kl;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += part[w];
+    block_sums[blockIdx.x] = t;
+  }
+}
+
+// loss = sum(block_sums) / count (0 when count == 0); one block, fixed reduction order.
+__global__ void loss_from_sums_kernel(const float* __restrict__ block_sums, int n_blocks,
+                                      const float* __restrict__ count, float* __restrict__ loss) {
+  __shared__ float part[32];
+  float acc = 0.f;
+  for (int i = threadIdx.x; i < n_blocks; i += blockDim.x) acc += block_sums[i];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
   if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;

@@ -188,9 +188,11 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
 }
-// Arrive on an mbarrier that may live in another CTA of the cluster.
+// Arrive on an mbarrier that may live in another CTA of the cluster.  Default (CTA-scope)
+// semantics: the arrivals this is used for publish no generic-memory data (TMA bytes are
+// tracked by the barrier's transaction count, TMEM reads by tcgen05 fences).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -250,6 +252,18 @@ __device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile_base, int k16) {
 // 16-row slice starts 16*128 = 2048*k bytes in.
 __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t tile_base, int k16) {
   return make_desc_sw128(tile_base + 2048u * k16, 8192u, 1024u);
+}
+// MN-major operand tile loaded as 32-element-wide boxes (64-byte swizzle) of 64 K-rows:
+// K-rows 64 B apart (8-row groups 512 B apart, SBO); 32-wide MN atoms one box
+// (64 rows * 64 B = 4096 B) apart (LBO); the k-th 16-row slice starts 1024*k bytes in.
+__device__ __forceinline__ uint64_t desc_mnmajor_sw64(uint32_t tile_base, int k16) {
+  uint64_t d = 0;
+  d |= (uint64_t)(((tile_base + 1024u * k16) >> 4) & 0x3FFF);
+  d |= (uint64_t)((4096u >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((512u >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;   // descriptor version (sm_100)
+  d |= (uint64_t)4 << 61;   // SWIZZLE_64B
+  return d;
 }
 // Instruction descriptor, kind::f16: fp32 D, bf16 A and B, dense.
 __host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N, bool a_mn_major, bool b_mn_major) {

@@ -162,6 +162,39 @@ def kl_backward(h_s, h_t, weight, mask, lse, count, grad: Optional[torch.Tensor]
     return dh, dw
 
 
+def kl_fwd_bwd(h_s, h_t, weight, mask, temperature: float = 1.0, count: Optional[torch.Tensor] = None,
+               grad: Optional[torch.Tensor] = None, need_dh: bool = True, need_dw: bool = True,
+               want_row_kl: bool = False, workspace_bytes: Optional[int] = None):
+    """Training step in one call: loss and gradients (for upstream gradient ``grad``, default 1).
+
+    Returns ``(loss, lse, count, row_kl, dH_s fp32 or None, dW fp32 or None)``.
+    """
+    m = mask_u8(mask)
+    dev = _require_cuda(h_s, h_t, weight, m)
+    N, H = h_s.shape
+    V = weight.shape[0]
+    if h_t.shape != h_s.shape or weight.shape[1] != H or m.numel() != N:
+        raise ValueError(f"shape mismatch: h_s {tuple(h_s.shape)} h_t {tuple(h_t.shape)} "
+                         f"weight {tuple(weight.shape)} mask {tuple(m.shape)}")
+    if workspace_bytes is None:
+        workspace_bytes = int(_lib.lib().klg_fwd_bwd_workspace_bytes(N, H, V))
+    ws = torch.empty(int(workspace_bytes), dtype=torch.uint8, device=dev)
+    given = count is not None
+    cnt = count if given else torch.empty(1, dtype=torch.float32, device=dev)
+    loss = torch.empty((), dtype=torch.float32, device=dev)
+    lse = torch.empty(2, N, dtype=torch.float32, device=dev)
+    row_kl = torch.empty(N, dtype=torch.float32, device=dev) if want_row_kl else None
+    dh = torch.empty(N, H, dtype=torch.float32, device=dev) if need_dh else None
+    dw = torch.empty(V, H, dtype=torch.float32, device=dev) if need_dw else None
+    g = None
+    if grad is not None:
+        g = grad.detach().to(device=dev, dtype=torch.float32).reshape(1).contiguous()
+    call("klg_fwd_bwd", _ptr(h_s), _ptr(h_t), _ptr(weight), _ptr(m), N, H, V, 1.0 / float(temperature), int(given),
+         _ptr(cnt), _ptr(g), _ptr(loss), _ptr(lse), _ptr(row_kl), _ptr(dh), _ptr(dw), _ptr(ws), int(workspace_bytes),
+         _stream(dev))
+    return loss, lse, cnt, row_kl, dh, dw
+
+
 # ----------------------------------------------------------------- autograd op
 
 class KLGemmFn(torch.autograd.Function):
@@ -173,6 +206,12 @@ class KLGemmFn(torch.autograd.Function):
     (float), ``count`` (optional ``[1]`` device tensor overriding sum(mask)).
     bf16 or fp32 inputs; compute is bf16 on the tensor cores with fp32
     accumulation and fp32 softmax arithmetic.
+
+    When a gradient will be needed the forward runs the whole training step
+    (``klg_fwd_bwd``) and keeps dH_s / dW for an upstream gradient of 1 (O(N*H +
+    V*H), never O(N*V)); backward scales them by the actual upstream gradient.
+    Without gradients (evaluation, train.py:845-911) it runs the single-pass
+    forward (``klg_fwd``): both views' statistics and the KL in one sweep.
     """
 
     @staticmethod
@@ -181,23 +220,22 @@ class KLGemmFn(torch.autograd.Function):
         ht = to_compute_dtype(h_t)
         w = to_compute_dtype(weight)
         m = mask_u8(mask)
-        loss, lse, cnt, _ = kl_forward(hs, ht, w, m, temperature, count=count)
-        ctx.save_for_backward(hs, ht, w, m, lse, cnt)
-        ctx.temperature = float(temperature)
+        need_dh, need_dw = ctx.needs_input_grad[0], ctx.needs_input_grad[2]
         ctx.dtypes = (h_s.dtype, weight.dtype)
+        if need_dh or need_dw:
+            loss, _, _, _, dh, dw = kl_fwd_bwd(hs, ht, w, m, temperature, count=count, need_dh=need_dh,
+                                               need_dw=need_dw)
+            ctx.save_for_backward(dh, dw)
+        else:
+            loss, _, _, _ = kl_forward(hs, ht, w, m, temperature, count=count)
         return loss
 
     @staticmethod
     def backward(ctx, g):
-        hs, ht, w, m, lse, cnt = ctx.saved_tensors
-        need_dh = ctx.needs_input_grad[0]
-        need_dw = ctx.needs_input_grad[2]
-        if not (need_dh or need_dw):
-            return None, None, None, None, None, None
-        dh, dw = kl_backward(hs, ht, w, m, lse, cnt, grad=g, temperature=ctx.temperature,
-                             need_dh=need_dh, need_dw=need_dw)
-        return (dh.to(ctx.dtypes[0]) if need_dh else None, None,
-                dw.to(ctx.dtypes[1]) if need_dw else None, None, None, None)
+        dh, dw = ctx.saved_tensors
+        g = g.to(torch.float32)
+        return ((dh * g).to(ctx.dtypes[0]) if dh is not None else None, None,
+                (dw * g).to(ctx.dtypes[1]) if dw is not None else None, None, None, None)
 
 
 def kl_gemm_loss(h_s: torch.Tensor, h_t: torch.Tensor, weight: torch.Tensor, mask: torch.Tensor,

@@ -68,6 +68,13 @@ class CudaEngine:
         return kl_backward(h_s, h_t, w, mask, lse, count, grad=grad, temperature=temperature, need_dh=need_dh,
                            need_dw=need_dw)
 
+    def forward_backward(self, h_s, h_t, w, mask, temperature, count, need_dh, need_dw):
+        """Training step with a given normaliser: ``(loss, dH, dW)`` for upstream gradient 1."""
+        from .ops import kl_fwd_bwd
+        loss, _, _, _, dh, dw = kl_fwd_bwd(h_s, h_t, w, mask, temperature, count=count, need_dh=need_dh,
+                                           need_dw=need_dw)
+        return loss, dh, dw
+
 
 def _engine(engine):
     return engine if engine is not None else CudaEngine()
@@ -80,23 +87,27 @@ class _RowShardedFn(torch.autograd.Function):
         hs, ht, w, m = eng.prepare(h_s), eng.prepare(h_t), eng.prepare(weight), eng.mask(mask)
         count = eng.count(m)
         dist.all_reduce(count, op=dist.ReduceOp.SUM, group=group)      # global normaliser
-        loss, lse = eng.forward(hs, ht, w, m, temperature, count)     # sum_local valid*KL / global count
+        need_dh, need_dw = ctx.needs_input_grad[0], ctx.needs_input_grad[2]
+        ctx.group = group
+        ctx.dtypes = (h_s.dtype, weight.dtype)
+        if need_dh or need_dw:
+            # sum_local valid*KL / global count, and its gradients for upstream gradient 1
+            loss, dh, dw = eng.forward_backward(hs, ht, w, m, temperature, count, need_dh, need_dw)
+            ctx.save_for_backward(dh, dw)
+        else:
+            loss, _ = eng.forward(hs, ht, w, m, temperature, count)
         loss = loss.reshape(1).clone()
         dist.all_reduce(loss, op=dist.ReduceOp.SUM, group=group)
-        ctx.save_for_backward(hs, ht, w, m, lse, count)
-        ctx.temperature, ctx.group, ctx.eng = float(temperature), group, eng
-        ctx.dtypes = (h_s.dtype, weight.dtype)
         return loss.reshape(())
 
     @staticmethod
     def backward(ctx, g):
-        hs, ht, w, m, lse, count = ctx.saved_tensors
-        need_dh, need_dw = ctx.needs_input_grad[0], ctx.needs_input_grad[2]
-        dh, dw = ctx.eng.backward(hs, ht, w, m, lse, count, g, ctx.temperature, need_dh, need_dw)
-        if need_dw:
+        dh, dw = ctx.saved_tensors
+        if dw is not None:
+            dw = dw * g
             dist.all_reduce(dw, op=dist.ReduceOp.SUM, group=ctx.group)  # data-parallel dW exchange
-        return (dh.to(ctx.dtypes[0]) if need_dh else None, None, dw.to(ctx.dtypes[1]) if need_dw else None,
-                None, None, None, None)
+        return ((dh * g).to(ctx.dtypes[0]) if dh is not None else None, None,
+                dw.to(ctx.dtypes[1]) if dw is not None else None, None, None, None, None)
 
 
 def row_sharded_kl_loss(h_s: torch.Tensor, h_t: torch.Tensor, weight: torch.Tensor, mask: torch.Tensor,

@@ -42,6 +42,11 @@ class CpuOracleEngine:
         loss, _, ls, lt = O.finalize_np(_np(stats), _np(mask).astype(bool), float(count.item()))
         return torch.tensor(loss, dtype=torch.float64), torch.from_numpy(np.stack([ls, lt]))
 
+    def forward_backward(self, h_s, h_t, w, mask, temperature, count, need_dh, need_dw):
+        loss, lse = self.forward(h_s, h_t, w, mask, temperature, count)
+        dh, dw = self.backward(h_s, h_t, w, mask, lse, count, None, temperature, need_dh, need_dw)
+        return loss, dh, dw
+
     def backward(self, h_s, h_t, w, mask, lse, count, grad, temperature, need_dh, need_dw):
         g = 1.0 if grad is None else float(grad.item())
         L = _np(lse)

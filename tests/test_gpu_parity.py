@@ -12,8 +12,8 @@ import torch
 
 from oracle import klgemm_oracle as O
 from tests.conftest import GOLDEN, golden_cases
-from tests.gpu_helpers import (GRAD_COS, GRAD_MAX_REL, LOSS_RTOL, assert_close, bf16_round, run_oracle_np,
-                               run_oracle_torch_gpu, run_ours)
+from tests.gpu_helpers import (GRAD_COS, GRAD_MAX_REL, LOSS_RTOL, assert_close, bf16_round, run_both,
+                               run_oracle_np, run_oracle_torch_gpu, run_ours)
 
 pytestmark = pytest.mark.gpu
 
@@ -25,6 +25,16 @@ def rand_problem(N, H, V, T=1.0, p=0.5, seed=0, tscale=1.0):
     W = torch.randn(V, H, generator=g) * 0.02
     mask = torch.rand(N, generator=g) < p
     return h_s, h_t, W, mask, T
+
+
+def test_fused_row_kl_and_lse_match_split():
+    """The training path's pass-1 log-sum-exps (CTA pairs) and per-row KL equal the single-pass forward's."""
+    h_s, h_t, W, mask, T = rand_problem(700, 576, 3000, seed=9, p=0.6)
+    a, b = run_both(h_s, h_t, W, mask, T)
+    np.testing.assert_allclose(b["lse"], a["lse"], rtol=1e-5, atol=1e-4)
+    m = mask.numpy()
+    np.testing.assert_allclose(b["row_kl"][m], a["row_kl"][m], rtol=2e-3, atol=2e-6)
+    assert not np.any(b["row_kl"][~m])
 
 
 def test_stats_small():
@@ -42,7 +52,7 @@ def test_stats_small():
 
 def test_bwd_small():
     h_s, h_t, W, mask, T = rand_problem(200, 128, 700, seed=2)
-    ours = run_ours(h_s, h_t, W, mask, T)
+    ours = run_both(h_s, h_t, W, mask, T)
     loss, dh, dw, *_ = run_oracle_np(h_s, h_t, W, mask, T)
     assert_close(ours, loss, dh, dw, "small")
 
@@ -54,11 +64,11 @@ def test_golden_aligned(name):
     h_s, h_t, W = (torch.tensor(g[k]) for k in ("h_s", "h_t", "weight"))
     mask = torch.tensor(g["mask"])
     T = float(g["temperature"])
-    ours = run_ours(h_s, h_t, W, mask, T)
+    ours = run_both(h_s, h_t, W, mask, T)
     # against the reference's own fp32 numbers (inputs rounded to bf16 by the op)
     B = g["anchor_positions"].shape[0]
     dp, _, _ = O.kl_indices(B, g["anchor_positions"].shape[1], int(g["K"]))
-    ref_dh = g["grad_diff_hidden"][np.arange(B)[:, None], dp].reshape(ours["dh"].shape)
+    ref_dh = g["grad_diff_hidden"][np.arange(B)[:, None], dp].reshape(ours[0]["dh"].shape)
     assert_close(ours, float(g["loss"]), ref_dh, g["grad_weight"], name)
 
 
@@ -98,9 +108,9 @@ def test_all_masked_op_gives_zero():
     """The op itself (no shim early-return): zero loss and exactly zero grads."""
     h_s, h_t, W, _, T = rand_problem(300, 64, 500, seed=3)
     mask = torch.zeros(300, dtype=torch.bool)
-    ours = run_ours(h_s, h_t, W, mask, T)
-    assert ours["loss"] == 0.0
-    assert not np.any(ours["dh"]) and not np.any(ours["dw"])
+    for ours in run_both(h_s, h_t, W, mask, T):
+        assert ours["loss"] == 0.0
+        assert not np.any(ours["dh"]) and not np.any(ours["dw"])
 
 
 @pytest.mark.parametrize("N,H,V", [(1, 64, 1), (1, 64, 129), (129, 192, 257), (333, 576, 1000), (256, 1024, 385),
@@ -109,7 +119,7 @@ def test_ragged_shapes(N, H, V):
     """N, V not multiples of the 128 tile; H = 576/1024/2048 and a non-multiple of 64."""
     h_s, h_t, W, mask, T = rand_problem(N, H, V, seed=N + V)
     mask[0] = True
-    ours = run_ours(h_s, h_t, W, mask, T)
+    ours = run_both(h_s, h_t, W, mask, T)
     loss, dh, dw, *_ = run_oracle_np(h_s, h_t, W, mask, T)
     assert_close(ours, loss, dh, dw, f"N{N} H{H} V{V}")
 
@@ -118,7 +128,7 @@ def test_temperature_and_peaky_teacher():
     h_s, h_t, W, mask, _ = rand_problem(400, 576, 2000, seed=5, tscale=4.0, p=0.25)
     mask[:8] = False
     for T in (2.0, 0.5):
-        ours = run_ours(h_s, h_t, W, mask, T)
+        ours = run_both(h_s, h_t, W, mask, T)
         loss, dh, dw, *_ = run_oracle_np(h_s, h_t, W, mask, T)
         assert_close(ours, loss, dh, dw, f"T={T}")
 
@@ -128,15 +138,21 @@ def test_chunking_invariance():
     h_s, h_t, W, mask, T = rand_problem(300, 128, 1500, seed=6)
     a = run_ours(h_s, h_t, W, mask, T)
     b = run_ours(h_s, h_t, W, mask, T, workspace_bytes=4096 + 300 * 128 * 2)
+    c = run_ours(h_s, h_t, W, mask, T, path="fused", workspace_bytes=256 * 1024)  # several fused chunks
+    for k in ("dh", "dw"):
+        mr, cos = O.grad_metrics(c[k], a[k])
+        assert mr < 1e-2 and cos > 0.99999, (k, mr, cos)
+    assert abs(c["loss"] - a["loss"]) <= 1e-4 * a["loss"]
     np.testing.assert_array_equal(a["dw"], b["dw"])  # dW chunks are computed independently
     mr, cos = O.grad_metrics(b["dh"], a["dh"])
     assert mr < 1e-5 and cos > 0.999999
 
 
-def test_upstream_grad_scales_linearly():
+@pytest.mark.parametrize("path", ["split", "fused"])
+def test_upstream_grad_scales_linearly(path):
     h_s, h_t, W, mask, T = rand_problem(200, 128, 600, seed=7)
-    a = run_ours(h_s, h_t, W, mask, T)
-    b = run_ours(h_s, h_t, W, mask, T, grad=3.0)
+    a = run_ours(h_s, h_t, W, mask, T, path=path)
+    b = run_ours(h_s, h_t, W, mask, T, grad=3.0, path=path)
     # dZ is stored in bf16, so 3*round(dz) and round(3*dz) differ by one rounding
     for k in ("dh", "dw"):
         mr, cos = O.grad_metrics(b[k], 3.0 * a[k])
@@ -164,7 +180,7 @@ def test_benchmark_configs_full_size(cfg):
     """Full-size configurations against the fp32 torch oracle run on the GPU."""
     n = 12288 - 37 if cfg == "c5" else None  # c5 also exercises a row count off the tile
     p = O.make_problem(cfg, n_rows=n)
-    ours = run_ours(p["h_s"], p["h_t"], p["W"], p["mask"], p["T"])
+    ours = run_both(p["h_s"], p["h_t"], p["W"], p["mask"], p["T"])
     # c1 is an fp32 configuration: compare with the fp32 reference on the unrounded inputs
     ref_loss, ref_dh, ref_dw = run_oracle_torch_gpu(p["h_s"], p["h_t"], p["W"], p["mask"], p["T"],
                                                     round_inputs=(cfg != "c1"))
@@ -174,6 +190,6 @@ def test_benchmark_configs_full_size(cfg):
 def test_c3_shape_subsample():
     """H=2048 (1.7B-shaped) on a 4096-row subsample of the 65,536-row configuration."""
     p = O.make_problem("c3", n_rows=4096)
-    ours = run_ours(p["h_s"], p["h_t"], p["W"], p["mask"], p["T"])
+    ours = run_both(p["h_s"], p["h_t"], p["W"], p["mask"], p["T"])
     ref_loss, ref_dh, ref_dw = run_oracle_torch_gpu(p["h_s"], p["h_t"], p["W"], p["mask"], p["T"])
     assert_close(ours, ref_loss, ref_dh, ref_dw, "c3-sub")
