@@ -56,16 +56,17 @@ EncodeTiledFn encode_fn() {
 // 2-D bf16 tensor map, 128-byte (default) or 64-byte swizzle, zero fill out of bounds.
 // inner = contiguous extent (elements), outer = row count, ld = row stride (elements).
 bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
-              uint32_t box_outer, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+              uint32_t box_outer, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B,
+              CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
+  const uint64_t esize = dt == CU_TENSOR_MAP_DATA_TYPE_FLOAT32 ? 4 : 2;
   cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {ld * 2};
+  cuuint64_t strides[1] = {ld * esize};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t es[2] = {1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // Per-launch timing trace (klg_trace_begin / klg_trace_end).
@@ -159,18 +160,17 @@ cudaError_t set_smem(Kern k, int bytes) {
   return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
-template <int MODE>
-int launch_dual(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMap& mw, const CUtensorMap& mout,
-                const klg::DualArgs& a, cudaStream_t s) {
-  auto k = klg::dual_kernel<MODE>;
-  constexpr int smem = klg::dual_smem(MODE);
+int launch_dual(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMap& mw, const klg::DualArgs& a,
+                cudaStream_t s) {
+  auto k = klg::dual_kernel;
+  constexpr int smem = klg::DUAL_SMEM;
   cudaError_t e = set_smem(k, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dual_kernel)");
   const int grid = a.n_units < num_sms() ? a.n_units : num_sms();
   const int slot = trace_pre(s);
-  k<<<grid, klg::NUM_THREADS, smem, s>>>(mhs, mht, mw, mout, a);
+  k<<<grid, klg::NUM_THREADS, smem, s>>>(mhs, mht, mw, a);
   e = cudaGetLastError();
-  trace_post(slot, s, MODE == klg::MODE_STATS ? KLG_KIND_STATS : KLG_KIND_DZ);
+  trace_post(slot, s, KLG_KIND_STATS);
   if (e != cudaSuccess) return cuda_fail(e, "launch dual_kernel");
   ++g_launches;
   return KLG_OK;
@@ -178,13 +178,16 @@ int launch_dual(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMa
 
 int launch_lse_pair(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMap& mw, const klg::LseArgs& a,
                     cudaStream_t s) {
-  cudaError_t e = set_smem(klg::lse_pair_kernel, klg::LSE_SMEM);
+  const bool res = a.n_kb <= klg::LSE_RES_MAX_KB;
+  auto k = res ? klg::lse_pair_kernel<true> : klg::lse_pair_kernel<false>;
+  const int smem = res ? klg::LSE_RES_SMEM : klg::LSE_SMEM;
+  cudaError_t e = set_smem(k, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(lse_pair_kernel)");
   const int pairs = a.n_units < num_sms() / 2 ? a.n_units : num_sms() / 2;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
   cfg.blockDim = dim3(klg::LSE_THREADS);
-  cfg.dynamicSmemBytes = klg::LSE_SMEM;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -194,7 +197,7 @@ int launch_lse_pair(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtens
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const int slot = trace_pre(s);
-  e = cudaLaunchKernelEx(&cfg, klg::lse_pair_kernel, mhs, mht, mw, a);
+  e = cudaLaunchKernelEx(&cfg, k, mhs, mht, mw, a);
   trace_post(slot, s, KLG_KIND_STATS);
   if (e != cudaSuccess) return cuda_fail(e, "launch lse_pair_kernel");
   ++g_launches;
@@ -255,7 +258,7 @@ void build_schedule(const klg::PairGemmArgs& g, int t_begin, int t_end, int pair
 
 template <int BN>
 int launch_gemm_pair_t(const CUtensorMap& a0, const CUtensorMap& b0, const CUtensorMap& a1, const CUtensorMap& b1,
-                       const klg::PairGemmArgs& g, cudaStream_t s) {
+                       const CUtensorMap& c0, const CUtensorMap& c1, const klg::PairGemmArgs& g, cudaStream_t s) {
   using Cfg = klg::PairGemmCfg<BN>;
   auto k = klg::gemm_pair_kernel<BN>;
   cudaError_t e = set_smem(k, Cfg::SMEM);
@@ -279,7 +282,7 @@ int launch_gemm_pair_t(const CUtensorMap& a0, const CUtensorMap& b0, const CUten
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     const int slot = trace_pre(s);
-    e = cudaLaunchKernelEx(&cfg, k, a0, b0, a1, b1, g, sc);
+    e = cudaLaunchKernelEx(&cfg, k, a0, b0, a1, b1, c0, c1, g, sc);
     trace_post(slot, s, KLG_KIND_GEMM);
     if (e != cudaSuccess) return cuda_fail(e, "launch gemm_pair_kernel");
     ++g_launches;
@@ -288,50 +291,29 @@ int launch_gemm_pair_t(const CUtensorMap& a0, const CUtensorMap& b0, const CUten
 }
 
 int launch_gemm_pair(int bn, const CUtensorMap& a0, const CUtensorMap& b0, const CUtensorMap& a1, const CUtensorMap& b1,
-                     const klg::PairGemmArgs& g, cudaStream_t s) {
+                     const CUtensorMap& c0, const CUtensorMap& c1, const klg::PairGemmArgs& g, cudaStream_t s) {
   switch (bn) {
-    case 128: return launch_gemm_pair_t<128>(a0, b0, a1, b1, g, s);
-    case 192: return launch_gemm_pair_t<192>(a0, b0, a1, b1, g, s);
-    default: return launch_gemm_pair_t<256>(a0, b0, a1, b1, g, s);
-  }
-}
-
-template <int BN>
-int launch_grouped_t(const CUtensorMap& a0, const CUtensorMap& b0, const CUtensorMap& a1, const CUtensorMap& b1,
-                     const klg::GroupedArgs& g, cudaStream_t s) {
-  auto k = klg::gemm_grouped_kernel<BN>;
-  constexpr int smem = klg::GemmCfg<BN>::SMEM;
-  cudaError_t e = set_smem(k, smem);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm_grouped_kernel)");
-  const int grid = g.n_tiles < num_sms() ? g.n_tiles : num_sms();
-  const int slot = trace_pre(s);
-  k<<<grid, klg::NUM_THREADS, smem, s>>>(a0, b0, a1, b1, g);
-  e = cudaGetLastError();
-  trace_post(slot, s, KLG_KIND_GEMM);
-  if (e != cudaSuccess) return cuda_fail(e, "launch gemm_grouped_kernel");
-  ++g_launches;
-  return KLG_OK;
-}
-
-int launch_grouped(int bn, const CUtensorMap& a0, const CUtensorMap& b0, const CUtensorMap& a1, const CUtensorMap& b1,
-                   const klg::GroupedArgs& g, cudaStream_t s) {
-  switch (bn) {
-    case 128: return launch_grouped_t<128>(a0, b0, a1, b1, g, s);
-    case 192: return launch_grouped_t<192>(a0, b0, a1, b1, g, s);
-    default: return launch_grouped_t<256>(a0, b0, a1, b1, g, s);
+    case 128: return launch_gemm_pair_t<128>(a0, b0, a1, b1, c0, c1, g, s);
+    case 192: return launch_gemm_pair_t<192>(a0, b0, a1, b1, c0, c1, g, s);
+    default: return launch_gemm_pair_t<256>(a0, b0, a1, b1, c0, c1, g, s);
   }
 }
 
 klg::GemmProblem gemm_problem(bool on, int M, int Ncol, int K, int bn, float* C, int ldc, int accumulate, int a_k0,
-                              int b_k0, int a_mn, int bm = klg::BM) {
+                              int b_k0, int a_mn, int bm = klg::BM, int n_split = 1, int c_row0 = 0) {
   klg::GemmProblem g{};
   g.M = M;
   g.Ncol = Ncol;
   g.K = K;
   g.n_mt = cdiv(M, bm);
   g.n_nt = cdiv(Ncol, bn);
-  g.n_tiles = on ? g.n_mt * g.n_nt : 0;
   g.n_kb = cdiv(K, klg::BK);
+  if (n_split > g.n_kb) n_split = g.n_kb;
+  if (n_split < 1) n_split = 1;
+  g.kb_per_split = cdiv(g.n_kb, n_split);
+  g.n_split = cdiv(g.n_kb, g.kb_per_split);
+  g.c_row0 = c_row0;
+  g.n_tiles = on ? g.n_mt * g.n_nt * g.n_split : 0;
   g.C = C;
   g.ldc = ldc;
   g.accumulate = accumulate;
@@ -414,7 +396,7 @@ int klg_fwd_stats(const void* hs, const void* ht, const void* w, int64_t n_rows,
       !make_map(&mht, ht, hidden, n_rows, hidden, klg::BK, klg::BM) ||
       !make_map(&mw, w, hidden, vocab, hidden, klg::BK, klg::DUAL_BN))
     return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
-  return launch_dual<klg::MODE_STATS>(mhs, mht, mw, mw, a, (cudaStream_t)stream);
+  return launch_dual(mhs, mht, mw, a, (cudaStream_t)stream);
 }
 
 int klg_merge_stats(const float* partials, int n_part, int64_t n_rows, float* stats, void* stream) {
@@ -496,11 +478,14 @@ int64_t klg_bwd_chunk_cols(int64_t n_rows, int64_t vocab, int64_t workspace_byte
 int64_t klg_bwd_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t vocab) {
   (void)hidden;
   if (n_rows < 1 || vocab < 1) return -1;
+  // dZ chunk of up to 256 MiB (at least 2048 columns): fewer, fuller launches beat an
+  // L2-resident chunk (measured: 64 MiB chunks were 30 % slower at the 16k-row shape)
   const int64_t full = (int64_t)cdiv(vocab, 128) * 128;
   int64_t cols = (256ll << 20) / (n_rows * 2);
   cols = (cols / 128) * 128;
   if (cols < 2048) cols = 2048;
   if (cols > full) cols = full;
+  while (cdiv(vocab, cols) > KLG_BWD_HEADER / 4) cols += 128;
   return KLG_BWD_HEADER + n_rows * cols * 2;
 }
 
@@ -508,8 +493,8 @@ int64_t klg_bwd_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t vocab) {
 
 namespace {
 
-// Pass 2 over vocab chunks of `cols` columns: dZ chunk (dual_kernel<MODE_DZ>) then one
-// grouped GEMM launch for dW_chunk and dH.  With a_parts set, the dZ pass also writes the
+// Pass 2 over vocab chunks of `cols` columns: dZ chunk (dz_pair_kernel) then one
+// pair-GEMM launch for dW_chunk and dH.  With a_parts set, the dZ pass also writes the
 // per-unit KL cross-term partials (at most 8 units per chunk), returning their count.
 int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask, const float* lse, const float* count,
               const float* grad, int64_t n_rows, int64_t hidden, int64_t vocab, float inv_temp, float* d_hs, float* d_w,
@@ -523,6 +508,19 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
       !make_map(&mw_mn, w, hidden, vocab, hidden, 32, klg::BK, CU_TENSOR_MAP_SWIZZLE_64B) ||
       !make_map(&mhs_mn, hs, hidden, n_rows, hidden, 32, klg::BK, CU_TENSOR_MAP_SWIZZLE_64B))
     return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+  // fp32 outputs, accumulated by TMA reduce-add from zero
+  alignas(64) CUtensorMap mdw, mdh;
+  if ((d_w && !make_map(&mdw, d_w, hidden, vocab, hidden, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_DATA_TYPE_FLOAT32)) ||
+      (d_hs && !make_map(&mdh, d_hs, hidden, n_rows, hidden, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_DATA_TYPE_FLOAT32)))
+    return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed (outputs)");
+  if (!d_w) mdw = mhs;   // unused placeholders
+  if (!d_hs) mdh = mhs;
+  cudaError_t ze = cudaSuccess;
+  if (d_w) ze = cudaMemsetAsync(d_w, 0, sizeof(float) * vocab * hidden, s);
+  if (ze == cudaSuccess && d_hs) ze = cudaMemsetAsync(d_hs, 0, sizeof(float) * n_rows * hidden, s);
+  if (ze != cudaSuccess) return cuda_fail(ze, "cudaMemsetAsync(gradients)");
 
   klg::DualArgs a{};
   a.n_rows = (int)n_rows;
@@ -550,23 +548,29 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
     plan_dual(a.n_rt, a.n_vt, num_sms() / 2, a.vt_per_unit, n_uv, a_parts ? 8 : 64);
     a.n_units = a.n_rt * n_uv;
     a.a_part_base = n_ap;
-    n_ap += 2 * n_uv;   // one cross-term partial per unit and 64-column half
+    n_ap += klg::DZP_CSPLIT * n_uv;   // one cross-term partial per unit and column slice
     alignas(64) CUtensorMap mdz_out;
-    if (!make_map(&mdz_out, dz, wv, n_rows, cols, 64, 32)) return fail(KLG_ERR_CUDA, "tensor map (dz store)");
+    if (!make_map(&mdz_out, dz, wv, n_rows, cols, klg::DZP_COLS_PER_WARP, 32,
+                  klg::DZP_COLS_PER_WARP == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
+      return fail(KLG_ERR_CUDA, "tensor map (dz store)");
     if ((rc = launch_dz_pair(mhs, mht, mw, mdz_out, a, s))) return rc;
     if (!d_hs && !d_w) continue;
     // one grouped launch: problem 0 = dW chunk (longer tiles first), problem 1 = dH += dZ W_chunk
     alignas(64) CUtensorMap mdz_k, mdz_mn;
     if (!make_map(&mdz_k, dz, wv, n_rows, cols, klg::BK, klg::BM) || !make_map(&mdz_mn, dz, wv, n_rows, cols, 64, klg::BK))
       return fail(KLG_ERR_CUDA, "tensor map (dz operand)");
+    // dW's K (all rows) is split in two when its tiles would be much longer than dH's
+    // (K = chunk width).  At most two partial sums meet in any dW element, and the
+    // reduce-adds onto zero give the same bits in either order, so dW stays deterministic.
+    const int split = n_rows >= 2 * wv ? 2 : 1;
     klg::PairGemmArgs g{};
-    g.p[0] = gemm_problem(d_w != nullptr, (int)wv, (int)hidden, (int)n_rows, bn, d_w ? d_w + v0 * hidden : nullptr,
-                          (int)hidden, 0, 0, 0, 1, 256);
-    g.p[1] = gemm_problem(d_hs != nullptr, (int)n_rows, (int)hidden, (int)wv, bn, d_hs, (int)hidden, v0 > 0, 0,
-                          (int)v0, 0, 256);
+    g.p[0] = gemm_problem(d_w != nullptr, (int)wv, (int)hidden, (int)n_rows, bn, nullptr, (int)hidden, 1, 0, 0, 1, 256,
+                          split, (int)v0);
+    g.p[1] = gemm_problem(d_hs != nullptr, (int)n_rows, (int)hidden, (int)wv, bn, nullptr, (int)hidden, 1, 0,
+                          (int)v0, 0, 256, 1, 0);
     g.n_tiles = g.p[0].n_tiles + g.p[1].n_tiles;
     (void)ci;
-    if ((rc = launch_gemm_pair(bn, mdz_mn, mhs_mn, mdz_k, mw_mn, g, s))) return rc;
+    if ((rc = launch_gemm_pair(bn, mdz_mn, mhs_mn, mdz_k, mw_mn, mdw, mdh, g, s))) return rc;
   }
   if (n_ap_out) *n_ap_out = n_ap;
   return KLG_OK;
@@ -580,7 +584,7 @@ int pass2_parts(int64_t n_rows, int64_t vocab, int64_t cols) {
     const int64_t wv = (vocab - v0) < cols ? (vocab - v0) : cols;
     int vpu, n_uv;
     plan_dual(n_rt, cdiv(wv, klg::DZP_BN), num_sms() / 2, vpu, n_uv, 8);
-    n_ap += 2 * n_uv;
+    n_ap += klg::DZP_CSPLIT * n_uv;
   }
   return n_ap;
 }
@@ -595,7 +599,7 @@ FwdBwdLayout fwd_bwd_layout(int64_t n_rows, int64_t vocab, int64_t workspace_byt
   FwdBwdLayout L{};
   int vpu, n_uv;
   plan_dual(2 * cdiv(n_rows, 256), cdiv(vocab, klg::LSE_BN), num_sms() / 2, vpu, n_uv);
-  L.n_lp = 2 * n_uv;
+  L.n_lp = klg::LSE_CSPLIT * n_uv;
   L.lse_parts_off = KLG_BWD_HEADER;
   L.a_parts_off = align256(L.lse_parts_off + (int64_t)L.n_lp * 2 * 2 * n_rows * 4);
   L.cols = -1;
@@ -687,7 +691,7 @@ int klg_fwd_bwd(const void* hs, const void* ht, const void* w, const uint8_t* ma
   la.n_kb = cdiv(hidden, klg::BK);
   la.scale_log2 = inv_temp * 1.4426950408889634f;
   la.parts = lse_parts;
-  if (2 * la.n_uv != L.n_lp) return fail(KLG_ERR_ARG, "internal plan mismatch");
+  if (klg::LSE_CSPLIT * la.n_uv != L.n_lp) return fail(KLG_ERR_ARG, "internal plan mismatch");
   if ((rc = launch_lse_pair(mhs, mht, mw, la, s))) return rc;
   {
     const int n2 = (int)(2 * n_rows);

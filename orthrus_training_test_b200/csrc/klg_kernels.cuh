@@ -37,12 +37,7 @@ constexpr int DUAL_BN = 128;
 constexpr int DUAL_STAGES = 4;
 constexpr int DUAL_STAGE_BYTES = 3 * TILE_128x64;  // A_s | A_t | B
 constexpr int DUAL_TMEM_COLS = 512;                // 2 buffers x (Z_s 128 | Z_t 128)
-constexpr int DUAL_STAGING_BYTES = 4 * 8192;          // MODE_DZ: per epilogue warp 32 rows x 128 bf16
-constexpr int dual_smem(int mode) {
-  return 1024 + DUAL_STAGES * DUAL_STAGE_BYTES + (mode == 1 ? DUAL_STAGING_BYTES : 0) + 256;
-}
-
-enum { MODE_STATS = 0, MODE_DZ = 1 };
+constexpr int DUAL_SMEM = 1024 + DUAL_STAGES * DUAL_STAGE_BYTES + 256;
 
 struct DualArgs {
   int n_rows;       // N
@@ -54,9 +49,9 @@ struct DualArgs {
   int n_units;      // n_rt * ceil(n_vt / vt_per_unit)
   int n_kb;         // ceil(H / 64)
   float scale_log2; // log2(e) / T
-  // MODE_STATS
+  // statistics pass (dual_kernel)
   float* partials;  // [n_uv][5][N]
-  // MODE_DZ
+  // dZ pass (dz_pair_kernel)
   const float* lse;      // [2][N] log2-domain log-sum-exp (student, teacher)
   const uint8_t* mask;   // [N]
   const float* count;    // device scalar: number of valid rows (global)
@@ -160,18 +155,15 @@ __device__ __forceinline__ void dz_chunk(const uint32_t (&bs)[32], const uint32_
   acc += a0 + a1;
 }
 
-// map_out (MODE_DZ only): the dZ chunk [N][v_count] with row stride ld_dz, box 64 x 32.
-template <int MODE>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ CUtensorMap map_ht,
-            const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_out, const DualArgs a) {
+            const __grid_constant__ CUtensorMap map_w, const DualArgs a) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t stg0 = sbase + DUAL_STAGES * DUAL_STAGE_BYTES;  // MODE_DZ staging (1024-aligned)
-  const uint32_t bar0 = stg0 + (MODE == MODE_DZ ? DUAL_STAGING_BYTES : 0);
+  const uint32_t bar0 = sbase + DUAL_STAGES * DUAL_STAGE_BYTES;
   const uint32_t full0 = bar0;                          // [STAGES]
   const uint32_t empty0 = bar0 + 8u * DUAL_STAGES;      // [STAGES]
   const uint32_t tfull0 = bar0 + 16u * DUAL_STAGES;     // [2]
@@ -205,8 +197,8 @@ dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ 
   volatile int* abort_p = &abort_flag;
 
   if (warp == 0) {
-    if (lane == 0) {
-      // ------------------------------------------------------------ TMA producer
+    {
+      // ------------------------------------------------------------ TMA producer (whole warp)
       int stage = 0;
       uint32_t phase = 0;
       long long issued = 0;
@@ -216,13 +208,15 @@ dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ 
         dual_unit(a, u, rt, uv, vt0, vt1);
         for (int vt = vt0; ok && vt < vt1; ++vt) {
           for (int kb = 0; kb < a.n_kb; ++kb) {
-            if (!mbar_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
-            const uint32_t sb = sbase + stage * DUAL_STAGE_BYTES;
-            const uint32_t fb = full0 + 8u * stage;
-            mbar_arrive_expect_tx(fb, DUAL_STAGE_BYTES);
-            tma_load_2d(sb, &map_hs, fb, kb * BK, rt * BM);
-            tma_load_2d(sb + TILE_128x64, &map_ht, fb, kb * BK, rt * BM);
-            tma_load_2d(sb + 2 * TILE_128x64, &map_w, fb, kb * BK, a.v_begin + vt * DUAL_BN);
+            if (!warp_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
+            if (elect_one()) {
+              const uint32_t sb = sbase + stage * DUAL_STAGE_BYTES;
+              const uint32_t fb = full0 + 8u * stage;
+              mbar_arrive_expect_tx(fb, DUAL_STAGE_BYTES);
+              tma_load_2d(sb, &map_hs, fb, kb * BK, rt * BM);
+              tma_load_2d(sb + TILE_128x64, &map_ht, fb, kb * BK, rt * BM);
+              tma_load_2d(sb + 2 * TILE_128x64, &map_w, fb, kb * BK, a.v_begin + vt * DUAL_BN);
+            }
             ++issued;
             if (++stage == DUAL_STAGES) { stage = 0; phase ^= 1; }
           }
@@ -231,8 +225,8 @@ dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ 
       drain_loads<DUAL_STAGES>(full0, stage, phase, issued);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ------------------------------------------------------------ MMA issuer
+    {
+      // ------------------------------------------------------------ MMA issuer (whole warp)
       constexpr uint32_t idesc = make_idesc_bf16(BM, DUAL_BN, false, false);
       int stage = 0;
       uint32_t phase = 0;
@@ -244,29 +238,31 @@ dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ 
         for (int vt = vt0; ok && vt < vt1; ++vt, ++tcount) {
           const int buf = tcount & 1;
           const uint32_t tph = (tcount >> 1) & 1;
-          if (!mbar_wait(tempty0 + 8u * buf, tph ^ 1, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
+          if (!warp_wait(tempty0 + 8u * buf, tph ^ 1, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
           tc_fence_after();
           const uint32_t d_s = tmem + buf * 256;
           const uint32_t d_t = d_s + 128;
           for (int kb = 0; kb < a.n_kb; ++kb) {
-            if (!mbar_wait(full0 + 8u * stage, phase, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
+            if (!warp_wait(full0 + 8u * stage, phase, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t sb = sbase + stage * DUAL_STAGE_BYTES;
+            if (elect_one()) {
+              const uint32_t sb = sbase + stage * DUAL_STAGE_BYTES;
 #pragma unroll
-            for (int k = 0; k < BK / 16; ++k) {
-              const uint64_t bdesc = desc_kmajor(sb + 2 * TILE_128x64, k);
-              const uint32_t acc = (kb | k) != 0;
-              mma_bf16(d_s, desc_kmajor(sb, k), bdesc, idesc, acc);
-              mma_bf16(d_t, desc_kmajor(sb + TILE_128x64, k), bdesc, idesc, acc);
+              for (int k = 0; k < BK / 16; ++k) {
+                const uint64_t bdesc = desc_kmajor(sb + 2 * TILE_128x64, k);
+                const uint32_t acc = (kb | k) != 0;
+                mma_bf16(d_s, desc_kmajor(sb, k), bdesc, idesc, acc);
+                mma_bf16(d_t, desc_kmajor(sb + TILE_128x64, k), bdesc, idesc, acc);
+              }
+              mma_commit(empty0 + 8u * stage);
             }
-            mma_commit(empty0 + 8u * stage);
             if (++stage == DUAL_STAGES) { stage = 0; phase ^= 1; }
           }
-          if (ok) mma_commit(tfull0 + 8u * buf);
+          if (ok && elect_one()) mma_commit(tfull0 + 8u * buf);
         }
       }
       // all issued MMAs must retire before TMEM is released
-      mma_commit(done_bar);
+      if (elect_one()) mma_commit(done_bar);
       mbar_wait_drain(done_bar, 0);
     }
   } else {
@@ -274,7 +270,6 @@ dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ 
     const int q = warp & 3;                 // TMEM lane quarter of this warp
     const int r_in_tile = q * 32 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
-    const uint32_t stg = stg0 + (uint32_t)(warp - EPI_WARP0) * 8192u;  // this warp's dZ staging (2 x 4 KB)
     int tcount = 0;
     bool ok = true;
     for (int u = blockIdx.x; ok && u < a.n_units; u += gridDim.x) {
@@ -282,82 +277,27 @@ dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ 
       dual_unit(a, u, rt, uv, vt0, vt1);
       const int row = rt * BM + r_in_tile;
       const bool row_ok = row < a.n_rows;
-      // per-row state
-      float ms = NEG_BIG, Ss = 0.f, mt = NEG_BIG, St = 0.f, A = 0.f;  // STATS
-      float Ls = 0.f, Lt = 0.f, coef = 0.f, acc = 0.f;                 // DZ
-      if (MODE == MODE_DZ && row_ok) {
-        Ls = a.lse[row];
-        Lt = a.lse[a.n_rows + row];
-        const float cnt = *a.count;
-        const float g = a.grad ? *a.grad : 1.0f;
-        coef = (a.mask[row] && cnt > 0.f) ? g / cnt * a.inv_temp : 0.f;
-      }
+      float ms = NEG_BIG, Ss = 0.f, mt = NEG_BIG, St = 0.f, A = 0.f;
       for (int vt = vt0; ok && vt < vt1; ++vt, ++tcount) {
         const int buf = tcount & 1;
         const uint32_t tph = (tcount >> 1) & 1;
         if (!mbar_wait(tfull0 + 8u * buf, tph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) { ok = false; break; }
         tc_fence_after();
-        if (MODE == MODE_DZ) {
-          if (lane == 0) bulk_wait_read0();   // staging free: previous tile's stores have read it
-          __syncwarp();
-        }
         const uint32_t tbase = lane_addr + buf * 256;
-        if (MODE == MODE_STATS) {
-          // load -> wait -> update per 32-column chunk
+        // load -> wait -> update per 32-column chunk
 #pragma unroll 1
-          for (int c = 0; c < DUAL_BN / 32; ++c) {
-            uint32_t bs[32], bt[32];
-            tmem_ld32_raw(tbase + c * 32, bs);
-            tmem_ld32_raw(tbase + 128 + c * 32, bt);
-            tmem_wait_ld_regs(bs, bt);
-            const int nvalid = min(32, a.v_count - (vt * DUAL_BN + c * 32));
-            if (nvalid > 0) stats_chunk(bs, bt, nvalid, a.scale_log2, ms, Ss, mt, St, A);
-          }
-        } else {
-          // TMEM reads software-pipelined: chunk c+1 is in flight while chunk c is processed.
-          uint32_t bs[2][32], bt[2][32];
-          tmem_ld32_raw(tbase, bs[0]);
-          tmem_ld32_raw(tbase + 128, bt[0]);
-          tmem_wait_ld_regs(bs[0], bt[0]);
-#pragma unroll
-          for (int c = 0; c < DUAL_BN / 32; ++c) {
-            const int cur = c & 1;
-            if (c + 1 < DUAL_BN / 32) {
-              tmem_ld32_raw(tbase + (c + 1) * 32, bs[cur ^ 1]);
-              tmem_ld32_raw(tbase + 128 + (c + 1) * 32, bt[cur ^ 1]);
-            }
-            const int nvalid = a.v_count - (vt * DUAL_BN + c * 32);
-            if (nvalid > 0) {
-              uint32_t pk[16];
-              dz_chunk(bs[cur], bt[cur], nvalid, a.scale_log2, Ls, Lt, coef, pk, acc);
-              // 128-byte-swizzled staging row: 16-byte chunk j of row r lives at chunk j ^ (r % 8)
-              const uint32_t rowp = stg + (uint32_t)(c >> 1) * 4096u + (uint32_t)lane * 128u;
-#pragma unroll
-              for (int k = 0; k < 4; ++k) {
-                const uint32_t j = (uint32_t)((c & 1) * 4 + k);
-                st_shared_v4(rowp + ((j ^ (uint32_t)(lane & 7)) << 4), pk[4 * k], pk[4 * k + 1], pk[4 * k + 2],
-                             pk[4 * k + 3]);
-              }
-            }
-            if (c + 1 < DUAL_BN / 32) tmem_wait_ld_regs(bs[cur ^ 1], bt[cur ^ 1]);
-          }
+        for (int c = 0; c < DUAL_BN / 32; ++c) {
+          uint32_t bs[32], bt[32];
+          tmem_ld32_raw(tbase + c * 32, bs);
+          tmem_ld32_raw(tbase + 128 + c * 32, bt);
+          tmem_wait_ld_regs(bs, bt);
+          const int nvalid = min(32, a.v_count - (vt * DUAL_BN + c * 32));
+          if (nvalid > 0) stats_chunk(bs, bt, nvalid, a.scale_log2, ms, Ss, mt, St, A);
         }
         tc_fence_before();
         mbar_arrive(tempty0 + 8u * buf);
-        if (MODE == MODE_DZ) {
-          fence_async_shared();
-          __syncwarp();
-          const int x0 = vt * DUAL_BN, y0 = rt * BM + q * 32;
-          if (lane == 0 && y0 < a.n_rows) {
-            tma_store_2d(&map_out, stg, x0, y0);
-            if (x0 + 64 < a.v_count) tma_store_2d(&map_out, stg + 4096, x0 + 64, y0);
-            bulk_commit();
-          }
-        }
       }
-      if (MODE == MODE_DZ && ok && row_ok && a.a_parts)
-        a.a_parts[(size_t)(a.a_part_base + uv) * a.n_rows + row] = acc * a.scale_log2;
-      if (MODE == MODE_STATS && ok && row_ok) {
+      if (ok && row_ok) {
         float* p = a.partials + (size_t)uv * 5 * a.n_rows + row;
         p[0] = ms;
         p[(size_t)a.n_rows] = Ss;
@@ -366,7 +306,6 @@ dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ 
         p[(size_t)4 * a.n_rows] = A;
       }
     }
-    if (MODE == MODE_DZ && lane == 0) bulk_wait0();   // dZ stores complete before exit
   }
   tc_fence_before();
   __syncthreads();
@@ -380,9 +319,9 @@ dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ 
 // One view at a time (student rows, then teacher rows): per unit (view, 256-row pair
 // tile, vocab range) the pair computes 256 x 256 logit tiles with
 // tcgen05.mma.cta_group::2 (each CTA: its own 128 rows as A, its half of the W tile as
-// B) into double-buffered TMEM, and 8 epilogue warps per CTA (two per TMEM lane
-// quarter, one per 128-column half) keep online (m, S) per row.  Output: partial
-// records parts[n_uv * 2 halves][2][2N] = (m, S) in log2 units, row index view*N + row.
+// B) into double-buffered TMEM, and LSE_CSPLIT epilogue warps per TMEM lane quarter
+// (each owning a column slice of the tile) keep online (m, S) per row.  Output: partial
+// records parts[n_uv * LSE_CSPLIT][2][2N] = (m, S) in log2 units, row index view*N + row.
 // The KL cross term is accumulated by the dZ pass, which has both views' values.
 // =====================================================================================
 constexpr int LSE_BN = 256;                                // vocab rows per pair tile
@@ -390,10 +329,20 @@ constexpr int LSE_STAGES = 6;
 constexpr int LSE_A_BYTES = TILE_128x64;                   // this CTA's 128 rows x 64
 constexpr int LSE_B_BYTES = (LSE_BN / 2) * BK * 2;         // this CTA's half of the W tile
 constexpr int LSE_STAGE_BYTES = LSE_A_BYTES + LSE_B_BYTES; // 32 KB
-constexpr int LSE_EPI_WARPS = 8;
+#ifndef KLG_EPI_SPLIT
+#define KLG_EPI_SPLIT 2
+#endif
+constexpr int LSE_CSPLIT = KLG_EPI_SPLIT;                  // epilogue warps per TMEM lane quarter
+constexpr int LSE_EPI_WARPS = 4 * LSE_CSPLIT;
+constexpr int LSE_COLS_PER_WARP = LSE_BN / LSE_CSPLIT;
 constexpr int LSE_THREADS = 64 + 32 * LSE_EPI_WARPS;
 constexpr int LSE_TMEM_COLS = 512;                         // 2 buffers x 256 columns
 constexpr int LSE_SMEM = 1024 + LSE_STAGES * LSE_STAGE_BYTES + 256;
+// Resident-A variant (H <= 576): the CTA's 128 x H row block stays in shared memory for a
+// whole unit and only the W halves stream, halving the bytes TMA writes per MMA.
+constexpr int LSE_RES_MAX_KB = 9;
+constexpr int LSE_RES_STAGES = 5;
+constexpr int LSE_RES_SMEM = 1024 + LSE_RES_MAX_KB * LSE_A_BYTES + LSE_RES_STAGES * LSE_B_BYTES + 256;
 
 struct LseArgs {
   int n_rows;       // N rows per view
@@ -405,7 +354,7 @@ struct LseArgs {
   int n_units;      // 2 * n_rp * n_uv
   int n_kb;         // ceil(H / 64)
   float scale_log2; // log2(e) / T
-  float* parts;     // [n_uv * 2][2][2N]
+  float* parts;     // [n_uv * LSE_CSPLIT][2][2N]
 };
 
 __device__ __forceinline__ void lse_unit(const LseArgs& a, int u, int& view, int& rp, int& uv, int& vt0, int& vt1) {
@@ -437,20 +386,27 @@ __device__ __forceinline__ void lse_chunk(const uint32_t (&b)[32], int nvalid, f
   S = fmaf(S, r, (s0 + s1) + (s2 + s3));
 }
 
+template <bool RES>
 __global__ void __launch_bounds__(LSE_THREADS, 1)
 lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ CUtensorMap map_ht,
                 const __grid_constant__ CUtensorMap map_w, const LseArgs a) {
+  constexpr int STAGES = RES ? LSE_RES_STAGES : LSE_STAGES;
+  constexpr int STAGE_BYTES = RES ? LSE_B_BYTES : LSE_STAGE_BYTES;   // W half [+ A k-block]
+  constexpr int A_REGION = RES ? LSE_RES_MAX_KB * LSE_A_BYTES : 0;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const uint32_t sbase = smem_u32(smem);
-  const uint32_t bar0 = sbase + LSE_STAGES * LSE_STAGE_BYTES;
+  const uint32_t abase = smem_u32(smem);               // resident A (RES)
+  const uint32_t sbase = abase + A_REGION;             // stage ring
+  const uint32_t bar0 = sbase + STAGES * STAGE_BYTES;
   const uint32_t full0 = bar0;                         // [STAGES] leader only: both CTAs' bytes
-  const uint32_t empty0 = bar0 + 8u * LSE_STAGES;      // [STAGES] each CTA
-  const uint32_t tfull0 = bar0 + 16u * LSE_STAGES;     // [2] each CTA
-  const uint32_t tempty0 = tfull0 + 16u;               // [2] leader only: 16 warp arrivals
+  const uint32_t empty0 = bar0 + 8u * STAGES;          // [STAGES] each CTA
+  const uint32_t tfull0 = bar0 + 16u * STAGES;         // [2] each CTA
+  const uint32_t tempty0 = tfull0 + 16u;               // [2] leader only: warp arrivals of both CTAs
   const uint32_t done_bar = tempty0 + 16u;
+  const uint32_t afull_bar = done_bar + 8u;            // RES: leader only, both CTAs' A bytes
+  const uint32_t aempty_bar = afull_bar + 8u;          // RES: each CTA
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
@@ -460,7 +416,7 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
-    for (int s = 0; s < LSE_STAGES; ++s) {
+    for (int s = 0; s < STAGES; ++s) {
       mbar_init(full0 + 8u * s, 2);
       mbar_init(empty0 + 8u * s, 1);
     }
@@ -469,6 +425,8 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
       mbar_init(tempty0 + 8u * b, 2 * LSE_EPI_WARPS);
     }
     mbar_init(done_bar, 1);
+    mbar_init(afull_bar, 2);
+    mbar_init(aempty_bar, 1);
     fence_mbar_init();
     tma_prefetch(&map_hs);
     tma_prefetch(&map_ht);
@@ -482,79 +440,111 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
   volatile int* abort_p = &abort_flag;
   const uint32_t lead_full0 = mapa_shared(full0, 0);
   const uint32_t lead_tempty0 = mapa_shared(tempty0, 0);
+  const uint32_t lead_afull = mapa_shared(afull_bar, 0);
   const uint32_t peer_empty0 = mapa_shared(empty0, 1);
   const uint32_t peer_tfull0 = mapa_shared(tfull0, 1);
+  const uint32_t peer_aempty = mapa_shared(aempty_bar, 1);
 
   if (warp == 0) {
-    if (lane == 0) {
-      // ------------------------------------------------------------ TMA producer (both CTAs)
+    {
+      // ------------------------------------------------------------ TMA producer (both CTAs, whole warp)
       int stage = 0;
       uint32_t phase = 0;
       long long issued = 0;
+      int ucount = 0;
       bool ok = true;
-      for (int u = cid; ok && u < a.n_units; u += n_clusters) {
+      for (int u = cid; ok && u < a.n_units; u += n_clusters, ++ucount) {
         int view, rp, uv, vt0, vt1;
         lse_unit(a, u, view, rp, uv, vt0, vt1);
         const CUtensorMap* ma = view ? &map_ht : &map_hs;
         const int row0 = rp * 256 + (int)rank * 128;
+        if (RES) {
+          // this unit's rows: wait until the previous unit's MMAs released the A region
+          if (!warp_wait(aempty_bar, (uint32_t)(ucount & 1) ^ 1u, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) break;
+          if (elect_one()) {
+            if (leader) mbar_arrive_expect_tx(afull_bar, 2 * a.n_kb * LSE_A_BYTES);
+            for (int kb = 0; kb < a.n_kb; ++kb)
+              tma_load_2d_pair(abase + kb * LSE_A_BYTES, ma, lead_afull, kb * BK, row0);
+            if (!leader) mbar_arrive_cluster(lead_afull);
+          }
+        }
         for (int vt = vt0; ok && vt < vt1; ++vt) {
           for (int kb = 0; kb < a.n_kb; ++kb) {
-            if (!mbar_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
-            const uint32_t sa = sbase + stage * LSE_STAGE_BYTES;
-            const uint32_t fb = lead_full0 + 8u * stage;
-            if (leader) mbar_arrive_expect_tx(full0 + 8u * stage, 2 * LSE_STAGE_BYTES);
-            tma_load_2d_pair(sa, ma, fb, kb * BK, row0);
-            tma_load_2d_pair(sa + LSE_A_BYTES, &map_w, fb, kb * BK, vt * LSE_BN + (int)rank * (LSE_BN / 2));
-            if (!leader) mbar_arrive_cluster(fb);
+            if (!warp_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
+            if (elect_one()) {
+              const uint32_t sa = sbase + stage * STAGE_BYTES;
+              const uint32_t fb = lead_full0 + 8u * stage;
+              if (leader) mbar_arrive_expect_tx(full0 + 8u * stage, 2 * STAGE_BYTES);
+              if (!RES) tma_load_2d_pair(sa, ma, fb, kb * BK, row0);
+              tma_load_2d_pair(sa + (RES ? 0 : LSE_A_BYTES), &map_w, fb, kb * BK,
+                               vt * LSE_BN + (int)rank * (LSE_BN / 2));
+              if (!leader) mbar_arrive_cluster(fb);
+            }
             ++issued;
-            if (++stage == LSE_STAGES) { stage = 0; phase ^= 1; }
+            if (++stage == STAGES) { stage = 0; phase ^= 1; }
           }
         }
       }
-      if (leader) drain_loads<LSE_STAGES>(full0, stage, phase, issued);
+      if (leader) {
+        drain_loads<STAGES>(full0, stage, phase, issued);
+        if (RES && ucount > 0) mbar_wait_drain(afull_bar, (uint32_t)((ucount - 1) & 1));
+      }
     }
   } else if (warp == 1) {
-    if (lane == 0 && leader) {
-      // ------------------------------------------------------------ pair MMA issuer (leader)
+    if (leader) {
+      // ------------------------------------------------------------ pair MMA issuer (leader, whole warp)
       constexpr uint32_t idesc = make_idesc_bf16(2 * BM, LSE_BN, false, false);
       int stage = 0;
       uint32_t phase = 0;
       int tcount = 0;
+      int ucount = 0;
       bool ok = true;
-      for (int u = cid; ok && u < a.n_units; u += n_clusters) {
+      for (int u = cid; ok && u < a.n_units; u += n_clusters, ++ucount) {
         int view, rp, uv, vt0, vt1;
         lse_unit(a, u, view, rp, uv, vt0, vt1);
+        if (RES) {
+          if (!warp_wait(afull_bar, (uint32_t)(ucount & 1), abort_p, KLG_STATUS_TIMEOUT_MMA)) break;
+          tc_fence_after();
+        }
         for (int vt = vt0; ok && vt < vt1; ++vt, ++tcount) {
           const int buf = tcount & 1;
           const uint32_t tph = (tcount >> 1) & 1;
-          if (!mbar_wait(tempty0 + 8u * buf, tph ^ 1, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
+          if (!warp_wait(tempty0 + 8u * buf, tph ^ 1, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
           tc_fence_after();
           const uint32_t d = tmem + buf * LSE_BN;
           for (int kb = 0; kb < a.n_kb; ++kb) {
-            if (!mbar_wait(full0 + 8u * stage, phase, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
+            if (!warp_wait(full0 + 8u * stage, phase, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t sa = sbase + stage * LSE_STAGE_BYTES;
+            if (elect_one()) {
+              const uint32_t sa = sbase + stage * STAGE_BYTES;
+              const uint32_t a_tile = RES ? abase + kb * LSE_A_BYTES : sa;
+              const uint32_t b_tile = RES ? sa : sa + LSE_A_BYTES;
 #pragma unroll
-            for (int k = 0; k < BK / 16; ++k)
-              mma_bf16_pair(d, desc_kmajor(sa, k), desc_kmajor(sa + LSE_A_BYTES, k), idesc, (kb | k) != 0);
-            mma_commit_pair(empty0 + 8u * stage);
-            mma_commit_pair(peer_empty0 + 8u * stage);
-            if (++stage == LSE_STAGES) { stage = 0; phase ^= 1; }
+              for (int k = 0; k < BK / 16; ++k)
+                mma_bf16_pair(d, desc_kmajor(a_tile, k), desc_kmajor(b_tile, k), idesc, (kb | k) != 0);
+              mma_commit_pair(empty0 + 8u * stage);
+              mma_commit_pair(peer_empty0 + 8u * stage);
+            }
+            if (++stage == STAGES) { stage = 0; phase ^= 1; }
           }
-          if (ok) {
+          if (ok && elect_one()) {
             mma_commit_pair(tfull0 + 8u * buf);
             mma_commit_pair(peer_tfull0 + 8u * buf);
           }
         }
+        if (RES && ok && elect_one()) {   // the unit's MMAs are issued: release the A region once they complete
+          mma_commit_pair(aempty_bar);
+          mma_commit_pair(peer_aempty);
+        }
       }
-      mma_commit_pair(done_bar);
+      if (elect_one()) mma_commit_pair(done_bar);
       mbar_wait_drain(done_bar, 0);
     }
   } else {
     // -------------------------------------------------------------- epilogue (both CTAs)
     const int q = warp & 3;
-    const int h = (warp - EPI_WARP0) >> 2;        // 128-column half of the 256-column tile
-    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 128);
+    const int h = (warp - EPI_WARP0) >> 2;        // column slice of the 256-column tile
+    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * LSE_COLS_PER_WARP);
     int tcount = 0;
     bool ok = true;
     for (int u = cid; ok && u < a.n_units; u += n_clusters) {
@@ -567,9 +557,9 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
         const uint32_t tph = (tcount >> 1) & 1;
         if (!mbar_wait(tfull0 + 8u * buf, tph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) { ok = false; break; }
         tc_fence_after();
-        const int col_base = vt * LSE_BN + h * 128;
+        const int col_base = vt * LSE_BN + h * LSE_COLS_PER_WARP;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < LSE_COLS_PER_WARP / 32; ++c) {
           uint32_t b0[32];
           tmem_ld32_raw(lane_addr + buf * LSE_BN + c * 32, b0);
           tmem_wait_ld_regs(b0);
@@ -585,7 +575,7 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
       }
       if (ok && row < a.n_rows) {
         const size_t n2 = 2 * (size_t)a.n_rows;
-        float* p = a.parts + ((size_t)(uv * 2 + h) * 2) * n2 + (size_t)view * a.n_rows + row;
+        float* p = a.parts + ((size_t)(uv * LSE_CSPLIT + h) * 2) * n2 + (size_t)view * a.n_rows + row;
         p[0] = m;
         p[n2] = S;
       }
@@ -610,12 +600,15 @@ constexpr int DZP_BN = 128;
 constexpr int DZP_STAGES = 4;
 constexpr int DZP_B_BYTES = (DZP_BN / 2) * BK * 2;                        // 8 KB
 constexpr int DZP_STAGE_BYTES = 2 * TILE_128x64 + DZP_B_BYTES;            // 40 KB
-constexpr int DZP_EPI_WARPS = 8;
+constexpr int DZP_CSPLIT = KLG_EPI_SPLIT;                                 // epilogue warps per lane quarter
+constexpr int DZP_EPI_WARPS = 4 * DZP_CSPLIT;
+constexpr int DZP_COLS_PER_WARP = DZP_BN / DZP_CSPLIT;                    // 64 or 32
 constexpr int DZP_THREADS = 64 + 32 * DZP_EPI_WARPS;
-constexpr int DZP_STAGING_BYTES = DZP_EPI_WARPS * 4096;                   // 32 rows x 64 bf16 per warp
+constexpr int DZP_STAGING_BYTES = DZP_EPI_WARPS * 32 * DZP_COLS_PER_WARP * 2;   // 32 rows per warp
 constexpr int DZP_SMEM = 1024 + DZP_STAGES * DZP_STAGE_BYTES + DZP_STAGING_BYTES + 256;
 
-// Units: n_rt counts 256-row pair tiles; a_parts rows: a_part_base + uv * 2 + column half.
+// Units: n_rt counts 256-row pair tiles; a_parts rows: a_part_base + uv * DZP_CSPLIT + column slice.
+// Staging rows are DZP_COLS_PER_WARP bf16 wide (128 or 64 bytes) in the matching TMA swizzle.
 __global__ void __launch_bounds__(DZP_THREADS, 1)
 dz_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ CUtensorMap map_ht,
                const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_out,
@@ -668,7 +661,7 @@ dz_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant
   const uint32_t peer_tfull0 = mapa_shared(tfull0, 1);
 
   if (warp == 0) {
-    if (lane == 0) {
+    {   // TMA producer (both CTAs, whole warp)
       int stage = 0;
       uint32_t phase = 0;
       long long issued = 0;
@@ -679,15 +672,17 @@ dz_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant
         const int row0 = rt * 256 + (int)rank * 128;
         for (int vt = vt0; ok && vt < vt1; ++vt) {
           for (int kb = 0; kb < a.n_kb; ++kb) {
-            if (!mbar_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
-            const uint32_t sa = sbase + stage * DZP_STAGE_BYTES;
-            const uint32_t fb = lead_full0 + 8u * stage;
-            if (leader) mbar_arrive_expect_tx(full0 + 8u * stage, 2 * DZP_STAGE_BYTES);
-            tma_load_2d_pair(sa, &map_hs, fb, kb * BK, row0);
-            tma_load_2d_pair(sa + TILE_128x64, &map_ht, fb, kb * BK, row0);
-            tma_load_2d_pair(sa + 2 * TILE_128x64, &map_w, fb, kb * BK,
-                             a.v_begin + vt * DZP_BN + (int)rank * (DZP_BN / 2));
-            if (!leader) mbar_arrive_cluster(fb);
+            if (!warp_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
+            if (elect_one()) {
+              const uint32_t sa = sbase + stage * DZP_STAGE_BYTES;
+              const uint32_t fb = lead_full0 + 8u * stage;
+              if (leader) mbar_arrive_expect_tx(full0 + 8u * stage, 2 * DZP_STAGE_BYTES);
+              tma_load_2d_pair(sa, &map_hs, fb, kb * BK, row0);
+              tma_load_2d_pair(sa + TILE_128x64, &map_ht, fb, kb * BK, row0);
+              tma_load_2d_pair(sa + 2 * TILE_128x64, &map_w, fb, kb * BK,
+                               a.v_begin + vt * DZP_BN + (int)rank * (DZP_BN / 2));
+              if (!leader) mbar_arrive_cluster(fb);
+            }
             ++issued;
             if (++stage == DZP_STAGES) { stage = 0; phase ^= 1; }
           }
@@ -696,7 +691,7 @@ dz_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant
       if (leader) drain_loads<DZP_STAGES>(full0, stage, phase, issued);
     }
   } else if (warp == 1) {
-    if (lane == 0 && leader) {
+    if (leader) {   // pair MMA issuer (leader, whole warp)
       constexpr uint32_t idesc = make_idesc_bf16(2 * BM, DZP_BN, false, false);
       int stage = 0;
       uint32_t phase = 0;
@@ -708,39 +703,46 @@ dz_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant
         for (int vt = vt0; ok && vt < vt1; ++vt, ++tcount) {
           const int buf = tcount & 1;
           const uint32_t tph = (tcount >> 1) & 1;
-          if (!mbar_wait(tempty0 + 8u * buf, tph ^ 1, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
+          if (!warp_wait(tempty0 + 8u * buf, tph ^ 1, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
           tc_fence_after();
           const uint32_t d_s = tmem + buf * 256;
           const uint32_t d_t = d_s + 128;
           for (int kb = 0; kb < a.n_kb; ++kb) {
-            if (!mbar_wait(full0 + 8u * stage, phase, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
+            if (!warp_wait(full0 + 8u * stage, phase, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t sa = sbase + stage * DZP_STAGE_BYTES;
+            if (elect_one()) {
+              const uint32_t sa = sbase + stage * DZP_STAGE_BYTES;
 #pragma unroll
-            for (int k = 0; k < BK / 16; ++k) {
-              const uint64_t bdesc = desc_kmajor(sa + 2 * TILE_128x64, k);
-              const uint32_t acc = (kb | k) != 0;
-              mma_bf16_pair(d_s, desc_kmajor(sa, k), bdesc, idesc, acc);
-              mma_bf16_pair(d_t, desc_kmajor(sa + TILE_128x64, k), bdesc, idesc, acc);
+              for (int k = 0; k < BK / 16; ++k) {
+                const uint64_t bdesc = desc_kmajor(sa + 2 * TILE_128x64, k);
+                const uint32_t acc = (kb | k) != 0;
+                mma_bf16_pair(d_s, desc_kmajor(sa, k), bdesc, idesc, acc);
+                mma_bf16_pair(d_t, desc_kmajor(sa + TILE_128x64, k), bdesc, idesc, acc);
+              }
+              mma_commit_pair(empty0 + 8u * stage);
+              mma_commit_pair(peer_empty0 + 8u * stage);
             }
-            mma_commit_pair(empty0 + 8u * stage);
-            mma_commit_pair(peer_empty0 + 8u * stage);
             if (++stage == DZP_STAGES) { stage = 0; phase ^= 1; }
           }
-          if (ok) {
+          if (ok && elect_one()) {
             mma_commit_pair(tfull0 + 8u * buf);
             mma_commit_pair(peer_tfull0 + 8u * buf);
           }
         }
       }
-      mma_commit_pair(done_bar);
+      if (elect_one()) mma_commit_pair(done_bar);
       mbar_wait_drain(done_bar, 0);
     }
   } else {
     const int q = warp & 3;
-    const int h = (warp - EPI_WARP0) >> 2;   // 64-column half of the 128-column tile
-    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * 64);
-    const uint32_t stg = stg0 + (uint32_t)(warp - EPI_WARP0) * 4096u;
+    const int h = (warp - EPI_WARP0) >> 2;   // column slice of the 128-column tile
+    constexpr int CW = DZP_COLS_PER_WARP;
+    constexpr int NCH = CW / 32;             // 32-column chunks per warp and tile
+    constexpr uint32_t ROWB = CW * 2;        // staging row bytes (128 or 64)
+    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * CW);
+    const uint32_t stg = stg0 + (uint32_t)(warp - EPI_WARP0) * (32u * ROWB);
+    // 16-byte chunk j of staging row r: 128-byte rows swizzle with r % 8, 64-byte rows with (r / 2) % 4
+    const uint32_t swz = ROWB == 128 ? (uint32_t)(lane & 7) : (uint32_t)((lane >> 1) & 3);
     int tcount = 0;
     bool ok = true;
     for (int u = cid; ok && u < a.n_units; u += n_clusters) {
@@ -764,30 +766,23 @@ dz_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant
         if (lane == 0) bulk_wait_read0();   // staging free: previous tile's store has read it
         __syncwarp();
         const uint32_t tbase = lane_addr + buf * 256;
-        uint32_t bs[2][32], bt[2][32];
-        tmem_ld32_raw(tbase, bs[0]);
-        tmem_ld32_raw(tbase + 128, bt[0]);
-        tmem_wait_ld_regs(bs[0], bt[0]);
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const int cur = c & 1;
-          if (c == 0) {
-            tmem_ld32_raw(tbase + 32, bs[1]);
-            tmem_ld32_raw(tbase + 128 + 32, bt[1]);
-          }
-          const int nvalid = a.v_count - (vt * DZP_BN + h * 64 + c * 32);
+        for (int c = 0; c < NCH; ++c) {
+          uint32_t bs[32], bt[32];
+          tmem_ld32_raw(tbase + c * 32, bs);
+          tmem_ld32_raw(tbase + 128 + c * 32, bt);
+          tmem_wait_ld_regs(bs, bt);
+          const int nvalid = a.v_count - (vt * DZP_BN + h * CW + c * 32);
           if (nvalid > 0) {
             uint32_t pk[16];
-            dz_chunk(bs[cur], bt[cur], nvalid, a.scale_log2, Ls, Lt, coef, pk, acc);
-            const uint32_t rowp = stg + (uint32_t)lane * 128u;
+            dz_chunk(bs, bt, nvalid, a.scale_log2, Ls, Lt, coef, pk, acc);
+            const uint32_t rowp = stg + (uint32_t)lane * ROWB;
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               const uint32_t j = (uint32_t)(c * 4 + k);
-              st_shared_v4(rowp + ((j ^ (uint32_t)(lane & 7)) << 4), pk[4 * k], pk[4 * k + 1], pk[4 * k + 2],
-                           pk[4 * k + 3]);
+              st_shared_v4(rowp + ((j ^ swz) << 4), pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
             }
           }
-          if (c == 0) tmem_wait_ld_regs(bs[1], bt[1]);
         }
         tc_fence_before();
         __syncwarp();
@@ -797,14 +792,14 @@ dz_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant
         }
         fence_async_shared();
         __syncwarp();
-        const int x0 = vt * DZP_BN + h * 64, y0 = rt * 256 + (int)rank * 128 + q * 32;
+        const int x0 = vt * DZP_BN + h * CW, y0 = rt * 256 + (int)rank * 128 + q * 32;
         if (lane == 0 && y0 < a.n_rows && x0 < a.v_count) {
           tma_store_2d(&map_out, stg, x0, y0);
           bulk_commit();
         }
       }
       if (ok && row_ok && a.a_parts)
-        a.a_parts[(size_t)(a.a_part_base + uv * 2 + h) * a.n_rows + row] = acc * a.scale_log2;
+        a.a_parts[(size_t)(a.a_part_base + uv * DZP_CSPLIT + h) * a.n_rows + row] = acc * a.scale_log2;
     }
     if (lane == 0) bulk_wait0();
   }
@@ -814,13 +809,8 @@ dz_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant
   if (warp == 1) tmem_dealloc_pair(tmem, DUAL_TMEM_COLS);
 }
 
-// =====================================================================================
-// grouped GEMM for the backward chunk: dW_chunk = dZ^T h_s and dH (+)= dZ W_chunk in one
-// persistent launch.  C[M][Ncol] (+)= A[M][K] * B[K][Ncol], bf16 in, fp32 out; B is
-// MN-major for both problems; A is MN-major for dW (dZ^T) and K-major for dH (dZ).
-// Tiles are handed out dynamically (global atomic counter) with the longer dW tiles first,
-// so SMs that finish early pick up the remaining work (greedy longest-first).
-// =====================================================================================
+// One GEMM of the backward chunk: C[M][Ncol] (+)= A[M][K] * B[K][Ncol], bf16 in, fp32 out.
+// B is MN-major for both problems; A is MN-major for dW (dZ^T) and K-major for dH (dZ).
 struct GemmProblem {
   int M, Ncol, K;
   int n_mt, n_nt, n_tiles, n_kb;
@@ -829,229 +819,10 @@ struct GemmProblem {
   int accumulate;   // 1: C += A*B, 0: C = A*B
   int a_k0, b_k0;   // K coordinate of the first k-block in A's and B's tensor maps
   int a_mn;         // A stored [K][M] (M contiguous) instead of [M][K]
+  int n_split;      // K split into n_split ranges of kb_per_split k-blocks (tiles = n_mt*n_nt*n_split)
+  int kb_per_split;
+  int c_row0;       // row coordinate of C row 0 in the output tensor map
 };
-struct GroupedArgs {
-  GemmProblem p[2];
-  int n_tiles;      // p[0].n_tiles + p[1].n_tiles
-  int* counter;     // zero before the launch
-};
-
-template <int BN>
-struct GemmCfg {
-  static constexpr int A_BYTES = TILE_128x64;
-  static constexpr int B_BYTES = BN * BK * 2;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN >= 192) ? 4 : 6;
-  static constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
-  static constexpr int SCHED = 4;   // tile-index ring depth
-  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 512;
-};
-
-__device__ __forceinline__ void grouped_tile(const GroupedArgs& g, int t, int& pi, int& mt, int& nt) {
-  pi = t < g.p[0].n_tiles ? 0 : 1;
-  const int lt = pi ? t - g.p[0].n_tiles : t;
-  mt = lt / g.p[pi].n_nt;
-  nt = lt % g.p[pi].n_nt;
-}
-
-template <int BN>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
-gemm_grouped_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_b0,
-                    const __grid_constant__ CUtensorMap map_a1, const __grid_constant__ CUtensorMap map_b1,
-                    const GroupedArgs g) {
-  using Cfg = GemmCfg<BN>;
-  constexpr int STAGES = Cfg::STAGES;
-  constexpr int SCHED = Cfg::SCHED;
-  extern __shared__ uint8_t smem_raw[];
-  __shared__ uint32_t tmem_slot;
-  __shared__ int abort_flag;
-  __shared__ int tile_ring[SCHED];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const uint32_t sbase = smem_u32(smem);
-  const uint32_t bar0 = sbase + STAGES * Cfg::STAGE_BYTES;
-  const uint32_t full0 = bar0;
-  const uint32_t empty0 = bar0 + 8u * STAGES;
-  const uint32_t tfull0 = bar0 + 16u * STAGES;
-  const uint32_t tempty0 = tfull0 + 16u;
-  const uint32_t done_bar = tempty0 + 16u;
-  const uint32_t sfull0 = done_bar + 8u;               // [SCHED] tile index published
-  const uint32_t sempty0 = sfull0 + 8u * SCHED;        // [SCHED] tile index consumed (MMA + 4 epilogue warps)
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-
-  if (threadIdx.x == 0) {
-    abort_flag = 0;
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(full0 + 8u * s, 1);
-      mbar_init(empty0 + 8u * s, 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(tfull0 + 8u * b, 1);
-      mbar_init(tempty0 + 8u * b, 4 * 32);
-    }
-    mbar_init(done_bar, 1);
-    for (int s = 0; s < SCHED; ++s) {
-      mbar_init(sfull0 + 8u * s, 1);
-      mbar_init(sempty0 + 8u * s, 1 + 4);
-    }
-    fence_mbar_init();
-    tma_prefetch(&map_a0);
-    tma_prefetch(&map_b0);
-    tma_prefetch(&map_a1);
-    tma_prefetch(&map_b1);
-  }
-  if (warp == 1) tmem_alloc(smem_u32(&tmem_slot), Cfg::TMEM_COLS);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = tmem_slot;
-  volatile int* abort_p = &abort_flag;
-  volatile int* ring = tile_ring;
-
-  if (warp == 0) {
-    if (lane == 0) {
-      // ------------------------------------------------------------ scheduler + TMA producer
-      int stage = 0;
-      uint32_t phase = 0;
-      long long issued = 0;
-      bool ok = true;
-      for (int k = 0; ok; ++k) {
-        const int slot = k % SCHED;
-        const uint32_t sph = (uint32_t)(k / SCHED) & 1u;
-        if (!mbar_wait(sempty0 + 8u * slot, sph ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) break;
-        const int t = atomicAdd(g.counter, 1);
-        ring[slot] = t;
-        mbar_arrive(sfull0 + 8u * slot);
-        if (t >= g.n_tiles) break;
-        int pi, mt, nt;
-        grouped_tile(g, t, pi, mt, nt);
-        const GemmProblem& P = g.p[pi];
-        const CUtensorMap* ma = pi ? &map_a1 : &map_a0;
-        const CUtensorMap* mb = pi ? &map_b1 : &map_b0;
-        for (int kb = 0; kb < P.n_kb; ++kb) {
-          if (!mbar_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
-          const uint32_t sa = sbase + stage * Cfg::STAGE_BYTES;
-          const uint32_t sb = sa + Cfg::A_BYTES;
-          const uint32_t fb = full0 + 8u * stage;
-          mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
-          const int ka = P.a_k0 + kb * BK, kbb = P.b_k0 + kb * BK;
-          if (P.a_mn) {
-            tma_load_2d(sa, ma, fb, mt * BM, ka);
-            tma_load_2d(sa + 8192, ma, fb, mt * BM + 64, ka);
-          } else {
-            tma_load_2d(sa, ma, fb, ka, mt * BM);
-          }
-#pragma unroll
-          for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + 8192 * j, mb, fb, nt * BN + 64 * j, kbb);
-          ++issued;
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
-        }
-      }
-      drain_loads<STAGES>(full0, stage, phase, issued);
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      // ------------------------------------------------------------ MMA issuer
-      constexpr uint32_t idesc_kmaj = make_idesc_bf16(BM, BN, false, true);
-      constexpr uint32_t idesc_mnmaj = make_idesc_bf16(BM, BN, true, true);
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      for (int k = 0; ok; ++k) {
-        const int slot = k % SCHED;
-        const uint32_t sph = (uint32_t)(k / SCHED) & 1u;
-        if (!mbar_wait(sfull0 + 8u * slot, sph, abort_p, KLG_STATUS_TIMEOUT_MMA)) break;
-        const int t = ring[slot];
-        mbar_arrive(sempty0 + 8u * slot);
-        if (t >= g.n_tiles) break;
-        int pi, mt, nt;
-        grouped_tile(g, t, pi, mt, nt);
-        const GemmProblem& P = g.p[pi];
-        const bool amn = P.a_mn != 0;
-        const uint32_t idesc = amn ? idesc_mnmaj : idesc_kmaj;
-        const int buf = k & 1;
-        const uint32_t tph = (uint32_t)(k >> 1) & 1u;
-        if (!mbar_wait(tempty0 + 8u * buf, tph ^ 1, abort_p, KLG_STATUS_TIMEOUT_MMA)) break;
-        tc_fence_after();
-        const uint32_t d = tmem + buf * BN;
-        for (int kb = 0; kb < P.n_kb; ++kb) {
-          if (!mbar_wait(full0 + 8u * stage, phase, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t sa = sbase + stage * Cfg::STAGE_BYTES;
-          const uint32_t sb = sa + Cfg::A_BYTES;
-#pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t ad = amn ? desc_mnmajor(sa, kk) : desc_kmajor(sa, kk);
-            mma_bf16(d, ad, desc_mnmajor(sb, kk), idesc, (kb | kk) != 0);
-          }
-          mma_commit(empty0 + 8u * stage);
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
-        }
-        if (ok) mma_commit(tfull0 + 8u * buf);
-      }
-      mma_commit(done_bar);
-      mbar_wait_drain(done_bar, 0);
-    }
-  } else {
-    // -------------------------------------------------------------- epilogue
-    const int q = warp & 3;
-    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
-    for (int k = 0;; ++k) {
-      const int slot = k % SCHED;
-      const uint32_t sph = (uint32_t)(k / SCHED) & 1u;
-      int t = 0;
-      if (lane == 0) {
-        if (!mbar_wait(sfull0 + 8u * slot, sph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) t = -1;
-        else {
-          t = ring[slot];
-          mbar_arrive(sempty0 + 8u * slot);
-        }
-      }
-      t = __shfl_sync(0xffffffffu, t, 0);
-      if (t < 0 || t >= g.n_tiles) break;
-      int pi, mt, nt;
-      grouped_tile(g, t, pi, mt, nt);
-      const GemmProblem& P = g.p[pi];
-      const int buf = k & 1;
-      const uint32_t tph = (uint32_t)(k >> 1) & 1u;
-      if (!mbar_wait(tfull0 + 8u * buf, tph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) break;
-      tc_fence_after();
-      const int row = mt * BM + q * 32 + lane;
-      const bool row_ok = row < P.M;
-      float* crow = P.C + (size_t)(row_ok ? row : 0) * P.ldc;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        float v[32];
-        tmem_ld32(lane_addr + buf * BN + c * 32, v);
-        tmem_wait_ld();
-        const int col0 = nt * BN + c * 32;
-        if (!row_ok || col0 >= P.Ncol) continue;
-        if (col0 + 32 <= P.Ncol) {
-          float4* d4 = reinterpret_cast<float4*>(crow + col0);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-            if (P.accumulate) {
-              const float4 old = d4[j];
-              o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
-            }
-            d4[j] = o;
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (col0 + j < P.Ncol) crow[col0 + j] = P.accumulate ? crow[col0 + j] + v[j] : v[j];
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(tempty0 + 8u * buf);
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, Cfg::TMEM_COLS);
-}
 
 // =====================================================================================
 // grouped GEMM on CTA pairs: the backward chunk's dW = dZ^T h_s and dH (+)= dZ W_chunk.
@@ -1076,24 +847,33 @@ struct PairGemmCfg {
   static constexpr int A_BYTES = TILE_128x64;          // this CTA's 128 rows x 64 K
   static constexpr int B_BYTES = (BN / 2) * BK * 2;    // this CTA's BN/2 columns x 64 K
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (227 * 1024 - 2048) / STAGE_BYTES > 8 ? 8 : (227 * 1024 - 2048) / STAGE_BYTES;
-  static constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
   static constexpr int EPI_WARPS = 4;
+  static constexpr int STAGING_BYTES = EPI_WARPS * 2 * 4096;   // per warp: 2 x (32 rows x 32 fp32)
+  static constexpr int STAGES_RAW = (227 * 1024 - 2048 - STAGING_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  static constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
-  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 256;
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + STAGING_BYTES + 256;
 };
 
-__device__ __forceinline__ void pair_tile(const PairGemmArgs& g, int t, int& pi, int& mt, int& nt) {
+__device__ __forceinline__ void pair_tile(const PairGemmArgs& g, int t, int& pi, int& mt, int& nt, int& kb0,
+                                          int& kb1) {
   pi = t < g.p[0].n_tiles ? 0 : 1;
-  const int lt = pi ? t - g.p[0].n_tiles : t;
-  mt = lt / g.p[pi].n_nt;
-  nt = lt % g.p[pi].n_nt;
+  const GemmProblem& P = g.p[pi];
+  int lt = pi ? t - g.p[0].n_tiles : t;
+  const int split = lt / (P.n_mt * P.n_nt);
+  lt -= split * P.n_mt * P.n_nt;
+  mt = lt / P.n_nt;
+  nt = lt % P.n_nt;
+  kb0 = split * P.kb_per_split;
+  kb1 = min(P.n_kb, kb0 + P.kb_per_split);
 }
 
 template <int BN>
 __global__ void __launch_bounds__(PairGemmCfg<BN>::THREADS, 1)
 gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_b0,
                  const __grid_constant__ CUtensorMap map_a1, const __grid_constant__ CUtensorMap map_b1,
+                 const __grid_constant__ CUtensorMap map_c0, const __grid_constant__ CUtensorMap map_c1,
                  const PairGemmArgs g, const __grid_constant__ PairSchedule sched) {
   using Cfg = PairGemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
@@ -1103,7 +883,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_consta
   __shared__ int abort_flag;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t bar0 = sbase + STAGES * Cfg::STAGE_BYTES;
+  const uint32_t stg0 = sbase + STAGES * Cfg::STAGE_BYTES;   // epilogue staging (1024-aligned)
+  const uint32_t bar0 = stg0 + Cfg::STAGING_BYTES;
   const uint32_t full0 = bar0;
   const uint32_t empty0 = bar0 + 8u * STAGES;
   const uint32_t tfull0 = bar0 + 16u * STAGES;
@@ -1132,6 +913,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_consta
     tma_prefetch(&map_b0);
     tma_prefetch(&map_a1);
     tma_prefetch(&map_b1);
+    tma_prefetch(&map_c0);
+    tma_prefetch(&map_c1);
   }
   if (warp == 1) tmem_alloc_pair(smem_u32(&tmem_slot), Cfg::TMEM_COLS);
   tc_fence_before();
@@ -1145,36 +928,38 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_consta
   const uint32_t peer_tfull0 = mapa_shared(tfull0, 1);
 
   if (warp == 0) {
-    if (lane == 0) {
-      // ------------------------------------------------------------ TMA producer (both CTAs)
+    {
+      // ------------------------------------------------------------ TMA producer (both CTAs, whole warp)
       int stage = 0;
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
       for (int i = i0; ok && i < i1; ++i) {
-        int pi, mt, nt;
-        pair_tile(g, sched.tile[i], pi, mt, nt);
+        int pi, mt, nt, kb0, kb1;
+        pair_tile(g, sched.tile[i], pi, mt, nt, kb0, kb1);
         const GemmProblem& P = g.p[pi];
         const CUtensorMap* ma = pi ? &map_a1 : &map_a0;
         const CUtensorMap* mb = pi ? &map_b1 : &map_b0;
         const int row0 = mt * 256 + (int)rank * 128;
         const int col0 = nt * BN + (int)rank * (BN / 2);
-        for (int kb = 0; kb < P.n_kb; ++kb) {
-          if (!mbar_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
-          const uint32_t sa = sbase + stage * Cfg::STAGE_BYTES;
-          const uint32_t sb = sa + Cfg::A_BYTES;
-          const uint32_t fb = lead_full0 + 8u * stage;
-          if (leader) mbar_arrive_expect_tx(full0 + 8u * stage, 2 * Cfg::STAGE_BYTES);
-          const int ka = P.a_k0 + kb * BK, kbb = P.b_k0 + kb * BK;
-          if (P.a_mn) {
-            tma_load_2d_pair(sa, ma, fb, row0, ka);
-            tma_load_2d_pair(sa + 8192, ma, fb, row0 + 64, ka);
-          } else {
-            tma_load_2d_pair(sa, ma, fb, ka, row0);
-          }
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!warp_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
+          if (elect_one()) {
+            const uint32_t sa = sbase + stage * Cfg::STAGE_BYTES;
+            const uint32_t sb = sa + Cfg::A_BYTES;
+            const uint32_t fb = lead_full0 + 8u * stage;
+            if (leader) mbar_arrive_expect_tx(full0 + 8u * stage, 2 * Cfg::STAGE_BYTES);
+            const int ka = P.a_k0 + kb * BK, kbb = P.b_k0 + kb * BK;
+            if (P.a_mn) {
+              tma_load_2d_pair(sa, ma, fb, row0, ka);
+              tma_load_2d_pair(sa + 8192, ma, fb, row0 + 64, ka);
+            } else {
+              tma_load_2d_pair(sa, ma, fb, ka, row0);
+            }
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j) tma_load_2d_pair(sb + 4096 * j, mb, fb, col0 + 32 * j, kbb);
-          if (!leader) mbar_arrive_cluster(fb);
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d_pair(sb + 4096 * j, mb, fb, col0 + 32 * j, kbb);
+            if (!leader) mbar_arrive_cluster(fb);
+          }
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -1182,84 +967,87 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_consta
       if (leader) drain_loads<STAGES>(full0, stage, phase, issued);
     }
   } else if (warp == 1) {
-    if (lane == 0 && leader) {
-      // ------------------------------------------------------------ pair MMA issuer (leader)
+    if (leader) {
+      // ------------------------------------------------------------ pair MMA issuer (leader, whole warp)
       constexpr uint32_t idesc_kmaj = make_idesc_bf16(2 * BM, BN, false, true);
       constexpr uint32_t idesc_mnmaj = make_idesc_bf16(2 * BM, BN, true, true);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
       for (int i = i0, k = 0; ok && i < i1; ++i, ++k) {
-        int pi, mt, nt;
-        pair_tile(g, sched.tile[i], pi, mt, nt);
+        int pi, mt, nt, kb0, kb1;
+        pair_tile(g, sched.tile[i], pi, mt, nt, kb0, kb1);
         const GemmProblem& P = g.p[pi];
         const bool amn = P.a_mn != 0;
         const uint32_t idesc = amn ? idesc_mnmaj : idesc_kmaj;
         const int buf = k & 1;
         const uint32_t tph = (uint32_t)(k >> 1) & 1u;
-        if (!mbar_wait(tempty0 + 8u * buf, tph ^ 1, abort_p, KLG_STATUS_TIMEOUT_MMA)) break;
+        if (!warp_wait(tempty0 + 8u * buf, tph ^ 1, abort_p, KLG_STATUS_TIMEOUT_MMA)) break;
         tc_fence_after();
         const uint32_t d = tmem + buf * BN;
-        for (int kb = 0; kb < P.n_kb; ++kb) {
-          if (!mbar_wait(full0 + 8u * stage, phase, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!warp_wait(full0 + 8u * stage, phase, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t sa = sbase + stage * Cfg::STAGE_BYTES;
-          const uint32_t sb = sa + Cfg::A_BYTES;
+          if (elect_one()) {
+            const uint32_t sa = sbase + stage * Cfg::STAGE_BYTES;
+            const uint32_t sb = sa + Cfg::A_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t ad = amn ? desc_mnmajor(sa, kk) : desc_kmajor(sa, kk);
-            mma_bf16_pair(d, ad, desc_mnmajor_sw64(sb, kk), idesc, (kb | kk) != 0);
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              const uint64_t ad = amn ? desc_mnmajor(sa, kk) : desc_kmajor(sa, kk);
+              mma_bf16_pair(d, ad, desc_mnmajor_sw64(sb, kk), idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+            }
+            mma_commit_pair(empty0 + 8u * stage);
+            mma_commit_pair(peer_empty0 + 8u * stage);
           }
-          mma_commit_pair(empty0 + 8u * stage);
-          mma_commit_pair(peer_empty0 + 8u * stage);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
-        if (ok) {
+        if (ok && elect_one()) {
           mma_commit_pair(tfull0 + 8u * buf);
           mma_commit_pair(peer_tfull0 + 8u * buf);
         }
       }
-      mma_commit_pair(done_bar);
+      if (elect_one()) mma_commit_pair(done_bar);
       mbar_wait_drain(done_bar, 0);
     }
   } else {
     // -------------------------------------------------------------- epilogue (both CTAs)
+    // Each 32 x 32 fp32 block goes through a 128-byte-swizzled staging buffer and is added
+    // into C by a TMA reduce-add (the add happens at L2; C was zeroed before the launch).
     const int q = warp & 3;
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+    const uint32_t stg = stg0 + (uint32_t)(warp - EPI_WARP0) * 8192u;
+    int sbuf = 0;
     for (int i = i0, k = 0; i < i1; ++i, ++k) {
-      int pi, mt, nt;
-      pair_tile(g, sched.tile[i], pi, mt, nt);
+      int pi, mt, nt, kb0, kb1;
+      pair_tile(g, sched.tile[i], pi, mt, nt, kb0, kb1);
       const GemmProblem& P = g.p[pi];
+      const CUtensorMap* mc = pi ? &map_c1 : &map_c0;
       const int buf = k & 1;
       const uint32_t tph = (uint32_t)(k >> 1) & 1u;
       if (!mbar_wait(tfull0 + 8u * buf, tph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
-      const int row = mt * 256 + (int)rank * 128 + q * 32 + lane;
-      const bool row_ok = row < P.M;
-      float* crow = P.C + (size_t)(row_ok ? row : 0) * P.ldc;
+      const int row_blk = mt * 256 + (int)rank * 128 + q * 32;   // first C row of this warp
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
-        float v[32];
-        tmem_ld32(lane_addr + buf * BN + c * 32, v);
-        tmem_wait_ld();
+        uint32_t v[32];
+        tmem_ld32_raw(lane_addr + buf * BN + c * 32, v);
+        tmem_wait_ld_regs(v);
         const int col0 = nt * BN + c * 32;
-        if (!row_ok || col0 >= P.Ncol) continue;
-        if (col0 + 32 <= P.Ncol) {
-          float4* d4 = reinterpret_cast<float4*>(crow + col0);
+        if (row_blk >= P.M || col0 >= P.Ncol) continue;   // warp-uniform
+        if (lane == 0) bulk_wait_read1();                 // the buffer written two blocks ago is free
+        __syncwarp();
+        const uint32_t rowp = stg + (uint32_t)sbuf * 4096u + (uint32_t)lane * 128u;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-            if (P.accumulate) {
-              const float4 old = d4[j];
-              o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
-            }
-            d4[j] = o;
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (col0 + j < P.Ncol) crow[col0 + j] = P.accumulate ? crow[col0 + j] + v[j] : v[j];
+        for (int j = 0; j < 8; ++j)
+          st_shared_v4(rowp + (((uint32_t)j ^ (uint32_t)(lane & 7)) << 4), v[4 * j], v[4 * j + 1], v[4 * j + 2],
+                       v[4 * j + 3]);
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_2d(mc, stg + (uint32_t)sbuf * 4096u, col0, P.c_row0 + row_blk);
+          bulk_commit();
         }
+        sbuf ^= 1;
       }
       tc_fence_before();
       __syncwarp();
@@ -1268,6 +1056,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_consta
         else mbar_arrive_cluster(lead_tempty0 + 8u * buf);
       }
     }
+    if (lane == 0) bulk_wait0();
   }
   tc_fence_before();
   cluster_sync();
