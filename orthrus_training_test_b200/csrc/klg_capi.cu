@@ -13,8 +13,10 @@
 #include <cstring>
 #include <algorithm>
 #include <functional>
+#include <map>
 #include <mutex>
 #include <queue>
+#include <tuple>
 #include <vector>
 
 #include "klg_kernels.cuh"
@@ -230,24 +232,45 @@ int launch_dz_pair(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtenso
 }
 
 // Longest-first greedy assignment of tiles [t_begin, t_end) to `pairs` CTA pairs.
-void build_schedule(const klg::PairGemmArgs& g, int t_begin, int t_end, int pairs, klg::PairSchedule& sc) {
-  std::vector<std::vector<uint32_t>> lists(pairs);
-  typedef std::pair<long long, int> Load;   // (assigned k-blocks, pair)
+// Cost of a tile in k-block units: its K range plus the epilogue and pipeline refill.
+constexpr int kTileOverheadKb = 4;
+
+int tile_kb(const klg::GemmProblem& P, int local) {
+  if (P.n_split == 1) return P.n_kb;
+  return local < P.n_mt * P.n_nt ? P.kb_split : P.n_kb - P.kb_split;
+}
+
+// Longest-processing-time-first assignment of tiles [t_begin, t_end) to `pairs` CTA pairs.
+// Returns the makespan in k-block units; fills `lists` when given.
+long long lpt_assign(const klg::PairGemmArgs& g, int t_begin, int t_end, int pairs,
+                     std::vector<std::vector<uint32_t>>* lists) {
+  std::vector<std::pair<int, uint32_t>> order;   // (cost, tile)
+  order.reserve(t_end - t_begin);
+  for (int t = t_begin; t < t_end; ++t) {
+    const int pi = t < g.p[0].n_tiles ? 0 : 1;
+    order.push_back({tile_kb(g.p[pi], pi ? t - g.p[0].n_tiles : t) + kTileOverheadKb, (uint32_t)t});
+  }
+  std::stable_sort(order.begin(), order.end(), [](const std::pair<int, uint32_t>& x, const std::pair<int, uint32_t>& y) {
+    return x.first > y.first;
+  });
+  typedef std::pair<long long, int> Load;   // (assigned cost, pair)
   std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
   for (int c = 0; c < pairs; ++c) heap.push(Load(0, c));
-  // problem 0 tiles first when they are the longer ones (equal costs within a problem)
-  const int first = g.p[0].n_kb >= g.p[1].n_kb ? 0 : 1;
-  for (int pass = 0; pass < 2; ++pass) {
-    const int pi = pass == 0 ? first : 1 - first;
-    const int lo = pi == 0 ? 0 : g.p[0].n_tiles, hi = pi == 0 ? g.p[0].n_tiles : g.n_tiles;
-    for (int t = std::max(lo, t_begin); t < std::min(hi, t_end); ++t) {
-      Load l = heap.top();
-      heap.pop();
-      lists[l.second].push_back((uint32_t)t);
-      l.first += g.p[pi].n_kb;
-      heap.push(l);
-    }
+  long long makespan = 0;
+  for (const auto& o : order) {
+    Load l = heap.top();
+    heap.pop();
+    if (lists) (*lists)[l.second].push_back(o.second);
+    l.first += o.first;
+    makespan = std::max(makespan, l.first);
+    heap.push(l);
   }
+  return makespan;
+}
+
+void build_schedule(const klg::PairGemmArgs& g, int t_begin, int t_end, int pairs, klg::PairSchedule& sc) {
+  std::vector<std::vector<uint32_t>> lists(pairs);
+  lpt_assign(g, t_begin, t_end, pairs, &lists);
   int n = 0;
   for (int c = 0; c < pairs; ++c) {
     sc.start[c] = (uint16_t)n;
@@ -299,8 +322,9 @@ int launch_gemm_pair(int bn, const CUtensorMap& a0, const CUtensorMap& b0, const
   }
 }
 
+// kb_split: 0 = no K split; else the first of two K pieces has kb_split k-blocks.
 klg::GemmProblem gemm_problem(bool on, int M, int Ncol, int K, int bn, float* C, int ldc, int accumulate, int a_k0,
-                              int b_k0, int a_mn, int bm = klg::BM, int n_split = 1, int c_row0 = 0) {
+                              int b_k0, int a_mn, int bm = klg::BM, int kb_split = 0, int c_row0 = 0) {
   klg::GemmProblem g{};
   g.M = M;
   g.Ncol = Ncol;
@@ -308,10 +332,8 @@ klg::GemmProblem gemm_problem(bool on, int M, int Ncol, int K, int bn, float* C,
   g.n_mt = cdiv(M, bm);
   g.n_nt = cdiv(Ncol, bn);
   g.n_kb = cdiv(K, klg::BK);
-  if (n_split > g.n_kb) n_split = g.n_kb;
-  if (n_split < 1) n_split = 1;
-  g.kb_per_split = cdiv(g.n_kb, n_split);
-  g.n_split = cdiv(g.n_kb, g.kb_per_split);
+  g.n_split = (kb_split > 0 && kb_split < g.n_kb) ? 2 : 1;
+  g.kb_split = g.n_split == 2 ? kb_split : g.n_kb;
   g.c_row0 = c_row0;
   g.n_tiles = on ? g.n_mt * g.n_nt * g.n_split : 0;
   g.C = C;
@@ -321,6 +343,40 @@ klg::GemmProblem gemm_problem(bool on, int M, int Ncol, int K, int bn, float* C,
   g.b_k0 = b_k0;
   g.a_mn = a_mn;
   return g;
+}
+
+// Split point of dW's K for one backward chunk (0 = no split): the candidate whose
+// longest-first schedule has the shortest makespan, memoised per shape.
+int pick_dw_split(int n_rows, int wv, int hidden, int bn) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int, int>, int> memo;
+  const int pairs = std::min(num_sms() / 2, klg::PAIR_MAX_CLUSTERS);
+  const auto key = std::make_tuple(n_rows, wv, hidden, bn, pairs);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = memo.find(key);
+    if (it != memo.end()) return it->second;
+  }
+  klg::PairGemmArgs g{};
+  g.p[1] = gemm_problem(true, n_rows, hidden, wv, bn, nullptr, hidden, 1, 0, 0, 0, 256, 0, 0);
+  const int dw_kb = cdiv(n_rows, klg::BK);
+  std::vector<int> cands(1, 0);
+  for (int c = (dw_kb + 1) / 2; c < dw_kb; c += 4) cands.push_back(c);
+  long long best = -1;
+  int pick = 0;
+  for (int c : cands) {
+    g.p[0] = gemm_problem(true, wv, hidden, n_rows, bn, nullptr, hidden, 1, 0, 0, 1, 256, c, 0);
+    g.n_tiles = g.p[0].n_tiles + g.p[1].n_tiles;
+    if (g.n_tiles > klg::PAIR_MAX_TILES) continue;
+    const long long m = lpt_assign(g, 0, g.n_tiles, std::min(pairs, g.n_tiles), nullptr);
+    if (best < 0 || m < best) {
+      best = m;
+      pick = c;
+    }
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  memo[key] = pick;
+  return pick;
 }
 
 int check_problem(const void* hs, const void* ht, const void* w, int64_t n_rows, int64_t hidden, int64_t vocab,
@@ -498,7 +554,7 @@ namespace {
 // per-unit KL cross-term partials (at most 8 units per chunk), returning their count.
 int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask, const float* lse, const float* count,
               const float* grad, int64_t n_rows, int64_t hidden, int64_t vocab, float inv_temp, float* d_hs, float* d_w,
-              int* counters, __nv_bfloat16* dz, int64_t cols, float* a_parts, int* n_ap_out, cudaStream_t s) {
+              __nv_bfloat16* dz, int64_t cols, float* a_parts, int* n_ap_out, cudaStream_t s) {
   int rc;
   const int bn = gemm_bn(hidden);
   alignas(64) CUtensorMap mhs, mht, mw, mw_mn, mhs_mn;
@@ -535,9 +591,6 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
   a.dz = dz;
   a.ld_dz = (int)cols;
   a.a_parts = a_parts;
-  const int n_chunks = cdiv(vocab, cols);
-  cudaError_t ce = cudaMemsetAsync(counters, 0, sizeof(int) * n_chunks, s);
-  if (ce != cudaSuccess) return cuda_fail(ce, "cudaMemsetAsync(tile counters)");
   int n_ap = 0;
   for (int64_t v0 = 0, ci = 0; v0 < vocab; v0 += cols, ++ci) {
     const int64_t wv = (vocab - v0) < cols ? (vocab - v0) : cols;
@@ -559,15 +612,16 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
     alignas(64) CUtensorMap mdz_k, mdz_mn;
     if (!make_map(&mdz_k, dz, wv, n_rows, cols, klg::BK, klg::BM) || !make_map(&mdz_mn, dz, wv, n_rows, cols, 64, klg::BK))
       return fail(KLG_ERR_CUDA, "tensor map (dz operand)");
-    // dW's K (all rows) is split in two when its tiles would be much longer than dH's
-    // (K = chunk width).  At most two partial sums meet in any dW element, and the
-    // reduce-adds onto zero give the same bits in either order, so dW stays deterministic.
-    const int split = n_rows >= 2 * wv ? 2 : 1;
+    // dW's K (all rows) may be split in two, at the point that gives the shortest
+    // simulated schedule (the uneven pieces fill the gaps the equal tiles leave).  At most
+    // two partial sums meet in any dW element, and the reduce-adds onto zero give the
+    // same bits in either order, so dW stays deterministic.
     klg::PairGemmArgs g{};
-    g.p[0] = gemm_problem(d_w != nullptr, (int)wv, (int)hidden, (int)n_rows, bn, nullptr, (int)hidden, 1, 0, 0, 1, 256,
-                          split, (int)v0);
     g.p[1] = gemm_problem(d_hs != nullptr, (int)n_rows, (int)hidden, (int)wv, bn, nullptr, (int)hidden, 1, 0,
-                          (int)v0, 0, 256, 1, 0);
+                          (int)v0, 0, 256, 0, 0);
+    const int kb_split = pick_dw_split((int)n_rows, (int)wv, (int)hidden, bn);
+    g.p[0] = gemm_problem(d_w != nullptr, (int)wv, (int)hidden, (int)n_rows, bn, nullptr, (int)hidden, 1, 0, 0, 1, 256,
+                          kb_split, (int)v0);
     g.n_tiles = g.p[0].n_tiles + g.p[1].n_tiles;
     (void)ci;
     if ((rc = launch_gemm_pair(bn, mdz_mn, mhs_mn, mdz_k, mw_mn, mdw, mdh, g, s))) return rc;
@@ -635,9 +689,9 @@ int klg_bwd(const void* hs, const void* ht, const void* w, const uint8_t* mask, 
     return fail(KLG_ERR_WORKSPACE, "backward workspace too small: needs >= %lld bytes",
                 (long long)(KLG_BWD_HEADER + n_rows * 256));
   if ((rc = bind_device(hs))) return rc;
-  int* counters = static_cast<int*>(workspace);
+
   __nv_bfloat16* dz = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(workspace) + KLG_BWD_HEADER);
-  return run_pass2(hs, ht, w, mask, lse, count, grad, n_rows, hidden, vocab, inv_temp, d_hs, d_w, counters, dz, cols,
+  return run_pass2(hs, ht, w, mask, lse, count, grad, n_rows, hidden, vocab, inv_temp, d_hs, d_w, dz, cols,
                    nullptr, nullptr, (cudaStream_t)stream);
 }
 
@@ -704,9 +758,9 @@ int klg_fwd_bwd(const void* hs, const void* ht, const void* w, const uint8_t* ma
   }
   // pass 2: dZ chunks (+ KL cross-term partials) and the dW / dH GEMMs
   int n_ap = 0;
-  int* counters = reinterpret_cast<int*>(ws);
+
   __nv_bfloat16* dz = reinterpret_cast<__nv_bfloat16*>(ws + L.dz_off);
-  if ((rc = run_pass2(hs, ht, w, mask, lse, count, grad, n_rows, hidden, vocab, inv_temp, d_hs, d_w, counters, dz,
+  if ((rc = run_pass2(hs, ht, w, mask, lse, count, grad, n_rows, hidden, vocab, inv_temp, d_hs, d_w, dz,
                       L.cols, a_parts, &n_ap, s)))
     return rc;
   if (n_ap != L.n_ap) return fail(KLG_ERR_ARG, "internal plan mismatch (cross-term partials)");

@@ -604,7 +604,7 @@ constexpr int DZP_CSPLIT = KLG_EPI_SPLIT;                                 // epi
 constexpr int DZP_EPI_WARPS = 4 * DZP_CSPLIT;
 constexpr int DZP_COLS_PER_WARP = DZP_BN / DZP_CSPLIT;                    // 64 or 32
 constexpr int DZP_THREADS = 64 + 32 * DZP_EPI_WARPS;
-constexpr int DZP_STAGING_BYTES = DZP_EPI_WARPS * 32 * DZP_COLS_PER_WARP * 2;   // 32 rows per warp
+constexpr int DZP_STAGING_BYTES = 2 * DZP_EPI_WARPS * 32 * DZP_COLS_PER_WARP * 2;   // 2 buffers x 32 rows per warp
 constexpr int DZP_SMEM = 1024 + DZP_STAGES * DZP_STAGE_BYTES + DZP_STAGING_BYTES + 256;
 
 // Units: n_rt counts 256-row pair tiles; a_parts rows: a_part_base + uv * DZP_CSPLIT + column slice.
@@ -740,7 +740,7 @@ dz_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant
     constexpr int NCH = CW / 32;             // 32-column chunks per warp and tile
     constexpr uint32_t ROWB = CW * 2;        // staging row bytes (128 or 64)
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * CW);
-    const uint32_t stg = stg0 + (uint32_t)(warp - EPI_WARP0) * (32u * ROWB);
+    const uint32_t stg = stg0 + (uint32_t)(warp - EPI_WARP0) * (64u * ROWB);   // two 32-row buffers
     // 16-byte chunk j of staging row r: 128-byte rows swizzle with r % 8, 64-byte rows with (r / 2) % 4
     const uint32_t swz = ROWB == 128 ? (uint32_t)(lane & 7) : (uint32_t)((lane >> 1) & 3);
     int tcount = 0;
@@ -763,8 +763,10 @@ dz_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant
         const uint32_t tph = (tcount >> 1) & 1;
         if (!mbar_wait(tfull0 + 8u * buf, tph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) { ok = false; break; }
         tc_fence_after();
-        if (lane == 0) bulk_wait_read0();   // staging free: previous tile's store has read it
+        // staging buffer `buf` is free once the store issued from it two tiles ago has read it
+        if (lane == 0) bulk_wait_read1();
         __syncwarp();
+        const uint32_t sstg = stg + (uint32_t)buf * (32u * ROWB);
         const uint32_t tbase = lane_addr + buf * 256;
 #pragma unroll
         for (int c = 0; c < NCH; ++c) {
@@ -776,7 +778,7 @@ dz_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant
           if (nvalid > 0) {
             uint32_t pk[16];
             dz_chunk(bs, bt, nvalid, a.scale_log2, Ls, Lt, coef, pk, acc);
-            const uint32_t rowp = stg + (uint32_t)lane * ROWB;
+            const uint32_t rowp = sstg + (uint32_t)lane * ROWB;
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               const uint32_t j = (uint32_t)(c * 4 + k);
@@ -793,8 +795,8 @@ dz_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant
         fence_async_shared();
         __syncwarp();
         const int x0 = vt * DZP_BN + h * CW, y0 = rt * 256 + (int)rank * 128 + q * 32;
-        if (lane == 0 && y0 < a.n_rows && x0 < a.v_count) {
-          tma_store_2d(&map_out, stg, x0, y0);
+        if (lane == 0) {   // one bulk group per tile (empty when the block is out of range)
+          if (y0 < a.n_rows && x0 < a.v_count) tma_store_2d_hint(&map_out, sstg, x0, y0, l2_evict_first_policy());
           bulk_commit();
         }
       }
@@ -819,8 +821,8 @@ struct GemmProblem {
   int accumulate;   // 1: C += A*B, 0: C = A*B
   int a_k0, b_k0;   // K coordinate of the first k-block in A's and B's tensor maps
   int a_mn;         // A stored [K][M] (M contiguous) instead of [M][K]
-  int n_split;      // K split into n_split ranges of kb_per_split k-blocks (tiles = n_mt*n_nt*n_split)
-  int kb_per_split;
+  int n_split;      // 1, or 2: K split into k-blocks [0, kb_split) and [kb_split, n_kb) (tiles = n_mt*n_nt*n_split)
+  int kb_split;
   int c_row0;       // row coordinate of C row 0 in the output tensor map
 };
 
@@ -842,11 +844,17 @@ struct PairGemmArgs {
   int n_tiles;
 };
 
+#ifndef KLG_GEMM_KPS
+#define KLG_GEMM_KPS 1
+#endif
 template <int BN>
 struct PairGemmCfg {
   static constexpr int A_BYTES = TILE_128x64;          // this CTA's 128 rows x 64 K
   static constexpr int B_BYTES = (BN / 2) * BK * 2;    // this CTA's BN/2 columns x 64 K
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  // k-blocks per pipeline stage (2 halves the barrier round trips but leaves 3 stages
+  // instead of 6, which measured ~9 % slower at the 16k-row shape)
+  static constexpr int KPS = KLG_GEMM_KPS;
+  static constexpr int STAGE_BYTES = KPS * (A_BYTES + B_BYTES);   // [A kb0 | A kb1 | B kb0 | B kb1]
   static constexpr int EPI_WARPS = 4;
   static constexpr int STAGING_BYTES = EPI_WARPS * 2 * 4096;   // per warp: 2 x (32 rows x 32 fp32)
   static constexpr int STAGES_RAW = (227 * 1024 - 2048 - STAGING_BYTES) / STAGE_BYTES;
@@ -865,8 +873,8 @@ __device__ __forceinline__ void pair_tile(const PairGemmArgs& g, int t, int& pi,
   lt -= split * P.n_mt * P.n_nt;
   mt = lt / P.n_nt;
   nt = lt % P.n_nt;
-  kb0 = split * P.kb_per_split;
-  kb1 = min(P.n_kb, kb0 + P.kb_per_split);
+  kb0 = split ? P.kb_split : 0;
+  kb1 = (split || P.n_split == 1) ? P.n_kb : P.kb_split;
 }
 
 template <int BN>
@@ -942,22 +950,26 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_consta
         const CUtensorMap* mb = pi ? &map_b1 : &map_b0;
         const int row0 = mt * 256 + (int)rank * 128;
         const int col0 = nt * BN + (int)rank * (BN / 2);
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kb = kb0; kb < kb1; kb += Cfg::KPS) {
+          const int nk = min(Cfg::KPS, kb1 - kb);
           if (!warp_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
           if (elect_one()) {
             const uint32_t sa = sbase + stage * Cfg::STAGE_BYTES;
-            const uint32_t sb = sa + Cfg::A_BYTES;
             const uint32_t fb = lead_full0 + 8u * stage;
-            if (leader) mbar_arrive_expect_tx(full0 + 8u * stage, 2 * Cfg::STAGE_BYTES);
-            const int ka = P.a_k0 + kb * BK, kbb = P.b_k0 + kb * BK;
-            if (P.a_mn) {
-              tma_load_2d_pair(sa, ma, fb, row0, ka);
-              tma_load_2d_pair(sa + 8192, ma, fb, row0 + 64, ka);
-            } else {
-              tma_load_2d_pair(sa, ma, fb, ka, row0);
-            }
+            if (leader) mbar_arrive_expect_tx(full0 + 8u * stage, 2 * nk * (Cfg::A_BYTES + Cfg::B_BYTES));
+            for (int j = 0; j < nk; ++j) {
+              const uint32_t saj = sa + j * Cfg::A_BYTES;
+              const uint32_t sbj = sa + Cfg::KPS * Cfg::A_BYTES + j * Cfg::B_BYTES;
+              const int ka = P.a_k0 + (kb + j) * BK, kbb = P.b_k0 + (kb + j) * BK;
+              if (P.a_mn) {
+                tma_load_2d_pair(saj, ma, fb, row0, ka);
+                tma_load_2d_pair(saj + 8192, ma, fb, row0 + 64, ka);
+              } else {
+                tma_load_2d_pair(saj, ma, fb, ka, row0);
+              }
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_2d_pair(sb + 4096 * j, mb, fb, col0 + 32 * j, kbb);
+              for (int jj = 0; jj < BN / 64; ++jj) tma_load_2d_pair(sbj + 4096 * jj, mb, fb, col0 + 32 * jj, kbb);
+            }
             if (!leader) mbar_arrive_cluster(fb);
           }
           ++issued;
@@ -985,16 +997,20 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_consta
         if (!warp_wait(tempty0 + 8u * buf, tph ^ 1, abort_p, KLG_STATUS_TIMEOUT_MMA)) break;
         tc_fence_after();
         const uint32_t d = tmem + buf * BN;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kb = kb0; kb < kb1; kb += Cfg::KPS) {
+          const int nk = min(Cfg::KPS, kb1 - kb);
           if (!warp_wait(full0 + 8u * stage, phase, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
           tc_fence_after();
           if (elect_one()) {
             const uint32_t sa = sbase + stage * Cfg::STAGE_BYTES;
-            const uint32_t sb = sa + Cfg::A_BYTES;
+            for (int j = 0; j < nk; ++j) {
+              const uint32_t saj = sa + j * Cfg::A_BYTES;
+              const uint32_t sbj = sa + Cfg::KPS * Cfg::A_BYTES + j * Cfg::B_BYTES;
 #pragma unroll
-            for (int kk = 0; kk < BK / 16; ++kk) {
-              const uint64_t ad = amn ? desc_mnmajor(sa, kk) : desc_kmajor(sa, kk);
-              mma_bf16_pair(d, ad, desc_mnmajor_sw64(sb, kk), idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+              for (int kk = 0; kk < BK / 16; ++kk) {
+                const uint64_t ad = amn ? desc_mnmajor(saj, kk) : desc_kmajor(saj, kk);
+                mma_bf16_pair(d, ad, desc_mnmajor_sw64(sbj, kk), idesc, (kb + j > kb0 || kk > 0) ? 1u : 0u);
+              }
             }
             mma_commit_pair(empty0 + 8u * stage);
             mma_commit_pair(peer_empty0 + 8u * stage);
