@@ -170,7 +170,7 @@ int launch_dual(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMa
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dual_kernel)");
   const int grid = a.n_units < num_sms() ? a.n_units : num_sms();
   const int slot = trace_pre(s);
-  k<<<grid, klg::NUM_THREADS, smem, s>>>(mhs, mht, mw, a);
+  k<<<grid, klg::DUAL_THREADS, smem, s>>>(mhs, mht, mw, a);
   e = cudaGetLastError();
   trace_post(slot, s, KLG_KIND_STATS);
   if (e != cudaSuccess) return cuda_fail(e, "launch dual_kernel");

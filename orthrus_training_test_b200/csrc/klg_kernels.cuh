@@ -26,8 +26,7 @@ namespace klg {
 constexpr int BM = 128;                     // rows per tile (TMEM lanes)
 constexpr int BK = 64;                      // bf16 elements per k-block (one 128 B swizzle row)
 constexpr int TILE_128x64 = BM * BK * 2;    // 16 KB
-constexpr int NUM_THREADS = 192;
-constexpr int EPI_WARP0 = 2;
+constexpr int EPI_WARP0 = 2;                // warp 0: TMA producer, warp 1: MMA issuer, then epilogue warps
 constexpr float NEG_BIG = -1.0e30f;
 
 // =====================================================================================
@@ -38,6 +37,13 @@ constexpr int DUAL_STAGES = 4;
 constexpr int DUAL_STAGE_BYTES = 3 * TILE_128x64;  // A_s | A_t | B
 constexpr int DUAL_TMEM_COLS = 512;                // 2 buffers x (Z_s 128 | Z_t 128)
 constexpr int DUAL_SMEM = 1024 + DUAL_STAGES * DUAL_STAGE_BYTES + 256;
+// A single thread issues about one TMA copy per ~250 cycles (measured on sm_100a), so the
+// load steps are spread round-robin over DUAL_PROD producer warps (warp 0 and the warps
+// after the epilogue).  DUAL_STAGES must be a multiple of DUAL_PROD.
+constexpr int DUAL_PROD = 2;
+constexpr int DUAL_PW = EPI_WARP0 + 4;                       // first extra producer warp
+constexpr int DUAL_THREADS = 32 * (DUAL_PW + DUAL_PROD - 1);
+static_assert(DUAL_STAGES % DUAL_PROD == 0, "stage ring must split evenly over the producers");
 
 struct DualArgs {
   int n_rows;       // N
@@ -155,7 +161,7 @@ __device__ __forceinline__ void dz_chunk(const uint32_t (&bs)[32], const uint32_
   acc += a0 + a1;
 }
 
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(DUAL_THREADS, 1)
 dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ CUtensorMap map_ht,
             const __grid_constant__ CUtensorMap map_w, const DualArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -196,7 +202,9 @@ dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ 
   const uint32_t tmem = tmem_slot;
   volatile int* abort_p = &abort_flag;
 
-  if (warp == 0) {
+  if (warp == 0 || warp >= DUAL_PW) {
+    // producer warps: warp 0 and warps DUAL_PW.. take the pipeline's load steps round-robin
+    const int prod = warp == 0 ? 0 : warp - DUAL_PW + 1;
     {
       // ------------------------------------------------------------ TMA producer (whole warp)
       int stage = 0;
@@ -208,21 +216,23 @@ dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ 
         dual_unit(a, u, rt, uv, vt0, vt1);
         for (int vt = vt0; ok && vt < vt1; ++vt) {
           for (int kb = 0; kb < a.n_kb; ++kb) {
-            if (!warp_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
-            if (elect_one()) {
-              const uint32_t sb = sbase + stage * DUAL_STAGE_BYTES;
-              const uint32_t fb = full0 + 8u * stage;
-              mbar_arrive_expect_tx(fb, DUAL_STAGE_BYTES);
-              tma_load_2d(sb, &map_hs, fb, kb * BK, rt * BM);
-              tma_load_2d(sb + TILE_128x64, &map_ht, fb, kb * BK, rt * BM);
-              tma_load_2d(sb + 2 * TILE_128x64, &map_w, fb, kb * BK, a.v_begin + vt * DUAL_BN);
+            if (issued % DUAL_PROD == prod) {
+              if (!warp_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
+              if (elect_one()) {
+                const uint32_t sb = sbase + stage * DUAL_STAGE_BYTES;
+                const uint32_t fb = full0 + 8u * stage;
+                mbar_arrive_expect_tx(fb, DUAL_STAGE_BYTES);
+                tma_load_2d(sb, &map_hs, fb, kb * BK, rt * BM);
+                tma_load_2d(sb + TILE_128x64, &map_ht, fb, kb * BK, rt * BM);
+                tma_load_2d(sb + 2 * TILE_128x64, &map_w, fb, kb * BK, a.v_begin + vt * DUAL_BN);
+              }
             }
             ++issued;
             if (++stage == DUAL_STAGES) { stage = 0; phase ^= 1; }
           }
         }
       }
-      drain_loads<DUAL_STAGES>(full0, stage, phase, issued);
+      if (prod == 0) drain_loads<DUAL_STAGES>(full0, stage, phase, issued);
     }
   } else if (warp == 1) {
     {
@@ -335,13 +345,15 @@ constexpr int LSE_STAGE_BYTES = LSE_A_BYTES + LSE_B_BYTES; // 32 KB
 constexpr int LSE_CSPLIT = KLG_EPI_SPLIT;                  // epilogue warps per TMEM lane quarter
 constexpr int LSE_EPI_WARPS = 4 * LSE_CSPLIT;
 constexpr int LSE_COLS_PER_WARP = LSE_BN / LSE_CSPLIT;
-constexpr int LSE_THREADS = 64 + 32 * LSE_EPI_WARPS;
+constexpr int LSE_PROD = 2;                                 // producer warps (round-robin load steps)
+constexpr int LSE_PW = EPI_WARP0 + LSE_EPI_WARPS;           // first extra producer warp
+constexpr int LSE_THREADS = 32 * (LSE_PW + LSE_PROD - 1);
 constexpr int LSE_TMEM_COLS = 512;                         // 2 buffers x 256 columns
 constexpr int LSE_SMEM = 1024 + LSE_STAGES * LSE_STAGE_BYTES + 256;
 // Resident-A variant (H <= 576): the CTA's 128 x H row block stays in shared memory for a
 // whole unit and only the W halves stream, halving the bytes TMA writes per MMA.
 constexpr int LSE_RES_MAX_KB = 9;
-constexpr int LSE_RES_STAGES = 5;
+constexpr int LSE_RES_STAGES = 4;
 constexpr int LSE_RES_SMEM = 1024 + LSE_RES_MAX_KB * LSE_A_BYTES + LSE_RES_STAGES * LSE_B_BYTES + 256;
 
 struct LseArgs {
@@ -391,6 +403,8 @@ __global__ void __launch_bounds__(LSE_THREADS, 1)
 lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ CUtensorMap map_ht,
                 const __grid_constant__ CUtensorMap map_w, const LseArgs a) {
   constexpr int STAGES = RES ? LSE_RES_STAGES : LSE_STAGES;
+  constexpr int NPROD = LSE_PROD;
+  static_assert(STAGES % NPROD == 0, "stage ring must split evenly over the producers");
   constexpr int STAGE_BYTES = RES ? LSE_B_BYTES : LSE_STAGE_BYTES;   // W half [+ A k-block]
   constexpr int A_REGION = RES ? LSE_RES_MAX_KB * LSE_A_BYTES : 0;
   extern __shared__ uint8_t smem_raw[];
@@ -445,7 +459,9 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
   const uint32_t peer_tfull0 = mapa_shared(tfull0, 1);
   const uint32_t peer_aempty = mapa_shared(aempty_bar, 1);
 
-  if (warp == 0) {
+  if (warp == 0 || warp >= LSE_PW) {
+    // producer warps: warp 0 and warps LSE_PW.. take the pipeline's load steps round-robin
+    const int prod = warp == 0 ? 0 : warp - LSE_PW + 1;
     {
       // ------------------------------------------------------------ TMA producer (both CTAs, whole warp)
       int stage = 0;
@@ -458,7 +474,7 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
         lse_unit(a, u, view, rp, uv, vt0, vt1);
         const CUtensorMap* ma = view ? &map_ht : &map_hs;
         const int row0 = rp * 256 + (int)rank * 128;
-        if (RES) {
+        if (RES && prod == 0) {
           // this unit's rows: wait until the previous unit's MMAs released the A region
           if (!warp_wait(aempty_bar, (uint32_t)(ucount & 1) ^ 1u, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) break;
           if (elect_one()) {
@@ -470,15 +486,17 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
         }
         for (int vt = vt0; ok && vt < vt1; ++vt) {
           for (int kb = 0; kb < a.n_kb; ++kb) {
-            if (!warp_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
-            if (elect_one()) {
-              const uint32_t sa = sbase + stage * STAGE_BYTES;
-              const uint32_t fb = lead_full0 + 8u * stage;
-              if (leader) mbar_arrive_expect_tx(full0 + 8u * stage, 2 * STAGE_BYTES);
-              if (!RES) tma_load_2d_pair(sa, ma, fb, kb * BK, row0);
-              tma_load_2d_pair(sa + (RES ? 0 : LSE_A_BYTES), &map_w, fb, kb * BK,
-                               vt * LSE_BN + (int)rank * (LSE_BN / 2));
-              if (!leader) mbar_arrive_cluster(fb);
+            if (issued % NPROD == prod) {
+              if (!warp_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
+              if (elect_one()) {
+                const uint32_t sa = sbase + stage * STAGE_BYTES;
+                const uint32_t fb = lead_full0 + 8u * stage;
+                if (leader) mbar_arrive_expect_tx(full0 + 8u * stage, 2 * STAGE_BYTES);
+                if (!RES) tma_load_2d_pair(sa, ma, fb, kb * BK, row0);
+                tma_load_2d_pair(sa + (RES ? 0 : LSE_A_BYTES), &map_w, fb, kb * BK,
+                                 vt * LSE_BN + (int)rank * (LSE_BN / 2));
+                if (!leader) mbar_arrive_cluster(fb);
+              }
             }
             ++issued;
             if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -486,8 +504,8 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
         }
       }
       if (leader) {
-        drain_loads<STAGES>(full0, stage, phase, issued);
-        if (RES && ucount > 0) mbar_wait_drain(afull_bar, (uint32_t)((ucount - 1) & 1));
+        if (prod == 0) drain_loads<STAGES>(full0, stage, phase, issued);
+        if (RES && prod == 0 && ucount > 0) mbar_wait_drain(afull_bar, (uint32_t)((ucount - 1) & 1));
       }
     }
   } else if (warp == 1) {
@@ -603,8 +621,11 @@ constexpr int DZP_STAGE_BYTES = 2 * TILE_128x64 + DZP_B_BYTES;            // 40 
 constexpr int DZP_CSPLIT = KLG_EPI_SPLIT;                                 // epilogue warps per lane quarter
 constexpr int DZP_EPI_WARPS = 4 * DZP_CSPLIT;
 constexpr int DZP_COLS_PER_WARP = DZP_BN / DZP_CSPLIT;                    // 64 or 32
-constexpr int DZP_THREADS = 64 + 32 * DZP_EPI_WARPS;
-constexpr int DZP_STAGING_BYTES = 2 * DZP_EPI_WARPS * 32 * DZP_COLS_PER_WARP * 2;   // 2 buffers x 32 rows per warp
+constexpr int DZP_PROD = 2;                                               // producer warps
+constexpr int DZP_PW = EPI_WARP0 + DZP_EPI_WARPS;                         // first extra producer warp
+constexpr int DZP_THREADS = 32 * (DZP_PW + DZP_PROD - 1);
+static_assert(DZP_STAGES % DZP_PROD == 0, "stage ring must split evenly over the producers");
+constexpr int DZP_STAGING_BYTES = 2 * DZP_EPI_WARPS * 32 * DZP_COLS_PER_WARP * 2;   // 2 x 32 rows per warp
 constexpr int DZP_SMEM = 1024 + DZP_STAGES * DZP_STAGE_BYTES + DZP_STAGING_BYTES + 256;
 
 // Units: n_rt counts 256-row pair tiles; a_parts rows: a_part_base + uv * DZP_CSPLIT + column slice.
@@ -660,7 +681,9 @@ dz_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant
   const uint32_t peer_empty0 = mapa_shared(empty0, 1);
   const uint32_t peer_tfull0 = mapa_shared(tfull0, 1);
 
-  if (warp == 0) {
+  if (warp == 0 || warp >= DZP_PW) {
+    // producer warps: warp 0 and warps DZP_PW.. take the pipeline's load steps round-robin
+    const int prod = warp == 0 ? 0 : warp - DZP_PW + 1;
     {   // TMA producer (both CTAs, whole warp)
       int stage = 0;
       uint32_t phase = 0;
@@ -672,23 +695,25 @@ dz_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant
         const int row0 = rt * 256 + (int)rank * 128;
         for (int vt = vt0; ok && vt < vt1; ++vt) {
           for (int kb = 0; kb < a.n_kb; ++kb) {
-            if (!warp_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
-            if (elect_one()) {
-              const uint32_t sa = sbase + stage * DZP_STAGE_BYTES;
-              const uint32_t fb = lead_full0 + 8u * stage;
-              if (leader) mbar_arrive_expect_tx(full0 + 8u * stage, 2 * DZP_STAGE_BYTES);
-              tma_load_2d_pair(sa, &map_hs, fb, kb * BK, row0);
-              tma_load_2d_pair(sa + TILE_128x64, &map_ht, fb, kb * BK, row0);
-              tma_load_2d_pair(sa + 2 * TILE_128x64, &map_w, fb, kb * BK,
-                               a.v_begin + vt * DZP_BN + (int)rank * (DZP_BN / 2));
-              if (!leader) mbar_arrive_cluster(fb);
+            if (issued % DZP_PROD == prod) {
+              if (!warp_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
+              if (elect_one()) {
+                const uint32_t sa = sbase + stage * DZP_STAGE_BYTES;
+                const uint32_t fb = lead_full0 + 8u * stage;
+                if (leader) mbar_arrive_expect_tx(full0 + 8u * stage, 2 * DZP_STAGE_BYTES);
+                tma_load_2d_pair(sa, &map_hs, fb, kb * BK, row0);
+                tma_load_2d_pair(sa + TILE_128x64, &map_ht, fb, kb * BK, row0);
+                tma_load_2d_pair(sa + 2 * TILE_128x64, &map_w, fb, kb * BK,
+                                 a.v_begin + vt * DZP_BN + (int)rank * (DZP_BN / 2));
+                if (!leader) mbar_arrive_cluster(fb);
+              }
             }
             ++issued;
             if (++stage == DZP_STAGES) { stage = 0; phase ^= 1; }
           }
         }
       }
-      if (leader) drain_loads<DZP_STAGES>(full0, stage, phase, issued);
+      if (leader && prod == 0) drain_loads<DZP_STAGES>(full0, stage, phase, issued);
     }
   } else if (warp == 1) {
     if (leader) {   // pair MMA issuer (leader, whole warp)
@@ -741,6 +766,7 @@ dz_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant
     constexpr uint32_t ROWB = CW * 2;        // staging row bytes (128 or 64)
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * CW);
     const uint32_t stg = stg0 + (uint32_t)(warp - EPI_WARP0) * (64u * ROWB);   // two 32-row buffers
+    const uint64_t pol = l2_evict_first_policy();   // dZ is streamed out once, read by the next kernel
     // 16-byte chunk j of staging row r: 128-byte rows swizzle with r % 8, 64-byte rows with (r / 2) % 4
     const uint32_t swz = ROWB == 128 ? (uint32_t)(lane & 7) : (uint32_t)((lane >> 1) & 3);
     int tcount = 0;
@@ -796,7 +822,7 @@ dz_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant
         __syncwarp();
         const int x0 = vt * DZP_BN + h * CW, y0 = rt * 256 + (int)rank * 128 + q * 32;
         if (lane == 0) {   // one bulk group per tile (empty when the block is out of range)
-          if (y0 < a.n_rows && x0 < a.v_count) tma_store_2d_hint(&map_out, sstg, x0, y0, l2_evict_first_policy());
+          if (y0 < a.n_rows && x0 < a.v_count) tma_store_2d_hint(&map_out, sstg, x0, y0, pol);
           bulk_commit();
         }
       }
@@ -857,10 +883,12 @@ struct PairGemmCfg {
   static constexpr int STAGE_BYTES = KPS * (A_BYTES + B_BYTES);   // [A kb0 | A kb1 | B kb0 | B kb1]
   static constexpr int EPI_WARPS = 4;
   static constexpr int STAGING_BYTES = EPI_WARPS * 2 * 4096;   // per warp: 2 x (32 rows x 32 fp32)
+  static constexpr int PROD = 3;                     // producer warps (round-robin load steps)
+  static constexpr int PW = EPI_WARP0 + EPI_WARPS;   // first extra producer warp
   static constexpr int STAGES_RAW = (227 * 1024 - 2048 - STAGING_BYTES) / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  static constexpr int STAGES = ((STAGES_RAW > 8 ? 8 : STAGES_RAW) / PROD) * PROD;
   static constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
-  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int THREADS = 32 * (PW + PROD - 1);
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + STAGING_BYTES + 256;
 };
 
@@ -935,7 +963,9 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_consta
   const uint32_t peer_empty0 = mapa_shared(empty0, 1);
   const uint32_t peer_tfull0 = mapa_shared(tfull0, 1);
 
-  if (warp == 0) {
+  if (warp == 0 || warp >= Cfg::PW) {
+    // producer warps: warp 0 and warps Cfg::PW.. take the pipeline's load steps round-robin
+    const int prod = warp == 0 ? 0 : warp - Cfg::PW + 1;
     {
       // ------------------------------------------------------------ TMA producer (both CTAs, whole warp)
       int stage = 0;
@@ -952,31 +982,33 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_consta
         const int col0 = nt * BN + (int)rank * (BN / 2);
         for (int kb = kb0; kb < kb1; kb += Cfg::KPS) {
           const int nk = min(Cfg::KPS, kb1 - kb);
-          if (!warp_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
-          if (elect_one()) {
-            const uint32_t sa = sbase + stage * Cfg::STAGE_BYTES;
-            const uint32_t fb = lead_full0 + 8u * stage;
-            if (leader) mbar_arrive_expect_tx(full0 + 8u * stage, 2 * nk * (Cfg::A_BYTES + Cfg::B_BYTES));
-            for (int j = 0; j < nk; ++j) {
-              const uint32_t saj = sa + j * Cfg::A_BYTES;
-              const uint32_t sbj = sa + Cfg::KPS * Cfg::A_BYTES + j * Cfg::B_BYTES;
-              const int ka = P.a_k0 + (kb + j) * BK, kbb = P.b_k0 + (kb + j) * BK;
-              if (P.a_mn) {
-                tma_load_2d_pair(saj, ma, fb, row0, ka);
-                tma_load_2d_pair(saj + 8192, ma, fb, row0 + 64, ka);
-              } else {
-                tma_load_2d_pair(saj, ma, fb, ka, row0);
+          if (issued % Cfg::PROD == prod) {
+            if (!warp_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
+            if (elect_one()) {
+              const uint32_t sa = sbase + stage * Cfg::STAGE_BYTES;
+              const uint32_t fb = lead_full0 + 8u * stage;
+              if (leader) mbar_arrive_expect_tx(full0 + 8u * stage, 2 * nk * (Cfg::A_BYTES + Cfg::B_BYTES));
+              for (int j = 0; j < nk; ++j) {
+                const uint32_t saj = sa + j * Cfg::A_BYTES;
+                const uint32_t sbj = sa + Cfg::KPS * Cfg::A_BYTES + j * Cfg::B_BYTES;
+                const int ka = P.a_k0 + (kb + j) * BK, kbb = P.b_k0 + (kb + j) * BK;
+                if (P.a_mn) {
+                  tma_load_2d_pair(saj, ma, fb, row0, ka);
+                  tma_load_2d_pair(saj + 8192, ma, fb, row0 + 64, ka);
+                } else {
+                  tma_load_2d_pair(saj, ma, fb, ka, row0);
+                }
+  #pragma unroll
+                for (int jj = 0; jj < BN / 64; ++jj) tma_load_2d_pair(sbj + 4096 * jj, mb, fb, col0 + 32 * jj, kbb);
               }
-#pragma unroll
-              for (int jj = 0; jj < BN / 64; ++jj) tma_load_2d_pair(sbj + 4096 * jj, mb, fb, col0 + 32 * jj, kbb);
+              if (!leader) mbar_arrive_cluster(fb);
             }
-            if (!leader) mbar_arrive_cluster(fb);
           }
           ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
-      if (leader) drain_loads<STAGES>(full0, stage, phase, issued);
+      if (leader && prod == 0) drain_loads<STAGES>(full0, stage, phase, issued);
     }
   } else if (warp == 1) {
     if (leader) {
