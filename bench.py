@@ -250,12 +250,14 @@ def main():
     assert _lib.device_status() == 0
 
     # ---------------------------------------------------------------- device-timed steps
+    # start the clock sampler first: every rank then leaves the barrier together, so no rank's
+    # first timed collective waits for another rank's set-up
     sampler = ClockSampler(local) if rank == 0 else None
-    barrier()
-    torch.cuda.synchronize()
     if sampler:
         sampler.start()
         time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
     launches0 = _lib.launch_count()
     _lib.trace_begin(8192)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
