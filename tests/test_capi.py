@@ -87,6 +87,6 @@ def test_workspace_sizes_bounded():
     # the dZ chunk stays far below a full [N, V] tensor at the benchmark sizes
     for n, h, v in [(16384, 576, 49152), (65536, 2048, 49152), (32768, 1024, 31040), (12251, 576, 49152)]:
         ws = L.klg_bwd_workspace_bytes(n, h, v)
-        assert 0 < ws <= (256 << 20) + HDR
+        assert 0 < ws <= (512 << 20) + HDR
         assert _lib.lib().klg_bwd_chunk_cols(n, v, ws) >= 2048
-        assert ws < n * v * 2 / 4
+        assert ws < n * v * 2 / 2
