@@ -604,8 +604,8 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
     a.a_part_base = n_ap;
     n_ap += klg::DZP_CSPLIT * n_uv;   // one cross-term partial per unit and column slice
     alignas(64) CUtensorMap mdz_out;
-    if (!make_map(&mdz_out, dz, wv, n_rows, cols, klg::DZP_COLS_PER_WARP, 32,
-                  klg::DZP_COLS_PER_WARP == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
+    if (!make_map(&mdz_out, dz, wv, n_rows, cols, klg::DZP_STORE_COLS, 32,
+                  CU_TENSOR_MAP_SWIZZLE_64B))
       return fail(KLG_ERR_CUDA, "tensor map (dz store)");
     if ((rc = launch_dz_pair(mhs, mht, mw, mdz_out, a, s))) return rc;
     if (!d_hs && !d_w) continue;
