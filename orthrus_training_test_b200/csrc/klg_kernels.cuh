@@ -38,12 +38,12 @@ constexpr int DUAL_STAGE_BYTES = 3 * TILE_128x64;  // A_s | A_t | B
 constexpr int DUAL_TMEM_COLS = 512;                // 2 buffers x (Z_s 128 | Z_t 128)
 constexpr int DUAL_SMEM = 1024 + DUAL_STAGES * DUAL_STAGE_BYTES + 256;
 // A single thread issues about one TMA copy per ~250 cycles (measured on sm_100a), so the
-// load steps are spread round-robin over DUAL_PROD producer warps (warp 0 and the warps
-// after the epilogue).  DUAL_STAGES must be a multiple of DUAL_PROD.
+// ring's stages are shared out over DUAL_PROD producer warps (warp 0 and the warps after
+// the epilogue): stage s always belongs to producer s % DUAL_PROD, which keeps every
+// producer's waits on a stage in phase order.
 constexpr int DUAL_PROD = 2;
 constexpr int DUAL_PW = EPI_WARP0 + 4;                       // first extra producer warp
 constexpr int DUAL_THREADS = 32 * (DUAL_PW + DUAL_PROD - 1);
-static_assert(DUAL_STAGES % DUAL_PROD == 0, "stage ring must split evenly over the producers");
 
 struct DualArgs {
   int n_rows;       // N
@@ -216,7 +216,7 @@ dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ 
         dual_unit(a, u, rt, uv, vt0, vt1);
         for (int vt = vt0; ok && vt < vt1; ++vt) {
           for (int kb = 0; kb < a.n_kb; ++kb) {
-            if (issued % DUAL_PROD == prod) {
+            if (stage % DUAL_PROD == prod) {
               if (!warp_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
               if (elect_one()) {
                 const uint32_t sb = sbase + stage * DUAL_STAGE_BYTES;
@@ -353,7 +353,10 @@ constexpr int LSE_SMEM = 1024 + LSE_STAGES * LSE_STAGE_BYTES + 256;
 // Resident-A variant (H <= 576): the CTA's 128 x H row block stays in shared memory for a
 // whole unit and only the W halves stream, halving the bytes TMA writes per MMA.
 constexpr int LSE_RES_MAX_KB = 9;
-constexpr int LSE_RES_STAGES = 4;
+#ifndef KLG_LSE_RES_STAGES
+#define KLG_LSE_RES_STAGES 4   // 5 fits but measured no faster
+#endif
+constexpr int LSE_RES_STAGES = KLG_LSE_RES_STAGES;
 constexpr int LSE_RES_SMEM = 1024 + LSE_RES_MAX_KB * LSE_A_BYTES + LSE_RES_STAGES * LSE_B_BYTES + 256;
 
 struct LseArgs {
@@ -404,7 +407,6 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
                 const __grid_constant__ CUtensorMap map_w, const LseArgs a) {
   constexpr int STAGES = RES ? LSE_RES_STAGES : LSE_STAGES;
   constexpr int NPROD = LSE_PROD;
-  static_assert(STAGES % NPROD == 0, "stage ring must split evenly over the producers");
   constexpr int STAGE_BYTES = RES ? LSE_B_BYTES : LSE_STAGE_BYTES;   // W half [+ A k-block]
   constexpr int A_REGION = RES ? LSE_RES_MAX_KB * LSE_A_BYTES : 0;
   extern __shared__ uint8_t smem_raw[];
@@ -486,7 +488,7 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
         }
         for (int vt = vt0; ok && vt < vt1; ++vt) {
           for (int kb = 0; kb < a.n_kb; ++kb) {
-            if (issued % NPROD == prod) {
+            if (stage % NPROD == prod) {
               if (!warp_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
               if (elect_one()) {
                 const uint32_t sa = sbase + stage * STAGE_BYTES;
@@ -884,11 +886,17 @@ struct PairGemmCfg {
   static constexpr int KPS = KLG_GEMM_KPS;
   static constexpr int STAGE_BYTES = KPS * (A_BYTES + B_BYTES);   // [A kb0 | A kb1 | B kb0 | B kb1]
   static constexpr int EPI_WARPS = 4;
-  static constexpr int STAGING_BYTES = EPI_WARPS * 2 * 4096;   // per warp: 2 x (32 rows x 32 fp32)
+#ifndef KLG_GEMM_STG_BUFS
+#define KLG_GEMM_STG_BUFS 2
+#endif
+  // per warp: KLG_GEMM_STG_BUFS x (32 rows x 32 fp32); a single buffer would leave room for a
+  // 7th stage but serialises the epilogue's reduce-adds (measured 5 % slower)
+  static constexpr int STG_BUFS = KLG_GEMM_STG_BUFS;
+  static constexpr int STAGING_BYTES = EPI_WARPS * STG_BUFS * 4096;
   static constexpr int PROD = 3;                     // producer warps (round-robin load steps)
   static constexpr int PW = EPI_WARP0 + EPI_WARPS;   // first extra producer warp
   static constexpr int STAGES_RAW = (227 * 1024 - 2048 - STAGING_BYTES) / STAGE_BYTES;
-  static constexpr int STAGES = ((STAGES_RAW > 8 ? 8 : STAGES_RAW) / PROD) * PROD;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
   static constexpr int THREADS = 32 * (PW + PROD - 1);
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + STAGING_BYTES + 256;
@@ -984,7 +992,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_consta
         const int col0 = nt * BN + (int)rank * (BN / 2);
         for (int kb = kb0; kb < kb1; kb += Cfg::KPS) {
           const int nk = min(Cfg::KPS, kb1 - kb);
-          if (issued % Cfg::PROD == prod) {
+          if (stage % Cfg::PROD == prod) {
             if (!warp_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
             if (elect_one()) {
               const uint32_t sa = sbase + stage * Cfg::STAGE_BYTES;
@@ -1065,7 +1073,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_consta
     // into C by a TMA reduce-add (the add happens at L2; C was zeroed before the launch).
     const int q = warp & 3;
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
-    const uint32_t stg = stg0 + (uint32_t)(warp - EPI_WARP0) * 8192u;
+    const uint32_t stg = stg0 + (uint32_t)(warp - EPI_WARP0) * (Cfg::STG_BUFS * 4096u);
     int sbuf = 0;
     for (int i = i0, k = 0; i < i1; ++i, ++k) {
       int pi, mt, nt, kb0, kb1;
@@ -1084,7 +1092,10 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_consta
         tmem_wait_ld_regs(v);
         const int col0 = nt * BN + c * 32;
         if (row_blk >= P.M || col0 >= P.Ncol) continue;   // warp-uniform
-        if (lane == 0) bulk_wait_read1();                 // the buffer written two blocks ago is free
+        if (lane == 0) {                                   // the buffer written STG_BUFS blocks ago is free
+          if (Cfg::STG_BUFS == 2) bulk_wait_read1();
+          else bulk_wait_read0();
+        }
         __syncwarp();
         const uint32_t rowp = stg + (uint32_t)sbuf * 4096u + (uint32_t)lane * 128u;
 #pragma unroll
@@ -1097,7 +1108,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_consta
           tma_reduce_add_2d(mc, stg + (uint32_t)sbuf * 4096u, col0, P.c_row0 + row_blk);
           bulk_commit();
         }
-        sbuf ^= 1;
+        sbuf = (sbuf + 1) % Cfg::STG_BUFS;
       }
       tc_fence_before();
       __syncwarp();
