@@ -11,6 +11,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <cstdlib>
 #include <algorithm>
 #include <functional>
 #include <map>
@@ -162,6 +163,45 @@ cudaError_t set_smem(Kern k, int bytes) {
   return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
+// Programmatic dependent launch (on unless KLG_PDL=0): each launch may start its set-up
+// while the previous kernel in the stream drains; the kernels wait (griddepcontrol.wait)
+// before touching global memory.
+bool pdl_on() {
+  static const bool on = [] {
+    const char* v = std::getenv("KLG_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+// Launch with an optional cluster of `cluster` CTAs and programmatic stream serialisation.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, int smem, cudaStream_t s, int cluster,
+                     Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (cluster > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (pdl_on()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
+}
+
 int launch_dual(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMap& mw, const klg::DualArgs& a,
                 cudaStream_t s) {
   auto k = klg::dual_kernel;
@@ -170,8 +210,7 @@ int launch_dual(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMa
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dual_kernel)");
   const int grid = a.n_units < num_sms() ? a.n_units : num_sms();
   const int slot = trace_pre(s);
-  k<<<grid, klg::DUAL_THREADS, smem, s>>>(mhs, mht, mw, a);
-  e = cudaGetLastError();
+  e = launch_k(k, dim3(grid), dim3(klg::DUAL_THREADS), smem, s, 1, mhs, mht, mw, a);
   trace_post(slot, s, KLG_KIND_STATS);
   if (e != cudaSuccess) return cuda_fail(e, "launch dual_kernel");
   ++g_launches;
@@ -186,20 +225,8 @@ int launch_lse_pair(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtens
   cudaError_t e = set_smem(k, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(lse_pair_kernel)");
   const int pairs = a.n_units < num_sms() / 2 ? a.n_units : num_sms() / 2;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * pairs);
-  cfg.blockDim = dim3(klg::LSE_THREADS);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
   const int slot = trace_pre(s);
-  e = cudaLaunchKernelEx(&cfg, k, mhs, mht, mw, a);
+  e = launch_k(k, dim3(2 * pairs), dim3(klg::LSE_THREADS), smem, s, 2, mhs, mht, mw, a);
   trace_post(slot, s, KLG_KIND_STATS);
   if (e != cudaSuccess) return cuda_fail(e, "launch lse_pair_kernel");
   ++g_launches;
@@ -211,20 +238,8 @@ int launch_dz_pair(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtenso
   cudaError_t e = set_smem(klg::dz_pair_kernel, klg::DZP_SMEM);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dz_pair_kernel)");
   const int pairs = a.n_units < num_sms() / 2 ? a.n_units : num_sms() / 2;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * pairs);
-  cfg.blockDim = dim3(klg::DZP_THREADS);
-  cfg.dynamicSmemBytes = klg::DZP_SMEM;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
   const int slot = trace_pre(s);
-  e = cudaLaunchKernelEx(&cfg, klg::dz_pair_kernel, mhs, mht, mw, mout, a);
+  e = launch_k(klg::dz_pair_kernel, dim3(2 * pairs), dim3(klg::DZP_THREADS), klg::DZP_SMEM, s, 2, mhs, mht, mw, mout, a);
   trace_post(slot, s, KLG_KIND_DZ);
   if (e != cudaSuccess) return cuda_fail(e, "launch dz_pair_kernel");
   ++g_launches;
@@ -292,20 +307,8 @@ int launch_gemm_pair_t(const CUtensorMap& a0, const CUtensorMap& b0, const CUten
     const int t1 = std::min(g.n_tiles, t0 + klg::PAIR_MAX_TILES);
     const int pairs = std::min(max_pairs, t1 - t0);
     build_schedule(g, t0, t1, pairs, sc);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * pairs);
-    cfg.blockDim = dim3(Cfg::THREADS);
-    cfg.dynamicSmemBytes = Cfg::SMEM;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
     const int slot = trace_pre(s);
-    e = cudaLaunchKernelEx(&cfg, k, a0, b0, a1, b1, c0, c1, g, sc);
+    e = launch_k(k, dim3(2 * pairs), dim3(Cfg::THREADS), Cfg::SMEM, s, 2, a0, b0, a1, b1, c0, c1, g, sc);
     trace_post(slot, s, KLG_KIND_GEMM);
     if (e != cudaSuccess) return cuda_fail(e, "launch gemm_pair_kernel");
     ++g_launches;
@@ -459,8 +462,8 @@ int klg_merge_stats(const float* partials, int n_part, int64_t n_rows, float* st
   if (!partials || !stats || n_part < 1 || n_rows < 1) return fail(KLG_ERR_ARG, "bad arguments to klg_merge_stats");
   if (int rc = bind_device(partials)) return rc;
   const int slot = trace_pre((cudaStream_t)stream);
-  klg::merge_kernel<<<cdiv(n_rows, 256), 256, 0, (cudaStream_t)stream>>>(partials, n_part, (int)n_rows, stats);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_k(klg::merge_kernel, dim3(cdiv(n_rows, 256)), dim3(256), 0, (cudaStream_t)stream, 1, partials, n_part,
+                           (int)n_rows, stats);
   trace_post(slot, (cudaStream_t)stream, KLG_KIND_MERGE);
   if (e != cudaSuccess) return cuda_fail(e, "launch merge_kernel");
   ++g_launches;
@@ -471,8 +474,7 @@ int klg_count_valid(const uint8_t* mask, int64_t n_rows, float* count, void* str
   if (!mask || !count || n_rows < 1 || n_rows > (1ll << 30)) return fail(KLG_ERR_ARG, "bad arguments to klg_count_valid");
   if (int rc = bind_device(mask)) return rc;
   const int slot = trace_pre((cudaStream_t)stream);
-  klg::count_valid_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(mask, (int)n_rows, count);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_k(klg::count_valid_kernel, dim3(1), dim3(1024), 0, (cudaStream_t)stream, 1, mask, (int)n_rows, count);
   trace_post(slot, (cudaStream_t)stream, KLG_KIND_COUNT);
   if (e != cudaSuccess) return cuda_fail(e, "launch count_valid_kernel");
   ++g_launches;
@@ -485,8 +487,8 @@ int klg_finalize(const float* stats, const uint8_t* mask, int64_t n_rows, const 
     return fail(KLG_ERR_ARG, "bad arguments to klg_finalize");
   if (int rc = bind_device(stats)) return rc;
   const int slot = trace_pre((cudaStream_t)stream);
-  klg::finalize_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(stats, mask, (int)n_rows, count, loss, lse, row_kl);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_k(klg::finalize_kernel, dim3(1), dim3(1024), 0, (cudaStream_t)stream, 1, stats, mask, (int)n_rows, count, loss,
+                           lse, row_kl);
   trace_post(slot, (cudaStream_t)stream, KLG_KIND_FINALIZE);
   if (e != cudaSuccess) return cuda_fail(e, "launch finalize_kernel");
   ++g_launches;
@@ -574,10 +576,16 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
     return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed (outputs)");
   if (!d_w) mdw = mhs;   // unused placeholders
   if (!d_hs) mdh = mhs;
-  cudaError_t ze = cudaSuccess;
-  if (d_w) ze = cudaMemsetAsync(d_w, 0, sizeof(float) * vocab * hidden, s);
-  if (ze == cudaSuccess && d_hs) ze = cudaMemsetAsync(d_hs, 0, sizeof(float) * n_rows * hidden, s);
-  if (ze != cudaSuccess) return cuda_fail(ze, "cudaMemsetAsync(gradients)");
+  // zero the fp32 gradients (H % 8 == 0, so every buffer is a whole number of float4)
+  for (int z = 0; z < 2; ++z) {
+    float* buf = z ? d_hs : d_w;
+    if (!buf) continue;
+    const long long n4 = (z ? n_rows : vocab) * hidden / 4;
+    const int blocks = (int)std::min<long long>(cdiv(n4, 256), 4ll * num_sms());
+    cudaError_t ze = launch_k(klg::zero_f32x4_kernel, dim3(blocks), dim3(256), 0, s, 1, reinterpret_cast<float4*>(buf), n4);
+    if (ze != cudaSuccess) return cuda_fail(ze, "launch zero_f32x4_kernel");
+    ++g_launches;
+  }
 
   klg::DualArgs a{};
   a.n_rows = (int)n_rows;
@@ -751,8 +759,7 @@ int klg_fwd_bwd(const void* hs, const void* ht, const void* w, const uint8_t* ma
   {
     const int n2 = (int)(2 * n_rows);
     const int slot = trace_pre(s);
-    klg::lse_merge_kernel<<<cdiv(n2, 256), 256, 0, s>>>(lse_parts, L.n_lp, n2, lse);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_k(klg::lse_merge_kernel, dim3(cdiv(n2, 256)), dim3(256), 0, s, 1, lse_parts, L.n_lp, n2, lse);
     trace_post(slot, s, KLG_KIND_MERGE);
     if (e != cudaSuccess) return cuda_fail(e, "launch lse_merge_kernel");
     ++g_launches;
@@ -770,14 +777,13 @@ int klg_fwd_bwd(const void* hs, const void* ht, const void* w, const uint8_t* ma
     const int nb = cdiv(n_rows, 256);
     float* block_sums = lse_parts;
     int slot = trace_pre(s);
-    klg::row_kl_pair_kernel<<<nb, 256, 0, s>>>(lse, a_parts, n_ap, mask, (int)n_rows, row_kl, block_sums);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_k(klg::row_kl_pair_kernel, dim3(nb), dim3(256), 0, s, 1, lse, a_parts, n_ap, mask,
+                             (int)n_rows, row_kl, block_sums);
     trace_post(slot, s, KLG_KIND_FINALIZE);
     if (e != cudaSuccess) return cuda_fail(e, "launch row_kl_pair_kernel");
     ++g_launches;
     slot = trace_pre(s);
-    klg::loss_from_sums_kernel<<<1, 1024, 0, s>>>(block_sums, nb, count, loss);
-    e = cudaGetLastError();
+    e = launch_k(klg::loss_from_sums_kernel, dim3(1), dim3(1024), 0, s, 1, block_sums, nb, count, loss);
     trace_post(slot, s, KLG_KIND_FINALIZE);
     if (e != cudaSuccess) return cuda_fail(e, "launch loss_from_sums_kernel");
     ++g_launches;
@@ -792,8 +798,8 @@ int klg_cast_f32_bf16(const float* in, void* out, int64_t n, void* stream) {
   long long blocks = (n + 255) / 256;
   if (blocks > 148 * 32) blocks = 148 * 32;
   const int slot = trace_pre((cudaStream_t)stream);
-  klg::cast_f32_bf16_kernel<<<(int)blocks, 256, 0, (cudaStream_t)stream>>>(in, static_cast<__nv_bfloat16*>(out), n);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_k(klg::cast_f32_bf16_kernel, dim3((int)blocks), dim3(256), 0, (cudaStream_t)stream, 1, in,
+                           static_cast<__nv_bfloat16*>(out), n);
   trace_post(slot, (cudaStream_t)stream, KLG_KIND_CAST);
   if (e != cudaSuccess) return cuda_fail(e, "launch cast_f32_bf16_kernel");
   ++g_launches;

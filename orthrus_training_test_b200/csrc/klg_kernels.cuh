@@ -200,6 +200,7 @@ dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ 
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
+  pdl_enter();   // inputs of this launch are complete from here on
   volatile int* abort_p = &abort_flag;
 
   if (warp == 0 || warp >= DUAL_PW) {
@@ -453,6 +454,7 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
   cluster_sync();   // barriers of both CTAs initialised, TMEM allocated
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
+  pdl_enter();   // inputs of this launch are complete from here on
   volatile int* abort_p = &abort_flag;
   const uint32_t lead_full0 = mapa_shared(full0, 0);
   const uint32_t lead_tempty0 = mapa_shared(tempty0, 0);
@@ -628,7 +630,10 @@ constexpr int DZP_STAGE_BYTES = 2 * TILE_128x64 + DZP_B_BYTES;            // 40 
 constexpr int DZP_CSPLIT = KLG_EPI_SPLIT;                                 // epilogue warps per lane quarter
 constexpr int DZP_EPI_WARPS = 4 * DZP_CSPLIT;
 constexpr int DZP_COLS_PER_WARP = DZP_BN / DZP_CSPLIT;                    // 64 or 32
-constexpr int DZP_PROD = 2;                                               // producer warps
+#ifndef KLG_DZ_PROD
+#define KLG_DZ_PROD 2
+#endif
+constexpr int DZP_PROD = KLG_DZ_PROD;                                     // producer warps
 constexpr int DZP_PW = EPI_WARP0 + DZP_EPI_WARPS;                         // first extra producer warp
 constexpr int DZP_THREADS = 32 * (DZP_PW + DZP_PROD - 1);
 // each stage of the ring always belongs to the same producer (stage % DZP_PROD)
@@ -683,6 +688,7 @@ dz_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
+  pdl_enter();   // inputs of this launch are complete from here on
   volatile int* abort_p = &abort_flag;
   const uint32_t lead_full0 = mapa_shared(full0, 0);
   const uint32_t lead_tempty0 = mapa_shared(tempty0, 0);
@@ -893,7 +899,10 @@ struct PairGemmCfg {
   // 7th stage but serialises the epilogue's reduce-adds (measured 5 % slower)
   static constexpr int STG_BUFS = KLG_GEMM_STG_BUFS;
   static constexpr int STAGING_BYTES = EPI_WARPS * STG_BUFS * 4096;
-  static constexpr int PROD = 3;                     // producer warps (round-robin load steps)
+#ifndef KLG_GEMM_PROD
+#define KLG_GEMM_PROD 3
+#endif
+  static constexpr int PROD = KLG_GEMM_PROD;         // producer warps (each owns stages s % PROD)
   static constexpr int PW = EPI_WARP0 + EPI_WARPS;   // first extra producer warp
   static constexpr int STAGES_RAW = (227 * 1024 - 2048 - STAGING_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
@@ -967,6 +976,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_consta
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
+  pdl_enter();   // inputs of this launch are complete from here on
   volatile int* abort_p = &abort_flag;
   const uint32_t lead_full0 = mapa_shared(full0, 0);
   const uint32_t lead_tempty0 = mapa_shared(tempty0, 0);
@@ -1131,6 +1141,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_consta
 
 // count = sum(mask), one block, deterministic.
 __global__ void count_valid_kernel(const uint8_t* __restrict__ mask, int n, float* __restrict__ count) {
+  pdl_enter();
   __shared__ int part[32];
   int c = 0;
   for (int i = threadIdx.x; i < n; i += blockDim.x) c += mask[i] != 0;
@@ -1148,6 +1159,7 @@ __global__ void count_valid_kernel(const uint8_t* __restrict__ mask, int n, floa
 
 // Online-softmax merge of n_part partial records [n_part][5][N] -> [5][N].
 __global__ void merge_kernel(const float* __restrict__ parts, int n_part, int n, float* __restrict__ out) {
+  pdl_enter();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const size_t st = (size_t)n;
@@ -1177,6 +1189,7 @@ __global__ void merge_kernel(const float* __restrict__ parts, int n_part, int n,
 __global__ void finalize_kernel(const float* __restrict__ stats, const uint8_t* __restrict__ mask, int n,
                                 const float* __restrict__ count, float* __restrict__ loss,
                                 float* __restrict__ lse, float* __restrict__ row_kl) {
+  pdl_enter();
   __shared__ float part[32];
   const size_t st = (size_t)n;
   const float ln2 = 0.69314718055994530942f;
@@ -1210,6 +1223,7 @@ __global__ void finalize_kernel(const float* __restrict__ stats, const uint8_t* 
 
 // lse[i] = log2-domain log-sum-exp of row i from n_part (m, S) records parts[n_part][2][n2].
 __global__ void lse_merge_kernel(const float* __restrict__ parts, int n_part, int n2, float* __restrict__ lse) {
+  pdl_enter();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n2) return;
   const size_t st = (size_t)n2;
@@ -1226,6 +1240,7 @@ __global__ void lse_merge_kernel(const float* __restrict__ parts, int n_part, in
 __global__ void row_kl_pair_kernel(const float* __restrict__ lse, const float* __restrict__ a_parts, int n_ap,
                                    const uint8_t* __restrict__ mask, int n, float* __restrict__ row_kl,
                                    float* __restrict__ block_sums) {
+  pdl_enter();
   __shared__ float part[8];
   const float ln2 = 0.69314718055994530942f;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -1251,6 +1266,7 @@ __global__ void row_kl_pair_kernel(const float* __restrict__ lse, const float* _
 // loss = sum(block_sums) / count (0 when count == 0); one block, fixed reduction order.
 __global__ void loss_from_sums_kernel(const float* __restrict__ block_sums, int n_blocks,
                                       const float* __restrict__ count, float* __restrict__ loss) {
+  pdl_enter();
   __shared__ float part[32];
   float acc = 0.f;
   for (int i = threadIdx.x; i < n_blocks; i += blockDim.x) acc += block_sums[i];
@@ -1269,7 +1285,15 @@ __global__ void loss_from_sums_kernel(const float* __restrict__ block_sums, int 
   }
 }
 
+// Zero n floats (n % 4 == 0, 16-byte aligned): gradient buffers before pass 2's reduce-adds.
+__global__ void zero_f32x4_kernel(float4* __restrict__ p, long long n4) {
+  pdl_enter();
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) p[i] = z;
+}
+
 __global__ void cast_f32_bf16_kernel(const float* __restrict__ in, __nv_bfloat16* __restrict__ out, long long n) {
+  pdl_enter();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long j = i; j < n; j += stride) out[j] = __float2bfloat16_rn(in[j]);

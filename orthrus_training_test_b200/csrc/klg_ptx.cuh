@@ -87,6 +87,18 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
   return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, status_bit)) != 0;
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization
+// may start (set-up only) while the previous kernel in the stream is finishing.  Every
+// kernel waits here before touching global memory, so completion stays transitive along
+// the stream, and lets the next kernel launch once all of its own blocks are running.
+// Both are no-ops for a normal launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_enter() {
+  pdl_wait();
+  pdl_launch_dependents();
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
