@@ -13,6 +13,10 @@ valid count and loss are all-reduced and dW is all-reduced over NCCL.
 
 ``value``  device-timed throughput with inputs resident (CUDA events per step,
            L2 flushed between steps by writing a 256 MiB buffer), max over ranks.
+``roofline`` / ``kernels``  per-kernel times from CUDA events recorded around every
+           launch on the launching stream, over K more steps run right after the
+           timed ones (the per-launch events would serialise the programmatic
+           dependent launches of the timed steps).
 ``e2e``    the same metric through the public autograd API with the step's
            inputs copied host->device (pinned) and the loss read back each step.
 ``--impl reference`` times the CPU restatement of the reference's loss (its
@@ -259,7 +263,6 @@ def main():
     barrier()
     torch.cuda.synchronize()
     launches0 = _lib.launch_count()
-    _lib.trace_begin(8192)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     for i in range(args.steps):
         flush.zero_()                                  # evict inputs from L2 (outside the timed events)
@@ -269,9 +272,15 @@ def main():
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
-    trace = _lib.trace_end(8192)
     launches = _lib.launch_count() - launches0
     clocks = sampler.stop() if sampler else None
+    # per-kernel breakdown: the same steps again with an event pair around every launch
+    _lib.trace_begin(8192)
+    for i in range(args.steps):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    trace = _lib.trace_end(8192)
     step_ms = [a.elapsed_time(b) for a, b in ev]
     total_ms = torch.tensor([sum(step_ms)], device=dev, dtype=torch.float64)
     if world > 1:

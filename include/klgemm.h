@@ -170,6 +170,7 @@ int klg_cast_f32_bf16(const float* in, void* out, int64_t n, void* stream);
 #define KLG_KIND_FINALIZE 5
 #define KLG_KIND_COUNT 6
 #define KLG_KIND_CAST 7
+#define KLG_KIND_ZERO 8      /* pass 2: zeroing of the fp32 dW / dH buffers            */
 int klg_trace_begin(int capacity);
 int klg_trace_end(int* kinds, float* ms, int capacity, int* n);
 

@@ -52,7 +52,7 @@ SIGNATURES = {
     "klg_trace_end": (c_int, [POINTER(c_int), POINTER(c_float), c_int, POINTER(c_int)]),
 }
 
-KIND_NAMES = {1: "stats", 2: "dz", 3: "gemm", 4: "merge", 5: "finalize", 6: "count", 7: "cast"}
+KIND_NAMES = {1: "stats", 2: "dz", 3: "gemm", 4: "merge", 5: "finalize", 6: "count", 7: "cast", 8: "zero"}
 
 _lib = None
 

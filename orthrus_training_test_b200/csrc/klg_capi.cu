@@ -582,7 +582,9 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
     if (!buf) continue;
     const long long n4 = (z ? n_rows : vocab) * hidden / 4;
     const int blocks = (int)std::min<long long>(cdiv(n4, 256), 4ll * num_sms());
+    const int slot = trace_pre(s);
     cudaError_t ze = launch_k(klg::zero_f32x4_kernel, dim3(blocks), dim3(256), 0, s, 1, reinterpret_cast<float4*>(buf), n4);
+    trace_post(slot, s, KLG_KIND_ZERO);
     if (ze != cudaSuccess) return cuda_fail(ze, "launch zero_f32x4_kernel");
     ++g_launches;
   }
