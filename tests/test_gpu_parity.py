@@ -203,3 +203,35 @@ def test_c3_shape_subsample():
     ours = run_both(p["h_s"], p["h_t"], p["W"], p["mask"], p["T"])
     ref_loss, ref_dh, ref_dw = run_oracle_torch_gpu(p["h_s"], p["h_t"], p["W"], p["mask"], p["T"])
     assert_close(ours, ref_loss, ref_dh, ref_dw, "c3-sub")
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_vocab_sharding_emulated_on_one_gpu(world):
+    """Vocab sharding's per-shard arithmetic on one device: the partial records of every
+    lm_head slice, merged with the online rule, give the full-vocabulary loss; each slice's
+    backward gives its dW rows and a partial dH whose sum is the full dH (what the NCCL
+    all-gather / all-reduce of parallel.vocab_sharded_kl_loss combine across GPUs)."""
+    from orthrus_training_test_b200.parallel import CudaEngine, shard_bounds
+
+    h_s, h_t, W, mask, T = rand_problem(900, 576, 7001, seed=21)
+    dev = torch.device("cuda:0")
+    eng = CudaEngine()
+    hs, ht, w, m = eng.prepare(h_s.to(dev)), eng.prepare(h_t.to(dev)), eng.prepare(W.to(dev)), eng.mask(mask.to(dev))
+    count = eng.count(m)
+    parts, slices = [], []
+    for r in range(world):
+        lo, hi = shard_bounds(W.shape[0], world, r)
+        slices.append((lo, hi))
+        parts.append(eng.partial_stats(hs, ht, w[lo:hi].contiguous(), T))
+    stats = eng.merge(torch.stack(parts))
+    loss, lse = eng.finalize(stats, m, count)
+    dh = torch.zeros(hs.shape, dtype=torch.float32, device=dev)
+    dws = []
+    for lo, hi in slices:
+        dh_r, dw_r = eng.backward(hs, ht, w[lo:hi].contiguous(), m, lse, count, None, T, True, True)
+        dh += dh_r
+        dws.append(dw_r)
+    torch.cuda.synchronize()
+    loss_ref, dh_ref, dw_ref, *_ = run_oracle_np(h_s, h_t, W, mask, T)
+    ours = dict(loss=float(loss.item()), dh=dh.double().cpu().numpy(), dw=torch.cat(dws).double().cpu().numpy())
+    assert_close(ours, loss_ref, dh_ref, dw_ref, f"vocab shards x{world}")
