@@ -660,7 +660,7 @@ struct FwdBwdLayout {
   int n_lp, n_ap;
 };
 int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
-FwdBwdLayout fwd_bwd_layout(int64_t n_rows, int64_t vocab, int64_t workspace_bytes) {
+FwdBwdLayout fwd_bwd_layout_uncached(int64_t n_rows, int64_t vocab, int64_t workspace_bytes) {
   FwdBwdLayout L{};
   int vpu, n_uv;
   plan_dual(2 * cdiv(n_rows, 256), cdiv(vocab, klg::LSE_BN), num_sms() / 2, vpu, n_uv);
@@ -669,7 +669,10 @@ FwdBwdLayout fwd_bwd_layout(int64_t n_rows, int64_t vocab, int64_t workspace_byt
   L.a_parts_off = align256(L.lse_parts_off + (int64_t)L.n_lp * 2 * 2 * n_rows * 4);
   L.cols = -1;
   const int64_t full = (int64_t)cdiv(vocab, 128) * 128;
-  for (int64_t c = full; c >= 128; c -= 128) {
+  // widest chunk that could fit (the cross-term partials only shrink the room), then narrower
+  int64_t c = (workspace_bytes - L.a_parts_off) / (n_rows * 2);
+  c = std::min(full, (c / 128) * 128);
+  for (; c >= 128; c -= 128) {
     if (cdiv(vocab, c) > KLG_BWD_HEADER / 4) break;
     const int n_ap = pass2_parts(n_rows, vocab, c);
     const int64_t dz_off = align256(L.a_parts_off + (int64_t)n_ap * n_rows * 4);
@@ -680,6 +683,23 @@ FwdBwdLayout fwd_bwd_layout(int64_t n_rows, int64_t vocab, int64_t workspace_byt
       break;
     }
   }
+  return L;
+}
+
+// Memoised: the layout is a pure function of the shape and workspace size.
+FwdBwdLayout fwd_bwd_layout(int64_t n_rows, int64_t vocab, int64_t workspace_bytes) {
+  static std::mutex mu;
+  static std::map<std::tuple<int64_t, int64_t, int64_t, int>, FwdBwdLayout> memo;
+  const auto key = std::make_tuple(n_rows, vocab, workspace_bytes, num_sms());
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = memo.find(key);
+    if (it != memo.end()) return it->second;
+  }
+  const FwdBwdLayout L = fwd_bwd_layout_uncached(n_rows, vocab, workspace_bytes);
+  std::lock_guard<std::mutex> lk(mu);
+  if (memo.size() > 256) memo.clear();
+  memo[key] = L;
   return L;
 }
 
