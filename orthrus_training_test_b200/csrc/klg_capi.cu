@@ -202,21 +202,6 @@ cudaError_t launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, int smem, cudaS
   return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
 }
 
-int launch_dual(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMap& mw, const klg::DualArgs& a,
-                cudaStream_t s) {
-  auto k = klg::dual_kernel;
-  constexpr int smem = klg::DUAL_SMEM;
-  cudaError_t e = set_smem(k, smem);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dual_kernel)");
-  const int grid = a.n_units < num_sms() ? a.n_units : num_sms();
-  const int slot = trace_pre(s);
-  e = launch_k(k, dim3(grid), dim3(klg::DUAL_THREADS), smem, s, 1, mhs, mht, mw, a);
-  trace_post(slot, s, KLG_KIND_STATS);
-  if (e != cudaSuccess) return cuda_fail(e, "launch dual_kernel");
-  ++g_launches;
-  return KLG_OK;
-}
-
 int launch_lse_pair(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMap& mw, const klg::LseArgs& a,
                     cudaStream_t s) {
   const bool res = a.n_kb <= klg::LSE_RES_MAX_KB;
@@ -233,15 +218,17 @@ int launch_lse_pair(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtens
   return KLG_OK;
 }
 
-int launch_dz_pair(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMap& mw, const CUtensorMap& mout,
-                   const klg::DualArgs& a, cudaStream_t s) {
-  cudaError_t e = set_smem(klg::dz_pair_kernel, klg::DZP_SMEM);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dz_pair_kernel)");
+template <int MODE>
+int launch_dual_pair(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMap& mw, const CUtensorMap& mout,
+                     const klg::DualArgs& a, cudaStream_t s) {
+  auto k = klg::dual_pair_kernel<MODE>;
+  cudaError_t e = set_smem(k, klg::DZP_SMEM);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dual_pair_kernel)");
   const int pairs = a.n_units < num_sms() / 2 ? a.n_units : num_sms() / 2;
   const int slot = trace_pre(s);
-  e = launch_k(klg::dz_pair_kernel, dim3(2 * pairs), dim3(klg::DZP_THREADS), klg::DZP_SMEM, s, 2, mhs, mht, mw, mout, a);
-  trace_post(slot, s, KLG_KIND_DZ);
-  if (e != cudaSuccess) return cuda_fail(e, "launch dz_pair_kernel");
+  e = launch_k(k, dim3(2 * pairs), dim3(klg::DZP_THREADS), klg::DZP_SMEM, s, 2, mhs, mht, mw, mout, a);
+  trace_post(slot, s, MODE == klg::MODE_DZ ? KLG_KIND_DZ : KLG_KIND_STATS);
+  if (e != cudaSuccess) return cuda_fail(e, "launch dual_pair_kernel");
   ++g_launches;
   return KLG_OK;
 }
@@ -423,11 +410,15 @@ int klg_device_status(int* status, int reset) {
 
 long long klg_launch_count(void) { return g_launches.load(); }
 
+// Forward statistics run on CTA pairs: (256-row pair tile, vocab range) units, at most 8
+// vocab ranges per row, one partial record per unit and epilogue column slice.
+constexpr int kStatsMaxRanges = 8;
+
 int klg_num_partials(int64_t n_rows, int64_t vocab, int* n_part) {
   if (!n_part || n_rows < 1 || vocab < 1) return fail(KLG_ERR_ARG, "bad arguments to klg_num_partials");
   int vpu, n_uv;
-  plan_dual(cdiv(n_rows, klg::BM), cdiv(vocab, klg::DUAL_BN), num_sms(), vpu, n_uv);
-  *n_part = n_uv;
+  plan_dual(cdiv(n_rows, 256), cdiv(vocab, klg::DZP_BN), num_sms() / 2, vpu, n_uv, kStatsMaxRanges);
+  *n_part = n_uv * klg::DZP_CSPLIT;
   return KLG_OK;
 }
 
@@ -440,11 +431,12 @@ int klg_fwd_stats(const void* hs, const void* ht, const void* w, int64_t n_rows,
   a.n_rows = (int)n_rows;
   a.v_begin = 0;
   a.v_count = (int)vocab;
-  a.n_rt = cdiv(n_rows, klg::BM);
-  a.n_vt = cdiv(vocab, klg::DUAL_BN);
+  a.n_rt = cdiv(n_rows, 256);
+  a.n_vt = cdiv(vocab, klg::DZP_BN);
   int n_uv;
-  plan_dual(a.n_rt, a.n_vt, num_sms(), a.vt_per_unit, n_uv);
-  if (n_part != n_uv) return fail(KLG_ERR_ARG, "n_part=%d but this device plans %d (use klg_num_partials)", n_part, n_uv);
+  plan_dual(a.n_rt, a.n_vt, num_sms() / 2, a.vt_per_unit, n_uv, kStatsMaxRanges);
+  if (n_part != n_uv * klg::DZP_CSPLIT)
+    return fail(KLG_ERR_ARG, "n_part=%d but this device plans %d (use klg_num_partials)", n_part, n_uv * klg::DZP_CSPLIT);
   if ((rc = bind_device(hs))) return rc;
   a.n_units = a.n_rt * n_uv;
   a.n_kb = cdiv(hidden, klg::BK);
@@ -453,9 +445,9 @@ int klg_fwd_stats(const void* hs, const void* ht, const void* w, int64_t n_rows,
   alignas(64) CUtensorMap mhs, mht, mw;
   if (!make_map(&mhs, hs, hidden, n_rows, hidden, klg::BK, klg::BM) ||
       !make_map(&mht, ht, hidden, n_rows, hidden, klg::BK, klg::BM) ||
-      !make_map(&mw, w, hidden, vocab, hidden, klg::BK, klg::DUAL_BN))
+      !make_map(&mw, w, hidden, vocab, hidden, klg::BK, klg::DZP_BN / 2))
     return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
-  return launch_dual(mhs, mht, mw, a, (cudaStream_t)stream);
+  return launch_dual_pair<klg::MODE_STATS>(mhs, mht, mw, mw, a, (cudaStream_t)stream);
 }
 
 int klg_merge_stats(const float* partials, int n_part, int64_t n_rows, float* stats, void* stream) {
@@ -552,7 +544,7 @@ int64_t klg_bwd_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t vocab) {
 
 namespace {
 
-// Pass 2 over vocab chunks of `cols` columns: dZ chunk (dz_pair_kernel) then one
+// Pass 2 over vocab chunks of `cols` columns: dZ chunk (dual_pair_kernel<MODE_DZ>) then one
 // pair-GEMM launch for dW_chunk and dH.  With a_parts set, the dZ pass also writes the
 // per-unit KL cross-term partials (at most 8 units per chunk), returning their count.
 int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask, const float* lse, const float* count,
@@ -617,7 +609,7 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
     if (!make_map(&mdz_out, dz, wv, n_rows, cols, klg::DZP_STORE_COLS, 32,
                   CU_TENSOR_MAP_SWIZZLE_64B))
       return fail(KLG_ERR_CUDA, "tensor map (dz store)");
-    if ((rc = launch_dz_pair(mhs, mht, mw, mdz_out, a, s))) return rc;
+    if ((rc = launch_dual_pair<klg::MODE_DZ>(mhs, mht, mw, mdz_out, a, s))) return rc;
     if (!d_hs && !d_w) continue;
     // one grouped launch: problem 0 = dW chunk (longer tiles first), problem 1 = dH += dZ W_chunk
     alignas(64) CUtensorMap mdz_k, mdz_mn;

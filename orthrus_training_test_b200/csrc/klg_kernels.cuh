@@ -4,19 +4,20 @@
 // Logits are z = h W^T / T.  All softmax arithmetic runs in the log2 domain:
 // u = z * log2(e) / T, so exp(z - m) = 2^(u - m2).
 //
-//  dual_kernel<STATS>  pass 1: per (row tile, vocab range) unit, both views'
-//                      logit tiles 128 x 128 via tcgen05.mma into TMEM, epilogue
-//                      keeps per-row online (m_s, S_s, m_t, S_t, A) and writes
-//                      one partial record per unit.
-//  dual_kernel<DZ>     pass 2: recomputes both views' logit tiles for one vocab
-//                      chunk and writes dZ = g/n * valid * (q - p) / T as bf16.
-//  gemm_kernel         D (+)= A * B with K-major or MN-major bf16 operands, fp32
-//                      out: dH += dZ W_chunk and dW_chunk = dZ^T h_s.
+//  lse_pair_kernel     training pass 1: per view, online (max, sum 2^(u - max)) per row
+//                      over all vocab tiles (row block resident for H <= 576).
+//  dual_pair_kernel    both views' logit tiles per (row pair tile, vocab tile):
+//     <MODE_DZ>        training pass 2: dZ = g valid/count (q - p)/T as bf16 for one vocab
+//                      chunk, plus the KL cross term sum_v p (u_t - u_s) per unit;
+//     <MODE_STATS>     forward only: per unit the online (m_s, S_s, m_t, S_t, A) record.
+//  gemm_pair_kernel    C (+)= A B over one backward chunk: dW_chunk = dZ^T h_s and
+//                      dH += dZ W_chunk in one launch (host-built longest-first schedule).
 //
-// Warp roles (all kernels): warp 0 issues TMA loads, warp 1 allocates TMEM and
-// issues tcgen05.mma from one thread, warps 2..5 are the epilogue (one TMEM lane,
-// i.e. one output row, per thread).  Shared-memory stages are recycled through
-// full/empty mbarriers; the two TMEM accumulator buffers through tmem_full /
+// All three run on CTA pairs (cluster of 2, tcgen05.mma.cta_group::2, M = 256).  Warp
+// roles: warp 0 (+ extra producer warps after the epilogue) issue TMA loads, warp 1
+// allocates TMEM and issues the MMAs, the other warps are the epilogue (warp w reads TMEM
+// lane quarter w % 4: one output row per thread).  Shared-memory stages are recycled
+// through full/empty mbarriers, the two TMEM accumulator buffers through tmem_full /
 // tmem_empty so the epilogue of tile j overlaps the MMAs of tile j+1.
 #pragma once
 #include "klg_ptx.cuh"
@@ -30,34 +31,23 @@ constexpr int EPI_WARP0 = 2;                // warp 0: TMA producer, warp 1: MMA
 constexpr float NEG_BIG = -1.0e30f;
 
 // =====================================================================================
-// dual-view kernel
+// per-(row pair tile, vocab range) work units shared by the dual-view kernels
 // =====================================================================================
-constexpr int DUAL_BN = 128;
-constexpr int DUAL_STAGES = 4;
-constexpr int DUAL_STAGE_BYTES = 3 * TILE_128x64;  // A_s | A_t | B
 constexpr int DUAL_TMEM_COLS = 512;                // 2 buffers x (Z_s 128 | Z_t 128)
-constexpr int DUAL_SMEM = 1024 + DUAL_STAGES * DUAL_STAGE_BYTES + 256;
-// A single thread issues about one TMA copy per ~250 cycles (measured on sm_100a), so the
-// ring's stages are shared out over DUAL_PROD producer warps (warp 0 and the warps after
-// the epilogue): stage s always belongs to producer s % DUAL_PROD, which keeps every
-// producer's waits on a stage in phase order.
-constexpr int DUAL_PROD = 2;
-constexpr int DUAL_PW = EPI_WARP0 + 4;                       // first extra producer warp
-constexpr int DUAL_THREADS = 32 * (DUAL_PW + DUAL_PROD - 1);
 
 struct DualArgs {
   int n_rows;       // N
   int v_begin;      // first W row of this launch
   int v_count;      // W rows covered by this launch
-  int n_rt;         // ceil(N / 128)
+  int n_rt;         // ceil(N / 256): 256-row pair tiles
   int n_vt;         // ceil(v_count / 128)
   int vt_per_unit;  // vocab tiles per work unit
   int n_units;      // n_rt * ceil(n_vt / vt_per_unit)
   int n_kb;         // ceil(H / 64)
   float scale_log2; // log2(e) / T
-  // statistics pass (dual_kernel)
-  float* partials;  // [n_uv][5][N]
-  // dZ pass (dz_pair_kernel)
+  // MODE_STATS
+  float* partials;  // [n_uv * DZP_CSPLIT][5][N]
+  // MODE_DZ
   const float* lse;      // [2][N] log2-domain log-sum-exp (student, teacher)
   const uint8_t* mask;   // [N]
   const float* count;    // device scalar: number of valid rows (global)
@@ -159,169 +149,6 @@ __device__ __forceinline__ void dz_chunk(const uint32_t (&bs)[32], const uint32_
     a1 = fmaf(j + 1 < nvalid ? p1 : 0.f, zt1 - zs1, a1);
   }
   acc += a0 + a1;
-}
-
-__global__ void __launch_bounds__(DUAL_THREADS, 1)
-dual_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ CUtensorMap map_ht,
-            const __grid_constant__ CUtensorMap map_w, const DualArgs a) {
-  extern __shared__ uint8_t smem_raw[];
-  __shared__ uint32_t tmem_slot;
-  __shared__ int abort_flag;
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const uint32_t sbase = smem_u32(smem);
-  const uint32_t bar0 = sbase + DUAL_STAGES * DUAL_STAGE_BYTES;
-  const uint32_t full0 = bar0;                          // [STAGES]
-  const uint32_t empty0 = bar0 + 8u * DUAL_STAGES;      // [STAGES]
-  const uint32_t tfull0 = bar0 + 16u * DUAL_STAGES;     // [2]
-  const uint32_t tempty0 = tfull0 + 16u;                // [2]
-  const uint32_t done_bar = tempty0 + 16u;
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-
-  if (threadIdx.x == 0) {
-    abort_flag = 0;
-    for (int s = 0; s < DUAL_STAGES; ++s) {
-      mbar_init(full0 + 8u * s, 1);
-      mbar_init(empty0 + 8u * s, 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(tfull0 + 8u * b, 1);
-      mbar_init(tempty0 + 8u * b, 4 * 32);
-    }
-    mbar_init(done_bar, 1);
-    fence_mbar_init();
-    tma_prefetch(&map_hs);
-    tma_prefetch(&map_ht);
-    tma_prefetch(&map_w);
-  }
-  if (warp == 1) tmem_alloc(smem_u32(&tmem_slot), DUAL_TMEM_COLS);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = tmem_slot;
-  pdl_enter();   // inputs of this launch are complete from here on
-  volatile int* abort_p = &abort_flag;
-
-  if (warp == 0 || warp >= DUAL_PW) {
-    // producer warps: warp 0 and warps DUAL_PW.. take the pipeline's load steps round-robin
-    const int prod = warp == 0 ? 0 : warp - DUAL_PW + 1;
-    {
-      // ------------------------------------------------------------ TMA producer (whole warp)
-      int stage = 0;
-      uint32_t phase = 0;
-      long long issued = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; ok && u < a.n_units; u += gridDim.x) {
-        int rt, uv, vt0, vt1;
-        dual_unit(a, u, rt, uv, vt0, vt1);
-        for (int vt = vt0; ok && vt < vt1; ++vt) {
-          for (int kb = 0; kb < a.n_kb; ++kb) {
-            if (stage % DUAL_PROD == prod) {
-              if (!warp_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
-              if (elect_one()) {
-                const uint32_t sb = sbase + stage * DUAL_STAGE_BYTES;
-                const uint32_t fb = full0 + 8u * stage;
-                mbar_arrive_expect_tx(fb, DUAL_STAGE_BYTES);
-                tma_load_2d(sb, &map_hs, fb, kb * BK, rt * BM);
-                tma_load_2d(sb + TILE_128x64, &map_ht, fb, kb * BK, rt * BM);
-                tma_load_2d(sb + 2 * TILE_128x64, &map_w, fb, kb * BK, a.v_begin + vt * DUAL_BN);
-              }
-            }
-            ++issued;
-            if (++stage == DUAL_STAGES) { stage = 0; phase ^= 1; }
-          }
-        }
-      }
-      if (prod == 0) drain_loads<DUAL_STAGES>(full0, stage, phase, issued);
-    }
-  } else if (warp == 1) {
-    {
-      // ------------------------------------------------------------ MMA issuer (whole warp)
-      constexpr uint32_t idesc = make_idesc_bf16(BM, DUAL_BN, false, false);
-      int stage = 0;
-      uint32_t phase = 0;
-      int tcount = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; ok && u < a.n_units; u += gridDim.x) {
-        int rt, uv, vt0, vt1;
-        dual_unit(a, u, rt, uv, vt0, vt1);
-        for (int vt = vt0; ok && vt < vt1; ++vt, ++tcount) {
-          const int buf = tcount & 1;
-          const uint32_t tph = (tcount >> 1) & 1;
-          if (!warp_wait(tempty0 + 8u * buf, tph ^ 1, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t d_s = tmem + buf * 256;
-          const uint32_t d_t = d_s + 128;
-          for (int kb = 0; kb < a.n_kb; ++kb) {
-            if (!warp_wait(full0 + 8u * stage, phase, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
-            tc_fence_after();
-            if (elect_one()) {
-              const uint32_t sb = sbase + stage * DUAL_STAGE_BYTES;
-#pragma unroll
-              for (int k = 0; k < BK / 16; ++k) {
-                const uint64_t bdesc = desc_kmajor(sb + 2 * TILE_128x64, k);
-                const uint32_t acc = (kb | k) != 0;
-                mma_bf16(d_s, desc_kmajor(sb, k), bdesc, idesc, acc);
-                mma_bf16(d_t, desc_kmajor(sb + TILE_128x64, k), bdesc, idesc, acc);
-              }
-              mma_commit(empty0 + 8u * stage);
-            }
-            if (++stage == DUAL_STAGES) { stage = 0; phase ^= 1; }
-          }
-          if (ok && elect_one()) mma_commit(tfull0 + 8u * buf);
-        }
-      }
-      // all issued MMAs must retire before TMEM is released
-      if (elect_one()) mma_commit(done_bar);
-      mbar_wait_drain(done_bar, 0);
-    }
-  } else {
-    // -------------------------------------------------------------- epilogue
-    const int q = warp & 3;                 // TMEM lane quarter of this warp
-    const int r_in_tile = q * 32 + lane;
-    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
-    int tcount = 0;
-    bool ok = true;
-    for (int u = blockIdx.x; ok && u < a.n_units; u += gridDim.x) {
-      int rt, uv, vt0, vt1;
-      dual_unit(a, u, rt, uv, vt0, vt1);
-      const int row = rt * BM + r_in_tile;
-      const bool row_ok = row < a.n_rows;
-      float ms = NEG_BIG, Ss = 0.f, mt = NEG_BIG, St = 0.f, A = 0.f;
-      for (int vt = vt0; ok && vt < vt1; ++vt, ++tcount) {
-        const int buf = tcount & 1;
-        const uint32_t tph = (tcount >> 1) & 1;
-        if (!mbar_wait(tfull0 + 8u * buf, tph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t tbase = lane_addr + buf * 256;
-        // load -> wait -> update per 32-column chunk
-#pragma unroll 1
-        for (int c = 0; c < DUAL_BN / 32; ++c) {
-          uint32_t bs[32], bt[32];
-          tmem_ld32_raw(tbase + c * 32, bs);
-          tmem_ld32_raw(tbase + 128 + c * 32, bt);
-          tmem_wait_ld_regs(bs, bt);
-          const int nvalid = min(32, a.v_count - (vt * DUAL_BN + c * 32));
-          if (nvalid > 0) stats_chunk(bs, bt, nvalid, a.scale_log2, ms, Ss, mt, St, A);
-        }
-        tc_fence_before();
-        mbar_arrive(tempty0 + 8u * buf);
-      }
-      if (ok && row_ok) {
-        float* p = a.partials + (size_t)uv * 5 * a.n_rows + row;
-        p[0] = ms;
-        p[(size_t)a.n_rows] = Ss;
-        p[(size_t)2 * a.n_rows] = mt;
-        p[(size_t)3 * a.n_rows] = St;
-        p[(size_t)4 * a.n_rows] = A;
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, DUAL_TMEM_COLS);
 }
 
 // =====================================================================================
@@ -643,8 +470,14 @@ constexpr int DZP_SMEM = 1024 + DZP_STAGES * DZP_STAGE_BYTES + DZP_STAGING_BYTES
 
 // Units: n_rt counts 256-row pair tiles; a_parts rows: a_part_base + uv * DZP_CSPLIT + column slice.
 // Staging rows are DZP_COLS_PER_WARP bf16 wide (128 or 64 bytes) in the matching TMA swizzle.
+enum { MODE_DZ = 0, MODE_STATS = 1 };
+
+// MODE_DZ: pass 2 (dZ chunk + cross-term partials).  MODE_STATS: the single-pass forward
+// for evaluation -- per row and unit the online (m_s, S_s, m_t, S_t, A) record over the
+// unit's vocabulary tiles (no dZ, no staging use).
+template <int MODE>
 __global__ void __launch_bounds__(DZP_THREADS, 1)
-dz_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ CUtensorMap map_ht,
+dual_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ CUtensorMap map_ht,
                const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_out,
                const DualArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -771,6 +604,50 @@ dz_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant
       }
       if (elect_one()) mma_commit_pair(done_bar);
       mbar_wait_drain(done_bar, 0);
+    }
+  } else if (MODE == MODE_STATS) {
+    // -------------------------------------------------------------- statistics epilogue
+    const int q = warp & 3;
+    const int h = (warp - EPI_WARP0) >> 2;   // column slice of the 128-column tile
+    constexpr int CW = DZP_COLS_PER_WARP;
+    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * CW);
+    int tcount = 0;
+    bool ok = true;
+    for (int u = cid; ok && u < a.n_units; u += n_clusters) {
+      int rt, uv, vt0, vt1;
+      dual_unit(a, u, rt, uv, vt0, vt1);
+      const int row = rt * 256 + (int)rank * 128 + q * 32 + lane;
+      float ms = NEG_BIG, Ss = 0.f, mt = NEG_BIG, St = 0.f, A = 0.f;
+      for (int vt = vt0; ok && vt < vt1; ++vt, ++tcount) {
+        const int buf = tcount & 1;
+        const uint32_t tph = (tcount >> 1) & 1;
+        if (!mbar_wait(tfull0 + 8u * buf, tph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t tbase = lane_addr + buf * 256;
+#pragma unroll 1
+        for (int c = 0; c < CW / 32; ++c) {
+          uint32_t bs[32], bt[32];
+          tmem_ld32_raw(tbase + c * 32, bs);
+          tmem_ld32_raw(tbase + 128 + c * 32, bt);
+          tmem_wait_ld_regs(bs, bt);
+          const int nvalid = min(32, a.v_count - (vt * DZP_BN + h * CW + c * 32));
+          if (nvalid > 0) stats_chunk(bs, bt, nvalid, a.scale_log2, ms, Ss, mt, St, A);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (leader) mbar_arrive(tempty0 + 8u * buf);
+          else mbar_arrive_cluster(lead_tempty0 + 8u * buf);
+        }
+      }
+      if (ok && row < a.n_rows) {
+        float* p = a.partials + (size_t)(uv * DZP_CSPLIT + h) * 5 * a.n_rows + row;
+        p[0] = ms;
+        p[(size_t)a.n_rows] = Ss;
+        p[(size_t)2 * a.n_rows] = mt;
+        p[(size_t)3 * a.n_rows] = St;
+        p[(size_t)4 * a.n_rows] = A;
+      }
     }
   } else {
     const int q = warp & 3;

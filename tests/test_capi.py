@@ -56,7 +56,8 @@ def test_argument_validation_codes():
     assert L.klg_fwd_stats(p, p, p, 4, 64, 4, float("inf"), p, 1, None) == _lib.KLG_ERR_ARG
     # wrong partial-record count for this problem
     n = ctypes.c_int(0)
-    assert L.klg_num_partials(4, 4, ctypes.byref(n)) == 0 and n.value == 1
+    # one (row pair tile, vocab range) unit x 2 epilogue column slices
+    assert L.klg_num_partials(4, 4, ctypes.byref(n)) == 0 and n.value == 2
     assert L.klg_fwd_stats(p, p, p, 4, 64, 4, 1.0, p, 7, None) == _lib.KLG_ERR_ARG
     # workspace too small
     assert L.klg_fwd(p, p, p, p, 4, 64, 4, 1.0, 0, p, p, p, None, p, 8, None) == _lib.KLG_ERR_WORKSPACE
