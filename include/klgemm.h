@@ -54,6 +54,20 @@ int klg_last_error(char* buf, int len);
  * bound (the kernel then ended early).  Synchronises the device. */
 int klg_device_status(int* status, int reset);
 
+/* Device status bits. */
+#define KLG_STATUS_TIMEOUT_PRODUCER 0x1   /* a TMA producer waited out its bound on a free stage   */
+#define KLG_STATUS_TIMEOUT_MMA 0x2        /* the MMA issuer waited out its bound on operands/TMEM  */
+#define KLG_STATUS_TIMEOUT_EPILOGUE 0x4   /* an epilogue warp waited out its bound on a tile       */
+#define KLG_STATUS_TIMEOUT_DRAIN 0x8      /* a final drain of copies / MMAs waited out its bound   */
+#define KLG_STATUS_SELFTEST 0x100         /* set by klg_selftest_wait_timeout                      */
+
+/* Test hook (no counterpart in the reference): launches one block that waits on an
+ * mbarrier nothing will complete, through the same bounded wait every pipeline uses.
+ * After the bound (~1 s) the wait gives up, sets KLG_STATUS_SELFTEST and the block
+ * exits normally, so the context stays usable.  Exercises the timeout path without
+ * faulting the GPU. */
+int klg_selftest_wait_timeout(void* stream);
+
 /* Number of kernels this library has launched in this process. */
 long long klg_launch_count(void);
 

@@ -27,6 +27,7 @@ SIGNATURES = {
     "klg_last_error": (c_int, [c_char_p, c_int]),
     "klg_device_status": (c_int, [POINTER(c_int), c_int]),
     "klg_launch_count": (c_longlong, []),
+    "klg_selftest_wait_timeout": (c_int, [c_void_p]),
     "klg_num_partials": (c_int, [c_int64, c_int64, POINTER(c_int)]),
     "klg_fwd_stats": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_float, c_void_p, c_int,
                               c_void_p]),

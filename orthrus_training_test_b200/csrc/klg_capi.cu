@@ -410,6 +410,13 @@ int klg_device_status(int* status, int reset) {
 
 long long klg_launch_count(void) { return g_launches.load(); }
 
+int klg_selftest_wait_timeout(void* stream) {
+  cudaError_t e = launch_k(klg::wait_selftest_kernel, dim3(1), dim3(32), 0, (cudaStream_t)stream, 1);
+  if (e != cudaSuccess) return cuda_fail(e, "launch wait_selftest_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
 // Forward statistics run on CTA pairs: (256-row pair tile, vocab range) units, at most 8
 // vocab ranges per row, one partial record per unit and epilogue column slice.
 constexpr int kStatsMaxRanges = 8;

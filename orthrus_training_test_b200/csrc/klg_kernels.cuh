@@ -1162,6 +1162,20 @@ __global__ void loss_from_sums_kernel(const float* __restrict__ block_sums, int 
   }
 }
 
+// Self-test of the bounded wait: one warp waits on an mbarrier that nothing arrives on.
+// mbar_wait gives up after KLG_WAIT_CYCLES, sets KLG_STATUS_SELFTEST and returns false.
+__global__ void wait_selftest_kernel() {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(smem_u32(&bar), 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  (void)warp_wait(smem_u32(&bar), 0, &abort_flag, KLG_STATUS_SELFTEST);
+}
+
 // Zero n floats (n % 4 == 0, 16-byte aligned): gradient buffers before pass 2's reduce-adds.
 __global__ void zero_f32x4_kernel(float4* __restrict__ p, long long n4) {
   pdl_enter();

@@ -13,11 +13,8 @@
 #define KLG_WAIT_CYCLES (1ll << 31)   // ~1.1 s at 1.9 GHz
 #endif
 
-// device status bits (read back by klg_device_status)
-#define KLG_STATUS_TIMEOUT_PRODUCER 0x1
-#define KLG_STATUS_TIMEOUT_MMA 0x2
-#define KLG_STATUS_TIMEOUT_EPILOGUE 0x4
-#define KLG_STATUS_TIMEOUT_DRAIN 0x8
+// device status bits (read back by klg_device_status; the values are in klgemm.h)
+#include "klgemm.h"
 
 namespace klg {
 
