@@ -133,8 +133,8 @@ long long klg_fwd_noalloc_max_floats(void);
  * Replaces: autograd of train.py:202-210 (which stores bf16 [chunk, V] logits)
  * and, with the lm_head trainable, its weight gradient. */
 
-/* Recommended workspace bytes for klg_bwd (4 KiB of tile counters + a [n_rows, C]
- * bf16 dZ chunk). */
+/* Recommended workspace bytes for klg_bwd (a 4 KiB reserved header + a [n_rows, C]
+ * bf16 dZ chunk of at most 512 MiB). */
 int64_t klg_bwd_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t vocab);
 
 /* Vocab columns per backward chunk for a given workspace size (-1 if < 128). */

@@ -519,7 +519,9 @@ int klg_fwd(const void* hs, const void* ht, const void* w, const uint8_t* mask, 
   return klg_finalize(stats, mask, n_rows, count, loss, lse, row_kl, stream);
 }
 
-// Backward workspace: [KLG_BWD_HEADER bytes: one tile counter per chunk][dZ chunk N x C bf16].
+// Backward workspace: [KLG_BWD_HEADER bytes, reserved][dZ chunk N x C bf16].  The header also
+// bounds the chunk count (cdiv(V, C) <= KLG_BWD_HEADER / 4) and, in the fused layout, is
+// where the pass-1 partials start.
 #define KLG_BWD_HEADER 4096
 
 int64_t klg_bwd_chunk_cols(int64_t n_rows, int64_t vocab, int64_t workspace_bytes) {

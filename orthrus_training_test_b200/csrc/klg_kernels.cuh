@@ -740,7 +740,7 @@ struct GemmProblem {
 };
 
 // =====================================================================================
-// grouped GEMM on CTA pairs: the backward chunk's dW = dZ^T h_s and dH (+)= dZ W_chunk.
+// pair GEMM: the backward chunk's dW = dZ^T h_s and dH (+)= dZ W_chunk in one launch.
 // Tile = (problem, 256-row pair tile, BN-column tile); each CTA holds 128 rows of A and
 // one BN/2-column half of B (MN-major, 64-byte swizzle: 32-column boxes).  Tiles are
 // assigned to pairs by a longest-first greedy schedule built on the host and passed in
