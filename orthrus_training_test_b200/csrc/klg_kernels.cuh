@@ -59,9 +59,14 @@ struct DualArgs {
   int a_part_base;
 };
 
+// Units are numbered row-tile-major: the pairs that run at the same time share a few row
+// tiles (both views: 2 x 256 rows x H), so the rows stay in L2 while each pair sweeps its own
+// vocabulary range.  (Numbered vocab-range-major, 74 pairs stream 74 different row tiles:
+// 148 MB at H = 2048, more than L2, and every vocabulary tile re-reads its rows from DRAM.)
 __device__ __forceinline__ void dual_unit(const DualArgs& a, int u, int& rt, int& uv, int& vt0, int& vt1) {
-  rt = u % a.n_rt;
-  uv = u / a.n_rt;
+  const int n_uv = (a.n_vt + a.vt_per_unit - 1) / a.vt_per_unit;
+  rt = u / n_uv;
+  uv = u - rt * n_uv;
   vt0 = uv * a.vt_per_unit;
   vt1 = min(vt0 + a.vt_per_unit, a.n_vt);
 }
