@@ -10,6 +10,10 @@ Workload at N=1 is the 16,384-row SmolLM2-135M training shape (H=576,
 V=49,152, bf16, block-32 mask with ratio U(0,1)); synthetic seeded inputs.
 At N>1 each rank runs its own 16,384 rows (weak scaling, row sharded): the
 valid count and loss are all-reduced and dW is all-reduced over NCCL.
+``--config c4`` at N>1 shards the 248,320-row lm_head by vocab instead (strong
+scaling): every rank holds all 32,768 rows and one W slice, the per-row
+(m, S, m, S, A) partial records are all-gathered and merged, and the partial
+dH is all-reduced; ``value`` then counts each row once.
 
 ``value``  device-timed throughput with inputs resident (CUDA events per step,
            L2 flushed between steps by writing a 256 MiB buffer), max over ranks.
@@ -46,6 +50,7 @@ CONFIGS = {
                               "block-32 mask ratio U(0,1)"),
     "c5": (12288, 576, 49152, "ragged/edge: 12288 rows, ~25% valid, teacher x4, T=2, bf16"),
     "c3": (65536, 2048, 49152, "SmolLM2-1.7B shape, [32,2048,2048] per view, V=49152, bf16"),
+    "c4": (32768, 1024, 248320, "large-vocab shape, [16,2048,1024] per view, V=248320, bf16 (vocab-sharded at N>1)"),
 }
 METRIC = "KL-GEMM fwd+bwd loss-rows/sec"
 L2_FLUSH_BYTES = 256 << 20
@@ -192,12 +197,32 @@ def run_reference_arm(args):
                          "sample": f"{sample} of {N} rows per step, full V, fp32 fwd+bwd incl. dW"},
         "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
+
+
+# stdout carries exactly one line, the JSON result: everything else written to file
+# descriptor 1 (NCCL's version banner, library messages) is sent to stderr.
+_RESULT_OUT = None
+
+
+def _claim_stdout():
+    global _RESULT_OUT
+    if _RESULT_OUT is None:
+        sys.stdout.flush()
+        _RESULT_OUT = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
+
+
+def emit(line: dict) -> None:
+    _claim_stdout()
+    _RESULT_OUT.write(json.dumps(line) + "\n")
+    _RESULT_OUT.flush()
 
 
 # ----------------------------------------------------------------------------- our arm
 def main():
     args = parse()
+    _claim_stdout()
     if args.impl == "reference":
         run_reference_arm(args)
         return
@@ -207,7 +232,7 @@ def main():
 
     from oracle import klgemm_oracle as O  # input generator only (seeded workload shapes)
     from orthrus_training_test_b200 import _lib, ops
-    from orthrus_training_test_b200.parallel import row_sharded_kl_loss
+    from orthrus_training_test_b200.parallel import row_sharded_kl_loss, shard_bounds, vocab_sharded_kl_loss
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -222,12 +247,18 @@ def main():
     _lib.lib()
 
     N, H, V, desc = CONFIGS[args.config]
-    p = O.make_problem(args.config, seed=42 + rank)       # this rank's rows
+    vocab_sharded = args.config == "c4" and world > 1
+    p = O.make_problem(args.config, seed=42 if vocab_sharded else 42 + rank)   # this rank's rows
     pw = O.make_problem(args.config, n_rows=1, seed=42)   # shared lm_head
     T = p["T"]
     hs = p["h_s"].to(dev)
     ht = p["h_t"].to(dev)
     W = pw["W"].to(dev)
+    V_work = V                                            # lm_head rows this rank computes over
+    if vocab_sharded:
+        lo, hi = shard_bounds(V, world, rank)
+        W = W[lo:hi].contiguous()
+        V_work = hi - lo
     m = ops.mask_u8(p["mask"].to(dev))
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
 
@@ -235,9 +266,25 @@ def main():
         if world > 1:
             dist.barrier()
 
-    fb_ws = int(_lib.lib().klg_fwd_bwd_workspace_bytes(N, H, V))
+    fb_ws = int(_lib.lib().klg_fwd_bwd_workspace_bytes(N, H, V_work))
+    bwd_ws = int(_lib.lib().klg_bwd_workspace_bytes(N, H, V_work))
+    gathered = torch.empty(world * 5, N, dtype=torch.float32, device=dev) if vocab_sharded else None
+
+    def step_vocab():
+        # vocab-sharded step: local partial records -> all-gather -> merge -> loss and log-sum-exps
+        # -> local pass 2 (this slice's dW, a partial dH) -> dH all-reduced
+        cnt = ops.count_valid(m)                       # the same rows on every rank
+        local = ops.merge_stats(ops.fwd_stats(hs, ht, W, T)).contiguous()
+        dist.all_gather_into_tensor(gathered, local)
+        stats = ops.merge_stats(gathered.view(world, 5, N))
+        loss, lse, _ = ops.finalize(stats, m, cnt)
+        dh, dw = ops.kl_backward(hs, ht, W, m, lse, cnt, temperature=T, workspace_bytes=bwd_ws)
+        dist.all_reduce(dh)
+        return loss
 
     def step():
+        if vocab_sharded:
+            return step_vocab()
         # the training step: count (all-reduced across ranks) -> loss + dH + dW -> loss and dW all-reduced
         cnt = ops.count_valid(m)
         if world > 1:
@@ -288,7 +335,7 @@ def main():
     total_ms = float(total_ms.item())
     assert _lib.device_status() == 0
 
-    rows_total = N * world * args.steps
+    rows_total = N * (1 if vocab_sharded else world) * args.steps
     value = rows_total / (total_ms / 1e3)
 
     # ---------------------------------------------------------------- per-kernel roofline
@@ -298,7 +345,7 @@ def main():
         t = by_kind.setdefault(kind, [0.0, 0])
         t[0] += ms
         t[1] += 1
-    flops_per_step = {"stats": 4.0 * N * H * V, "dz": 4.0 * N * H * V, "gemm": 4.0 * N * H * V}
+    flops_per_step = {"stats": 4.0 * N * H * V_work, "dz": 4.0 * N * H * V_work, "gemm": 4.0 * N * H * V_work}
     dom = max((k for k in by_kind if k in flops_per_step), key=lambda k: by_kind[k][0])
     dom_ms, dom_n = by_kind[dom]
     dom_flops_per_launch = flops_per_step[dom] * args.steps / dom_n
@@ -310,7 +357,7 @@ def main():
                 "peak_kind": f"{peak_src} sustained bf16 (kernel timed inside back-to-back steps)",
                 "frac_of_burst_peak": achieved / peak_burst,
                 "algorithmic_flops_per_launch": dom_flops_per_launch}
-    step_flops = 8.0 * N * H * V
+    step_flops = 8.0 * N * H * V_work   # per GPU
     kernels = {k: {"launches": n, "total_ms": t, "share": t / sum(x[0] for x in by_kind.values())}
                for k, (t, n) in sorted(by_kind.items(), key=lambda kv: -kv[1][0])}
 
@@ -327,7 +374,9 @@ def main():
             hs_d = hs_h.to(dev, non_blocking=True).requires_grad_(True)
             ht_d = ht_h.to(dev, non_blocking=True)
             m_d = m_h.to(dev, non_blocking=True)
-            if world > 1:
+            if vocab_sharded:
+                loss = vocab_sharded_kl_loss(hs_d, ht_d, Wp, m_d, T)
+            elif world > 1:
                 loss = row_sharded_kl_loss(hs_d, ht_d, Wp, m_d, T)
             else:
                 loss = ops.kl_gemm_loss(hs_d, ht_d, Wp, m_d, T)
@@ -354,7 +403,8 @@ def main():
             dist.all_reduce(et, op=dist.ReduceOp.MAX)
         e2e = {"value": rows_total / (float(et.item()) / 1e3), "unit": "rows/s", "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": 4, "ms_per_step": float(et.item()) / args.steps,
-               "api": "row_sharded_kl_loss" if world > 1 else "kl_gemm_loss (KLGemmFn autograd)"}
+               "api": ("vocab_sharded_kl_loss" if vocab_sharded else "row_sharded_kl_loss" if world > 1
+                       else "kl_gemm_loss (KLGemmFn autograd)")}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -366,10 +416,13 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) hidden, "
+            "scaling": "strong" if vocab_sharded else "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) hidden, "
             "N(0,0.02) lm_head)",
             "config": {"workload": f"{args.config}: {desc}", "rows_per_gpu": N, "hidden": H, "vocab": V,
-                       "temperature": T, "parallelism": f"row-sharded dp{world}" if world > 1 else "single GPU",
+                       "vocab_per_gpu": V_work,
+                       "temperature": T, "parallelism": (f"vocab-sharded x{world}" if vocab_sharded else
+                                                         f"row-sharded dp{world}" if world > 1 else "single GPU"),
                        "l2": "flushed between steps (256 MiB write)"},
             "tensor_peak_frac": {"algorithmic_flops_per_step": step_flops,
                                  "achieved_tflops": step_flops / (total_ms / args.steps / 1e3) / 1e12,
@@ -383,7 +436,7 @@ def main():
             "cpu_baseline": cpu,
             "clocks": clocks,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         dist.destroy_process_group()
 
