@@ -20,6 +20,8 @@
 #include <tuple>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>   // header-only; ranges are free unless a profiler is attached
+
 #include "klg_kernels.cuh"
 #include "klgemm.h"
 
@@ -97,6 +99,14 @@ void trace_post(int slot, cudaStream_t s, int kind) {
   cudaEventRecord(g_trace.ev[2 * slot + 1], s);
   g_trace.kind[slot] = kind;
 }
+
+// NVTX range around an entry point or pass, visible in Nsight timelines.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 int num_sms() {
   int dev = 0, n = 0;
@@ -445,6 +455,7 @@ int klg_fwd_stats(const void* hs, const void* ht, const void* w, int64_t n_rows,
   if (n_part != n_uv * klg::DZP_CSPLIT)
     return fail(KLG_ERR_ARG, "n_part=%d but this device plans %d (use klg_num_partials)", n_part, n_uv * klg::DZP_CSPLIT);
   if ((rc = bind_device(hs))) return rc;
+  NvtxRange nvtx_range("klg_fwd_stats");
   a.n_units = a.n_rt * n_uv;
   a.n_kb = cdiv(hidden, klg::BK);
   a.scale_log2 = inv_temp * 1.4426950408889634f;
@@ -511,6 +522,7 @@ int klg_fwd(const void* hs, const void* ht, const void* w, const uint8_t* mask, 
   const int64_t need = (int64_t)(n_part + 1) * 5 * n_rows * 4;
   if (!workspace || workspace_bytes < need || !aligned16(workspace))
     return fail(KLG_ERR_WORKSPACE, "forward workspace needs %lld bytes (16-byte aligned)", (long long)need);
+  NvtxRange nvtx_range("klg_fwd");
   float* parts = static_cast<float*>(workspace);
   float* stats = parts + (size_t)n_part * 5 * n_rows;
   if (!count_given && (rc = klg_count_valid(mask, n_rows, count, stream))) return rc;
@@ -721,6 +733,7 @@ int klg_bwd(const void* hs, const void* ht, const void* w, const uint8_t* mask, 
     return fail(KLG_ERR_WORKSPACE, "backward workspace too small: needs >= %lld bytes",
                 (long long)(KLG_BWD_HEADER + n_rows * 256));
   if ((rc = bind_device(hs))) return rc;
+  NvtxRange nvtx_range("klg_bwd (pass 2)");
 
   __nv_bfloat16* dz = reinterpret_cast<__nv_bfloat16*>(static_cast<uint8_t*>(workspace) + KLG_BWD_HEADER);
   return run_pass2(hs, ht, w, mask, lse, count, grad, n_rows, hidden, vocab, inv_temp, d_hs, d_w, dz, cols,
@@ -755,6 +768,7 @@ int klg_fwd_bwd(const void* hs, const void* ht, const void* w, const uint8_t* ma
     return fail(KLG_ERR_WORKSPACE, "workspace of %lld bytes too small (see klg_fwd_bwd_workspace_bytes)",
                 (long long)workspace_bytes);
   if ((rc = bind_device(hs))) return rc;
+  NvtxRange nvtx_range("klg_fwd_bwd");
   cudaStream_t s = (cudaStream_t)stream;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   float* lse_parts = reinterpret_cast<float*>(ws + L.lse_parts_off);

@@ -124,6 +124,15 @@ def test_ragged_shapes(N, H, V):
     assert_close(ours, loss, dh, dw, f"N{N} H{H} V{V}")
 
 
+def test_trainer_vocab_with_mask_token():
+    """The trainer adds a <mask> token to SmolLM2's 49,152-row vocabulary (V = 49,153: one
+    row past the last 128 tile, and a ragged last chunk); 2,048 rows of that shape."""
+    h_s, h_t, W, mask, T = rand_problem(2048, 576, 49153, seed=17)
+    ours = run_both(h_s, h_t, W, mask, T)
+    loss, dh, dw, *_ = run_oracle_np(h_s, h_t, W, mask, T)
+    assert_close(ours, loss, dh, dw, "V=49153")
+
+
 def test_temperature_and_peaky_teacher():
     h_s, h_t, W, mask, _ = rand_problem(400, 576, 2000, seed=5, tscale=4.0, p=0.25)
     mask[:8] = False
