@@ -773,7 +773,12 @@ struct PairGemmCfg {
   // instead of 6, which measured ~9 % slower at the 16k-row shape)
   static constexpr int KPS = KLG_GEMM_KPS;
   static constexpr int STAGE_BYTES = KPS * (A_BYTES + B_BYTES);   // [A kb0 | A kb1 | B kb0 | B kb1]
-  static constexpr int EPI_WARPS = 4;
+#ifndef KLG_GEMM_EPI
+#define KLG_GEMM_EPI 4
+#endif
+  // 4 or 8 epilogue warps (8: two per TMEM lane quarter); 8 measured no faster at the
+  // 16k-row shape (with one staging buffer per warp) and slower with two (5 load stages)
+  static constexpr int EPI_WARPS = KLG_GEMM_EPI;
 #ifndef KLG_GEMM_STG_BUFS
 #define KLG_GEMM_STG_BUFS 2
 #endif
@@ -964,6 +969,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_consta
     // Each 32 x 32 fp32 block goes through a 128-byte-swizzled staging buffer and is added
     // into C by a TMA reduce-add (the add happens at L2; C was zeroed before the launch).
     const int q = warp & 3;
+    const int hh = (warp - EPI_WARP0) >> 2;          // column half when two warps share a quarter
+    constexpr int PER = (BN / 32) / (EPI / 4);       // 32-column blocks per warp and tile
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
     const uint32_t stg = stg0 + (uint32_t)(warp - EPI_WARP0) * (Cfg::STG_BUFS * 4096u);
     int sbuf = 0;
@@ -978,7 +985,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_consta
       tc_fence_after();
       const int row_blk = mt * 256 + (int)rank * 128 + q * 32;   // first C row of this warp
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = hh * PER; c < (hh + 1) * PER; ++c) {
         uint32_t v[32];
         tmem_ld32_raw(lane_addr + buf * BN + c * 32, v);
         tmem_wait_ld_regs(v);
