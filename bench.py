@@ -53,6 +53,13 @@ CONFIGS = {
     "c4": (32768, 1024, 248320, "large-vocab shape, [16,2048,1024] per view, V=248320, bf16 (vocab-sharded at N>1)"),
 }
 METRIC = "KL-GEMM fwd+bwd loss-rows/sec"
+SAMPLE_METRIC = "lm_head token selections/sec"
+# fused lm_head + token selection (inference): rows, hidden, vocab, temperature, description
+SAMPLE_CONFIGS = {
+    "s1": (32, 576, 49153, 1.0, "decode: one K=32 block of rows (generate.py:149-188), SmolLM2-135M lm_head "
+                               "H=576, V=49153 (with the mask token), T=1 sampling"),
+    "s2": (16384, 576, 49153, 1.0, "scoring: 16384 rows, H=576, V=49153, T=1 sampling"),
+}
 L2_FLUSH_BYTES = 256 << 20
 
 
@@ -62,7 +69,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS), default="c2")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + sorted(SAMPLE_CONFIGS), default="c2")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="time budget of the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -75,6 +82,13 @@ def load_peaks():
         d = json.loads(p.read_text())
         return d.get("bf16_tflops", 1590.0), d.get("bf16_tflops_sustained", 1400.0), "measured"
     return 1590.0, 1400.0, "fallback"
+
+
+def load_hbm_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()).get("hbm_gbs", 6650.0), "measured"
+    return 6650.0, "fallback"
 
 
 def load_traffic(kernel: str, config: str):
@@ -219,10 +233,181 @@ def emit(line: dict) -> None:
     _RESULT_OUT.flush()
 
 
+# ----------------------------------------------------------------------------- sampling workload
+def _timed(fn, steps, flush):
+    import torch
+    ms = []
+    for _ in range(steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        ms.append(a.elapsed_time(b))
+    return ms
+
+
+def run_sample(args):
+    """One step = one token per row of ``h`` from ``h @ W^T`` (the lm_head of generate.py:161-188
+    followed by sample_token, generate.py:40-78): the fused kernel against the reference's op
+    sequence on cuBLAS logits (same GPU) and the float64 oracle on the host."""
+    import torch
+    import torch.nn.functional as F
+
+    from oracle import klgemm_oracle as O
+    from orthrus_training_test_b200 import _lib, sampling
+
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        if int(os.environ.get("RANK", "0")) == 0:
+            emit({"metric": SAMPLE_METRIC, "impl": args.impl, "unavailable": "sampling workloads run on one GPU"})
+        return
+    N, H, V, T, desc = SAMPLE_CONFIGS[args.config]
+    if args.impl == "reference":
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        g = torch.Generator().manual_seed(1)
+        sample = min(N, 32)
+        h = torch.randn(sample, H, generator=g).to(torch.bfloat16).float()
+        W = (torch.randn(V, H, generator=g) * 0.05).to(torch.bfloat16).float()
+        for _ in range(max(1, args.warmup)):
+            O.sample_token_torch(F.linear(h, W), T)
+        times = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            O.sample_token_torch(F.linear(h, W), T)
+            times.append(time.perf_counter() - t0)
+        value = sample * args.steps / sum(times)
+        emit({"metric": SAMPLE_METRIC, "value": value, "unit": "rows/s", "n_gpus": args.gpus, "steps": args.steps,
+              "warmup": args.warmup, "ms_per_step": 1e3 * sum(times) / args.steps, "higher_is_better": True,
+              "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded)",
+              "impl": "reference",
+              "config": {"workload": f"{args.config}: {desc}", "rows": N, "hidden": H, "vocab": V,
+                         "rows_per_step_sample": sample, "parallelism": "host CPU"},
+              "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "port",
+                               "sample": f"{sample} of {N} rows per step: fp32 F.linear + sample_token op sequence"},
+              "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+        return
+
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    g = torch.Generator().manual_seed(1)
+    h_host = torch.randn(N, H, generator=g).to(torch.bfloat16)
+    W = (torch.randn(V, H, generator=g) * 0.05).to(torch.bfloat16).to(dev)
+    h = h_host.to(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    ws = torch.empty(sampling.workspace_bytes(N, V), dtype=torch.uint8, device=dev)
+    seeds = iter(range(1, 1 << 30))
+
+    def ours(temp):
+        return sampling.lm_head_sample(h, W, temp, next(seeds), workspace=ws)
+
+    def torch_ref(temp):
+        return O.sample_token_torch(F.linear(h, W).float(), temp)
+
+    for _ in range(args.warmup):
+        ours(T), ours(0.0), torch_ref(T), torch_ref(0.0)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    sampler = ClockSampler(0)
+    sampler.start()
+    time.sleep(0.3)
+    launches0 = _lib.launch_count()
+    ms = _timed(lambda: ours(T), args.steps, flush)
+    launches = _lib.launch_count() - launches0
+    ms_greedy = _timed(lambda: ours(0.0), args.steps, flush)
+    clocks = sampler.stop()
+    ms_torch = _timed(lambda: torch_ref(T), args.steps, flush)
+    ms_torch_greedy = _timed(lambda: torch_ref(0.0), args.steps, flush)
+    _lib.trace_begin(4096)
+    for _ in range(args.steps):
+        flush.zero_()
+        ours(T)
+    torch.cuda.synchronize()
+    trace = _lib.trace_end(4096)
+    assert _lib.device_status() == 0
+    k_ms = [t for kind, t in trace if kind == "sample"]
+    k_avg = sum(k_ms) / len(k_ms)
+    by_kind = {}
+    for kind, t in trace:
+        by_kind.setdefault(kind, [0.0, 0])
+        by_kind[kind][0] += t
+        by_kind[kind][1] += 1
+    tot = sum(v[0] for v in by_kind.values())
+    kernels = {k: {"launches": n, "total_ms": t, "share": t / tot} for k, (t, n) in by_kind.items()}
+
+    hbm_peak, hbm_src = load_hbm_peak()
+    peak_burst, _, peak_src = load_peaks()
+    bytes_alg = 2.0 * V * H + 2.0 * N * H + 12.0 * N
+    flops = 2.0 * N * H * V
+    if bytes_alg / (hbm_peak * 1e9) >= flops / (peak_burst * 1e12):
+        ach = bytes_alg / (k_avg / 1e3) / 1e9
+        roofline = {"bound": "hbm", "kernel": "sample", "achieved": ach, "peak": hbm_peak, "unit": "GB/s",
+                    "frac": ach / hbm_peak, "traffic": load_traffic("sample", args.config),
+                    "peak_kind": f"{hbm_src} copy bandwidth", "algorithmic_bytes_per_launch": bytes_alg}
+    else:
+        ach = flops / (k_avg / 1e3) / 1e12
+        roofline = {"bound": "tensor", "kernel": "sample", "achieved": ach, "peak": peak_burst, "unit": "TFLOP/s",
+                    "frac": ach / peak_burst, "traffic": load_traffic("sample", args.config),
+                    "peak_kind": f"{peak_src} burst bf16", "algorithmic_flops_per_launch": flops}
+
+    # end to end: h from pinned host memory, tokens back to the host every step
+    h_pin = h_host.pin_memory()
+    tok_host = torch.empty(N, dtype=torch.int64).pin_memory()
+
+    def e2e_step():
+        hd = h_pin.to(dev, non_blocking=True)
+        tok, _, _ = sampling.lm_head_sample(hd, W, T, next(seeds), workspace=ws)
+        tok_host.copy_(tok, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for _ in range(3):
+        e2e_step()
+    e_ms = _timed(e2e_step, args.steps, flush)
+
+    cpu = None
+    if not args.no_cpu_baseline:
+        sample = min(N, 8)
+        hs = h_host[:sample].float().numpy()
+        Wn = W.float().cpu().numpy()
+        times = []
+        t_end = time.perf_counter() + min(args.cpu_seconds, 10.0)
+        while True:
+            t0 = time.perf_counter()
+            O.lm_head_sample_np(hs, Wn, T, seed=1)
+            times.append(time.perf_counter() - t0)
+            if time.perf_counter() > t_end and len(times) >= 2:
+                break
+        cpu = {"value": sample / statistics.median(times), "unit": "rows/s", "cores": 1, "kind": "port",
+               "sample": f"{sample} rows x V={V}: float64 numpy lm_head + Gumbel-max keys (the oracle)"}
+
+    total = sum(ms)
+    emit({
+        "metric": SAMPLE_METRIC, "value": N * args.steps / (total / 1e3), "unit": "rows/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) hidden, "
+        "N(0,0.05) lm_head)",
+        "config": {"workload": f"{args.config}: {desc}", "rows": N, "hidden": H, "vocab": V, "temperature": T,
+                   "parallelism": "single GPU", "l2": "flushed between steps (256 MiB write)"},
+        "greedy_ms_per_step": sum(ms_greedy) / args.steps,
+        "torch_cublas_ms_per_step": {"sampled": sum(ms_torch) / args.steps,
+                                     "greedy": sum(ms_torch_greedy) / args.steps,
+                                     "what": "F.linear (cuBLAS, bf16) + the reference's sample_token ops, same GPU"},
+        "roofline": roofline, "kernels": kernels, "gpu_launches": int(launches),
+        "e2e": {"value": N * args.steps / (sum(e_ms) / 1e3), "unit": "rows/s", "h2d_bytes_per_step": 2 * N * H,
+                "d2h_bytes_per_step": 8 * N, "ms_per_step": sum(e_ms) / args.steps,
+                "api": "sampling.lm_head_sample"},
+        "cpu_baseline": cpu, "clocks": clocks,
+    })
+
+
 # ----------------------------------------------------------------------------- our arm
 def main():
     args = parse()
     _claim_stdout()
+    if args.config in SAMPLE_CONFIGS:
+        run_sample(args)
+        return
     if args.impl == "reference":
         run_reference_arm(args)
         return

@@ -168,6 +168,20 @@ int klg_fwd_bwd(const void* h_s, const void* h_t, const void* w, const uint8_t* 
                 float* lse, float* row_kl, float* d_h_s, float* d_w, void* workspace, int64_t workspace_bytes,
                 void* stream);
 
+/* ---------------------------------------------------------------- inference lm_head
+ * The reference's sample_token (generate.py:40-78) on the lm_head output, without the
+ * [N, V] logits (generate.py:161-188 computes the full logits first).  For each row of
+ * h [N, H] (bf16): sample = 0 -> the argmax of z = h W^T (lowest index among equal
+ * maxima, as torch.argmax); sample = 1 -> a draw from softmax(z * inv_temp) by the
+ * Gumbel-max rule with a counter-based generator (seed, row, column) -- distributed like
+ * torch.multinomial over the same probabilities, not the same stream.  Outputs: tokens
+ * [N] int32, logit [N] = z of the chosen token, lse [N] = log sum exp(z * inv_temp), so
+ * p(token) = exp(logit * inv_temp - lse).  top-k / top-p filtering is not fused. */
+int64_t klg_lm_head_sample_workspace_bytes(int64_t n_rows, int64_t vocab);
+int klg_lm_head_sample(const void* h, const void* w, int64_t n_rows, int64_t hidden, int64_t vocab, float inv_temp,
+                       int sample, uint64_t seed, int32_t* tokens, float* logit, float* lse, void* workspace,
+                       int64_t workspace_bytes, void* stream);
+
 /* fp32 -> bf16 conversion (round to nearest even) for fp32 callers. */
 int klg_cast_f32_bf16(const float* in, void* out, int64_t n, void* stream);
 
@@ -185,6 +199,7 @@ int klg_cast_f32_bf16(const float* in, void* out, int64_t n, void* stream);
 #define KLG_KIND_COUNT 6
 #define KLG_KIND_CAST 7
 #define KLG_KIND_ZERO 8      /* pass 2: zeroing of the fp32 dW / dH buffers            */
+#define KLG_KIND_SAMPLE 9    /* inference: lm_head logits -> argmax / Gumbel-max sample   */
 int klg_trace_begin(int capacity);
 int klg_trace_end(int* kinds, float* ms, int capacity, int* n);
 

@@ -421,3 +421,112 @@ def grad_metrics(ours, ref) -> Tuple[float, float]:
 
 
 LN2 = math.log(2.0)
+
+
+# --------------------------------------------------------------------------
+# Inference lm_head sampling (reference generate.py:40-78, infer.py:60-69)
+# --------------------------------------------------------------------------
+
+GREEDY_TEMPERATURE = 1e-5   # generate.py:52: below this, argmax and no probabilities
+
+
+def sample_token_np(logits, temperature: float = 0.0):
+    """Restates ``sample_token`` (generate.py:40-78) without top-k / top-p.
+
+    ``temperature < 1e-5``: ``(argmax(logits, -1), None)`` -- the first index among
+    equal maxima, as ``torch.argmax``.  Otherwise ``probs = softmax(logits / T)``
+    (generate.py:75) and the token is a draw from ``probs`` (generate.py:77, by
+    ``torch.multinomial`` there); this restatement returns ``(None, probs)`` since the
+    draw itself is defined only by its distribution.
+    """
+    z = np.asarray(logits, dtype=np.float64)
+    if temperature < GREEDY_TEMPERATURE:
+        return np.argmax(z, axis=-1), None
+    s = z / temperature
+    s = s - s.max(axis=-1, keepdims=True)
+    e = np.exp(s)
+    return None, e / e.sum(axis=-1, keepdims=True)
+
+
+def sample_hash_np(seed: int, rows, cols) -> np.ndarray:
+    """The 32-bit counter hash of (seed, row, column) the fused sampler draws from.
+
+    The row, column and both seed halves are combined with odd multipliers
+    (0x9E3779B1, 0x85EBCA77, 0xC2B2AE3D), then mixed by the "lowbias32" finaliser
+    (xorshift 16, x 0x7FEB352D, xorshift 15, x 0x846CA68B, xorshift 16).
+    """
+    M = np.uint64(0xFFFFFFFF)
+    r = np.asarray(rows, dtype=np.uint64)[..., None] if np.ndim(rows) else np.uint64(rows)
+    c = np.asarray(cols, dtype=np.uint64)
+    lo, hi = np.uint64(seed & 0xFFFFFFFF), np.uint64((seed >> 32) & 0xFFFFFFFF)
+    x = lo ^ ((r * np.uint64(0x9E3779B1)) & M) ^ ((c * np.uint64(0x85EBCA77)) & M) ^ ((hi * np.uint64(0xC2B2AE3D)) & M)
+    x = x ^ (x >> np.uint64(16))
+    x = (x * np.uint64(0x7FEB352D)) & M
+    x = x ^ (x >> np.uint64(15))
+    x = (x * np.uint64(0x846CA68B)) & M
+    x = x ^ (x >> np.uint64(16))
+    return x.astype(np.uint32)
+
+
+def exp_variate_log2_np(x) -> np.ndarray:
+    """Exponential variate in log2 units from a hash: ``V = (2 (x >> 9) + 1) 2^-24``,
+    ``E = -log2(1 - V)`` (exact in float64 via log1p)."""
+    v = (2.0 * (np.asarray(x, dtype=np.uint32) >> np.uint32(9)).astype(np.float64) + 1.0) * 2.0 ** -24
+    return -np.log1p(-v) / math.log(2.0)
+
+
+def sample_keys_np(z, temperature: float, seed: int) -> np.ndarray:
+    """Per-column keys whose row argmax is the fused sampler's token.
+
+    Greedy: the logits.  Sampling: ``u - log2(E)`` with ``u = z log2(e) / T`` and
+    ``E`` the exponential variate of (seed, row, column) -- the Gumbel-max rule, whose
+    argmax is distributed as ``softmax(z / T)`` (the distribution generate.py:75-77
+    draws from).
+    """
+    z = np.asarray(z, dtype=np.float64)
+    if temperature < GREEDY_TEMPERATURE:
+        return z
+    n, v = z.shape
+    x = sample_hash_np(seed, np.arange(n), np.arange(v))
+    return z * (math.log2(math.e) / temperature) - np.log2(exp_variate_log2_np(x))
+
+
+def lm_head_sample_np(h, W, temperature: float = 0.0, seed: int = 0):
+    """``sample_token(h @ W^T, temperature)`` as the fused op defines it, in float64.
+
+    Returns ``(tokens, logit, lse, keys)``: the chosen column per row (first index
+    among equal keys), its logit, ``log sum exp(z / T')`` with ``T' = T`` when sampling
+    and ``1`` when greedy, and the key matrix (for tolerance checks on near-ties).
+    """
+    z = np.asarray(h, dtype=np.float64) @ np.asarray(W, dtype=np.float64).T
+    keys = sample_keys_np(z, temperature, seed)
+    tokens = np.argmax(keys, axis=-1)
+    inv = 1.0 if temperature < GREEDY_TEMPERATURE else 1.0 / temperature
+    lse = _lse(z * inv)
+    return tokens, z[np.arange(z.shape[0]), tokens], lse, keys
+
+
+def sample_token_torch(logits, temperature: float = 0.0, top_k: int = 0, top_p: float = 1.0):
+    """The reference's ``sample_token`` op sequence (generate.py:40-78) in torch, any device.
+
+    Used as the comparison arm of the sampling benchmark (cuBLAS logits, then these
+    ops) and nowhere in the product.
+    """
+    torch = _torch()
+    F = torch.nn.functional
+    if temperature < GREEDY_TEMPERATURE:
+        return logits.argmax(dim=-1), None
+    scaled = logits / temperature
+    if top_k > 0:
+        v, _ = torch.topk(scaled, min(top_k, scaled.size(-1)), dim=-1)
+        scaled[scaled < v[..., [-1]]] = -float("inf")
+    if top_p < 1.0:
+        sorted_logits, sorted_idx = torch.sort(scaled, descending=True, dim=-1)
+        cum = torch.cumsum(F.softmax(sorted_logits, dim=-1), dim=-1)
+        remove = cum > top_p
+        remove[..., 1:] = remove[..., :-1].clone()
+        remove[..., 0] = 0
+        scaled[remove.scatter(-1, sorted_idx, remove)] = -float("inf")
+    probs = F.softmax(scaled, dim=-1)
+    tokens = torch.multinomial(probs.view(-1, probs.size(-1)), 1).view(probs.shape[:-1])
+    return tokens, probs

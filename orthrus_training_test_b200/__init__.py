@@ -5,6 +5,7 @@ Public API
   kl_gemm_loss      the fused loss on aligned rows (``KLGemmFn.apply``)
   KLGemmFn          the ``torch.autograd.Function``
   parallel          row-sharded and vocab-sharded multi-GPU variants
+  sampling          fused lm_head + greedy / sampled token selection for inference
 """
 from .ops import KLGemmFn, kl_gemm_loss, kl_forward, kl_backward  # noqa: F401
 from .loss import compute_kl_loss, select_rows  # noqa: F401

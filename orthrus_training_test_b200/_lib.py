@@ -6,7 +6,7 @@ loaded, :func:`lib` raises.  There is no CPU or pure-PyTorch path.
 from __future__ import annotations
 
 import ctypes
-from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_longlong, c_uint8, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_longlong, c_uint8, c_ulonglong, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libklgemm.so"
@@ -28,6 +28,9 @@ SIGNATURES = {
     "klg_device_status": (c_int, [POINTER(c_int), c_int]),
     "klg_launch_count": (c_longlong, []),
     "klg_selftest_wait_timeout": (c_int, [c_void_p]),
+    "klg_lm_head_sample_workspace_bytes": (c_longlong, [c_longlong, c_longlong]),
+    "klg_lm_head_sample": (c_int, [c_void_p, c_void_p, c_longlong, c_longlong, c_longlong, c_float, c_int, c_ulonglong,
+                                   c_void_p, c_void_p, c_void_p, c_void_p, c_longlong, c_void_p]),
     "klg_num_partials": (c_int, [c_int64, c_int64, POINTER(c_int)]),
     "klg_fwd_stats": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_float, c_void_p, c_int,
                               c_void_p]),
@@ -53,7 +56,7 @@ SIGNATURES = {
     "klg_trace_end": (c_int, [POINTER(c_int), POINTER(c_float), c_int, POINTER(c_int)]),
 }
 
-KIND_NAMES = {1: "stats", 2: "dz", 3: "gemm", 4: "merge", 5: "finalize", 6: "count", 7: "cast", 8: "zero"}
+KIND_NAMES = {1: "stats", 2: "dz", 3: "gemm", 4: "merge", 5: "finalize", 6: "count", 7: "cast", 8: "zero", 9: "sample"}
 
 _lib = None
 

@@ -142,8 +142,8 @@ inline int cdiv(long long a, long long b) { return (int)((a + b - 1) / b); }
 // into units of vpu vocab tiles.  Picks vpu (>= 4 where possible) so the unit
 // count fills the SMs in whole waves as closely as possible, preferring the
 // largest vpu among near-ties.
-void plan_dual(int n_rt, int n_vt, int n_sm, int& vpu, int& n_uv, int max_uv = 64) {
-  const int vmin = n_vt < 4 ? n_vt : 4;
+void plan_dual(int n_rt, int n_vt, int n_sm, int& vpu, int& n_uv, int max_uv = 64, int min_vpu = 4) {
+  const int vmin = n_vt < min_vpu ? n_vt : min_vpu;
   double best = -1.0;
   vpu = n_vt;
   for (int v = n_vt; v >= vmin; --v) {
@@ -212,17 +212,18 @@ cudaError_t launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, int smem, cudaS
   return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
 }
 
+template <int EPI>
 int launch_lse_pair(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMap& mw, const klg::LseArgs& a,
                     cudaStream_t s) {
   const bool res = a.n_kb <= klg::LSE_RES_MAX_KB;
-  auto k = res ? klg::lse_pair_kernel<true> : klg::lse_pair_kernel<false>;
+  auto k = res ? klg::lse_pair_kernel<true, EPI> : klg::lse_pair_kernel<false, EPI>;
   const int smem = res ? klg::LSE_RES_SMEM : klg::LSE_SMEM;
   cudaError_t e = set_smem(k, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(lse_pair_kernel)");
   const int pairs = a.n_units < num_sms() / 2 ? a.n_units : num_sms() / 2;
   const int slot = trace_pre(s);
   e = launch_k(k, dim3(2 * pairs), dim3(klg::LSE_THREADS), smem, s, 2, mhs, mht, mw, a);
-  trace_post(slot, s, KLG_KIND_STATS);
+  trace_post(slot, s, EPI == klg::EPI_LSE ? KLG_KIND_STATS : KLG_KIND_SAMPLE);
   if (e != cudaSuccess) return cuda_fail(e, "launch lse_pair_kernel");
   ++g_launches;
   return KLG_OK;
@@ -791,8 +792,9 @@ int klg_fwd_bwd(const void* hs, const void* ht, const void* w, const uint8_t* ma
   la.n_kb = cdiv(hidden, klg::BK);
   la.scale_log2 = inv_temp * 1.4426950408889634f;
   la.parts = lse_parts;
+  la.n_views = 2;
   if (klg::LSE_CSPLIT * la.n_uv != L.n_lp) return fail(KLG_ERR_ARG, "internal plan mismatch");
-  if ((rc = launch_lse_pair(mhs, mht, mw, la, s))) return rc;
+  if ((rc = launch_lse_pair<klg::EPI_LSE>(mhs, mht, mw, la, s))) return rc;
   {
     const int n2 = (int)(2 * n_rows);
     const int slot = trace_pre(s);
@@ -825,6 +827,61 @@ int klg_fwd_bwd(const void* hs, const void* ht, const void* w, const uint8_t* ma
     if (e != cudaSuccess) return cuda_fail(e, "launch loss_from_sums_kernel");
     ++g_launches;
   }
+  return KLG_OK;
+}
+
+// ---------------------------------------------------------------- lm_head sampling (inference)
+namespace {
+int sample_plan(int64_t n_rows, int64_t vocab, klg::LseArgs& la) {
+  la.n_rows = (int)n_rows;
+  la.vocab = (int)vocab;
+  la.n_rp = cdiv(n_rows, 256);
+  la.n_vt = cdiv(vocab, klg::LSE_BN);
+  la.n_views = 1;
+  // few row tiles (decode) spread the vocab over more CTA pairs: units of >= 2 tiles
+  plan_dual(la.n_rp, la.n_vt, num_sms() / 2, la.vt_per_unit, la.n_uv, 64, 2);
+  la.n_units = la.n_rp * la.n_uv;
+  return klg::LSE_CSPLIT * la.n_uv;
+}
+}  // namespace
+
+int64_t klg_lm_head_sample_workspace_bytes(int64_t n_rows, int64_t vocab) {
+  if (n_rows < 1 || vocab < 1 || n_rows > (1ll << 30) || vocab > (1ll << 30)) return -1;
+  klg::LseArgs la{};
+  return (int64_t)sample_plan(n_rows, vocab, la) * 5 * n_rows * 4;
+}
+
+int klg_lm_head_sample(const void* h, const void* w, int64_t n_rows, int64_t hidden, int64_t vocab, float inv_temp,
+                       int sample, uint64_t seed, int32_t* tokens, float* logit, float* lse, void* workspace,
+                       int64_t workspace_bytes, void* stream) {
+  int rc = check_problem(h, h, w, n_rows, hidden, vocab, inv_temp);
+  if (rc) return rc;
+  if (!tokens || !logit || !lse) return fail(KLG_ERR_ARG, "null output pointer");
+  klg::LseArgs la{};
+  const int n_part = sample_plan(n_rows, vocab, la);
+  const int64_t need = (int64_t)n_part * 5 * n_rows * 4;
+  if (!workspace || workspace_bytes < need || !aligned16(workspace))
+    return fail(KLG_ERR_WORKSPACE, "sampling workspace needs %lld bytes (16-byte aligned)", (long long)need);
+  if ((rc = bind_device(h))) return rc;
+  NvtxRange nvtx_range("klg_lm_head_sample");
+  cudaStream_t s = (cudaStream_t)stream;
+  la.n_kb = cdiv(hidden, klg::BK);
+  la.scale_log2 = inv_temp * 1.4426950408889634f;
+  la.parts = static_cast<float*>(workspace);
+  la.sample = sample ? 1 : 0;
+  la.seed_lo = (uint32_t)seed;
+  la.seed_hi = (uint32_t)(seed >> 32);
+  alignas(64) CUtensorMap mh, mw;
+  if (!make_map(&mh, h, hidden, n_rows, hidden, klg::BK, klg::BM) ||
+      !make_map(&mw, w, hidden, vocab, hidden, klg::BK, klg::LSE_BN / 2))
+    return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+  if ((rc = launch_lse_pair<klg::EPI_SAMPLE>(mh, mh, mw, la, s))) return rc;
+  const int slot = trace_pre(s);
+  cudaError_t e = launch_k(klg::sample_merge_kernel, dim3(cdiv(n_rows, 256)), dim3(256), 0, s, 1,
+                           static_cast<const float*>(workspace), n_part, (int)n_rows, tokens, logit, lse);
+  trace_post(slot, s, KLG_KIND_MERGE);
+  if (e != cudaSuccess) return cuda_fail(e, "launch sample_merge_kernel");
+  ++g_launches;
   return KLG_OK;
 }
 

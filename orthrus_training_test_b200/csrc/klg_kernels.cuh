@@ -202,11 +202,29 @@ struct LseArgs {
   int n_units;      // 2 * n_rp * n_uv
   int n_kb;         // ceil(H / 64)
   float scale_log2; // log2(e) / T
-  float* parts;     // [n_uv * LSE_CSPLIT][2][2N]
+  float* parts;     // EPI_LSE: [n_uv * LSE_CSPLIT][2][n_views * N]; EPI_SAMPLE: [n_uv * LSE_CSPLIT][5][N]
+  int n_views;      // 2: student rows then teacher rows (training pass 1); 1: one matrix (EPI_SAMPLE)
+  int sample;       // EPI_SAMPLE: 0 greedy argmax of z, 1 Gumbel-max sample of softmax(z / T)
+  uint32_t seed_lo, seed_hi;
 };
 
+enum { EPI_LSE = 0, EPI_SAMPLE = 1 };
+
+// Counter-based 32-bit hash of (seed, row, column): the three keys combined with odd
+// multipliers, then the "lowbias32" avalanche finaliser (public domain).  The oracle
+// restates it bit for bit.
+__host__ __device__ __forceinline__ uint32_t sample_hash(uint32_t seed_lo, uint32_t seed_hi, uint32_t row, uint32_t col) {
+  uint32_t x = seed_lo ^ (row * 0x9E3779B1u) ^ (col * 0x85EBCA77u) ^ (seed_hi * 0xC2B2AE3Du);
+  x ^= x >> 16;
+  x *= 0x7FEB352Du;
+  x ^= x >> 15;
+  x *= 0x846CA68Bu;
+  x ^= x >> 16;
+  return x;
+}
+
 __device__ __forceinline__ void lse_unit(const LseArgs& a, int u, int& view, int& rp, int& uv, int& vt0, int& vt1) {
-  const int per_uv = 2 * a.n_rp;
+  const int per_uv = a.n_views * a.n_rp;
   uv = u / per_uv;
   const int r = u % per_uv;
   view = r / a.n_rp;
@@ -234,7 +252,48 @@ __device__ __forceinline__ void lse_chunk(const uint32_t (&b)[32], int nvalid, f
   S = fmaf(S, r, (s0 + s1) + (s2 + s3));
 }
 
-template <bool RES>
+// Exponential variate in log2 units, E = -log2(1 - V), from the hash's top 23 bits:
+// V = (2k + 1) 2^-24 in [2^-24, 1 - 2^-24], exact in fp32 (the float 1.k minus 1 - 2^-24).
+// Small V (the large-key tail of the Gumbel variate) takes the series of -ln(1 - V), whose
+// truncation error is below 2^-32 relative for V < 1/32; elsewhere 1 - V >= 31/32 and
+// lg2.approx carries ~2^-22 absolute error on a result >= 0.045.
+__device__ __forceinline__ float uniform_open(uint32_t x) {
+  return __uint_as_float(0x3F800000u | (x >> 9)) - 0.99999994039535522461f;
+}
+
+__device__ __forceinline__ float exp_variate_log2(uint32_t x) {
+  const float v = uniform_open(x);
+  const float ser = v * fmaf(v, fmaf(v, fmaf(v, fmaf(v, fmaf(v, 1.f / 6.f, 0.2f), 0.25f), 1.f / 3.f), 0.5f), 1.f) *
+                    1.44269504088896341f;
+  return v < 0.03125f ? ser : -__log2f(1.f - v);
+}
+
+// Online best key over one 32-column chunk (columns col0..col0+31 of this thread's row):
+// greedy keys are the raw logits; sampling keys are u - log2(E), u = z log2(e) / T and E an
+// exponential variate in log2 units -- the Gumbel-max rule (argmax of u + Gumbel noise
+// draws from softmax(z / T)) with the constant log2(ln 2) dropped.  Strict '>' keeps the
+// lowest column among equal keys.
+__device__ __forceinline__ void best_chunk(const uint32_t (&b)[32], int nvalid, int col0, int row, const LseArgs& a,
+                                           float& bk, int& bi, float& bz) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (j < nvalid) {
+      const float z = __uint_as_float(b[j]);
+      float key = z;
+      if (a.sample) {
+        const uint32_t x = sample_hash(a.seed_lo, a.seed_hi, (uint32_t)row, (uint32_t)(col0 + j));
+        key = fmaf(z, a.scale_log2, -__log2f(exp_variate_log2(x)));
+      }
+      if (key > bk) {
+        bk = key;
+        bi = col0 + j;
+        bz = z;
+      }
+    }
+  }
+}
+
+template <bool RES, int EPI>
 __global__ void __launch_bounds__(LSE_THREADS, 1)
 lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ CUtensorMap map_ht,
                 const __grid_constant__ CUtensorMap map_w, const LseArgs a) {
@@ -405,7 +464,10 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
       int view, rp, uv, vt0, vt1;
       lse_unit(a, u, view, rp, uv, vt0, vt1);
       const int row = rp * 256 + (int)rank * 128 + q * 32 + lane;
+      const bool live = rp * 256 + (int)rank * 128 + q * 32 < a.n_rows;   // warp-uniform
       float m = NEG_BIG, S = 0.f;
+      float bk = -INFINITY, bz = 0.f;   // EPI_SAMPLE: best key, its logit
+      int bi = -1;
       for (int vt = vt0; ok && vt < vt1; ++vt, ++tcount) {
         const int buf = tcount & 1;
         const uint32_t tph = (tcount >> 1) & 1;
@@ -413,12 +475,15 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
         tc_fence_after();
         const int col_base = vt * LSE_BN + h * LSE_COLS_PER_WARP;
 #pragma unroll 1
-        for (int c = 0; c < LSE_COLS_PER_WARP / 32; ++c) {
+        for (int c = 0; live && c < LSE_COLS_PER_WARP / 32; ++c) {
           uint32_t b0[32];
           tmem_ld32_raw(lane_addr + buf * LSE_BN + c * 32, b0);
           tmem_wait_ld_regs(b0);
           const int nvalid = min(32, a.vocab - (col_base + c * 32));
-          if (nvalid > 0) lse_chunk(b0, nvalid, a.scale_log2, m, S);
+          if (nvalid > 0) {
+            lse_chunk(b0, nvalid, a.scale_log2, m, S);
+            if (EPI == EPI_SAMPLE) best_chunk(b0, nvalid, col_base + c * 32, row, a, bk, bi, bz);
+          }
         }
         tc_fence_before();
         __syncwarp();
@@ -428,10 +493,20 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
         }
       }
       if (ok && row < a.n_rows) {
-        const size_t n2 = 2 * (size_t)a.n_rows;
-        float* p = a.parts + ((size_t)(uv * LSE_CSPLIT + h) * 2) * n2 + (size_t)view * a.n_rows + row;
-        p[0] = m;
-        p[n2] = S;
+        if (EPI == EPI_LSE) {
+          const size_t n2 = (size_t)a.n_views * a.n_rows;
+          float* p = a.parts + ((size_t)(uv * LSE_CSPLIT + h) * 2) * n2 + (size_t)view * a.n_rows + row;
+          p[0] = m;
+          p[n2] = S;
+        } else {
+          const size_t n = (size_t)a.n_rows;
+          float* p = a.parts + (size_t)(uv * LSE_CSPLIT + h) * 5 * n + row;
+          p[0] = m;
+          p[n] = S;
+          p[2 * n] = bk;
+          p[3 * n] = __int_as_float(bi);
+          p[4 * n] = bz;
+        }
       }
     }
   }
@@ -1121,6 +1196,35 @@ __global__ void lse_merge_kernel(const float* __restrict__ parts, int n_part, in
   float S = 0.f;
   for (int p = 0; p < n_part; ++p) S = fmaf(parts[(size_t)p * 2 * st + st + i], ex2(parts[(size_t)p * 2 * st + i] - M), S);
   lse[i] = M + __log2f(S);
+}
+
+// lm_head sampling: merge the per-unit records (m, S, key, index, z) of each row into the
+// chosen token (highest key, lowest index among equals), its logit and the natural-log
+// log-sum-exp of z / T (so p(token) = exp(z_token / T - lse)).
+__global__ void sample_merge_kernel(const float* __restrict__ parts, int n_part, int n, int* __restrict__ tokens,
+                                    float* __restrict__ logit, float* __restrict__ lse) {
+  pdl_enter();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const size_t st = (size_t)n;
+  float M = NEG_BIG, bk = -INFINITY, bz = 0.f;
+  int bi = -1;
+  for (int p = 0; p < n_part; ++p) {
+    const float* r = parts + (size_t)p * 5 * st + i;
+    M = fmaxf(M, r[0]);
+    const float k = r[2 * st];
+    const int idx = __float_as_int(r[3 * st]);
+    if (idx >= 0 && (k > bk || (k == bk && idx < bi))) {
+      bk = k;
+      bi = idx;
+      bz = r[4 * st];
+    }
+  }
+  float S = 0.f;
+  for (int p = 0; p < n_part; ++p) S = fmaf(parts[(size_t)p * 5 * st + st + i], ex2(parts[(size_t)p * 5 * st + i] - M), S);
+  tokens[i] = bi;
+  logit[i] = bz;
+  lse[i] = (M + __log2f(S)) * 0.69314718055994530942f;
 }
 
 // Training-path per-row KL: KL_i = ln2 * (sum_p a_parts[p][i] + L_s,i - L_t,i) for rows

@@ -1,0 +1,92 @@
+"""Fused lm_head + token selection for inference.
+
+The reference picks tokens with ``sample_token(logits, temperature, top_k, top_p)``
+(generate.py:40-78, and the temperature-only copy at infer.py:60-69) on logits the
+model has already written out as ``[..., V]`` (generate.py:161-188).  Here the
+lm_head GEMM and the selection run in one CUDA kernel over vocab tiles: greedy
+argmax, or a draw from ``softmax(z / T)`` by the Gumbel-max rule with a counter-based
+generator keyed by (seed, row, column), plus the per-row log-sum-exp -- no ``[N, V]``
+tensor is ever stored.
+
+Every function here calls the CUDA library; there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib  # noqa: F401  (loads the library)
+from ._lib import call
+from .ops import _ptr, _require_cuda, _stream, to_compute_dtype
+
+GREEDY_TEMPERATURE = 1e-5   # generate.py:52
+
+
+def workspace_bytes(n_rows: int, vocab: int) -> int:
+    n = _lib.lib().klg_lm_head_sample_workspace_bytes(int(n_rows), int(vocab))
+    if n < 0:
+        raise ValueError(f"unsupported sampling problem n_rows={n_rows} vocab={vocab}")
+    return int(n)
+
+
+def lm_head_sample(h: torch.Tensor, weight: torch.Tensor, temperature: float = 0.0, seed: int = 0,
+                   workspace: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Select one token per row of ``z = h @ weight^T`` without storing ``z``.
+
+    ``h`` ``[N, H]`` and ``weight`` ``[V, H]`` (bf16; fp32 is cast).  ``temperature <
+    1e-5`` (the reference's greedy threshold, generate.py:52) selects ``argmax z`` --
+    the first index among equal maxima, as ``torch.argmax``; otherwise a draw from
+    ``softmax(z / temperature)`` fixed by ``seed`` (the same seed, rows and logits give
+    the same tokens on any device and any vocab split).
+
+    Returns ``(tokens int64 [N], logit float32 [N], lse float32 [N])``: the chosen
+    column, its logit ``z``, and ``log sum exp(z / T')`` with ``T' = temperature`` when
+    sampling and ``1`` when greedy, so ``p(token) = exp(logit / T' - lse)``.
+    """
+    if h.dim() != 2 or weight.dim() != 2 or h.shape[1] != weight.shape[1]:
+        raise ValueError(f"expected h [N, H] and weight [V, H], got {tuple(h.shape)} and {tuple(weight.shape)}")
+    dev = _require_cuda(h, weight)
+    h = to_compute_dtype(h)
+    weight = to_compute_dtype(weight)
+    N, H = h.shape
+    V = weight.shape[0]
+    sample = temperature >= GREEDY_TEMPERATURE
+    inv_temp = 1.0 / float(temperature) if sample else 1.0
+    need = workspace_bytes(N, V)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+    tokens = torch.empty(N, dtype=torch.int32, device=dev)
+    logit = torch.empty(N, dtype=torch.float32, device=dev)
+    lse = torch.empty(N, dtype=torch.float32, device=dev)
+    call("klg_lm_head_sample", _ptr(h), _ptr(weight), N, H, V, inv_temp, int(sample),
+         ctypes.c_ulonglong(int(seed) & 0xFFFFFFFFFFFFFFFF), _ptr(tokens), _ptr(logit), _ptr(lse), _ptr(workspace),
+         workspace.numel() * workspace.element_size(), _stream(dev))
+    return tokens.long(), logit, lse
+
+
+def sample_token(hidden: torch.Tensor, weight: torch.Tensor, temperature: float = 0.0, top_k: int = 0,
+                 top_p: float = 1.0, seed: Optional[int] = None) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """``sample_token`` (generate.py:40-78) applied to ``hidden @ weight^T``.
+
+    ``hidden`` is ``[H]``, ``[L, H]`` or ``[B, L, H]`` (the logits' shape minus the vocab
+    dimension becomes the token shape, as in the reference).  Returns ``(tokens,
+    None)`` when greedy and ``(tokens, p_token)`` otherwise, where ``p_token`` is the
+    probability of each chosen token -- the reference returns the whole ``[..., V]``
+    probability tensor, which the fused op never forms.  ``seed=None`` draws a seed
+    from torch's default generator, so successive calls differ as
+    ``torch.multinomial``'s draws do.  top-k / top-p filtering (generate.py:58-72) is
+    not fused and raises.
+    """
+    if top_k > 0 or top_p < 1.0:
+        raise NotImplementedError("top-k / top-p filtering is not fused; select from materialised logits instead")
+    lead = hidden.shape[:-1]
+    h2 = hidden.reshape(-1, hidden.shape[-1])
+    if seed is None:
+        seed = int(torch.randint(0, 2 ** 62, (1,)).item())
+    tokens, logit, lse = lm_head_sample(h2, weight, temperature, seed)
+    tokens = tokens.view(lead)
+    if temperature < GREEDY_TEMPERATURE:
+        return tokens, None
+    return tokens, torch.exp(logit / float(temperature) - lse).view(lead)
