@@ -215,7 +215,10 @@ cudaError_t launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, int smem, cudaS
 template <int EPI>
 int launch_lse_pair(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMap& mw, const klg::LseArgs& a,
                     cudaStream_t s) {
-  const bool res = a.n_kb <= klg::LSE_RES_MAX_KB;
+  // A resident across the unit's tiles when it fits -- except for replicated rows (a handful
+  // of rows, W streamed once from HBM), where the streamed-A ring's six W stages in flight
+  // measured 2-4 us faster than the resident ring's four (32-128 rows, H=576, V=49153)
+  const bool res = a.n_kb <= klg::LSE_RES_MAX_KB && a.rep == 1;
   auto k = res ? klg::lse_pair_kernel<true, EPI> : klg::lse_pair_kernel<false, EPI>;
   const int smem = res ? klg::LSE_RES_SMEM : klg::LSE_SMEM;
   cudaError_t e = set_smem(k, smem);
@@ -793,6 +796,7 @@ int klg_fwd_bwd(const void* hs, const void* ht, const void* w, const uint8_t* ma
   la.scale_log2 = inv_temp * 1.4426950408889634f;
   la.parts = lse_parts;
   la.n_views = 2;
+  la.rep = 1;
   if (klg::LSE_CSPLIT * la.n_uv != L.n_lp) return fail(KLG_ERR_ARG, "internal plan mismatch");
   if ((rc = launch_lse_pair<klg::EPI_LSE>(mhs, mht, mw, la, s))) return rc;
   {
@@ -838,17 +842,31 @@ int sample_plan(int64_t n_rows, int64_t vocab, klg::LseArgs& la) {
   la.n_rp = cdiv(n_rows, 256);
   la.n_vt = cdiv(vocab, klg::LSE_BN);
   la.n_views = 1;
+  la.rep = n_rows <= 64 ? 4 : n_rows <= 128 ? 2 : 1;
   // few row tiles (decode) spread the vocab over more CTA pairs: units of >= 2 tiles
-  plan_dual(la.n_rp, la.n_vt, num_sms() / 2, la.vt_per_unit, la.n_uv, 64, 2);
+  plan_dual(la.n_rp, la.n_vt, num_sms() / 2, la.vt_per_unit, la.n_uv, num_sms() / 2, 2);
   la.n_units = la.n_rp * la.n_uv;
-  return klg::LSE_CSPLIT * la.n_uv;
+  return klg::LSE_CSPLIT * la.rep * la.n_uv;
+}
+
+// Record groups of the first merge launch: one when the rows alone give the GPU enough
+// blocks, else groups of ~32 records (two per warp) merged again by a second launch.
+int sample_merge_groups(int64_t n_rows, int n_part) {
+  if (cdiv(n_rows, 32) >= num_sms() || n_part <= 64) return 1;
+  const int g = cdiv(n_part, 32);
+  return g < 64 ? g : 64;
+}
+
+int64_t sample_workspace(int64_t n_rows, int n_part) {
+  const int g = sample_merge_groups(n_rows, n_part);
+  return ((int64_t)n_part + (g > 1 ? g : 0)) * 5 * n_rows * 4;
 }
 }  // namespace
 
 int64_t klg_lm_head_sample_workspace_bytes(int64_t n_rows, int64_t vocab) {
   if (n_rows < 1 || vocab < 1 || n_rows > (1ll << 30) || vocab > (1ll << 30)) return -1;
   klg::LseArgs la{};
-  return (int64_t)sample_plan(n_rows, vocab, la) * 5 * n_rows * 4;
+  return sample_workspace(n_rows, sample_plan(n_rows, vocab, la));
 }
 
 int klg_lm_head_sample(const void* h, const void* w, int64_t n_rows, int64_t hidden, int64_t vocab, float inv_temp,
@@ -859,7 +877,7 @@ int klg_lm_head_sample(const void* h, const void* w, int64_t n_rows, int64_t hid
   if (!tokens || !logit || !lse) return fail(KLG_ERR_ARG, "null output pointer");
   klg::LseArgs la{};
   const int n_part = sample_plan(n_rows, vocab, la);
-  const int64_t need = (int64_t)n_part * 5 * n_rows * 4;
+  const int64_t need = sample_workspace(n_rows, n_part);
   if (!workspace || workspace_bytes < need || !aligned16(workspace))
     return fail(KLG_ERR_WORKSPACE, "sampling workspace needs %lld bytes (16-byte aligned)", (long long)need);
   if ((rc = bind_device(h))) return rc;
@@ -868,20 +886,30 @@ int klg_lm_head_sample(const void* h, const void* w, int64_t n_rows, int64_t hid
   la.n_kb = cdiv(hidden, klg::BK);
   la.scale_log2 = inv_temp * 1.4426950408889634f;
   la.parts = static_cast<float*>(workspace);
-  la.sample = sample ? 1 : 0;
   la.seed_lo = (uint32_t)seed;
   la.seed_hi = (uint32_t)(seed >> 32);
-  alignas(64) CUtensorMap mh, mw;
+  alignas(64) CUtensorMap mh, mh64, mw;   // mh64: box of 64 rows for the 4-copy row replication
   if (!make_map(&mh, h, hidden, n_rows, hidden, klg::BK, klg::BM) ||
+      !make_map(&mh64, h, hidden, n_rows, hidden, klg::BK, 64) ||
       !make_map(&mw, w, hidden, vocab, hidden, klg::BK, klg::LSE_BN / 2))
     return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
-  if ((rc = launch_lse_pair<klg::EPI_SAMPLE>(mh, mh, mw, la, s))) return rc;
-  const int slot = trace_pre(s);
-  cudaError_t e = launch_k(klg::sample_merge_kernel, dim3(cdiv(n_rows, 256)), dim3(256), 0, s, 1,
-                           static_cast<const float*>(workspace), n_part, (int)n_rows, tokens, logit, lse);
-  trace_post(slot, s, KLG_KIND_MERGE);
-  if (e != cudaSuccess) return cuda_fail(e, "launch sample_merge_kernel");
-  ++g_launches;
+  rc = sample ? launch_lse_pair<klg::EPI_SAMPLE>(mh, mh64, mw, la, s) : launch_lse_pair<klg::EPI_GREEDY>(mh, mh64, mw, la, s);
+  if (rc) return rc;
+  const int groups = sample_merge_groups(n_rows, n_part);
+  const float* parts = static_cast<const float*>(workspace);
+  float* grouped = static_cast<float*>(workspace) + (size_t)n_part * 5 * n_rows;
+  for (int pass = groups > 1 ? 0 : 1; pass < 2; ++pass) {
+    const int slot = trace_pre(s);
+    cudaError_t e = pass == 0
+        ? launch_k(klg::sample_merge_kernel, dim3(cdiv(n_rows, 32), groups), dim3(32 * klg::SMERGE_WARPS), 0, s, 1,
+                   parts, n_part, (int)n_rows, grouped, tokens, logit, lse)
+        : launch_k(klg::sample_merge_kernel, dim3(cdiv(n_rows, 32), 1), dim3(32 * klg::SMERGE_WARPS), 0, s, 1,
+                   groups > 1 ? static_cast<const float*>(grouped) : parts, groups > 1 ? groups : n_part,
+                   (int)n_rows, static_cast<float*>(nullptr), tokens, logit, lse);
+    trace_post(slot, s, KLG_KIND_MERGE);
+    if (e != cudaSuccess) return cuda_fail(e, "launch sample_merge_kernel");
+    ++g_launches;
+  }
   return KLG_OK;
 }
 

@@ -168,7 +168,10 @@ __device__ __forceinline__ void dz_chunk(const uint32_t (&bs)[32], const uint32_
 // The KL cross term is accumulated by the dZ pass, which has both views' values.
 // =====================================================================================
 constexpr int LSE_BN = 256;                                // vocab rows per pair tile
-constexpr int LSE_STAGES = 6;
+#ifndef KLG_LSE_STAGES
+#define KLG_LSE_STAGES 6
+#endif
+constexpr int LSE_STAGES = KLG_LSE_STAGES;
 constexpr int LSE_A_BYTES = TILE_128x64;                   // this CTA's 128 rows x 64
 constexpr int LSE_B_BYTES = (LSE_BN / 2) * BK * 2;         // this CTA's half of the W tile
 constexpr int LSE_STAGE_BYTES = LSE_A_BYTES + LSE_B_BYTES; // 32 KB
@@ -178,7 +181,10 @@ constexpr int LSE_STAGE_BYTES = LSE_A_BYTES + LSE_B_BYTES; // 32 KB
 constexpr int LSE_CSPLIT = KLG_EPI_SPLIT;                  // epilogue warps per TMEM lane quarter
 constexpr int LSE_EPI_WARPS = 4 * LSE_CSPLIT;
 constexpr int LSE_COLS_PER_WARP = LSE_BN / LSE_CSPLIT;
-constexpr int LSE_PROD = 2;                                 // producer warps (round-robin load steps)
+#ifndef KLG_LSE_PROD
+#define KLG_LSE_PROD 2
+#endif
+constexpr int LSE_PROD = KLG_LSE_PROD;                      // producer warps (round-robin load steps)
 constexpr int LSE_PW = EPI_WARP0 + LSE_EPI_WARPS;           // first extra producer warp
 constexpr int LSE_THREADS = 32 * (LSE_PW + LSE_PROD - 1);
 constexpr int LSE_TMEM_COLS = 512;                         // 2 buffers x 256 columns
@@ -202,25 +208,36 @@ struct LseArgs {
   int n_units;      // 2 * n_rp * n_uv
   int n_kb;         // ceil(H / 64)
   float scale_log2; // log2(e) / T
-  float* parts;     // EPI_LSE: [n_uv * LSE_CSPLIT][2][n_views * N]; EPI_SAMPLE: [n_uv * LSE_CSPLIT][5][N]
+  float* parts;     // EPI_LSE: [n_uv * LSE_CSPLIT][2][n_views * N]; else [n_uv * rep * LSE_CSPLIT][5][N]
   int n_views;      // 2: student rows then teacher rows (training pass 1); 1: one matrix (EPI_SAMPLE)
-  int sample;       // EPI_SAMPLE: 0 greedy argmax of z, 1 Gumbel-max sample of softmax(z / T)
-  uint32_t seed_lo, seed_hi;
+  uint32_t seed_lo, seed_hi;   // EPI_SAMPLE
+  // Row replication (EPI_GREEDY / EPI_SAMPLE with N <= 128, one row tile): the pair tile's
+  // 256 M rows hold `rep` copies of rows 0..256/rep-1, and the copy j of a warp's rows
+  // takes the j-th 1/rep of the tile's columns -- every epilogue warp gets work instead of
+  // the few whose TMEM lanes hold the real rows.  rep = 1: none; 2: each CTA loads rows
+  // 0..127 with map_hs; 4: each CTA loads rows 0..63 twice with map_ht (box 64 rows).
+  int rep;
 };
 
-enum { EPI_LSE = 0, EPI_SAMPLE = 1 };
+// EPI_LSE: (m, S) per row and view (training pass 1).  EPI_GREEDY: (m, S) and the argmax of
+// z.  EPI_SAMPLE: (m, S) and a Gumbel-max draw from softmax(z / T).
+enum { EPI_LSE = 0, EPI_GREEDY = 1, EPI_SAMPLE = 2 };
+constexpr uint32_t HASH_ROW = 0x9E3779B1u, HASH_COL = 0x85EBCA77u, HASH_SEED = 0xC2B2AE3Du;
 
 // Counter-based 32-bit hash of (seed, row, column): the three keys combined with odd
 // multipliers, then the "lowbias32" avalanche finaliser (public domain).  The oracle
 // restates it bit for bit.
-__host__ __device__ __forceinline__ uint32_t sample_hash(uint32_t seed_lo, uint32_t seed_hi, uint32_t row, uint32_t col) {
-  uint32_t x = seed_lo ^ (row * 0x9E3779B1u) ^ (col * 0x85EBCA77u) ^ (seed_hi * 0xC2B2AE3Du);
+__host__ __device__ __forceinline__ uint32_t hash_mix(uint32_t x) {
   x ^= x >> 16;
   x *= 0x7FEB352Du;
   x ^= x >> 15;
   x *= 0x846CA68Bu;
   x ^= x >> 16;
   return x;
+}
+
+__host__ __device__ __forceinline__ uint32_t sample_hash(uint32_t seed_lo, uint32_t seed_hi, uint32_t row, uint32_t col) {
+  return hash_mix(seed_lo ^ (row * HASH_ROW) ^ (col * HASH_COL) ^ (seed_hi * HASH_SEED));
 }
 
 __device__ __forceinline__ void lse_unit(const LseArgs& a, int u, int& view, int& rp, int& uv, int& vt0, int& vt1) {
@@ -268,29 +285,74 @@ __device__ __forceinline__ float exp_variate_log2(uint32_t x) {
   return v < 0.03125f ? ser : -__log2f(1.f - v);
 }
 
-// Online best key over one 32-column chunk (columns col0..col0+31 of this thread's row):
-// greedy keys are the raw logits; sampling keys are u - log2(E), u = z log2(e) / T and E an
-// exponential variate in log2 units -- the Gumbel-max rule (argmax of u + Gumbel noise
-// draws from softmax(z / T)) with the constant log2(ln 2) dropped.  Strict '>' keeps the
-// lowest column among equal keys.
-__device__ __forceinline__ void best_chunk(const uint32_t (&b)[32], int nvalid, int col0, int row, const LseArgs& a,
-                                           float& bk, int& bi, float& bz) {
+// Online (m, S) and best-key update of one 32-column chunk (columns col0..col0+31 of this
+// thread's row), branch-free, with trees instead of serial chains.  Greedy keys are the raw
+// logits; sampling keys are u - log2(E), u = z log2(e) / T and E the exponential variate of
+// (seed, row, column) -- the Gumbel-max rule (the argmax of u + Gumbel noise is a draw from
+// softmax(z / T)) with the constant log2(ln 2) dropped.  Ties keep the lowest column: the
+// tree takes the right (higher) operand only when strictly greater, and a chunk replaces
+// the running best (from lower columns) only when strictly greater.
+// rk = seed_lo ^ row * HASH_ROW ^ seed_hi * HASH_SEED, so rk ^ col * HASH_COL is sample_hash's key.
+template <bool SAMPLE>
+__device__ __forceinline__ void select_chunk(const uint32_t (&b)[32], int nvalid, int col0, float sl2, uint32_t rk,
+                                             float& m, float& S, float& bk, int& bi, float& bz) {
+  float z[32];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    if (j < nvalid) {
-      const float z = __uint_as_float(b[j]);
-      float key = z;
-      if (a.sample) {
-        const uint32_t x = sample_hash(a.seed_lo, a.seed_hi, (uint32_t)row, (uint32_t)(col0 + j));
-        key = fmaf(z, a.scale_log2, -__log2f(exp_variate_log2(x)));
-      }
-      if (key > bk) {
-        bk = key;
-        bi = col0 + j;
-        bz = z;
-      }
-    }
+  for (int j = 0; j < 32; ++j) z[j] = j < nvalid ? __uint_as_float(b[j]) : -INFINITY;
+  float t[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) t[j] = fmaxf(z[2 * j], z[2 * j + 1]);
+#pragma unroll
+  for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+    for (int j = 0; j < w; ++j) t[j] = fmaxf(t[2 * j], t[2 * j + 1]);
+  const float nm = fmaxf(m, t[0] * sl2);
+  const float r = ex2(m - nm);
+  m = nm;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;   // ex2(-inf) = 0 for the invalid columns
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    s0 += ex2(fmaf(z[j], sl2, -m));
+    s1 += ex2(fmaf(z[j + 1], sl2, -m));
+    s2 += ex2(fmaf(z[j + 2], sl2, -m));
+    s3 += ex2(fmaf(z[j + 3], sl2, -m));
   }
+  S = fmaf(S, r, (s0 + s1) + (s2 + s3));
+
+  float k[32];
+  if (SAMPLE) {
+    const uint32_t cb = (uint32_t)col0 * HASH_COL;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const uint32_t x = hash_mix(rk ^ (cb + (uint32_t)j * HASH_COL));
+      k[j] = fmaf(z[j], sl2, -__log2f(exp_variate_log2(x)));
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) k[j] = z[j];
+  }
+  float kk[16], zz[16];
+  int ii[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const bool right = k[2 * j + 1] > k[2 * j];
+    kk[j] = right ? k[2 * j + 1] : k[2 * j];
+    ii[j] = 2 * j + (right ? 1 : 0);
+    if (SAMPLE) zz[j] = right ? z[2 * j + 1] : z[2 * j];
+  }
+#pragma unroll
+  for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+    for (int j = 0; j < w; ++j) {
+      const bool right = kk[2 * j + 1] > kk[2 * j];
+      kk[j] = right ? kk[2 * j + 1] : kk[2 * j];
+      ii[j] = right ? ii[2 * j + 1] : ii[2 * j];
+      if (SAMPLE) zz[j] = right ? zz[2 * j + 1] : zz[2 * j];
+    }
+  const bool take = kk[0] > bk;
+  bk = take ? kk[0] : bk;
+  bi = take ? col0 + ii[0] : bi;
+  bz = take ? (SAMPLE ? zz[0] : kk[0]) : bz;
 }
 
 template <bool RES, int EPI>
@@ -369,13 +431,23 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
         lse_unit(a, u, view, rp, uv, vt0, vt1);
         const CUtensorMap* ma = view ? &map_ht : &map_hs;
         const int row0 = rp * 256 + (int)rank * 128;
+        // this CTA's 128 A rows of k-block kb (replicated rows when a.rep > 1)
+        auto load_a = [&](uint32_t dst, uint32_t bar, int kb) {
+          if (a.rep == 1) {
+            tma_load_2d_pair(dst, ma, bar, kb * BK, row0);
+          } else if (a.rep == 2) {
+            tma_load_2d_pair(dst, &map_hs, bar, kb * BK, 0);
+          } else {
+            tma_load_2d_pair(dst, &map_ht, bar, kb * BK, 0);
+            tma_load_2d_pair(dst + 64 * 128, &map_ht, bar, kb * BK, 0);
+          }
+        };
         if (RES && prod == 0) {
           // this unit's rows: wait until the previous unit's MMAs released the A region
           if (!warp_wait(aempty_bar, (uint32_t)(ucount & 1) ^ 1u, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) break;
           if (elect_one()) {
             if (leader) mbar_arrive_expect_tx(afull_bar, 2 * a.n_kb * LSE_A_BYTES);
-            for (int kb = 0; kb < a.n_kb; ++kb)
-              tma_load_2d_pair(abase + kb * LSE_A_BYTES, ma, lead_afull, kb * BK, row0);
+            for (int kb = 0; kb < a.n_kb; ++kb) load_a(abase + kb * LSE_A_BYTES, lead_afull, kb);
             if (!leader) mbar_arrive_cluster(lead_afull);
           }
         }
@@ -387,7 +459,7 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
                 const uint32_t sa = sbase + stage * STAGE_BYTES;
                 const uint32_t fb = lead_full0 + 8u * stage;
                 if (leader) mbar_arrive_expect_tx(full0 + 8u * stage, 2 * STAGE_BYTES);
-                if (!RES) tma_load_2d_pair(sa, ma, fb, kb * BK, row0);
+                if (!RES) load_a(sa, fb, kb);
                 tma_load_2d_pair(sa + (RES ? 0 : LSE_A_BYTES), &map_w, fb, kb * BK,
                                  vt * LSE_BN + (int)rank * (LSE_BN / 2));
                 if (!leader) mbar_arrive_cluster(fb);
@@ -457,32 +529,39 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
     // -------------------------------------------------------------- epilogue (both CTAs)
     const int q = warp & 3;
     const int h = (warp - EPI_WARP0) >> 2;        // column slice of the 256-column tile
-    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * LSE_COLS_PER_WARP);
+    const int rw = 256 / a.rep;                   // rows per copy
+    const int prow = (int)rank * 128 + q * 32;    // the warp's first M row in the pair tile
+    const int copy = prow / rw;                   // which copy of the rows these lanes hold
+    const int ncol = LSE_BN / (a.rep * LSE_CSPLIT);   // columns per warp and tile (multiple of 32)
+    const int slice = (copy * LSE_CSPLIT + h);        // column slice, also the record index
+    const int n_slices = a.rep * LSE_CSPLIT;
+    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(slice * ncol);
     int tcount = 0;
     bool ok = true;
     for (int u = cid; ok && u < a.n_units; u += n_clusters) {
       int view, rp, uv, vt0, vt1;
       lse_unit(a, u, view, rp, uv, vt0, vt1);
-      const int row = rp * 256 + (int)rank * 128 + q * 32 + lane;
-      const bool live = rp * 256 + (int)rank * 128 + q * 32 < a.n_rows;   // warp-uniform
+      const int row = rp * 256 + prow % rw + lane;
+      const bool live = rp * 256 + prow % rw < a.n_rows;   // warp-uniform
+      const uint32_t rk = a.seed_lo ^ ((uint32_t)row * HASH_ROW) ^ (a.seed_hi * HASH_SEED);
       float m = NEG_BIG, S = 0.f;
-      float bk = -INFINITY, bz = 0.f;   // EPI_SAMPLE: best key, its logit
+      float bk = -INFINITY, bz = 0.f;   // EPI_GREEDY / EPI_SAMPLE: best key, its logit
       int bi = -1;
       for (int vt = vt0; ok && vt < vt1; ++vt, ++tcount) {
         const int buf = tcount & 1;
         const uint32_t tph = (tcount >> 1) & 1;
         if (!mbar_wait(tfull0 + 8u * buf, tph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) { ok = false; break; }
         tc_fence_after();
-        const int col_base = vt * LSE_BN + h * LSE_COLS_PER_WARP;
+        const int col_base = vt * LSE_BN + slice * ncol;
 #pragma unroll 1
-        for (int c = 0; live && c < LSE_COLS_PER_WARP / 32; ++c) {
+        for (int c = 0; live && c < ncol / 32; ++c) {
           uint32_t b0[32];
           tmem_ld32_raw(lane_addr + buf * LSE_BN + c * 32, b0);
           tmem_wait_ld_regs(b0);
           const int nvalid = min(32, a.vocab - (col_base + c * 32));
           if (nvalid > 0) {
-            lse_chunk(b0, nvalid, a.scale_log2, m, S);
-            if (EPI == EPI_SAMPLE) best_chunk(b0, nvalid, col_base + c * 32, row, a, bk, bi, bz);
+            if (EPI == EPI_LSE) lse_chunk(b0, nvalid, a.scale_log2, m, S);
+            else select_chunk<EPI == EPI_SAMPLE>(b0, nvalid, col_base + c * 32, a.scale_log2, rk, m, S, bk, bi, bz);
           }
         }
         tc_fence_before();
@@ -495,12 +574,12 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
       if (ok && row < a.n_rows) {
         if (EPI == EPI_LSE) {
           const size_t n2 = (size_t)a.n_views * a.n_rows;
-          float* p = a.parts + ((size_t)(uv * LSE_CSPLIT + h) * 2) * n2 + (size_t)view * a.n_rows + row;
+          float* p = a.parts + ((size_t)(uv * n_slices + slice) * 2) * n2 + (size_t)view * a.n_rows + row;
           p[0] = m;
           p[n2] = S;
         } else {
           const size_t n = (size_t)a.n_rows;
-          float* p = a.parts + (size_t)(uv * LSE_CSPLIT + h) * 5 * n + row;
+          float* p = a.parts + (size_t)(uv * n_slices + slice) * 5 * n + row;
           p[0] = m;
           p[n] = S;
           p[2 * n] = bk;
@@ -1198,33 +1277,76 @@ __global__ void lse_merge_kernel(const float* __restrict__ parts, int n_part, in
   lse[i] = M + __log2f(S);
 }
 
-// lm_head sampling: merge the per-unit records (m, S, key, index, z) of each row into the
+// lm_head selection: merge the per-unit records (m, S, key, index, z) of each row into the
 // chosen token (highest key, lowest index among equals), its logit and the natural-log
-// log-sum-exp of z / T (so p(token) = exp(z_token / T - lse)).
-__global__ void sample_merge_kernel(const float* __restrict__ parts, int n_part, int n, int* __restrict__ tokens,
-                                    float* __restrict__ logit, float* __restrict__ lse) {
+// log-sum-exp of z / T (so p(token) = exp(z_token / T - lse)).  A block takes 32 rows (one
+// per lane, coalesced loads) and the records of group blockIdx.y (gridDim.y groups); its
+// warps take the group's records round-robin and combine through shared memory.  With
+// out_parts set, each group writes one merged record [gridDim.y][5][N] for a second launch
+// (one group) to finish: a few rows with hundreds of records are then not a serial chain
+// of loads on one SM.
+constexpr int SMERGE_WARPS = 16;
+__device__ __forceinline__ void merge_best(float k, int idx, float z, float& bk, int& bi, float& bz) {
+  const bool take = idx >= 0 && (k > bk || (k == bk && idx < bi));
+  bk = take ? k : bk;
+  bi = take ? idx : bi;
+  bz = take ? z : bz;
+}
+
+__global__ void __launch_bounds__(SMERGE_WARPS * 32)
+sample_merge_kernel(const float* __restrict__ parts, int n_part, int n, float* __restrict__ out_parts,
+                    int* __restrict__ tokens, float* __restrict__ logit, float* __restrict__ lse) {
   pdl_enter();
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
+  __shared__ float sm_m[SMERGE_WARPS][32], sm_s[SMERGE_WARPS][32], sm_k[SMERGE_WARPS][32], sm_z[SMERGE_WARPS][32];
+  __shared__ int sm_i[SMERGE_WARPS][32];
+  const int lane = threadIdx.x & 31;
+  const int w = threadIdx.x >> 5;
+  const int i = blockIdx.x * 32 + lane;
   const size_t st = (size_t)n;
-  float M = NEG_BIG, bk = -INFINITY, bz = 0.f;
+  float M = NEG_BIG, S = 0.f, bk = -INFINITY, bz = 0.f;
   int bi = -1;
-  for (int p = 0; p < n_part; ++p) {
-    const float* r = parts + (size_t)p * 5 * st + i;
-    M = fmaxf(M, r[0]);
-    const float k = r[2 * st];
-    const int idx = __float_as_int(r[3 * st]);
-    if (idx >= 0 && (k > bk || (k == bk && idx < bi))) {
-      bk = k;
-      bi = idx;
-      bz = r[4 * st];
+  const int per = (n_part + gridDim.y - 1) / gridDim.y;
+  const int p0 = blockIdx.y * per;
+  const int p1 = min(n_part, p0 + per);
+  if (i < n) {
+#pragma unroll 4
+    for (int p = p0 + w; p < p1; p += SMERGE_WARPS) {
+      const float* r = parts + (size_t)p * 5 * st + i;
+      const float m = r[0], s = r[st], k = r[2 * st], z = r[4 * st];
+      const int idx = __float_as_int(r[3 * st]);
+      const float nm = fmaxf(M, m);
+      S = fmaf(S, ex2(M - nm), s * ex2(m - nm));
+      M = nm;
+      merge_best(k, idx, z, bk, bi, bz);
     }
   }
-  float S = 0.f;
-  for (int p = 0; p < n_part; ++p) S = fmaf(parts[(size_t)p * 5 * st + st + i], ex2(parts[(size_t)p * 5 * st + i] - M), S);
-  tokens[i] = bi;
-  logit[i] = bz;
-  lse[i] = (M + __log2f(S)) * 0.69314718055994530942f;
+  sm_m[w][lane] = M;
+  sm_s[w][lane] = S;
+  sm_k[w][lane] = bk;
+  sm_i[w][lane] = bi;
+  sm_z[w][lane] = bz;
+  __syncthreads();
+  if (w == 0 && i < n) {
+    for (int v = 1; v < SMERGE_WARPS; ++v) {
+      const float m = sm_m[v][lane];
+      const float nm = fmaxf(M, m);
+      S = fmaf(S, ex2(M - nm), sm_s[v][lane] * ex2(m - nm));
+      M = nm;
+      merge_best(sm_k[v][lane], sm_i[v][lane], sm_z[v][lane], bk, bi, bz);
+    }
+    if (out_parts) {
+      float* o = out_parts + (size_t)blockIdx.y * 5 * st + i;
+      o[0] = M;
+      o[st] = S;
+      o[2 * st] = bk;
+      o[3 * st] = __int_as_float(bi);
+      o[4 * st] = bz;
+    } else {
+      tokens[i] = bi;
+      logit[i] = bz;
+      lse[i] = (M + __log2f(S)) * 0.69314718055994530942f;
+    }
+  }
 }
 
 // Training-path per-row KL: KL_i = ln2 * (sum_p a_parts[p][i] + L_s,i - L_t,i) for rows

@@ -73,14 +73,17 @@ def test_greedy_exact_ties_keep_first_index():
     np.testing.assert_array_equal(logit, z.max(axis=1))
 
 
-@pytest.mark.parametrize("N,H,V", [(1, 576, 49153), (7, 576, 49152), (32, 576, 49153), (300, 128, 517),
-                                   (1000, 576, 5000), (513, 192, 256)])
+# N <= 64: rows in 4 copies per pair tile; N <= 128: 2 copies; H > 576: A streamed per stage
+@pytest.mark.parametrize("N,H,V", [(1, 576, 49153), (7, 576, 49152), (32, 576, 49153), (64, 576, 4096),
+                                   (100, 576, 49153), (128, 192, 1000), (129, 128, 517), (300, 128, 517),
+                                   (1000, 576, 5000), (513, 192, 256), (32, 1024, 5000), (100, 2048, 3000)])
 def test_greedy_matches_oracle(N, H, V):
     h, W = _problem(N, H, V, seed=N + V)
     _check(h, W, 0.0, 0, min_exact=0.99 if N >= 100 else 1.0)
 
 
-@pytest.mark.parametrize("N,H,V,T", [(32, 576, 49153, 1.0), (300, 128, 517, 0.7), (1000, 576, 5000, 1.3),
+@pytest.mark.parametrize("N,H,V,T", [(32, 576, 49153, 1.0), (64, 1024, 3000, 1.0), (100, 576, 49153, 0.8),
+                                     (128, 2048, 4000, 1.2), (300, 128, 517, 0.7), (1000, 576, 5000, 1.3),
                                      (2048, 576, 8192, 0.5)])
 def test_sampled_tokens_match_oracle_keys(N, H, V, T):
     h, W = _problem(N, H, V, seed=3 * N + V, scale=4.0)
