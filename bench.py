@@ -51,6 +51,8 @@ CONFIGS = {
     "c5": (12288, 576, 49152, "ragged/edge: 12288 rows, ~25% valid, teacher x4, T=2, bf16"),
     "c3": (65536, 2048, 49152, "SmolLM2-1.7B shape, [32,2048,2048] per view, V=49152, bf16"),
     "c4": (32768, 1024, 248320, "large-vocab shape, [16,2048,1024] per view, V=248320, bf16 (vocab-sharded at N>1)"),
+    "c2n": (16384, 576, 49152, "the 16384-row SmolLM2-135M shape on hidden states before the final RMSNorm: "
+                               "norm (both views) + loss + norm backward in the step, bf16"),
 }
 METRIC = "KL-GEMM fwd+bwd loss-rows/sec"
 SAMPLE_METRIC = "lm_head token selections/sec"
@@ -162,7 +164,7 @@ def cpu_baseline(config: str, seconds: float):
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     sample = 256
-    p = O.make_problem(config, n_rows=sample, seed=7)
+    p = O.make_problem("c2" if config == "c2n" else config, n_rows=sample, seed=7)
     hs, ht, W, m, T = p["h_s"].float(), p["h_t"].float(), p["W"].float(), p["mask"], p["T"]
     times = []
     t_end = time.perf_counter() + seconds
@@ -189,7 +191,7 @@ def run_reference_arm(args):
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     sample = 128
-    p = O.make_problem(args.config, n_rows=sample, seed=7)
+    p = O.make_problem("c2" if args.config == "c2n" else args.config, n_rows=sample, seed=7)
     hs, ht, W, m, T = p["h_s"].float(), p["h_t"].float(), p["W"].float(), p["mask"], p["T"]
     for _ in range(max(1, args.warmup)):
         O.aligned_kl_torch_with_grads(hs, ht, W, m, T)
@@ -433,8 +435,10 @@ def main():
 
     N, H, V, desc = CONFIGS[args.config]
     vocab_sharded = args.config == "c4" and world > 1
-    p = O.make_problem(args.config, seed=42 if vocab_sharded else 42 + rank)   # this rank's rows
-    pw = O.make_problem(args.config, n_rows=1, seed=42)   # shared lm_head
+    prenorm = args.config == "c2n"
+    pcfg = "c2" if prenorm else args.config
+    p = O.make_problem(pcfg, seed=42 if vocab_sharded else 42 + rank)   # this rank's rows
+    pw = O.make_problem(pcfg, n_rows=1, seed=42)   # shared lm_head
     T = p["T"]
     hs = p["h_s"].to(dev)
     ht = p["h_t"].to(dev)
@@ -446,6 +450,12 @@ def main():
         V_work = hi - lo
     m = ops.mask_u8(p["mask"].to(dev))
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    if prenorm:
+        # pre-norm residual-stream rows (scale 3) and a norm weight around 1
+        gn = torch.Generator().manual_seed(43 + rank)
+        hs = (p["h_s"].float() * 3.0).to(torch.bfloat16).to(dev)
+        ht = (p["h_t"].float() * 3.0).to(torch.bfloat16).to(dev)
+        gamma = (1.0 + 0.1 * torch.randn(H, generator=gn)).to(torch.bfloat16).float().to(dev)
 
     def barrier():
         if world > 1:
@@ -467,9 +477,24 @@ def main():
         dist.all_reduce(dh)
         return loss
 
+    def step_prenorm():
+        cnt = ops.count_valid(m)
+        if world > 1:
+            dist.all_reduce(cnt)
+        ys, rs = ops.rmsnorm_rows(hs, gamma)
+        yt, _ = ops.rmsnorm_rows(ht, gamma, want_rstd=False)
+        loss, _, _, _, dh, dw = ops.kl_fwd_bwd(ys, yt, W, m, T, count=cnt, workspace_bytes=fb_ws)
+        ops.rmsnorm_rows_backward(hs, gamma, rs, dh)
+        if world > 1:
+            dist.all_reduce(loss)
+            dist.all_reduce(dw)
+        return loss
+
     def step():
         if vocab_sharded:
             return step_vocab()
+        if prenorm:
+            return step_prenorm()
         # the training step: count (all-reduced across ranks) -> loss + dH + dW -> loss and dW all-reduced
         cnt = ops.count_valid(m)
         if world > 1:
@@ -549,8 +574,8 @@ def main():
     # ---------------------------------------------------------------- end-to-end (public API)
     e2e = None
     if not args.no_e2e:
-        hs_h = p["h_s"].pin_memory()
-        ht_h = p["h_t"].pin_memory()
+        hs_h = hs.cpu().pin_memory() if prenorm else p["h_s"].pin_memory()
+        ht_h = ht.cpu().pin_memory() if prenorm else p["h_t"].pin_memory()
         m_h = p["mask"].to(torch.uint8).pin_memory()
         Wp = W.clone().requires_grad_(True)
         h2d = hs_h.numel() * hs_h.element_size() + ht_h.numel() * ht_h.element_size() + m_h.numel()
@@ -559,7 +584,9 @@ def main():
             hs_d = hs_h.to(dev, non_blocking=True).requires_grad_(True)
             ht_d = ht_h.to(dev, non_blocking=True)
             m_d = m_h.to(dev, non_blocking=True)
-            if vocab_sharded:
+            if prenorm and world == 1:
+                loss = ops.prenorm_kl_loss(hs_d, ht_d, gamma, Wp, m_d, T)
+            elif vocab_sharded:
                 loss = vocab_sharded_kl_loss(hs_d, ht_d, Wp, m_d, T)
             elif world > 1:
                 loss = row_sharded_kl_loss(hs_d, ht_d, Wp, m_d, T)

@@ -182,6 +182,21 @@ int klg_lm_head_sample(const void* h, const void* w, int64_t n_rows, int64_t hid
                        int sample, uint64_t seed, int32_t* tokens, float* logit, float* lse, void* workspace,
                        int64_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------- final RMSNorm prologue
+ * For pre-norm hidden states: the backbone's final norm (model.py:493, `self.norm`, a
+ * transformers LlamaRMSNorm) applied row by row, so the fused loss can take the states
+ * before the norm.  x [N, H] bf16 (x_f32 = 0) or fp32 (x_f32 = 1); gamma [H] fp32 (the
+ * norm weight; bf16 weights convert exactly).  r = 1 / sqrt(mean(x^2) + eps) (fp32);
+ * y [N, H] bf16 = gamma * bf16(x r) rounded to bf16 for bf16 x -- the norm's own result
+ * in a bf16 model -- and bf16(gamma * x r) for fp32 x.  rstd [N] (may be NULL) keeps r.
+ * The backward gives dx [N, H] fp32 from dy [N, H] fp32 (the loss's dH):
+ * dx = r gamma dy - (r^3 / H) x sum(gamma dy x).  The norm weight is frozen in the
+ * reference (model.py:323-324), so no weight gradient is formed. */
+int klg_rmsnorm_rows(const void* x, int x_f32, const float* gamma, int64_t n_rows, int64_t hidden, float eps, void* y,
+                     float* rstd, void* stream);
+int klg_rmsnorm_rows_bwd(const void* x, int x_f32, const float* gamma, const float* rstd, const float* dy,
+                         int64_t n_rows, int64_t hidden, float* dx, void* stream);
+
 /* fp32 -> bf16 conversion (round to nearest even) for fp32 callers. */
 int klg_cast_f32_bf16(const float* in, void* out, int64_t n, void* stream);
 
@@ -200,6 +215,7 @@ int klg_cast_f32_bf16(const float* in, void* out, int64_t n, void* stream);
 #define KLG_KIND_CAST 7
 #define KLG_KIND_ZERO 8      /* pass 2: zeroing of the fp32 dW / dH buffers            */
 #define KLG_KIND_SAMPLE 9    /* inference: lm_head logits -> argmax / Gumbel-max sample   */
+#define KLG_KIND_NORM 10     /* final RMSNorm of pre-norm rows, forward or backward       */
 int klg_trace_begin(int capacity);
 int klg_trace_end(int* kinds, float* ms, int capacity, int* n);
 

@@ -530,3 +530,55 @@ def sample_token_torch(logits, temperature: float = 0.0, top_k: int = 0, top_p: 
     probs = F.softmax(scaled, dim=-1)
     tokens = torch.multinomial(probs.view(-1, probs.size(-1)), 1).view(probs.shape[:-1])
     return tokens, probs
+
+
+# --------------------------------------------------------------------------
+# Final RMSNorm of pre-norm rows (reference model.py:493; transformers LlamaRMSNorm)
+# --------------------------------------------------------------------------
+
+def _bf16_round_np(a):
+    """Round float32 values to the nearest bf16 (ties to even), returned as float32."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)
+
+
+def rmsnorm_np(x, gamma, eps: float = 1e-5, bf16_input: bool = True, r=None):
+    """``LlamaRMSNorm`` (transformers, as ``model.py:493`` uses it) row by row.
+
+    ``r = 1 / sqrt(mean(x^2) + eps)`` in fp32 (float64 sum, rounded); bf16 input:
+    ``y = bf16(gamma * bf16(x r))`` -- the cast back to the input dtype, then the bf16
+    weight product; fp32 input: ``y = gamma * (x r)`` in fp32.  Returns ``(y, r)`` as
+    float32 arrays.  ``r`` may be given (e.g. a device's, whose fp32 sum of squares runs
+    in another order) to check the rest bit for bit.
+    """
+    x32 = np.asarray(x, dtype=np.float32)
+    g32 = np.asarray(gamma, dtype=np.float32)
+    if r is None:
+        var = np.float32(np.mean(x32.astype(np.float64) ** 2, axis=-1))
+        r = (np.float32(1.0) / np.sqrt(var + np.float32(eps), dtype=np.float32)).astype(np.float32)
+    r = np.asarray(r, dtype=np.float32)
+    t = x32 * r[:, None]
+    if bf16_input:
+        return _bf16_round_np(g32[None, :] * _bf16_round_np(t)), r
+    return (g32[None, :] * t).astype(np.float32), r
+
+
+def rmsnorm_backward_np(x, gamma, r, dy):
+    """Gradient through the norm in float64 (roundings pass the gradient unchanged):
+    ``dx = r gamma dy - (r^3 / H) x sum(gamma dy x)``."""
+    x = np.asarray(x, dtype=np.float64)
+    g = np.asarray(gamma, dtype=np.float64)[None, :]
+    r = np.asarray(r, dtype=np.float64)[:, None]
+    dy = np.asarray(dy, dtype=np.float64)
+    s = (g * dy * x).sum(axis=-1, keepdims=True)
+    return r * g * dy - (r ** 3 / x.shape[-1]) * x * s
+
+
+def prenorm_kl_loss_np(x_s, x_t, gamma, W, mask, temperature: float = 1.0, eps: float = 1e-5):
+    """The loss on pre-norm rows in float64: norm both views (fp32 semantics), the fused
+    loss's math on the normed rows, and the gradient of the pre-norm student rows."""
+    ys, rs = rmsnorm_np(x_s, gamma, eps, bf16_input=False)
+    yt, _ = rmsnorm_np(x_t, gamma, eps, bf16_input=False)
+    loss, dh, _, _, _, _ = aligned_kl_loss_np(ys, yt, W, mask, temperature)
+    return loss, rmsnorm_backward_np(x_s, gamma, rs, dh)

@@ -29,6 +29,10 @@ SIGNATURES = {
     "klg_launch_count": (c_longlong, []),
     "klg_selftest_wait_timeout": (c_int, [c_void_p]),
     "klg_lm_head_sample_workspace_bytes": (c_longlong, [c_longlong, c_longlong]),
+    "klg_rmsnorm_rows": (c_int, [c_void_p, c_int, c_void_p, c_longlong, c_longlong, c_float, c_void_p, c_void_p,
+                                 c_void_p]),
+    "klg_rmsnorm_rows_bwd": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_longlong, c_longlong, c_void_p,
+                                     c_void_p]),
     "klg_lm_head_sample": (c_int, [c_void_p, c_void_p, c_longlong, c_longlong, c_longlong, c_float, c_int, c_ulonglong,
                                    c_void_p, c_void_p, c_void_p, c_void_p, c_longlong, c_void_p]),
     "klg_num_partials": (c_int, [c_int64, c_int64, POINTER(c_int)]),
@@ -56,7 +60,7 @@ SIGNATURES = {
     "klg_trace_end": (c_int, [POINTER(c_int), POINTER(c_float), c_int, POINTER(c_int)]),
 }
 
-KIND_NAMES = {1: "stats", 2: "dz", 3: "gemm", 4: "merge", 5: "finalize", 6: "count", 7: "cast", 8: "zero", 9: "sample"}
+KIND_NAMES = {1: "stats", 2: "dz", 3: "gemm", 4: "merge", 5: "finalize", 6: "count", 7: "cast", 8: "zero", 9: "sample", 10: "norm"}
 
 _lib = None
 

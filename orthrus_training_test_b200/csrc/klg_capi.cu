@@ -913,6 +913,54 @@ int klg_lm_head_sample(const void* h, const void* w, int64_t n_rows, int64_t hid
   return KLG_OK;
 }
 
+namespace {
+int check_norm(const void* x, int x_f32, const float* gamma, int64_t n_rows, int64_t hidden) {
+  if (!x || !gamma) return fail(KLG_ERR_ARG, "null input pointer");
+  if (x_f32 != 0 && x_f32 != 1) return fail(KLG_ERR_ARG, "x_f32 must be 0 (bf16) or 1 (fp32)");
+  if (n_rows < 1 || hidden < 8 || n_rows > (1ll << 30) || hidden > (1ll << 20))
+    return fail(KLG_ERR_ARG, "bad shape N=%lld H=%lld", (long long)n_rows, (long long)hidden);
+  if (hidden % 8 != 0) return fail(KLG_ERR_ALIGN, "hidden=%lld must be a multiple of 8", (long long)hidden);
+  if (!aligned16(x) || !aligned16(gamma)) return fail(KLG_ERR_ALIGN, "x and gamma must be 16-byte aligned");
+  return KLG_OK;
+}
+}  // namespace
+
+int klg_rmsnorm_rows(const void* x, int x_f32, const float* gamma, int64_t n_rows, int64_t hidden, float eps, void* y,
+                     float* rstd, void* stream) {
+  int rc = check_norm(x, x_f32, gamma, n_rows, hidden);
+  if (rc) return rc;
+  if (!y || !aligned16(y)) return fail(KLG_ERR_ALIGN, "y must be non-null and 16-byte aligned");
+  if (!(eps >= 0.f) || !std::isfinite(eps)) return fail(KLG_ERR_ARG, "eps must be finite and >= 0");
+  if ((rc = bind_device(x))) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int slot = trace_pre(s);
+  auto k = x_f32 ? klg::rmsnorm_rows_kernel<true> : klg::rmsnorm_rows_kernel<false>;
+  cudaError_t e = launch_k(k, dim3(cdiv(n_rows, 8)), dim3(256), 0, s, 1, x, gamma, (int)n_rows, (int)hidden, eps,
+                           static_cast<__nv_bfloat16*>(y), rstd);
+  trace_post(slot, s, KLG_KIND_NORM);
+  if (e != cudaSuccess) return cuda_fail(e, "launch rmsnorm_rows_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
+int klg_rmsnorm_rows_bwd(const void* x, int x_f32, const float* gamma, const float* rstd, const float* dy,
+                         int64_t n_rows, int64_t hidden, float* dx, void* stream) {
+  int rc = check_norm(x, x_f32, gamma, n_rows, hidden);
+  if (rc) return rc;
+  if (!rstd || !dy || !dx) return fail(KLG_ERR_ARG, "null rstd/dy/dx");
+  if (!aligned16(dy) || !aligned16(dx)) return fail(KLG_ERR_ALIGN, "dy and dx must be 16-byte aligned");
+  if ((rc = bind_device(x))) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int slot = trace_pre(s);
+  auto k = x_f32 ? klg::rmsnorm_rows_bwd_kernel<true> : klg::rmsnorm_rows_bwd_kernel<false>;
+  cudaError_t e = launch_k(k, dim3(cdiv(n_rows, 8)), dim3(256), 0, s, 1, x, gamma, rstd, dy, (int)n_rows, (int)hidden,
+                           dx);
+  trace_post(slot, s, KLG_KIND_NORM);
+  if (e != cudaSuccess) return cuda_fail(e, "launch rmsnorm_rows_bwd_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
 int klg_cast_f32_bf16(const float* in, void* out, int64_t n, void* stream) {
   if (!in || !out || n < 0) return fail(KLG_ERR_ARG, "bad arguments to klg_cast_f32_bf16");
   if (n == 0) return KLG_OK;

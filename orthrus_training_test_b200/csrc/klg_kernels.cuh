@@ -1421,6 +1421,120 @@ __global__ void zero_f32x4_kernel(float4* __restrict__ p, long long n4) {
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) p[i] = z;
 }
 
+// ---------------------------------------------------------------- final RMSNorm (pre-norm inputs)
+// The backbone's final norm (LlamaRMSNorm): r = 1 / sqrt(mean_k x_k^2 + eps) in fp32, and
+// bf16 rows  y = bf16(gamma * bf16(x r))  for bf16 x (the norm's own rounding to the input
+// dtype, then a bf16 product), y = bf16(gamma * (x r)) for fp32 x (the fp32 norm output,
+// rounded once for the GEMM).  One warp per row, 16-byte vector loads (H % 8 == 0).
+__device__ __forceinline__ float warp_sum_f32(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <bool F32>
+__device__ __forceinline__ void load8(const void* __restrict__ x, size_t off, float (&v)[8]) {
+  if (F32) {
+    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(x) + off);
+    const float4 a = p[0], b = p[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) + off);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[2 * j] = __uint_as_float(w[j] << 16);
+      v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+    }
+  }
+}
+
+template <bool F32>
+__global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const void* __restrict__ x, const float* __restrict__ gamma,
+                                                           int n, int hidden, float eps,
+                                                           __nv_bfloat16* __restrict__ y, float* __restrict__ rstd) {
+  pdl_enter();
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= n) return;
+  const size_t base = (size_t)row * hidden;
+  float ss = 0.f;
+  for (int c = lane * 8; c < hidden; c += 256) {
+    float v[8];
+    load8<F32>(x, base + c, v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
+  }
+  ss = warp_sum_f32(ss);
+  const float r = 1.0f / sqrtf(ss / (float)hidden + eps);
+  for (int c = lane * 8; c < hidden; c += 256) {
+    float v[8];
+    load8<F32>(x, base + c, v);
+    const float4 g0 = *reinterpret_cast<const float4*>(gamma + c);
+    const float4 g1 = *reinterpret_cast<const float4*>(gamma + c + 4);
+    const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float a = v[2 * j] * r, b = v[2 * j + 1] * r;
+      if (!F32) {
+        a = __bfloat162float(__float2bfloat16_rn(a));
+        b = __bfloat162float(__float2bfloat16_rn(b));
+      }
+      const __nv_bfloat162 t = __floats2bfloat162_rn(g[2 * j] * a, g[2 * j + 1] * b);
+      o[j] = *reinterpret_cast<const uint32_t*>(&t);
+    }
+    *reinterpret_cast<uint4*>(y + base + c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  if (rstd && lane == 0) rstd[row] = r;
+}
+
+// Gradient through the norm (the roundings pass the gradient through unchanged, as
+// autograd's dtype casts do):  dx_k = r gamma_k dy_k - (r^3 / H) x_k sum_j gamma_j dy_j x_j.
+template <bool F32>
+__global__ void __launch_bounds__(256) rmsnorm_rows_bwd_kernel(const void* __restrict__ x,
+                                                               const float* __restrict__ gamma,
+                                                               const float* __restrict__ rstd,
+                                                               const float* __restrict__ dy, int n, int hidden,
+                                                               float* __restrict__ dx) {
+  pdl_enter();
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= n) return;
+  const size_t base = (size_t)row * hidden;
+  float s = 0.f;
+  for (int c = lane * 8; c < hidden; c += 256) {
+    float v[8];
+    load8<F32>(x, base + c, v);
+    const float4 d0 = *reinterpret_cast<const float4*>(dy + base + c);
+    const float4 d1 = *reinterpret_cast<const float4*>(dy + base + c + 4);
+    const float4 g0 = *reinterpret_cast<const float4*>(gamma + c);
+    const float4 g1 = *reinterpret_cast<const float4*>(gamma + c + 4);
+    s = fmaf(g0.x * d0.x, v[0], s); s = fmaf(g0.y * d0.y, v[1], s);
+    s = fmaf(g0.z * d0.z, v[2], s); s = fmaf(g0.w * d0.w, v[3], s);
+    s = fmaf(g1.x * d1.x, v[4], s); s = fmaf(g1.y * d1.y, v[5], s);
+    s = fmaf(g1.z * d1.z, v[6], s); s = fmaf(g1.w * d1.w, v[7], s);
+  }
+  s = warp_sum_f32(s);
+  const float r = rstd[row];
+  const float c3 = r * r * r * s / (float)hidden;
+  for (int c = lane * 8; c < hidden; c += 256) {
+    float v[8];
+    load8<F32>(x, base + c, v);
+    const float4 d0 = *reinterpret_cast<const float4*>(dy + base + c);
+    const float4 d1 = *reinterpret_cast<const float4*>(dy + base + c + 4);
+    const float4 g0 = *reinterpret_cast<const float4*>(gamma + c);
+    const float4 g1 = *reinterpret_cast<const float4*>(gamma + c + 4);
+    float4 o0, o1;
+    o0.x = fmaf(r * g0.x, d0.x, -c3 * v[0]); o0.y = fmaf(r * g0.y, d0.y, -c3 * v[1]);
+    o0.z = fmaf(r * g0.z, d0.z, -c3 * v[2]); o0.w = fmaf(r * g0.w, d0.w, -c3 * v[3]);
+    o1.x = fmaf(r * g1.x, d1.x, -c3 * v[4]); o1.y = fmaf(r * g1.y, d1.y, -c3 * v[5]);
+    o1.z = fmaf(r * g1.z, d1.z, -c3 * v[6]); o1.w = fmaf(r * g1.w, d1.w, -c3 * v[7]);
+    *reinterpret_cast<float4*>(dx + base + c) = o0;
+    *reinterpret_cast<float4*>(dx + base + c + 4) = o1;
+  }
+}
+
 __global__ void cast_f32_bf16_kernel(const float* __restrict__ in, __nv_bfloat16* __restrict__ out, long long n) {
   pdl_enter();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;

@@ -8,11 +8,11 @@ train.py:549-567.
 """
 from __future__ import annotations
 
-from typing import Tuple
+from typing import Optional, Tuple
 
 import torch
 
-from .ops import KLGemmFn
+from .ops import KLGemmFn, PrenormKLGemmFn
 
 _index_cache: dict = {}
 
@@ -56,16 +56,23 @@ def select_rows(diff_hidden, ar_hidden_states, anchor_positions, K, target_ids, 
 
 def compute_kl_loss(diff_hidden: torch.Tensor, ar_hidden_states: torch.Tensor, lm_head: torch.nn.Module,
                     anchor_positions: torch.Tensor, K: int, target_ids: torch.Tensor, pad_token_id: int,
-                    teacher_probs=None, teacher_ent=None, temperature: float = 1.0) -> torch.Tensor:
+                    teacher_probs=None, teacher_ent=None, temperature: float = 1.0, *,
+                    norm_weight: Optional[torch.Tensor] = None, norm_eps: float = 1e-5) -> torch.Tensor:
     """Forward KL(teacher || student) averaged over valid diffusion positions.
 
     Signature of train.py:142-152 (plus an optional ``temperature``, default 1
     = the reference).  Returns a 0-d fp32 tensor; ``0.0`` with
     ``requires_grad`` when no position is valid (train.py:166-167).
+    With ``norm_weight`` given, ``diff_hidden`` and ``ar_hidden_states`` are the hidden
+    states before the backbone's final norm (model.py:493) and the norm runs inside the
+    op on the selected rows only (it is per row, so selecting first is the same).
     """
     if getattr(lm_head, "bias", None) is not None:
         raise ValueError("lm_head with a bias is not supported (the reference's tied lm_head has none)")
     h_s, h_t, valid = select_rows(diff_hidden, ar_hidden_states, anchor_positions, K, target_ids, pad_token_id)
     if not bool(valid.any()):
         return torch.tensor(0.0, device=diff_hidden.device, requires_grad=True)
+    if norm_weight is not None:
+        return PrenormKLGemmFn.apply(h_s, h_t.detach(), norm_weight, lm_head.weight, valid, float(temperature),
+                                     float(norm_eps), None)
     return KLGemmFn.apply(h_s, h_t.detach(), lm_head.weight, valid, float(temperature), None)

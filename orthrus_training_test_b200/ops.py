@@ -242,3 +242,88 @@ def kl_gemm_loss(h_s: torch.Tensor, h_t: torch.Tensor, weight: torch.Tensor, mas
                  temperature: float = 1.0, count: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Fused forward-KL distillation loss on aligned rows (see :class:`KLGemmFn`)."""
     return KLGemmFn.apply(h_s, h_t, weight, mask, temperature, count)
+
+
+# ----------------------------------------------------------------- final RMSNorm prologue
+
+def _norm_input(x: torch.Tensor) -> Tuple[torch.Tensor, int]:
+    x = x.detach()
+    _require_cuda(x)
+    if x.dtype == torch.bfloat16:
+        return x.contiguous(), 0
+    if x.dtype == torch.float32:
+        return x.contiguous(), 1
+    raise TypeError(f"unsupported dtype {x.dtype} (bf16 or fp32)")
+
+
+def rmsnorm_rows(x: torch.Tensor, gamma: torch.Tensor, eps: float = 1e-5,
+                 want_rstd: bool = True) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """The backbone's final norm (model.py:493, a LlamaRMSNorm) row by row -> bf16 rows.
+
+    ``x [N, H]`` bf16 or fp32, ``gamma [H]`` the norm weight.  Returns ``(y bf16 [N, H],
+    rstd fp32 [N] or None)`` with ``y = gamma * bf16(x r)`` (bf16 x) or ``bf16(gamma * x r)``
+    (fp32 x), ``r = 1 / sqrt(mean(x^2) + eps)``.
+    """
+    xc, f32 = _norm_input(x)
+    dev = xc.device
+    N, H = xc.shape
+    g = gamma.detach().to(device=dev, dtype=torch.float32).contiguous()
+    y = torch.empty(N, H, dtype=torch.bfloat16, device=dev)
+    rstd = torch.empty(N, dtype=torch.float32, device=dev) if want_rstd else None
+    call("klg_rmsnorm_rows", _ptr(xc), f32, _ptr(g), N, H, float(eps), _ptr(y), _ptr(rstd), _stream(dev))
+    return y, rstd
+
+
+def rmsnorm_rows_backward(x: torch.Tensor, gamma: torch.Tensor, rstd: torch.Tensor, dy: torch.Tensor) -> torch.Tensor:
+    """``dx`` fp32 ``[N, H]`` through the norm for ``dy`` fp32 ``[N, H]`` (weight frozen)."""
+    xc, f32 = _norm_input(x)
+    dev = xc.device
+    N, H = xc.shape
+    g = gamma.detach().to(device=dev, dtype=torch.float32).contiguous()
+    dyc = dy.detach().to(torch.float32).contiguous()
+    dx = torch.empty(N, H, dtype=torch.float32, device=dev)
+    call("klg_rmsnorm_rows_bwd", _ptr(xc), f32, _ptr(g), _ptr(rstd), _ptr(dyc), N, H, _ptr(dx), _stream(dev))
+    return dx
+
+
+class PrenormKLGemmFn(torch.autograd.Function):
+    """:class:`KLGemmFn` on pre-norm rows: the backbone's final norm (model.py:493) runs as
+    the op's prologue and its gradient as the epilogue of the backward, so the caller hands
+    over the hidden states before ``self.norm`` and the normed rows exist only inside the op.
+
+    Arguments: ``x_s``, ``x_t`` ``[N, H]`` pre-norm rows (bf16 or fp32; ``x_t`` detached),
+    ``norm_weight [H]`` (frozen, as in the reference, model.py:323-324), ``weight [V, H]``,
+    ``mask [N]``, ``temperature``, ``eps``, ``count``.  dH of the normed rows stays fp32
+    between the loss and the norm's backward.
+    """
+
+    @staticmethod
+    def forward(ctx, x_s, x_t, norm_weight, weight, mask, temperature=1.0, eps=1e-5, count=None):
+        need_dx, need_dw = ctx.needs_input_grad[0], ctx.needs_input_grad[3]
+        ys, rs = rmsnorm_rows(x_s, norm_weight, eps, want_rstd=need_dx)
+        yt, _ = rmsnorm_rows(x_t, norm_weight, eps, want_rstd=False)
+        w = to_compute_dtype(weight)
+        m = mask_u8(mask)
+        ctx.dtypes = (x_s.dtype, weight.dtype)
+        if need_dx or need_dw:
+            loss, _, _, _, dh, dw = kl_fwd_bwd(ys, yt, w, m, temperature, count=count, need_dh=need_dx,
+                                               need_dw=need_dw)
+            dx = rmsnorm_rows_backward(x_s, norm_weight, rs, dh) if need_dx else None
+            ctx.save_for_backward(dx, dw)
+        else:
+            loss, _, _, _ = kl_forward(ys, yt, w, m, temperature, count=count)
+        return loss
+
+    @staticmethod
+    def backward(ctx, g):
+        dx, dw = ctx.saved_tensors
+        g = g.to(torch.float32)
+        return ((dx * g).to(ctx.dtypes[0]) if dx is not None else None, None, None,
+                (dw * g).to(ctx.dtypes[1]) if dw is not None else None, None, None, None, None)
+
+
+def prenorm_kl_loss(x_s: torch.Tensor, x_t: torch.Tensor, norm_weight: torch.Tensor, weight: torch.Tensor,
+                    mask: torch.Tensor, temperature: float = 1.0, eps: float = 1e-5,
+                    count: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Fused loss on pre-norm rows (see :class:`PrenormKLGemmFn`)."""
+    return PrenormKLGemmFn.apply(x_s, x_t, norm_weight, weight, mask, temperature, eps, count)
