@@ -91,3 +91,26 @@ def test_workspace_sizes_bounded():
         assert 0 < ws <= (512 << 20) + HDR
         assert _lib.lib().klg_bwd_chunk_cols(n, v, ws) >= 2048
         assert ws < n * v * 2 / 2
+
+
+def test_sampler_and_norm_argument_validation():
+    L = _lib.lib()
+    keep, p = _buf(1 << 16)
+    seed = ctypes.c_ulonglong(1)
+    ws = L.klg_lm_head_sample_workspace_bytes(32, 49153)
+    assert ws > 0 and ws < 32 * 49153 * 4             # records, never the [N, V] logits
+    assert L.klg_lm_head_sample_workspace_bytes(0, 10) == -1
+    assert L.klg_lm_head_sample_workspace_bytes(10, 0) == -1
+    # null output, misaligned hidden, bad temperature, small workspace
+    assert L.klg_lm_head_sample(p, p, 4, 64, 4, 1.0, 1, seed, None, p, p, p, 1 << 16, None) == _lib.KLG_ERR_ARG
+    assert L.klg_lm_head_sample(p, p, 4, 12, 4, 1.0, 1, seed, p, p, p, p, 1 << 16, None) == _lib.KLG_ERR_ALIGN
+    assert L.klg_lm_head_sample(p, p, 4, 64, 4, 0.0, 1, seed, p, p, p, p, 1 << 16, None) == _lib.KLG_ERR_ARG
+    assert L.klg_lm_head_sample(p, p, 4, 64, 4, 1.0, 1, seed, p, p, p, p, 16, None) == _lib.KLG_ERR_WORKSPACE
+    # final norm: dtype flag, alignment, eps, null buffers
+    assert L.klg_rmsnorm_rows(p, 2, p, 4, 64, 1e-5, p, None, None) == _lib.KLG_ERR_ARG
+    assert L.klg_rmsnorm_rows(p, 0, p, 4, 12, 1e-5, p, None, None) == _lib.KLG_ERR_ALIGN
+    assert L.klg_rmsnorm_rows(p, 0, p, 4, 64, -1.0, p, None, None) == _lib.KLG_ERR_ARG
+    assert L.klg_rmsnorm_rows(p, 0, p, 4, 64, 1e-5, None, None, None) == _lib.KLG_ERR_ALIGN
+    assert L.klg_rmsnorm_rows(None, 0, p, 4, 64, 1e-5, p, None, None) == _lib.KLG_ERR_ARG
+    assert L.klg_rmsnorm_rows_bwd(p, 0, p, None, p, 4, 64, p, None) == _lib.KLG_ERR_ARG
+    del keep
