@@ -60,9 +60,41 @@ EncodeTiledFn encode_fn() {
 
 // 2-D bf16 tensor map, 128-byte (default) or 64-byte swizzle, zero fill out of bounds.
 // inner = contiguous extent (elements), outer = row count, ld = row stride (elements).
+// A map is a pure function of these arguments, so encoded maps are kept in a small cache
+// (round-robin replacement) keyed by all of them: a decode loop re-encodes nothing for its
+// fixed lm_head weight and its reused activation buffers.
+struct MapKey {
+  const void* base;
+  uint64_t inner, outer, ld;
+  uint32_t box_inner, box_outer;
+  int swz, dt;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && inner == o.inner && outer == o.outer && ld == o.ld && box_inner == o.box_inner &&
+           box_outer == o.box_outer && swz == o.swz && dt == o.dt;
+  }
+};
+struct MapCache {
+  static constexpr int kSlots = 64;
+  std::mutex mu;
+  MapKey key[kSlots];
+  CUtensorMap map[kSlots];
+  bool used[kSlots] = {};
+  int next = 0;
+};
+MapCache g_maps;
+
 bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
               uint32_t box_outer, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B,
               CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
+  const MapKey k{base, inner, outer, ld, box_inner, box_outer, (int)swz, (int)dt};
+  {
+    std::lock_guard<std::mutex> lk(g_maps.mu);
+    for (int i = 0; i < MapCache::kSlots; ++i)
+      if (g_maps.used[i] && g_maps.key[i] == k) {
+        *m = g_maps.map[i];
+        return true;
+      }
+  }
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const uint64_t esize = dt == CU_TENSOR_MAP_DATA_TYPE_FLOAT32 ? 4 : 2;
@@ -70,8 +102,16 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, 
   cuuint64_t strides[1] = {ld * esize};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t es[2] = {1, 1};
-  return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  if (fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  std::lock_guard<std::mutex> lk(g_maps.mu);
+  const int i = g_maps.next;
+  g_maps.next = (i + 1) % MapCache::kSlots;
+  g_maps.key[i] = k;
+  g_maps.map[i] = *m;
+  g_maps.used[i] = true;
+  return true;
 }
 
 // Per-launch timing trace (klg_trace_begin / klg_trace_end).
@@ -109,9 +149,12 @@ struct NvtxRange {
 };
 
 int num_sms() {
+  static std::atomic<int> cache[64];   // per device, 0 = not read yet
   int dev = 0, n = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev >= 0 && dev < 64 && (n = cache[dev].load(std::memory_order_relaxed)) > 0) return n;
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+  if (dev >= 0 && dev < 64) cache[dev].store(n, std::memory_order_relaxed);
   return n;
 }
 
@@ -170,7 +213,18 @@ int gemm_bn(long long hidden) {
 
 template <typename Kern>
 cudaError_t set_smem(Kern k, int bytes) {
-  return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  // once per (kernel, device, size): the attribute persists in the context
+  static std::mutex mu;
+  static std::vector<std::tuple<const void*, int, int>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const auto key = std::make_tuple(reinterpret_cast<const void*>(k), dev, bytes);
+  std::lock_guard<std::mutex> lk(mu);
+  if (std::find(done.begin(), done.end(), key) != done.end()) return cudaSuccess;
+  e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.push_back(key);
+  return e;
 }
 
 // Programmatic dependent launch (on unless KLG_PDL=0): each launch may start its set-up
