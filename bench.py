@@ -71,7 +71,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + sorted(SAMPLE_CONFIGS), default="c2")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + sorted(SAMPLE_CONFIGS) + sorted(ATTN_CONFIGS), default="c2")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="time budget of the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -403,12 +403,164 @@ def run_sample(args):
     })
 
 
+# ----------------------------------------------------------------------------- block-diffusion attention
+ATTN_METRIC = "diffusion-attention query rows/sec"
+# batch, heads, kv heads, block K, diffusion length, AR length, description (one layer, SmolLM2-135M heads)
+ATTN_CONFIGS = {
+    "a1": (1, 9, 3, 32, 32, 2048, "decode: one K=32 block over a 2048-token AR cache (generate.py:149-176), "
+                                  "9 heads / 3 KV heads, head_dim 64, per layer"),
+    "a2": (4, 9, 3, 32, 2048, 2048, "training diffusion pass: 4 x 64 blocks of 32, each over the AR prefix "
+                                    "before its anchor (model.py:400-446), per layer"),
+}
+
+
+def run_attn(args):
+    """One step = one layer's diffusion attention (model.py:136-176) over the config's
+    queries: the fused kernel against torch SDPA with the same boolean mask on the same GPU,
+    and the float64 oracle on the host."""
+    import torch
+    import torch.nn.functional as F
+
+    from oracle import klgemm_oracle as O
+    from orthrus_training_test_b200 import _lib
+    from orthrus_training_test_b200.attention import block_attention, workspace_bytes
+
+    B, H, Hkv, K, Ld, AL, desc = ATTN_CONFIGS[args.config]
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1 or args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) == 0:
+            emit({"metric": ATTN_METRIC, "impl": args.impl, "unavailable":
+                  "attention workloads run on one GPU; the reference arm is the SDPA line inside ours"})
+        return
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    g = torch.Generator().manual_seed(3)
+    bf = lambda *sh: torch.randn(*sh, generator=g).to(torch.bfloat16).to(dev)
+    q, ks, vs, ka, va = bf(B, H, Ld, 64), bf(B, Hkv, Ld, 64), bf(B, Hkv, Ld, 64), bf(B, Hkv, AL, 64), bf(B, Hkv, AL, 64)
+    if Ld == K:
+        lim = torch.full((B, Ld), AL - 1, dtype=torch.int32)
+    else:
+        anchors = torch.randint(1, AL, (B, Ld // K), generator=g).sort(dim=1).values
+        lim = (anchors - 1).repeat_interleave(K, dim=1).to(torch.int32)
+    lim_d = lim.to(dev)
+    ws = torch.empty(workspace_bytes(B, H, Hkv, Ld, K, AL), dtype=torch.uint8, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    # SDPA comparison: keys [AR ; own diffusion keys], boolean mask of the same visibility
+    kv_idx = torch.arange(AL + Ld, device=dev)
+    q_blk = torch.arange(Ld, device=dev) // K
+    vis_ar = kv_idx[None, None, :AL] <= lim_d.long()[:, :, None]
+    vis_self = (q_blk[:, None] == (kv_idx[AL:] - AL)[None, :] // K)[None].expand(B, -1, -1)
+    mask = torch.cat([vis_ar, vis_self], dim=2)[:, None]               # [B, 1, Ld, AL + Ld]
+    k_full, v_full = torch.cat([ka, ks], dim=2), torch.cat([va, vs], dim=2)
+
+    def ours():
+        return block_attention(q, ks, vs, ka, va, lim_d, K, workspace=ws)
+
+    def sdpa():
+        return F.scaled_dot_product_attention(q, k_full, v_full, attn_mask=mask, enable_gqa=True)
+
+    for _ in range(args.warmup):
+        ours(), sdpa()
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    sampler = ClockSampler(0)
+    sampler.start()
+    time.sleep(0.3)
+    launches0 = _lib.launch_count()
+    ms = _timed(ours, args.steps, flush)
+    launches = _lib.launch_count() - launches0
+    clocks = sampler.stop()
+    ms_sdpa = _timed(sdpa, args.steps, flush)
+    _lib.trace_begin(4096)
+    for _ in range(args.steps):
+        flush.zero_()
+        ours()
+    torch.cuda.synchronize()
+    trace = _lib.trace_end(4096)
+    assert _lib.device_status() == 0
+    by_kind = {}
+    for kind, t in trace:
+        by_kind.setdefault(kind, [0.0, 0])
+        by_kind[kind][0] += t
+        by_kind[kind][1] += 1
+    tot = sum(v[0] for v in by_kind.values())
+    kernels = {k: {"launches": n, "total_ms": t, "share": t / tot} for k, (t, n) in by_kind.items()}
+    k_avg = by_kind["attn"][0] / by_kind["attn"][1]
+    # algorithmic work: every visible (query, key) pair costs 2 x 64 MACs (Q K and P V)
+    visible = float((lim.clamp(-1, AL - 1).long() + 1).sum()) * H + B * H * Ld * K
+    flops = 4.0 * 64 * visible
+    # bytes: Q + O + the KV rows a unit reads (AR prefix up to its block's largest limit, own keys)
+    lim_blk = lim.clamp(-1, AL - 1).long().view(B, Ld // K, K).amax(dim=2) + 1
+    kv_rows = float(lim_blk.sum()) * Hkv + B * Hkv * Ld
+    bytes_alg = 2.0 * B * H * Ld * 64 * 2 + kv_rows * 64 * 2 * 2
+    hbm_peak, hbm_src = load_hbm_peak()
+    peak_burst, _, peak_src = load_peaks()
+    if bytes_alg / (hbm_peak * 1e9) >= flops / (peak_burst * 1e12):
+        ach = bytes_alg / (k_avg / 1e3) / 1e9
+        roofline = {"bound": "hbm", "kernel": "attn", "achieved": ach, "peak": hbm_peak, "unit": "GB/s",
+                    "frac": ach / hbm_peak, "traffic": load_traffic("attn", args.config),
+                    "peak_kind": f"{hbm_src} copy bandwidth", "algorithmic_bytes_per_launch": bytes_alg}
+    else:
+        ach = flops / (k_avg / 1e3) / 1e12
+        roofline = {"bound": "tensor", "kernel": "attn", "achieved": ach, "peak": peak_burst, "unit": "TFLOP/s",
+                    "frac": ach / peak_burst, "traffic": load_traffic("attn", args.config),
+                    "peak_kind": f"{peak_src} burst bf16", "algorithmic_flops_per_launch": flops}
+    # e2e: q and the diffusion keys / values from pinned host memory, the output back to the host
+    q_h, ks_h, vs_h = q.cpu().pin_memory(), ks.cpu().pin_memory(), vs.cpu().pin_memory()
+    out_h = torch.empty(B, H, Ld, 64, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        o = block_attention(q_h.to(dev, non_blocking=True), ks_h.to(dev, non_blocking=True),
+                            vs_h.to(dev, non_blocking=True), ka, va, lim_d, K, workspace=ws)
+        out_h.copy_(o, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for _ in range(3):
+        e2e_step()
+    e_ms = _timed(e2e_step, args.steps, flush)
+    cpu = None
+    if not args.no_cpu_baseline:
+        nb = 1
+        sl = slice(0, nb * K)
+        qs = q[:1, :, sl].float().cpu().numpy()
+        t_end = time.perf_counter() + min(args.cpu_seconds, 10.0)
+        times = []
+        while True:
+            t0 = time.perf_counter()
+            O.block_attention_np(qs, ks[:1, :, sl].float().cpu().numpy(), vs[:1, :, sl].float().cpu().numpy(),
+                                 ka[:1].float().cpu().numpy(), va[:1].float().cpu().numpy(), lim[:1, sl].numpy(), K)
+            times.append(time.perf_counter() - t0)
+            if time.perf_counter() > t_end and len(times) >= 2:
+                break
+        cpu = {"value": H * K / statistics.median(times), "unit": "rows/s", "cores": 1, "kind": "port",
+               "sample": f"one block of {K} positions x {H} heads over its AR prefix: the float64 oracle"}
+    rows = B * H * Ld
+    total = sum(ms)
+    emit({
+        "metric": ATTN_METRIC, "value": rows * args.steps / (total / 1e3), "unit": "rows/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) q, k, v)",
+        "config": {"workload": f"{args.config}: {desc}", "batch": B, "heads": H, "kv_heads": Hkv, "block": K,
+                   "diff_len": Ld, "ar_len": AL, "parallelism": "single GPU", "l2": "flushed between steps (256 MiB write)"},
+        "sdpa_ms_per_step": sum(ms_sdpa) / args.steps,
+        "sdpa_what": "torch scaled_dot_product_attention with the same boolean mask and GQA, same GPU",
+        "roofline": roofline, "kernels": kernels, "gpu_launches": int(launches),
+        "e2e": {"value": rows * args.steps / (sum(e_ms) / 1e3), "unit": "rows/s",
+                "h2d_bytes_per_step": int((q_h.numel() + ks_h.numel() + vs_h.numel()) * 2),
+                "d2h_bytes_per_step": int(out_h.numel() * 2), "ms_per_step": sum(e_ms) / args.steps,
+                "api": "attention.block_attention"},
+        "cpu_baseline": cpu, "clocks": clocks,
+    })
+
+
 # ----------------------------------------------------------------------------- our arm
 def main():
     args = parse()
     _claim_stdout()
     if args.config in SAMPLE_CONFIGS:
         run_sample(args)
+        return
+    if args.config in ATTN_CONFIGS:
+        run_attn(args)
         return
     if args.impl == "reference":
         run_reference_arm(args)

@@ -197,6 +197,23 @@ int klg_rmsnorm_rows(const void* x, int x_f32, const float* gamma, int64_t n_row
 int klg_rmsnorm_rows_bwd(const void* x, int x_f32, const float* gamma, const float* rstd, const float* dy,
                          int64_t n_rows, int64_t hidden, float* dx, void* stream);
 
+/* ---------------------------------------------------------------- block-diffusion attention
+ * The diffusion heads' attention (reference model.py:45-96 flex block mask, score_mod
+ * model.py:435-446; the broken Triton version triton_kernels.py:18-83, API
+ * triton_kernels.py:281-290), forward only: for query position p of block p / K, keys are
+ * the AR cache rows 0..limits[b, p] (clamped to ar_len - 1; -1 = none) and the K rows of
+ * its own block, scores scaled by `scale`, GQA (head h uses KV head h / (H / Hkv)).
+ *   q [B, H, Ld, 64], k_self / v_self [B, Hkv, Ld, 64] (bf16, contiguous),
+ *   k_ar / v_ar: rows 0..ar_len-1 of a [B, Hkv, ar_stride, 64] bf16 cache,
+ *   limits [B, Ld] int32; out [B, H, Ld, 64] bf16; lse [B, H, Ld] fp32 natural log (may be NULL).
+ * head_dim 64; K a multiple of 16, <= 128; Ld a multiple of K. */
+int64_t klg_block_attn_workspace_bytes(int64_t batch, int64_t heads, int64_t kv_heads, int64_t diff_len,
+                                       int64_t block, int64_t ar_len, int64_t head_dim);
+int klg_block_attn_fwd(const void* q, const void* k_self, const void* v_self, const void* k_ar, const void* v_ar,
+                       int64_t ar_stride, const int32_t* limits, int64_t batch, int64_t heads, int64_t kv_heads,
+                       int64_t diff_len, int64_t block, int64_t ar_len, int64_t head_dim, float scale, void* out,
+                       float* lse, void* workspace, int64_t workspace_bytes, void* stream);
+
 /* fp32 -> bf16 conversion (round to nearest even) for fp32 callers. */
 int klg_cast_f32_bf16(const float* in, void* out, int64_t n, void* stream);
 
@@ -216,6 +233,7 @@ int klg_cast_f32_bf16(const float* in, void* out, int64_t n, void* stream);
 #define KLG_KIND_ZERO 8      /* pass 2: zeroing of the fp32 dW / dH buffers            */
 #define KLG_KIND_SAMPLE 9    /* inference: lm_head logits -> argmax / Gumbel-max sample   */
 #define KLG_KIND_NORM 10     /* final RMSNorm of pre-norm rows, forward or backward       */
+#define KLG_KIND_ATTN 11     /* block-diffusion attention, forward                        */
 int klg_trace_begin(int capacity);
 int klg_trace_end(int* kinds, float* ms, int capacity, int* n);
 

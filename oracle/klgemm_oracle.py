@@ -582,3 +582,44 @@ def prenorm_kl_loss_np(x_s, x_t, gamma, W, mask, temperature: float = 1.0, eps: 
     yt, _ = rmsnorm_np(x_t, gamma, eps, bf16_input=False)
     loss, dh, _, _, _, _ = aligned_kl_loss_np(ys, yt, W, mask, temperature)
     return loss, rmsnorm_backward_np(x_s, gamma, rs, dh)
+
+
+# --------------------------------------------------------------------------
+# Block-diffusion attention (reference model.py:45-96, 435-446; flex_attention semantics)
+# --------------------------------------------------------------------------
+
+def block_attention_np(q, k_self, v_self, k_ar, v_ar, limits, K: int, scale: Optional[float] = None):
+    """float64 restatement.  Query position p of block p // K attends to AR keys
+    ``0..limits[b, p]`` (clipped to the cache; below 0: none) and to the K keys of its own
+    block; GQA head h reads KV head ``h // (H / Hkv)``; scores scaled by ``scale``
+    (default ``1/sqrt(D)``).  Returns ``(out [B, H, Ld, D], lse [B, H, Ld])``, lse in
+    natural log."""
+    q = np.asarray(q, np.float64)
+    ks, vs = np.asarray(k_self, np.float64), np.asarray(v_self, np.float64)
+    ka, va = np.asarray(k_ar, np.float64), np.asarray(v_ar, np.float64)
+    lim = np.asarray(limits)
+    B, H, Ld, D = q.shape
+    Hkv, AL = ks.shape[1], ka.shape[2]
+    ng = H // Hkv
+    sc = 1.0 / math.sqrt(D) if scale is None else scale
+    out = np.zeros((B, H, Ld, D))
+    lse = np.zeros((B, H, Ld))
+    ar_idx = np.arange(AL)
+    for b in range(B):
+        for h in range(H):
+            hk = h // ng
+            for blk in range(Ld // K):
+                rows = slice(blk * K, (blk + 1) * K)
+                qq = q[b, h, rows]                                   # [K, D]
+                s_ar = qq @ ka[b, hk].T * sc                         # [K, AL]
+                s_self = qq @ ks[b, hk, rows].T * sc                 # [K, K]
+                vis = ar_idx[None, :] <= np.clip(lim[b, rows], -1, AL - 1)[:, None]
+                s_ar = np.where(vis, s_ar, -np.inf)
+                s = np.concatenate([s_ar, s_self], axis=1)
+                m = s.max(axis=1, keepdims=True)
+                e = np.exp(s - m)
+                z = e.sum(axis=1, keepdims=True)
+                vv = np.concatenate([va[b, hk], vs[b, hk, rows]], axis=0)
+                out[b, h, rows] = (e / z) @ vv
+                lse[b, h, rows] = (m + np.log(z))[:, 0]
+    return out, lse

@@ -1,0 +1,329 @@
+// Block-diffusion attention, forward (inference), sm_100a.
+//
+// The reference's diffusion heads attend, for a query at diffusion position q of block
+// q / K, to the AR key/value cache up to the query's causal limit (kv <= limit[b, q]) and to
+// the K keys of their own block, bidirectionally (model.py:64-96 block mask + model.py:
+// 435-446 score_mod, through flex_attention with GQA, model.py:45-58; the Triton version,
+// triton_kernels.py:18-83, is marked broken).  Scores are scaled by 1 / sqrt(D).
+//
+// One CTA takes a unit (batch b, KV head, group of hg query heads sharing it, block) and a
+// split of the AR key range.  Its queries -- hg heads x K positions <= 128 rows, zero rows
+// after -- stay in shared memory; key tiles (128 AR keys, or the block's own K keys) stream
+// through a TMA ring.  Per tile: S = Q K^T (tcgen05, M = 128, N = keys, K = 64) into one of
+// two TMEM buffers; four softmax warps (one TMEM lane each row) take the masked online max /
+// sum in log2 units and write P = 2^(s - m) as bf16 into a 128-byte-swizzled K-major shared
+// tile; O_tile = P V (M = 128, N = 64, K = keys; V read MN-major) lands in TMEM and is
+// accumulated with the running rescale in registers.  Each CTA writes its rows' (O, m, l)
+// record; block_attn_merge_kernel combines the splits and writes bf16 O and the natural-log
+// log-sum-exp.
+#pragma once
+#include "klg_kernels.cuh"
+
+namespace klg {
+
+constexpr int ATT_D = 64;                              // head dimension
+constexpr int ATT_BN = 128;                            // AR keys per tile
+constexpr int ATT_STAGES = 3;
+constexpr int ATT_TILE_BYTES = ATT_BN * ATT_D * 2;     // K or V tile, 16 KB
+constexpr int ATT_Q_BYTES = 128 * ATT_D * 2;           // 16 KB
+constexpr int ATT_P_BYTES = 128 * ATT_BN * 2;          // two 64-key K-major sub-tiles, 32 KB
+constexpr int ATT_THREADS = 192;                       // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
+constexpr int ATT_SMEM = 1024 + ATT_Q_BYTES + ATT_P_BYTES + ATT_STAGES * 2 * ATT_TILE_BYTES + 256;
+constexpr int ATT_TMEM_COLS = 512;                     // S: 2 x 128 columns; O tile: 64 columns at 256
+constexpr int ATT_O_COL = 256;
+
+struct AttnArgs {
+  const int* limits;   // [B, Ld] causal limit per query position (AR keys 0..limit)
+  float* part_o;       // [n_cta][128][64] unnormalised O per split
+  float* part_ml;      // [n_cta][2][128] (m in log2 units, l)
+  int B, H, Hkv, Ld, K, ar_len;
+  int ng, hg, n_hg, nb;   // query heads per KV head, per unit; head groups; blocks
+  int n_units, splits, tps;   // tps: AR tiles per split
+  float sl2;                  // scale * log2(e)
+};
+
+__device__ __forceinline__ void attn_unit(const AttnArgs& a, int u, int& b, int& hkv, int& hgi, int& blk) {
+  blk = u % a.nb;
+  int r = u / a.nb;
+  hgi = r % a.n_hg;
+  r /= a.n_hg;
+  hkv = r % a.Hkv;
+  b = r / a.Hkv;
+}
+
+__global__ void __launch_bounds__(ATT_THREADS, 1)
+block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_ks,
+                  const __grid_constant__ CUtensorMap map_vs, const __grid_constant__ CUtensorMap map_ka,
+                  const __grid_constant__ CUtensorMap map_va, const AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  __shared__ int s_maxlim;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t q_s = smem_u32(smem);
+  const uint32_t p_s = q_s + ATT_Q_BYTES;
+  const uint32_t st_s = p_s + ATT_P_BYTES;   // stage j: K tile at st_s + 2j * TILE, V tile right after
+  const uint32_t bar0 = st_s + ATT_STAGES * 2 * ATT_TILE_BYTES;
+  const uint32_t full0 = bar0;                        // [STAGES] TMA bytes of K + V
+  const uint32_t empty0 = bar0 + 8u * ATT_STAGES;     // [STAGES] P V of the stage retired
+  const uint32_t qbar = bar0 + 16u * ATT_STAGES;      // queries landed
+  const uint32_t sfull0 = qbar + 8u;                  // [2] S tile in TMEM
+  const uint32_t sempty0 = sfull0 + 16u;              // [2] softmax warps read the S tile
+  const uint32_t pfull = sempty0 + 16u;               // P written to shared memory
+  const uint32_t ofull = pfull + 8u;                  // O tile in TMEM
+  const uint32_t oempty = ofull + 8u;                 // softmax warps read the O tile
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int u = blockIdx.x / a.splits;
+  const int sp = blockIdx.x - u * a.splits;
+  int b, hkv, hgi, blk;
+  attn_unit(a, u, b, hkv, hgi, blk);
+  const int rows = a.hg * a.K;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    s_maxlim = -1;
+    for (int s = 0; s < ATT_STAGES; ++s) {
+      mbar_init(full0 + 8u * s, 1);
+      mbar_init(empty0 + 8u * s, 1);
+    }
+    mbar_init(qbar, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(sfull0 + 8u * s, 1);
+      mbar_init(sempty0 + 8u * s, 4);
+    }
+    mbar_init(pfull, 4);
+    mbar_init(ofull, 1);
+    mbar_init(oempty, 4);
+    fence_mbar_init();
+    tma_prefetch(&map_q);
+    tma_prefetch(&map_ks);
+    tma_prefetch(&map_vs);
+    tma_prefetch(&map_ka);
+    tma_prefetch(&map_va);
+  }
+  // query rows past the unit's rows: zeros (their S / P rows are formed and never read)
+  for (int i = threadIdx.x; i < (128 - rows) * 8; i += blockDim.x) st_shared_v4(q_s + rows * 128 + i * 16, 0, 0, 0, 0);
+  fence_async_shared();
+  if (warp == 1) tmem_alloc(smem_u32(&tmem_slot), ATT_TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_enter();   // inputs of this launch are complete from here on
+  if (threadIdx.x < a.K) atomicMax(&s_maxlim, a.limits[(size_t)b * a.Ld + blk * a.K + threadIdx.x]);
+  __syncthreads();
+  const uint32_t tmem = tmem_slot;
+  volatile int* abort_p = &abort_flag;
+  const int maxlim = min(s_maxlim, a.ar_len - 1);
+  const int n_ar = maxlim < 0 ? 0 : maxlim / ATT_BN + 1;   // AR tiles holding keys 0..maxlim
+  const int t0 = sp * a.tps;
+  const int n_my = max(0, min(t0 + a.tps, n_ar) - t0);
+  const int ntiles = n_my + (sp == a.splits - 1 ? 1 : 0);   // the last split also takes the block's own keys
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (whole warp)
+    int stage = 0;
+    uint32_t phase = 0;
+    long long issued = 0;
+    if (elect_one()) {
+      mbar_arrive_expect_tx(qbar, (uint32_t)rows * 128u);
+      for (int i = 0; i < a.hg; ++i) {
+        const int h = hkv * a.ng + hgi * a.hg + i;
+        tma_load_2d(q_s + i * a.K * 128, &map_q, qbar, 0, (b * a.H + h) * a.Ld + blk * a.K);
+      }
+    }
+    __syncwarp();
+    for (int i = 0; i < ntiles; ++i) {
+      if (!warp_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) break;
+      if (elect_one()) {
+        const uint32_t ks = st_s + stage * 2 * ATT_TILE_BYTES;
+        const uint32_t fb = full0 + 8u * stage;
+        if (i < n_my) {
+          mbar_arrive_expect_tx(fb, 2 * ATT_TILE_BYTES);
+          tma_load_3d(ks, &map_ka, fb, 0, (t0 + i) * ATT_BN, b * a.Hkv + hkv);
+          tma_load_3d(ks + ATT_TILE_BYTES, &map_va, fb, 0, (t0 + i) * ATT_BN, b * a.Hkv + hkv);
+        } else {
+          mbar_arrive_expect_tx(fb, (uint32_t)(2 * a.K * 128));
+          const int row = (b * a.Hkv + hkv) * a.Ld + blk * a.K;
+          tma_load_2d(ks, &map_ks, fb, 0, row);
+          tma_load_2d(ks + ATT_TILE_BYTES, &map_vs, fb, 0, row);
+        }
+      }
+      __syncwarp();
+      ++issued;
+      if (++stage == ATT_STAGES) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+    if (lane == 0) {
+      drain_loads<ATT_STAGES>(full0, stage, phase, issued);
+      mbar_wait_drain(qbar, 0);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (whole warp)
+    bool ok = warp_wait(qbar, 0, abort_p, KLG_STATUS_TIMEOUT_MMA);
+    tc_fence_after();
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int i = 0; ok && i < ntiles; ++i) {
+      const int nk = i < n_my ? ATT_BN : a.K;
+      const int sb = i & 1;
+      if (!warp_wait(full0 + 8u * stage, phase, abort_p, KLG_STATUS_TIMEOUT_MMA)) break;
+      if (!warp_wait(sempty0 + 8u * sb, ((uint32_t)(i >> 1) & 1u) ^ 1u, abort_p, KLG_STATUS_TIMEOUT_MMA)) break;
+      tc_fence_after();
+      const uint32_t ks = st_s + stage * 2 * ATT_TILE_BYTES;
+      if (elect_one()) {
+        const uint32_t idesc = make_idesc_bf16(128, nk, false, false);
+#pragma unroll
+        for (int k = 0; k < ATT_D / 16; ++k)
+          mma_bf16(tmem + sb * ATT_BN, desc_kmajor(q_s, k), desc_kmajor(ks, k), idesc, k != 0);
+        mma_commit(sfull0 + 8u * sb);
+      }
+      __syncwarp();
+      if (!warp_wait(pfull, (uint32_t)i & 1u, abort_p, KLG_STATUS_TIMEOUT_MMA)) break;
+      if (!warp_wait(oempty, ((uint32_t)i & 1u) ^ 1u, abort_p, KLG_STATUS_TIMEOUT_MMA)) break;
+      tc_fence_after();
+      if (elect_one()) {
+        const uint32_t idesc = make_idesc_bf16(128, ATT_D, false, true);
+        for (int k = 0; k < nk / 16; ++k)
+          mma_bf16(tmem + ATT_O_COL, desc_kmajor(p_s + (k >> 2) * 16384, k & 3),
+                   desc_mnmajor(ks + ATT_TILE_BYTES, k), idesc, k != 0);
+        mma_commit(ofull);
+        mma_commit(empty0 + 8u * stage);
+      }
+      __syncwarp();
+      if (++stage == ATT_STAGES) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax warps (one row per thread)
+    const int q4 = warp & 3;   // TMEM lane quarter of this warp
+    const int r = q4 * 32 + lane;
+    const int pos = r % a.K;
+    const int lim = r < rows ? min(max(a.limits[(size_t)b * a.Ld + blk * a.K + pos], -1), a.ar_len - 1) : -1;
+    const uint32_t lrow = tmem + ((uint32_t)(q4 * 32) << 16);
+    const uint32_t prow = p_s + (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u;
+    float m = NEG_BIG, l = 0.f;
+    float o[ATT_D];
+#pragma unroll
+    for (int j = 0; j < ATT_D; ++j) o[j] = 0.f;
+    bool ok = true;
+    for (int i = 0; ok && i < ntiles; ++i) {
+      const bool self = i >= n_my;
+      const int nk = self ? a.K : ATT_BN;
+      const int kmax = self ? a.K - 1 : lim - (t0 + i) * ATT_BN;   // last visible key of the tile
+      const int sb = i & 1;
+      if (!mbar_wait(sfull0 + 8u * sb, (uint32_t)(i >> 1) & 1u, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int nch = (nk + 31) >> 5;
+      float tmax = -INFINITY;
+      for (int c = 0; c < nch; ++c) {
+        uint32_t v[32];
+        tmem_ld32_raw(lrow + sb * ATT_BN + c * 32, v);
+        tmem_wait_ld_regs(v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) tmax = fmaxf(tmax, c * 32 + j <= kmax ? __uint_as_float(v[j]) * a.sl2 : -INFINITY);
+      }
+      const float mn = fmaxf(m, tmax);
+      const float alpha = ex2(m - mn);
+      float sum = 0.f;
+      for (int c = 0; c < nch; ++c) {
+        uint32_t v[32];
+        tmem_ld32_raw(lrow + sb * ATT_BN + c * 32, v);
+        tmem_wait_ld_regs(v);
+        float p[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          p[j] = c * 32 + j <= kmax ? ex2(fmaf(__uint_as_float(v[j]), a.sl2, -mn)) : 0.f;
+          sum += p[j];
+        }
+#pragma unroll
+        for (int q8 = 0; q8 < 4; ++q8) {
+          const int chunk = c * 4 + q8;   // 8 keys = 16 bytes; 8 chunks per 64-key sub-tile row
+          if (chunk * 8 < nk) {
+            const uint32_t addr = prow + (uint32_t)(chunk >> 3) * 16384u + (uint32_t)(((chunk & 7) ^ (r & 7)) << 4);
+            st_shared_v4(addr, pack_bf16x2(p[8 * q8], p[8 * q8 + 1]), pack_bf16x2(p[8 * q8 + 2], p[8 * q8 + 3]),
+                         pack_bf16x2(p[8 * q8 + 4], p[8 * q8 + 5]), pack_bf16x2(p[8 * q8 + 6], p[8 * q8 + 7]));
+          }
+        }
+      }
+      l = fmaf(l, alpha, sum);
+      m = mn;
+      tc_fence_before();
+      fence_async_shared();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(sempty0 + 8u * sb);
+        mbar_arrive(pfull);
+      }
+      if (!mbar_wait(ofull, (uint32_t)i & 1u, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t v0[32], v1[32];
+      tmem_ld32_raw(lrow + ATT_O_COL, v0);
+      tmem_ld32_raw(lrow + ATT_O_COL + 32, v1);
+      tmem_wait_ld_regs(v0, v1);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        o[j] = fmaf(o[j], alpha, __uint_as_float(v0[j]));
+        o[32 + j] = fmaf(o[32 + j], alpha, __uint_as_float(v1[j]));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(oempty);
+    }
+    // this split's record for the row (also written when the split had no tiles or gave up)
+    float4* po = reinterpret_cast<float4*>(a.part_o + ((size_t)blockIdx.x * 128 + r) * ATT_D);
+#pragma unroll
+    for (int j = 0; j < ATT_D / 4; ++j)
+      po[j] = ok ? make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]) : make_float4(0.f, 0.f, 0.f, 0.f);
+    a.part_ml[(size_t)blockIdx.x * 256 + r] = m;
+    a.part_ml[(size_t)blockIdx.x * 256 + 128 + r] = ok ? l : 0.f;
+  }
+  tc_fence_before();
+  __syncthreads();   // every MMA retired (the softmax warps consumed the last O tile) before TMEM is freed
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, ATT_TMEM_COLS);
+}
+
+// Combines the splits of each unit row: O = sum_s O_s 2^(m_s - M) / sum_s l_s 2^(m_s - M),
+// written as bf16 to out [B, H, Ld, 64]; lse [B, H, Ld] = (M + log2 L) ln 2.  One warp per
+// row, two head-dimension columns per lane.
+__global__ void __launch_bounds__(256) block_attn_merge_kernel(const AttnArgs a, __nv_bfloat16* __restrict__ out,
+                                                              float* __restrict__ lse) {
+  pdl_enter();
+  const int rows = a.hg * a.K;
+  const long long gw = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (gw >= (long long)a.n_units * rows) return;
+  const int u = (int)(gw / rows);
+  const int r = (int)(gw - (long long)u * rows);
+  int b, hkv, hgi, blk;
+  attn_unit(a, u, b, hkv, hgi, blk);
+  float M = NEG_BIG;
+  for (int s = 0; s < a.splits; ++s) M = fmaxf(M, a.part_ml[(size_t)(u * a.splits + s) * 256 + r]);
+  float L = 0.f, o0 = 0.f, o1 = 0.f;
+  for (int s = 0; s < a.splits; ++s) {
+    const size_t c = (size_t)(u * a.splits + s);
+    const float w = ex2(a.part_ml[c * 256 + r] - M);
+    L = fmaf(a.part_ml[c * 256 + 128 + r], w, L);
+    const float2 v = reinterpret_cast<const float2*>(a.part_o + (c * 128 + r) * ATT_D)[lane];
+    o0 = fmaf(v.x, w, o0);
+    o1 = fmaf(v.y, w, o1);
+  }
+  const int h = hkv * a.ng + hgi * a.hg + r / a.K;
+  const size_t row = ((size_t)b * a.H + h) * a.Ld + blk * a.K + r % a.K;
+  const float inv = 1.0f / L;
+  reinterpret_cast<uint32_t*>(out + row * ATT_D)[lane] = pack_bf16x2(o0 * inv, o1 * inv);
+  if (lse && lane == 0) lse[row] = (M + __log2f(L)) * 0.69314718055994530942f;
+}
+
+}  // namespace klg

@@ -23,6 +23,7 @@
 #include <nvtx3/nvToolsExt.h>   // header-only; ranges are free unless a profiler is attached
 
 #include "klg_kernels.cuh"
+#include "klg_attn.cuh"
 #include "klgemm.h"
 
 namespace {
@@ -112,6 +113,21 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer, 
   g_maps.map[i] = *m;
   g_maps.used[i] = true;
   return true;
+}
+
+// 3-D bf16 tensor map {inner, mid, outer} with row strides in elements, 128-byte swizzle,
+// zero fill past every extent (not cached: encoded once per call).
+bool make_map_3d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t mid, uint64_t outer, uint64_t ld_mid,
+                 uint64_t ld_outer, uint32_t box_inner, uint32_t box_mid) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {inner, mid, outer};
+  cuuint64_t strides[2] = {ld_mid * 2, ld_outer * 2};
+  cuuint32_t box[3] = {box_inner, box_mid, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // Per-launch timing trace (klg_trace_begin / klg_trace_end).
@@ -1011,6 +1027,101 @@ int klg_rmsnorm_rows_bwd(const void* x, int x_f32, const float* gamma, const flo
                            dx);
   trace_post(slot, s, KLG_KIND_NORM);
   if (e != cudaSuccess) return cuda_fail(e, "launch rmsnorm_rows_bwd_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
+// ---------------------------------------------------------------- block-diffusion attention
+namespace {
+struct AttnPlan {
+  klg::AttnArgs a;
+  int64_t ws_bytes;
+};
+
+int attn_plan(int64_t B, int64_t H, int64_t Hkv, int64_t Ld, int64_t K, int64_t ar_len, int64_t head_dim,
+              AttnPlan& P) {
+  if (B < 1 || H < 1 || Hkv < 1 || Ld < 1 || K < 1 || ar_len < 1)
+    return fail(KLG_ERR_ARG, "bad attention shape B=%lld H=%lld Hkv=%lld Ld=%lld K=%lld ar_len=%lld", (long long)B,
+                (long long)H, (long long)Hkv, (long long)Ld, (long long)K, (long long)ar_len);
+  if (head_dim != klg::ATT_D) return fail(KLG_ERR_ARG, "head_dim=%lld: only 64 is built", (long long)head_dim);
+  if (K % 16 != 0 || K > 128) return fail(KLG_ERR_ARG, "block size K=%lld must be a multiple of 16 and <= 128", (long long)K);
+  if (Ld % K != 0) return fail(KLG_ERR_ARG, "diffusion length %lld is not a multiple of K=%lld", (long long)Ld, (long long)K);
+  if (H % Hkv != 0) return fail(KLG_ERR_ARG, "H=%lld is not a multiple of Hkv=%lld", (long long)H, (long long)Hkv);
+  if (B * H * Ld > (1ll << 31) || ar_len > (1 << 24) || B * Hkv > (1 << 20))
+    return fail(KLG_ERR_ARG, "attention shape too large");
+  klg::AttnArgs& a = P.a;
+  a = klg::AttnArgs{};
+  a.B = (int)B; a.H = (int)H; a.Hkv = (int)Hkv; a.Ld = (int)Ld; a.K = (int)K; a.ar_len = (int)ar_len;
+  a.ng = (int)(H / Hkv);
+  a.hg = 1;
+  for (int d = 1; d <= a.ng; ++d)
+    if (a.ng % d == 0 && d * a.K <= 128) a.hg = d;
+  a.n_hg = a.ng / a.hg;
+  a.nb = (int)(Ld / K);
+  a.n_units = a.B * a.Hkv * a.n_hg * a.nb;
+  const int n_ar = cdiv(ar_len, klg::ATT_BN);
+  // few units (decode): split the AR keys so that about two CTAs per SM exist
+  int splits = cdiv(2 * num_sms(), a.n_units);
+  splits = std::max(1, std::min(splits, n_ar));
+  a.tps = cdiv(n_ar, splits);
+  a.splits = cdiv(n_ar, a.tps);
+  const int64_t n_cta = (int64_t)a.n_units * a.splits;
+  P.ws_bytes = n_cta * 128 * (klg::ATT_D + 2) * 4;
+  return KLG_OK;
+}
+}  // namespace
+
+int64_t klg_block_attn_workspace_bytes(int64_t batch, int64_t heads, int64_t kv_heads, int64_t diff_len,
+                                       int64_t block, int64_t ar_len, int64_t head_dim) {
+  AttnPlan P;
+  if (attn_plan(batch, heads, kv_heads, diff_len, block, ar_len, head_dim, P)) return -1;
+  return P.ws_bytes;
+}
+
+int klg_block_attn_fwd(const void* q, const void* k_self, const void* v_self, const void* k_ar, const void* v_ar,
+                       int64_t ar_stride, const int32_t* limits, int64_t batch, int64_t heads, int64_t kv_heads,
+                       int64_t diff_len, int64_t block, int64_t ar_len, int64_t head_dim, float scale, void* out,
+                       float* lse, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!q || !k_self || !v_self || !k_ar || !v_ar || !limits || !out) return fail(KLG_ERR_ARG, "null pointer");
+  AttnPlan P;
+  int rc = attn_plan(batch, heads, kv_heads, diff_len, block, ar_len, head_dim, P);
+  if (rc) return rc;
+  if (ar_stride < ar_len) return fail(KLG_ERR_ARG, "ar_stride %lld < ar_len %lld", (long long)ar_stride, (long long)ar_len);
+  if (!(scale > 0.f) || !std::isfinite(scale)) return fail(KLG_ERR_ARG, "scale must be finite and > 0");
+  for (const void* p : {q, k_self, v_self, k_ar, v_ar, (const void*)out})
+    if (!aligned16(p)) return fail(KLG_ERR_ALIGN, "q/k/v/out must be 16-byte aligned");
+  if (!workspace || !aligned16(workspace) || workspace_bytes < P.ws_bytes)
+    return fail(KLG_ERR_WORKSPACE, "attention workspace needs %lld bytes (16-byte aligned)", (long long)P.ws_bytes);
+  if ((rc = bind_device(q))) return rc;
+  NvtxRange nvtx_range("klg_block_attn_fwd");
+  cudaStream_t s = (cudaStream_t)stream;
+  klg::AttnArgs a = P.a;
+  a.limits = limits;
+  a.part_o = static_cast<float*>(workspace);
+  a.part_ml = a.part_o + (size_t)a.n_units * a.splits * 128 * klg::ATT_D;
+  a.sl2 = scale * 1.4426950408889634f;
+  const int D = klg::ATT_D;
+  alignas(64) CUtensorMap mq, mks, mvs, mka, mva;
+  if (!make_map(&mq, q, D, (uint64_t)batch * heads * diff_len, D, D, (uint32_t)block) ||
+      !make_map(&mks, k_self, D, (uint64_t)batch * kv_heads * diff_len, D, D, (uint32_t)block) ||
+      !make_map(&mvs, v_self, D, (uint64_t)batch * kv_heads * diff_len, D, D, (uint32_t)block) ||
+      !make_map_3d(&mka, k_ar, D, ar_len, (uint64_t)batch * kv_heads, D, (uint64_t)ar_stride * D, D, klg::ATT_BN) ||
+      !make_map_3d(&mva, v_ar, D, ar_len, (uint64_t)batch * kv_heads, D, (uint64_t)ar_stride * D, D, klg::ATT_BN))
+    return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+  cudaError_t e = set_smem(klg::block_attn_kernel, klg::ATT_SMEM);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(block_attn_kernel)");
+  int slot = trace_pre(s);
+  e = launch_k(klg::block_attn_kernel, dim3(a.n_units * a.splits), dim3(klg::ATT_THREADS), klg::ATT_SMEM, s, 1, mq, mks,
+               mvs, mka, mva, a);
+  trace_post(slot, s, KLG_KIND_ATTN);
+  if (e != cudaSuccess) return cuda_fail(e, "launch block_attn_kernel");
+  ++g_launches;
+  const long long warps = (long long)a.n_units * a.hg * a.K;
+  slot = trace_pre(s);
+  e = launch_k(klg::block_attn_merge_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, s, 1, a,
+               static_cast<__nv_bfloat16*>(out), lse);
+  trace_post(slot, s, KLG_KIND_MERGE);
+  if (e != cudaSuccess) return cuda_fail(e, "launch block_attn_merge_kernel");
   ++g_launches;
   return KLG_OK;
 }

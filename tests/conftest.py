@@ -22,5 +22,6 @@ def golden_dir():
 
 
 def golden_cases():
-    """The loss fixtures (the sampler's and the norm's fixtures are read by their own tests)."""
-    return sorted(p.stem for p in GOLDEN.glob("*.npz") if p.stem != "sample_token" and not p.stem.startswith("norm_"))
+    """The loss fixtures (the sampler's, norm's and attention's are read by their own tests)."""
+    return sorted(p.stem for p in GOLDEN.glob("*.npz")
+                  if p.stem != "sample_token" and not p.stem.startswith(("norm_", "attn_")))

@@ -1,0 +1,34 @@
+"""Pin the block-diffusion attention oracle against the reference's flex-attention path.
+
+Fixture ``tests/golden/attn_block.npz`` (generator ``make_golden_attn.py``): the
+reference's ``fused_flex_attention`` with its block mask and causal-limit score_mod
+(``model.py:45-96``, ``model.py:435-446``), GQA, per-position limits, -1 and past-the-end
+limits.
+"""
+import numpy as np
+
+from oracle import klgemm_oracle as O
+from tests.conftest import GOLDEN
+
+
+def test_block_attention_oracle_matches_reference_flex():
+    g = dict(np.load(GOLDEN / "attn_block.npz"))
+    out, lse = O.block_attention_np(g["q"], g["k_self"], g["v_self"], g["k_ar"], g["v_ar"], g["limits"], int(g["K"]))
+    np.testing.assert_allclose(out, g["out"], rtol=1e-4, atol=2e-5)
+    np.testing.assert_allclose(lse, g["lse"], rtol=1e-5, atol=2e-5)
+
+
+def test_oracle_limits_clip_and_self_keys():
+    rng = np.random.default_rng(0)
+    B, H, Hkv, K, Ld, D, AL = 1, 2, 1, 4, 8, 64, 10
+    q, ks, vs = (rng.normal(size=s) for s in [(B, H, Ld, D), (B, Hkv, Ld, D), (B, Hkv, Ld, D)])
+    ka, va = rng.normal(size=(B, Hkv, AL, D)), rng.normal(size=(B, Hkv, AL, D))
+    lim = np.array([[-1] * 4 + [99] * 4])
+    out, _ = O.block_attention_np(q, ks, vs, ka, va, lim, K)
+    # block 0 with no AR keys: plain softmax attention over its own 4 keys
+    s = q[0, 0, :4] @ ks[0, 0, :4].T / 8.0
+    p = np.exp(s - s.max(1, keepdims=True))
+    np.testing.assert_allclose(out[0, 0, :4], (p / p.sum(1, keepdims=True)) @ vs[0, 0, :4], rtol=1e-12)
+    # a limit past the cache end sees the whole cache
+    out2, _ = O.block_attention_np(q, ks, vs, ka, va, np.array([[-1] * 4 + [AL - 1] * 4]), K)
+    np.testing.assert_allclose(out, out2, rtol=1e-12)
