@@ -488,9 +488,10 @@ def run_attn(args):
     # algorithmic work: every visible (query, key) pair costs 2 x 64 MACs (Q K and P V)
     visible = float((lim.clamp(-1, AL - 1).long() + 1).sum()) * H + B * H * Ld * K
     flops = 4.0 * 64 * visible
-    # bytes: Q + O + the KV rows a unit reads (AR prefix up to its block's largest limit, own keys)
-    lim_blk = lim.clamp(-1, AL - 1).long().view(B, Ld // K, K).amax(dim=2) + 1
-    kv_rows = float(lim_blk.sum()) * Hkv + B * Hkv * Ld
+    # bytes: Q + O + every K / V row some query sees, once (the AR prefix up to the sequence's
+    # largest limit, and the diffusion positions' own keys)
+    ar_rows = float((lim.clamp(-1, AL - 1).long().amax(dim=1) + 1).sum()) * Hkv
+    kv_rows = ar_rows + B * Hkv * Ld
     bytes_alg = 2.0 * B * H * Ld * 64 * 2 + kv_rows * 64 * 2 * 2
     hbm_peak, hbm_src = load_hbm_peak()
     peak_burst, _, peak_src = load_peaks()

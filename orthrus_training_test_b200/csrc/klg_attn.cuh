@@ -9,13 +9,17 @@
 // One CTA takes a unit (batch b, KV head, group of hg query heads sharing it, block) and a
 // split of the AR key range.  Its queries -- hg heads x K positions <= 128 rows, zero rows
 // after -- stay in shared memory; key tiles (128 AR keys, or the block's own K keys) stream
-// through a TMA ring.  Per tile: S = Q K^T (tcgen05, M = 128, N = keys, K = 64) into one of
-// two TMEM buffers; four softmax warps (one TMEM lane each row) take the masked online max /
-// sum in log2 units and write P = 2^(s - m) as bf16 into a 128-byte-swizzled K-major shared
-// tile; O_tile = P V (M = 128, N = 64, K = keys; V read MN-major) lands in TMEM and is
-// accumulated with the running rescale in registers.  Each CTA writes its rows' (O, m, l)
-// record; block_attn_merge_kernel combines the splits and writes bf16 O and the natural-log
-// log-sum-exp.
+// through a TMA ring.  Per tile: S = Q K^T (tcgen05, M = 128, N = keys, K = 64) into the TMEM
+// buffer of the tile's parity; the softmax warp group of that parity (four warps, one TMEM
+// lane = one row per thread) takes the masked online max / sum in log2 units and writes
+// P = 2^(s - m) as bf16 into its 128-byte-swizzled K-major shared tile; O_tile = P V
+// (M = 128, N = 64, K = keys; V read MN-major) lands in the parity's TMEM O buffer and is
+// accumulated with the running rescale in registers.  The MMA warp issues S one tile ahead,
+// so the two groups (two warps per SM sub-partition) work on consecutive tiles at once;
+// at the end the odd group's (m, l, O) is merged into the even group's through shared
+// memory.  Each CTA writes its rows' record; block_attn_merge_kernel combines the splits
+// and writes bf16 O and the natural-log log-sum-exp (with a single split the kernel writes
+// them itself and no merge runs).
 #pragma once
 #include "klg_kernels.cuh"
 
@@ -26,16 +30,19 @@ constexpr int ATT_BN = 128;                            // AR keys per tile
 constexpr int ATT_STAGES = 3;
 constexpr int ATT_TILE_BYTES = ATT_BN * ATT_D * 2;     // K or V tile, 16 KB
 constexpr int ATT_Q_BYTES = 128 * ATT_D * 2;           // 16 KB
-constexpr int ATT_P_BYTES = 128 * ATT_BN * 2;          // two 64-key K-major sub-tiles, 32 KB
-constexpr int ATT_THREADS = 192;                       // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
-constexpr int ATT_SMEM = 1024 + ATT_Q_BYTES + ATT_P_BYTES + ATT_STAGES * 2 * ATT_TILE_BYTES + 256;
-constexpr int ATT_TMEM_COLS = 512;                     // S: 2 x 128 columns; O tile: 64 columns at 256
+constexpr int ATT_P_BYTES = 128 * ATT_BN * 2;          // two 64-key K-major sub-tiles, 32 KB (per parity)
+constexpr int ATT_X_BYTES = 128 * (ATT_D + 2) * 4;     // odd group's (O, m, l) handed to the even group
+constexpr int ATT_THREADS = 320;                       // warp 0 TMA, warp 1 MMA, warps 2-9 softmax
+constexpr int ATT_SMEM = 1024 + ATT_Q_BYTES + 2 * ATT_P_BYTES + ATT_STAGES * 2 * ATT_TILE_BYTES + ATT_X_BYTES + 256;
+constexpr int ATT_TMEM_COLS = 512;                     // S: 2 x 128 columns; O tiles: 2 x 64 at 256
 constexpr int ATT_O_COL = 256;
 
 struct AttnArgs {
   const int* limits;   // [B, Ld] causal limit per query position (AR keys 0..limit)
   float* part_o;       // [n_cta][128][64] unnormalised O per split
   float* part_ml;      // [n_cta][2][128] (m in log2 units, l)
+  __nv_bfloat16* out;  // with one split the kernel writes O [B, H, Ld, 64] and lse itself
+  float* lse;
   int B, H, Hkv, Ld, K, ar_len;
   int ng, hg, n_hg, nb;   // query heads per KV head, per unit; head groups; blocks
   int n_units, splits, tps;   // tps: AR tiles per split
@@ -61,17 +68,18 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
   __shared__ int s_maxlim;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t q_s = smem_u32(smem);
-  const uint32_t p_s = q_s + ATT_Q_BYTES;
-  const uint32_t st_s = p_s + ATT_P_BYTES;   // stage j: K tile at st_s + 2j * TILE, V tile right after
-  const uint32_t bar0 = st_s + ATT_STAGES * 2 * ATT_TILE_BYTES;
+  const uint32_t p_s = q_s + ATT_Q_BYTES;                  // [2] P tiles, one per parity
+  const uint32_t st_s = p_s + 2 * ATT_P_BYTES;   // stage j: K tile at st_s + 2j * TILE, V tile right after
+  float* xch = reinterpret_cast<float*>(smem + ATT_Q_BYTES + 2 * ATT_P_BYTES + ATT_STAGES * 2 * ATT_TILE_BYTES);
+  const uint32_t bar0 = st_s + ATT_STAGES * 2 * ATT_TILE_BYTES + ATT_X_BYTES;
   const uint32_t full0 = bar0;                        // [STAGES] TMA bytes of K + V
   const uint32_t empty0 = bar0 + 8u * ATT_STAGES;     // [STAGES] P V of the stage retired
   const uint32_t qbar = bar0 + 16u * ATT_STAGES;      // queries landed
-  const uint32_t sfull0 = qbar + 8u;                  // [2] S tile in TMEM
-  const uint32_t sempty0 = sfull0 + 16u;              // [2] softmax warps read the S tile
-  const uint32_t pfull = sempty0 + 16u;               // P written to shared memory
-  const uint32_t ofull = pfull + 8u;                  // O tile in TMEM
-  const uint32_t oempty = ofull + 8u;                 // softmax warps read the O tile
+  const uint32_t sfull0 = qbar + 8u;                  // [2] S tile in TMEM (per parity)
+  const uint32_t sempty0 = sfull0 + 16u;              // [2] the parity's softmax warps read it
+  const uint32_t pfull0 = sempty0 + 16u;              // [2] P written to shared memory
+  const uint32_t ofull0 = pfull0 + 16u;               // [2] O tile in TMEM
+  const uint32_t oempty0 = ofull0 + 16u;              // [2] the parity's softmax warps read it
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int u = blockIdx.x / a.splits;
@@ -91,10 +99,10 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
     for (int s = 0; s < 2; ++s) {
       mbar_init(sfull0 + 8u * s, 1);
       mbar_init(sempty0 + 8u * s, 4);
+      mbar_init(pfull0 + 8u * s, 4);
+      mbar_init(ofull0 + 8u * s, 1);
+      mbar_init(oempty0 + 8u * s, 4);
     }
-    mbar_init(pfull, 4);
-    mbar_init(ofull, 1);
-    mbar_init(oempty, 4);
     fence_mbar_init();
     tma_prefetch(&map_q);
     tma_prefetch(&map_ks);
@@ -162,61 +170,69 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (whole warp)
+    // S of tile i + 1 is issued before P V of tile i, so both softmax groups have work.
     bool ok = warp_wait(qbar, 0, abort_p, KLG_STATUS_TIMEOUT_MMA);
     tc_fence_after();
-    int stage = 0;
-    uint32_t phase = 0;
-    for (int i = 0; ok && i < ntiles; ++i) {
-      const int nk = i < n_my ? ATT_BN : a.K;
-      const int sb = i & 1;
-      if (!warp_wait(full0 + 8u * stage, phase, abort_p, KLG_STATUS_TIMEOUT_MMA)) break;
-      if (!warp_wait(sempty0 + 8u * sb, ((uint32_t)(i >> 1) & 1u) ^ 1u, abort_p, KLG_STATUS_TIMEOUT_MMA)) break;
+    auto issue_s = [&](int i) -> bool {   // S_i = Q K_i^T into the parity's S buffer
+      const int stage = i % ATT_STAGES;
+      const uint32_t phase = (uint32_t)(i / ATT_STAGES) & 1u;
+      const int par = i & 1;
+      if (!warp_wait(full0 + 8u * stage, phase, abort_p, KLG_STATUS_TIMEOUT_MMA)) return false;
+      if (!warp_wait(sempty0 + 8u * par, ((uint32_t)(i >> 1) & 1u) ^ 1u, abort_p, KLG_STATUS_TIMEOUT_MMA)) return false;
       tc_fence_after();
-      const uint32_t ks = st_s + stage * 2 * ATT_TILE_BYTES;
       if (elect_one()) {
-        const uint32_t idesc = make_idesc_bf16(128, nk, false, false);
+        const uint32_t idesc = make_idesc_bf16(128, i < n_my ? ATT_BN : a.K, false, false);
+        const uint32_t ks = st_s + stage * 2 * ATT_TILE_BYTES;
 #pragma unroll
         for (int k = 0; k < ATT_D / 16; ++k)
-          mma_bf16(tmem + sb * ATT_BN, desc_kmajor(q_s, k), desc_kmajor(ks, k), idesc, k != 0);
-        mma_commit(sfull0 + 8u * sb);
+          mma_bf16(tmem + par * ATT_BN, desc_kmajor(q_s, k), desc_kmajor(ks, k), idesc, k != 0);
+        mma_commit(sfull0 + 8u * par);
       }
       __syncwarp();
-      if (!warp_wait(pfull, (uint32_t)i & 1u, abort_p, KLG_STATUS_TIMEOUT_MMA)) break;
-      if (!warp_wait(oempty, ((uint32_t)i & 1u) ^ 1u, abort_p, KLG_STATUS_TIMEOUT_MMA)) break;
+      return true;
+    };
+    if (ok && ntiles > 0) ok = issue_s(0);
+    for (int i = 0; ok && i < ntiles; ++i) {
+      if (i + 1 < ntiles && !(ok = issue_s(i + 1))) break;
+      const int par = i & 1;
+      const int stage = i % ATT_STAGES;
+      const int nk = i < n_my ? ATT_BN : a.K;
+      if (!warp_wait(pfull0 + 8u * par, (uint32_t)(i >> 1) & 1u, abort_p, KLG_STATUS_TIMEOUT_MMA)) break;
+      if (!warp_wait(oempty0 + 8u * par, ((uint32_t)(i >> 1) & 1u) ^ 1u, abort_p, KLG_STATUS_TIMEOUT_MMA)) break;
       tc_fence_after();
       if (elect_one()) {
         const uint32_t idesc = make_idesc_bf16(128, ATT_D, false, true);
+        const uint32_t vs = st_s + stage * 2 * ATT_TILE_BYTES + ATT_TILE_BYTES;
+        const uint32_t pp = p_s + par * ATT_P_BYTES;
         for (int k = 0; k < nk / 16; ++k)
-          mma_bf16(tmem + ATT_O_COL, desc_kmajor(p_s + (k >> 2) * 16384, k & 3),
-                   desc_mnmajor(ks + ATT_TILE_BYTES, k), idesc, k != 0);
-        mma_commit(ofull);
+          mma_bf16(tmem + ATT_O_COL + par * ATT_D, desc_kmajor(pp + (k >> 2) * 16384, k & 3), desc_mnmajor(vs, k),
+                   idesc, k != 0);
+        mma_commit(ofull0 + 8u * par);
         mma_commit(empty0 + 8u * stage);
       }
       __syncwarp();
-      if (++stage == ATT_STAGES) {
-        stage = 0;
-        phase ^= 1;
-      }
     }
   } else {
     // ------------------------------------------------------------ softmax warps (one row per thread)
     const int q4 = warp & 3;   // TMEM lane quarter of this warp
+    const int par = (warp - 2) >> 2;   // tiles of this parity
     const int r = q4 * 32 + lane;
     const int pos = r % a.K;
     const int lim = r < rows ? min(max(a.limits[(size_t)b * a.Ld + blk * a.K + pos], -1), a.ar_len - 1) : -1;
     const uint32_t lrow = tmem + ((uint32_t)(q4 * 32) << 16);
-    const uint32_t prow = p_s + (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u;
+    const uint32_t prow = p_s + par * ATT_P_BYTES + (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u;
     float m = NEG_BIG, l = 0.f;
     float o[ATT_D];
 #pragma unroll
     for (int j = 0; j < ATT_D; ++j) o[j] = 0.f;
     bool ok = true;
-    for (int i = 0; ok && i < ntiles; ++i) {
+    for (int i = par; ok && i < ntiles; i += 2) {
       const bool self = i >= n_my;
       const int nk = self ? a.K : ATT_BN;
       const int kmax = self ? a.K - 1 : lim - (t0 + i) * ATT_BN;   // last visible key of the tile
-      const int sb = i & 1;
-      if (!mbar_wait(sfull0 + 8u * sb, (uint32_t)(i >> 1) & 1u, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) {
+      const int sb = par;
+      const uint32_t jph = (uint32_t)(i >> 1) & 1u;   // this parity's use count of its buffers
+      if (!mbar_wait(sfull0 + 8u * sb, jph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) {
         ok = false;
         break;
       }
@@ -260,16 +276,16 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(sempty0 + 8u * sb);
-        mbar_arrive(pfull);
+        mbar_arrive(pfull0 + 8u * sb);
       }
-      if (!mbar_wait(ofull, (uint32_t)i & 1u, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) {
+      if (!mbar_wait(ofull0 + 8u * sb, jph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) {
         ok = false;
         break;
       }
       tc_fence_after();
       uint32_t v0[32], v1[32];
-      tmem_ld32_raw(lrow + ATT_O_COL, v0);
-      tmem_ld32_raw(lrow + ATT_O_COL + 32, v1);
+      tmem_ld32_raw(lrow + ATT_O_COL + par * ATT_D, v0);
+      tmem_ld32_raw(lrow + ATT_O_COL + par * ATT_D + 32, v1);
       tmem_wait_ld_regs(v0, v1);
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
@@ -278,15 +294,55 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(oempty);
+      if (lane == 0) mbar_arrive(oempty0 + 8u * sb);
     }
-    // this split's record for the row (also written when the split had no tiles or gave up)
-    float4* po = reinterpret_cast<float4*>(a.part_o + ((size_t)blockIdx.x * 128 + r) * ATT_D);
+    if (!ok) {   // a group that gave up contributes nothing
+      m = NEG_BIG;
+      l = 0.f;
 #pragma unroll
-    for (int j = 0; j < ATT_D / 4; ++j)
-      po[j] = ok ? make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]) : make_float4(0.f, 0.f, 0.f, 0.f);
-    a.part_ml[(size_t)blockIdx.x * 256 + r] = m;
-    a.part_ml[(size_t)blockIdx.x * 256 + 128 + r] = ok ? l : 0.f;
+      for (int j = 0; j < ATT_D; ++j) o[j] = 0.f;
+    }
+    // the odd group hands its state to the even group through shared memory
+    float* x = xch + r * (ATT_D + 2);
+    if (par == 1) {
+#pragma unroll
+      for (int j = 0; j < ATT_D; ++j) x[j] = o[j];
+      x[ATT_D] = m;
+      x[ATT_D + 1] = l;
+    }
+    asm volatile("bar.sync 1, 256;" ::: "memory");   // the eight softmax warps
+    if (par == 0) {
+      const float m1 = x[ATT_D];
+      const float mm = fmaxf(m, m1);
+      const float w0 = ex2(m - mm), w1 = ex2(m1 - mm);
+      l = l * w0 + x[ATT_D + 1] * w1;
+      m = mm;
+#pragma unroll
+      for (int j = 0; j < ATT_D; ++j) o[j] = o[j] * w0 + x[j] * w1;
+      if (a.splits == 1) {
+        // the whole key range is here: normalise and write the output row directly
+        if (r < rows) {
+          const int h = hkv * a.ng + hgi * a.hg + r / a.K;
+          const size_t row = ((size_t)b * a.H + h) * a.Ld + blk * a.K + pos;
+          const float inv = l > 0.f ? 1.0f / l : 0.f;
+          uint4* dst = reinterpret_cast<uint4*>(a.out + row * ATT_D);
+#pragma unroll
+          for (int j = 0; j < ATT_D / 8; ++j)
+            dst[j] = make_uint4(pack_bf16x2(o[8 * j] * inv, o[8 * j + 1] * inv),
+                                pack_bf16x2(o[8 * j + 2] * inv, o[8 * j + 3] * inv),
+                                pack_bf16x2(o[8 * j + 4] * inv, o[8 * j + 5] * inv),
+                                pack_bf16x2(o[8 * j + 6] * inv, o[8 * j + 7] * inv));
+          if (a.lse) a.lse[row] = (m + __log2f(l)) * 0.69314718055994530942f;
+        }
+      } else {
+        // this split's record for the row (also written when the split had no tiles)
+        float4* po = reinterpret_cast<float4*>(a.part_o + ((size_t)blockIdx.x * 128 + r) * ATT_D);
+#pragma unroll
+        for (int j = 0; j < ATT_D / 4; ++j) po[j] = make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+        a.part_ml[(size_t)blockIdx.x * 256 + r] = m;
+        a.part_ml[(size_t)blockIdx.x * 256 + 128 + r] = l;
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();   // every MMA retired (the softmax warps consumed the last O tile) before TMEM is freed
@@ -296,7 +352,8 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
 
 // Combines the splits of each unit row: O = sum_s O_s 2^(m_s - M) / sum_s l_s 2^(m_s - M),
 // written as bf16 to out [B, H, Ld, 64]; lse [B, H, Ld] = (M + log2 L) ln 2.  One warp per
-// row, two head-dimension columns per lane.
+// row: lane j reads split j's (m, l) (32 at a time, reduced across the warp), then each lane
+// accumulates two head-dimension columns over the splits (independent loads, unrolled).
 __global__ void __launch_bounds__(256) block_attn_merge_kernel(const AttnArgs a, __nv_bfloat16* __restrict__ out,
                                                               float* __restrict__ lse) {
   pdl_enter();
@@ -308,17 +365,31 @@ __global__ void __launch_bounds__(256) block_attn_merge_kernel(const AttnArgs a,
   const int r = (int)(gw - (long long)u * rows);
   int b, hkv, hgi, blk;
   attn_unit(a, u, b, hkv, hgi, blk);
+  const size_t c0 = (size_t)u * a.splits;
   float M = NEG_BIG;
-  for (int s = 0; s < a.splits; ++s) M = fmaxf(M, a.part_ml[(size_t)(u * a.splits + s) * 256 + r]);
+  for (int s0 = 0; s0 < a.splits; s0 += 32)
+    if (s0 + lane < a.splits) M = fmaxf(M, a.part_ml[(c0 + s0 + lane) * 256 + r]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
   float L = 0.f, o0 = 0.f, o1 = 0.f;
-  for (int s = 0; s < a.splits; ++s) {
-    const size_t c = (size_t)(u * a.splits + s);
-    const float w = ex2(a.part_ml[c * 256 + r] - M);
-    L = fmaf(a.part_ml[c * 256 + 128 + r], w, L);
-    const float2 v = reinterpret_cast<const float2*>(a.part_o + (c * 128 + r) * ATT_D)[lane];
-    o0 = fmaf(v.x, w, o0);
-    o1 = fmaf(v.y, w, o1);
+  for (int s0 = 0; s0 < a.splits; s0 += 32) {
+    const int n = min(32, a.splits - s0);
+    float w = 0.f;
+    if (lane < n) {
+      const size_t c = c0 + s0 + lane;
+      w = ex2(a.part_ml[c * 256 + r] - M);
+      L = fmaf(a.part_ml[c * 256 + 128 + r], w, L);
+    }
+#pragma unroll 4
+    for (int j = 0; j < n; ++j) {
+      const float wj = __shfl_sync(0xffffffffu, w, j);
+      const float2 v = reinterpret_cast<const float2*>(a.part_o + ((c0 + s0 + j) * 128 + r) * ATT_D)[lane];
+      o0 = fmaf(v.x, wj, o0);
+      o1 = fmaf(v.y, wj, o1);
+    }
   }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
   const int h = hkv * a.ng + hgi * a.hg + r / a.K;
   const size_t row = ((size_t)b * a.H + h) * a.Ld + blk * a.K + r % a.K;
   const float inv = 1.0f / L;

@@ -1066,7 +1066,7 @@ int attn_plan(int64_t B, int64_t H, int64_t Hkv, int64_t Ld, int64_t K, int64_t 
   a.tps = cdiv(n_ar, splits);
   a.splits = cdiv(n_ar, a.tps);
   const int64_t n_cta = (int64_t)a.n_units * a.splits;
-  P.ws_bytes = n_cta * 128 * (klg::ATT_D + 2) * 4;
+  P.ws_bytes = a.splits > 1 ? n_cta * 128 * (klg::ATT_D + 2) * 4 : 16;   // one split writes the output directly
   return KLG_OK;
 }
 }  // namespace
@@ -1100,6 +1100,8 @@ int klg_block_attn_fwd(const void* q, const void* k_self, const void* v_self, co
   a.part_o = static_cast<float*>(workspace);
   a.part_ml = a.part_o + (size_t)a.n_units * a.splits * 128 * klg::ATT_D;
   a.sl2 = scale * 1.4426950408889634f;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.lse = lse;
   const int D = klg::ATT_D;
   alignas(64) CUtensorMap mq, mks, mvs, mka, mva;
   if (!make_map(&mq, q, D, (uint64_t)batch * heads * diff_len, D, D, (uint32_t)block) ||
@@ -1116,6 +1118,7 @@ int klg_block_attn_fwd(const void* q, const void* k_self, const void* v_self, co
   trace_post(slot, s, KLG_KIND_ATTN);
   if (e != cudaSuccess) return cuda_fail(e, "launch block_attn_kernel");
   ++g_launches;
+  if (a.splits == 1) return KLG_OK;
   const long long warps = (long long)a.n_units * a.hg * a.K;
   slot = trace_pre(s);
   e = launch_k(klg::block_attn_merge_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, s, 1, a,

@@ -60,6 +60,7 @@ def test_matches_reference_flex_golden():
     (1, 6, 2, 64, 128, 500, "random"),        # K = 64: one query head per unit
     (1, 4, 4, 128, 256, 129, "random"),       # K = 128, no GQA, a last AR tile with one key
     (2, 6, 2, 16, 64, 300, "random"),
+    (4, 9, 3, 32, 1024, 500, "anchored"),     # >= 2 units per SM: one split, output written by the kernel
 ])
 def test_matches_oracle(B, H, Hkv, K, Ld, AL, kind):
     from orthrus_training_test_b200.attention import block_attention
