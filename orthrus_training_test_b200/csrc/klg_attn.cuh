@@ -238,13 +238,26 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
       }
       tc_fence_after();
       const int nch = (nk + 31) >> 5;
+      // every key of the tile visible to all 32 rows of the warp: no per-key mask
+      const bool open = __all_sync(0xffffffffu, kmax >= nk - 1) && (nk & 31) == 0;
       float tmax = -INFINITY;
       for (int c = 0; c < nch; ++c) {
         uint32_t v[32];
         tmem_ld32_raw(lrow + sb * ATT_BN + c * 32, v);
         tmem_wait_ld_regs(v);
+        if (open) {
+          float t0 = __uint_as_float(v[0]), t1 = __uint_as_float(v[1]);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) tmax = fmaxf(tmax, c * 32 + j <= kmax ? __uint_as_float(v[j]) * a.sl2 : -INFINITY);
+          for (int j = 2; j < 32; j += 2) {
+            t0 = fmaxf(t0, __uint_as_float(v[j]));
+            t1 = fmaxf(t1, __uint_as_float(v[j + 1]));
+          }
+          tmax = fmaxf(tmax, fmaxf(t0, t1) * a.sl2);   // scale > 0 commutes with max
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            tmax = fmaxf(tmax, c * 32 + j <= kmax ? __uint_as_float(v[j]) * a.sl2 : -INFINITY);
+        }
       }
       const float mn = fmaxf(m, tmax);
       const float alpha = ex2(m - mn);
@@ -254,11 +267,20 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
         tmem_ld32_raw(lrow + sb * ATT_BN + c * 32, v);
         tmem_wait_ld_regs(v);
         float p[32];
+        if (open) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          p[j] = c * 32 + j <= kmax ? ex2(fmaf(__uint_as_float(v[j]), a.sl2, -mn)) : 0.f;
-          sum += p[j];
+          for (int j = 0; j < 32; ++j) p[j] = ex2(fmaf(__uint_as_float(v[j]), a.sl2, -mn));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) p[j] = c * 32 + j <= kmax ? ex2(fmaf(__uint_as_float(v[j]), a.sl2, -mn)) : 0.f;
         }
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          s0 += p[j];
+          s1 += p[j + 1];
+        }
+        sum += s0 + s1;
 #pragma unroll
         for (int q8 = 0; q8 < 4; ++q8) {
           const int chunk = c * 4 + q8;   // 8 keys = 16 bytes; 8 chunks per 64-key sub-tile row
