@@ -49,13 +49,60 @@ struct AttnArgs {
   float sl2;                  // scale * log2(e)
 };
 
+// Units are numbered with the blocks of a sequence in reverse: later blocks see longer AR
+// prefixes (their anchors come later), so CTAs start longest-first and the short units fill
+// the tail of the grid.
 __device__ __forceinline__ void attn_unit(const AttnArgs& a, int u, int& b, int& hkv, int& hgi, int& blk) {
-  blk = u % a.nb;
+  blk = a.nb - 1 - u % a.nb;
   int r = u / a.nb;
   hgi = r % a.n_hg;
   r /= a.n_hg;
   hkv = r % a.Hkv;
   b = r / a.Hkv;
+}
+
+// One 32-key chunk c of a row of S (raw fp32 bits): P = 2^(s sl2 - ref) for the visible keys
+// (key <= kmax; all of them when `open`), written as bf16 into the row's swizzled P tile;
+// folds the chunk's max (scaled) and sum into tmax / sum.
+__device__ __forceinline__ void attn_p_chunk(const uint32_t (&v)[32], int c, int nk, int kmax, bool open, float sl2,
+                                             float ref, uint32_t prow, int r, float& tmax, float& sum) {
+  uint32_t pk[16];   // P as bf16 pairs
+  float t0 = -INFINITY, t1 = -INFINITY, s0 = 0.f, s1 = 0.f;
+  if (open) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+      const float x0 = __uint_as_float(v[j]), x1 = __uint_as_float(v[j + 1]);
+      t0 = fmaxf(t0, x0);
+      t1 = fmaxf(t1, x1);
+      const float p0 = ex2(fmaf(x0, sl2, -ref)), p1 = ex2(fmaf(x1, sl2, -ref));
+      s0 += p0;
+      s1 += p1;
+      pk[j >> 1] = pack_bf16x2(p0, p1);
+    }
+    tmax = fmaxf(tmax, fmaxf(t0, t1) * sl2);   // scale > 0 commutes with max
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+      const float x0 = c * 32 + j <= kmax ? __uint_as_float(v[j]) * sl2 : -INFINITY;
+      const float x1 = c * 32 + j + 1 <= kmax ? __uint_as_float(v[j + 1]) * sl2 : -INFINITY;
+      t0 = fmaxf(t0, x0);
+      t1 = fmaxf(t1, x1);
+      const float p0 = ex2(x0 - ref), p1 = ex2(x1 - ref);
+      s0 += p0;
+      s1 += p1;
+      pk[j >> 1] = pack_bf16x2(p0, p1);
+    }
+    tmax = fmaxf(tmax, fmaxf(t0, t1));
+  }
+  sum += s0 + s1;
+#pragma unroll
+  for (int q8 = 0; q8 < 4; ++q8) {
+    const int chunk = c * 4 + q8;   // 8 keys = 16 bytes; 8 chunks per 64-key sub-tile row
+    if (chunk * 8 < nk) {
+      const uint32_t addr = prow + (uint32_t)(chunk >> 3) * 16384u + (uint32_t)(((chunk & 7) ^ (r & 7)) << 4);
+      st_shared_v4(addr, pk[4 * q8], pk[4 * q8 + 1], pk[4 * q8 + 2], pk[4 * q8 + 3]);
+    }
+  }
 }
 
 __global__ void __launch_bounds__(ATT_THREADS, 1)
@@ -240,57 +287,30 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
       const int nch = (nk + 31) >> 5;
       // every key of the tile visible to all 32 rows of the warp: no per-key mask
       const bool open = __all_sync(0xffffffffu, kmax >= nk - 1) && (nk & 31) == 0;
-      float tmax = -INFINITY;
-      for (int c = 0; c < nch; ++c) {
-        uint32_t v[32];
-        tmem_ld32_raw(lrow + sb * ATT_BN + c * 32, v);
-        tmem_wait_ld_regs(v);
-        if (open) {
-          float t0 = __uint_as_float(v[0]), t1 = __uint_as_float(v[1]);
-#pragma unroll
-          for (int j = 2; j < 32; j += 2) {
-            t0 = fmaxf(t0, __uint_as_float(v[j]));
-            t1 = fmaxf(t1, __uint_as_float(v[j + 1]));
-          }
-          tmax = fmaxf(tmax, fmaxf(t0, t1) * a.sl2);   // scale > 0 commutes with max
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            tmax = fmaxf(tmax, c * 32 + j <= kmax ? __uint_as_float(v[j]) * a.sl2 : -INFINITY);
+      // One pass over S writes P = 2^(s - ref) for the reference max `ref` and returns the
+      // tile's max and sum.  (Double-buffering the TMEM loads needs 64 more registers than the
+      // 168 a thread can have with ten warps -- three per SM sub-partition -- and spills.)
+      auto p_pass = [&](float ref, float& tmax, float& sum) {
+        tmax = -INFINITY;
+        sum = 0.f;
+        for (int c = 0; c < nch; ++c) {
+          uint32_t v[32];
+          tmem_ld32_raw(lrow + sb * ATT_BN + c * 32, v);
+          tmem_wait_ld_regs(v);
+          attn_p_chunk(v, c, nk, kmax, open, a.sl2, ref, prow, r, tmax, sum);
         }
+      };
+      // P against the running max; only when a row's tile max exceeds it by more than 2^10
+      // (always on a row's first visible tile) is the tile redone against the new max.  l and
+      // O use the same reference either way, so the result is exact; P stays <= 2^10.
+      float tmax, sum;
+      p_pass(m, tmax, sum);
+      float mn = m;
+      if (__any_sync(0xffffffffu, tmax > m + 10.f)) {
+        mn = fmaxf(m, tmax);
+        p_pass(mn, tmax, sum);
       }
-      const float mn = fmaxf(m, tmax);
       const float alpha = ex2(m - mn);
-      float sum = 0.f;
-      for (int c = 0; c < nch; ++c) {
-        uint32_t v[32];
-        tmem_ld32_raw(lrow + sb * ATT_BN + c * 32, v);
-        tmem_wait_ld_regs(v);
-        float p[32];
-        if (open) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) p[j] = ex2(fmaf(__uint_as_float(v[j]), a.sl2, -mn));
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) p[j] = c * 32 + j <= kmax ? ex2(fmaf(__uint_as_float(v[j]), a.sl2, -mn)) : 0.f;
-        }
-        float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          s0 += p[j];
-          s1 += p[j + 1];
-        }
-        sum += s0 + s1;
-#pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {
-          const int chunk = c * 4 + q8;   // 8 keys = 16 bytes; 8 chunks per 64-key sub-tile row
-          if (chunk * 8 < nk) {
-            const uint32_t addr = prow + (uint32_t)(chunk >> 3) * 16384u + (uint32_t)(((chunk & 7) ^ (r & 7)) << 4);
-            st_shared_v4(addr, pack_bf16x2(p[8 * q8], p[8 * q8 + 1]), pack_bf16x2(p[8 * q8 + 2], p[8 * q8 + 3]),
-                         pack_bf16x2(p[8 * q8 + 4], p[8 * q8 + 5]), pack_bf16x2(p[8 * q8 + 6], p[8 * q8 + 7]));
-          }
-        }
-      }
       l = fmaf(l, alpha, sum);
       m = mn;
       tc_fence_before();

@@ -114,3 +114,23 @@ def test_sampler_and_norm_argument_validation():
     assert L.klg_rmsnorm_rows(None, 0, p, 4, 64, 1e-5, p, None, None) == _lib.KLG_ERR_ARG
     assert L.klg_rmsnorm_rows_bwd(p, 0, p, None, p, 4, 64, p, None) == _lib.KLG_ERR_ARG
     del keep
+
+
+def test_attention_argument_validation():
+    L = _lib.lib()
+    keep, p = _buf(1 << 16)
+    ws = L.klg_block_attn_workspace_bytes
+    assert ws(1, 9, 3, 32, 32, 2048, 64) > 0                 # decode: AR range split over CTAs
+    assert ws(4, 9, 3, 2048, 32, 2048, 64) == 16             # many units: one split, no records
+    assert ws(1, 9, 3, 32, 32, 2048, 128) == -1              # head_dim 64 only
+    assert ws(1, 9, 3, 32, 24, 2048, 64) == -1               # K a multiple of 16
+    assert ws(1, 9, 3, 40, 32, 2048, 64) == -1               # Ld a multiple of K
+    assert ws(1, 9, 4, 32, 32, 2048, 64) == -1               # H a multiple of Hkv
+    assert ws(1, 9, 3, 32, 32, 0, 64) == -1                  # an AR cache
+    args = lambda **kw: [kw.get("q", p), p, p, p, p, kw.get("stride", 2048), p, 1, 9, 3, 32, 32, 2048, 64,
+                         kw.get("scale", 0.125), p, None, p, kw.get("wsb", 1 << 16), None]
+    assert L.klg_block_attn_fwd(*args(q=None)) == _lib.KLG_ERR_ARG
+    assert L.klg_block_attn_fwd(*args(stride=100)) == _lib.KLG_ERR_ARG     # stride < ar_len
+    assert L.klg_block_attn_fwd(*args(scale=0.0)) == _lib.KLG_ERR_ARG
+    assert L.klg_block_attn_fwd(*args(wsb=8)) == _lib.KLG_ERR_WORKSPACE
+    del keep
