@@ -182,6 +182,20 @@ int klg_lm_head_sample(const void* h, const void* w, int64_t n_rows, int64_t hid
                        int sample, uint64_t seed, int32_t* tokens, float* logit, float* lse, void* workspace,
                        int64_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------- row selection
+ * The gathers of compute_kl_loss (train.py:124-139, 156-164) in one kernel:
+ *   diff [B, nb*K, row] (the diffusion hidden states), ar [B, L, row] (AR hidden states),
+ *   anchors [B, nb] int64, targets [B, nb*K] int64;
+ *   row i = (b, blk, k), k = 1..K-1:  h_s[i] = diff[b, blk*K + k],
+ *   h_t[i] = ar[b, clamp(anchors[b, blk] + k - 1, 0, L - 1)], valid[i] = targets[b, blk*K + k] != pad_id.
+ * Rows are copied as bytes (row_bytes = H * element size, a multiple of 16).  The scatter is
+ * the student gather's backward: d_diff[b, p] = d_hs[row of (b, p)], zeros at anchors (p % K == 0). */
+int klg_gather_rows(const void* diff, const void* ar, const int64_t* anchors, const int64_t* targets, int64_t batch,
+                    int64_t n_blocks, int64_t block, int64_t ar_len, int64_t row_bytes, int64_t pad_id, void* h_s,
+                    void* h_t, uint8_t* valid, void* stream);
+int klg_scatter_rows_grad(const void* d_hs, int64_t batch, int64_t n_blocks, int64_t block, int64_t row_bytes,
+                          void* d_diff, void* stream);
+
 /* ---------------------------------------------------------------- final RMSNorm prologue
  * For pre-norm hidden states: the backbone's final norm (model.py:493, `self.norm`, a
  * transformers LlamaRMSNorm) applied row by row, so the fused loss can take the states
@@ -234,6 +248,7 @@ int klg_cast_f32_bf16(const float* in, void* out, int64_t n, void* stream);
 #define KLG_KIND_SAMPLE 9    /* inference: lm_head logits -> argmax / Gumbel-max sample   */
 #define KLG_KIND_NORM 10     /* final RMSNorm of pre-norm rows, forward or backward       */
 #define KLG_KIND_ATTN 11     /* block-diffusion attention, forward                        */
+#define KLG_KIND_GATHER 12   /* row selection (gather) or its gradient scatter            */
 int klg_trace_begin(int capacity);
 int klg_trace_end(int* kinds, float* ms, int capacity, int* n);
 

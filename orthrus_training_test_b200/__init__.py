@@ -9,6 +9,6 @@ Public API
   sampling          fused lm_head + greedy / sampled token selection for inference
 """
 from .ops import KLGemmFn, PrenormKLGemmFn, kl_gemm_loss, kl_forward, kl_backward, prenorm_kl_loss  # noqa: F401
-from .loss import compute_kl_loss, select_rows  # noqa: F401
+from .loss import compute_kl_loss, gather_rows, select_rows  # noqa: F401
 
-__all__ = ["KLGemmFn", "PrenormKLGemmFn", "prenorm_kl_loss", "kl_gemm_loss", "kl_forward", "kl_backward", "compute_kl_loss", "select_rows"]
+__all__ = ["KLGemmFn", "PrenormKLGemmFn", "prenorm_kl_loss", "kl_gemm_loss", "kl_forward", "kl_backward", "compute_kl_loss", "gather_rows", "select_rows"]

@@ -32,6 +32,9 @@ SIGNATURES = {
     "klg_block_attn_workspace_bytes": (c_longlong, [c_longlong] * 7),
     "klg_block_attn_fwd": (c_int, [c_void_p] * 5 + [c_longlong, c_void_p] + [c_longlong] * 7 +
                            [c_float, c_void_p, c_void_p, c_void_p, c_longlong, c_void_p]),
+    "klg_gather_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p] + [c_longlong] * 6 +
+                        [c_void_p, c_void_p, c_void_p, c_void_p]),
+    "klg_scatter_rows_grad": (c_int, [c_void_p] + [c_longlong] * 4 + [c_void_p, c_void_p]),
     "klg_rmsnorm_rows": (c_int, [c_void_p, c_int, c_void_p, c_longlong, c_longlong, c_float, c_void_p, c_void_p,
                                  c_void_p]),
     "klg_rmsnorm_rows_bwd": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_longlong, c_longlong, c_void_p,
@@ -63,7 +66,7 @@ SIGNATURES = {
     "klg_trace_end": (c_int, [POINTER(c_int), POINTER(c_float), c_int, POINTER(c_int)]),
 }
 
-KIND_NAMES = {1: "stats", 2: "dz", 3: "gemm", 4: "merge", 5: "finalize", 6: "count", 7: "cast", 8: "zero", 9: "sample", 10: "norm", 11: "attn"}
+KIND_NAMES = {1: "stats", 2: "dz", 3: "gemm", 4: "merge", 5: "finalize", 6: "count", 7: "cast", 8: "zero", 9: "sample", 10: "norm", 11: "attn", 12: "gather"}
 
 _lib = None
 

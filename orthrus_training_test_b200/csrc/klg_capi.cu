@@ -983,6 +983,53 @@ int klg_lm_head_sample(const void* h, const void* w, int64_t n_rows, int64_t hid
   return KLG_OK;
 }
 
+int klg_gather_rows(const void* diff, const void* ar, const int64_t* anchors, const int64_t* targets, int64_t batch,
+                    int64_t n_blocks, int64_t block, int64_t ar_len, int64_t row_bytes, int64_t pad_id, void* h_s,
+                    void* h_t, uint8_t* valid, void* stream) {
+  if (!diff || !ar || !anchors || !targets || !h_s || !h_t || !valid) return fail(KLG_ERR_ARG, "null pointer");
+  if (batch < 1 || n_blocks < 1 || block < 2 || ar_len < 1 || row_bytes < 16 ||
+      batch * n_blocks * block > (1ll << 31) || batch * ar_len > (1ll << 40))
+    return fail(KLG_ERR_ARG, "bad row-selection shape");
+  if (row_bytes % 16 != 0) return fail(KLG_ERR_ALIGN, "row_bytes=%lld must be a multiple of 16", (long long)row_bytes);
+  for (const void* p : {diff, ar, (const void*)h_s, (const void*)h_t})
+    if (!aligned16(p)) return fail(KLG_ERR_ALIGN, "rows must be 16-byte aligned");
+  int rc = bind_device(diff);
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  const long long rows = batch * n_blocks * (block - 1);
+  const int slot = trace_pre(s);
+  cudaError_t e = launch_k(klg::gather_rows_kernel, dim3((unsigned)((rows + 7) / 8)), dim3(256), 0, s, 1,
+                           static_cast<const uint8_t*>(diff), static_cast<const uint8_t*>(ar),
+                           reinterpret_cast<const long long*>(anchors), reinterpret_cast<const long long*>(targets),
+                           (int)batch, (int)n_blocks, (int)block, (int)ar_len, (int)row_bytes, (long long)pad_id,
+                           static_cast<uint8_t*>(h_s), static_cast<uint8_t*>(h_t), valid);
+  trace_post(slot, s, KLG_KIND_GATHER);
+  if (e != cudaSuccess) return cuda_fail(e, "launch gather_rows_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
+int klg_scatter_rows_grad(const void* d_hs, int64_t batch, int64_t n_blocks, int64_t block, int64_t row_bytes,
+                          void* d_diff, void* stream) {
+  if (!d_hs || !d_diff) return fail(KLG_ERR_ARG, "null pointer");
+  if (batch < 1 || n_blocks < 1 || block < 2 || row_bytes < 16 || batch * n_blocks * block > (1ll << 31))
+    return fail(KLG_ERR_ARG, "bad row-selection shape");
+  if (row_bytes % 16 != 0 || !aligned16(d_hs) || !aligned16(d_diff))
+    return fail(KLG_ERR_ALIGN, "rows must be 16-byte aligned, row_bytes a multiple of 16");
+  int rc = bind_device(d_hs);
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  const long long rows = batch * n_blocks * block;
+  const int slot = trace_pre(s);
+  cudaError_t e = launch_k(klg::scatter_rows_grad_kernel, dim3((unsigned)((rows + 7) / 8)), dim3(256), 0, s, 1,
+                           static_cast<const uint8_t*>(d_hs), (int)batch, (int)n_blocks, (int)block, (int)row_bytes,
+                           static_cast<uint8_t*>(d_diff));
+  trace_post(slot, s, KLG_KIND_GATHER);
+  if (e != cudaSuccess) return cuda_fail(e, "launch scatter_rows_grad_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
 namespace {
 int check_norm(const void* x, int x_f32, const float* gamma, int64_t n_rows, int64_t hidden) {
   if (!x || !gamma) return fail(KLG_ERR_ARG, "null input pointer");

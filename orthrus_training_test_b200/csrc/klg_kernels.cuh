@@ -1421,6 +1421,62 @@ __global__ void zero_f32x4_kernel(float4* __restrict__ p, long long n4) {
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) p[i] = z;
 }
 
+// ---------------------------------------------------------------- row selection (train.py:124-164)
+// One warp per selected row i = (b, blk, k), k = 1..K-1: student row b*(nb*K) + blk*K + k of
+// diff, teacher row b*L + clamp(anchor[b, blk] + k - 1, 0, L - 1) of ar, valid = target of the
+// student position != pad.  Rows are copied as bytes (any dtype; row_bytes % 16 == 0).
+__global__ void __launch_bounds__(256) gather_rows_kernel(const uint8_t* __restrict__ diff,
+                                                          const uint8_t* __restrict__ ar,
+                                                          const long long* __restrict__ anchors,
+                                                          const long long* __restrict__ targets, int B, int nb,
+                                                          int K, int L, int row_bytes, long long pad,
+                                                          uint8_t* __restrict__ hs, uint8_t* __restrict__ ht,
+                                                          uint8_t* __restrict__ valid) {
+  pdl_enter();
+  const int n = nb * (K - 1);
+  const long long i = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (i >= (long long)B * n) return;
+  const int b = (int)(i / n);
+  const int j = (int)(i - (long long)b * n);
+  const int blk = j / (K - 1);
+  const int k = j - blk * (K - 1) + 1;
+  const long long srow = (long long)b * nb * K + (long long)blk * K + k;
+  long long t = anchors[(size_t)b * nb + blk] + k - 1;
+  t = t < 0 ? 0 : (t > L - 1 ? L - 1 : t);
+  const long long trow = (long long)b * L + t;
+  if (lane == 0) valid[i] = targets[srow] != pad ? 1 : 0;
+  const uint4* s4 = reinterpret_cast<const uint4*>(diff + srow * row_bytes);
+  const uint4* t4 = reinterpret_cast<const uint4*>(ar + trow * row_bytes);
+  uint4* hs4 = reinterpret_cast<uint4*>(hs + i * row_bytes);
+  uint4* ht4 = reinterpret_cast<uint4*>(ht + i * row_bytes);
+  for (int c = lane; c < row_bytes / 16; c += 32) {
+    hs4[c] = s4[c];
+    ht4[c] = t4[c];
+  }
+}
+
+// Backward of the student selection: every diff position (b, p) gets the gradient row of its
+// selected row, or zeros at the anchors (p % K == 0), which carry no loss.
+__global__ void __launch_bounds__(256) scatter_rows_grad_kernel(const uint8_t* __restrict__ dhs, int B, int nb, int K,
+                                                                int row_bytes, uint8_t* __restrict__ ddiff) {
+  pdl_enter();
+  const long long p = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (p >= (long long)B * nb * K) return;
+  const int b = (int)(p / ((long long)nb * K));
+  const int pos = (int)(p - (long long)b * nb * K);
+  const int k = pos % K;
+  uint4* d4 = reinterpret_cast<uint4*>(ddiff + p * row_bytes);
+  if (k == 0) {
+    for (int c = lane; c < row_bytes / 16; c += 32) d4[c] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const long long i = (long long)b * nb * (K - 1) + (long long)(pos / K) * (K - 1) + k - 1;
+  const uint4* s4 = reinterpret_cast<const uint4*>(dhs + i * row_bytes);
+  for (int c = lane; c < row_bytes / 16; c += 32) d4[c] = s4[c];
+}
+
 // ---------------------------------------------------------------- final RMSNorm (pre-norm inputs)
 // The backbone's final norm (LlamaRMSNorm): r = 1 / sqrt(mean_k x_k^2 + eps) in fp32, and
 // bf16 rows  y = bf16(gamma * bf16(x r))  for bf16 x (the norm's own rounding to the input

@@ -12,7 +12,9 @@ from typing import Optional, Tuple
 
 import torch
 
-from .ops import KLGemmFn, PrenormKLGemmFn
+from . import _lib  # noqa: F401  (loads the library)
+from ._lib import call
+from .ops import KLGemmFn, PrenormKLGemmFn, _ptr, _require_cuda, _stream
 
 _index_cache: dict = {}
 
@@ -37,7 +39,8 @@ def kl_indices(B: int, B_blocks: int, K: int, device) -> Tuple[torch.Tensor, tor
 
 
 def select_rows(diff_hidden, ar_hidden_states, anchor_positions, K, target_ids, pad_token_id):
-    """Aligned ``(h_s [B*N, H], h_t [B*N, H], valid [B*N])`` of train.py:156-164.
+    """Aligned ``(h_s [B*N, H], h_t [B*N, H], valid [B*N])`` of train.py:156-164 in torch
+    index ops (any device; the loss uses the one-kernel :func:`gather_rows`).
 
     Teacher row = ``anchor + k - 1`` clamped to ``[0, L-1]`` (train.py:161);
     valid = ``target != pad_token_id`` (train.py:163-164).  The student gather
@@ -52,6 +55,53 @@ def select_rows(diff_hidden, ar_hidden_states, anchor_positions, K, target_ids, 
     h_s = diff_hidden[batch_idx, diff_pos].reshape(B * N, -1)
     h_t = ar_hidden_states[batch_idx, ar_pos].reshape(B * N, -1)
     return h_s, h_t, valid.reshape(-1)
+
+
+class GatherRowsFn(torch.autograd.Function):
+    """The row selection of train.py:124-139, 156-164 as one CUDA kernel.
+
+    ``(h_s [B*N, H], h_t [B*N, H], valid [B*N] uint8)`` with ``N = B_blocks*(K-1)``: the
+    student rows ``diff_hidden[b, blk*K + k]`` (k = 1..K-1), the teacher rows
+    ``ar_hidden[b, clamp(anchor + k - 1, 0, L-1)]`` and ``target != pad``.  The backward
+    writes the student rows' gradient back to their positions of ``diff_hidden`` (zeros at
+    the anchors), in one kernel as well.  ``h_t`` and ``valid`` carry no gradient (the
+    teacher is detached, train.py:183).
+    """
+
+    @staticmethod
+    def forward(ctx, diff_hidden, ar_hidden_states, anchor_positions, K, target_ids, pad_token_id):
+        dev = _require_cuda(diff_hidden, ar_hidden_states, anchor_positions, target_ids)
+        diff = diff_hidden.detach().contiguous()
+        ar = ar_hidden_states.detach().to(diff.dtype).contiguous()
+        B, P, H = diff.shape
+        Bb = anchor_positions.shape[1]
+        if P != Bb * K:
+            raise ValueError(f"diff_hidden has {P} positions, expected B_blocks*K = {Bb * K}")
+        row_bytes = H * diff.element_size()
+        anchors = anchor_positions.detach().to(torch.int64).contiguous()
+        targets = target_ids.detach().to(torch.int64).contiguous()
+        n = B * Bb * (K - 1)
+        h_s = torch.empty(n, H, dtype=diff.dtype, device=dev)
+        h_t = torch.empty(n, H, dtype=diff.dtype, device=dev)
+        valid = torch.empty(n, dtype=torch.uint8, device=dev)
+        call("klg_gather_rows", _ptr(diff), _ptr(ar), _ptr(anchors), _ptr(targets), B, Bb, K, ar.shape[1], row_bytes,
+             int(pad_token_id), _ptr(h_s), _ptr(h_t), _ptr(valid), _stream(dev))
+        ctx.meta = (B, Bb, K, H, diff.dtype, row_bytes)
+        ctx.mark_non_differentiable(h_t, valid)
+        return h_s, h_t, valid
+
+    @staticmethod
+    def backward(ctx, g_hs, g_ht, g_valid):
+        B, Bb, K, H, dtype, row_bytes = ctx.meta
+        g = g_hs.detach().to(dtype).contiguous()
+        d_diff = torch.empty(B, Bb * K, H, dtype=dtype, device=g.device)
+        call("klg_scatter_rows_grad", _ptr(g), B, Bb, K, row_bytes, _ptr(d_diff), _stream(g.device))
+        return d_diff, None, None, None, None, None
+
+
+def gather_rows(diff_hidden, ar_hidden_states, anchor_positions, K, target_ids, pad_token_id):
+    """``(h_s, h_t, valid)`` of :func:`select_rows`, computed by one CUDA kernel."""
+    return GatherRowsFn.apply(diff_hidden, ar_hidden_states, anchor_positions, int(K), target_ids, int(pad_token_id))
 
 
 def compute_kl_loss(diff_hidden: torch.Tensor, ar_hidden_states: torch.Tensor, lm_head: torch.nn.Module,
@@ -69,7 +119,7 @@ def compute_kl_loss(diff_hidden: torch.Tensor, ar_hidden_states: torch.Tensor, l
     """
     if getattr(lm_head, "bias", None) is not None:
         raise ValueError("lm_head with a bias is not supported (the reference's tied lm_head has none)")
-    h_s, h_t, valid = select_rows(diff_hidden, ar_hidden_states, anchor_positions, K, target_ids, pad_token_id)
+    h_s, h_t, valid = gather_rows(diff_hidden, ar_hidden_states, anchor_positions, K, target_ids, pad_token_id)
     if not bool(valid.any()):
         return torch.tensor(0.0, device=diff_hidden.device, requires_grad=True)
     if norm_weight is not None:
