@@ -13,8 +13,9 @@
 // buffer of the tile's parity; the softmax warp group of that parity (four warps, one TMEM
 // lane = one row per thread) takes the masked online max / sum in log2 units and writes
 // P = 2^(s - m) as bf16 into its 128-byte-swizzled K-major shared tile; O_tile = P V
-// (M = 128, N = 64, K = keys; V read MN-major) lands in the parity's TMEM O buffer and is
-// accumulated with the running rescale in registers.  The MMA warp issues S one tile ahead,
+// (M = 128, N = 64, K = keys; V read MN-major) accumulates in the parity's TMEM O buffer
+// (the group rescales that buffer in place on the rare tiles where a row's reference max
+// moves, and reads it once at the end).  The MMA warp issues S one tile ahead,
 // so the two groups (two warps per SM sub-partition) work on consecutive tiles at once;
 // at the end the odd group's (m, l, O) is merged into the even group's through shared
 // memory.  Each CTA writes its rows' record; block_attn_merge_kernel combines the splits
@@ -125,8 +126,7 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
   const uint32_t sfull0 = qbar + 8u;                  // [2] S tile in TMEM (per parity)
   const uint32_t sempty0 = sfull0 + 16u;              // [2] the parity's softmax warps read it
   const uint32_t pfull0 = sempty0 + 16u;              // [2] P written to shared memory
-  const uint32_t ofull0 = pfull0 + 16u;               // [2] O tile in TMEM
-  const uint32_t oempty0 = ofull0 + 16u;              // [2] the parity's softmax warps read it
+  const uint32_t ofull0 = pfull0 + 16u;               // [2] the parity's latest P V retired
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int u = blockIdx.x / a.splits;
@@ -148,7 +148,6 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
       mbar_init(sempty0 + 8u * s, 4);
       mbar_init(pfull0 + 8u * s, 4);
       mbar_init(ofull0 + 8u * s, 1);
-      mbar_init(oempty0 + 8u * s, 4);
     }
     fence_mbar_init();
     tma_prefetch(&map_q);
@@ -245,7 +244,6 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
       const int stage = i % ATT_STAGES;
       const int nk = i < n_my ? ATT_BN : a.K;
       if (!warp_wait(pfull0 + 8u * par, (uint32_t)(i >> 1) & 1u, abort_p, KLG_STATUS_TIMEOUT_MMA)) break;
-      if (!warp_wait(oempty0 + 8u * par, ((uint32_t)(i >> 1) & 1u) ^ 1u, abort_p, KLG_STATUS_TIMEOUT_MMA)) break;
       tc_fence_after();
       if (elect_one()) {
         const uint32_t idesc = make_idesc_bf16(128, ATT_D, false, true);
@@ -253,7 +251,7 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
         const uint32_t pp = p_s + par * ATT_P_BYTES;
         for (int k = 0; k < nk / 16; ++k)
           mma_bf16(tmem + ATT_O_COL + par * ATT_D, desc_kmajor(pp + (k >> 2) * 16384, k & 3), desc_mnmajor(vs, k),
-                   idesc, k != 0);
+                   idesc, (k != 0 || i >= 2) ? 1u : 0u);   // the parity's first tile starts O
         mma_commit(ofull0 + 8u * par);
         mma_commit(empty0 + 8u * stage);
       }
@@ -269,21 +267,24 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
     const uint32_t lrow = tmem + ((uint32_t)(q4 * 32) << 16);
     const uint32_t prow = p_s + par * ATT_P_BYTES + (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u;
     float m = NEG_BIG, l = 0.f;
-    float o[ATT_D];
-#pragma unroll
-    for (int j = 0; j < ATT_D; ++j) o[j] = 0.f;
     bool ok = true;
+    int n_pv = 0;   // P V products this group handed to the MMA warp
     for (int i = par; ok && i < ntiles; i += 2) {
       const bool self = i >= n_my;
       const int nk = self ? a.K : ATT_BN;
       const int kmax = self ? a.K - 1 : lim - (t0 + i) * ATT_BN;   // last visible key of the tile
       const int sb = par;
-      const uint32_t jph = (uint32_t)(i >> 1) & 1u;   // this parity's use count of its buffers
+      const uint32_t jph = (uint32_t)(i >> 1) & 1u;   // this parity's use count of its S buffer
       if (!mbar_wait(sfull0 + 8u * sb, jph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      // P of this parity's previous tile is still an MMA operand until its P V completes
+      if (n_pv > 0 && !mbar_wait(ofull0 + 8u * sb, (uint32_t)(n_pv - 1) & 1u, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) {
+        ok = false;
+        break;
+      }
       const int nch = (nk + 31) >> 5;
       // every key of the tile visible to all 32 rows of the warp: no per-key mask
       const bool open = __all_sync(0xffffffffu, kmax >= nk - 1) && (nk & 31) == 0;
@@ -313,6 +314,21 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
       const float alpha = ex2(m - mn);
       l = fmaf(l, alpha, sum);
       m = mn;
+      // a moved reference: rescale the O accumulated so far (its last P V completed above)
+      if (n_pv > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        tc_fence_after();
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t v[32];
+          tmem_ld32_raw(lrow + ATT_O_COL + par * ATT_D + h * 32, v);
+          tmem_wait_ld_regs(v);
+          float w[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) w[j] = __uint_as_float(v[j]) * alpha;
+          tmem_st32(lrow + ATT_O_COL + par * ATT_D + h * 32, w);
+        }
+        tmem_wait_st();
+      }
       tc_fence_before();
       fence_async_shared();
       __syncwarp();
@@ -320,10 +336,14 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
         mbar_arrive(sempty0 + 8u * sb);
         mbar_arrive(pfull0 + 8u * sb);
       }
-      if (!mbar_wait(ofull0 + 8u * sb, jph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) {
-        ok = false;
-        break;
-      }
+      ++n_pv;
+    }
+    // the group's O: its last P V retired (bounded wait even after an abort, so no MMA is in
+    // flight when TMEM is freed)
+    float o[ATT_D];
+    bool have = false;
+    if (n_pv > 0 && (ok ? mbar_wait(ofull0 + 8u * par, (uint32_t)(n_pv - 1) & 1u, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)
+                        : mbar_wait_drain(ofull0 + 8u * par, (uint32_t)(n_pv - 1) & 1u))) {
       tc_fence_after();
       uint32_t v0[32], v1[32];
       tmem_ld32_raw(lrow + ATT_O_COL + par * ATT_D, v0);
@@ -331,14 +351,12 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
       tmem_wait_ld_regs(v0, v1);
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        o[j] = fmaf(o[j], alpha, __uint_as_float(v0[j]));
-        o[32 + j] = fmaf(o[32 + j], alpha, __uint_as_float(v1[j]));
+        o[j] = __uint_as_float(v0[j]);
+        o[32 + j] = __uint_as_float(v1[j]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(oempty0 + 8u * sb);
+      have = ok;
     }
-    if (!ok) {   // a group that gave up contributes nothing
+    if (!have) {   // no tile, or a group that gave up: contributes nothing
       m = NEG_BIG;
       l = 0.f;
 #pragma unroll
