@@ -922,7 +922,10 @@ int sample_plan(int64_t n_rows, int64_t vocab, klg::LseArgs& la) {
 // Record groups of the first merge launch: one when the rows alone give the GPU enough
 // blocks, else groups of ~32 records (two per warp) merged again by a second launch.
 int sample_merge_groups(int64_t n_rows, int n_part) {
-  if (cdiv(n_rows, 32) >= num_sms() || n_part <= 64) return 1;
+#ifndef KLG_SMERGE_SINGLE
+#define KLG_SMERGE_SINGLE 64
+#endif
+  if (cdiv(n_rows, 32) >= num_sms() || n_part <= KLG_SMERGE_SINGLE) return 1;
   const int g = cdiv(n_part, 32);
   return g < 64 ? g : 64;
 }

@@ -1285,7 +1285,10 @@ __global__ void lse_merge_kernel(const float* __restrict__ parts, int n_part, in
 // out_parts set, each group writes one merged record [gridDim.y][5][N] for a second launch
 // (one group) to finish: a few rows with hundreds of records are then not a serial chain
 // of loads on one SM.
-constexpr int SMERGE_WARPS = 16;
+#ifndef KLG_SMERGE_WARPS
+#define KLG_SMERGE_WARPS 16
+#endif
+constexpr int SMERGE_WARPS = KLG_SMERGE_WARPS;
 __device__ __forceinline__ void merge_best(float k, int idx, float z, float& bk, int& bi, float& bz) {
   const bool take = idx >= 0 && (k > bk || (k == bk && idx < bi));
   bk = take ? k : bk;
