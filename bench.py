@@ -421,6 +421,7 @@ def run_attn(args):
     """One step = one layer's diffusion attention (model.py:136-176) over the config's
     queries: the fused kernel against torch SDPA with the same boolean mask on the same GPU,
     and the float64 oracle on the host."""
+    import numpy as np
     import torch
     import torch.nn.functional as F
 
@@ -429,10 +430,32 @@ def run_attn(args):
     from orthrus_training_test_b200.attention import block_attention, workspace_bytes
 
     B, H, Hkv, K, Ld, AL, desc = ATTN_CONFIGS[args.config]
-    if int(os.environ.get("WORLD_SIZE", "1")) > 1 or args.impl == "reference":
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
         if int(os.environ.get("RANK", "0")) == 0:
-            emit({"metric": ATTN_METRIC, "impl": args.impl, "unavailable":
-                  "attention workloads run on one GPU; the reference arm is the SDPA line inside ours"})
+            emit({"metric": ATTN_METRIC, "impl": args.impl, "unavailable": "attention workloads run on one GPU"})
+        return
+    if args.impl == "reference":
+        # the attention semantics of the reference's flex path (model.py:45-96, 435-446) in the
+        # float64 oracle on the host, one block of K positions x H heads per step
+        g = torch.Generator().manual_seed(3)
+        q = torch.randn(1, H, K, 64, generator=g).numpy()
+        ks, vs = torch.randn(1, Hkv, K, 64, generator=g).numpy(), torch.randn(1, Hkv, K, 64, generator=g).numpy()
+        ka, va = torch.randn(1, Hkv, AL, 64, generator=g).numpy(), torch.randn(1, Hkv, AL, 64, generator=g).numpy()
+        lim = np.full((1, K), AL // 2 if Ld > K else AL - 1)
+        for _ in range(max(1, args.warmup)):
+            O.block_attention_np(q, ks, vs, ka, va, lim, K)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            O.block_attention_np(q, ks, vs, ka, va, lim, K)
+        dt = time.perf_counter() - t0
+        value = H * K * args.steps / dt
+        emit({"metric": ATTN_METRIC, "value": value, "unit": "rows/s", "n_gpus": args.gpus, "steps": args.steps,
+              "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
+              "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded)", "impl": "reference",
+              "config": {"workload": f"{args.config}: {desc}", "rows_per_step_sample": H * K, "parallelism": "host CPU"},
+              "cpu_baseline": {"value": value, "unit": "rows/s", "cores": 1, "kind": "port",
+                               "sample": f"one block of {K} positions x {H} heads per step: the float64 oracle"},
+              "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
         return
     dev = torch.device("cuda:0")
     torch.cuda.set_device(dev)
