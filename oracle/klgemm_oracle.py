@@ -2,7 +2,8 @@
 
 TEST INFRASTRUCTURE ONLY.  The product (``orthrus_training_test_b200``) never
 imports this module; ``tests/``, ``__graft_entry__.smoke()`` and the
-CPU-baseline leg of ``bench.py`` use it as the checker / CPU baseline.
+CPU-baseline leg of ``bench.py`` use it for the expected results of parity
+checks and as the CPU baseline.
 
 Parity pin: every function here is checked against golden vectors produced by
 running the reference's own ``train.compute_kl_loss`` (reference
