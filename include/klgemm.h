@@ -228,6 +228,13 @@ int klg_block_attn_fwd(const void* q, const void* k_self, const void* v_self, co
                        int64_t diff_len, int64_t block, int64_t ar_len, int64_t head_dim, float scale, void* out,
                        float* lse, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* The logit z[i] = h[i] . W[tokens[i]] (fp32 accumulate of bf16 rows) of a token chosen
+ * elsewhere -- with the lse of klg_lm_head_sample, exp(z * inv_temp - lse) is that token's
+ * probability, the value the consensus step of generate.py:201-202 reads from the other
+ * distribution's probs.  tokens [N] int32; a token outside [0, vocab) gives NaN. */
+int klg_token_logit(const void* h, const void* w, const int32_t* tokens, int64_t n_rows, int64_t hidden, int64_t vocab,
+                    float* z, void* stream);
+
 /* fp32 -> bf16 conversion (round to nearest even) for fp32 callers. */
 int klg_cast_f32_bf16(const float* in, void* out, int64_t n, void* stream);
 

@@ -32,6 +32,7 @@ SIGNATURES = {
     "klg_block_attn_workspace_bytes": (c_longlong, [c_longlong] * 7),
     "klg_block_attn_fwd": (c_int, [c_void_p] * 5 + [c_longlong, c_void_p] + [c_longlong] * 7 +
                            [c_float, c_void_p, c_void_p, c_void_p, c_longlong, c_void_p]),
+    "klg_token_logit": (c_int, [c_void_p, c_void_p, c_void_p] + [c_longlong] * 3 + [c_void_p, c_void_p]),
     "klg_gather_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p] + [c_longlong] * 6 +
                         [c_void_p, c_void_p, c_void_p, c_void_p]),
     "klg_scatter_rows_grad": (c_int, [c_void_p] + [c_longlong] * 4 + [c_void_p, c_void_p]),

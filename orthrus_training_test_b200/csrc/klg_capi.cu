@@ -1179,6 +1179,26 @@ int klg_block_attn_fwd(const void* q, const void* k_self, const void* v_self, co
   return KLG_OK;
 }
 
+int klg_token_logit(const void* h, const void* w, const int32_t* tokens, int64_t n_rows, int64_t hidden, int64_t vocab,
+                    float* z, void* stream) {
+  if (!h || !w || !tokens || !z) return fail(KLG_ERR_ARG, "null pointer");
+  if (n_rows < 1 || hidden < 8 || vocab < 1 || n_rows > (1ll << 30) || hidden > (1ll << 20) || vocab > (1ll << 30))
+    return fail(KLG_ERR_ARG, "bad shape N=%lld H=%lld V=%lld", (long long)n_rows, (long long)hidden, (long long)vocab);
+  if (hidden % 8 != 0 || !aligned16(h) || !aligned16(w))
+    return fail(KLG_ERR_ALIGN, "hidden must be a multiple of 8 and rows 16-byte aligned");
+  int rc = bind_device(h);
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int slot = trace_pre(s);
+  cudaError_t e = launch_k(klg::token_logit_kernel, dim3(cdiv(n_rows, 8)), dim3(256), 0, s, 1,
+                           static_cast<const __nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(w), tokens,
+                           (int)n_rows, (int)hidden, (int)vocab, z);
+  trace_post(slot, s, KLG_KIND_SAMPLE);
+  if (e != cudaSuccess) return cuda_fail(e, "launch token_logit_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
 int klg_cast_f32_bf16(const float* in, void* out, int64_t n, void* stream) {
   if (!in || !out || n < 0) return fail(KLG_ERR_ARG, "bad arguments to klg_cast_f32_bf16");
   if (n == 0) return KLG_OK;

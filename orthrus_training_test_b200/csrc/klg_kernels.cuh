@@ -1594,6 +1594,33 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_bwd_kernel(const void* __res
   }
 }
 
+// ---------------------------------------------------------------- logit of a given token
+// z[i] = h[i] . W[tokens[i]] in fp32 from bf16 rows (one warp per row, 16-byte loads): the
+// logit the fused sampler never writes out, for a token chosen elsewhere.
+__global__ void __launch_bounds__(256) token_logit_kernel(const __nv_bfloat16* __restrict__ h,
+                                                          const __nv_bfloat16* __restrict__ w,
+                                                          const int* __restrict__ tokens, int n, int hidden, int vocab,
+                                                          float* __restrict__ z) {
+  pdl_enter();
+  const int i = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (i >= n) return;
+  const int t = tokens[i];
+  float acc = 0.f;
+  if (t >= 0 && t < vocab) {
+    const size_t hr = (size_t)i * hidden, wr = (size_t)t * hidden;
+    for (int c = lane * 8; c < hidden; c += 256) {
+      float a[8], b[8];
+      load8<false>(h, hr + c, a);
+      load8<false>(w, wr + c, b);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc = fmaf(a[j], b[j], acc);
+    }
+  }
+  acc = warp_sum_f32(acc);
+  if (lane == 0) z[i] = (t >= 0 && t < vocab) ? acc : __int_as_float(0x7fc00000);   // NaN for a token out of range
+}
+
 __global__ void cast_f32_bf16_kernel(const float* __restrict__ in, __nv_bfloat16* __restrict__ out, long long n) {
   pdl_enter();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;

@@ -90,3 +90,23 @@ def sample_token(hidden: torch.Tensor, weight: torch.Tensor, temperature: float 
     if temperature < GREEDY_TEMPERATURE:
         return tokens, None
     return tokens, torch.exp(logit / float(temperature) - lse).view(lead)
+
+
+def token_logprob(h: torch.Tensor, weight: torch.Tensor, tokens: torch.Tensor, lse: torch.Tensor,
+                  temperature: float = 1.0) -> torch.Tensor:
+    """``log p(token)`` under ``softmax(h @ weight^T / T)`` for tokens chosen elsewhere.
+
+    ``lse`` is :func:`lm_head_sample`'s output for the same rows and temperature.  This is
+    what the consensus step reads as ``p_prob = ar_probs[0, i, diff_tokens[0, i]]``
+    (generate.py:201-202): the AR distribution's probability of the diffusion head's token,
+    here without the ``[N, V]`` probability tensor.  Returns fp32 ``[N]``.
+    """
+    dev = _require_cuda(h, weight, tokens, lse)
+    h = to_compute_dtype(h)
+    weight = to_compute_dtype(weight)
+    N, H = h.shape
+    tok = tokens.detach().to(torch.int32).contiguous()
+    z = torch.empty(N, dtype=torch.float32, device=dev)
+    call("klg_token_logit", _ptr(h), _ptr(weight), _ptr(tok), N, H, weight.shape[0], _ptr(z), _stream(dev))
+    T = float(temperature) if temperature >= GREEDY_TEMPERATURE else 1.0
+    return z / T - lse

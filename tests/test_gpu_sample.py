@@ -133,3 +133,18 @@ def test_sample_token_wrapper_shapes_and_errors():
     assert tok1.shape == ()
     with pytest.raises(NotImplementedError):
         sampling.sample_token(hd, wd, 0.8, top_k=5)
+
+
+def test_token_logprob_of_another_distribution():
+    """The consensus step's p_prob (generate.py:201-202): the probability, under the AR rows'
+    distribution, of tokens drawn from the diffusion rows' distribution."""
+    from orthrus_training_test_b200 import sampling
+    N, H, V, T = 31, 576, 49153, 0.9
+    h_d, W = _problem(N, H, V, seed=41, scale=4.0)
+    h_a, _ = _problem(N, H, V, seed=42, scale=4.0)
+    tok, _, _ = _run(h_d, W, T, seed=5)
+    _, _, lse_a = sampling.lm_head_sample(h_a.to(_dev()), W.to(_dev()), T, 6)
+    lp = sampling.token_logprob(h_a.to(_dev()), W.to(_dev()), torch.tensor(tok).to(_dev()), lse_a, T)
+    z = h_a.double().numpy() @ W.double().numpy().T
+    ref = z[np.arange(N), tok] / T - O._lse(z / T)
+    np.testing.assert_allclose(lp.cpu().numpy(), ref, rtol=0, atol=1e-3)
