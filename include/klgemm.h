@@ -220,7 +220,9 @@ int klg_rmsnorm_rows_bwd(const void* x, int x_f32, const float* gamma, const flo
  *   q [B, H, Ld, 64], k_self / v_self [B, Hkv, Ld, 64] (bf16, contiguous),
  *   k_ar / v_ar: rows 0..ar_len-1 of a [B, Hkv, ar_stride, 64] bf16 cache,
  *   limits [B, Ld] int32; out [B, H, Ld, 64] bf16; lse [B, H, Ld] fp32 natural log (may be NULL).
- * head_dim 64; K a multiple of 16, <= 128; Ld a multiple of K. */
+ * head_dim 64; K a multiple of 16, <= 128; Ld a multiple of K.  The workspace is a token
+ * 16 bytes (the key-range splits of a decode call combine on chip); the parameter stays so
+ * that a later variant can use global scratch without an interface change. */
 int64_t klg_block_attn_workspace_bytes(int64_t batch, int64_t heads, int64_t kv_heads, int64_t diff_len,
                                        int64_t block, int64_t ar_len, int64_t head_dim);
 int klg_block_attn_fwd(const void* q, const void* k_self, const void* v_self, const void* k_ar, const void* v_ar,

@@ -18,9 +18,11 @@
 // moves, and reads it once at the end).  The MMA warp issues S one tile ahead,
 // so the two groups (two warps per SM sub-partition) work on consecutive tiles at once;
 // at the end the odd group's (m, l, O) is merged into the even group's through shared
-// memory.  Each CTA writes its rows' record; block_attn_merge_kernel combines the splits
-// and writes bf16 O and the natural-log log-sum-exp (with a single split the kernel writes
-// them itself and no merge runs).
+// memory.  With one split the CTA writes bf16 O and the natural-log log-sum-exp itself.
+// With several (decode: few units, the AR range split over up to 8 CTAs), the splits of a
+// unit form one thread-block cluster: each CTA leaves its rows' (O, m, l) record in its own
+// shared memory, and after a cluster barrier every CTA combines a share of the rows from all
+// the records through distributed shared memory and writes them.
 #pragma once
 #include "klg_kernels.cuh"
 
@@ -40,13 +42,11 @@ constexpr int ATT_O_COL = 256;
 
 struct AttnArgs {
   const int* limits;   // [B, Ld] causal limit per query position (AR keys 0..limit)
-  float* part_o;       // [n_cta][128][64] unnormalised O per split
-  float* part_ml;      // [n_cta][2][128] (m in log2 units, l)
-  __nv_bfloat16* out;  // with one split the kernel writes O [B, H, Ld, 64] and lse itself
-  float* lse;
+  __nv_bfloat16* out;  // O [B, H, Ld, 64]
+  float* lse;          // [B, H, Ld] natural log, or null
   int B, H, Hkv, Ld, K, ar_len;
   int ng, hg, n_hg, nb;   // query heads per KV head, per unit; head groups; blocks
-  int n_units, splits, tps;   // tps: AR tiles per split
+  int n_units, splits, tps;   // splits = cluster size (<= 8); tps: AR tiles per split
   float sl2;                  // scale * log2(e)
 };
 
@@ -395,66 +395,55 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
           if (a.lse) a.lse[row] = (m + __log2f(l)) * 0.69314718055994530942f;
         }
       } else {
-        // this split's record for the row (also written when the split had no tiles)
-        float4* po = reinterpret_cast<float4*>(a.part_o + ((size_t)blockIdx.x * 128 + r) * ATT_D);
+        // this split's record of the row, in place of the odd group's state it just read
+        // (same thread, same row); also written when the split had no tiles
 #pragma unroll
-        for (int j = 0; j < ATT_D / 4; ++j) po[j] = make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
-        a.part_ml[(size_t)blockIdx.x * 256 + r] = m;
-        a.part_ml[(size_t)blockIdx.x * 256 + 128 + r] = l;
+        for (int j = 0; j < ATT_D; ++j) x[j] = o[j];
+        x[ATT_D] = m;
+        x[ATT_D + 1] = l;
       }
     }
+  }
+  if (a.splits > 1) {
+    cluster_sync();   // every split's records of the unit are in its CTA's shared memory
+    const uint32_t rank = cluster_rank();
+    const uint32_t xbase = smem_u32(xch);
+    // rows rank, rank + splits, ...: one warp per row, lane j reads split j's (m, l) and then
+    // two head-dimension columns of every split's O
+    for (int rr = (int)rank + a.splits * warp; rr < rows; rr += a.splits * (ATT_THREADS / 32)) {
+      const uint32_t rec = xbase + (uint32_t)(rr * (ATT_D + 2)) * 4u;
+      float mj = NEG_BIG, lj = 0.f;
+      if (lane < a.splits) {
+        const uint32_t peer = mapa_shared(rec, (uint32_t)lane);
+        mj = ld_shared_cluster_f32(peer + ATT_D * 4);
+        lj = ld_shared_cluster_f32(peer + (ATT_D + 1) * 4);
+      }
+      float M = mj;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+      const float w = lane < a.splits ? ex2(mj - M) : 0.f;
+      float L = lj * w;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+      float o0 = 0.f, o1 = 0.f;
+      for (int sp2 = 0; sp2 < a.splits; ++sp2) {
+        const float wp = __shfl_sync(0xffffffffu, w, sp2);
+        const uint32_t peer = mapa_shared(rec + (uint32_t)(2 * lane) * 4u, (uint32_t)sp2);
+        o0 = fmaf(ld_shared_cluster_f32(peer), wp, o0);
+        o1 = fmaf(ld_shared_cluster_f32(peer + 4), wp, o1);
+      }
+      const int h = hkv * a.ng + hgi * a.hg + rr / a.K;
+      const size_t row = ((size_t)b * a.H + h) * a.Ld + blk * a.K + rr % a.K;
+      const float inv = L > 0.f ? 1.0f / L : 0.f;
+      reinterpret_cast<uint32_t*>(a.out + row * ATT_D)[lane] = pack_bf16x2(o0 * inv, o1 * inv);
+      if (a.lse && lane == 0) a.lse[row] = (M + __log2f(L)) * 0.69314718055994530942f;
+    }
+    cluster_sync();   // no CTA leaves while a peer may still read its records
   }
   tc_fence_before();
   __syncthreads();   // every MMA retired (the softmax warps consumed the last O tile) before TMEM is freed
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, ATT_TMEM_COLS);
-}
-
-// Combines the splits of each unit row: O = sum_s O_s 2^(m_s - M) / sum_s l_s 2^(m_s - M),
-// written as bf16 to out [B, H, Ld, 64]; lse [B, H, Ld] = (M + log2 L) ln 2.  One warp per
-// row: lane j reads split j's (m, l) (32 at a time, reduced across the warp), then each lane
-// accumulates two head-dimension columns over the splits (independent loads, unrolled).
-__global__ void __launch_bounds__(256) block_attn_merge_kernel(const AttnArgs a, __nv_bfloat16* __restrict__ out,
-                                                              float* __restrict__ lse) {
-  pdl_enter();
-  const int rows = a.hg * a.K;
-  const long long gw = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (gw >= (long long)a.n_units * rows) return;
-  const int u = (int)(gw / rows);
-  const int r = (int)(gw - (long long)u * rows);
-  int b, hkv, hgi, blk;
-  attn_unit(a, u, b, hkv, hgi, blk);
-  const size_t c0 = (size_t)u * a.splits;
-  float M = NEG_BIG;
-  for (int s0 = 0; s0 < a.splits; s0 += 32)
-    if (s0 + lane < a.splits) M = fmaxf(M, a.part_ml[(c0 + s0 + lane) * 256 + r]);
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-  float L = 0.f, o0 = 0.f, o1 = 0.f;
-  for (int s0 = 0; s0 < a.splits; s0 += 32) {
-    const int n = min(32, a.splits - s0);
-    float w = 0.f;
-    if (lane < n) {
-      const size_t c = c0 + s0 + lane;
-      w = ex2(a.part_ml[c * 256 + r] - M);
-      L = fmaf(a.part_ml[c * 256 + 128 + r], w, L);
-    }
-#pragma unroll 4
-    for (int j = 0; j < n; ++j) {
-      const float wj = __shfl_sync(0xffffffffu, w, j);
-      const float2 v = reinterpret_cast<const float2*>(a.part_o + ((c0 + s0 + j) * 128 + r) * ATT_D)[lane];
-      o0 = fmaf(v.x, wj, o0);
-      o1 = fmaf(v.y, wj, o1);
-    }
-  }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-  const int h = hkv * a.ng + hgi * a.hg + r / a.K;
-  const size_t row = ((size_t)b * a.H + h) * a.Ld + blk * a.K + r % a.K;
-  const float inv = 1.0f / L;
-  reinterpret_cast<uint32_t*>(out + row * ATT_D)[lane] = pack_bf16x2(o0 * inv, o1 * inv);
-  if (lse && lane == 0) lse[row] = (M + __log2f(L)) * 0.69314718055994530942f;
 }
 
 }  // namespace klg

@@ -1110,13 +1110,13 @@ int attn_plan(int64_t B, int64_t H, int64_t Hkv, int64_t Ld, int64_t K, int64_t 
   a.nb = (int)(Ld / K);
   a.n_units = a.B * a.Hkv * a.n_hg * a.nb;
   const int n_ar = cdiv(ar_len, klg::ATT_BN);
-  // few units (decode): split the AR keys so that about two CTAs per SM exist
+  // few units (decode): split the AR keys over a cluster of up to 8 CTAs (the portable
+  // cluster size), aiming at about two CTAs per SM
   int splits = cdiv(2 * num_sms(), a.n_units);
-  splits = std::max(1, std::min(splits, n_ar));
+  splits = std::max(1, std::min(std::min(splits, n_ar), 8));
   a.tps = cdiv(n_ar, splits);
   a.splits = cdiv(n_ar, a.tps);
-  const int64_t n_cta = (int64_t)a.n_units * a.splits;
-  P.ws_bytes = a.splits > 1 ? n_cta * 128 * (klg::ATT_D + 2) * 4 : 16;   // one split writes the output directly
+  P.ws_bytes = 16;   // the splits combine through distributed shared memory: no global scratch
   return KLG_OK;
 }
 }  // namespace
@@ -1147,8 +1147,6 @@ int klg_block_attn_fwd(const void* q, const void* k_self, const void* v_self, co
   cudaStream_t s = (cudaStream_t)stream;
   klg::AttnArgs a = P.a;
   a.limits = limits;
-  a.part_o = static_cast<float*>(workspace);
-  a.part_ml = a.part_o + (size_t)a.n_units * a.splits * 128 * klg::ATT_D;
   a.sl2 = scale * 1.4426950408889634f;
   a.out = static_cast<__nv_bfloat16*>(out);
   a.lse = lse;
@@ -1163,18 +1161,10 @@ int klg_block_attn_fwd(const void* q, const void* k_self, const void* v_self, co
   cudaError_t e = set_smem(klg::block_attn_kernel, klg::ATT_SMEM);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(block_attn_kernel)");
   int slot = trace_pre(s);
-  e = launch_k(klg::block_attn_kernel, dim3(a.n_units * a.splits), dim3(klg::ATT_THREADS), klg::ATT_SMEM, s, 1, mq, mks,
-               mvs, mka, mva, a);
+  e = launch_k(klg::block_attn_kernel, dim3(a.n_units * a.splits), dim3(klg::ATT_THREADS), klg::ATT_SMEM, s, a.splits,
+               mq, mks, mvs, mka, mva, a);
   trace_post(slot, s, KLG_KIND_ATTN);
   if (e != cudaSuccess) return cuda_fail(e, "launch block_attn_kernel");
-  ++g_launches;
-  if (a.splits == 1) return KLG_OK;
-  const long long warps = (long long)a.n_units * a.hg * a.K;
-  slot = trace_pre(s);
-  e = launch_k(klg::block_attn_merge_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, s, 1, a,
-               static_cast<__nv_bfloat16*>(out), lse);
-  trace_post(slot, s, KLG_KIND_MERGE);
-  if (e != cudaSuccess) return cuda_fail(e, "launch block_attn_merge_kernel");
   ++g_launches;
   return KLG_OK;
 }
