@@ -5,8 +5,8 @@
  * the Python entry point is compute_kl_loss (train.py:142-195), its compiled
  * chunk body _kl_chunk_body (train.py:198-210), and the teacher-probability
  * precompute it consumes (train.py:549-567).  The binding a Python caller
- * uses (ctypes) is orthrus_training_test_b200/_lib.py; INTEGRATION.md shows
- * how the reference's call site reaches it.
+ * uses (ctypes) is orthrus_training_test_b200/_lib.py, which the drop-in
+ * compute_kl_loss shim (orthrus_training_test_b200/loss.py) calls.
  *
  * Math (natural log, z = h W^T / T, W = lm_head weight [V, H]):
  *   KL_i  = sum_v p_v (z_t - z_s) - lse(z_t) + lse(z_s),  p = softmax(z_t)
@@ -168,6 +168,31 @@ int klg_fwd_bwd(const void* h_s, const void* h_t, const void* w, const uint8_t* 
                 float* lse, float* row_kl, float* d_h_s, float* d_w, void* workspace, int64_t workspace_bytes,
                 void* stream);
 
+/* ---------------------------------------------------------------- training step in pieces
+ * klg_fwd_bwd split at the points where a vocab-sharded step exchanges data (each rank holds
+ * all rows and a slice of W's rows; the reference's loss is train.py:142-210 on one device):
+ *   klg_lse_record   pass 1 over this W: one merged (m, S) record per row and view,
+ *                    rec [2][2 * n_rows] = (m, S) in log2 units, rows 0..N-1 the student
+ *                    view and N..2N-1 the teacher view            -> all-gather the records
+ *   klg_lse_merge    n_rec such records (e.g. one per vocab shard) -> lse [2][n_rows]
+ *   klg_pass2        with the global lse: dZ over this W, d_h_s (partial over the vocabulary:
+ *                    all-reduce) and d_w (this W's rows, complete), and cross [n_rows], this
+ *                    W's part of the KL cross term sum_v p_v (u_t - u_s) (log2 units) -> all-reduce
+ *   klg_kl_loss      KL_i = ln2 (cross_i + lse_s,i - lse_t,i) for rows with mask set, and
+ *                    loss = sum KL / count (0 when count == 0); row_kl may be NULL.
+ * On one device with the whole W, klg_lse_record + klg_lse_merge (n_rec = 1) + klg_pass2 +
+ * klg_kl_loss compute what klg_fwd_bwd computes. */
+int64_t klg_lse_workspace_bytes(int64_t n_rows, int64_t vocab);
+int klg_lse_record(const void* h_s, const void* h_t, const void* w, int64_t n_rows, int64_t hidden, int64_t vocab,
+                   float inv_temp, float* rec, void* workspace, int64_t workspace_bytes, void* stream);
+int klg_lse_merge(const float* recs, int n_rec, int64_t n_rows, float* lse, void* stream);
+int64_t klg_pass2_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t vocab);
+int klg_pass2(const void* h_s, const void* h_t, const void* w, const uint8_t* mask, const float* lse, const float* count,
+              const float* grad, int64_t n_rows, int64_t hidden, int64_t vocab, float inv_temp, float* d_h_s,
+              float* d_w, float* cross, void* workspace, int64_t workspace_bytes, void* stream);
+int klg_kl_loss(const float* lse, const float* cross, const uint8_t* mask, int64_t n_rows, const float* count,
+                float* loss, float* row_kl, void* stream);
+
 /* ---------------------------------------------------------------- inference lm_head
  * The reference's sample_token (generate.py:40-78) on the lm_head output, without the
  * [N, V] logits (generate.py:161-188 computes the full logits first).  For each row of
@@ -229,6 +254,22 @@ int klg_block_attn_fwd(const void* q, const void* k_self, const void* v_self, co
                        int64_t ar_stride, const int32_t* limits, int64_t batch, int64_t heads, int64_t kv_heads,
                        int64_t diff_len, int64_t block, int64_t ar_len, int64_t head_dim, float scale, void* out,
                        float* lse, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Number of AR key-range splits (the thread-block cluster size) klg_block_attn_fwd uses
+ * for this shape on the current device; -1 for an unsupported shape. */
+int klg_block_attn_splits(int64_t batch, int64_t heads, int64_t kv_heads, int64_t diff_len, int64_t block,
+                          int64_t ar_len, int64_t head_dim);
+
+/* Test hook (no counterpart in the reference): klg_block_attn_fwd with split `stall_split`
+ * of every unit issuing no key/value loads, on a decode shape (splits >= 2).  That split's
+ * operand wait runs out its bound (~1 s), sets a KLG_STATUS_TIMEOUT_* bit, and every CTA of
+ * the cluster still meets at the cluster barriers and exits: the timeout path of a split
+ * kernel ends with a status, not a hang.  The output is not meaningful. */
+int klg_selftest_attn_split_stall(const void* q, const void* k_self, const void* v_self, const void* k_ar,
+                                  const void* v_ar, int64_t ar_stride, const int32_t* limits, int64_t batch,
+                                  int64_t heads, int64_t kv_heads, int64_t diff_len, int64_t block, int64_t ar_len,
+                                  int64_t head_dim, float scale, void* out, float* lse, void* workspace,
+                                  int64_t workspace_bytes, int stall_split, void* stream);
 
 /* The logit z[i] = h[i] . W[tokens[i]] (fp32 accumulate of bf16 rows) of a token chosen
  * elsewhere -- with the lse of klg_lm_head_sample, exp(z * inv_temp - lse) is that token's

@@ -32,6 +32,9 @@ SIGNATURES = {
     "klg_block_attn_workspace_bytes": (c_longlong, [c_longlong] * 7),
     "klg_block_attn_fwd": (c_int, [c_void_p] * 5 + [c_longlong, c_void_p] + [c_longlong] * 7 +
                            [c_float, c_void_p, c_void_p, c_void_p, c_longlong, c_void_p]),
+    "klg_block_attn_splits": (c_int, [c_longlong] * 7),
+    "klg_selftest_attn_split_stall": (c_int, [c_void_p] * 5 + [c_longlong, c_void_p] + [c_longlong] * 7 +
+                                      [c_float, c_void_p, c_void_p, c_void_p, c_longlong, c_int, c_void_p]),
     "klg_token_logit": (c_int, [c_void_p, c_void_p, c_void_p] + [c_longlong] * 3 + [c_void_p, c_void_p]),
     "klg_gather_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p] + [c_longlong] * 6 +
                         [c_void_p, c_void_p, c_void_p, c_void_p]),
@@ -60,6 +63,14 @@ SIGNATURES = {
     "klg_fwd_bwd_chunk_cols": (c_int64, [c_int64, c_int64, c_int64]),
     "klg_fwd_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_float, c_int, c_void_p,
                             c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+    "klg_lse_workspace_bytes": (c_int64, [c_int64, c_int64]),
+    "klg_lse_record": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_float, c_void_p, c_void_p,
+                               c_int64, c_void_p]),
+    "klg_lse_merge": (c_int, [c_void_p, c_int, c_int64, c_void_p, c_void_p]),
+    "klg_pass2_workspace_bytes": (c_int64, [c_int64, c_int64, c_int64]),
+    "klg_pass2": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64,
+                          c_int64, c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+    "klg_kl_loss": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p]),
     "klg_fwd_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_float, c_int,
                                 c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "klg_fwd_noalloc_max_floats": (c_longlong, []),

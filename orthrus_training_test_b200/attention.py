@@ -6,7 +6,8 @@ K diffusion keys, bidirectionally (model.py:64-96) -- and a score_mod that hides
 keys past each query's causal limit (model.py:435-446); GQA maps query head h to KV head
 h / (H / Hkv).  The Triton replacement (triton_kernels.py:18-83, 281-290) is marked broken
 in the reference.  ``block_attention`` computes the same attention in one CUDA kernel per
-(batch, KV head, head group, block, key split) plus a split-merge kernel.
+(batch, KV head, head group, block, key split); the key splits of a decode call form a
+thread-block cluster and combine through distributed shared memory.
 
 Forward only (inference).  Every function here calls the CUDA library; there is no CPU
 fallback.

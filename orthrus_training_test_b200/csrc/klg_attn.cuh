@@ -48,6 +48,7 @@ struct AttnArgs {
   int ng, hg, n_hg, nb;   // query heads per KV head, per unit; head groups; blocks
   int n_units, splits, tps;   // splits = cluster size (<= 8); tps: AR tiles per split
   float sl2;                  // scale * log2(e)
+  int stall_split;            // test hook: the CTA of this split issues no key/value loads (-1: none)
 };
 
 // Units are numbered with the blocks of a sequence in reverse: later blocks see longer AR
@@ -127,6 +128,7 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
   const uint32_t sempty0 = sfull0 + 16u;              // [2] the parity's softmax warps read it
   const uint32_t pfull0 = sempty0 + 16u;              // [2] P written to shared memory
   const uint32_t ofull0 = pfull0 + 16u;               // [2] the parity's latest P V retired
+  const uint32_t done_bar = ofull0 + 16u;             // every MMA this CTA issued retired
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int u = blockIdx.x / a.splits;
@@ -149,6 +151,7 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
       mbar_init(pfull0 + 8u * s, 4);
       mbar_init(ofull0 + 8u * s, 1);
     }
+    mbar_init(done_bar, 1);
     fence_mbar_init();
     tma_prefetch(&map_q);
     tma_prefetch(&map_ks);
@@ -187,7 +190,10 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
       }
     }
     __syncwarp();
-    for (int i = 0; i < ntiles; ++i) {
+    // (test hook) a stalled split loads no tiles: its MMA warp's first operand wait runs out its
+    // bound, and the CTA still reaches both cluster barriers below
+    const int n_load = sp == a.stall_split ? 0 : ntiles;
+    for (int i = 0; i < n_load; ++i) {
       if (!warp_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) break;
       if (elect_one()) {
         const uint32_t ks = st_s + stage * 2 * ATT_TILE_BYTES;
@@ -257,6 +263,11 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
       }
       __syncwarp();
     }
+    // every MMA issued above has retired before TMEM is freed, also when a wait gave up
+    // with an S tile still in flight that no softmax warp will read
+    if (elect_one()) mma_commit(done_bar);
+    __syncwarp();
+    mbar_wait_drain(done_bar, 0);
   } else {
     // ------------------------------------------------------------ softmax warps (one row per thread)
     const int q4 = warp & 3;   // TMEM lane quarter of this warp
@@ -404,6 +415,10 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
       }
     }
   }
+  // Every thread of every CTA of the cluster must reach both cluster barriers: they have no
+  // time bound.  Nothing above returns early -- each role leaves its loop on a bounded wait
+  // that gave up (or on the CTA's abort flag) and falls through to here -- and any early exit
+  // added above would leave the other splits of the unit waiting here for good.
   if (a.splits > 1) {
     cluster_sync();   // every split's records of the unit are in its CTA's shared memory
     const uint32_t rank = cluster_rank();

@@ -518,6 +518,9 @@ int klg_fwd_stats(const void* hs, const void* ht, const void* w, int64_t n_rows,
   int rc = check_problem(hs, ht, w, n_rows, hidden, vocab, inv_temp);
   if (rc) return rc;
   if (!partials || !aligned16(partials)) return fail(KLG_ERR_ARG, "partials must be non-null and 16-byte aligned");
+  if (n_part < klg::DZP_CSPLIT || n_part % klg::DZP_CSPLIT != 0 || n_part > kStatsMaxRanges * klg::DZP_CSPLIT)
+    return fail(KLG_ERR_ARG, "n_part=%d is not a record count this kernel writes (use klg_num_partials)", n_part);
+  if ((rc = bind_device(hs))) return rc;   // the exact plan below depends on the SM count of hs's device
   klg::DualArgs a{};
   a.n_rows = (int)n_rows;
   a.v_begin = 0;
@@ -528,7 +531,6 @@ int klg_fwd_stats(const void* hs, const void* ht, const void* w, int64_t n_rows,
   plan_dual(a.n_rt, a.n_vt, num_sms() / 2, a.vt_per_unit, n_uv, kStatsMaxRanges);
   if (n_part != n_uv * klg::DZP_CSPLIT)
     return fail(KLG_ERR_ARG, "n_part=%d but this device plans %d (use klg_num_partials)", n_part, n_uv * klg::DZP_CSPLIT);
-  if ((rc = bind_device(hs))) return rc;
   NvtxRange nvtx_range("klg_fwd_stats");
   a.n_units = a.n_rt * n_uv;
   a.n_kb = cdiv(hidden, klg::BK);
@@ -591,6 +593,11 @@ int klg_fwd(const void* hs, const void* ht, const void* w, const uint8_t* mask, 
   int rc = check_problem(hs, ht, w, n_rows, hidden, vocab, inv_temp);
   if (rc) return rc;
   if (!mask || !count || !loss || !lse) return fail(KLG_ERR_ARG, "null output pointer");
+  // at least one vocab range (DZP_CSPLIT records) plus the merged record: checked before any device call
+  if (!workspace || workspace_bytes < (int64_t)(klg::DZP_CSPLIT + 1) * 5 * n_rows * 4 || !aligned16(workspace))
+    return fail(KLG_ERR_WORKSPACE, "forward workspace needs at least %lld bytes (16-byte aligned)",
+                (long long)(klg::DZP_CSPLIT + 1) * 5 * n_rows * 4);
+  if ((rc = bind_device(hs))) return rc;   // the partial-record count depends on hs's device
   int n_part = 0;
   if ((rc = klg_num_partials(n_rows, vocab, &n_part))) return rc;
   const int64_t need = (int64_t)(n_part + 1) * 5 * n_rows * 4;
@@ -790,6 +797,40 @@ FwdBwdLayout fwd_bwd_layout(int64_t n_rows, int64_t vocab, int64_t workspace_byt
   return L;
 }
 
+// Pass 1 of the training path: both views' (m, S) per row over W's rows on CTA pairs
+// (partial records into lse_parts, n_lp of them), merged into the log-sum-exps `lse` [2][N]
+// and/or one merged record `rec` [2][2N].
+int run_pass1(const void* hs, const void* ht, const void* w, int64_t n_rows, int64_t hidden, int64_t vocab,
+              float inv_temp, float* lse_parts, int n_lp, float* lse, float* rec, cudaStream_t s) {
+  alignas(64) CUtensorMap mhs, mht, mw;
+  if (!make_map(&mhs, hs, hidden, n_rows, hidden, klg::BK, klg::BM) ||
+      !make_map(&mht, ht, hidden, n_rows, hidden, klg::BK, klg::BM) ||
+      !make_map(&mw, w, hidden, vocab, hidden, klg::BK, klg::LSE_BN / 2))
+    return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+  klg::LseArgs la{};
+  la.n_rows = (int)n_rows;
+  la.vocab = (int)vocab;
+  la.n_rp = cdiv(n_rows, 256);
+  la.n_vt = cdiv(vocab, klg::LSE_BN);
+  plan_dual(2 * la.n_rp, la.n_vt, num_sms() / 2, la.vt_per_unit, la.n_uv);
+  la.n_units = 2 * la.n_rp * la.n_uv;
+  la.n_kb = cdiv(hidden, klg::BK);
+  la.scale_log2 = inv_temp * 1.4426950408889634f;
+  la.parts = lse_parts;
+  la.n_views = 2;
+  la.rep = 1;
+  if (klg::LSE_CSPLIT * la.n_uv != n_lp) return fail(KLG_ERR_ARG, "internal plan mismatch");
+  int rc = launch_lse_pair<klg::EPI_LSE>(mhs, mht, mw, la, s);
+  if (rc) return rc;
+  const int n2 = (int)(2 * n_rows);
+  const int slot = trace_pre(s);
+  cudaError_t e = launch_k(klg::lse_merge_kernel, dim3(cdiv(n2, 256)), dim3(256), 0, s, 1, lse_parts, n_lp, n2, lse, rec);
+  trace_post(slot, s, KLG_KIND_MERGE);
+  if (e != cudaSuccess) return cuda_fail(e, "launch lse_merge_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -837,11 +878,11 @@ int klg_fwd_bwd(const void* hs, const void* ht, const void* w, const uint8_t* ma
   if (!mask || !count || !loss || !lse) return fail(KLG_ERR_ARG, "null mask/count/loss/lse");
   if ((d_hs && !aligned16(d_hs)) || (d_w && !aligned16(d_w))) return fail(KLG_ERR_ALIGN, "outputs must be 16-byte aligned");
   if (!workspace || !aligned16(workspace)) return fail(KLG_ERR_WORKSPACE, "null or misaligned workspace");
+  if ((rc = bind_device(hs))) return rc;   // the layout depends on the SM count of hs's device
   const FwdBwdLayout L = fwd_bwd_layout(n_rows, vocab, workspace_bytes);
   if (L.cols < 0)
     return fail(KLG_ERR_WORKSPACE, "workspace of %lld bytes too small (see klg_fwd_bwd_workspace_bytes)",
                 (long long)workspace_bytes);
-  if ((rc = bind_device(hs))) return rc;
   NvtxRange nvtx_range("klg_fwd_bwd");
   cudaStream_t s = (cudaStream_t)stream;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -850,33 +891,7 @@ int klg_fwd_bwd(const void* hs, const void* ht, const void* w, const uint8_t* ma
   if (!count_given && (rc = klg_count_valid(mask, n_rows, count, stream))) return rc;
 
   // pass 1: log-sum-exp of both views on CTA pairs
-  alignas(64) CUtensorMap mhs, mht, mw;
-  if (!make_map(&mhs, hs, hidden, n_rows, hidden, klg::BK, klg::BM) ||
-      !make_map(&mht, ht, hidden, n_rows, hidden, klg::BK, klg::BM) ||
-      !make_map(&mw, w, hidden, vocab, hidden, klg::BK, klg::LSE_BN / 2))
-    return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
-  klg::LseArgs la{};
-  la.n_rows = (int)n_rows;
-  la.vocab = (int)vocab;
-  la.n_rp = cdiv(n_rows, 256);
-  la.n_vt = cdiv(vocab, klg::LSE_BN);
-  plan_dual(2 * la.n_rp, la.n_vt, num_sms() / 2, la.vt_per_unit, la.n_uv);
-  la.n_units = 2 * la.n_rp * la.n_uv;
-  la.n_kb = cdiv(hidden, klg::BK);
-  la.scale_log2 = inv_temp * 1.4426950408889634f;
-  la.parts = lse_parts;
-  la.n_views = 2;
-  la.rep = 1;
-  if (klg::LSE_CSPLIT * la.n_uv != L.n_lp) return fail(KLG_ERR_ARG, "internal plan mismatch");
-  if ((rc = launch_lse_pair<klg::EPI_LSE>(mhs, mht, mw, la, s))) return rc;
-  {
-    const int n2 = (int)(2 * n_rows);
-    const int slot = trace_pre(s);
-    cudaError_t e = launch_k(klg::lse_merge_kernel, dim3(cdiv(n2, 256)), dim3(256), 0, s, 1, lse_parts, L.n_lp, n2, lse);
-    trace_post(slot, s, KLG_KIND_MERGE);
-    if (e != cudaSuccess) return cuda_fail(e, "launch lse_merge_kernel");
-    ++g_launches;
-  }
+  if ((rc = run_pass1(hs, ht, w, n_rows, hidden, vocab, inv_temp, lse_parts, L.n_lp, lse, nullptr, s))) return rc;
   // pass 2: dZ chunks (+ KL cross-term partials) and the dW / dH GEMMs
   int n_ap = 0;
 
@@ -901,6 +916,94 @@ int klg_fwd_bwd(const void* hs, const void* ht, const void* w, const uint8_t* ma
     if (e != cudaSuccess) return cuda_fail(e, "launch loss_from_sums_kernel");
     ++g_launches;
   }
+  return KLG_OK;
+}
+
+// ---------------------------------------------------------------- training step in pieces (vocab sharding)
+int64_t klg_lse_workspace_bytes(int64_t n_rows, int64_t vocab) {
+  if (n_rows < 1 || vocab < 1 || n_rows > (1ll << 30) || vocab > (1ll << 30)) return -1;
+  const FwdBwdLayout L = fwd_bwd_layout(n_rows, vocab, INT64_MAX / 4);
+  return (int64_t)L.n_lp * 2 * 2 * n_rows * 4;
+}
+
+int klg_lse_record(const void* hs, const void* ht, const void* w, int64_t n_rows, int64_t hidden, int64_t vocab,
+                   float inv_temp, float* rec, void* workspace, int64_t workspace_bytes, void* stream) {
+  int rc = check_problem(hs, ht, w, n_rows, hidden, vocab, inv_temp);
+  if (rc) return rc;
+  if (!rec || !aligned16(rec)) return fail(KLG_ERR_ARG, "rec must be non-null and 16-byte aligned");
+  if (!workspace || !aligned16(workspace)) return fail(KLG_ERR_WORKSPACE, "null or misaligned workspace");
+  if ((rc = bind_device(hs))) return rc;   // the plan depends on the SM count of hs's device
+  const FwdBwdLayout L = fwd_bwd_layout(n_rows, vocab, INT64_MAX / 4);
+  const int64_t need = (int64_t)L.n_lp * 2 * 2 * n_rows * 4;
+  if (workspace_bytes < need)
+    return fail(KLG_ERR_WORKSPACE, "pass-1 workspace needs %lld bytes (see klg_lse_workspace_bytes)", (long long)need);
+  NvtxRange nvtx_range("klg_lse_record");
+  return run_pass1(hs, ht, w, n_rows, hidden, vocab, inv_temp, static_cast<float*>(workspace), L.n_lp, nullptr, rec,
+                   (cudaStream_t)stream);
+}
+
+int klg_lse_merge(const float* recs, int n_rec, int64_t n_rows, float* lse, void* stream) {
+  if (!recs || !lse || n_rec < 1 || n_rows < 1 || n_rows > (1ll << 29)) return fail(KLG_ERR_ARG, "bad arguments to klg_lse_merge");
+  if (int rc = bind_device(recs)) return rc;
+  const int n2 = (int)(2 * n_rows);
+  cudaStream_t s = (cudaStream_t)stream;
+  const int slot = trace_pre(s);
+  cudaError_t e = launch_k(klg::lse_merge_kernel, dim3(cdiv(n2, 256)), dim3(256), 0, s, 1, recs, n_rec, n2, lse,
+                           static_cast<float*>(nullptr));
+  trace_post(slot, s, KLG_KIND_MERGE);
+  if (e != cudaSuccess) return cuda_fail(e, "launch lse_merge_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
+int64_t klg_pass2_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t vocab) {
+  return klg_fwd_bwd_workspace_bytes(n_rows, hidden, vocab);
+}
+
+int klg_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask, const float* lse, const float* count,
+              const float* grad, int64_t n_rows, int64_t hidden, int64_t vocab, float inv_temp, float* d_hs, float* d_w,
+              float* cross, void* workspace, int64_t workspace_bytes, void* stream) {
+  int rc = check_problem(hs, ht, w, n_rows, hidden, vocab, inv_temp);
+  if (rc) return rc;
+  if (!mask || !lse || !count || !cross) return fail(KLG_ERR_ARG, "null mask/lse/count/cross");
+  if ((d_hs && !aligned16(d_hs)) || (d_w && !aligned16(d_w))) return fail(KLG_ERR_ALIGN, "outputs must be 16-byte aligned");
+  if (!workspace || !aligned16(workspace)) return fail(KLG_ERR_WORKSPACE, "null or misaligned workspace");
+  if ((rc = bind_device(hs))) return rc;   // the layout depends on the SM count of hs's device
+  const FwdBwdLayout L = fwd_bwd_layout(n_rows, vocab, workspace_bytes);
+  if (L.cols < 0)
+    return fail(KLG_ERR_WORKSPACE, "workspace of %lld bytes too small (see klg_pass2_workspace_bytes)",
+                (long long)workspace_bytes);
+  NvtxRange nvtx_range("klg_pass2");
+  cudaStream_t s = (cudaStream_t)stream;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* a_parts = reinterpret_cast<float*>(ws + L.a_parts_off);
+  __nv_bfloat16* dz = reinterpret_cast<__nv_bfloat16*>(ws + L.dz_off);
+  int n_ap = 0;
+  if ((rc = run_pass2(hs, ht, w, mask, lse, count, grad, n_rows, hidden, vocab, inv_temp, d_hs, d_w, dz, L.cols,
+                      a_parts, &n_ap, s)))
+    return rc;
+  if (n_ap != L.n_ap) return fail(KLG_ERR_ARG, "internal plan mismatch (cross-term partials)");
+  const int slot = trace_pre(s);
+  cudaError_t e = launch_k(klg::cross_sum_kernel, dim3(cdiv(n_rows, 256)), dim3(256), 0, s, 1, a_parts, n_ap,
+                           (int)n_rows, cross);
+  trace_post(slot, s, KLG_KIND_FINALIZE);
+  if (e != cudaSuccess) return cuda_fail(e, "launch cross_sum_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
+int klg_kl_loss(const float* lse, const float* cross, const uint8_t* mask, int64_t n_rows, const float* count,
+                float* loss, float* row_kl, void* stream) {
+  if (!lse || !cross || !mask || !count || !loss || n_rows < 1 || n_rows > (1ll << 30))
+    return fail(KLG_ERR_ARG, "bad arguments to klg_kl_loss");
+  if (int rc = bind_device(lse)) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int slot = trace_pre(s);
+  cudaError_t e = launch_k(klg::kl_loss_kernel, dim3(1), dim3(1024), 0, s, 1, lse, cross, mask, (int)n_rows, count,
+                           loss, row_kl);
+  trace_post(slot, s, KLG_KIND_FINALIZE);
+  if (e != cudaSuccess) return cuda_fail(e, "launch kl_loss_kernel");
+  ++g_launches;
   return KLG_OK;
 }
 
@@ -948,12 +1051,16 @@ int klg_lm_head_sample(const void* h, const void* w, int64_t n_rows, int64_t hid
   int rc = check_problem(h, h, w, n_rows, hidden, vocab, inv_temp);
   if (rc) return rc;
   if (!tokens || !logit || !lse) return fail(KLG_ERR_ARG, "null output pointer");
+  // at least one record per row and epilogue column slice: checked before any device call
+  if (!workspace || workspace_bytes < (int64_t)klg::LSE_CSPLIT * 5 * n_rows * 4 || !aligned16(workspace))
+    return fail(KLG_ERR_WORKSPACE, "sampling workspace needs at least %lld bytes (16-byte aligned)",
+                (long long)klg::LSE_CSPLIT * 5 * n_rows * 4);
+  if ((rc = bind_device(h))) return rc;   // the plan depends on the SM count of h's device
   klg::LseArgs la{};
   const int n_part = sample_plan(n_rows, vocab, la);
   const int64_t need = sample_workspace(n_rows, n_part);
   if (!workspace || workspace_bytes < need || !aligned16(workspace))
     return fail(KLG_ERR_WORKSPACE, "sampling workspace needs %lld bytes (16-byte aligned)", (long long)need);
-  if ((rc = bind_device(h))) return rc;
   NvtxRange nvtx_range("klg_lm_head_sample");
   cudaStream_t s = (cudaStream_t)stream;
   la.n_kb = cdiv(hidden, klg::BK);
@@ -1116,6 +1223,7 @@ int attn_plan(int64_t B, int64_t H, int64_t Hkv, int64_t Ld, int64_t K, int64_t 
   splits = std::max(1, std::min(std::min(splits, n_ar), 8));
   a.tps = cdiv(n_ar, splits);
   a.splits = cdiv(n_ar, a.tps);
+  a.stall_split = -1;
   P.ws_bytes = 16;   // the splits combine through distributed shared memory: no global scratch
   return KLG_OK;
 }
@@ -1128,10 +1236,11 @@ int64_t klg_block_attn_workspace_bytes(int64_t batch, int64_t heads, int64_t kv_
   return P.ws_bytes;
 }
 
-int klg_block_attn_fwd(const void* q, const void* k_self, const void* v_self, const void* k_ar, const void* v_ar,
-                       int64_t ar_stride, const int32_t* limits, int64_t batch, int64_t heads, int64_t kv_heads,
-                       int64_t diff_len, int64_t block, int64_t ar_len, int64_t head_dim, float scale, void* out,
-                       float* lse, void* workspace, int64_t workspace_bytes, void* stream) {
+namespace {
+int block_attn_fwd(const void* q, const void* k_self, const void* v_self, const void* k_ar, const void* v_ar,
+                   int64_t ar_stride, const int32_t* limits, int64_t batch, int64_t heads, int64_t kv_heads,
+                   int64_t diff_len, int64_t block, int64_t ar_len, int64_t head_dim, float scale, void* out,
+                   float* lse, void* workspace, int64_t workspace_bytes, void* stream, int stall_split) {
   if (!q || !k_self || !v_self || !k_ar || !v_ar || !limits || !out) return fail(KLG_ERR_ARG, "null pointer");
   AttnPlan P;
   int rc = attn_plan(batch, heads, kv_heads, diff_len, block, ar_len, head_dim, P);
@@ -1146,6 +1255,12 @@ int klg_block_attn_fwd(const void* q, const void* k_self, const void* v_self, co
   NvtxRange nvtx_range("klg_block_attn_fwd");
   cudaStream_t s = (cudaStream_t)stream;
   klg::AttnArgs a = P.a;
+  if (stall_split >= 0) {
+    if (a.splits < 2 || stall_split >= a.splits)
+      return fail(KLG_ERR_ARG, "stall_split %d needs a decode shape with more splits (this one has %d)", stall_split,
+                  a.splits);
+    a.stall_split = stall_split;
+  }
   a.limits = limits;
   a.sl2 = scale * 1.4426950408889634f;
   a.out = static_cast<__nv_bfloat16*>(out);
@@ -1167,6 +1282,32 @@ int klg_block_attn_fwd(const void* q, const void* k_self, const void* v_self, co
   if (e != cudaSuccess) return cuda_fail(e, "launch block_attn_kernel");
   ++g_launches;
   return KLG_OK;
+}
+}  // namespace
+
+int klg_block_attn_fwd(const void* q, const void* k_self, const void* v_self, const void* k_ar, const void* v_ar,
+                       int64_t ar_stride, const int32_t* limits, int64_t batch, int64_t heads, int64_t kv_heads,
+                       int64_t diff_len, int64_t block, int64_t ar_len, int64_t head_dim, float scale, void* out,
+                       float* lse, void* workspace, int64_t workspace_bytes, void* stream) {
+  return block_attn_fwd(q, k_self, v_self, k_ar, v_ar, ar_stride, limits, batch, heads, kv_heads, diff_len, block,
+                        ar_len, head_dim, scale, out, lse, workspace, workspace_bytes, stream, -1);
+}
+
+int klg_selftest_attn_split_stall(const void* q, const void* k_self, const void* v_self, const void* k_ar,
+                                  const void* v_ar, int64_t ar_stride, const int32_t* limits, int64_t batch,
+                                  int64_t heads, int64_t kv_heads, int64_t diff_len, int64_t block, int64_t ar_len,
+                                  int64_t head_dim, float scale, void* out, float* lse, void* workspace,
+                                  int64_t workspace_bytes, int stall_split, void* stream) {
+  if (stall_split < 0) return fail(KLG_ERR_ARG, "stall_split must be >= 0");
+  return block_attn_fwd(q, k_self, v_self, k_ar, v_ar, ar_stride, limits, batch, heads, kv_heads, diff_len, block,
+                        ar_len, head_dim, scale, out, lse, workspace, workspace_bytes, stream, stall_split);
+}
+
+int klg_block_attn_splits(int64_t batch, int64_t heads, int64_t kv_heads, int64_t diff_len, int64_t block,
+                          int64_t ar_len, int64_t head_dim) {
+  AttnPlan P;
+  if (attn_plan(batch, heads, kv_heads, diff_len, block, ar_len, head_dim, P)) return -1;
+  return P.a.splits;
 }
 
 int klg_token_logit(const void* h, const void* w, const int32_t* tokens, int64_t n_rows, int64_t hidden, int64_t vocab,
@@ -1298,6 +1439,7 @@ int klg_fwd_noalloc(const void* hs, const void* ht, const void* w, const uint8_t
   int rc = check_problem(hs, ht, w, n_rows, hidden, vocab, inv_temp);
   if (rc) return rc;
   if (!mask || !count || !loss || !lse) return fail(KLG_ERR_ARG, "null output pointer");
+  if ((rc = bind_device(hs))) return rc;   // the partial-record count depends on hs's device
   int n_part = 0;
   if ((rc = klg_num_partials(n_rows, vocab, &n_part))) return rc;
   const long long need = (long long)(n_part + 1) * 5 * n_rows;
@@ -1306,7 +1448,6 @@ int klg_fwd_noalloc(const void* hs, const void* ht, const void* w, const uint8_t
                 "klg_fwd_noalloc: %lld rows x %lld vocab needs %lld scratch floats, above its fixed %lld "
                 "(use klg_fwd with a workspace)",
                 (long long)n_rows, (long long)vocab, need, (long long)KLG_NOALLOC_SCRATCH_FLOATS);
-  if ((rc = bind_device(hs))) return rc;
   float* parts = nullptr;
   if ((rc = noalloc_scratch(&parts))) return rc;
   float* stats = parts + (size_t)n_part * 5 * n_rows;

@@ -1264,8 +1264,11 @@ __global__ void finalize_kernel(const float* __restrict__ stats, const uint8_t* 
   }
 }
 
-// lse[i] = log2-domain log-sum-exp of row i from n_part (m, S) records parts[n_part][2][n2].
-__global__ void lse_merge_kernel(const float* __restrict__ parts, int n_part, int n2, float* __restrict__ lse) {
+// Merge of n_part (m, S) records parts[n_part][2][n2] (log2 units) per row i: lse[i] = the
+// log-sum-exp (when lse is set) and/or rec = the merged record [2][n2] (when rec is set; a
+// vocab shard's record, to be gathered with the other shards' and merged again).
+__global__ void lse_merge_kernel(const float* __restrict__ parts, int n_part, int n2, float* __restrict__ lse,
+                                 float* __restrict__ rec) {
   pdl_enter();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n2) return;
@@ -1274,7 +1277,52 @@ __global__ void lse_merge_kernel(const float* __restrict__ parts, int n_part, in
   for (int p = 0; p < n_part; ++p) M = fmaxf(M, parts[(size_t)p * 2 * st + i]);
   float S = 0.f;
   for (int p = 0; p < n_part; ++p) S = fmaf(parts[(size_t)p * 2 * st + st + i], ex2(parts[(size_t)p * 2 * st + i] - M), S);
-  lse[i] = M + __log2f(S);
+  if (lse) lse[i] = M + __log2f(S);
+  if (rec) {
+    rec[i] = M;
+    rec[st + i] = S;
+  }
+}
+
+// cross[i] = sum over the pass-2 partial rows a_parts[p][i] in a fixed order: the KL cross
+// term sum_v p_v (u_t - u_s) (log2 units) of row i over the vocabulary the pass covered.
+__global__ void cross_sum_kernel(const float* __restrict__ a_parts, int n_ap, int n, float* __restrict__ cross) {
+  pdl_enter();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float A = 0.f;
+  for (int p = 0; p < n_ap; ++p) A += a_parts[(size_t)p * n + i];
+  cross[i] = A;
+}
+
+// Loss from complete cross terms (e.g. summed over vocab shards): KL_i = ln2 (cross_i + L_s,i -
+// L_t,i) for rows with mask set (0 elsewhere), loss = sum KL / count (0 when count == 0).  One
+// block; fixed reduction order.
+__global__ void kl_loss_kernel(const float* __restrict__ lse, const float* __restrict__ cross,
+                               const uint8_t* __restrict__ mask, int n, const float* __restrict__ count,
+                               float* __restrict__ loss, float* __restrict__ row_kl) {
+  pdl_enter();
+  __shared__ float part[32];
+  const float ln2 = 0.69314718055994530942f;
+  float acc = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float kl = mask[i] ? ln2 * (cross[i] + lse[i] - lse[(size_t)n + i]) : 0.f;
+    if (row_kl) row_kl[i] = kl;
+    acc += kl;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    acc = (threadIdx.x < (blockDim.x >> 5)) ? part[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (threadIdx.x == 0) {
+      const float c = *count;
+      *loss = c > 0.f ? acc / c : 0.f;
+    }
+  }
 }
 
 // lm_head selection: merge the per-unit records (m, S, key, index, z) of each row into the

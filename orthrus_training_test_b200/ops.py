@@ -195,6 +195,68 @@ def kl_fwd_bwd(h_s, h_t, weight, mask, temperature: float = 1.0, count: Optional
     return loss, lse, cnt, row_kl, dh, dw
 
 
+# ----------------------------------------------------------------- the training step in pieces
+
+def lse_record(h_s, h_t, weight, temperature: float = 1.0) -> torch.Tensor:
+    """Pass 1 over ``weight``'s rows: the merged ``(m, S)`` record ``[2, 2N]`` (log2 units;
+    rows ``0..N-1`` student, ``N..2N-1`` teacher) -- one vocab shard's contribution."""
+    dev = _require_cuda(h_s, h_t, weight)
+    N, H = h_s.shape
+    V = weight.shape[0]
+    ws_bytes = int(_lib.lib().klg_lse_workspace_bytes(N, V))
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+    rec = torch.empty(2, 2 * N, dtype=torch.float32, device=dev)
+    call("klg_lse_record", _ptr(h_s), _ptr(h_t), _ptr(weight), N, H, V, 1.0 / float(temperature), _ptr(rec), _ptr(ws),
+         ws_bytes, _stream(dev))
+    return rec
+
+
+def lse_merge(recs: torch.Tensor) -> torch.Tensor:
+    """``[R, 2, 2N]`` records (e.g. gathered from R vocab shards) -> ``lse [2, N]`` (log2 units)."""
+    recs = recs.contiguous()
+    dev = _require_cuda(recs)
+    R, _, N2 = recs.shape
+    lse = torch.empty(2, N2 // 2, dtype=torch.float32, device=dev)
+    call("klg_lse_merge", _ptr(recs), R, N2 // 2, _ptr(lse), _stream(dev))
+    return lse
+
+
+def pass2(h_s, h_t, weight, mask, lse, count, grad: Optional[torch.Tensor] = None, temperature: float = 1.0,
+          need_dh: bool = True, need_dw: bool = True, workspace_bytes: Optional[int] = None, dh_out=None):
+    """Pass 2 over ``weight``'s rows with the global ``lse``: ``(dH [N, H] fp32 or None,
+    dW [V, H] fp32 or None, cross [N] fp32)``; ``cross`` is this weight's part of the KL
+    cross term (log2 units).  ``dh_out`` may supply the dH buffer (e.g. a view into a larger
+    buffer that one all-reduce carries)."""
+    m = mask_u8(mask)
+    dev = _require_cuda(h_s, h_t, weight, m, lse, count)
+    N, H = h_s.shape
+    V = weight.shape[0]
+    if workspace_bytes is None:
+        workspace_bytes = int(_lib.lib().klg_pass2_workspace_bytes(N, H, V))
+    ws = torch.empty(int(workspace_bytes), dtype=torch.uint8, device=dev)
+    dh = (dh_out if dh_out is not None else torch.empty(N, H, dtype=torch.float32, device=dev)) if need_dh else None
+    dw = torch.empty(V, H, dtype=torch.float32, device=dev) if need_dw else None
+    cross = torch.empty(N, dtype=torch.float32, device=dev)
+    g = None
+    if grad is not None:
+        g = grad.detach().to(device=dev, dtype=torch.float32).reshape(1).contiguous()
+    call("klg_pass2", _ptr(h_s), _ptr(h_t), _ptr(weight), _ptr(m), _ptr(lse), _ptr(count), _ptr(g), N, H, V,
+         1.0 / float(temperature), _ptr(dh), _ptr(dw), _ptr(cross), _ptr(ws), int(workspace_bytes), _stream(dev))
+    return dh, dw, cross
+
+
+def kl_loss(lse, cross, mask, count, want_row_kl: bool = False):
+    """``(loss [] fp32, row_kl [N] or None)`` from complete cross terms."""
+    m = mask_u8(mask)
+    dev = _require_cuda(lse, cross, m, count)
+    N = m.numel()
+    loss = torch.empty((), dtype=torch.float32, device=dev)
+    row_kl = torch.empty(N, dtype=torch.float32, device=dev) if want_row_kl else None
+    call("klg_kl_loss", _ptr(lse), _ptr(cross.contiguous()), _ptr(m), N, _ptr(count), _ptr(loss), _ptr(row_kl),
+         _stream(dev))
+    return loss, row_kl
+
+
 # ----------------------------------------------------------------- autograd op
 
 class KLGemmFn(torch.autograd.Function):

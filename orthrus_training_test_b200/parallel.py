@@ -10,11 +10,15 @@ exchanges are the global valid-row count (normaliser, one float), the loss
 data-parallel gradient exchange).  dH stays local.
 
 Vocab sharding (``vocab_sharded_kl_loss``): each rank owns all rows and one
-contiguous slice of the lm_head's rows (vocab entries).  Pass 1 yields per-row
-partial records ``(m_s, S_s, m_t, S_t, A)`` over the local slice; one
-all-gather plus the online-softmax merge gives every rank the global loss and
-log-sum-exps.  Pass 2 yields the local dW slice (complete, no exchange) and a
-partial dH that is all-reduced.
+contiguous slice of the lm_head's rows (vocab entries).  When gradients are
+needed the step follows the single-device training route split at its exchange
+points: pass 1 gives one ``(m, S)`` record per row and view over the local
+slice; one all-gather and a merge give every rank the global log-sum-exps;
+pass 2 over the local slice gives the complete local dW slice, a partial dH and
+the slice's part of the KL cross term ``sum_v p_v (u_t - u_s)``; one
+all-reduce of ``[dH | cross]`` completes both, and the loss follows on every
+rank.  Without gradients (evaluation) one all-gather of the single-pass
+records ``(m_s, S_s, m_t, S_t, A)`` gives the loss.
 
 The per-device arithmetic comes from an *engine*.  The product engine is
 :class:`CudaEngine` (the sm_100a library).  Tests substitute a CPU engine
@@ -75,6 +79,29 @@ class CudaEngine:
                                            need_dw=need_dw)
         return loss, dh, dw
 
+    # the training step in pieces (vocab sharding exchanges data between them)
+    acc_dtype = torch.float32
+
+    def lse_record(self, h_s, h_t, w, temperature):
+        """One merged ``(m, S)`` record per row and view over ``w``'s rows: ``[2, 2N]``."""
+        from .ops import lse_record
+        return lse_record(h_s, h_t, w, temperature)
+
+    def lse_merge(self, recs):
+        """``[R, 2, 2N]`` records -> the log-sum-exps ``[2, N]``."""
+        from .ops import lse_merge
+        return lse_merge(recs)
+
+    def pass2(self, h_s, h_t, w, mask, lse, count, temperature, need_dh, need_dw, dh_out=None):
+        """``(dH partial, dW of w's rows, cross-term part [N])`` for upstream gradient 1."""
+        from .ops import pass2
+        return pass2(h_s, h_t, w, mask, lse, count, temperature=temperature, need_dh=need_dh, need_dw=need_dw,
+                     dh_out=dh_out)
+
+    def kl_loss(self, lse, cross, mask, count):
+        from .ops import kl_loss
+        return kl_loss(lse, cross, mask, count)[0]
+
 
 def _engine(engine):
     return engine if engine is not None else CudaEngine()
@@ -128,26 +155,41 @@ class _VocabShardedFn(torch.autograd.Function):
         eng = _engine(engine)
         hs, ht, w, m = eng.prepare(h_s), eng.prepare(h_t), eng.prepare(w_shard), eng.mask(mask)
         count = eng.count(m)                                          # identical rows on every rank
-        local = eng.partial_stats(hs, ht, w, temperature).contiguous()
         world = dist.get_world_size(group)
-        gathered = torch.empty((world * local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype,
-                               device=local.device)
-        dist.all_gather_into_tensor(gathered, local, group=group)     # per-row (m, S, m, S, A) partials
-        stats = eng.merge(gathered.view((world,) + tuple(local.shape)))
-        loss, lse = eng.finalize(stats, m, count)
-        ctx.save_for_backward(hs, ht, w, m, lse, count)
-        ctx.temperature, ctx.group, ctx.eng = float(temperature), group, eng
+        need_dh, need_dw = ctx.needs_input_grad[0], ctx.needs_input_grad[2]
         ctx.dtypes = (h_s.dtype, w_shard.dtype)
+        if not (need_dh or need_dw):
+            # evaluation: the single-pass records (m_s, S_s, m_t, S_t, A) over the local slice
+            local = eng.partial_stats(hs, ht, w, temperature).contiguous()
+            gathered = torch.empty((world * local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype,
+                                   device=local.device)
+            dist.all_gather_into_tensor(gathered, local, group=group)
+            stats = eng.merge(gathered.view((world,) + tuple(local.shape)))
+            loss, _ = eng.finalize(stats, m, count)
+            ctx.save_for_backward(None, None)
+            return loss
+        # pass 1 over the local slice -> all-gather of the (m, S) records -> global log-sum-exps
+        rec = eng.lse_record(hs, ht, w, temperature).contiguous()
+        gathered = torch.empty((world * rec.shape[0],) + tuple(rec.shape[1:]), dtype=rec.dtype, device=rec.device)
+        dist.all_gather_into_tensor(gathered, rec, group=group)
+        lse = eng.lse_merge(gathered.view((world,) + tuple(rec.shape)))
+        # pass 2 over the local slice: this slice's dW (complete), partial dH and cross term,
+        # then one all-reduce of [dH | cross]
+        N, H = hs.shape
+        buf = torch.empty(N * H * (1 if need_dh else 0) + N, dtype=eng.acc_dtype, device=hs.device)
+        dh_view = buf[:N * H].view(N, H) if need_dh else None
+        dh, dw, cross = eng.pass2(hs, ht, w, m, lse, count, temperature, need_dh, need_dw, dh_out=dh_view)
+        buf[buf.numel() - N:].copy_(cross)
+        dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=group)
+        loss = eng.kl_loss(lse, buf[buf.numel() - N:], m, count)
+        ctx.save_for_backward(dh_view, dw)
         return loss
 
     @staticmethod
     def backward(ctx, g):
-        hs, ht, w, m, lse, count = ctx.saved_tensors
-        need_dh, need_dw = ctx.needs_input_grad[0], ctx.needs_input_grad[2]
-        dh, dw = ctx.eng.backward(hs, ht, w, m, lse, count, g, ctx.temperature, True, need_dw)
-        dist.all_reduce(dh, op=dist.ReduceOp.SUM, group=ctx.group)     # partial dH over vocab slices
-        return (dh.to(ctx.dtypes[0]) if need_dh else None, None, dw.to(ctx.dtypes[1]) if need_dw else None,
-                None, None, None, None)
+        dh, dw = ctx.saved_tensors
+        return ((dh * g).to(ctx.dtypes[0]) if dh is not None else None, None,
+                (dw * g).to(ctx.dtypes[1]) if dw is not None else None, None, None, None, None)
 
 
 def vocab_sharded_kl_loss(h_s: torch.Tensor, h_t: torch.Tensor, weight_shard: torch.Tensor, mask: torch.Tensor,

@@ -100,7 +100,16 @@ def token_logprob(h: torch.Tensor, weight: torch.Tensor, tokens: torch.Tensor, l
     what the consensus step reads as ``p_prob = ar_probs[0, i, diff_tokens[0, i]]``
     (generate.py:201-202): the AR distribution's probability of the diffusion head's token,
     here without the ``[N, V]`` probability tensor.  Returns fp32 ``[N]``.
+
+    Shapes are checked before anything reaches the device: ``h [N, H]``, ``weight [V, H]``,
+    ``tokens`` with ``N`` elements and ``lse [N]`` (the kernel reads one token and one
+    weight row per row of ``h``).
     """
+    if h.dim() != 2 or weight.dim() != 2 or weight.shape[1] != h.shape[1]:
+        raise ValueError(f"expected h [N, H] and weight [V, H], got {tuple(h.shape)} and {tuple(weight.shape)}")
+    if tokens.numel() != h.shape[0] or tuple(lse.shape) != (h.shape[0],):
+        raise ValueError(f"tokens must have N={h.shape[0]} elements and lse shape ({h.shape[0]},), got "
+                         f"{tokens.numel()} and {tuple(lse.shape)}")
     dev = _require_cuda(h, weight, tokens, lse)
     h = to_compute_dtype(h)
     weight = to_compute_dtype(weight)

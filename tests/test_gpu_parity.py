@@ -206,41 +206,92 @@ def test_benchmark_configs_full_size(cfg):
     assert_close(ours, ref_loss, ref_dh, ref_dw, cfg)
 
 
-def test_c3_shape_subsample():
-    """H=2048 (1.7B-shaped) on a 4096-row subsample of the 65,536-row configuration."""
-    p = O.make_problem("c3", n_rows=4096)
+def test_c3_full_size():
+    """The 1.7B-shaped configuration at its full 65,536 rows (H=2048, V=49,152: twelve dZ
+    chunks of the training path) against the fp32 torch oracle on the GPU."""
+    p = O.make_problem("c3")
     ours = run_both(p["h_s"], p["h_t"], p["W"], p["mask"], p["T"])
     ref_loss, ref_dh, ref_dw = run_oracle_torch_gpu(p["h_s"], p["h_t"], p["W"], p["mask"], p["T"])
-    assert_close(ours, ref_loss, ref_dh, ref_dw, "c3-sub")
+    assert_close(ours, ref_loss, ref_dh, ref_dw, "c3")
 
 
-@pytest.mark.parametrize("world", [2, 3])
-def test_vocab_sharding_emulated_on_one_gpu(world):
-    """Vocab sharding's per-shard arithmetic on one device: the partial records of every
-    lm_head slice, merged with the online rule, give the full-vocabulary loss; each slice's
-    backward gives its dW rows and a partial dH whose sum is the full dH (what the NCCL
-    all-gather / all-reduce of parallel.vocab_sharded_kl_loss combine across GPUs)."""
+def test_c4_shape_full_vocab_subsample():
+    """The large-vocabulary configuration's shape (H=1024, V=248,320) on 2,048 of its rows
+    with the whole vocabulary on one device, both entry paths."""
+    p = O.make_problem("c4", n_rows=2048)
+    ours = run_both(p["h_s"], p["h_t"], p["W"], p["mask"], p["T"])
+    ref_loss, ref_dh, ref_dw = run_oracle_torch_gpu(p["h_s"], p["h_t"], p["W"], p["mask"], p["T"], chunk=1024)
+    assert_close(ours, ref_loss, ref_dh, ref_dw, "c4-sub")
+
+
+def _vocab_sharded_on_one_gpu(h_s, h_t, W, mask, T, world):
+    """The vocab-sharded training step's per-shard arithmetic on one device, combined the way
+    parallel.vocab_sharded_kl_loss combines it across GPUs: every lm_head slice's pass-1
+    (m, S) record, stacked (the all-gather) and merged into the global log-sum-exps; every
+    slice's pass 2 with them (its dW rows, a partial dH and its part of the KL cross term),
+    summed (the all-reduce of [dH | cross]); the loss from the summed cross terms."""
+    from orthrus_training_test_b200 import ops
     from orthrus_training_test_b200.parallel import CudaEngine, shard_bounds
 
-    h_s, h_t, W, mask, T = rand_problem(900, 576, 7001, seed=21)
     dev = torch.device("cuda:0")
     eng = CudaEngine()
     hs, ht, w, m = eng.prepare(h_s.to(dev)), eng.prepare(h_t.to(dev)), eng.prepare(W.to(dev)), eng.mask(mask.to(dev))
     count = eng.count(m)
-    parts, slices = [], []
-    for r in range(world):
-        lo, hi = shard_bounds(W.shape[0], world, r)
-        slices.append((lo, hi))
-        parts.append(eng.partial_stats(hs, ht, w[lo:hi].contiguous(), T))
-    stats = eng.merge(torch.stack(parts))
-    loss, lse = eng.finalize(stats, m, count)
+    slices = [shard_bounds(W.shape[0], world, r) for r in range(world)]
+    recs = torch.stack([eng.lse_record(hs, ht, w[lo:hi].contiguous(), T) for lo, hi in slices])
+    lse = eng.lse_merge(recs)
     dh = torch.zeros(hs.shape, dtype=torch.float32, device=dev)
+    cross = torch.zeros(hs.shape[0], dtype=torch.float32, device=dev)
     dws = []
     for lo, hi in slices:
-        dh_r, dw_r = eng.backward(hs, ht, w[lo:hi].contiguous(), m, lse, count, None, T, True, True)
+        dh_r, dw_r, c_r = eng.pass2(hs, ht, w[lo:hi].contiguous(), m, lse, count, T, True, True)
         dh += dh_r
+        cross += c_r
         dws.append(dw_r)
+    loss = eng.kl_loss(lse, cross, m, count)
+    # the evaluation route (no gradients): single-pass records all-gathered and merged
+    parts = torch.stack([eng.partial_stats(hs, ht, w[lo:hi].contiguous(), T) for lo, hi in slices])
+    loss_eval, _ = eng.finalize(eng.merge(parts), m, count)
     torch.cuda.synchronize()
+    return dict(loss=float(loss.item()), dh=dh.double().cpu().numpy(), dw=torch.cat(dws).double().cpu().numpy(),
+                loss_eval=float(loss_eval.item()))
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_vocab_sharding_emulated_on_one_gpu(world):
+    """Vocab sharding's per-shard arithmetic on one device, against the float64 oracle."""
+    h_s, h_t, W, mask, T = rand_problem(900, 576, 7001, seed=21)
+    ours = _vocab_sharded_on_one_gpu(h_s, h_t, W, mask, T, world)
     loss_ref, dh_ref, dw_ref, *_ = run_oracle_np(h_s, h_t, W, mask, T)
-    ours = dict(loss=float(loss.item()), dh=dh.double().cpu().numpy(), dw=torch.cat(dws).double().cpu().numpy())
     assert_close(ours, loss_ref, dh_ref, dw_ref, f"vocab shards x{world}")
+    assert abs(ours["loss_eval"] - loss_ref) <= LOSS_RTOL * abs(loss_ref)
+
+
+def test_vocab_sharding_c4_shape_world8_emulated():
+    """The large-vocabulary configuration as eight vocab shards of 31,040 lm_head rows (a
+    shard is not a multiple of the 128/256-row tiles), on 1,061 rows (ragged), against the
+    fp32 torch oracle over the whole vocabulary."""
+    p = O.make_problem("c4", n_rows=1024 + 37)
+    ours = _vocab_sharded_on_one_gpu(p["h_s"], p["h_t"], p["W"], p["mask"], p["T"], 8)
+    ref_loss, ref_dh, ref_dw = run_oracle_torch_gpu(p["h_s"], p["h_t"], p["W"], p["mask"], p["T"], chunk=512)
+    assert_close(ours, ref_loss, ref_dh, ref_dw, "c4 x8 shards")
+    assert abs(ours["loss_eval"] - ref_loss) <= LOSS_RTOL * abs(ref_loss)
+
+
+def test_pass_pieces_equal_training_step():
+    """klg_lse_record + klg_lse_merge + klg_pass2 + klg_kl_loss on the whole vocabulary
+    reproduce klg_fwd_bwd: the same kernels and plans, so bit for bit."""
+    from orthrus_training_test_b200 import ops
+    h_s, h_t, W, mask, T = rand_problem(700, 576, 5000, seed=23, tscale=2.0)
+    dev = torch.device("cuda:0")
+    hs, ht, w = (ops.to_compute_dtype(x.to(dev)) for x in (h_s, h_t, W))
+    m = ops.mask_u8(mask.to(dev))
+    loss, lse, cnt, row_kl, dh, dw = ops.kl_fwd_bwd(hs, ht, w, m, T, want_row_kl=True)
+    lse2 = ops.lse_merge(ops.lse_record(hs, ht, w, T)[None])
+    dh2, dw2, cross = ops.pass2(hs, ht, w, m, lse2, cnt, temperature=T)
+    loss2, row_kl2 = ops.kl_loss(lse2, cross, m, cnt, want_row_kl=True)
+    torch.cuda.synchronize()
+    assert torch.equal(lse, lse2)
+    assert torch.equal(dh, dh2) and torch.equal(dw, dw2)
+    torch.testing.assert_close(row_kl2, row_kl, rtol=1e-6, atol=1e-7)
+    assert abs(float(loss2) - float(loss)) <= 1e-6 * abs(float(loss))

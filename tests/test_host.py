@@ -47,3 +47,17 @@ def test_shim_rejects_cpu_tensors():
     x = torch.zeros(4, 64)
     with pytest.raises(RuntimeError, match="CUDA"):
         kl_gemm_loss(x, x, torch.zeros(10, 64), torch.ones(4, dtype=torch.bool))
+
+
+@pytest.mark.parametrize("h_shape,w_shape,n_tok,lse_shape", [
+    ((4, 64), (10, 32), 4, (4,)),      # hidden sizes differ
+    ((4, 64), (10, 64), 3, (4,)),      # too few tokens
+    ((4, 64), (10, 64), 4, (2, 2)),    # lse not [N]
+    ((64,), (10, 64), 1, (1,)),        # h not 2-D
+])
+def test_token_logprob_rejects_bad_shapes(h_shape, w_shape, n_tok, lse_shape):
+    """Shapes are checked on the host before any device pointer is formed."""
+    from orthrus_training_test_b200.sampling import token_logprob
+    with pytest.raises(ValueError):
+        token_logprob(torch.zeros(h_shape), torch.zeros(w_shape), torch.zeros(n_tok, dtype=torch.long),
+                      torch.zeros(lse_shape))
