@@ -302,15 +302,41 @@ int launch_lse_pair(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtens
   return KLG_OK;
 }
 
+// The resident-student-row variant (H <= 576) measured slower than the streamed kernel at the
+// 16,384-row shape (dZ chunk 0.66 vs 0.51 ms: its five 12 KB stages hide ~1,300 cycles of load
+// latency against the streamed ring's ~2,600), so it runs only with KLG_DZ_RES=1.
+bool dual_res_on(int n_kb) {
+  static const bool on = [] {
+    const char* v = std::getenv("KLG_DZ_RES");
+    return v && v[0] == '1';
+  }();
+  return on && n_kb <= klg::DZR_MAX_KB;
+}
+
+// Tensor maps of a dual-view launch: h_s with 128 x 64 boxes; h_t and W with 128 x 64 / 64 x 64
+// boxes (128-byte swizzle), or 128 x 32 / 64 x 32 (64-byte swizzle) for the resident variant.
+bool dual_maps(const void* hs, const void* ht, const void* w, int64_t n_rows, int64_t hidden, int64_t vocab, bool res,
+               CUtensorMap* mhs, CUtensorMap* mht, CUtensorMap* mw) {
+  if (!make_map(mhs, hs, hidden, n_rows, hidden, klg::BK, klg::BM)) return false;
+  if (res)
+    return make_map(mht, ht, hidden, n_rows, hidden, klg::DZR_SUB, klg::BM, CU_TENSOR_MAP_SWIZZLE_64B) &&
+           make_map(mw, w, hidden, vocab, hidden, klg::DZR_SUB, klg::DZP_BN / 2, CU_TENSOR_MAP_SWIZZLE_64B);
+  return make_map(mht, ht, hidden, n_rows, hidden, klg::BK, klg::BM) &&
+         make_map(mw, w, hidden, vocab, hidden, klg::BK, klg::DZP_BN / 2);
+}
+
 template <int MODE>
 int launch_dual_pair(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMap& mw, const CUtensorMap& mout,
                      const klg::DualArgs& a, cudaStream_t s) {
-  auto k = klg::dual_pair_kernel<MODE>;
-  cudaError_t e = set_smem(k, klg::DZP_SMEM);
+  const bool res = dual_res_on(a.n_kb);
+  auto k = res ? klg::dual_pair_kernel<MODE, true> : klg::dual_pair_kernel<MODE, false>;
+  const int smem = res ? klg::DualResCfg<MODE>::SMEM : klg::DZP_SMEM;
+  const int threads = res ? klg::DZR_THREADS : klg::DZP_THREADS;
+  cudaError_t e = set_smem(k, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dual_pair_kernel)");
   const int pairs = a.n_units < num_sms() / 2 ? a.n_units : num_sms() / 2;
   const int slot = trace_pre(s);
-  e = launch_k(k, dim3(2 * pairs), dim3(klg::DZP_THREADS), klg::DZP_SMEM, s, 2, mhs, mht, mw, mout, a);
+  e = launch_k(k, dim3(2 * pairs), dim3(threads), smem, s, 2, mhs, mht, mw, mout, a);
   trace_post(slot, s, MODE == klg::MODE_DZ ? KLG_KIND_DZ : KLG_KIND_STATS);
   if (e != cudaSuccess) return cuda_fail(e, "launch dual_pair_kernel");
   ++g_launches;
@@ -537,9 +563,7 @@ int klg_fwd_stats(const void* hs, const void* ht, const void* w, int64_t n_rows,
   a.scale_log2 = inv_temp * 1.4426950408889634f;
   a.partials = partials;
   alignas(64) CUtensorMap mhs, mht, mw;
-  if (!make_map(&mhs, hs, hidden, n_rows, hidden, klg::BK, klg::BM) ||
-      !make_map(&mht, ht, hidden, n_rows, hidden, klg::BK, klg::BM) ||
-      !make_map(&mw, w, hidden, vocab, hidden, klg::BK, klg::DZP_BN / 2))
+  if (!dual_maps(hs, ht, w, n_rows, hidden, vocab, dual_res_on(a.n_kb), &mhs, &mht, &mw))
     return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
   return launch_dual_pair<klg::MODE_STATS>(mhs, mht, mw, mw, a, (cudaStream_t)stream);
 }
@@ -655,9 +679,7 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
   int rc;
   const int bn = gemm_bn(hidden);
   alignas(64) CUtensorMap mhs, mht, mw, mw_mn, mhs_mn;
-  if (!make_map(&mhs, hs, hidden, n_rows, hidden, klg::BK, klg::BM) ||
-      !make_map(&mht, ht, hidden, n_rows, hidden, klg::BK, klg::BM) ||
-      !make_map(&mw, w, hidden, vocab, hidden, klg::BK, klg::DZP_BN / 2) ||
+  if (!dual_maps(hs, ht, w, n_rows, hidden, vocab, dual_res_on(cdiv(hidden, klg::BK)), &mhs, &mht, &mw) ||
       !make_map(&mw_mn, w, hidden, vocab, hidden, 32, klg::BK, CU_TENSOR_MAP_SWIZZLE_64B) ||
       !make_map(&mhs_mn, hs, hidden, n_rows, hidden, 32, klg::BK, CU_TENSOR_MAP_SWIZZLE_64B))
     return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");

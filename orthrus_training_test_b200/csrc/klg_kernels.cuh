@@ -631,26 +631,64 @@ constexpr int DZP_SMEM = 1024 + DZP_STAGES * DZP_STAGE_BYTES + DZP_STAGING_BYTES
 // Staging rows are DZP_COLS_PER_WARP bf16 wide (128 or 64 bytes) in the matching TMA swizzle.
 enum { MODE_DZ = 0, MODE_STATS = 1 };
 
+// Resident-row variant (RES, H <= 576): the CTA's 128 student rows (up to 9 k-blocks, 144 KB)
+// stay in shared memory for a whole unit, so only the teacher rows and the W half stream:
+// 12 KB per 256 MMA cycles (47 B/clk/SM) instead of 40 KB per 512 (78 B/clk/SM).  To leave
+// room for enough stages beside the resident block, the streamed operands come in
+// 32-column sub-blocks (64-byte swizzle), 12 KB a stage.  The resident block is released
+// k-block by k-block: the last tile of a unit commits each k-block's release once its MMAs
+// retire, and a loader warp (warp 0) refills it with the next unit's rows right away, so a
+// unit boundary costs no pipeline drain.
+constexpr int DZR_MAX_KB = 9;
+constexpr int DZR_SUB = 32;                                   // bf16 per streamed sub-block row (64 B)
+constexpr int DZR_HT_BYTES = BM * DZR_SUB * 2;                // 8 KB: 128 teacher rows x 32
+constexpr int DZR_W_BYTES = (DZP_BN / 2) * DZR_SUB * 2;       // 4 KB: this CTA's 64 W rows x 32
+constexpr int DZR_STAGE_BYTES = DZR_HT_BYTES + DZR_W_BYTES;   // 12 KB
+constexpr int DZR_A_BYTES = DZR_MAX_KB * TILE_128x64;         // 144 KB resident student rows
+#ifndef KLG_DZR_PROD
+#define KLG_DZR_PROD 2
+#endif
+constexpr int DZR_PROD = KLG_DZR_PROD;                        // streaming producer warps (after the epilogue)
+constexpr int DZR_THREADS = 32 * (DZP_PW + DZR_PROD);         // warp 0: resident loader
+constexpr int DZR_BAR_BYTES = 512;
+template <int MODE>
+struct DualResCfg {
+  static constexpr int STAGING = MODE == MODE_DZ ? DZP_STAGING_BYTES : 0;
+  static constexpr int STAGES_RAW = (227 * 1024 - 1024 - DZR_A_BYTES - STAGING - DZR_BAR_BYTES) / DZR_STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  static constexpr int SMEM = 1024 + DZR_A_BYTES + STAGES * DZR_STAGE_BYTES + STAGING + DZR_BAR_BYTES;
+};
+
 // MODE_DZ: pass 2 (dZ chunk + cross-term partials).  MODE_STATS: the single-pass forward
 // for evaluation -- per row and unit the online (m_s, S_s, m_t, S_t, A) record over the
 // unit's vocabulary tiles (no dZ, no staging use).
-template <int MODE>
-__global__ void __launch_bounds__(DZP_THREADS, 1)
+// RES = false: maps h_s, h_t (128 x 64 boxes) and W (64 x 64), 128-byte swizzle.
+// RES = true: map_hs as above; map_ht (128 x 32 boxes) and map_w (64 x 32), 64-byte swizzle.
+template <int MODE, bool RES>
+__global__ void __launch_bounds__(RES ? DZR_THREADS : DZP_THREADS, 1)
 dual_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ CUtensorMap map_ht,
                const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_out,
                const DualArgs a) {
+  constexpr int STAGES = RES ? DualResCfg<MODE>::STAGES : DZP_STAGES;
+  constexpr int STAGE_BYTES = RES ? DZR_STAGE_BYTES : DZP_STAGE_BYTES;
+  constexpr int A_REGION = RES ? DZR_A_BYTES : 0;
+  constexpr int STAGING = RES ? DualResCfg<MODE>::STAGING : DZP_STAGING_BYTES;
+  constexpr int NPROD = RES ? DZR_PROD : DZP_PROD;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const uint32_t sbase = smem_u32(smem);
-  const uint32_t stg0 = sbase + DZP_STAGES * DZP_STAGE_BYTES;
-  const uint32_t bar0 = stg0 + DZP_STAGING_BYTES;
+  const uint32_t abase = smem_u32(smem);                // resident student rows (RES)
+  const uint32_t sbase = abase + A_REGION;              // stage ring
+  const uint32_t stg0 = sbase + STAGES * STAGE_BYTES;
+  const uint32_t bar0 = stg0 + STAGING;
   const uint32_t full0 = bar0;
-  const uint32_t empty0 = bar0 + 8u * DZP_STAGES;
-  const uint32_t tfull0 = bar0 + 16u * DZP_STAGES;
+  const uint32_t empty0 = bar0 + 8u * STAGES;
+  const uint32_t tfull0 = bar0 + 16u * STAGES;
   const uint32_t tempty0 = tfull0 + 16u;
   const uint32_t done_bar = tempty0 + 16u;
+  const uint32_t afull0 = done_bar + 8u;                // RES [DZR_MAX_KB]: leader, both CTAs' resident bytes
+  const uint32_t aempty0 = afull0 + 8u * DZR_MAX_KB;    // RES [DZR_MAX_KB]: each CTA
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
@@ -660,7 +698,7 @@ dual_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_consta
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
-    for (int s = 0; s < DZP_STAGES; ++s) {
+    for (int s = 0; s < STAGES; ++s) {
       mbar_init(full0 + 8u * s, 2);
       mbar_init(empty0 + 8u * s, 1);
     }
@@ -669,6 +707,12 @@ dual_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_consta
       mbar_init(tempty0 + 8u * b, 2 * DZP_EPI_WARPS);
     }
     mbar_init(done_bar, 1);
+    if (RES) {
+      for (int kb = 0; kb < DZR_MAX_KB; ++kb) {
+        mbar_init(afull0 + 8u * kb, 2);
+        mbar_init(aempty0 + 8u * kb, 1);
+      }
+    }
     fence_mbar_init();
     tma_prefetch(&map_hs);
     tma_prefetch(&map_ht);
@@ -684,10 +728,77 @@ dual_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_consta
   volatile int* abort_p = &abort_flag;
   const uint32_t lead_full0 = mapa_shared(full0, 0);
   const uint32_t lead_tempty0 = mapa_shared(tempty0, 0);
+  const uint32_t lead_afull0 = mapa_shared(afull0, 0);
   const uint32_t peer_empty0 = mapa_shared(empty0, 1);
   const uint32_t peer_tfull0 = mapa_shared(tfull0, 1);
+  const uint32_t peer_aempty0 = mapa_shared(aempty0, 1);
 
-  if (warp == 0 || warp >= DZP_PW) {
+  if (RES && warp == 0) {
+    // ------------------------------------------------------------ resident loader (both CTAs, whole warp)
+    // k-block kb of a unit's student rows is loaded once the previous unit's last tile has
+    // retired its MMAs on kb (aempty), so the next unit's rows arrive while that tile finishes.
+    int uidx = -1, kb_loaded = 0;
+    bool ok = true;
+    for (int u = cid; ok && u < a.n_units; u += n_clusters) {
+      int rt, uv, vt0, vt1;
+      dual_unit(a, u, rt, uv, vt0, vt1);
+      const int row0 = rt * 256 + (int)rank * 128;
+      ++uidx;
+      kb_loaded = 0;
+      for (int kb = 0; kb < a.n_kb; ++kb) {
+        if (!warp_wait(aempty0 + 8u * kb, (uint32_t)(uidx & 1) ^ 1u, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        if (elect_one()) {
+          if (leader) mbar_arrive_expect_tx(afull0 + 8u * kb, 2 * TILE_128x64);
+          tma_load_2d_pair(abase + kb * TILE_128x64, &map_hs, lead_afull0 + 8u * kb, kb * BK, row0);
+          if (!leader) mbar_arrive_cluster(lead_afull0 + 8u * kb);
+        }
+        __syncwarp();
+        kb_loaded = kb + 1;
+      }
+    }
+    if (leader) {   // every resident load issued has landed (both CTAs' bytes count on the leader)
+      for (int kb = 0; kb < a.n_kb; ++kb) {
+        const int last = kb < kb_loaded ? uidx : uidx - 1;
+        if (last >= 0) mbar_wait_drain(afull0 + 8u * kb, (uint32_t)(last & 1));
+      }
+    }
+  } else if (RES && warp >= DZP_PW) {
+    // ------------------------------------------------------------ streaming producers (both CTAs, whole warp)
+    // teacher rows and the W half in 32-column sub-blocks; stage s belongs to producer s % NPROD
+    const int prod = warp - DZP_PW;
+    int stage = 0;
+    uint32_t phase = 0;
+    long long issued = 0;
+    bool ok = true;
+    for (int u = cid; ok && u < a.n_units; u += n_clusters) {
+      int rt, uv, vt0, vt1;
+      dual_unit(a, u, rt, uv, vt0, vt1);
+      const int row0 = rt * 256 + (int)rank * 128;
+      for (int vt = vt0; ok && vt < vt1; ++vt) {
+        const int wrow = a.v_begin + vt * DZP_BN + (int)rank * (DZP_BN / 2);
+        for (int ks = 0; ks < 2 * a.n_kb; ++ks) {
+          if (stage % NPROD == prod) {
+            if (!warp_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
+            if (elect_one()) {
+              const uint32_t sa = sbase + stage * STAGE_BYTES;
+              const uint32_t fb = lead_full0 + 8u * stage;
+              if (leader) mbar_arrive_expect_tx(full0 + 8u * stage, 2 * STAGE_BYTES);
+              tma_load_2d_pair(sa, &map_ht, fb, ks * DZR_SUB, row0);
+              tma_load_2d_pair(sa + DZR_HT_BYTES, &map_w, fb, ks * DZR_SUB, wrow);
+              if (!leader) mbar_arrive_cluster(fb);
+            }
+            __syncwarp();
+          }
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+    if (leader && prod == 0) drain_loads<STAGES>(full0, stage, phase, issued);
+  } else if (!RES && (warp == 0 || warp >= DZP_PW)) {
     // producer warps: warp 0 and warps DZP_PW.. take the pipeline's load steps round-robin
     const int prod = warp == 0 ? 0 : warp - DZP_PW + 1;
     {   // TMA producer (both CTAs, whole warp)
@@ -715,14 +826,73 @@ dual_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_consta
               }
             }
             ++issued;
-            if (++stage == DZP_STAGES) { stage = 0; phase ^= 1; }
+            if (++stage == STAGES) { stage = 0; phase ^= 1; }
           }
         }
       }
-      if (leader && prod == 0) drain_loads<DZP_STAGES>(full0, stage, phase, issued);
+      if (leader && prod == 0) drain_loads<STAGES>(full0, stage, phase, issued);
     }
   } else if (warp == 1) {
-    if (leader) {   // pair MMA issuer (leader, whole warp)
+    if (leader && RES) {   // pair MMA issuer, resident student rows (leader, whole warp)
+      constexpr uint32_t idesc = make_idesc_bf16(2 * BM, DZP_BN, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      int tcount = 0;
+      int uidx = -1;
+      bool ok = true;
+      for (int u = cid; ok && u < a.n_units; u += n_clusters) {
+        int rt, uv, vt0, vt1;
+        dual_unit(a, u, rt, uv, vt0, vt1);
+        ++uidx;
+        for (int vt = vt0; ok && vt < vt1; ++vt, ++tcount) {
+          const int buf = tcount & 1;
+          const uint32_t tph = (tcount >> 1) & 1;
+          if (!warp_wait(tempty0 + 8u * buf, tph ^ 1, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d_s = tmem + buf * 256;
+          const uint32_t d_t = d_s + 128;
+          const bool first = vt == vt0, last = vt == vt1 - 1;
+          for (int kb = 0; ok && kb < a.n_kb; ++kb) {
+            if (first) {   // this unit's k-block kb of the student rows has landed in both CTAs
+              if (!warp_wait(afull0 + 8u * kb, (uint32_t)(uidx & 1), abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
+              tc_fence_after();
+            }
+            for (int hf = 0; hf < 2; ++hf) {
+              if (!warp_wait(full0 + 8u * stage, phase, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
+              tc_fence_after();
+              if (elect_one()) {
+                const uint32_t sa = sbase + stage * STAGE_BYTES;
+                const uint32_t a_res = abase + kb * TILE_128x64;
+#pragma unroll
+                for (int j = 0; j < DZR_SUB / 16; ++j) {
+                  const uint64_t bdesc = desc_kmajor_sw64(sa + DZR_HT_BYTES, j);
+                  const uint32_t acc = (kb | hf | j) != 0;
+                  mma_bf16_pair(d_s, desc_kmajor(a_res, 2 * hf + j), bdesc, idesc, acc);
+                  mma_bf16_pair(d_t, desc_kmajor_sw64(sa, j), bdesc, idesc, acc);
+                }
+                mma_commit_pair(empty0 + 8u * stage);
+                mma_commit_pair(peer_empty0 + 8u * stage);
+              }
+              __syncwarp();
+              if (++stage == STAGES) { stage = 0; phase ^= 1; }
+            }
+            if (ok && last && elect_one()) {   // the unit's MMAs on kb are issued: release kb once they retire
+              mma_commit_pair(aempty0 + 8u * kb);
+              mma_commit_pair(peer_aempty0 + 8u * kb);
+            }
+            __syncwarp();
+          }
+          if (ok && elect_one()) {
+            mma_commit_pair(tfull0 + 8u * buf);
+            mma_commit_pair(peer_tfull0 + 8u * buf);
+          }
+          __syncwarp();
+        }
+      }
+      if (elect_one()) mma_commit_pair(done_bar);
+      __syncwarp();
+      mbar_wait_drain(done_bar, 0);
+    } else if (leader) {   // pair MMA issuer (leader, whole warp)
       constexpr uint32_t idesc = make_idesc_bf16(2 * BM, DZP_BN, false, false);
       int stage = 0;
       uint32_t phase = 0;
@@ -753,7 +923,7 @@ dual_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_consta
               mma_commit_pair(empty0 + 8u * stage);
               mma_commit_pair(peer_empty0 + 8u * stage);
             }
-            if (++stage == DZP_STAGES) { stage = 0; phase ^= 1; }
+            if (++stage == STAGES) { stage = 0; phase ^= 1; }
           }
           if (ok && elect_one()) {
             mma_commit_pair(tfull0 + 8u * buf);

@@ -328,6 +328,17 @@ __device__ __forceinline__ uint64_t make_desc_sw128(uint32_t saddr, uint32_t lbo
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t tile_base, int k16) {
   return make_desc_sw128(tile_base + 32u * k16, 16u, 1024u);
 }
+// K-major operand tile with 64-byte swizzle: rows of 32 bf16 (64 B) along K, 8-row groups
+// 512 B apart; the k-th 16-element slice starts 32*k bytes into the row (k = 0, 1).
+__device__ __forceinline__ uint64_t desc_kmajor_sw64(uint32_t tile_base, int k16) {
+  uint64_t d = 0;
+  d |= (uint64_t)(((tile_base + 32u * k16) >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;                          // leading byte offset (unused when K fits the row): 16 B
+  d |= (uint64_t)((512u >> 4) & 0x3FFF) << 32;     // stride byte offset: 8-row groups
+  d |= (uint64_t)1 << 46;                          // descriptor version (sm_100)
+  d |= (uint64_t)4 << 61;                          // SWIZZLE_64B
+  return d;
+}
 // MN-major operand tile loaded as 64-element-wide boxes of 64 K-rows each:
 // K-rows are 128 B apart (8-row groups 1024 B apart, SBO); successive 64-wide
 // MN atoms are one box (64 rows * 128 B = 8192 B) apart (LBO).  The k-th
