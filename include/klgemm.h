@@ -16,7 +16,8 @@
  *
  * Conventions
  *   - Inputs h_s, h_t [N, H] and W [V, H] are bf16, row-major, 16-byte aligned,
- *     H a multiple of 8.  (fp32 callers convert with klg_cast_f32_bf16.)
+ *     H a multiple of 8.  (fp32 callers use the *_f32 entry points, which keep fp32
+ *     fidelity, or round with klg_cast_f32_bf16.)
  *   - mask [N] is uint8 (nonzero = row carries loss), the reference's
  *     target != pad_token_id (train.py:163-164).
  *   - Every pointer is device memory owned by the caller; the library holds no
@@ -167,6 +168,26 @@ int klg_fwd_bwd(const void* h_s, const void* h_t, const void* w, const uint8_t* 
                 int64_t vocab, float inv_temp, int count_given, float* count, const float* grad, float* loss,
                 float* lse, float* row_kl, float* d_h_s, float* d_w, void* workspace, int64_t workspace_bytes,
                 void* stream);
+
+/* ---------------------------------------------------------------- fp32 inputs
+ * The CPU-runnable configuration and the reference's fp32 teacher path (train.py:188-191)
+ * compute in fp32; these variants keep fp32 fidelity on the bf16 tensor cores.  Each fp32
+ * operand x is split into bf16 planes hi = bf16(x), lo = bf16(x - hi) and the planes are laid
+ * side by side along H (hidden states [hi | hi | lo], lm_head [hi | lo | hi]), so a bf16
+ * product over the 3H columns is h_hi w_hi + h_hi w_lo + h_lo w_hi: the logits carry ~2^-16
+ * relative error before the fp32 accumulation.  dZ is kept as two bf16 planes (hi and lo) and
+ * the dW / dH GEMMs add up both; the 3H-wide gradients are folded back to H.  Work is about
+ * 3x (logits) to 6x (GEMMs) the bf16 path's.  Inputs h_s, h_t [N, H] and w [V, H] are fp32;
+ * every other argument is as for klg_fwd_bwd / klg_fwd. */
+int64_t klg_fwd_bwd_f32_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t vocab);
+int klg_fwd_bwd_f32(const float* h_s, const float* h_t, const float* w, const uint8_t* mask, int64_t n_rows,
+                    int64_t hidden, int64_t vocab, float inv_temp, int count_given, float* count, const float* grad,
+                    float* loss, float* lse, float* row_kl, float* d_h_s, float* d_w, void* workspace,
+                    int64_t workspace_bytes, void* stream);
+int64_t klg_fwd_f32_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t vocab);
+int klg_fwd_f32(const float* h_s, const float* h_t, const float* w, const uint8_t* mask, int64_t n_rows, int64_t hidden,
+                int64_t vocab, float inv_temp, int count_given, float* count, float* loss, float* lse, float* row_kl,
+                void* workspace, int64_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------- training step in pieces
  * klg_fwd_bwd split at the points where a vocab-sharded step exchanges data (each rank holds

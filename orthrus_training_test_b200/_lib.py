@@ -63,6 +63,13 @@ SIGNATURES = {
     "klg_fwd_bwd_chunk_cols": (c_int64, [c_int64, c_int64, c_int64]),
     "klg_fwd_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_float, c_int, c_void_p,
                             c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+    "klg_fwd_bwd_f32_workspace_bytes": (c_int64, [c_int64, c_int64, c_int64]),
+    "klg_fwd_bwd_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_float, c_int,
+                                c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                c_int64, c_void_p]),
+    "klg_fwd_f32_workspace_bytes": (c_int64, [c_int64, c_int64, c_int64]),
+    "klg_fwd_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_float, c_int, c_void_p,
+                            c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
     "klg_lse_workspace_bytes": (c_int64, [c_int64, c_int64]),
     "klg_lse_record": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_float, c_void_p, c_void_p,
                                c_int64, c_void_p]),

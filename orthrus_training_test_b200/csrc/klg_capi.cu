@@ -327,16 +327,17 @@ bool dual_maps(const void* hs, const void* ht, const void* w, int64_t n_rows, in
 
 template <int MODE>
 int launch_dual_pair(const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMap& mw, const CUtensorMap& mout,
-                     const klg::DualArgs& a, cudaStream_t s) {
-  const bool res = dual_res_on(a.n_kb);
-  auto k = res ? klg::dual_pair_kernel<MODE, true> : klg::dual_pair_kernel<MODE, false>;
+                     const CUtensorMap& mout2, const klg::DualArgs& a, cudaStream_t s, bool split = false) {
+  const bool res = !split && dual_res_on(a.n_kb);
+  auto k = split ? klg::dual_pair_kernel<MODE, false, true>
+                 : (res ? klg::dual_pair_kernel<MODE, true> : klg::dual_pair_kernel<MODE, false>);
   const int smem = res ? klg::DualResCfg<MODE>::SMEM : klg::DZP_SMEM;
   const int threads = res ? klg::DZR_THREADS : klg::DZP_THREADS;
   cudaError_t e = set_smem(k, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dual_pair_kernel)");
   const int pairs = a.n_units < num_sms() / 2 ? a.n_units : num_sms() / 2;
   const int slot = trace_pre(s);
-  e = launch_k(k, dim3(2 * pairs), dim3(threads), smem, s, 2, mhs, mht, mw, mout, a);
+  e = launch_k(k, dim3(2 * pairs), dim3(threads), smem, s, 2, mhs, mht, mw, mout, mout2, a);
   trace_post(slot, s, MODE == klg::MODE_DZ ? KLG_KIND_DZ : KLG_KIND_STATS);
   if (e != cudaSuccess) return cuda_fail(e, "launch dual_pair_kernel");
   ++g_launches;
@@ -565,7 +566,7 @@ int klg_fwd_stats(const void* hs, const void* ht, const void* w, int64_t n_rows,
   alignas(64) CUtensorMap mhs, mht, mw;
   if (!dual_maps(hs, ht, w, n_rows, hidden, vocab, dual_res_on(a.n_kb), &mhs, &mht, &mw))
     return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
-  return launch_dual_pair<klg::MODE_STATS>(mhs, mht, mw, mw, a, (cudaStream_t)stream);
+  return launch_dual_pair<klg::MODE_STATS>(mhs, mht, mw, mw, mw, a, (cudaStream_t)stream);
 }
 
 int klg_merge_stats(const float* partials, int n_part, int64_t n_rows, float* stats, void* stream) {
@@ -673,10 +674,14 @@ namespace {
 // Pass 2 over vocab chunks of `cols` columns: dZ chunk (dual_pair_kernel<MODE_DZ>) then one
 // pair-GEMM launch for dW_chunk and dH.  With a_parts set, the dZ pass also writes the
 // per-unit KL cross-term partials (at most 8 units per chunk), returning their count.
+// split (the fp32-faithful path): dZ is kept as two bf16 planes (hi and lo, row stride 2 * cols)
+// and each chunk's GEMM runs once per plane, both adding into the same fp32 dW and dH; dW's
+// K is then never split, so every dW element gets one addend per plane, in plane order.
 int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask, const float* lse, const float* count,
               const float* grad, int64_t n_rows, int64_t hidden, int64_t vocab, float inv_temp, float* d_hs, float* d_w,
-              __nv_bfloat16* dz, int64_t cols, float* a_parts, int* n_ap_out, cudaStream_t s) {
+              __nv_bfloat16* dz, int64_t cols, float* a_parts, int* n_ap_out, cudaStream_t s, bool split = false) {
   int rc;
+  const int64_t ld_dz = split ? 2 * cols : cols;
   const int bn = gemm_bn(hidden);
   alignas(64) CUtensorMap mhs, mht, mw, mw_mn, mhs_mn;
   if (!dual_maps(hs, ht, w, n_rows, hidden, vocab, dual_res_on(cdiv(hidden, klg::BK)), &mhs, &mht, &mw) ||
@@ -716,7 +721,7 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
   a.grad = grad;
   a.inv_temp = inv_temp;
   a.dz = dz;
-  a.ld_dz = (int)cols;
+  a.ld_dz = (int)ld_dz;
   a.a_parts = a_parts;
   int n_ap = 0;
   for (int64_t v0 = 0, ci = 0; v0 < vocab; v0 += cols, ++ci) {
@@ -729,16 +734,14 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
     a.n_units = a.n_rt * n_uv;
     a.a_part_base = n_ap;
     n_ap += klg::DZP_CSPLIT * n_uv;   // one cross-term partial per unit and column slice
-    alignas(64) CUtensorMap mdz_out;
-    if (!make_map(&mdz_out, dz, wv, n_rows, cols, klg::DZP_STORE_COLS, 32,
-                  CU_TENSOR_MAP_SWIZZLE_64B))
+    alignas(64) CUtensorMap mdz_out, mdz_out2;
+    if (!make_map(&mdz_out, dz, wv, n_rows, ld_dz, klg::DZP_STORE_COLS, 32, CU_TENSOR_MAP_SWIZZLE_64B) ||
+        (split && !make_map(&mdz_out2, dz + cols, wv, n_rows, ld_dz, klg::DZP_STORE_COLS, 32, CU_TENSOR_MAP_SWIZZLE_64B)))
       return fail(KLG_ERR_CUDA, "tensor map (dz store)");
-    if ((rc = launch_dual_pair<klg::MODE_DZ>(mhs, mht, mw, mdz_out, a, s))) return rc;
+    if (!split) mdz_out2 = mdz_out;
+    if ((rc = launch_dual_pair<klg::MODE_DZ>(mhs, mht, mw, mdz_out, mdz_out2, a, s, split))) return rc;
     if (!d_hs && !d_w) continue;
-    // one grouped launch: problem 0 = dW chunk (longer tiles first), problem 1 = dH += dZ W_chunk
-    alignas(64) CUtensorMap mdz_k, mdz_mn;
-    if (!make_map(&mdz_k, dz, wv, n_rows, cols, klg::BK, klg::BM) || !make_map(&mdz_mn, dz, wv, n_rows, cols, 64, klg::BK))
-      return fail(KLG_ERR_CUDA, "tensor map (dz operand)");
+    // one grouped launch per dZ plane: problem 0 = dW chunk (longer tiles first), problem 1 = dH += dZ W_chunk
     // dW's K (all rows) may be split in two, at the point that gives the shortest
     // simulated schedule (the uneven pieces fill the gaps the equal tiles leave).  At most
     // two partial sums meet in any dW element, and the reduce-adds onto zero give the
@@ -746,12 +749,19 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
     klg::PairGemmArgs g{};
     g.p[1] = gemm_problem(d_hs != nullptr, (int)n_rows, (int)hidden, (int)wv, bn, nullptr, (int)hidden, 1, 0,
                           (int)v0, 0, 256, 0, 0);
-    const int kb_split = pick_dw_split((int)n_rows, (int)wv, (int)hidden, bn);
+    const int kb_split = split ? 0 : pick_dw_split((int)n_rows, (int)wv, (int)hidden, bn);
     g.p[0] = gemm_problem(d_w != nullptr, (int)wv, (int)hidden, (int)n_rows, bn, nullptr, (int)hidden, 1, 0, 0, 1, 256,
                           kb_split, (int)v0);
     g.n_tiles = g.p[0].n_tiles + g.p[1].n_tiles;
     (void)ci;
-    if ((rc = launch_gemm_pair(bn, mdz_mn, mhs_mn, mdz_k, mw_mn, mdw, mdh, g, s))) return rc;
+    for (int plane = 0; plane < (split ? 2 : 1); ++plane) {
+      const __nv_bfloat16* dzp = dz + plane * cols;
+      alignas(64) CUtensorMap mdz_k, mdz_mn;
+      if (!make_map(&mdz_k, dzp, wv, n_rows, ld_dz, klg::BK, klg::BM) ||
+          !make_map(&mdz_mn, dzp, wv, n_rows, ld_dz, 64, klg::BK))
+        return fail(KLG_ERR_CUDA, "tensor map (dz operand)");
+      if ((rc = launch_gemm_pair(bn, mdz_mn, mhs_mn, mdz_k, mw_mn, mdw, mdh, g, s))) return rc;
+    }
   }
   if (n_ap_out) *n_ap_out = n_ap;
   return KLG_OK;
@@ -776,7 +786,7 @@ struct FwdBwdLayout {
   int n_lp, n_ap;
 };
 int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
-FwdBwdLayout fwd_bwd_layout_uncached(int64_t n_rows, int64_t vocab, int64_t workspace_bytes) {
+FwdBwdLayout fwd_bwd_layout_uncached(int64_t n_rows, int64_t vocab, int64_t workspace_bytes, int planes) {
   FwdBwdLayout L{};
   int vpu, n_uv;
   plan_dual(2 * cdiv(n_rows, 256), cdiv(vocab, klg::LSE_BN), num_sms() / 2, vpu, n_uv);
@@ -786,13 +796,13 @@ FwdBwdLayout fwd_bwd_layout_uncached(int64_t n_rows, int64_t vocab, int64_t work
   L.cols = -1;
   const int64_t full = (int64_t)cdiv(vocab, 128) * 128;
   // widest chunk that could fit (the cross-term partials only shrink the room), then narrower
-  int64_t c = (workspace_bytes - L.a_parts_off) / (n_rows * 2);
+  int64_t c = (workspace_bytes - L.a_parts_off) / (n_rows * 2 * planes);
   c = std::min(full, (c / 128) * 128);
   for (; c >= 128; c -= 128) {
     if (cdiv(vocab, c) > KLG_BWD_HEADER / 4) break;
     const int n_ap = pass2_parts(n_rows, vocab, c);
     const int64_t dz_off = align256(L.a_parts_off + (int64_t)n_ap * n_rows * 4);
-    if (dz_off + n_rows * c * 2 <= workspace_bytes) {
+    if (dz_off + n_rows * c * 2 * planes <= workspace_bytes) {
       L.cols = c;
       L.n_ap = n_ap;
       L.dz_off = dz_off;
@@ -803,16 +813,16 @@ FwdBwdLayout fwd_bwd_layout_uncached(int64_t n_rows, int64_t vocab, int64_t work
 }
 
 // Memoised: the layout is a pure function of the shape and workspace size.
-FwdBwdLayout fwd_bwd_layout(int64_t n_rows, int64_t vocab, int64_t workspace_bytes) {
+FwdBwdLayout fwd_bwd_layout(int64_t n_rows, int64_t vocab, int64_t workspace_bytes, int planes = 1) {
   static std::mutex mu;
-  static std::map<std::tuple<int64_t, int64_t, int64_t, int>, FwdBwdLayout> memo;
-  const auto key = std::make_tuple(n_rows, vocab, workspace_bytes, num_sms());
+  static std::map<std::tuple<int64_t, int64_t, int64_t, int, int>, FwdBwdLayout> memo;
+  const auto key = std::make_tuple(n_rows, vocab, workspace_bytes, num_sms(), planes);
   {
     std::lock_guard<std::mutex> lk(mu);
     auto it = memo.find(key);
     if (it != memo.end()) return it->second;
   }
-  const FwdBwdLayout L = fwd_bwd_layout_uncached(n_rows, vocab, workspace_bytes);
+  const FwdBwdLayout L = fwd_bwd_layout_uncached(n_rows, vocab, workspace_bytes, planes);
   std::lock_guard<std::mutex> lk(mu);
   if (memo.size() > 256) memo.clear();
   memo[key] = L;
@@ -877,13 +887,118 @@ int klg_bwd(const void* hs, const void* ht, const void* w, const uint8_t* mask, 
                    nullptr, nullptr, (cudaStream_t)stream);
 }
 
-int64_t klg_fwd_bwd_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t vocab) {
+}  // extern "C"
+
+namespace {
+
+// Workspace of the training step with `planes` bf16 planes of dZ (1, or 2 for the fp32-faithful path).
+int64_t fwd_bwd_ws(int64_t n_rows, int64_t hidden, int64_t vocab, int planes) {
   if (n_rows < 1 || vocab < 1) return -1;
   const int64_t dz_bytes = klg_bwd_workspace_bytes(n_rows, hidden, vocab) - KLG_BWD_HEADER;
   const int64_t cols = dz_bytes / (n_rows * 2);
   FwdBwdLayout L = fwd_bwd_layout(n_rows, vocab, INT64_MAX / 4);
   const int n_ap = pass2_parts(n_rows, vocab, cols);
-  return align256(L.a_parts_off + (int64_t)n_ap * n_rows * 4) + dz_bytes;
+  return align256(L.a_parts_off + (int64_t)n_ap * n_rows * 4) + dz_bytes * planes;
+}
+
+// The training step on bf16 rows (validated, device bound): count, pass 1, pass 2, loss.
+int fwd_bwd_core(const void* hs, const void* ht, const void* w, const uint8_t* mask, int64_t n_rows, int64_t hidden,
+                 int64_t vocab, float inv_temp, int count_given, float* count, const float* grad, float* loss,
+                 float* lse, float* row_kl, float* d_hs, float* d_w, void* workspace, int64_t workspace_bytes,
+                 cudaStream_t s, int planes) {
+  int rc;
+  const FwdBwdLayout L = fwd_bwd_layout(n_rows, vocab, workspace_bytes, planes);
+  if (L.cols < 0)
+    return fail(KLG_ERR_WORKSPACE, "workspace of %lld bytes too small (see the *_workspace_bytes functions)",
+                (long long)workspace_bytes);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* lse_parts = reinterpret_cast<float*>(ws + L.lse_parts_off);
+  float* a_parts = reinterpret_cast<float*>(ws + L.a_parts_off);
+  if (!count_given && (rc = klg_count_valid(mask, n_rows, count, s))) return rc;
+
+  // pass 1: log-sum-exp of both views on CTA pairs
+  if ((rc = run_pass1(hs, ht, w, n_rows, hidden, vocab, inv_temp, lse_parts, L.n_lp, lse, nullptr, s))) return rc;
+  // pass 2: dZ chunks (+ KL cross-term partials) and the dW / dH GEMMs
+  int n_ap = 0;
+  __nv_bfloat16* dz = reinterpret_cast<__nv_bfloat16*>(ws + L.dz_off);
+  if ((rc = run_pass2(hs, ht, w, mask, lse, count, grad, n_rows, hidden, vocab, inv_temp, d_hs, d_w, dz,
+                      L.cols, a_parts, &n_ap, s, planes == 2)))
+    return rc;
+  if (n_ap != L.n_ap) return fail(KLG_ERR_ARG, "internal plan mismatch (cross-term partials)");
+  // per-row KL in 256-row blocks (block sums reuse the pass-1 partial area), then the loss
+  const int nb = cdiv(n_rows, 256);
+  float* block_sums = lse_parts;
+  int slot = trace_pre(s);
+  cudaError_t e = launch_k(klg::row_kl_pair_kernel, dim3(nb), dim3(256), 0, s, 1, lse, a_parts, n_ap, mask,
+                           (int)n_rows, row_kl, block_sums);
+  trace_post(slot, s, KLG_KIND_FINALIZE);
+  if (e != cudaSuccess) return cuda_fail(e, "launch row_kl_pair_kernel");
+  ++g_launches;
+  slot = trace_pre(s);
+  e = launch_k(klg::loss_from_sums_kernel, dim3(1), dim3(1024), 0, s, 1, block_sums, nb, count, loss);
+  trace_post(slot, s, KLG_KIND_FINALIZE);
+  if (e != cudaSuccess) return cuda_fail(e, "launch loss_from_sums_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
+// fp32-faithful inputs: [hi | hi | lo] rows for the hidden states, [hi | lo | hi] for the lm_head.
+int launch_split3(const float* x, int64_t n_rows, int64_t hidden, int order, __nv_bfloat16* out, cudaStream_t s) {
+  const long long n = n_rows * hidden;
+  const int blocks = (int)std::min<long long>(cdiv(n, 256), 8ll * num_sms());
+  const int slot = trace_pre(s);
+  cudaError_t e = launch_k(klg::split3_kernel, dim3(blocks), dim3(256), 0, s, 1, x, (long long)n_rows, (int)hidden,
+                           order, out);
+  trace_post(slot, s, KLG_KIND_CAST);
+  if (e != cudaSuccess) return cuda_fail(e, "launch split3_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
+int launch_fold2(const float* in, int64_t n_rows, int64_t hidden, int a, int b, float* out, cudaStream_t s) {
+  const long long n = n_rows * hidden;
+  const int blocks = (int)std::min<long long>(cdiv(n, 256), 8ll * num_sms());
+  const int slot = trace_pre(s);
+  cudaError_t e = launch_k(klg::fold2_kernel, dim3(blocks), dim3(256), 0, s, 1, in, (long long)n_rows, (int)hidden,
+                           a, b, out);
+  trace_post(slot, s, KLG_KIND_CAST);
+  if (e != cudaSuccess) return cuda_fail(e, "launch fold2_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
+// Layout of the fp32 path's workspace: split rows, then (fwd_bwd) the 3H-wide gradients, then
+// the bf16 path's own workspace.
+struct F32Layout {
+  int64_t hs, ht, w, dh, dw, core, total;
+};
+F32Layout f32_layout(int64_t n_rows, int64_t hidden, int64_t vocab, int64_t core_bytes, bool grads) {
+  F32Layout L{};
+  const int64_t h3 = 3 * hidden;
+  L.hs = 0;
+  L.ht = align256(L.hs + n_rows * h3 * 2);
+  L.w = align256(L.ht + n_rows * h3 * 2);
+  L.dh = align256(L.w + vocab * h3 * 2);
+  L.dw = align256(L.dh + (grads ? n_rows * h3 * 4 : 0));
+  L.core = align256(L.dw + (grads ? vocab * h3 * 4 : 0));
+  L.total = core_bytes < 0 ? -1 : L.core + core_bytes;
+  return L;
+}
+
+int check_f32(const float* hs, const float* ht, const float* w, int64_t n_rows, int64_t hidden, int64_t vocab,
+              float inv_temp) {
+  int rc = check_problem(hs, ht, w, n_rows, hidden, vocab, inv_temp);
+  if (rc) return rc;
+  if (3 * hidden > (1ll << 20)) return fail(KLG_ERR_ARG, "hidden=%lld too large for the fp32 path", (long long)hidden);
+  return KLG_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t klg_fwd_bwd_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t vocab) {
+  return fwd_bwd_ws(n_rows, hidden, vocab, 1);
 }
 
 int64_t klg_fwd_bwd_chunk_cols(int64_t n_rows, int64_t vocab, int64_t workspace_bytes) {
@@ -901,44 +1016,79 @@ int klg_fwd_bwd(const void* hs, const void* ht, const void* w, const uint8_t* ma
   if ((d_hs && !aligned16(d_hs)) || (d_w && !aligned16(d_w))) return fail(KLG_ERR_ALIGN, "outputs must be 16-byte aligned");
   if (!workspace || !aligned16(workspace)) return fail(KLG_ERR_WORKSPACE, "null or misaligned workspace");
   if ((rc = bind_device(hs))) return rc;   // the layout depends on the SM count of hs's device
-  const FwdBwdLayout L = fwd_bwd_layout(n_rows, vocab, workspace_bytes);
-  if (L.cols < 0)
-    return fail(KLG_ERR_WORKSPACE, "workspace of %lld bytes too small (see klg_fwd_bwd_workspace_bytes)",
-                (long long)workspace_bytes);
   NvtxRange nvtx_range("klg_fwd_bwd");
+  return fwd_bwd_core(hs, ht, w, mask, n_rows, hidden, vocab, inv_temp, count_given, count, grad, loss, lse, row_kl,
+                      d_hs, d_w, workspace, workspace_bytes, (cudaStream_t)stream, 1);
+}
+
+// ---------------------------------------------------------------- fp32-faithful path
+int64_t klg_fwd_bwd_f32_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t vocab) {
+  if (n_rows < 1 || vocab < 1 || hidden < 8) return -1;
+  return f32_layout(n_rows, hidden, vocab, fwd_bwd_ws(n_rows, 3 * hidden, vocab, 2), true).total;
+}
+
+int klg_fwd_bwd_f32(const float* hs, const float* ht, const float* w, const uint8_t* mask, int64_t n_rows,
+                    int64_t hidden, int64_t vocab, float inv_temp, int count_given, float* count, const float* grad,
+                    float* loss, float* lse, float* row_kl, float* d_hs, float* d_w, void* workspace,
+                    int64_t workspace_bytes, void* stream) {
+  int rc = check_f32(hs, ht, w, n_rows, hidden, vocab, inv_temp);
+  if (rc) return rc;
+  if (!mask || !count || !loss || !lse) return fail(KLG_ERR_ARG, "null mask/count/loss/lse");
+  if ((d_hs && !aligned16(d_hs)) || (d_w && !aligned16(d_w))) return fail(KLG_ERR_ALIGN, "outputs must be 16-byte aligned");
+  if (!workspace || !aligned16(workspace)) return fail(KLG_ERR_WORKSPACE, "null or misaligned workspace");
+  if ((rc = bind_device(hs))) return rc;
+  const F32Layout F = f32_layout(n_rows, hidden, vocab, 0, true);
+  if (workspace_bytes <= F.core)
+    return fail(KLG_ERR_WORKSPACE, "fp32 workspace of %lld bytes too small (see klg_fwd_bwd_f32_workspace_bytes)",
+                (long long)workspace_bytes);
+  NvtxRange nvtx_range("klg_fwd_bwd_f32");
   cudaStream_t s = (cudaStream_t)stream;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  float* lse_parts = reinterpret_cast<float*>(ws + L.lse_parts_off);
-  float* a_parts = reinterpret_cast<float*>(ws + L.a_parts_off);
-  if (!count_given && (rc = klg_count_valid(mask, n_rows, count, stream))) return rc;
-
-  // pass 1: log-sum-exp of both views on CTA pairs
-  if ((rc = run_pass1(hs, ht, w, n_rows, hidden, vocab, inv_temp, lse_parts, L.n_lp, lse, nullptr, s))) return rc;
-  // pass 2: dZ chunks (+ KL cross-term partials) and the dW / dH GEMMs
-  int n_ap = 0;
-
-  __nv_bfloat16* dz = reinterpret_cast<__nv_bfloat16*>(ws + L.dz_off);
-  if ((rc = run_pass2(hs, ht, w, mask, lse, count, grad, n_rows, hidden, vocab, inv_temp, d_hs, d_w, dz,
-                      L.cols, a_parts, &n_ap, s)))
+  auto* hs3 = reinterpret_cast<__nv_bfloat16*>(ws + F.hs);
+  auto* ht3 = reinterpret_cast<__nv_bfloat16*>(ws + F.ht);
+  auto* w3 = reinterpret_cast<__nv_bfloat16*>(ws + F.w);
+  float* dh3 = d_hs ? reinterpret_cast<float*>(ws + F.dh) : nullptr;
+  float* dw3 = d_w ? reinterpret_cast<float*>(ws + F.dw) : nullptr;
+  if ((rc = launch_split3(hs, n_rows, hidden, 0, hs3, s)) || (rc = launch_split3(ht, n_rows, hidden, 0, ht3, s)) ||
+      (rc = launch_split3(w, vocab, hidden, 1, w3, s)))
     return rc;
-  if (n_ap != L.n_ap) return fail(KLG_ERR_ARG, "internal plan mismatch (cross-term partials)");
-  {
-    // per-row KL in 256-row blocks (block sums reuse the pass-1 partial area), then the loss
-    const int nb = cdiv(n_rows, 256);
-    float* block_sums = lse_parts;
-    int slot = trace_pre(s);
-    cudaError_t e = launch_k(klg::row_kl_pair_kernel, dim3(nb), dim3(256), 0, s, 1, lse, a_parts, n_ap, mask,
-                             (int)n_rows, row_kl, block_sums);
-    trace_post(slot, s, KLG_KIND_FINALIZE);
-    if (e != cudaSuccess) return cuda_fail(e, "launch row_kl_pair_kernel");
-    ++g_launches;
-    slot = trace_pre(s);
-    e = launch_k(klg::loss_from_sums_kernel, dim3(1), dim3(1024), 0, s, 1, block_sums, nb, count, loss);
-    trace_post(slot, s, KLG_KIND_FINALIZE);
-    if (e != cudaSuccess) return cuda_fail(e, "launch loss_from_sums_kernel");
-    ++g_launches;
-  }
+  if ((rc = fwd_bwd_core(hs3, ht3, w3, mask, n_rows, 3 * hidden, vocab, inv_temp, count_given, count, grad, loss, lse,
+                         row_kl, dh3, dw3, ws + F.core, workspace_bytes - F.core, s, 2)))
+    return rc;
+  // dH' = dZ [W_hi | W_lo | W_hi] -> dH = blocks 0 + 1;  dW' = dZ^T [h_hi | h_hi | h_lo] -> dW = blocks 0 + 2
+  if (d_hs && (rc = launch_fold2(dh3, n_rows, hidden, 0, 1, d_hs, s))) return rc;
+  if (d_w && (rc = launch_fold2(dw3, vocab, hidden, 0, 2, d_w, s))) return rc;
   return KLG_OK;
+}
+
+int64_t klg_fwd_f32_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t vocab) {
+  if (n_rows < 1 || vocab < 1 || hidden < 8) return -1;
+  return f32_layout(n_rows, hidden, vocab, klg_fwd_workspace_bytes(n_rows, vocab), false).total;
+}
+
+int klg_fwd_f32(const float* hs, const float* ht, const float* w, const uint8_t* mask, int64_t n_rows, int64_t hidden,
+                int64_t vocab, float inv_temp, int count_given, float* count, float* loss, float* lse, float* row_kl,
+                void* workspace, int64_t workspace_bytes, void* stream) {
+  int rc = check_f32(hs, ht, w, n_rows, hidden, vocab, inv_temp);
+  if (rc) return rc;
+  if (!mask || !count || !loss || !lse) return fail(KLG_ERR_ARG, "null output pointer");
+  if (!workspace || !aligned16(workspace)) return fail(KLG_ERR_WORKSPACE, "null or misaligned workspace");
+  if ((rc = bind_device(hs))) return rc;
+  const F32Layout F = f32_layout(n_rows, hidden, vocab, 0, false);
+  if (workspace_bytes <= F.core)
+    return fail(KLG_ERR_WORKSPACE, "fp32 workspace of %lld bytes too small (see klg_fwd_f32_workspace_bytes)",
+                (long long)workspace_bytes);
+  NvtxRange nvtx_range("klg_fwd_f32");
+  cudaStream_t s = (cudaStream_t)stream;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  auto* hs3 = reinterpret_cast<__nv_bfloat16*>(ws + F.hs);
+  auto* ht3 = reinterpret_cast<__nv_bfloat16*>(ws + F.ht);
+  auto* w3 = reinterpret_cast<__nv_bfloat16*>(ws + F.w);
+  if ((rc = launch_split3(hs, n_rows, hidden, 0, hs3, s)) || (rc = launch_split3(ht, n_rows, hidden, 0, ht3, s)) ||
+      (rc = launch_split3(w, vocab, hidden, 1, w3, s)))
+    return rc;
+  return klg_fwd(hs3, ht3, w3, mask, n_rows, 3 * hidden, vocab, inv_temp, count_given, count, loss, lse, row_kl,
+                 ws + F.core, workspace_bytes - F.core, stream);
 }
 
 // ---------------------------------------------------------------- training step in pieces (vocab sharding)

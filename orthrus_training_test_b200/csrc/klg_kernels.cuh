@@ -156,6 +156,30 @@ __device__ __forceinline__ void dz_chunk(const uint32_t (&bs)[32], const uint32_
   acc += a0 + a1;
 }
 
+// dz_chunk for the fp32-faithful path: dZ as two bf16 planes, hi = bf16(d) and
+// lo = bf16(d - hi), so hi + lo carries d to ~2^-16 relative.
+__device__ __forceinline__ void dz_chunk_split(const uint32_t (&bs)[32], const uint32_t (&bt)[32], int nvalid,
+                                               float sl2, float Ls, float Lt, float coef, uint32_t (&ph)[16],
+                                               uint32_t (&pl)[16], float& acc) {
+  float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) {
+    const float zs0 = __uint_as_float(bs[j]), zs1 = __uint_as_float(bs[j + 1]);
+    const float zt0 = __uint_as_float(bt[j]), zt1 = __uint_as_float(bt[j + 1]);
+    const float q0 = ex2(fmaf(zs0, sl2, -Ls));
+    const float q1 = ex2(fmaf(zs1, sl2, -Ls));
+    const float p0 = ex2(fmaf(zt0, sl2, -Lt));
+    const float p1 = ex2(fmaf(zt1, sl2, -Lt));
+    const float d0 = coef * (q0 - p0), d1 = coef * (q1 - p1);
+    const __nv_bfloat162 h = __floats2bfloat162_rn(d0, d1);
+    ph[j / 2] = *reinterpret_cast<const uint32_t*>(&h);
+    pl[j / 2] = pack_bf16x2(d0 - __low2float(h), d1 - __high2float(h));
+    a0 = fmaf(j < nvalid ? p0 : 0.f, zt0 - zs0, a0);
+    a1 = fmaf(j + 1 < nvalid ? p1 : 0.f, zt1 - zs1, a1);
+  }
+  acc += a0 + a1;
+}
+
 // =====================================================================================
 // pass-1 log-sum-exp on CTA pairs (training path)
 //
@@ -664,11 +688,13 @@ struct DualResCfg {
 // unit's vocabulary tiles (no dZ, no staging use).
 // RES = false: maps h_s, h_t (128 x 64 boxes) and W (64 x 64), 128-byte swizzle.
 // RES = true: map_hs as above; map_ht (128 x 32 boxes) and map_w (64 x 32), 64-byte swizzle.
-template <int MODE, bool RES>
+// SPLIT (MODE_DZ, fp32-faithful path): dZ leaves as two bf16 planes, hi through map_out and
+// lo = bf16(dZ - hi) through map_out2.
+template <int MODE, bool RES, bool SPLIT = false>
 __global__ void __launch_bounds__(RES ? DZR_THREADS : DZP_THREADS, 1)
 dual_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constant__ CUtensorMap map_ht,
                const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_out,
-               const DualArgs a) {
+               const __grid_constant__ CUtensorMap map_out2, const DualArgs a) {
   constexpr int STAGES = RES ? DualResCfg<MODE>::STAGES : DZP_STAGES;
   constexpr int STAGE_BYTES = RES ? DZR_STAGE_BYTES : DZP_STAGE_BYTES;
   constexpr int A_REGION = RES ? DZR_A_BYTES : 0;
@@ -718,6 +744,7 @@ dual_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_consta
     tma_prefetch(&map_ht);
     tma_prefetch(&map_w);
     tma_prefetch(&map_out);
+    if (SPLIT) tma_prefetch(&map_out2);
   }
   if (warp == 1) tmem_alloc_pair(smem_u32(&tmem_slot), DUAL_TMEM_COLS);
   tc_fence_before();
@@ -1016,7 +1043,28 @@ dual_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_consta
           tmem_ld32_raw(tbase + 128 + c * 32, bt);
           tmem_wait_ld_regs(bs, bt);
           const int nvalid = a.v_count - (vt * DZP_BN + h * CW + c * 32);
-          if (nvalid > 0) {
+          if (SPLIT && nvalid > 0) {
+            uint32_t ph[16], pl[16];
+            dz_chunk_split(bs, bt, nvalid, a.scale_log2, Ls, Lt, coef, ph, pl, acc);
+            const uint32_t rowp = stg + (uint32_t)lane * 64u;
+            const int x0 = vt * DZP_BN + h * CW + c * 32, y0 = rt * 256 + (int)rank * 128 + q * 32;
+#pragma unroll
+            for (int plane = 0; plane < 2; ++plane) {   // the staging buffer serves both planes in turn
+              if (lane == 0) bulk_wait_read0();
+              __syncwarp();
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const uint32_t* v = plane ? pl : ph;
+                st_shared_v4(rowp + (((uint32_t)k ^ swz) << 4), v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+              }
+              fence_async_shared();
+              __syncwarp();
+              if (lane == 0) {
+                if (y0 < a.n_rows) tma_store_2d(plane ? &map_out2 : &map_out, stg, x0, y0);
+                bulk_commit();
+              }
+            }
+          } else if (nvalid > 0) {
             uint32_t pk[16];
             dz_chunk(bs, bt, nvalid, a.scale_log2, Ls, Lt, coef, pk, acc);
             // staging is free once the previous chunk's store has read it
@@ -1837,6 +1885,41 @@ __global__ void __launch_bounds__(256) token_logit_kernel(const __nv_bfloat16* _
   }
   acc = warp_sum_f32(acc);
   if (lane == 0) z[i] = (t >= 0 && t < vocab) ? acc : __int_as_float(0x7fc00000);   // NaN for a token out of range
+}
+
+// fp32 rows -> bf16 rows three times as wide, for the fp32-faithful path: with hi = bf16(x)
+// and lo = bf16(x - hi), row r of out is [hi | hi | lo] (order 0, the hidden states) or
+// [hi | lo | hi] (order 1, the lm_head), so the products of the two kinds of rows along the
+// 3H columns add up to x_hi w_hi + x_hi w_lo + x_lo w_hi.
+__global__ void split3_kernel(const float* __restrict__ x, long long n_rows, int hidden, int order,
+                              __nv_bfloat16* __restrict__ out) {
+  pdl_enter();
+  const long long n = n_rows * hidden;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / hidden;
+    const int c = (int)(i - r * hidden);
+    const float v = x[i];
+    const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+    const __nv_bfloat16 lo = __float2bfloat16_rn(v - __bfloat162float(hi));
+    __nv_bfloat16* o = out + r * 3 * hidden + c;
+    o[0] = hi;
+    o[hidden] = order ? lo : hi;
+    o[2 * hidden] = order ? hi : lo;
+  }
+}
+
+// out[r][c] = in[r][a H + c] + in[r][b H + c] for in [n_rows][3H] (the gradient blocks of the
+// fp32-faithful path that carry the hi and lo parts of the same operand).
+__global__ void fold2_kernel(const float* __restrict__ in, long long n_rows, int hidden, int a, int b,
+                             float* __restrict__ out) {
+  pdl_enter();
+  const long long n = n_rows * hidden;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / hidden;
+    const int c = (int)(i - r * hidden);
+    const float* row = in + r * 3 * hidden;
+    out[i] = row[a * hidden + c] + row[b * hidden + c];
+  }
 }
 
 __global__ void cast_f32_bf16_kernel(const float* __restrict__ in, __nv_bfloat16* __restrict__ out, long long n) {

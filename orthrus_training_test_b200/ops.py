@@ -40,6 +40,23 @@ def _require_cuda(*ts):
     return dev
 
 
+def to_fp32(x: torch.Tensor) -> torch.Tensor:
+    """fp32, contiguous (bf16 inputs widen exactly): the operands of the fp32-faithful path."""
+    x = x.detach()
+    _require_cuda(x)
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError(f"unsupported dtype {x.dtype} (bf16 or fp32)")
+    return x.float().contiguous()
+
+
+def prepare_inputs(h_s: torch.Tensor, h_t: torch.Tensor, weight: torch.Tensor):
+    """The operands in the arithmetic the op will use: all fp32 when any input is fp32 (the
+    fp32-faithful path, split-bf16 on the tensor cores), else bf16."""
+    if any(x.dtype == torch.float32 for x in (h_s, h_t, weight)):
+        return to_fp32(h_s), to_fp32(h_t), to_fp32(weight)
+    return to_compute_dtype(h_s), to_compute_dtype(h_t), to_compute_dtype(weight)
+
+
 def to_compute_dtype(x: torch.Tensor) -> torch.Tensor:
     """bf16, contiguous.  fp32 inputs are rounded to bf16 by the library's cast kernel."""
     x = x.detach()
@@ -115,7 +132,8 @@ def finalize(stats: torch.Tensor, mask: torch.Tensor, count: torch.Tensor,
 def kl_forward(h_s: torch.Tensor, h_t: torch.Tensor, weight: torch.Tensor, mask: torch.Tensor,
                temperature: float = 1.0, count: Optional[torch.Tensor] = None, want_row_kl: bool = False):
     """Whole forward on one device.  ``count`` (a ``[1]`` fp32 device tensor)
-    overrides the normaliser (e.g. an all-reduced global count).
+    overrides the normaliser (e.g. an all-reduced global count).  bf16 inputs take the bf16
+    path; fp32 inputs (all three) the fp32-faithful split-bf16 path.
 
     Returns ``(loss, lse, count, row_kl)``.
     """
@@ -126,14 +144,15 @@ def kl_forward(h_s: torch.Tensor, h_t: torch.Tensor, weight: torch.Tensor, mask:
     if h_t.shape != h_s.shape or weight.shape[1] != H or m.numel() != N:
         raise ValueError(f"shape mismatch: h_s {tuple(h_s.shape)} h_t {tuple(h_t.shape)} "
                          f"weight {tuple(weight.shape)} mask {tuple(m.shape)}")
-    ws_bytes = int(_lib.lib().klg_fwd_workspace_bytes(N, V))
+    f32 = h_s.dtype == torch.float32
+    ws_bytes = int(_lib.lib().klg_fwd_f32_workspace_bytes(N, H, V) if f32 else _lib.lib().klg_fwd_workspace_bytes(N, V))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     given = count is not None
     cnt = count if given else torch.empty(1, dtype=torch.float32, device=dev)
     loss = torch.empty((), dtype=torch.float32, device=dev)
     lse = torch.empty(2, N, dtype=torch.float32, device=dev)
     row_kl = torch.empty(N, dtype=torch.float32, device=dev) if want_row_kl else None
-    call("klg_fwd", _ptr(h_s), _ptr(h_t), _ptr(weight), _ptr(m), N, H, V, 1.0 / float(temperature), int(given),
+    call("klg_fwd_f32" if f32 else "klg_fwd", _ptr(h_s), _ptr(h_t), _ptr(weight), _ptr(m), N, H, V, 1.0 / float(temperature), int(given),
          _ptr(cnt), _ptr(loss), _ptr(lse), _ptr(row_kl), _ptr(ws), ws_bytes, _stream(dev))
     return loss, lse, cnt, row_kl
 
@@ -166,6 +185,7 @@ def kl_fwd_bwd(h_s, h_t, weight, mask, temperature: float = 1.0, count: Optional
                grad: Optional[torch.Tensor] = None, need_dh: bool = True, need_dw: bool = True,
                want_row_kl: bool = False, workspace_bytes: Optional[int] = None):
     """Training step in one call: loss and gradients (for upstream gradient ``grad``, default 1).
+    bf16 inputs take the bf16 path; fp32 inputs (all three) the fp32-faithful split-bf16 path.
 
     Returns ``(loss, lse, count, row_kl, dH_s fp32 or None, dW fp32 or None)``.
     """
@@ -176,8 +196,10 @@ def kl_fwd_bwd(h_s, h_t, weight, mask, temperature: float = 1.0, count: Optional
     if h_t.shape != h_s.shape or weight.shape[1] != H or m.numel() != N:
         raise ValueError(f"shape mismatch: h_s {tuple(h_s.shape)} h_t {tuple(h_t.shape)} "
                          f"weight {tuple(weight.shape)} mask {tuple(m.shape)}")
+    f32 = h_s.dtype == torch.float32
     if workspace_bytes is None:
-        workspace_bytes = int(_lib.lib().klg_fwd_bwd_workspace_bytes(N, H, V))
+        workspace_bytes = int(_lib.lib().klg_fwd_bwd_f32_workspace_bytes(N, H, V) if f32
+                              else _lib.lib().klg_fwd_bwd_workspace_bytes(N, H, V))
     ws = torch.empty(int(workspace_bytes), dtype=torch.uint8, device=dev)
     given = count is not None
     cnt = count if given else torch.empty(1, dtype=torch.float32, device=dev)
@@ -189,7 +211,7 @@ def kl_fwd_bwd(h_s, h_t, weight, mask, temperature: float = 1.0, count: Optional
     g = None
     if grad is not None:
         g = grad.detach().to(device=dev, dtype=torch.float32).reshape(1).contiguous()
-    call("klg_fwd_bwd", _ptr(h_s), _ptr(h_t), _ptr(weight), _ptr(m), N, H, V, 1.0 / float(temperature), int(given),
+    call("klg_fwd_bwd_f32" if f32 else "klg_fwd_bwd", _ptr(h_s), _ptr(h_t), _ptr(weight), _ptr(m), N, H, V, 1.0 / float(temperature), int(given),
          _ptr(cnt), _ptr(g), _ptr(loss), _ptr(lse), _ptr(row_kl), _ptr(dh), _ptr(dw), _ptr(ws), int(workspace_bytes),
          _stream(dev))
     return loss, lse, cnt, row_kl, dh, dw
@@ -266,8 +288,11 @@ class KLGemmFn(torch.autograd.Function):
     (teacher rows, treated as detached like train.py:183), ``weight [V, H]``
     (lm_head, differentiable if it requires grad), ``mask [N]``, ``temperature``
     (float), ``count`` (optional ``[1]`` device tensor overriding sum(mask)).
-    bf16 or fp32 inputs; compute is bf16 on the tensor cores with fp32
-    accumulation and fp32 softmax arithmetic.
+    bf16 inputs compute in bf16 on the tensor cores with fp32 accumulation and fp32
+    softmax arithmetic; fp32 inputs (any of the three) take the fp32-faithful path: every
+    operand split into bf16 hi / lo planes, logits and gradients to ~2^-16 relative before
+    fp32 accumulation (the reference's CPU-runnable configuration and its fp32 teacher path,
+    train.py:188-191, are fp32).
 
     When a gradient will be needed the forward runs the whole training step
     (``klg_fwd_bwd``) and keeps dH_s / dW for an upstream gradient of 1 (O(N*H +
@@ -278,9 +303,7 @@ class KLGemmFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, h_s, h_t, weight, mask, temperature=1.0, count=None):
-        hs = to_compute_dtype(h_s)
-        ht = to_compute_dtype(h_t)
-        w = to_compute_dtype(weight)
+        hs, ht, w = prepare_inputs(h_s, h_t, weight)
         m = mask_u8(mask)
         need_dh, need_dw = ctx.needs_input_grad[0], ctx.needs_input_grad[2]
         ctx.dtypes = (h_s.dtype, weight.dtype)

@@ -295,3 +295,62 @@ def test_pass_pieces_equal_training_step():
     assert torch.equal(dh, dh2) and torch.equal(dw, dw2)
     torch.testing.assert_close(row_kl2, row_kl, rtol=1e-6, atol=1e-7)
     assert abs(float(loss2) - float(loss)) <= 1e-6 * abs(float(loss))
+
+
+# fp32-faithful path (fp32 inputs: split-bf16 planes on the tensor cores).  Tolerances against
+# the unrounded fp32 oracle, tighter than the bf16 path's: loss 1e-5 relative, gradients
+# 2e-3 normalised max error and cosine >= 0.999999.
+F32_LOSS_RTOL = 1e-5
+F32_GRAD_MAX_REL = 2e-3
+F32_GRAD_COS = 0.999999
+
+
+def _f32_close(loss, dh, dw, ref_loss, ref_dh, ref_dw, label):
+    rel = abs(loss - ref_loss) / abs(ref_loss)
+    assert rel <= F32_LOSS_RTOL, f"{label} loss {loss} vs {ref_loss} (rel {rel:.2e})"
+    for name, ours, ref in (("dH", dh, ref_dh), ("dW", dw, ref_dw)):
+        mr, cos = O.grad_metrics(ours, ref)
+        assert mr <= F32_GRAD_MAX_REL and cos >= F32_GRAD_COS, f"{label} {name} max_rel {mr:.2e} cos {cos:.8f}"
+    return rel
+
+
+def test_fp32_path_c1_full_size_beats_bf16_rounding():
+    """The CPU-runnable configuration (fp32, 1,024 x 576 x 49,152) through the fp32 path, against
+    the fp32 torch oracle on the unrounded inputs; its errors are below the bf16 path's."""
+    from orthrus_training_test_b200 import ops
+    p = O.make_problem("c1")
+    dev = torch.device("cuda:0")
+    ref_loss, ref_dh, ref_dw = run_oracle_torch_gpu(p["h_s"], p["h_t"], p["W"], p["mask"], p["T"], round_inputs=False)
+    hs, ht, w = (x.to(dev).float().contiguous() for x in (p["h_s"], p["h_t"], p["W"]))
+    loss, lse, cnt, row_kl, dh, dw = ops.kl_fwd_bwd(hs, ht, w, p["mask"].to(dev), p["T"], want_row_kl=True)
+    torch.cuda.synchronize()
+    f32_dh, f32_dw = dh.double().cpu().numpy(), dw.double().cpu().numpy()
+    rel = _f32_close(float(loss), f32_dh, f32_dw, ref_loss, ref_dh, ref_dw, "c1 fp32 path")
+    # the forward-only route (evaluation) on the same fp32 inputs
+    loss_f, lse_f, _, _ = ops.kl_forward(hs, ht, w, p["mask"].to(dev), p["T"])
+    assert abs(float(loss_f) - ref_loss) <= F32_LOSS_RTOL * abs(ref_loss)
+    torch.testing.assert_close(lse_f, lse, rtol=1e-6, atol=1e-5)
+    # the bf16 path on the same problem is less accurate on every measure
+    b = run_ours(p["h_s"], p["h_t"], p["W"], p["mask"], p["T"], path="fused")
+    assert rel <= abs(b["loss"] - ref_loss) / abs(ref_loss) or rel < 1e-6
+    for ours, bf, ref in ((f32_dh, b["dh"], ref_dh), (f32_dw, b["dw"], ref_dw)):
+        assert O.grad_metrics(ours, ref)[0] < O.grad_metrics(bf, ref)[0]
+
+
+@pytest.mark.parametrize("name", [n for n in golden_cases() if n.startswith("aligned")])
+def test_fp32_path_golden(name):
+    """The reference's own fp32 outputs (golden fixtures), through the autograd op with fp32
+    parameters -- the fp32 path -- at the fp32 tolerances."""
+    from orthrus_training_test_b200 import kl_gemm_loss
+    g = dict(np.load(GOLDEN / f"{name}.npz"))
+    dev = torch.device("cuda:0")
+    h_s = torch.tensor(g["h_s"], device=dev, requires_grad=True)
+    w = torch.tensor(g["weight"], device=dev, requires_grad=True)
+    loss = kl_gemm_loss(h_s, torch.tensor(g["h_t"], device=dev), w, torch.tensor(g["mask"], device=dev),
+                        float(g["temperature"]))
+    loss.backward()
+    B = g["anchor_positions"].shape[0]
+    dp, _, _ = O.kl_indices(B, g["anchor_positions"].shape[1], int(g["K"]))
+    ref_dh = g["grad_diff_hidden"][np.arange(B)[:, None], dp].reshape(h_s.shape)
+    _f32_close(float(loss), h_s.grad.double().cpu().numpy(), w.grad.double().cpu().numpy(), float(g["loss"]), ref_dh,
+               g["grad_weight"], name)
