@@ -77,6 +77,10 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="time budget of the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="row sharding: one dW all-reduce after the step instead of per-chunk buckets overlapped")
+    ap.add_argument("--sm-reserve", type=int, default=0,
+                    help="SMs left out of the persistent kernels' grids (room for NCCL beside them)")
     ap.add_argument("--sustained-seconds", type=float, default=2.5,
                     help="length of the extra back-to-back region reported as 'sustained' (0: skip)")
     return ap.parse_args()
@@ -614,6 +618,8 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     _lib.lib()
+    if args.sm_reserve:
+        ops.set_sm_reserve(args.sm_reserve)
 
     N, H, V, desc = CONFIGS[args.config]
     vocab_sharded = args.config == "c4" and world > 1
@@ -675,6 +681,13 @@ def main():
             dist.all_reduce(dw)
         return loss
 
+    # row sharding: dW is exchanged in vocab-chunk buckets, each all-reduced on a side stream as
+    # soon as its chunk's GEMM is done (overlapping the chunks still computing)
+    overlap = world > 1 and not vocab_sharded and not prenorm and not args.no_overlap
+    buckets = ops.chunk_bounds(N, H, V_work, fb_ws) if overlap else None
+    chunk_evs = ops.new_chunk_events(len(buckets)) if overlap else None
+    side = torch.cuda.Stream(device=dev) if overlap else None
+
     def step():
         if vocab_sharded:
             return step_vocab()
@@ -684,10 +697,20 @@ def main():
         cnt = ops.count_valid(m)
         if world > 1:
             dist.all_reduce(cnt)
-        loss, _, _, _, dh, dw = ops.kl_fwd_bwd(hs, ht, W, m, T, count=cnt, workspace_bytes=fb_ws)
+        loss, _, _, _, dh, dw = ops.kl_fwd_bwd(hs, ht, W, m, T, count=cnt, workspace_bytes=fb_ws,
+                                               chunk_events=chunk_evs)
         if world > 1:
+            works = []
+            if overlap:
+                with torch.cuda.stream(side):
+                    for (v0, v1), ev in zip(buckets, chunk_evs):
+                        side.wait_event(ev)
+                        works.append(dist.all_reduce(dw[v0:v1], async_op=True))
+            else:
+                dist.all_reduce(dw)
             dist.all_reduce(loss)
-            dist.all_reduce(dw)
+            for wk in works:
+                wk.wait()
         return loss
 
     for _ in range(args.warmup):
@@ -874,6 +897,9 @@ def main():
                        "vocab_per_gpu": V_work,
                        "temperature": T, "parallelism": (f"vocab-sharded x{world}" if vocab_sharded else
                                                          f"row-sharded dp{world}" if world > 1 else "single GPU"),
+                       "dw_exchange": ("per-chunk buckets overlapped on a side stream" if overlap else
+                                       "one all-reduce after the step" if world > 1 and not vocab_sharded else None),
+                       "sm_reserve": args.sm_reserve,
                        "l2": "flushed between steps (256 MiB write)"},
             "sustained": (dict(sustained, achieved_tflops=step_flops / (sustained["ms_per_step"] / 1e3) / 1e12,
                                frac_of_sustained=step_flops / (sustained["ms_per_step"] / 1e3) / 1e12 / peak_sust,

@@ -162,12 +162,27 @@ int klg_bwd(const void* h_s, const void* h_t, const void* w, const uint8_t* mask
 int64_t klg_fwd_bwd_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t vocab);
 
 /* dZ chunk width klg_fwd_bwd uses for a workspace of this size (-1 if too small). */
-int64_t klg_fwd_bwd_chunk_cols(int64_t n_rows, int64_t vocab, int64_t workspace_bytes);
+int64_t klg_fwd_bwd_chunk_cols(int64_t n_rows, int64_t hidden, int64_t vocab, int64_t workspace_bytes);
 
 int klg_fwd_bwd(const void* h_s, const void* h_t, const void* w, const uint8_t* mask, int64_t n_rows, int64_t hidden,
                 int64_t vocab, float inv_temp, int count_given, float* count, const float* grad, float* loss,
                 float* lse, float* row_kl, float* d_h_s, float* d_w, void* workspace, int64_t workspace_bytes,
                 void* stream);
+
+/* klg_fwd_bwd that also records chunk_events[c] (cudaEvent_t handles, one per vocab chunk:
+ * ceil(V / klg_fwd_bwd_chunk_cols(N, H, V, workspace_bytes)) of them) on the stream once chunk c's
+ * GEMM is enqueued: from then on dW rows [c * cols, min(V, (c + 1) * cols)) are final, so a
+ * row-sharded caller can all-reduce that slice on another stream while later chunks compute
+ * (the bucketed, overlapped data-parallel gradient exchange). */
+int klg_fwd_bwd_events(const void* h_s, const void* h_t, const void* w, const uint8_t* mask, int64_t n_rows,
+                       int64_t hidden, int64_t vocab, float inv_temp, int count_given, float* count, const float* grad,
+                       float* loss, float* lse, float* row_kl, float* d_h_s, float* d_w, void* workspace,
+                       int64_t workspace_bytes, void* const* chunk_events, int n_events, void* stream);
+
+/* Leaves n_sms SMs of every device out of the persistent kernels' grids (0 = use all; at most
+ * 64; process-wide, for launches planned after the call), so that communication kernels -- an
+ * NCCL all-reduce of finished dW slices -- can run beside them. */
+int klg_set_sm_reserve(int n_sms);
 
 /* ---------------------------------------------------------------- fp32 inputs
  * The CPU-runnable configuration and the reference's fp32 teacher path (train.py:188-191)

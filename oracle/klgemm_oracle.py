@@ -449,6 +449,39 @@ def sample_token_np(logits, temperature: float = 0.0):
     return None, e / e.sum(axis=-1, keepdims=True)
 
 
+def filtered_probs_np(logits, temperature: float, top_k: int = 0, top_p: float = 1.0):
+    """The distribution ``sample_token`` draws from with top-k / top-p (generate.py:55-75).
+
+    ``scaled = logits / T``; top-k removes every entry below the k-th largest scaled value
+    (generate.py:59-61: entries equal to it stay); top-p sorts the (top-k filtered) scaled
+    values in descending order, takes the cumulative softmax, and removes an entry when the
+    cumulative probability *before* it already exceeds ``top_p`` (generate.py:64-73: the
+    shift by one keeps the entry that crosses ``top_p``, and the first entry always stays).
+    Returns ``(probs, kept)``: ``softmax`` over the kept entries and the boolean mask.
+    """
+    z = np.atleast_2d(np.asarray(logits, dtype=np.float64)) / float(temperature)
+    n, V = z.shape
+    kept = np.ones_like(z, dtype=bool)
+    if top_k > 0:
+        kth = -np.sort(-z, axis=-1)[:, min(top_k, V) - 1]
+        kept &= z >= kth[:, None]
+    if top_p < 1.0:
+        zf = np.where(kept, z, -np.inf)
+        order = np.argsort(-zf, axis=-1, kind="stable")
+        zs = np.take_along_axis(zf, order, axis=-1)
+        e = np.exp(zs - zs[:, :1])
+        cum = np.cumsum(e / e.sum(axis=-1, keepdims=True), axis=-1)
+        remove = cum > top_p
+        remove[:, 1:] = remove[:, :-1].copy()
+        remove[:, 0] = False
+        rm = np.zeros_like(remove)
+        np.put_along_axis(rm, order, remove, axis=-1)
+        kept &= ~rm
+    zf = np.where(kept, z, -np.inf)
+    e = np.exp(zf - zf.max(axis=-1, keepdims=True))
+    return e / e.sum(axis=-1, keepdims=True), kept
+
+
 def sample_hash_np(seed: int, rows, cols) -> np.ndarray:
     """The 32-bit counter hash of (seed, row, column) the fused sampler draws from.
 
@@ -490,6 +523,15 @@ def sample_keys_np(z, temperature: float, seed: int) -> np.ndarray:
     n, v = z.shape
     x = sample_hash_np(seed, np.arange(n), np.arange(v))
     return z * (math.log2(math.e) / temperature) - np.log2(exp_variate_log2_np(x))
+
+
+def filtered_keys_np(z, temperature: float, seed: int, top_k: int = 0, top_p: float = 1.0) -> np.ndarray:
+    """Gumbel-max keys of the fused filtered sampler: ``sample_keys_np`` on the entries that
+    top-k / top-p keep, ``-inf`` elsewhere; the row argmax is a draw from
+    ``filtered_probs_np``."""
+    keys = sample_keys_np(z, temperature, seed)
+    _, kept = filtered_probs_np(z, temperature, top_k, top_p)
+    return np.where(kept, keys, -np.inf)
 
 
 def lm_head_sample_np(h, W, temperature: float = 0.0, seed: int = 0):

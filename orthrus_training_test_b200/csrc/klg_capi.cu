@@ -24,6 +24,7 @@
 
 #include "klg_kernels.cuh"
 #include "klg_attn.cuh"
+#include "klg_dzt.cuh"
 #include "klgemm.h"
 
 namespace {
@@ -164,7 +165,11 @@ struct NvtxRange {
   NvtxRange& operator=(const NvtxRange&) = delete;
 };
 
-int num_sms() {
+// SMs the persistent kernels leave free (klg_set_sm_reserve): room for communication kernels
+// (e.g. an NCCL all-reduce of finished gradient slices) to run beside them.
+std::atomic<int> g_sm_reserve{0};
+
+int device_sms() {
   static std::atomic<int> cache[64];   // per device, 0 = not read yet
   int dev = 0, n = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
@@ -172,6 +177,12 @@ int num_sms() {
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
   if (dev >= 0 && dev < 64) cache[dev].store(n, std::memory_order_relaxed);
   return n;
+}
+
+// SMs the kernels plan for: the device's, minus the reserve (kept even: CTA pairs).
+int num_sms() {
+  const int n = device_sms() - g_sm_reserve.load(std::memory_order_relaxed);
+  return n < 2 ? 2 : (n & ~1);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -340,6 +351,67 @@ int launch_dual_pair(const CUtensorMap& mhs, const CUtensorMap& mht, const CUten
   e = launch_k(k, dim3(2 * pairs), dim3(threads), smem, s, 2, mhs, mht, mw, mout, mout2, a);
   trace_post(slot, s, MODE == klg::MODE_DZ ? KLG_KIND_DZ : KLG_KIND_STATS);
   if (e != cudaSuccess) return cuda_fail(e, "launch dual_pair_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
+// The transposed dZ kernel (klg_dzt.cuh) is pass 2's dZ kernel on the bf16 path for H >= 1536:
+// its main loop moves 20 % fewer (streamed W) to 60 % fewer (resident W) bytes per MMA cycle,
+// but its epilogue -- per-column row constants and a cross-lane reduction of the KL cross
+// term -- takes ~10k cycles a tile, hidden only behind the 24+ k-blocks of MMA of a wide row
+// (measured, dZ time per training step: H = 2048: 21.2 ms vs 22.9 ms row-major; H = 1024:
+// 30.8 vs 27.2; H = 576: 1.82 vs 1.48).  KLG_DZT=0 / 1 forces either kernel (A/B timing).
+bool dzt_on(int64_t hidden) {
+  static const int force = [] {
+    const char* v = std::getenv("KLG_DZT");
+    return v ? (v[0] == '1' ? 1 : 0) : -1;
+  }();
+  return force >= 0 ? force == 1 : hidden >= 1536;
+}
+
+inline int64_t round8(int64_t x) { return (x + 7) & ~int64_t(7); }
+
+// Work split of a transposed dZ launch: units of g vocab pair tiles x rpu row tiles.  Picks
+// the split that fills the pairs in whole waves best, then the most row tiles per unit (the
+// reuse of a resident W tile), then the most vocab tiles per unit (fewer cross-term partial
+// rows), with the partial rows of the whole pass (n_chunks launches) kept within 64 MiB.
+struct DztPlan {
+  int g, rpu, n_vg, n_rg;
+};
+DztPlan plan_dzt(int n_vp, int n_rt, int pairs, int64_t n_rows, int n_chunks) {
+  DztPlan best{1, 1, n_vp, n_rt};
+  double best_eff = -1.0;
+  const int64_t cap_rows = std::max<int64_t>(2, (64ll << 20) / (4 * n_rows * std::max(1, n_chunks)));
+  for (int rpu = klg::DZT_RPU_MAX; rpu >= 1; rpu >>= 1) {
+    for (int g = 1; g <= 64; g <<= 1) {
+      const int n_vg = cdiv(n_vp, g), n_rg = cdiv(n_rt, rpu);
+      const bool last_g = g >= n_vp;
+      if (2ll * n_vg > cap_rows && !last_g) continue;
+      const long long units = (long long)n_vg * n_rg;
+      const long long waves = (units + pairs - 1) / pairs;
+      const double eff = (double)n_vp * n_rt / ((double)waves * pairs * g * rpu);
+      if (eff > best_eff + 0.02) {
+        best_eff = eff;
+        best = DztPlan{g, rpu, n_vg, n_rg};
+      }
+      if (last_g) break;
+    }
+  }
+  return best;
+}
+
+int launch_dzt(const CUtensorMap& mw, const CUtensorMap& mhs, const CUtensorMap& mht, const CUtensorMap& mout,
+               const klg::DztArgs& a, cudaStream_t s) {
+  const bool res = a.n_kb <= klg::DZT_MAX_KB;
+  auto k = res ? klg::dzt_pair_kernel<true> : klg::dzt_pair_kernel<false>;
+  const int smem = res ? klg::DztCfg<true>::SMEM : klg::DztCfg<false>::SMEM;
+  cudaError_t e = set_smem(k, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dzt_pair_kernel)");
+  const int pairs = a.n_units < num_sms() / 2 ? a.n_units : num_sms() / 2;
+  const int slot = trace_pre(s);
+  e = launch_k(k, dim3(2 * pairs), dim3(klg::DZT_THREADS), smem, s, 2, mw, mhs, mht, mout, a);
+  trace_post(slot, s, KLG_KIND_DZ);
+  if (e != cudaSuccess) return cuda_fail(e, "launch dzt_pair_kernel");
   ++g_launches;
   return KLG_OK;
 }
@@ -521,6 +593,12 @@ int klg_device_status(int* status, int reset) {
 
 long long klg_launch_count(void) { return g_launches.load(); }
 
+int klg_set_sm_reserve(int n_sms) {
+  if (n_sms < 0 || n_sms > 64) return fail(KLG_ERR_ARG, "SM reserve %d out of range [0, 64]", n_sms);
+  g_sm_reserve.store(n_sms, std::memory_order_relaxed);
+  return KLG_OK;
+}
+
 int klg_selftest_wait_timeout(void* stream) {
   cudaError_t e = launch_k(klg::wait_selftest_kernel, dim3(1), dim3(32), 0, (cudaStream_t)stream, 1);
   if (e != cudaSuccess) return cuda_fail(e, "launch wait_selftest_kernel");
@@ -645,7 +723,7 @@ int klg_fwd(const void* hs, const void* ht, const void* w, const uint8_t* mask, 
 int64_t klg_bwd_chunk_cols(int64_t n_rows, int64_t vocab, int64_t workspace_bytes) {
   if (n_rows < 1 || vocab < 1) return -1;
   const int64_t full = (int64_t)cdiv(vocab, 128) * 128;
-  int64_t c = (workspace_bytes - KLG_BWD_HEADER) / (n_rows * 2);
+  int64_t c = (workspace_bytes - KLG_BWD_HEADER) / (round8(n_rows) * 2);
   c = (c / 128) * 128;
   if (c > full) c = full;
   if (c < 128 || cdiv(vocab, c) > KLG_BWD_HEADER / 4) return -1;
@@ -659,12 +737,12 @@ int64_t klg_bwd_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t vocab) {
   // L2-resident chunk (measured at the 16k-row shape, pass 2 per step: 64 MiB chunks
   // 3.9 ms, 256 MiB 3.0 ms, 512 MiB 2.9 ms; wider chunks gained nothing more)
   const int64_t full = (int64_t)cdiv(vocab, 128) * 128;
-  int64_t cols = (512ll << 20) / (n_rows * 2);
+  int64_t cols = (512ll << 20) / (round8(n_rows) * 2);
   cols = (cols / 128) * 128;
   if (cols < 2048) cols = 2048;
   if (cols > full) cols = full;
   while (cdiv(vocab, cols) > KLG_BWD_HEADER / 4) cols += 128;
-  return KLG_BWD_HEADER + n_rows * cols * 2;
+  return KLG_BWD_HEADER + round8(n_rows) * cols * 2;
 }
 
 }  // extern "C"
@@ -677,15 +755,27 @@ namespace {
 // split (the fp32-faithful path): dZ is kept as two bf16 planes (hi and lo, row stride 2 * cols)
 // and each chunk's GEMM runs once per plane, both adding into the same fp32 dW and dH; dW's
 // K is then never split, so every dW element gets one addend per plane, in plane order.
+// chunk_events (optional, n_events of them): event c is recorded on the stream once chunk c's
+// GEMM is enqueued, i.e. when dW rows [c * cols, (c + 1) * cols) are final.
 int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask, const float* lse, const float* count,
               const float* grad, int64_t n_rows, int64_t hidden, int64_t vocab, float inv_temp, float* d_hs, float* d_w,
-              __nv_bfloat16* dz, int64_t cols, float* a_parts, int* n_ap_out, cudaStream_t s, bool split = false) {
+              __nv_bfloat16* dz, int64_t cols, float* a_parts, int* n_ap_out, cudaStream_t s, bool split = false,
+              void* const* chunk_events = nullptr, int n_events = 0) {
   int rc;
-  const int64_t ld_dz = split ? 2 * cols : cols;
+  const bool tr = !split && dzt_on(hidden);           // dZ^T [cols][ld_n] from the transposed kernel
+  const int64_t ld_n = round8(n_rows);
+  const int64_t ld_dz = split ? 2 * cols : cols;      // row-major dZ [n_rows][ld_dz]
   const int bn = gemm_bn(hidden);
   alignas(64) CUtensorMap mhs, mht, mw, mw_mn, mhs_mn;
-  if (!dual_maps(hs, ht, w, n_rows, hidden, vocab, dual_res_on(cdiv(hidden, klg::BK)), &mhs, &mht, &mw) ||
-      !make_map(&mw_mn, w, hidden, vocab, hidden, 32, klg::BK, CU_TENSOR_MAP_SWIZZLE_64B) ||
+  if (tr) {   // W as the A operand (128-row boxes), each CTA's 64-row halves of both views
+    if (!make_map(&mw, w, hidden, vocab, hidden, klg::BK, klg::BM) ||
+        !make_map(&mhs, hs, hidden, n_rows, hidden, klg::BK, klg::DZT_BN / 2) ||
+        !make_map(&mht, ht, hidden, n_rows, hidden, klg::BK, klg::DZT_BN / 2))
+      return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+  } else if (!dual_maps(hs, ht, w, n_rows, hidden, vocab, dual_res_on(cdiv(hidden, klg::BK)), &mhs, &mht, &mw)) {
+    return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+  }
+  if (!make_map(&mw_mn, w, hidden, vocab, hidden, 32, klg::BK, CU_TENSOR_MAP_SWIZZLE_64B) ||
       !make_map(&mhs_mn, hs, hidden, n_rows, hidden, 32, klg::BK, CU_TENSOR_MAP_SWIZZLE_64B))
     return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
   // fp32 outputs, accumulated by TMA reduce-add from zero
@@ -724,8 +814,56 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
   a.ld_dz = (int)ld_dz;
   a.a_parts = a_parts;
   int n_ap = 0;
+  const int n_chunks = cdiv(vocab, cols);
   for (int64_t v0 = 0, ci = 0; v0 < vocab; v0 += cols, ++ci) {
     const int64_t wv = (vocab - v0) < cols ? (vocab - v0) : cols;
+    if (tr) {
+      klg::DztArgs t{};
+      t.n_rows = (int)n_rows;
+      t.v_begin = (int)v0;
+      t.v_count = (int)wv;
+      t.n_vp = cdiv(wv, 256);
+      t.n_rt = cdiv(n_rows, klg::DZT_BN);
+      const DztPlan P = plan_dzt(t.n_vp, t.n_rt, num_sms() / 2, n_rows, n_chunks);
+      t.g = P.g;
+      t.rpu = P.rpu;
+      t.n_vg = P.n_vg;
+      t.n_units = P.n_vg * P.n_rg;
+      t.n_kb = cdiv(hidden, klg::BK);
+      t.scale_log2 = inv_temp * 1.4426950408889634f;
+      t.lse = lse;
+      t.mask = mask;
+      t.count = count;
+      t.grad = grad;
+      t.inv_temp = inv_temp;
+      t.a_parts = a_parts;
+      t.a_part_base = n_ap;
+      n_ap += 2 * P.n_vg;   // one cross-term partial row per vocab group and CTA of the pair
+      alignas(64) CUtensorMap mdzt_out;
+      if (!make_map(&mdzt_out, dz, n_rows, wv, ld_n, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+        return fail(KLG_ERR_CUDA, "tensor map (dz^T store)");
+      if ((rc = launch_dzt(mw, mhs, mht, mdzt_out, t, s))) return rc;
+      if (d_hs || d_w) {
+        // problem 0: dW chunk = dZ^T h_s (A = dZ^T, K-major); problem 1: dH += dZ W_chunk (A = dZ^T read MN-major)
+        klg::PairGemmArgs g{};
+        g.p[1] = gemm_problem(d_hs != nullptr, (int)n_rows, (int)hidden, (int)wv, bn, nullptr, (int)hidden, 1, 0,
+                              (int)v0, 1, 256, 0, 0);
+        const int kb_split = pick_dw_split((int)n_rows, (int)wv, (int)hidden, bn);
+        g.p[0] = gemm_problem(d_w != nullptr, (int)wv, (int)hidden, (int)n_rows, bn, nullptr, (int)hidden, 1, 0, 0, 0,
+                              256, kb_split, (int)v0);
+        g.n_tiles = g.p[0].n_tiles + g.p[1].n_tiles;
+        alignas(64) CUtensorMap mdzt_k, mdzt_mn;
+        if (!make_map(&mdzt_k, dz, n_rows, wv, ld_n, klg::BK, klg::BM) ||
+            !make_map(&mdzt_mn, dz, n_rows, wv, ld_n, 64, klg::BK))
+          return fail(KLG_ERR_CUDA, "tensor map (dz^T operand)");
+        if ((rc = launch_gemm_pair(bn, mdzt_k, mhs_mn, mdzt_mn, mw_mn, mdw, mdh, g, s))) return rc;
+      }
+      if (chunk_events && ci < n_events && chunk_events[ci]) {
+        cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(chunk_events[ci]), s);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord (chunk event)");
+      }
+      continue;
+    }
     a.v_begin = (int)v0;
     a.v_count = (int)wv;
     a.n_vt = cdiv(wv, klg::DZP_BN);
@@ -762,22 +900,38 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
         return fail(KLG_ERR_CUDA, "tensor map (dz operand)");
       if ((rc = launch_gemm_pair(bn, mdz_mn, mhs_mn, mdz_k, mw_mn, mdw, mdh, g, s))) return rc;
     }
+    if (chunk_events && ci < n_events && chunk_events[ci]) {
+      cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(chunk_events[ci]), s);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord (chunk event)");
+    }
   }
   if (n_ap_out) *n_ap_out = n_ap;
   return KLG_OK;
 }
 
-// Number of cross-term partial rows pass 2 writes for chunks of `cols` columns.
-int pass2_parts(int64_t n_rows, int64_t vocab, int64_t cols) {
+// Number of cross-term partial rows pass 2 writes for chunks of `cols` columns (transposed
+// kernel unless the dZ planes are split).
+int pass2_parts(int64_t n_rows, int64_t hidden, int64_t vocab, int64_t cols, bool split = false) {
   int n_ap = 0;
-  const int n_rt = cdiv(n_rows, 256);
+  const int n_chunks = cdiv(vocab, cols);
   for (int64_t v0 = 0; v0 < vocab; v0 += cols) {
     const int64_t wv = (vocab - v0) < cols ? (vocab - v0) : cols;
+    if (!split && dzt_on(hidden)) {
+      n_ap += 2 * plan_dzt(cdiv(wv, 256), cdiv(n_rows, klg::DZT_BN), num_sms() / 2, n_rows, n_chunks).n_vg;
+      continue;
+    }
     int vpu, n_uv;
-    plan_dual(n_rt, cdiv(wv, klg::DZP_BN), num_sms() / 2, vpu, n_uv, 8);
+    plan_dual(cdiv(n_rows, 256), cdiv(wv, klg::DZP_BN), num_sms() / 2, vpu, n_uv, 8);
     n_ap += klg::DZP_CSPLIT * n_uv;
   }
   return n_ap;
+}
+
+// Pass-1 partial records per row and view (lse_pair_kernel's units x column slices).
+int pass1_parts(int64_t n_rows, int64_t vocab) {
+  int vpu, n_uv;
+  plan_dual(2 * cdiv(n_rows, 256), cdiv(vocab, klg::LSE_BN), num_sms() / 2, vpu, n_uv);
+  return klg::LSE_CSPLIT * n_uv;
 }
 
 // Training-path workspace layout for a given total size: returns the dZ chunk width (or -1).
@@ -786,23 +940,23 @@ struct FwdBwdLayout {
   int n_lp, n_ap;
 };
 int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
-FwdBwdLayout fwd_bwd_layout_uncached(int64_t n_rows, int64_t vocab, int64_t workspace_bytes, int planes) {
+FwdBwdLayout fwd_bwd_layout_uncached(int64_t n_rows, int64_t hidden, int64_t vocab, int64_t workspace_bytes,
+                                     int planes) {
   FwdBwdLayout L{};
-  int vpu, n_uv;
-  plan_dual(2 * cdiv(n_rows, 256), cdiv(vocab, klg::LSE_BN), num_sms() / 2, vpu, n_uv);
-  L.n_lp = klg::LSE_CSPLIT * n_uv;
+  L.n_lp = pass1_parts(n_rows, vocab);
   L.lse_parts_off = KLG_BWD_HEADER;
   L.a_parts_off = align256(L.lse_parts_off + (int64_t)L.n_lp * 2 * 2 * n_rows * 4);
   L.cols = -1;
   const int64_t full = (int64_t)cdiv(vocab, 128) * 128;
   // widest chunk that could fit (the cross-term partials only shrink the room), then narrower
-  int64_t c = (workspace_bytes - L.a_parts_off) / (n_rows * 2 * planes);
+  const int64_t dz_rows = round8(n_rows);   // dZ^T rows are padded to 16 bytes
+  int64_t c = (workspace_bytes - L.a_parts_off) / (dz_rows * 2 * planes);
   c = std::min(full, (c / 128) * 128);
   for (; c >= 128; c -= 128) {
     if (cdiv(vocab, c) > KLG_BWD_HEADER / 4) break;
-    const int n_ap = pass2_parts(n_rows, vocab, c);
+    const int n_ap = pass2_parts(n_rows, hidden, vocab, c, planes == 2);
     const int64_t dz_off = align256(L.a_parts_off + (int64_t)n_ap * n_rows * 4);
-    if (dz_off + n_rows * c * 2 * planes <= workspace_bytes) {
+    if (dz_off + dz_rows * c * 2 * planes <= workspace_bytes) {
       L.cols = c;
       L.n_ap = n_ap;
       L.dz_off = dz_off;
@@ -813,16 +967,16 @@ FwdBwdLayout fwd_bwd_layout_uncached(int64_t n_rows, int64_t vocab, int64_t work
 }
 
 // Memoised: the layout is a pure function of the shape and workspace size.
-FwdBwdLayout fwd_bwd_layout(int64_t n_rows, int64_t vocab, int64_t workspace_bytes, int planes = 1) {
+FwdBwdLayout fwd_bwd_layout(int64_t n_rows, int64_t hidden, int64_t vocab, int64_t workspace_bytes, int planes = 1) {
   static std::mutex mu;
-  static std::map<std::tuple<int64_t, int64_t, int64_t, int, int>, FwdBwdLayout> memo;
-  const auto key = std::make_tuple(n_rows, vocab, workspace_bytes, num_sms(), planes);
+  static std::map<std::tuple<int64_t, int64_t, int64_t, int64_t, int, int>, FwdBwdLayout> memo;
+  const auto key = std::make_tuple(n_rows, hidden, vocab, workspace_bytes, num_sms(), planes);
   {
     std::lock_guard<std::mutex> lk(mu);
     auto it = memo.find(key);
     if (it != memo.end()) return it->second;
   }
-  const FwdBwdLayout L = fwd_bwd_layout_uncached(n_rows, vocab, workspace_bytes, planes);
+  const FwdBwdLayout L = fwd_bwd_layout_uncached(n_rows, hidden, vocab, workspace_bytes, planes);
   std::lock_guard<std::mutex> lk(mu);
   if (memo.size() > 256) memo.clear();
   memo[key] = L;
@@ -895,9 +1049,9 @@ namespace {
 int64_t fwd_bwd_ws(int64_t n_rows, int64_t hidden, int64_t vocab, int planes) {
   if (n_rows < 1 || vocab < 1) return -1;
   const int64_t dz_bytes = klg_bwd_workspace_bytes(n_rows, hidden, vocab) - KLG_BWD_HEADER;
-  const int64_t cols = dz_bytes / (n_rows * 2);
-  FwdBwdLayout L = fwd_bwd_layout(n_rows, vocab, INT64_MAX / 4);
-  const int n_ap = pass2_parts(n_rows, vocab, cols);
+  const int64_t cols = dz_bytes / (round8(n_rows) * 2);
+  FwdBwdLayout L = fwd_bwd_layout(n_rows, hidden, vocab, INT64_MAX / 4);
+  const int n_ap = pass2_parts(n_rows, hidden, vocab, cols, planes == 2);
   return align256(L.a_parts_off + (int64_t)n_ap * n_rows * 4) + dz_bytes * planes;
 }
 
@@ -905,9 +1059,9 @@ int64_t fwd_bwd_ws(int64_t n_rows, int64_t hidden, int64_t vocab, int planes) {
 int fwd_bwd_core(const void* hs, const void* ht, const void* w, const uint8_t* mask, int64_t n_rows, int64_t hidden,
                  int64_t vocab, float inv_temp, int count_given, float* count, const float* grad, float* loss,
                  float* lse, float* row_kl, float* d_hs, float* d_w, void* workspace, int64_t workspace_bytes,
-                 cudaStream_t s, int planes) {
+                 cudaStream_t s, int planes, void* const* chunk_events = nullptr, int n_events = 0) {
   int rc;
-  const FwdBwdLayout L = fwd_bwd_layout(n_rows, vocab, workspace_bytes, planes);
+  const FwdBwdLayout L = fwd_bwd_layout(n_rows, hidden, vocab, workspace_bytes, planes);
   if (L.cols < 0)
     return fail(KLG_ERR_WORKSPACE, "workspace of %lld bytes too small (see the *_workspace_bytes functions)",
                 (long long)workspace_bytes);
@@ -922,7 +1076,7 @@ int fwd_bwd_core(const void* hs, const void* ht, const void* w, const uint8_t* m
   int n_ap = 0;
   __nv_bfloat16* dz = reinterpret_cast<__nv_bfloat16*>(ws + L.dz_off);
   if ((rc = run_pass2(hs, ht, w, mask, lse, count, grad, n_rows, hidden, vocab, inv_temp, d_hs, d_w, dz,
-                      L.cols, a_parts, &n_ap, s, planes == 2)))
+                      L.cols, a_parts, &n_ap, s, planes == 2, chunk_events, n_events)))
     return rc;
   if (n_ap != L.n_ap) return fail(KLG_ERR_ARG, "internal plan mismatch (cross-term partials)");
   // per-row KL in 256-row blocks (block sums reuse the pass-1 partial area), then the loss
@@ -1001,9 +1155,9 @@ int64_t klg_fwd_bwd_workspace_bytes(int64_t n_rows, int64_t hidden, int64_t voca
   return fwd_bwd_ws(n_rows, hidden, vocab, 1);
 }
 
-int64_t klg_fwd_bwd_chunk_cols(int64_t n_rows, int64_t vocab, int64_t workspace_bytes) {
-  if (n_rows < 1 || vocab < 1) return -1;
-  return fwd_bwd_layout(n_rows, vocab, workspace_bytes).cols;
+int64_t klg_fwd_bwd_chunk_cols(int64_t n_rows, int64_t hidden, int64_t vocab, int64_t workspace_bytes) {
+  if (n_rows < 1 || vocab < 1 || hidden < 8) return -1;
+  return fwd_bwd_layout(n_rows, hidden, vocab, workspace_bytes).cols;
 }
 
 int klg_fwd_bwd(const void* hs, const void* ht, const void* w, const uint8_t* mask, int64_t n_rows, int64_t hidden,
@@ -1019,6 +1173,26 @@ int klg_fwd_bwd(const void* hs, const void* ht, const void* w, const uint8_t* ma
   NvtxRange nvtx_range("klg_fwd_bwd");
   return fwd_bwd_core(hs, ht, w, mask, n_rows, hidden, vocab, inv_temp, count_given, count, grad, loss, lse, row_kl,
                       d_hs, d_w, workspace, workspace_bytes, (cudaStream_t)stream, 1);
+}
+
+int klg_fwd_bwd_events(const void* hs, const void* ht, const void* w, const uint8_t* mask, int64_t n_rows,
+                       int64_t hidden, int64_t vocab, float inv_temp, int count_given, float* count, const float* grad,
+                       float* loss, float* lse, float* row_kl, float* d_hs, float* d_w, void* workspace,
+                       int64_t workspace_bytes, void* const* chunk_events, int n_events, void* stream) {
+  int rc = check_problem(hs, ht, w, n_rows, hidden, vocab, inv_temp);
+  if (rc) return rc;
+  if (!mask || !count || !loss || !lse) return fail(KLG_ERR_ARG, "null mask/count/loss/lse");
+  if ((d_hs && !aligned16(d_hs)) || (d_w && !aligned16(d_w))) return fail(KLG_ERR_ALIGN, "outputs must be 16-byte aligned");
+  if (!workspace || !aligned16(workspace)) return fail(KLG_ERR_WORKSPACE, "null or misaligned workspace");
+  if (n_events < 0 || (n_events > 0 && !chunk_events)) return fail(KLG_ERR_ARG, "bad chunk event array");
+  if ((rc = bind_device(hs))) return rc;
+  const int64_t cols = fwd_bwd_layout(n_rows, hidden, vocab, workspace_bytes).cols;
+  if (cols > 0 && n_events < cdiv(vocab, cols))
+    return fail(KLG_ERR_ARG, "%d chunk events for %d chunks (klg_fwd_bwd_chunk_cols gives the chunk width)", n_events,
+                cdiv(vocab, cols));
+  NvtxRange nvtx_range("klg_fwd_bwd_events");
+  return fwd_bwd_core(hs, ht, w, mask, n_rows, hidden, vocab, inv_temp, count_given, count, grad, loss, lse, row_kl,
+                      d_hs, d_w, workspace, workspace_bytes, (cudaStream_t)stream, 1, chunk_events, n_events);
 }
 
 // ---------------------------------------------------------------- fp32-faithful path
@@ -1094,8 +1268,7 @@ int klg_fwd_f32(const float* hs, const float* ht, const float* w, const uint8_t*
 // ---------------------------------------------------------------- training step in pieces (vocab sharding)
 int64_t klg_lse_workspace_bytes(int64_t n_rows, int64_t vocab) {
   if (n_rows < 1 || vocab < 1 || n_rows > (1ll << 30) || vocab > (1ll << 30)) return -1;
-  const FwdBwdLayout L = fwd_bwd_layout(n_rows, vocab, INT64_MAX / 4);
-  return (int64_t)L.n_lp * 2 * 2 * n_rows * 4;
+  return (int64_t)pass1_parts(n_rows, vocab) * 2 * 2 * n_rows * 4;
 }
 
 int klg_lse_record(const void* hs, const void* ht, const void* w, int64_t n_rows, int64_t hidden, int64_t vocab,
@@ -1105,12 +1278,12 @@ int klg_lse_record(const void* hs, const void* ht, const void* w, int64_t n_rows
   if (!rec || !aligned16(rec)) return fail(KLG_ERR_ARG, "rec must be non-null and 16-byte aligned");
   if (!workspace || !aligned16(workspace)) return fail(KLG_ERR_WORKSPACE, "null or misaligned workspace");
   if ((rc = bind_device(hs))) return rc;   // the plan depends on the SM count of hs's device
-  const FwdBwdLayout L = fwd_bwd_layout(n_rows, vocab, INT64_MAX / 4);
-  const int64_t need = (int64_t)L.n_lp * 2 * 2 * n_rows * 4;
+  const int n_lp = pass1_parts(n_rows, vocab);
+  const int64_t need = (int64_t)n_lp * 2 * 2 * n_rows * 4;
   if (workspace_bytes < need)
     return fail(KLG_ERR_WORKSPACE, "pass-1 workspace needs %lld bytes (see klg_lse_workspace_bytes)", (long long)need);
   NvtxRange nvtx_range("klg_lse_record");
-  return run_pass1(hs, ht, w, n_rows, hidden, vocab, inv_temp, static_cast<float*>(workspace), L.n_lp, nullptr, rec,
+  return run_pass1(hs, ht, w, n_rows, hidden, vocab, inv_temp, static_cast<float*>(workspace), n_lp, nullptr, rec,
                    (cudaStream_t)stream);
 }
 
@@ -1141,7 +1314,7 @@ int klg_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
   if ((d_hs && !aligned16(d_hs)) || (d_w && !aligned16(d_w))) return fail(KLG_ERR_ALIGN, "outputs must be 16-byte aligned");
   if (!workspace || !aligned16(workspace)) return fail(KLG_ERR_WORKSPACE, "null or misaligned workspace");
   if ((rc = bind_device(hs))) return rc;   // the layout depends on the SM count of hs's device
-  const FwdBwdLayout L = fwd_bwd_layout(n_rows, vocab, workspace_bytes);
+  const FwdBwdLayout L = fwd_bwd_layout(n_rows, hidden, vocab, workspace_bytes);
   if (L.cols < 0)
     return fail(KLG_ERR_WORKSPACE, "workspace of %lld bytes too small (see klg_pass2_workspace_bytes)",
                 (long long)workspace_bytes);

@@ -181,11 +181,41 @@ def kl_backward(h_s, h_t, weight, mask, lse, count, grad: Optional[torch.Tensor]
     return dh, dw
 
 
+def chunk_bounds(n_rows: int, hidden: int, vocab: int, workspace_bytes: Optional[int] = None):
+    """``[(v0, v1), ...]``: the vocab chunks of the training step's pass 2 (bf16 path) for this
+    workspace size (default: the recommended one); dW rows ``[v0, v1)`` are final once that
+    chunk's GEMM has run."""
+    L = _lib.lib()
+    if workspace_bytes is None:
+        workspace_bytes = int(L.klg_fwd_bwd_workspace_bytes(n_rows, hidden, vocab))
+    cols = int(L.klg_fwd_bwd_chunk_cols(n_rows, hidden, vocab, int(workspace_bytes)))
+    if cols <= 0:
+        raise ValueError(f"workspace of {workspace_bytes} bytes is too small")
+    return [(v0, min(vocab, v0 + cols)) for v0 in range(0, vocab, cols)]
+
+
+def new_chunk_events(n: int):
+    """``n`` CUDA events (created, so that their handles exist) for ``kl_fwd_bwd(chunk_events=)``."""
+    evs = [torch.cuda.Event() for _ in range(n)]
+    for e in evs:
+        e.record()
+    return evs
+
+
+def set_sm_reserve(n_sms: int) -> None:
+    """Leave ``n_sms`` SMs of each device out of the persistent kernels' grids (room for NCCL)."""
+    call("klg_set_sm_reserve", int(n_sms))
+
+
 def kl_fwd_bwd(h_s, h_t, weight, mask, temperature: float = 1.0, count: Optional[torch.Tensor] = None,
                grad: Optional[torch.Tensor] = None, need_dh: bool = True, need_dw: bool = True,
-               want_row_kl: bool = False, workspace_bytes: Optional[int] = None):
+               want_row_kl: bool = False, workspace_bytes: Optional[int] = None, chunk_events=None):
     """Training step in one call: loss and gradients (for upstream gradient ``grad``, default 1).
     bf16 inputs take the bf16 path; fp32 inputs (all three) the fp32-faithful split-bf16 path.
+
+    ``chunk_events`` (bf16 path): one ``torch.cuda.Event`` per vocab chunk of
+    :func:`chunk_bounds`; event c is recorded on the current stream once chunk c's dW rows
+    are final, so another stream can start exchanging them.
 
     Returns ``(loss, lse, count, row_kl, dH_s fp32 or None, dW fp32 or None)``.
     """
@@ -211,9 +241,15 @@ def kl_fwd_bwd(h_s, h_t, weight, mask, temperature: float = 1.0, count: Optional
     g = None
     if grad is not None:
         g = grad.detach().to(device=dev, dtype=torch.float32).reshape(1).contiguous()
-    call("klg_fwd_bwd_f32" if f32 else "klg_fwd_bwd", _ptr(h_s), _ptr(h_t), _ptr(weight), _ptr(m), N, H, V, 1.0 / float(temperature), int(given),
-         _ptr(cnt), _ptr(g), _ptr(loss), _ptr(lse), _ptr(row_kl), _ptr(dh), _ptr(dw), _ptr(ws), int(workspace_bytes),
-         _stream(dev))
+    args = (_ptr(h_s), _ptr(h_t), _ptr(weight), _ptr(m), N, H, V, 1.0 / float(temperature), int(given), _ptr(cnt),
+            _ptr(g), _ptr(loss), _ptr(lse), _ptr(row_kl), _ptr(dh), _ptr(dw), _ptr(ws), int(workspace_bytes))
+    if chunk_events is not None:
+        if f32:
+            raise ValueError("chunk_events is for the bf16 path")
+        handles = (ctypes.c_void_p * len(chunk_events))(*[e.cuda_event for e in chunk_events])
+        call("klg_fwd_bwd_events", *args, handles, len(chunk_events), _stream(dev))
+    else:
+        call("klg_fwd_bwd_f32" if f32 else "klg_fwd_bwd", *args, _stream(dev))
     return loss, lse, cnt, row_kl, dh, dw
 
 

@@ -7,7 +7,8 @@ Row sharding (``row_sharded_kl_loss``): each rank owns different token rows
 and a full replica of the lm_head.  Rows are independent, so the only
 exchanges are the global valid-row count (normaliser, one float), the loss
 (one float) and the lm_head gradient dW ``[V, H]`` (all-reduce, the
-data-parallel gradient exchange).  dH stays local.
+data-parallel gradient exchange, bucketed by vocab chunk and overlapped with
+the chunks still computing).  dH stays local.
 
 Vocab sharding (``vocab_sharded_kl_loss``): each rank owns all rows and one
 contiguous slice of the lm_head's rows (vocab entries).  When gradients are
@@ -72,12 +73,21 @@ class CudaEngine:
         return kl_backward(h_s, h_t, w, mask, lse, count, grad=grad, temperature=temperature, need_dh=need_dh,
                            need_dw=need_dw)
 
-    def forward_backward(self, h_s, h_t, w, mask, temperature, count, need_dh, need_dw):
+    def forward_backward(self, h_s, h_t, w, mask, temperature, count, need_dh, need_dw, chunk_events=None):
         """Training step with a given normaliser: ``(loss, dH, dW)`` for upstream gradient 1."""
         from .ops import kl_fwd_bwd
         loss, _, _, _, dh, dw = kl_fwd_bwd(h_s, h_t, w, mask, temperature, count=count, need_dh=need_dh,
-                                           need_dw=need_dw)
+                                           need_dw=need_dw, chunk_events=chunk_events)
         return loss, dh, dw
+
+    def dw_buckets(self, h_s, w):
+        """Vocab chunks whose dW rows become final one after another during the training step
+        (bf16 path), with one fresh event per chunk; None when the step cannot report them."""
+        from .ops import chunk_bounds, new_chunk_events
+        if h_s.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+            return None
+        bounds = chunk_bounds(h_s.shape[0], h_s.shape[1], w.shape[0])
+        return bounds, new_chunk_events(len(bounds))
 
     # the training step in pieces (vocab sharding exchanges data between them)
     acc_dtype = torch.float32
@@ -117,24 +127,41 @@ class _RowShardedFn(torch.autograd.Function):
         need_dh, need_dw = ctx.needs_input_grad[0], ctx.needs_input_grad[2]
         ctx.group = group
         ctx.dtypes = (h_s.dtype, weight.dtype)
+        works = []
         if need_dh or need_dw:
-            # sum_local valid*KL / global count, and its gradients for upstream gradient 1
-            loss, dh, dw = eng.forward_backward(hs, ht, w, m, temperature, count, need_dh, need_dw)
+            # sum_local valid*KL / global count, and its gradients for upstream gradient 1.  The
+            # data-parallel dW exchange is issued here, bucketed by vocab chunk: each chunk's dW
+            # rows are all-reduced on a side stream as soon as its GEMM is done, overlapping the
+            # chunks still computing.  (The upstream gradient is the same on every rank -- it is
+            # the gradient of the same global loss -- so reducing before scaling is the same sum.)
+            buckets = eng.dw_buckets(hs, w) if (need_dw and hasattr(eng, "dw_buckets")) else None
+            if buckets is not None:
+                bounds, events = buckets
+                loss, dh, dw = eng.forward_backward(hs, ht, w, m, temperature, count, need_dh, need_dw,
+                                                    chunk_events=events)
+                side = torch.cuda.Stream(device=hs.device)
+                with torch.cuda.stream(side):
+                    for (v0, v1), ev in zip(bounds, events):
+                        side.wait_event(ev)
+                        works.append(dist.all_reduce(dw[v0:v1], op=dist.ReduceOp.SUM, group=group, async_op=True))
+            else:
+                loss, dh, dw = eng.forward_backward(hs, ht, w, m, temperature, count, need_dh, need_dw)
+                if dw is not None:
+                    dist.all_reduce(dw, op=dist.ReduceOp.SUM, group=group)
             ctx.save_for_backward(dh, dw)
         else:
             loss, _ = eng.forward(hs, ht, w, m, temperature, count)
         loss = loss.reshape(1).clone()
         dist.all_reduce(loss, op=dist.ReduceOp.SUM, group=group)
+        for wk in works:
+            wk.wait()
         return loss.reshape(())
 
     @staticmethod
     def backward(ctx, g):
-        dh, dw = ctx.saved_tensors
-        if dw is not None:
-            dw = dw * g
-            dist.all_reduce(dw, op=dist.ReduceOp.SUM, group=ctx.group)  # data-parallel dW exchange
+        dh, dw = ctx.saved_tensors          # dW already summed over ranks
         return ((dh * g).to(ctx.dtypes[0]) if dh is not None else None, None,
-                dw.to(ctx.dtypes[1]) if dw is not None else None, None, None, None, None)
+                (dw * g).to(ctx.dtypes[1]) if dw is not None else None, None, None, None, None)
 
 
 def row_sharded_kl_loss(h_s: torch.Tensor, h_t: torch.Tensor, weight: torch.Tensor, mask: torch.Tensor,

@@ -41,6 +41,11 @@ def main():
     assert probs is None
     _, p07 = generate.sample_token(z.clone(), 0.7)
     arrays.update(h=h.numpy(), weight=W.numpy(), greedy=tok.numpy(), probs_t07=p07.numpy())
+    # top-k / top-p (generate.py:59-73): the reference's filtered probabilities
+    for name, (T, k, p) in {"k20": (0.7, 20, 1.0), "p09": (1.0, 0, 0.9), "k50p08": (0.8, 50, 0.8),
+                            "p05": (0.5, 0, 0.5), "k1": (1.0, 1, 1.0)}.items():
+        _, pf = generate.sample_token(z.clone(), T, k, p)
+        arrays[f"probs_{name}"] = pf.numpy()
 
     # small integer rows and duplicated weight rows: exact ties, where argmax keeps the first
     Ni, Hi, Vi = 16, 32, 40

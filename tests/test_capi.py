@@ -75,8 +75,10 @@ def test_argument_validation_codes():
 HDR = 4096  # tile counters ahead of the dZ chunk
 
 
-@pytest.mark.parametrize("n,v,ws,expect", [(16384, 49152, HDR + 16384 * 8192 * 2, 8192), (1, 1, HDR + 256, 128),
-                                           (300, 1500, HDR + 300 * 256, 128), (100, 50000, HDR + 100 * 2 * 200, 128),
+# dZ chunk rows are padded to a multiple of 8 (16-byte rows of the transposed layout)
+@pytest.mark.parametrize("n,v,ws,expect", [(16384, 49152, HDR + 16384 * 8192 * 2, 8192), (1, 1, HDR + 8 * 256, 128),
+                                           (1, 1, HDR + 256, -1),
+                                           (300, 1500, HDR + 304 * 256, 128), (100, 50000, HDR + 104 * 2 * 200, 128),
                                            (100, 50000, 100, -1), (10, 1000, 1 << 30, 1024),
                                            (10, 128 * 2000, HDR + 10 * 256, -1)])  # > 1024 chunks
 def test_backward_chunk_plan(n, v, ws, expect):

@@ -118,10 +118,15 @@ def test_compute_kl_loss_with_norm_weight_equals_prenormed_call():
     d1 = diff.clone().requires_grad_(True)
     l1 = compute_kl_loss(d1, ar, head, anchors, K, tgt, 0, norm_weight=gam)
     l1.backward()
-    # the same through an explicit norm: fp32 rows normed by the kernel, then the plain op
+    # the same through an explicit norm: the kernel's bf16 normed rows, then the plain op on bf16
+    # operands (the fused norm's loss runs on bf16 rows and the bf16-rounded head; fp32 operands
+    # would take the fp32-faithful path instead)
     d2 = diff.clone().requires_grad_(True)
-    y = ops.rmsnorm_rows(d2.reshape(-1, H), gam)[0].float().reshape(d2.shape)
-    ya = ops.rmsnorm_rows(ar.reshape(-1, H), gam)[0].float().reshape(ar.shape)
-    l2 = compute_kl_loss(y, ya, head, anchors, K, tgt, 0)
+    y = ops.rmsnorm_rows(d2.reshape(-1, H), gam)[0].reshape(d2.shape)
+    ya = ops.rmsnorm_rows(ar.reshape(-1, H), gam)[0].reshape(ar.shape)
+    head16 = torch.nn.Linear(H, V, bias=False).to(_dev(), torch.bfloat16)
+    with torch.no_grad():
+        head16.weight.copy_(head.weight)
+    l2 = compute_kl_loss(y, ya, head16, anchors, K, tgt, 0)
     assert abs(float(l1) - float(l2)) <= 1e-6 * abs(float(l2))
     assert d1.grad is not None and torch.isfinite(d1.grad).all()
