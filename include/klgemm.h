@@ -237,11 +237,30 @@ int klg_kl_loss(const float* lse, const float* cross, const uint8_t* mask, int64
  * Gumbel-max rule with a counter-based generator (seed, row, column) -- distributed like
  * torch.multinomial over the same probabilities, not the same stream.  Outputs: tokens
  * [N] int32, logit [N] = z of the chosen token, lse [N] = log sum exp(z * inv_temp), so
- * p(token) = exp(logit * inv_temp - lse).  top-k / top-p filtering is not fused. */
+ * p(token) = exp(logit * inv_temp - lse).  top-k / top-p: klg_lm_head_sample_filtered. */
 int64_t klg_lm_head_sample_workspace_bytes(int64_t n_rows, int64_t vocab);
 int klg_lm_head_sample(const void* h, const void* w, int64_t n_rows, int64_t hidden, int64_t vocab, float inv_temp,
                        int sample, uint64_t seed, int32_t* tokens, float* logit, float* lse, void* workspace,
                        int64_t workspace_bytes, void* stream);
+
+/* Token selection with top-k / top-p filtering (generate.py:55-75) at temperature 1 / inv_temp,
+ * still without [N, V] logits.  Two sweeps over W: the first gives each row's log-sum-exp and
+ * its 32-column chunk maxima, from which a per-row threshold follows that no surviving logit is
+ * below (the k-th largest chunk maximum; the chunk maximum at which the chunk maxima's own
+ * softmax mass passes top_p); the second collects every logit at or above it (at most `cap`
+ * per row).  A per-row kernel then applies the reference's rules exactly to those candidates
+ * -- top-k keeps values >= the k-th largest, top-p keeps an entry while the mass strictly above
+ * it is <= top_p (renormalised over the top-k survivors) -- and draws the Gumbel-max token
+ * among the survivors with the unfiltered sampler's keys.  lse = log sum exp(z inv_temp) over
+ * the survivors, so p(token) = exp(logit inv_temp - lse) is the reference's renormalised
+ * probability.  *overflow (device int) is set when a row had more than `cap` candidates (its
+ * token is then -1; call again with a larger cap, at most vocab).  top_k = 0 and top_p = 1
+ * mean no filter.  Greedy selection has no filter (generate.py:52-53): use klg_lm_head_sample. */
+int64_t klg_lm_head_sample_filtered_workspace_bytes(int64_t n_rows, int64_t vocab, int64_t cap);
+int klg_lm_head_sample_filtered(const void* h, const void* w, int64_t n_rows, int64_t hidden, int64_t vocab,
+                                float inv_temp, int top_k, float top_p, uint64_t seed, int64_t cap, int32_t* tokens,
+                                float* logit, float* lse, int* overflow, void* workspace, int64_t workspace_bytes,
+                                void* stream);
 
 /* ---------------------------------------------------------------- row selection
  * The gathers of compute_kl_loss (train.py:124-139, 156-164) in one kernel:

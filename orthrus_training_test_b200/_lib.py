@@ -45,6 +45,10 @@ SIGNATURES = {
                                      c_void_p]),
     "klg_lm_head_sample": (c_int, [c_void_p, c_void_p, c_longlong, c_longlong, c_longlong, c_float, c_int, c_ulonglong,
                                    c_void_p, c_void_p, c_void_p, c_void_p, c_longlong, c_void_p]),
+    "klg_lm_head_sample_filtered_workspace_bytes": (c_longlong, [c_longlong, c_longlong, c_longlong]),
+    "klg_lm_head_sample_filtered": (c_int, [c_void_p, c_void_p, c_longlong, c_longlong, c_longlong, c_float, c_int,
+                                            c_float, c_ulonglong, c_longlong, c_void_p, c_void_p, c_void_p, c_void_p,
+                                            c_void_p, c_longlong, c_void_p]),
     "klg_num_partials": (c_int, [c_int64, c_int64, POINTER(c_int)]),
     "klg_fwd_stats": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_float, c_void_p, c_int,
                               c_void_p]),

@@ -1438,6 +1438,119 @@ int klg_lm_head_sample(const void* h, const void* w, int64_t n_rows, int64_t hid
   return KLG_OK;
 }
 
+// ---------------------------------------------------------------- filtered sampling (top-k / top-p)
+namespace {
+struct FilterLayout {
+  int64_t rec, cmax, thr, lse, tok, lgt, cnt, cz, ci, total;
+};
+FilterLayout filter_layout(int64_t n_rows, int64_t vocab, int64_t cap, int n_part) {
+  FilterLayout L{};
+  const int64_t n_ck = cdiv(vocab, 32);
+  L.rec = 0;
+  L.cmax = align256(L.rec + sample_workspace(n_rows, n_part));
+  L.thr = align256(L.cmax + n_rows * n_ck * 4);
+  L.lse = align256(L.thr + n_rows * 4);
+  L.tok = align256(L.lse + n_rows * 4);
+  L.lgt = align256(L.tok + n_rows * 4);
+  L.cnt = align256(L.lgt + n_rows * 4);
+  L.cz = align256(L.cnt + n_rows * 4);
+  L.ci = align256(L.cz + n_rows * cap * 4);
+  L.total = align256(L.ci + n_rows * cap * 4);
+  return L;
+}
+}  // namespace
+
+int64_t klg_lm_head_sample_filtered_workspace_bytes(int64_t n_rows, int64_t vocab, int64_t cap) {
+  if (n_rows < 1 || vocab < 1 || n_rows > (1ll << 24) || vocab > (1ll << 24) || cap < 1 || cap > vocab) return -1;
+  klg::LseArgs la{};
+  return filter_layout(n_rows, vocab, cap, sample_plan(n_rows, vocab, la)).total;
+}
+
+int klg_lm_head_sample_filtered(const void* h, const void* w, int64_t n_rows, int64_t hidden, int64_t vocab,
+                                float inv_temp, int top_k, float top_p, uint64_t seed, int64_t cap, int32_t* tokens,
+                                float* logit, float* lse, int* overflow, void* workspace, int64_t workspace_bytes,
+                                void* stream) {
+  int rc = check_problem(h, h, w, n_rows, hidden, vocab, inv_temp);
+  if (rc) return rc;
+  if (!tokens || !logit || !lse || !overflow) return fail(KLG_ERR_ARG, "null output pointer");
+  if (top_k < 0 || !(top_p > 0.f) || top_p > 1.f) return fail(KLG_ERR_ARG, "top_k must be >= 0 and top_p in (0, 1]");
+  if (n_rows > (1ll << 24) || vocab > (1ll << 24) || cap < 1 || cap > vocab)
+    return fail(KLG_ERR_ARG, "bad filtered-sampling shape N=%lld V=%lld cap=%lld", (long long)n_rows, (long long)vocab,
+                (long long)cap);
+  if (!workspace || !aligned16(workspace)) return fail(KLG_ERR_WORKSPACE, "null or misaligned workspace");
+  if ((rc = bind_device(h))) return rc;
+  klg::LseArgs la{};
+  const int n_part = sample_plan(n_rows, vocab, la);
+  const FilterLayout F = filter_layout(n_rows, vocab, cap, n_part);
+  if (workspace_bytes < F.total)
+    return fail(KLG_ERR_WORKSPACE, "filtered-sampling workspace needs %lld bytes", (long long)F.total);
+  NvtxRange nvtx_range("klg_lm_head_sample_filtered");
+  cudaStream_t s = (cudaStream_t)stream;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* rec = reinterpret_cast<float*>(ws + F.rec);
+  float* cmax = reinterpret_cast<float*>(ws + F.cmax);
+  float* thr = reinterpret_cast<float*>(ws + F.thr);
+  float* lse_all = reinterpret_cast<float*>(ws + F.lse);
+  int32_t* tok_a = reinterpret_cast<int32_t*>(ws + F.tok);
+  float* lgt_a = reinterpret_cast<float*>(ws + F.lgt);
+  int* cnt = reinterpret_cast<int*>(ws + F.cnt);
+  float* cz = reinterpret_cast<float*>(ws + F.cz);
+  int* ci = reinterpret_cast<int*>(ws + F.ci);
+  la.n_kb = cdiv(hidden, klg::BK);
+  la.scale_log2 = inv_temp * 1.4426950408889634f;
+  la.parts = rec;
+  la.n_ck = cdiv(vocab, 32);
+  la.cap = (int)cap;
+  alignas(64) CUtensorMap mh, mh64, mw;
+  if (!make_map(&mh, h, hidden, n_rows, hidden, klg::BK, klg::BM) ||
+      !make_map(&mh64, h, hidden, n_rows, hidden, klg::BK, 64) ||
+      !make_map(&mw, w, hidden, vocab, hidden, klg::BK, klg::LSE_BN / 2))
+    return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+  // sweep 1: per row (m, S) of z / T and the 32-column chunk maxima; merged to the row's lse
+  la.cmax = cmax;
+  if ((rc = launch_lse_pair<klg::EPI_GREEDY>(mh, mh64, mw, la, s))) return rc;
+  {
+    const int slot = trace_pre(s);
+    cudaError_t e = launch_k(klg::sample_merge_kernel, dim3(cdiv(n_rows, 32), 1), dim3(32 * klg::SMERGE_WARPS), 0, s, 1,
+                             static_cast<const float*>(rec), n_part, (int)n_rows, static_cast<float*>(nullptr), tok_a,
+                             lgt_a, lse_all);
+    trace_post(slot, s, KLG_KIND_MERGE);
+    if (e != cudaSuccess) return cuda_fail(e, "launch sample_merge_kernel");
+    ++g_launches;
+  }
+  // per row: the threshold no surviving logit is below
+  {
+    const int slot = trace_pre(s);
+    cudaError_t e = launch_k(klg::filter_threshold_kernel, dim3((unsigned)n_rows), dim3(klg::FILT_THREADS), 0, s, 1,
+                             static_cast<const float*>(cmax), la.n_ck, static_cast<const float*>(lse_all), inv_temp,
+                             top_k, top_p, thr);
+    trace_post(slot, s, KLG_KIND_SAMPLE);
+    if (e != cudaSuccess) return cuda_fail(e, "launch filter_threshold_kernel");
+    ++g_launches;
+  }
+  // sweep 2: the candidates (every logit at or above the threshold)
+  cudaError_t e = cudaMemsetAsync(cnt, 0, (size_t)n_rows * sizeof(int), s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync (candidate counters)");
+  e = cudaMemsetAsync(overflow, 0, sizeof(int), s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync (overflow flag)");
+  la.cmax = nullptr;
+  la.thr = thr;
+  la.cand_cnt = cnt;
+  la.cand_z = cz;
+  la.cand_i = ci;
+  if ((rc = launch_lse_pair<klg::EPI_CAND>(mh, mh64, mw, la, s))) return rc;
+  // per row: top-k / top-p on the candidates and the Gumbel-max draw among the survivors
+  const int slot = trace_pre(s);
+  e = launch_k(klg::filter_select_kernel, dim3((unsigned)n_rows), dim3(klg::FILT_THREADS), 0, s, 1,
+               static_cast<const int*>(cnt), static_cast<const float*>(cz), static_cast<const int*>(ci), (int)cap,
+               static_cast<const float*>(lse_all), inv_temp, top_k, top_p, (uint32_t)seed, (uint32_t)(seed >> 32), tokens,
+               logit, lse, overflow);
+  trace_post(slot, s, KLG_KIND_SAMPLE);
+  if (e != cudaSuccess) return cuda_fail(e, "launch filter_select_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
 int klg_gather_rows(const void* diff, const void* ar, const int64_t* anchors, const int64_t* targets, int64_t batch,
                     int64_t n_blocks, int64_t block, int64_t ar_len, int64_t row_bytes, int64_t pad_id, void* h_s,
                     void* h_t, uint8_t* valid, void* stream) {

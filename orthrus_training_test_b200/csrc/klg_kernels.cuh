@@ -235,6 +235,17 @@ struct LseArgs {
   float* parts;     // EPI_LSE: [n_uv * LSE_CSPLIT][2][n_views * N]; else [n_uv * rep * LSE_CSPLIT][5][N]
   int n_views;      // 2: student rows then teacher rows (training pass 1); 1: one matrix (EPI_SAMPLE)
   uint32_t seed_lo, seed_hi;   // EPI_SAMPLE
+  // Filtered sampling (top-k / top-p): EPI_GREEDY also writes each row's 32-column chunk
+  // maxima cmax[row][n_ck] (raw logits) when cmax is set; EPI_CAND appends every logit
+  // z >= thr[row] with its column to the row's candidate list (cand_z / cand_i [row][cap],
+  // counter cand_cnt[row]; entries past cap are counted, not stored).
+  float* cmax;
+  int n_ck;
+  const float* thr;
+  int* cand_cnt;
+  float* cand_z;
+  int* cand_i;
+  int cap;
   // Row replication (EPI_GREEDY / EPI_SAMPLE with N <= 128, one row tile): the pair tile's
   // 256 M rows hold `rep` copies of rows 0..256/rep-1, and the copy j of a warp's rows
   // takes the j-th 1/rep of the tile's columns -- every epilogue warp gets work instead of
@@ -245,7 +256,7 @@ struct LseArgs {
 
 // EPI_LSE: (m, S) per row and view (training pass 1).  EPI_GREEDY: (m, S) and the argmax of
 // z.  EPI_SAMPLE: (m, S) and a Gumbel-max draw from softmax(z / T).
-enum { EPI_LSE = 0, EPI_GREEDY = 1, EPI_SAMPLE = 2 };
+enum { EPI_LSE = 0, EPI_GREEDY = 1, EPI_SAMPLE = 2, EPI_CAND = 3 };
 constexpr uint32_t HASH_ROW = 0x9E3779B1u, HASH_COL = 0x85EBCA77u, HASH_SEED = 0xC2B2AE3Du;
 
 // Counter-based 32-bit hash of (seed, row, column): the three keys combined with odd
@@ -319,7 +330,7 @@ __device__ __forceinline__ float exp_variate_log2(uint32_t x) {
 // rk = seed_lo ^ row * HASH_ROW ^ seed_hi * HASH_SEED, so rk ^ col * HASH_COL is sample_hash's key.
 template <bool SAMPLE>
 __device__ __forceinline__ void select_chunk(const uint32_t (&b)[32], int nvalid, int col0, float sl2, uint32_t rk,
-                                             float& m, float& S, float& bk, int& bi, float& bz) {
+                                             float& m, float& S, float& bk, int& bi, float& bz, float& cmx) {
   float z[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) z[j] = j < nvalid ? __uint_as_float(b[j]) : -INFINITY;
@@ -330,6 +341,7 @@ __device__ __forceinline__ void select_chunk(const uint32_t (&b)[32], int nvalid
   for (int w = 8; w >= 1; w >>= 1)
 #pragma unroll
     for (int j = 0; j < w; ++j) t[j] = fmaxf(t[2 * j], t[2 * j + 1]);
+  cmx = t[0];
   const float nm = fmaxf(m, t[0] * sl2);
   const float r = ex2(m - nm);
   m = nm;
@@ -568,6 +580,7 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
       const int row = rp * 256 + prow % rw + lane;
       const bool live = rp * 256 + prow % rw < a.n_rows;   // warp-uniform
       const uint32_t rk = a.seed_lo ^ ((uint32_t)row * HASH_ROW) ^ (a.seed_hi * HASH_SEED);
+      const float thr_row = (EPI == EPI_CAND && live && row < a.n_rows) ? a.thr[row] : INFINITY;
       float m = NEG_BIG, S = 0.f;
       float bk = -INFINITY, bz = 0.f;   // EPI_GREEDY / EPI_SAMPLE: best key, its logit
       int bi = -1;
@@ -584,8 +597,26 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
           tmem_wait_ld_regs(b0);
           const int nvalid = min(32, a.vocab - (col_base + c * 32));
           if (nvalid > 0) {
-            if (EPI == EPI_LSE) lse_chunk(b0, nvalid, a.scale_log2, m, S);
-            else select_chunk<EPI == EPI_SAMPLE>(b0, nvalid, col_base + c * 32, a.scale_log2, rk, m, S, bk, bi, bz);
+            if (EPI == EPI_LSE) {
+              lse_chunk(b0, nvalid, a.scale_log2, m, S);
+            } else if (EPI == EPI_CAND) {
+              // candidates of the filtered sampler: every logit at or above the row's threshold
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const float z = __uint_as_float(b0[j]);
+                if (j < nvalid && z >= thr_row) {
+                  const int slot = atomicAdd(a.cand_cnt + row, 1);
+                  if (slot < a.cap) {
+                    a.cand_z[(size_t)row * a.cap + slot] = z;
+                    a.cand_i[(size_t)row * a.cap + slot] = col_base + c * 32 + j;
+                  }
+                }
+              }
+            } else {
+              float cmx;
+              select_chunk<EPI == EPI_SAMPLE>(b0, nvalid, col_base + c * 32, a.scale_log2, rk, m, S, bk, bi, bz, cmx);
+              if (a.cmax && row < a.n_rows) a.cmax[(size_t)row * a.n_ck + (col_base + c * 32) / 32] = cmx;
+            }
           }
         }
         tc_fence_before();
@@ -595,7 +626,7 @@ lse_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_constan
           else mbar_arrive_cluster(lead_tempty0 + 8u * buf);
         }
       }
-      if (ok && row < a.n_rows) {
+      if (ok && row < a.n_rows && EPI != EPI_CAND) {
         if (EPI == EPI_LSE) {
           const size_t n2 = (size_t)a.n_views * a.n_rows;
           float* p = a.parts + ((size_t)(uv * n_slices + slice) * 2) * n2 + (size_t)view * a.n_rows + row;
@@ -1615,6 +1646,224 @@ sample_merge_kernel(const float* __restrict__ parts, int n_part, int n, float* _
       logit[i] = bz;
       lse[i] = (M + __log2f(S)) * 0.69314718055994530942f;
     }
+  }
+}
+
+// ---------------------------------------------------------------- filtered sampling (top-k / top-p)
+// Order-preserving 32-bit keys of floats (a larger float has a larger key), and back.
+__device__ __forceinline__ uint32_t fkey(float f) {
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float fkey_value(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+constexpr int FILT_THREADS = 256;
+
+template <typename T>
+__device__ __forceinline__ T block_sum(T v, T* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();   // red is free (a previous call's readers are done)
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  T t = 0;
+#pragma unroll
+  for (int i = 0; i < FILT_THREADS / 32; ++i) t += red[i];
+  return t;
+}
+
+// Per row (one block): a threshold below which no logit survives top-k / top-p, from the
+// row's 32-column chunk maxima c (raw logits) and its log-sum-exp lse (natural log, of z / T).
+//  top-k: the k-th largest chunk maximum -- the k chunks holding the largest maxima give k
+//         logits at or above it, so the k-th largest logit is too;
+//  top-p: the largest chunk maximum c* whose chunk maxima at or above it carry softmax mass
+//         > top_p -- the logits at or above c* then carry more than top_p, so every logit
+//         below c* has more than top_p of mass above it and top-p removes it.
+// thr[row] = the larger of the two (-inf when neither applies).  Both are found by a
+// bit-by-bit search over the order-preserving keys (32 block-wide passes).
+__global__ void __launch_bounds__(FILT_THREADS) filter_threshold_kernel(const float* __restrict__ cmax, int n_ck,
+                                                                        const float* __restrict__ lse, float inv_temp,
+                                                                        int top_k, float top_p,
+                                                                        float* __restrict__ thr) {
+  pdl_enter();
+  __shared__ double redd[FILT_THREADS / 32];
+  __shared__ int redi[FILT_THREADS / 32];
+  const int row = blockIdx.x;
+  const float* c = cmax + (size_t)row * n_ck;
+  const float L = lse[row];
+  float tk = -INFINITY, tp = -INFINITY;
+  if (top_k > 0 && top_k <= n_ck) {
+    uint32_t T = 0;
+    for (int bit = 31; bit >= 0; --bit) {
+      const uint32_t cand = T | (1u << bit);
+      int cnt = 0;
+      for (int i = threadIdx.x; i < n_ck; i += FILT_THREADS) cnt += fkey(c[i]) >= cand;
+      if (block_sum(cnt, redi) >= top_k) T = cand;
+    }
+    tk = fkey_value(T);
+  }
+  if (top_p < 1.f) {
+    auto mass_at_or_above = [&](uint32_t T) {
+      double m = 0.0;
+      for (int i = threadIdx.x; i < n_ck; i += FILT_THREADS)
+        if (fkey(c[i]) >= T) m += exp((double)c[i] * inv_temp - (double)L);
+      return block_sum(m, redd);
+    };
+    if (mass_at_or_above(0u) > (double)top_p) {
+      uint32_t T = 0;
+      for (int bit = 31; bit >= 0; --bit) {
+        const uint32_t cand = T | (1u << bit);
+        if (mass_at_or_above(cand) > (double)top_p) T = cand;
+      }
+      tp = fkey_value(T);
+    }
+  }
+  if (threadIdx.x == 0) thr[row] = fmaxf(tk, tp);
+}
+
+// Per row (one block): the filtered draw from the candidates (every logit >= the row's
+// threshold, so a superset of what top-k / top-p keep).  top-k keeps the candidates at or
+// above the k-th largest value (ties stay, as generate.py:61); top-p keeps a candidate when
+// the softmax mass strictly above it (over the top-k survivors, or over the whole row when
+// top_k = 0, whose mass is exp(z / T - lse)) is <= top_p (generate.py:64-73: the shifted
+// removal keeps the entry that crosses top_p).  The token is the Gumbel-max draw over the
+// kept candidates with the same keys as the unfiltered sampler (hash of seed, row, column);
+// lse_out is log sum exp(z / T) over the kept entries, so p(token) = exp(z / T - lse_out)
+// -- the reference's renormalised probability.  A row with more candidates than the list
+// holds sets *overflow and gets token -1.
+__global__ void __launch_bounds__(FILT_THREADS) filter_select_kernel(
+    const int* __restrict__ cand_cnt, const float* __restrict__ cand_z, const int* __restrict__ cand_i, int cap,
+    const float* __restrict__ lse, float inv_temp, int top_k, float top_p, uint32_t seed_lo, uint32_t seed_hi,
+    int32_t* __restrict__ tokens, float* __restrict__ logit, float* __restrict__ lse_out, int* __restrict__ overflow) {
+  pdl_enter();
+  __shared__ double redd[FILT_THREADS / 32];
+  __shared__ int redi[FILT_THREADS / 32];
+  __shared__ float redf[FILT_THREADS / 32];
+  __shared__ uint32_t redk[FILT_THREADS / 32];
+  const int row = blockIdx.x;
+  const int total = cand_cnt[row];
+  if (total > cap) {
+    if (threadIdx.x == 0) {
+      atomicOr(overflow, 1);
+      tokens[row] = -1;
+      logit[row] = __int_as_float(0x7fc00000);
+      lse_out[row] = __int_as_float(0x7fc00000);
+    }
+    return;
+  }
+  const int n = total;
+  const float* z = cand_z + (size_t)row * cap;
+  const int* ix = cand_i + (size_t)row * cap;
+  const double L = lse[row];
+  // top-k: the k-th largest candidate value's key
+  uint32_t Tk = 0;
+  if (top_k > 0 && top_k <= n) {
+    uint32_t T = 0;
+    for (int bit = 31; bit >= 0; --bit) {
+      const uint32_t cand = T | (1u << bit);
+      int cnt = 0;
+      for (int i = threadIdx.x; i < n; i += FILT_THREADS) cnt += fkey(z[i]) >= cand;
+      if (block_sum(cnt, redi) >= top_k) T = cand;
+    }
+    Tk = T;
+  }
+  // softmax weights of the entries top-p measures: over the top-k survivors, or the whole row
+  double mref = L, Z = 1.0;
+  if (top_k > 0) {
+    float mx = -INFINITY;
+    for (int i = threadIdx.x; i < n; i += FILT_THREADS)
+      if (fkey(z[i]) >= Tk) mx = fmaxf(mx, z[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) redf[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    for (int i = 0; i < FILT_THREADS / 32; ++i) mx = fmaxf(mx, redf[i]);
+    mref = (double)mx * inv_temp;
+    double zs = 0.0;
+    for (int i = threadIdx.x; i < n; i += FILT_THREADS)
+      if (fkey(z[i]) >= Tk) zs += exp((double)z[i] * inv_temp - mref);
+    Z = block_sum(zs, redd);
+  }
+  // top-p: keep key >= Tp, Tp = 1 + the largest T whose strictly-larger mass exceeds top_p
+  uint32_t Tp = 0;
+  if (top_p < 1.f) {
+    auto mass_above = [&](uint32_t T) {
+      double m = 0.0;
+      for (int i = threadIdx.x; i < n; i += FILT_THREADS) {
+        const uint32_t k = fkey(z[i]);
+        if (k > T && k >= Tk) m += exp((double)z[i] * inv_temp - mref);
+      }
+      return block_sum(m, redd) / Z;
+    };
+    if (mass_above(0u) > (double)top_p) {
+      uint32_t T = 0;
+      for (int bit = 31; bit >= 0; --bit) {
+        const uint32_t cand = T | (1u << bit);
+        if (mass_above(cand) > (double)top_p) T = cand;
+      }
+      Tp = T + 1;
+    }
+  }
+  const uint32_t Tkeep = Tk > Tp ? Tk : Tp;
+  // Gumbel-max over the kept candidates (lowest column among equal keys), and their lse
+  const float sl2 = inv_temp * 1.4426950408889634f;
+  float bk = -INFINITY, bz = 0.f, mk = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < n; i += FILT_THREADS) {
+    if (fkey(z[i]) < Tkeep) continue;
+    const int col = ix[i];
+    const float key = fmaf(z[i], sl2, -__log2f(exp_variate_log2(sample_hash(seed_lo, seed_hi, (uint32_t)row, (uint32_t)col))));
+    if (key > bk || (key == bk && col < bi)) {
+      bk = key;
+      bi = col;
+      bz = z[i];
+    }
+    mk = fmaxf(mk, z[i]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ok = __shfl_xor_sync(0xffffffffu, bk, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    const float oz = __shfl_xor_sync(0xffffffffu, bz, o);
+    if (ok > bk || (ok == bk && oi < bi)) {
+      bk = ok;
+      bi = oi;
+      bz = oz;
+    }
+    mk = fmaxf(mk, __shfl_xor_sync(0xffffffffu, mk, o));
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) {
+    redf[threadIdx.x >> 5] = bk;
+    redi[threadIdx.x >> 5] = bi;
+    redk[threadIdx.x >> 5] = __float_as_uint(bz);
+    redd[threadIdx.x >> 5] = mk;
+  }
+  __syncthreads();
+  bk = -INFINITY;
+  bi = 0x7fffffff;
+  bz = 0.f;
+  mk = -INFINITY;
+  for (int w = 0; w < FILT_THREADS / 32; ++w) {
+    if (redf[w] > bk || (redf[w] == bk && redi[w] < bi)) {
+      bk = redf[w];
+      bi = redi[w];
+      bz = __uint_as_float(redk[w]);
+    }
+    mk = fmaxf(mk, (float)redd[w]);
+  }
+  double ss = 0.0;
+  for (int i = threadIdx.x; i < n; i += FILT_THREADS)
+    if (fkey(z[i]) >= Tkeep) ss += exp((double)(z[i] - mk) * inv_temp);
+  ss = block_sum(ss, redd);
+  if (threadIdx.x == 0) {
+    tokens[row] = bi == 0x7fffffff ? -1 : bi;
+    logit[row] = bz;
+    lse_out[row] = (float)((double)mk * inv_temp + log(ss));
   }
 }
 

@@ -108,6 +108,17 @@ def test_sampler_and_norm_argument_validation():
     assert L.klg_lm_head_sample(p, p, 4, 12, 4, 1.0, 1, seed, p, p, p, p, 1 << 16, None) == _lib.KLG_ERR_ALIGN
     assert L.klg_lm_head_sample(p, p, 4, 64, 4, 0.0, 1, seed, p, p, p, p, 1 << 16, None) == _lib.KLG_ERR_ARG
     assert L.klg_lm_head_sample(p, p, 4, 64, 4, 1.0, 1, seed, p, p, p, p, 16, None) == _lib.KLG_ERR_WORKSPACE
+    # filtered sampling: cap within [1, V], top_p in (0, 1], top_k >= 0, outputs present
+    assert L.klg_lm_head_sample_filtered_workspace_bytes(4, 300, 0) == -1
+    assert L.klg_lm_head_sample_filtered_workspace_bytes(4, 300, 301) == -1
+    assert L.klg_lm_head_sample_filtered_workspace_bytes(4, 300, 300) > 4 * 300 * 8
+    fargs = lambda **kw: [p, p, 4, 64, 300, 1.0, kw.get("k", 5), kw.get("tp", 1.0), seed, kw.get("cap", 16), p, p, p,
+                          kw.get("ov", p), p, 1 << 16, None]
+    assert L.klg_lm_head_sample_filtered(*fargs(tp=0.0)) == _lib.KLG_ERR_ARG
+    assert L.klg_lm_head_sample_filtered(*fargs(tp=1.5)) == _lib.KLG_ERR_ARG
+    assert L.klg_lm_head_sample_filtered(*fargs(k=-1)) == _lib.KLG_ERR_ARG
+    assert L.klg_lm_head_sample_filtered(*fargs(cap=301)) == _lib.KLG_ERR_ARG
+    assert L.klg_lm_head_sample_filtered(*fargs(ov=None)) == _lib.KLG_ERR_ARG
     # final norm: dtype flag, alignment, eps, null buffers
     assert L.klg_rmsnorm_rows(p, 2, p, 4, 64, 1e-5, p, None, None) == _lib.KLG_ERR_ARG
     assert L.klg_rmsnorm_rows(p, 0, p, 4, 12, 1e-5, p, None, None) == _lib.KLG_ERR_ALIGN

@@ -148,3 +148,109 @@ def test_token_logprob_of_another_distribution():
     z = h_a.double().numpy() @ W.double().numpy().T
     ref = z[np.arange(N), tok] / T - O._lse(z / T)
     np.testing.assert_allclose(lp.cpu().numpy(), ref, rtol=0, atol=1e-3)
+
+
+# ----------------------------------------------------------------- top-k / top-p (fused)
+FILTERS = {"k20": (0.7, 20, 1.0), "p09": (1.0, 0, 0.9), "k50p08": (0.8, 50, 0.8), "p05": (0.5, 0, 0.5),
+           "k1": (1.0, 1, 1.0)}
+
+
+def _run_filtered(h, W, T, k, p, seed=0, cap=None):
+    from orthrus_training_test_b200 import _lib, sampling
+    tok, logit, lse = sampling.lm_head_sample_filtered(h.to(_dev()), W.to(_dev()), T, k, p, seed, cap=cap)
+    torch.cuda.synchronize()
+    assert _lib.device_status(reset=True) == 0
+    return tok.cpu().numpy(), logit.cpu().numpy().astype(np.float64), lse.cpu().numpy().astype(np.float64)
+
+
+@pytest.mark.parametrize("name", sorted(FILTERS))
+def test_filtered_matches_reference_golden(name):
+    """Every draw lies in the support of the reference's filtered distribution and its
+    probability exp(z / T - lse) is the reference's renormalised probability."""
+    T, k, p = FILTERS[name]
+    g = dict(np.load(GOLDEN / "sample_token.npz"))
+    h = torch.tensor(g["h"]).to(torch.bfloat16)
+    W = torch.tensor(g["weight"]).to(torch.bfloat16)
+    ref = g[f"probs_{name}"]
+    rows = np.arange(h.shape[0])
+    for seed in (1, 2, 3):
+        tok, logit, lse = _run_filtered(h, W, T, k, p, seed)
+        assert np.all(ref[rows, tok] > 0), (name, seed)
+        np.testing.assert_allclose(np.exp(logit / T - lse), ref[rows, tok], rtol=1e-4, atol=1e-7)
+
+
+def test_filtered_draws_follow_filtered_softmax():
+    """8192 rows with one logit vector and independent keys: token frequencies follow the
+    reference's filtered distribution (Pearson chi-square over its support)."""
+    g = dict(np.load(GOLDEN / "sample_token.npz"))
+    T, k, p = 0.8, 50, 0.8
+    n = 8192
+    h = torch.tensor(g["h"][:1]).to(torch.bfloat16).repeat(n, 1)
+    W = torch.tensor(g["weight"]).to(torch.bfloat16)
+    tok, _, _ = _run_filtered(h, W, T, k, p, seed=11)
+    probs = g["probs_k50p08"][0]
+    support = np.flatnonzero(probs > 0)
+    assert np.isin(tok, support).all()
+    observed = np.bincount(tok, minlength=len(probs))[support]
+    expected = probs[support] * n
+    chi2 = float(((observed - expected) ** 2 / expected).sum())
+    assert chi2 < 3.0 * len(support) + 30.0, chi2
+
+
+@pytest.mark.parametrize("N,k,p", [(32, 50, 0.9), (32, 0, 0.95), (300, 8, 1.0), (5, 0, 0.3)])
+def test_filtered_trainer_vocab(N, k, p):
+    """SmolLM2-135M's lm_head shape (H = 576, V = 49,153): the draw is in the float64
+    oracle's filtered support -- on every row within the support one rank / 1e-3 of mass
+    wider (the fp32 logits may order entries at the boundary differently), on >= 95 % of rows
+    within the exact one -- and its probability matches the oracle's there."""
+    h, W = _problem(N, 576, 49153, seed=N + k, scale=3.0)
+    T = 0.9
+    tok, logit, lse = _run_filtered(h, W, T, k, p, seed=5)
+    z = h.double().numpy() @ W.double().numpy().T
+    probs, kept = O.filtered_probs_np(z, T, k, p)
+    _, wider = O.filtered_probs_np(z, T, k + 1 if k else 0, min(1.0, p + 1e-3))
+    rows = np.arange(N)
+    assert wider[rows, tok].all(), np.flatnonzero(~wider[rows, tok])
+    ok = kept[rows, tok]
+    assert ok.mean() >= 0.95, ok.mean()
+    np.testing.assert_allclose(np.exp(logit / T - lse)[ok], probs[rows, tok][ok], rtol=2e-3)
+
+
+def test_filtered_candidate_overflow_is_reported():
+    """A candidate list too short for the row (cap 2, top_k 10) sets the overflow flag and the
+    row's token to -1 -- the C entry point reports instead of truncating -- and the Python
+    wrapper retries with room for the whole vocabulary."""
+    import ctypes
+
+    from orthrus_training_test_b200 import _lib
+    from orthrus_training_test_b200.ops import _ptr, _stream
+    h, W = _problem(4, 64, 300, seed=2)
+    hd, Wd = h.to(_dev()), W.to(_dev())
+    tok = torch.empty(4, dtype=torch.int32, device=_dev())
+    lg, ls = (torch.empty(4, dtype=torch.float32, device=_dev()) for _ in range(2))
+    ov = torch.zeros(1, dtype=torch.int32, device=_dev())
+    need = int(_lib.lib().klg_lm_head_sample_filtered_workspace_bytes(4, 300, 2))
+    ws = torch.empty(need, dtype=torch.uint8, device=_dev())
+    _lib.call("klg_lm_head_sample_filtered", _ptr(hd), _ptr(Wd), 4, 64, 300, 1.0, 10, 1.0, ctypes.c_ulonglong(3), 2,
+              _ptr(tok), _ptr(lg), _ptr(ls), _ptr(ov), _ptr(ws), need, _stream(_dev()))
+    torch.cuda.synchronize()
+    assert int(ov.item()) == 1 and (tok.cpu() == -1).all()
+    t2, _, _ = _run_filtered(h, W, 1.0, 10, 1.0, seed=3, cap=2)   # retried with cap = V
+    probs, kept = O.filtered_probs_np(h.double().numpy() @ W.double().numpy().T, 1.0, 10, 1.0)
+    assert kept[np.arange(4), t2].all()
+
+
+def test_sample_token_with_filters_returns_token_probabilities():
+    """The reference-signature entry (generate.py:40-78 on hidden states) with top-k / top-p."""
+    from orthrus_training_test_b200.sampling import sample_token
+    g = dict(np.load(GOLDEN / "sample_token.npz"))
+    h = torch.tensor(g["h"]).to(torch.bfloat16).to(_dev())
+    W = torch.tensor(g["weight"]).to(torch.bfloat16).to(_dev())
+    tok, p_tok = sample_token(h, W, 0.8, 50, 0.8, seed=4)
+    ref = g["probs_k50p08"]
+    rows = np.arange(h.shape[0])
+    t = tok.cpu().numpy()
+    assert np.all(ref[rows, t] > 0)
+    np.testing.assert_allclose(p_tok.cpu().numpy(), ref[rows, t], rtol=1e-4, atol=1e-7)
+    tok0, none = sample_token(h, W, 0.0, 50, 0.8)            # greedy: no filter, as the reference
+    assert none is None and np.array_equal(tok0.cpu().numpy(), g["greedy"])

@@ -73,3 +73,36 @@ def test_gumbel_max_draws_from_softmax():
     observed = np.bincount(tok, minlength=V)
     chi2 = float(((observed - expected) ** 2 / expected).sum())
     assert chi2 < 60.0, chi2          # 23 degrees of freedom: p < 1e-4 beyond 60
+
+
+FILTERS = {"k20": (0.7, 20, 1.0), "p09": (1.0, 0, 0.9), "k50p08": (0.8, 50, 0.8), "p05": (0.5, 0, 0.5),
+           "k1": (1.0, 1, 1.0)}
+
+
+def test_filtered_probabilities_match_reference():
+    """top-k / top-p (generate.py:55-75): the oracle's filtered distribution equals the
+    reference's own ``sample_token`` probabilities on the fixture, support and values."""
+    g = load()
+    z = g["h"].astype(np.float64) @ g["weight"].astype(np.float64).T
+    for name, (T, k, p) in FILTERS.items():
+        probs, kept = O.filtered_probs_np(z, T, k, p)
+        ref = g[f"probs_{name}"]
+        np.testing.assert_array_equal(kept, ref > 0, err_msg=name)
+        np.testing.assert_allclose(probs, ref, rtol=2e-5, atol=1e-9, err_msg=name)
+    assert (g["probs_k1"] > 0).sum(axis=1).max() == 1          # top-1 keeps one entry per row
+
+
+def test_filtered_gumbel_keys_draw_from_filtered_softmax():
+    """Gumbel-max over the kept entries draws from the filtered distribution (chi-square)."""
+    rng = np.random.default_rng(3)
+    V, n, T, k, p = 40, 60000, 0.9, 12, 0.85
+    z = rng.normal(size=V) * 1.5
+    keys = O.filtered_keys_np(np.broadcast_to(z, (n, V)), T, seed=7, top_k=k, top_p=p)
+    tok = np.argmax(keys, axis=-1)
+    probs, kept = O.filtered_probs_np(z[None], T, k, p)
+    assert kept[0, tok].all()
+    support = np.flatnonzero(kept[0])
+    expected = probs[0, support] * n
+    observed = np.bincount(tok, minlength=V)[support]
+    chi2 = float(((observed - expected) ** 2 / expected).sum())
+    assert chi2 < 3.0 * len(support) + 30.0, chi2
