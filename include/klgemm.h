@@ -297,6 +297,7 @@ int klg_rmsnorm_rows_bwd(const void* x, int x_f32, const float* gamma, const flo
  * triton_kernels.py:281-290), forward only: for query position p of block p / K, keys are
  * the AR cache rows 0..limits[b, p] (clamped to ar_len - 1; -1 = none) and the K rows of
  * its own block, scores scaled by `scale`, GQA (head h uses KV head h / (H / Hkv)).
+ * The backward is klg_block_attn_bwd.
  *   q [B, H, Ld, 64], k_self / v_self [B, Hkv, Ld, 64] (bf16, contiguous),
  *   k_ar / v_ar: rows 0..ar_len-1 of a [B, Hkv, ar_stride, 64] bf16 cache,
  *   limits [B, Ld] int32; out [B, H, Ld, 64] bf16; lse [B, H, Ld] fp32 natural log (may be NULL).
@@ -309,6 +310,18 @@ int klg_block_attn_fwd(const void* q, const void* k_self, const void* v_self, co
                        int64_t ar_stride, const int32_t* limits, int64_t batch, int64_t heads, int64_t kv_heads,
                        int64_t diff_len, int64_t block, int64_t ar_len, int64_t head_dim, float scale, void* out,
                        float* lse, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Backward of klg_block_attn_fwd (training the diffusion heads; the reference's Triton backward,
+ * triton_kernels.py:73-141 and its autograd at 161-172, which the reference marks broken): for
+ * the upstream gradient d_out [B, H, Ld, 64] bf16 and the forward's out (bf16) and lse (fp32,
+ * natural log), writes d_q [B, H, Ld, 64] and the block keys' d_k_self / d_v_self
+ * [B, Hkv, Ld, 64] (fp32; the dK / dV of a KV head sum over the query heads sharing it).  The
+ * AR cache gets no gradient (it comes from the frozen backbone).  Same shapes and limits as the
+ * forward; no workspace. */
+int klg_block_attn_bwd(const void* q, const void* k_self, const void* v_self, const void* k_ar, const void* v_ar,
+                       int64_t ar_stride, const int32_t* limits, const void* out, const float* lse, const void* d_out,
+                       int64_t batch, int64_t heads, int64_t kv_heads, int64_t diff_len, int64_t block, int64_t ar_len,
+                       int64_t head_dim, float scale, float* d_q, float* d_k_self, float* d_v_self, void* stream);
 
 /* Number of AR key-range splits (the thread-block cluster size) klg_block_attn_fwd uses
  * for this shape on the current device; -1 for an unsupported shape. */

@@ -666,3 +666,53 @@ def block_attention_np(q, k_self, v_self, k_ar, v_ar, limits, K: int, scale: Opt
                 out[b, h, rows] = (e / z) @ vv
                 lse[b, h, rows] = (m + np.log(z))[:, 0]
     return out, lse
+
+
+def block_attention_bwd_np(q, k_self, v_self, k_ar, v_ar, limits, K: int, d_out, scale: Optional[float] = None):
+    """float64 closed-form backward of ``block_attention_np`` for an upstream gradient
+    ``d_out [B, H, Ld, D]``: ``(dq [B, H, Ld, D], dk_self, dv_self [B, Hkv, Ld, D])``.
+
+    Per query block, with P the attention probabilities over [AR keys | own block keys],
+    V the matching values and O = P V:  dV = P^T dO,  dP = dO V^T,  dS = P (dP - rowsum(dO O)),
+    dQ = scale dS K,  dK = scale dS^T Q; the self keys' dK / dV sum over the query heads that
+    share the KV head (GQA).  The AR cache gets no gradient (it comes from the frozen
+    backbone: the reference's Triton backward, triton_kernels.py:73-141 and 161-172, returns
+    None for it as well).
+    """
+    q = np.asarray(q, np.float64)
+    ks, vs = np.asarray(k_self, np.float64), np.asarray(v_self, np.float64)
+    ka, va = np.asarray(k_ar, np.float64), np.asarray(v_ar, np.float64)
+    do = np.asarray(d_out, np.float64)
+    lim = np.asarray(limits)
+    B, H, Ld, D = q.shape
+    Hkv, AL = ks.shape[1], ka.shape[2]
+    ng = H // Hkv
+    sc = 1.0 / math.sqrt(D) if scale is None else scale
+    dq = np.zeros_like(q)
+    dks = np.zeros_like(ks)
+    dvs = np.zeros_like(vs)
+    ar_idx = np.arange(AL)
+    for b in range(B):
+        for h in range(H):
+            hk = h // ng
+            for blk in range(Ld // K):
+                rows = slice(blk * K, (blk + 1) * K)
+                qq = q[b, h, rows]
+                kk = np.concatenate([ka[b, hk], ks[b, hk, rows]], axis=0)
+                vv = np.concatenate([va[b, hk], vs[b, hk, rows]], axis=0)
+                s = qq @ kk.T * sc
+                vis = np.concatenate([ar_idx[None, :] <= np.clip(lim[b, rows], -1, AL - 1)[:, None],
+                                      np.ones((K, K), bool)], axis=1)
+                s = np.where(vis, s, -np.inf)
+                e = np.exp(s - s.max(axis=1, keepdims=True))
+                p = e / e.sum(axis=1, keepdims=True)
+                o = p @ vv
+                g = do[b, h, rows]
+                dv = p.T @ g
+                dp = g @ vv.T
+                ds = p * (dp - (g * o).sum(axis=1, keepdims=True))
+                dq[b, h, rows] = sc * ds @ kk
+                dk = sc * ds.T @ qq
+                dks[b, hk, rows] += dk[AL:]
+                dvs[b, hk, rows] += dv[AL:]
+    return dq, dks, dvs

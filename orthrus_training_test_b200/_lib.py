@@ -32,6 +32,8 @@ SIGNATURES = {
     "klg_block_attn_workspace_bytes": (c_longlong, [c_longlong] * 7),
     "klg_block_attn_fwd": (c_int, [c_void_p] * 5 + [c_longlong, c_void_p] + [c_longlong] * 7 +
                            [c_float, c_void_p, c_void_p, c_void_p, c_longlong, c_void_p]),
+    "klg_block_attn_bwd": (c_int, [c_void_p] * 5 + [c_longlong, c_void_p, c_void_p, c_void_p, c_void_p] +
+                           [c_longlong] * 7 + [c_float, c_void_p, c_void_p, c_void_p, c_void_p]),
     "klg_block_attn_splits": (c_int, [c_longlong] * 7),
     "klg_selftest_attn_split_stall": (c_int, [c_void_p] * 5 + [c_longlong, c_void_p] + [c_longlong] * 7 +
                                       [c_float, c_void_p, c_void_p, c_void_p, c_longlong, c_int, c_void_p]),

@@ -9,8 +9,9 @@ in the reference.  ``block_attention`` computes the same attention in one CUDA k
 (batch, KV head, head group, block, key split); the key splits of a decode call form a
 thread-block cluster and combine through distributed shared memory.
 
-Forward only (inference).  Every function here calls the CUDA library; there is no CPU
-fallback.
+Forward for generation and, through :class:`BlockAttentionFn`, a backward (dQ and the
+block keys' dK / dV) for training the heads.  Every function here calls the CUDA library;
+there is no CPU fallback.
 """
 from __future__ import annotations
 
@@ -63,9 +64,21 @@ def block_attention(q: torch.Tensor, k_self: torch.Tensor, v_self: torch.Tensor,
     ``limits [B, Ld]`` -- query position p sees AR keys ``0..limits[b, p]`` (clamped; -1:
     none) and the ``block_size`` keys of block ``p // block_size``.  ``scale`` defaults to
     ``1/sqrt(64)``.  Returns ``out [B, H, Ld, 64]`` bf16 (and ``lse [B, H, Ld]`` fp32,
-    natural log, when ``want_lse``).
+    natural log, when ``want_lse``).  When ``q``, ``k_self`` or ``v_self`` requires a gradient
+    (and ``want_lse`` is not asked), the call is differentiable through
+    :class:`BlockAttentionFn`.
     """
-    dev = _require_cuda(q, k_self, v_self, k_ar, v_ar, limits)
+    if (torch.is_grad_enabled() and not want_lse and workspace is None
+            and any(t.requires_grad for t in (q, k_self, v_self))):
+        if k_ar.requires_grad or v_ar.requires_grad:
+            raise ValueError("the AR cache gets no gradient (frozen backbone): pass it detached")
+        return BlockAttentionFn.apply(q, k_self, v_self, k_ar, v_ar, limits, block_size, scale)
+    return _attn_forward(q, k_self, v_self, k_ar, v_ar, limits, block_size, scale, want_lse, workspace)
+
+
+def _prepare(q, k_self, v_self, k_ar, v_ar, limits, block_size, scale):
+    """Checked, contiguous bf16 operands and the launch sizes of a forward / backward call."""
+    _require_cuda(q, k_self, v_self, k_ar, v_ar, limits)
     B, H, Ld, D = q.shape
     Hkv = k_self.shape[1]
     ar_len = k_ar.shape[2]
@@ -88,15 +101,56 @@ def block_attention(q: torch.Tensor, k_self: torch.Tensor, v_self: torch.Tensor,
     lim = limits.detach().to(torch.int32).contiguous()
     if scale is None:
         scale = 1.0 / math.sqrt(D)
-    need = workspace_bytes(B, H, Hkv, Ld, block_size, ar_len, D)
+    return (qc, ks, vs, ka, va, lim), (stride_k, B, H, Hkv, Ld, int(block_size), ar_len, D, float(scale))
+
+
+def _launch_fwd(tensors, meta, want_lse=False, workspace=None):
+    qc, ks, vs, ka, va, lim = tensors
+    stride_k, B, H, Hkv, Ld, K, ar_len, D, scale = meta
+    dev = qc.device
+    need = workspace_bytes(B, H, Hkv, Ld, K, ar_len, D)
     if workspace is None or workspace.numel() * workspace.element_size() < need:
         workspace = torch.empty(need, dtype=torch.uint8, device=dev)
     out = torch.empty(B, H, Ld, D, dtype=torch.bfloat16, device=dev)
     lse = torch.empty(B, H, Ld, dtype=torch.float32, device=dev) if want_lse else None
     call("klg_block_attn_fwd", _ptr(qc), _ptr(ks), _ptr(vs), _ptr(ka), _ptr(va), stride_k, _ptr(lim), B, H, Hkv, Ld,
-         block_size, ar_len, D, float(scale), _ptr(out), _ptr(lse), _ptr(workspace),
-         workspace.numel() * workspace.element_size(), _stream(dev))
+         K, ar_len, D, scale, _ptr(out), _ptr(lse), _ptr(workspace), workspace.numel() * workspace.element_size(),
+         _stream(dev))
     return (out, lse) if want_lse else out
+
+
+def _attn_forward(q, k_self, v_self, k_ar, v_ar, limits, block_size, scale, want_lse=False, workspace=None):
+    tensors, meta = _prepare(q, k_self, v_self, k_ar, v_ar, limits, block_size, scale)
+    return _launch_fwd(tensors, meta, want_lse, workspace)
+
+
+class BlockAttentionFn(torch.autograd.Function):
+    """:func:`block_attention` with a backward: dQ and the block keys' dK / dV from the forward's
+    log-sum-exps (``klg_block_attn_bwd``; the reference's Triton autograd is
+    triton_kernels.py:144-172).  The AR cache gets no gradient -- it comes from the frozen
+    backbone -- so ``k_ar`` / ``v_ar`` must not require one."""
+
+    @staticmethod
+    def forward(ctx, q, k_self, v_self, k_ar, v_ar, limits, block_size, scale):
+        tensors, meta = _prepare(q, k_self, v_self, k_ar, v_ar, limits, block_size, scale)
+        out, lse = _launch_fwd(tensors, meta, want_lse=True)
+        ctx.save_for_backward(*tensors, out, lse)
+        ctx.meta = meta
+        ctx.dtypes = (q.dtype, k_self.dtype, v_self.dtype)
+        return out
+
+    @staticmethod
+    def backward(ctx, d_out):
+        qc, ks, vs, ka, va, lim, out, lse = ctx.saved_tensors
+        stride, B, H, Hkv, Ld, K, ar_len, D, scale = ctx.meta
+        dev = qc.device
+        do = d_out.detach().to(torch.bfloat16).contiguous()
+        dq = torch.empty(B, H, Ld, D, dtype=torch.float32, device=dev)
+        dk = torch.empty(B, Hkv, Ld, D, dtype=torch.float32, device=dev)
+        dv = torch.empty(B, Hkv, Ld, D, dtype=torch.float32, device=dev)
+        call("klg_block_attn_bwd", _ptr(qc), _ptr(ks), _ptr(vs), _ptr(ka), _ptr(va), stride, _ptr(lim), _ptr(out),
+             _ptr(lse), _ptr(do), B, H, Hkv, Ld, K, ar_len, D, float(scale), _ptr(dq), _ptr(dk), _ptr(dv), _stream(dev))
+        return dq.to(ctx.dtypes[0]), dk.to(ctx.dtypes[1]), dv.to(ctx.dtypes[2]), None, None, None, None, None
 
 
 def triton_block_attention(q, k_self, v_self, k_ar, v_ar, limits, B, H, Hkv, ng, BG, n_blocks, K, ar_len, D):

@@ -461,4 +461,331 @@ block_attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_consta
   if (warp == 1) tmem_dealloc(tmem, ATT_TMEM_COLS);
 }
 
+
+// =====================================================================================
+// Backward (training the diffusion heads): dQ, and dK / dV of the block's own keys.
+//
+// Per unit (batch b, KV head, group of hg query heads sharing it, block) one CTA walks the
+// key tiles of the forward -- the AR tiles the block's limits reach, then the block's own K
+// keys -- with the forward's row log-sum-exps: S = Q K^T and dP = dO V^T (tcgen05, TMEM),
+// then softmax warps (one query row per thread) form P = 2^(s sl2 - lse2) on the visible keys
+// and dS = P (dP - D), D = rowsum(dO O), as bf16 tiles in shared memory; the MMA warp
+// accumulates dQ += dS K in TMEM across tiles and, on the block's own tile, dV = P^T dO and
+// dK = dS^T Q (the unit's rows cover every query head of the group, so these sum over the
+// heads sharing the KV head).  The AR cache gets no gradient: it comes from the frozen
+// backbone (the reference's Triton backward, triton_kernels.py:73-141 / 161-172, returns
+// none for it either).  dq and the self keys' dk / dv are fp32; with more than one head group
+// per KV head the units add into dk / dv (the host zeroes them first).
+// =====================================================================================
+constexpr int ATB_STAGES = 2;
+constexpr int ATB_THREADS = 320;                       // warp 0 TMA, warp 1 MMA, warps 2-9 softmax
+constexpr int ATB_SMEM = 1024 + 2 * ATT_Q_BYTES + 2 * ATT_P_BYTES + ATB_STAGES * 2 * ATT_TILE_BYTES + 256;
+constexpr int ATB_S_COL = 0, ATB_DP_COL = 128, ATB_DQ_COL = 256, ATB_DV_COL = 320, ATB_DK_COL = 384;
+
+struct AttnBwdArgs {
+  const int* limits;          // [B, Ld]
+  const __nv_bfloat16* out;   // forward output O [B, H, Ld, 64]
+  const __nv_bfloat16* dout;  // upstream gradient dO [B, H, Ld, 64]
+  const float* lse;           // forward log-sum-exp [B, H, Ld], natural log
+  float* dq;                  // [B, H, Ld, 64]
+  float* dk;                  // [B, Hkv, Ld, 64] (self keys)
+  float* dv;                  // [B, Hkv, Ld, 64]
+  int B, H, Hkv, Ld, K, ar_len;
+  int ng, hg, n_hg, nb, n_units;
+  float scale;                // softmax scale (scores = scale q k)
+  float sl2;                  // scale * log2(e)
+  int accumulate_kv;          // 1: add into dk / dv (several head groups per KV head)
+};
+
+__device__ __forceinline__ void attn_bwd_unit(const AttnBwdArgs& a, int u, int& b, int& hkv, int& hgi, int& blk) {
+  blk = a.nb - 1 - u % a.nb;
+  int r = u / a.nb;
+  hgi = r % a.n_hg;
+  r /= a.n_hg;
+  hkv = r % a.Hkv;
+  b = r / a.Hkv;
+}
+
+// Writes 32 bf16 (one row r, keys c32 * 32 .. + 31 of a 128-key tile) into a tile stored as
+// two 64-key K-major sub-tiles with the 128-byte swizzle (the forward's P layout).
+__device__ __forceinline__ void atb_store_row32(uint32_t tile, int r, int c32, const uint32_t (&pk)[16]) {
+  const uint32_t rowb = tile + (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u;
+#pragma unroll
+  for (int q8 = 0; q8 < 4; ++q8) {
+    const int chunk = c32 * 4 + q8;   // 8 keys = 16 bytes
+    st_shared_v4(rowb + (uint32_t)(chunk >> 3) * 16384u + (uint32_t)(((chunk & 7) ^ (r & 7)) << 4), pk[4 * q8],
+                 pk[4 * q8 + 1], pk[4 * q8 + 2], pk[4 * q8 + 3]);
+  }
+}
+
+__global__ void __launch_bounds__(ATB_THREADS, 1)
+block_attn_bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_do,
+                      const __grid_constant__ CUtensorMap map_ks, const __grid_constant__ CUtensorMap map_vs,
+                      const __grid_constant__ CUtensorMap map_ka, const __grid_constant__ CUtensorMap map_va,
+                      const AttnBwdArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  __shared__ int s_maxlim;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t q_s = smem_u32(smem);
+  const uint32_t do_s = q_s + ATT_Q_BYTES;
+  const uint32_t p_s = do_s + ATT_Q_BYTES;              // P tile (self tile only), two 64-key sub-tiles
+  const uint32_t ds_s = p_s + ATT_P_BYTES;              // dS tile
+  const uint32_t st_s = ds_s + ATT_P_BYTES;             // stage j: K tile, then V tile
+  const uint32_t bar0 = st_s + ATB_STAGES * 2 * ATT_TILE_BYTES;
+  const uint32_t full0 = bar0;                          // [STAGES] K + V bytes landed
+  const uint32_t empty0 = bar0 + 8u * ATB_STAGES;       // [STAGES] the stage's MMAs retired
+  const uint32_t qbar = bar0 + 16u * ATB_STAGES;        // Q and dO landed
+  const uint32_t sfull = qbar + 8u;                     // S and dP of the current tile in TMEM
+  const uint32_t pfull = sfull + 8u;                    // the softmax warps wrote P / dS and read S / dP
+  const uint32_t dsfree = pfull + 8u;                   // the MMAs reading P / dS retired
+  const uint32_t done_bar = dsfree + 8u;                // every MMA of the CTA retired
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  int b, hkv, hgi, blk;
+  attn_bwd_unit(a, blockIdx.x, b, hkv, hgi, blk);
+  const int rows = a.hg * a.K;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    s_maxlim = -1;
+    for (int s = 0; s < ATB_STAGES; ++s) {
+      mbar_init(full0 + 8u * s, 1);
+      mbar_init(empty0 + 8u * s, 1);
+    }
+    mbar_init(qbar, 1);
+    mbar_init(sfull, 1);
+    mbar_init(pfull, 8);
+    mbar_init(dsfree, 1);
+    mbar_init(done_bar, 1);
+    fence_mbar_init();
+    tma_prefetch(&map_q);
+    tma_prefetch(&map_do);
+    tma_prefetch(&map_ks);
+    tma_prefetch(&map_vs);
+    tma_prefetch(&map_ka);
+    tma_prefetch(&map_va);
+  }
+  // rows past the unit's: zero queries and upstream gradients (their P / dS rows are zero too)
+  for (int i = threadIdx.x; i < (128 - rows) * 8; i += blockDim.x) {
+    st_shared_v4(q_s + rows * 128 + i * 16, 0, 0, 0, 0);
+    st_shared_v4(do_s + rows * 128 + i * 16, 0, 0, 0, 0);
+  }
+  fence_async_shared();
+  if (warp == 1) tmem_alloc(smem_u32(&tmem_slot), ATT_TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_enter();   // inputs of this launch are complete from here on
+  if (threadIdx.x < a.K) atomicMax(&s_maxlim, a.limits[(size_t)b * a.Ld + blk * a.K + threadIdx.x]);
+  __syncthreads();
+  const uint32_t tmem = tmem_slot;
+  volatile int* abort_p = &abort_flag;
+  const int maxlim = min(s_maxlim, a.ar_len - 1);
+  const int n_ar = maxlim < 0 ? 0 : maxlim / ATT_BN + 1;   // AR tiles holding keys 0..maxlim
+  const int ntiles = n_ar + 1;                             // + the block's own keys
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (whole warp)
+    int stage = 0;
+    uint32_t phase = 0;
+    long long issued = 0;
+    if (elect_one()) {
+      mbar_arrive_expect_tx(qbar, 2u * (uint32_t)rows * 128u);
+      for (int i = 0; i < a.hg; ++i) {
+        const int h = hkv * a.ng + hgi * a.hg + i;
+        const int grow = (b * a.H + h) * a.Ld + blk * a.K;
+        tma_load_2d(q_s + i * a.K * 128, &map_q, qbar, 0, grow);
+        tma_load_2d(do_s + i * a.K * 128, &map_do, qbar, 0, grow);
+      }
+    }
+    __syncwarp();
+    for (int i = 0; i < ntiles; ++i) {
+      if (!warp_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) break;
+      if (elect_one()) {
+        const uint32_t ks = st_s + stage * 2 * ATT_TILE_BYTES;
+        const uint32_t fb = full0 + 8u * stage;
+        if (i < n_ar) {
+          mbar_arrive_expect_tx(fb, 2 * ATT_TILE_BYTES);
+          tma_load_3d(ks, &map_ka, fb, 0, i * ATT_BN, b * a.Hkv + hkv);
+          tma_load_3d(ks + ATT_TILE_BYTES, &map_va, fb, 0, i * ATT_BN, b * a.Hkv + hkv);
+        } else {
+          mbar_arrive_expect_tx(fb, (uint32_t)(2 * a.K * 128));
+          const int row = (b * a.Hkv + hkv) * a.Ld + blk * a.K;
+          tma_load_2d(ks, &map_ks, fb, 0, row);
+          tma_load_2d(ks + ATT_TILE_BYTES, &map_vs, fb, 0, row);
+        }
+      }
+      __syncwarp();
+      ++issued;
+      if (++stage == ATB_STAGES) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+    if (lane == 0) {
+      drain_loads<ATB_STAGES>(full0, stage, phase, issued);
+      mbar_wait_drain(qbar, 0);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (whole warp)
+    bool ok = warp_wait(qbar, 0, abort_p, KLG_STATUS_TIMEOUT_MMA);
+    tc_fence_after();
+    auto issue_s_dp = [&](int i) -> bool {   // S_i = Q K_i^T and dP_i = dO V_i^T
+      const int stage = i % ATB_STAGES;
+      if (!warp_wait(full0 + 8u * stage, (uint32_t)(i / ATB_STAGES) & 1u, abort_p, KLG_STATUS_TIMEOUT_MMA)) return false;
+      tc_fence_after();
+      if (elect_one()) {
+        const uint32_t idesc = make_idesc_bf16(128, i < n_ar ? ATT_BN : a.K, false, false);
+        const uint32_t ks = st_s + stage * 2 * ATT_TILE_BYTES;
+#pragma unroll
+        for (int k = 0; k < ATT_D / 16; ++k) {
+          mma_bf16(tmem + ATB_S_COL, desc_kmajor(q_s, k), desc_kmajor(ks, k), idesc, k != 0);
+          mma_bf16(tmem + ATB_DP_COL, desc_kmajor(do_s, k), desc_kmajor(ks + ATT_TILE_BYTES, k), idesc, k != 0);
+        }
+        mma_commit(sfull);
+      }
+      __syncwarp();
+      return true;
+    };
+    if (ok) ok = issue_s_dp(0);
+    for (int i = 0; ok && i < ntiles; ++i) {
+      const int stage = i % ATB_STAGES;
+      const bool self = i == n_ar;
+      const int nk = self ? a.K : ATT_BN;
+      // the softmax warps wrote P_i / dS_i and are done with S_i / dP_i in TMEM
+      if (!warp_wait(pfull, (uint32_t)i & 1u, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
+      tc_fence_after();
+      if (elect_one()) {
+        const uint32_t ks = st_s + stage * 2 * ATT_TILE_BYTES;
+        const uint32_t idesc_q = make_idesc_bf16(128, ATT_D, false, true);
+        for (int k = 0; k < nk / 16; ++k)   // dQ += dS K (K-major dS, K read MN-major)
+          mma_bf16(tmem + ATB_DQ_COL, desc_kmajor(ds_s + (k >> 2) * 16384, k & 3), desc_mnmajor(ks, k), idesc_q,
+                   (k != 0 || i != 0) ? 1u : 0u);
+        if (self) {   // dV = P^T dO, dK = dS^T Q over the unit's 128 (padded) query rows
+          const uint32_t idesc_t = make_idesc_bf16(128, ATT_D, true, true);
+#pragma unroll
+          for (int k = 0; k < 128 / 16; ++k) {
+            mma_bf16(tmem + ATB_DV_COL, make_desc_sw128(p_s + 2048u * k, 16384u, 1024u), desc_mnmajor(do_s, k),
+                     idesc_t, k != 0);
+            mma_bf16(tmem + ATB_DK_COL, make_desc_sw128(ds_s + 2048u * k, 16384u, 1024u), desc_mnmajor(q_s, k),
+                     idesc_t, k != 0);
+          }
+        }
+        mma_commit(empty0 + 8u * stage);   // K_i / V_i free once these retire
+        mma_commit(dsfree);                // P_i / dS_i free once these retire
+      }
+      __syncwarp();
+      if (i + 1 < ntiles && !(ok = issue_s_dp(i + 1))) break;
+    }
+    if (elect_one()) mma_commit(done_bar);
+    __syncwarp();
+    mbar_wait_drain(done_bar, 0);
+  } else {
+    // ------------------------------------------------------------ softmax warps (one row per thread)
+    const int q4 = warp & 3;
+    const int hf = (warp - 2) >> 2;   // key half (64 keys) of each tile
+    const int r = q4 * 32 + lane;
+    const bool live = r < rows;
+    const int h = hkv * a.ng + hgi * a.hg + (live ? r / a.K : 0);
+    const int pos = r % a.K;
+    const size_t grow = ((size_t)(b * a.H + h) * a.Ld + blk * a.K + pos);
+    const int lim = live ? min(max(a.limits[(size_t)b * a.Ld + blk * a.K + pos], -1), a.ar_len - 1) : -1;
+    const float lse2 = live ? a.lse[grow] * 1.4426950408889634f : 0.f;
+    // D = rowsum(dO * O) of the forward output
+    float D = 0.f;
+    if (live) {
+      const uint4* o4 = reinterpret_cast<const uint4*>(a.out + grow * ATT_D);
+      const uint4* d4 = reinterpret_cast<const uint4*>(a.dout + grow * ATT_D);
+#pragma unroll
+      for (int j = 0; j < ATT_D / 8; ++j) {
+        const uint4 ov = o4[j], dv = d4[j];
+        const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w}, dw[4] = {dv.x, dv.y, dv.z, dv.w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          D = fmaf(__uint_as_float(ow[t] << 16), __uint_as_float(dw[t] << 16), D);
+          D = fmaf(__uint_as_float(ow[t] & 0xFFFF0000u), __uint_as_float(dw[t] & 0xFFFF0000u), D);
+        }
+      }
+    }
+    const uint32_t lrow = tmem + ((uint32_t)(q4 * 32) << 16);
+    bool ok = true;
+    for (int i = 0; ok && i < ntiles; ++i) {
+      const bool self = i == n_ar;
+      if (!mbar_wait(sfull, (uint32_t)i & 1u, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      // P / dS of the previous tile are still MMA operands until those MMAs retire
+      if (i > 0 && !mbar_wait(dsfree, (uint32_t)(i - 1) & 1u, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        const int c32 = hf * 2 + c;                  // 32-key chunk of the 128-key tile
+        uint32_t sv[32], pv[32];
+        tmem_ld32_raw(lrow + ATB_S_COL + c32 * 32, sv);
+        tmem_ld32_raw(lrow + ATB_DP_COL + c32 * 32, pv);
+        tmem_wait_ld_regs(sv, pv);
+        uint32_t pp[16], dd[16];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          const int key0 = c32 * 32 + j;             // key index within the tile
+          const bool v0 = live && (self ? key0 < a.K : i * ATT_BN + key0 <= lim);
+          const bool v1 = live && (self ? key0 + 1 < a.K : i * ATT_BN + key0 + 1 <= lim);
+          const float p0 = v0 ? ex2(fmaf(__uint_as_float(sv[j]), a.sl2, -lse2)) : 0.f;
+          const float p1 = v1 ? ex2(fmaf(__uint_as_float(sv[j + 1]), a.sl2, -lse2)) : 0.f;
+          const float d0 = p0 * (__uint_as_float(pv[j]) - D);
+          const float d1 = p1 * (__uint_as_float(pv[j + 1]) - D);
+          pp[j / 2] = pack_bf16x2(p0, p1);
+          dd[j / 2] = pack_bf16x2(d0, d1);
+        }
+        atb_store_row32(ds_s, r, c32, dd);
+        if (self) atb_store_row32(p_s, r, c32, pp);
+      }
+      tc_fence_before();
+      fence_async_shared();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pfull);
+    }
+    // dQ (this warp's 32 of the 64 columns), and dK / dV of the block's own keys
+    const bool fin = mbar_wait(done_bar, 0, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE);
+    tc_fence_after();
+    if (fin && ok) {
+      uint32_t v[32];
+      tmem_ld32_raw(lrow + ATB_DQ_COL + hf * 32, v);
+      tmem_wait_ld_regs(v);
+      if (live) {
+        float4* dst = reinterpret_cast<float4*>(a.dq + grow * ATT_D + hf * 32);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          dst[j] = make_float4(__uint_as_float(v[4 * j]) * a.scale, __uint_as_float(v[4 * j + 1]) * a.scale,
+                               __uint_as_float(v[4 * j + 2]) * a.scale, __uint_as_float(v[4 * j + 3]) * a.scale);
+      }
+      const int key = r;   // TMEM lane of dK / dV = the block's key index
+      const size_t krow = ((size_t)(b * a.Hkv + hkv) * a.Ld + blk * a.K + key);
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        tmem_ld32_raw(lrow + (t ? ATB_DK_COL : ATB_DV_COL) + hf * 32, v);
+        tmem_wait_ld_regs(v);
+        if (key < a.K) {
+          float* dst = (t ? a.dk : a.dv) + krow * ATT_D + hf * 32;
+          const float sc = t ? a.scale : 1.f;
+          if (a.accumulate_kv) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) atomicAdd(dst + j, __uint_as_float(v[j]) * sc);
+          } else {
+            float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              d4[j] = make_float4(__uint_as_float(v[4 * j]) * sc, __uint_as_float(v[4 * j + 1]) * sc,
+                                  __uint_as_float(v[4 * j + 2]) * sc, __uint_as_float(v[4 * j + 3]) * sc);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();   // every MMA retired (done_bar) before TMEM is freed
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, ATT_TMEM_COLS);
+}
+
 }  // namespace klg

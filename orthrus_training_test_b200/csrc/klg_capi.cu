@@ -1768,6 +1768,66 @@ int klg_block_attn_splits(int64_t batch, int64_t heads, int64_t kv_heads, int64_
   return P.a.splits;
 }
 
+int klg_block_attn_bwd(const void* q, const void* k_self, const void* v_self, const void* k_ar, const void* v_ar,
+                       int64_t ar_stride, const int32_t* limits, const void* out, const float* lse, const void* d_out,
+                       int64_t batch, int64_t heads, int64_t kv_heads, int64_t diff_len, int64_t block, int64_t ar_len,
+                       int64_t head_dim, float scale, float* d_q, float* d_k_self, float* d_v_self, void* stream) {
+  if (!q || !k_self || !v_self || !k_ar || !v_ar || !limits || !out || !lse || !d_out || !d_q || !d_k_self || !d_v_self)
+    return fail(KLG_ERR_ARG, "null pointer");
+  AttnPlan P;
+  int rc = attn_plan(batch, heads, kv_heads, diff_len, block, ar_len, head_dim, P);
+  if (rc) return rc;
+  if (ar_stride < ar_len) return fail(KLG_ERR_ARG, "ar_stride %lld < ar_len %lld", (long long)ar_stride, (long long)ar_len);
+  if (!(scale > 0.f) || !std::isfinite(scale)) return fail(KLG_ERR_ARG, "scale must be finite and > 0");
+  for (const void* p : {q, k_self, v_self, k_ar, v_ar, out, d_out, (const void*)d_q, (const void*)d_k_self,
+                        (const void*)d_v_self})
+    if (!aligned16(p)) return fail(KLG_ERR_ALIGN, "q/k/v/out/gradients must be 16-byte aligned");
+  if ((rc = bind_device(q))) return rc;
+  NvtxRange nvtx_range("klg_block_attn_bwd");
+  cudaStream_t s = (cudaStream_t)stream;
+  const klg::AttnArgs& f = P.a;
+  klg::AttnBwdArgs a{};
+  a.limits = limits;
+  a.out = static_cast<const __nv_bfloat16*>(out);
+  a.dout = static_cast<const __nv_bfloat16*>(d_out);
+  a.lse = lse;
+  a.dq = d_q;
+  a.dk = d_k_self;
+  a.dv = d_v_self;
+  a.B = f.B; a.H = f.H; a.Hkv = f.Hkv; a.Ld = f.Ld; a.K = f.K; a.ar_len = f.ar_len;
+  a.ng = f.ng; a.hg = f.hg; a.n_hg = f.n_hg; a.nb = f.nb; a.n_units = f.n_units;
+  a.scale = scale;
+  a.sl2 = scale * 1.4426950408889634f;
+  a.accumulate_kv = f.n_hg > 1;
+  if (a.accumulate_kv) {   // several head groups add into the same self keys' dk / dv
+    const long long n4 = (long long)batch * kv_heads * diff_len * head_dim / 4;
+    for (float* buf : {d_k_self, d_v_self}) {
+      const int blocks = (int)std::min<long long>(cdiv(n4, 256), 4ll * num_sms());
+      cudaError_t ze = launch_k(klg::zero_f32x4_kernel, dim3(blocks), dim3(256), 0, s, 1, reinterpret_cast<float4*>(buf), n4);
+      if (ze != cudaSuccess) return cuda_fail(ze, "launch zero_f32x4_kernel");
+      ++g_launches;
+    }
+  }
+  const int D = klg::ATT_D;
+  alignas(64) CUtensorMap mq, mdo, mks, mvs, mka, mva;
+  if (!make_map(&mq, q, D, (uint64_t)batch * heads * diff_len, D, D, (uint32_t)block) ||
+      !make_map(&mdo, d_out, D, (uint64_t)batch * heads * diff_len, D, D, (uint32_t)block) ||
+      !make_map(&mks, k_self, D, (uint64_t)batch * kv_heads * diff_len, D, D, (uint32_t)block) ||
+      !make_map(&mvs, v_self, D, (uint64_t)batch * kv_heads * diff_len, D, D, (uint32_t)block) ||
+      !make_map_3d(&mka, k_ar, D, ar_len, (uint64_t)batch * kv_heads, D, (uint64_t)ar_stride * D, D, klg::ATT_BN) ||
+      !make_map_3d(&mva, v_ar, D, ar_len, (uint64_t)batch * kv_heads, D, (uint64_t)ar_stride * D, D, klg::ATT_BN))
+    return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+  cudaError_t e = set_smem(klg::block_attn_bwd_kernel, klg::ATB_SMEM);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(block_attn_bwd_kernel)");
+  const int slot = trace_pre(s);
+  e = launch_k(klg::block_attn_bwd_kernel, dim3(a.n_units), dim3(klg::ATB_THREADS), klg::ATB_SMEM, s, 1, mq, mdo, mks,
+               mvs, mka, mva, a);
+  trace_post(slot, s, KLG_KIND_ATTN);
+  if (e != cudaSuccess) return cuda_fail(e, "launch block_attn_bwd_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
 int klg_token_logit(const void* h, const void* w, const int32_t* tokens, int64_t n_rows, int64_t hidden, int64_t vocab,
                     float* z, void* stream) {
   if (!h || !w || !tokens || !z) return fail(KLG_ERR_ARG, "null pointer");

@@ -110,3 +110,65 @@ def test_reference_triton_api_and_fp32_inputs():
     ro, _ = O.block_attention_np(q.float().numpy(), ks.float().numpy(), vs.float().numpy(), ka.float().numpy(),
                                  va.float().numpy(), lim.numpy(), K)
     _check(out.view(B, H, Ld, 64), None, ro, None)
+
+
+# ----------------------------------------------------------------- backward
+# P and dS pass through bf16 shared-memory tiles (as the forward's P does), so the gradients
+# are compared with float64 at 3e-2 normalised max error and cosine >= 0.9995.
+BWD_MAX_REL = 3e-2
+BWD_COS = 0.9995
+
+
+def _bwd_close(ours, ref, what):
+    mr, cos = O.grad_metrics(ours, ref)
+    assert mr <= BWD_MAX_REL and cos >= BWD_COS, f"{what}: max-rel {mr:.3e} cos {cos:.6f}"
+
+
+def _run_bwd(q, ks, vs, ka, va, lim, K, d_out):
+    from orthrus_training_test_b200 import _lib
+    from orthrus_training_test_b200.attention import block_attention
+    dev = torch.device("cuda:0")
+    qd = q.to(dev, torch.bfloat16).requires_grad_(True)
+    ksd = ks.to(dev, torch.bfloat16).requires_grad_(True)
+    vsd = vs.to(dev, torch.bfloat16).requires_grad_(True)
+    out = block_attention(qd, ksd, vsd, ka.to(dev, torch.bfloat16), va.to(dev, torch.bfloat16), lim.to(dev), K)
+    out.backward(d_out.to(dev, torch.bfloat16))
+    torch.cuda.synchronize()
+    assert _lib.device_status(reset=True) == 0
+    return out, qd.grad.double().cpu().numpy(), ksd.grad.double().cpu().numpy(), vsd.grad.double().cpu().numpy()
+
+
+def test_backward_matches_reference_golden():
+    """dQ, dK_self, dV_self against gradients of the reference's attention (fixture from its
+    block mask and causal-limit rule; GQA with 3 query heads per KV head, per-position limits,
+    -1 and past-the-end limits)."""
+    g = dict(np.load(GOLDEN / "attn_block_bwd.npz"))
+    t = lambda k: torch.tensor(g[k])
+    out, dq, dks, dvs = _run_bwd(t("q"), t("k_self"), t("v_self"), t("k_ar"), t("v_ar"), t("limits"), int(g["K"]),
+                                 t("d_out"))
+    assert float((out.float().cpu() - t("out")).abs().max()) <= 3e-2
+    _bwd_close(dq, g["dq"], "dq")
+    _bwd_close(dks, g["dk_self"], "dk_self")
+    _bwd_close(dvs, g["dv_self"], "dv_self")
+
+
+@pytest.mark.parametrize("B,H,Hkv,K,NB,AL", [(1, 9, 3, 32, 8, 600), (2, 16, 2, 32, 3, 300), (1, 4, 4, 64, 2, 129),
+                                             (1, 3, 1, 128, 2, 256)])
+def test_backward_against_oracle(B, H, Hkv, K, NB, AL):
+    """SmolLM2-135M heads (9 / 3, K = 32), eight query heads per KV head (two head groups add
+    into the same dK / dV), no GQA with K = 64, and one head with K = 128; limits vary per
+    position, including -1 and the cache end."""
+    g = torch.Generator().manual_seed(B * 100 + H + K)
+    Ld = NB * K
+    q = torch.randn(B, H, Ld, 64, generator=g).to(torch.bfloat16).float()
+    ks, vs = (torch.randn(B, Hkv, Ld, 64, generator=g).to(torch.bfloat16).float() for _ in range(2))
+    ka, va = (torch.randn(B, Hkv, AL, 64, generator=g).to(torch.bfloat16).float() for _ in range(2))
+    d_out = torch.randn(B, H, Ld, 64, generator=g).to(torch.bfloat16).float()
+    lim = torch.randint(-1, AL + 5, (B, Ld), generator=g)
+    lim[0, :K] = -1
+    _, dq, dks, dvs = _run_bwd(q, ks, vs, ka, va, lim, K, d_out)
+    rq, rks, rvs = O.block_attention_bwd_np(q.numpy(), ks.numpy(), vs.numpy(), ka.numpy(), va.numpy(), lim.numpy(),
+                                            K, d_out.numpy())
+    _bwd_close(dq, rq, "dq")
+    _bwd_close(dks, rks, "dk_self")
+    _bwd_close(dvs, rvs, "dv_self")

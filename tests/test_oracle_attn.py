@@ -32,3 +32,17 @@ def test_oracle_limits_clip_and_self_keys():
     # a limit past the cache end sees the whole cache
     out2, _ = O.block_attention_np(q, ks, vs, ka, va, np.array([[-1] * 4 + [AL - 1] * 4]), K)
     np.testing.assert_allclose(out, out2, rtol=1e-12)
+
+
+def test_block_attention_backward_oracle_matches_reference_mask():
+    """The closed-form backward against gradients of the reference's attention (its own block
+    mask and causal-limit rule, a dense float64 restatement whose forward the generator
+    checked against the reference's flex-attention output)."""
+    g = dict(np.load(GOLDEN / "attn_block_bwd.npz"))
+    args = (g["q"], g["k_self"], g["v_self"], g["k_ar"], g["v_ar"], g["limits"], int(g["K"]))
+    out, lse = O.block_attention_np(*args)
+    np.testing.assert_allclose(out, g["out"], rtol=1e-10, atol=1e-12)
+    np.testing.assert_allclose(lse, g["lse"], rtol=1e-10, atol=1e-12)
+    dq, dks, dvs = O.block_attention_bwd_np(*args, g["d_out"])
+    for ours, ref in ((dq, g["dq"]), (dks, g["dk_self"]), (dvs, g["dv_self"])):
+        np.testing.assert_allclose(ours, ref, rtol=1e-9, atol=1e-11)
