@@ -63,7 +63,10 @@ SAMPLE_CONFIGS = {
     "s1": (32, 576, 49153, 1.0, "decode: one K=32 block of rows (generate.py:149-188), SmolLM2-135M lm_head "
                                "H=576, V=49153 (with the mask token), T=1 sampling"),
     "s2": (16384, 576, 49153, 1.0, "scoring: 16384 rows, H=576, V=49153, T=1 sampling"),
+    "s1f": (32, 576, 49153, 0.8, "decode with top-k 50 / top-p 0.9 (generate.py:59-73): one K=32 block of rows, "
+                                "H=576, V=49153, T=0.8"),
 }
+SAMPLE_FILTERS = {"s1f": (50, 0.9)}   # top_k, top_p of the filtered workloads
 L2_FLUSH_BYTES = 256 << 20
 
 
@@ -309,11 +312,16 @@ def run_sample(args):
     ws = torch.empty(sampling.workspace_bytes(N, V), dtype=torch.uint8, device=dev)
     seeds = iter(range(1, 1 << 30))
 
+    top_k, top_p = SAMPLE_FILTERS.get(args.config, (0, 1.0))
+    filtered = top_k > 0 or top_p < 1.0
+
     def ours(temp):
+        if filtered and temp >= sampling.GREEDY_TEMPERATURE:
+            return sampling.lm_head_sample_filtered(h, W, temp, top_k, top_p, next(seeds))
         return sampling.lm_head_sample(h, W, temp, next(seeds), workspace=ws)
 
     def torch_ref(temp):
-        return O.sample_token_torch(F.linear(h, W).float(), temp)
+        return O.sample_token_torch(F.linear(h, W).float(), temp, top_k, top_p)
 
     for _ in range(args.warmup):
         ours(T), ours(0.0), torch_ref(T), torch_ref(0.0)
@@ -337,7 +345,9 @@ def run_sample(args):
     torch.cuda.synchronize()
     trace = _lib.trace_end(4096)
     assert _lib.device_status() == 0
+    # the dominant kernel: the lm_head sweep (the filtered path runs two of them per call)
     k_ms = [t for kind, t in trace if kind == "sample"]
+    k_ms = sorted(k_ms)[len(k_ms) // 2:] if filtered else k_ms
     k_avg = sum(k_ms) / len(k_ms)
     by_kind = {}
     for kind, t in trace:
@@ -368,7 +378,10 @@ def run_sample(args):
 
     def e2e_step():
         hd = h_pin.to(dev, non_blocking=True)
-        tok, _, _ = sampling.lm_head_sample(hd, W, T, next(seeds), workspace=ws)
+        if filtered:
+            tok, _, _ = sampling.lm_head_sample_filtered(hd, W, T, top_k, top_p, next(seeds))
+        else:
+            tok, _, _ = sampling.lm_head_sample(hd, W, T, next(seeds), workspace=ws)
         tok_host.copy_(tok, non_blocking=True)
         torch.cuda.current_stream().synchronize()
 
@@ -399,6 +412,7 @@ def run_sample(args):
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) hidden, "
         "N(0,0.05) lm_head)",
         "config": {"workload": f"{args.config}: {desc}", "rows": N, "hidden": H, "vocab": V, "temperature": T,
+                   "top_k": top_k, "top_p": top_p,
                    "parallelism": "single GPU", "l2": "flushed between steps (256 MiB write)"},
         "greedy_ms_per_step": sum(ms_greedy) / args.steps,
         "torch_cublas_ms_per_step": {"sampled": sum(ms_torch) / args.steps,
@@ -420,6 +434,8 @@ ATTN_CONFIGS = {
                                   "9 heads / 3 KV heads, head_dim 64, per layer"),
     "a2": (4, 9, 3, 32, 2048, 2048, "training diffusion pass: 4 x 64 blocks of 32, each over the AR prefix "
                                     "before its anchor (model.py:400-446), per layer"),
+    "a2b": (4, 9, 3, 32, 2048, 2048, "training diffusion pass, forward + backward (dQ and the blocks' own dK / dV; "
+                                     "the AR cache is frozen): 4 x 64 blocks of 32 over their AR prefixes, per layer"),
 }
 
 
@@ -448,11 +464,19 @@ def run_attn(args):
         ks, vs = torch.randn(1, Hkv, K, 64, generator=g).numpy(), torch.randn(1, Hkv, K, 64, generator=g).numpy()
         ka, va = torch.randn(1, Hkv, AL, 64, generator=g).numpy(), torch.randn(1, Hkv, AL, 64, generator=g).numpy()
         lim = np.full((1, K), AL // 2 if Ld > K else AL - 1)
-        for _ in range(max(1, args.warmup)):
+        do = torch.randn(1, H, K, 64, generator=g).numpy()
+        train_ref = args.config.endswith("b")
+
+        def ref_step():
             O.block_attention_np(q, ks, vs, ka, va, lim, K)
+            if train_ref:
+                O.block_attention_bwd_np(q, ks, vs, ka, va, lim, K, do)
+
+        for _ in range(max(1, args.warmup)):
+            ref_step()
         t0 = time.perf_counter()
         for _ in range(args.steps):
-            O.block_attention_np(q, ks, vs, ka, va, lim, K)
+            ref_step()
         dt = time.perf_counter() - t0
         value = H * K * args.steps / dt
         emit({"metric": ATTN_METRIC, "value": value, "unit": "rows/s", "n_gpus": args.gpus, "steps": args.steps,
@@ -484,10 +508,25 @@ def run_attn(args):
     mask = torch.cat([vis_ar, vis_self], dim=2)[:, None]               # [B, 1, Ld, AL + Ld]
     k_full, v_full = torch.cat([ka, ks], dim=2), torch.cat([va, vs], dim=2)
 
+    train = args.config.endswith("b")   # forward + backward
+    d_out = bf(B, H, Ld, 64)
+    qg, ksg, vsg = (t.detach().clone().requires_grad_(True) for t in (q, ks, vs))
+
     def ours():
+        if train:
+            qg.grad = ksg.grad = vsg.grad = None
+            o = block_attention(qg, ksg, vsg, ka, va, lim_d, K)
+            o.backward(d_out)
+            return o
         return block_attention(q, ks, vs, ka, va, lim_d, K, workspace=ws)
 
     def sdpa():
+        if train:
+            qg.grad = ksg.grad = vsg.grad = None
+            kf, vf = torch.cat([ka, ksg], dim=2), torch.cat([va, vsg], dim=2)
+            o = F.scaled_dot_product_attention(qg, kf, vf, attn_mask=mask, enable_gqa=True)
+            o.backward(d_out)
+            return o
         return F.scaled_dot_product_attention(q, k_full, v_full, attn_mask=mask, enable_gqa=True)
 
     for _ in range(args.warmup):
@@ -518,9 +557,14 @@ def run_attn(args):
     tot = sum(v[0] for v in by_kind.values())
     kernels = {k: {"launches": n, "total_ms": t, "share": t / tot} for k, (t, n) in by_kind.items()}
     k_avg = by_kind["attn"][0] / by_kind["attn"][1]
-    # algorithmic work: every visible (query, key) pair costs 2 x 64 MACs (Q K and P V)
+    # algorithmic work: every visible (query, key) pair costs 2 x 64 MACs (Q K and P V) forward;
+    # the backward recomputes Q K and adds dO V^T and dS K (3 x 64 MACs; dV / dK of the blocks'
+    # own keys add 2 x 64 on those pairs); with the forward and backward launches alternating,
+    # k_avg is their mean and the work per launch is half the step's
     visible = float((lim.clamp(-1, AL - 1).long() + 1).sum()) * H + B * H * Ld * K
     flops = 4.0 * 64 * visible
+    if train:
+        flops = (4.0 * 64 * visible + 6.0 * 64 * visible + 4.0 * 64 * B * H * Ld * K) / 2
     # bytes: Q + O + every K / V row some query sees, once (the AR prefix up to the sequence's
     # largest limit, and the diffusion positions' own keys)
     ar_rows = float((lim.clamp(-1, AL - 1).long().amax(dim=1) + 1).sum()) * Hkv
@@ -543,9 +587,17 @@ def run_attn(args):
     out_h = torch.empty(B, H, Ld, 64, dtype=torch.bfloat16).pin_memory()
 
     def e2e_step():
-        o = block_attention(q_h.to(dev, non_blocking=True), ks_h.to(dev, non_blocking=True),
-                            vs_h.to(dev, non_blocking=True), ka, va, lim_d, K, workspace=ws)
-        out_h.copy_(o, non_blocking=True)
+        if train:
+            qd = q_h.to(dev, non_blocking=True).requires_grad_(True)
+            ksd = ks_h.to(dev, non_blocking=True).requires_grad_(True)
+            vsd = vs_h.to(dev, non_blocking=True).requires_grad_(True)
+            o = block_attention(qd, ksd, vsd, ka, va, lim_d, K)
+            o.backward(d_out)
+            out_h.copy_(qd.grad, non_blocking=True)   # the step's result read back: dQ
+        else:
+            o = block_attention(q_h.to(dev, non_blocking=True), ks_h.to(dev, non_blocking=True),
+                                vs_h.to(dev, non_blocking=True), ka, va, lim_d, K, workspace=ws)
+            out_h.copy_(o, non_blocking=True)
         torch.cuda.current_stream().synchronize()
 
     for _ in range(3):
@@ -558,15 +610,20 @@ def run_attn(args):
         qs = q[:1, :, sl].float().cpu().numpy()
         t_end = time.perf_counter() + min(args.cpu_seconds, 10.0)
         times = []
+        cargs = (qs, ks[:1, :, sl].float().cpu().numpy(), vs[:1, :, sl].float().cpu().numpy(),
+                 ka[:1].float().cpu().numpy(), va[:1].float().cpu().numpy(), lim[:1, sl].numpy(), K)
+        dos = d_out[:1, :, sl].float().cpu().numpy()
         while True:
             t0 = time.perf_counter()
-            O.block_attention_np(qs, ks[:1, :, sl].float().cpu().numpy(), vs[:1, :, sl].float().cpu().numpy(),
-                                 ka[:1].float().cpu().numpy(), va[:1].float().cpu().numpy(), lim[:1, sl].numpy(), K)
+            O.block_attention_np(*cargs)
+            if train:
+                O.block_attention_bwd_np(*cargs, dos)
             times.append(time.perf_counter() - t0)
             if time.perf_counter() > t_end and len(times) >= 2:
                 break
         cpu = {"value": H * K / statistics.median(times), "unit": "rows/s", "cores": 1, "kind": "port",
-               "sample": f"one block of {K} positions x {H} heads over its AR prefix: the float64 oracle"}
+               "sample": f"one block of {K} positions x {H} heads over its AR prefix: the float64 oracle"
+                         + (" forward and backward" if train else "")}
     rows = B * H * Ld
     total = sum(ms)
     emit({
@@ -576,7 +633,8 @@ def run_attn(args):
         "config": {"workload": f"{args.config}: {desc}", "batch": B, "heads": H, "kv_heads": Hkv, "block": K,
                    "diff_len": Ld, "ar_len": AL, "parallelism": "single GPU", "l2": "flushed between steps (256 MiB write)"},
         "sdpa_ms_per_step": sum(ms_sdpa) / args.steps,
-        "sdpa_what": "torch scaled_dot_product_attention with the same boolean mask and GQA, same GPU",
+        "sdpa_what": "torch scaled_dot_product_attention with the same boolean mask and GQA, same GPU"
+                     + (" (forward + autograd backward)" if train else ""),
         "roofline": roofline, "kernels": kernels, "gpu_launches": int(launches),
         "e2e": {"value": rows * args.steps / (sum(e_ms) / 1e3), "unit": "rows/s",
                 "h2d_bytes_per_step": int((q_h.numel() + ks_h.numel() + vs_h.numel()) * 2),
