@@ -246,8 +246,9 @@ int klg_lm_head_sample(const void* h, const void* w, int64_t n_rows, int64_t hid
 /* Token selection with top-k / top-p filtering (generate.py:55-75) at temperature 1 / inv_temp,
  * still without [N, V] logits.  Two sweeps over W: the first gives each row's log-sum-exp and
  * its 32-column chunk maxima, from which a per-row threshold follows that no surviving logit is
- * below (the k-th largest chunk maximum; the chunk maximum at which the chunk maxima's own
- * softmax mass passes top_p); the second collects every logit at or above it (at most `cap`
+ * below (with top-k on, the k-th largest chunk maximum, so that top-p then sees the whole top-k
+ * set; for top-p alone, the chunk maximum at which the chunk maxima's own softmax mass passes
+ * top_p); the second collects every logit at or above it (at most `cap`
  * per row).  A per-row kernel then applies the reference's rules exactly to those candidates
  * -- top-k keeps values >= the k-th largest, top-p keeps an entry while the mass strictly above
  * it is <= top_p (renormalised over the top-k survivors) -- and draws the Gumbel-max token

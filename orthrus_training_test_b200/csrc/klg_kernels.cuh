@@ -1682,8 +1682,10 @@ __device__ __forceinline__ T block_sum(T v, T* red) {
 //  top-p: the largest chunk maximum c* whose chunk maxima at or above it carry softmax mass
 //         > top_p -- the logits at or above c* then carry more than top_p, so every logit
 //         below c* has more than top_p of mass above it and top-p removes it.
-// thr[row] = the larger of the two (-inf when neither applies).  Both are found by a
-// bit-by-bit search over the order-preserving keys (32 block-wide passes).
+// thr[row] = the top-k bound when top-k is on -- top-p then renormalises over the top-k set,
+// all of which must be among the candidates -- else the top-p bound (-inf when neither
+// applies).  Both are found by a bit-by-bit search over the order-preserving keys (32
+// block-wide passes).
 __global__ void __launch_bounds__(FILT_THREADS) filter_threshold_kernel(const float* __restrict__ cmax, int n_ck,
                                                                         const float* __restrict__ lse, float inv_temp,
                                                                         int top_k, float top_p,
@@ -1705,7 +1707,7 @@ __global__ void __launch_bounds__(FILT_THREADS) filter_threshold_kernel(const fl
     }
     tk = fkey_value(T);
   }
-  if (top_p < 1.f) {
+  if (top_k == 0 && top_p < 1.f) {
     auto mass_at_or_above = [&](uint32_t T) {
       double m = 0.0;
       for (int i = threadIdx.x; i < n_ck; i += FILT_THREADS)
@@ -1721,7 +1723,7 @@ __global__ void __launch_bounds__(FILT_THREADS) filter_threshold_kernel(const fl
       tp = fkey_value(T);
     }
   }
-  if (threadIdx.x == 0) thr[row] = fmaxf(tk, tp);
+  if (threadIdx.x == 0) thr[row] = top_k > 0 ? tk : tp;
 }
 
 // Per row (one block): the filtered draw from the candidates (every logit >= the row's

@@ -131,8 +131,13 @@ def test_sample_token_wrapper_shapes_and_errors():
     torch.testing.assert_close(p.cpu().double(), ref, rtol=1e-4, atol=1e-6)
     tok1, _ = sampling.sample_token(hd[0, 0], wd, 0.0)
     assert tok1.shape == ()
-    with pytest.raises(NotImplementedError):
-        sampling.sample_token(hd, wd, 0.8, top_k=5)
+    tok, p = sampling.sample_token(hd, wd, 0.8, top_k=5, seed=2)
+    assert tok.shape == (2, 5) and p.shape == (2, 5)
+    top5 = z.topk(5, dim=-1).indices
+    assert (top5 == tok.cpu().view(-1, 1)).any(-1).all()
+    ref = torch.softmax(z.gather(1, top5) / 0.8, -1)
+    ref = ref.gather(1, (top5 == tok.cpu().view(-1, 1)).long().argmax(-1, keepdim=True)).view(2, 5)
+    torch.testing.assert_close(p.cpu().double(), ref, rtol=1e-4, atol=1e-6)
 
 
 def test_token_logprob_of_another_distribution():
