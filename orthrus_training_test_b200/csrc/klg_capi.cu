@@ -25,6 +25,7 @@
 #include "klg_kernels.cuh"
 #include "klg_attn.cuh"
 #include "klg_dzt.cuh"
+#include "klg_dzi.cuh"
 #include "klgemm.h"
 
 namespace {
@@ -355,21 +356,70 @@ int launch_dual_pair(const CUtensorMap& mhs, const CUtensorMap& mht, const CUten
   return KLG_OK;
 }
 
-// The transposed dZ kernel (klg_dzt.cuh) is pass 2's dZ kernel on the bf16 path for H >= 1536:
-// its main loop moves 20 % fewer (streamed W) to 60 % fewer (resident W) bytes per MMA cycle,
-// but its epilogue -- per-column row constants and a cross-lane reduction of the KL cross
-// term -- takes ~10k cycles a tile, hidden only behind the 24+ k-blocks of MMA of a wide row
-// (measured, dZ time per training step: H = 2048: 21.2 ms vs 22.9 ms row-major; H = 1024:
-// 30.8 vs 27.2; H = 576: 1.82 vs 1.48).  KLG_DZT=0 / 1 forces either kernel (A/B timing).
+// The transposed dZ kernel (klg_dzt.cuh) runs only with KLG_DZT=1 (A/B timing).  Its main loop
+// moves 20 % fewer (streamed W) to 60 % fewer (resident W) bytes per MMA cycle than the
+// row-major kernel, but its epilogue -- per-column row constants and a cross-lane reduction of
+// the KL cross term -- takes ~10k cycles a tile.  Measured dZ time per training step, transposed
+// / row-major / interleaved-view kernel: H = 2048: 20.5 / 21.3 / 19.0 ms; H = 1024: 30.8 / 26.1
+// / 24.0 ms; H = 576: 1.82 / 1.44 / 1.41 ms.  The interleaved-view kernel is the default.
 bool dzt_on(int64_t hidden) {
-  static const int force = [] {
+  static const bool force = [] {
     const char* v = std::getenv("KLG_DZT");
-    return v ? (v[0] == '1' ? 1 : 0) : -1;
+    return v && v[0] == '1';
   }();
-  return force >= 0 ? force == 1 : hidden >= 1536;
+  (void)hidden;
+  return force;
 }
 
 inline int64_t round8(int64_t x) { return (x + 7) & ~int64_t(7); }
+
+// The interleaved-view dZ kernel (klg_dzi.cuh) replaces the row-major one on the bf16 path
+// wherever the transposed kernel is not used.  KLG_DZI=0 keeps the row-major kernel (A/B
+// timing); KLG_DZI=2 makes a rejected interleaved map an error instead of a fallback (tests).
+int dzi_mode() {
+  static const int mode = [] {
+    const char* v = std::getenv("KLG_DZI");
+    return v ? (v[0] == '0' ? 0 : v[0] == '2' ? 2 : 1) : 1;
+  }();
+  return mode;
+}
+bool dzi_on() { return dzi_mode() > 0; }
+
+// Tensor map of both views interleaved along M: dims {H, 2 views, N rows} over the lower of the
+// two base pointers, strides {distance between the bases, 2H bytes}; a {64, 2, 64} box lands in
+// shared memory as 128 rows in (token row, view) order.  *s_view = the student's view index.
+// Fails (the caller keeps the row-major kernel) when both views are the same tensor or the
+// driver rejects the strides.
+bool dzi_map(CUtensorMap* m, const void* hs, const void* ht, int64_t n_rows, int64_t hidden, int* s_view) {
+  const uintptr_t ps = reinterpret_cast<uintptr_t>(hs), pt = reinterpret_cast<uintptr_t>(ht);
+  if (ps == pt) return false;
+  const uint64_t gap = ps < pt ? pt - ps : ps - pt;
+  if (gap % 16 != 0 || gap >= (1ull << 40)) return false;
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  *s_view = ps < pt ? 0 : 1;
+  cuuint64_t dims[3] = {(cuuint64_t)hidden, 2, (cuuint64_t)n_rows};
+  cuuint64_t strides[2] = {gap, (cuuint64_t)hidden * 2};
+  cuuint32_t box[3] = {klg::BK, 2, klg::DZI_ROWS / 2};
+  cuuint32_t es[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ps < pt ? hs : ht), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int launch_dzi(const CUtensorMap& mh, const CUtensorMap& mw, const CUtensorMap& mout, const klg::DziArgs& a,
+               cudaStream_t s) {
+  auto k = klg::dzi_pair_kernel;
+  cudaError_t e = set_smem(k, klg::DZI_SMEM);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dzi_pair_kernel)");
+  const int pairs = a.n_units < num_sms() / 2 ? a.n_units : num_sms() / 2;
+  const int slot = trace_pre(s);
+  e = launch_k(k, dim3(2 * pairs), dim3(klg::DZI_THREADS), klg::DZI_SMEM, s, 2, mh, mw, mout, a);
+  trace_post(slot, s, KLG_KIND_DZ);
+  if (e != cudaSuccess) return cuda_fail(e, "launch dzi_pair_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
 
 // Work split of a transposed dZ launch: units of g vocab pair tiles x rpu row tiles.  Picks
 // the split that fills the pairs in whole waves best, then the most row tiles per unit (the
@@ -775,6 +825,15 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
   } else if (!dual_maps(hs, ht, w, n_rows, hidden, vocab, dual_res_on(cdiv(hidden, klg::BK)), &mhs, &mht, &mw)) {
     return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
   }
+  // interleaved-view dZ kernel: both views through one 3-D map, W in 128-row halves
+  alignas(64) CUtensorMap mhi, mw256;
+  int s_view = 0;
+  bool il = false;
+  if (!split && !tr && dzi_on() && hs != ht) {
+    il = dzi_map(&mhi, hs, ht, n_rows, hidden, &s_view) &&
+         make_map(&mw256, w, hidden, vocab, hidden, klg::BK, klg::DZI_BN / 2);
+    if (!il && dzi_mode() == 2) return fail(KLG_ERR_CUDA, "interleaved-view tensor map rejected (KLG_DZI=2)");
+  }
   if (!make_map(&mw_mn, w, hidden, vocab, hidden, 32, klg::BK, CU_TENSOR_MAP_SWIZZLE_64B) ||
       !make_map(&mhs_mn, hs, hidden, n_rows, hidden, 32, klg::BK, CU_TENSOR_MAP_SWIZZLE_64B))
     return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
@@ -864,20 +923,47 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
       }
       continue;
     }
-    a.v_begin = (int)v0;
-    a.v_count = (int)wv;
-    a.n_vt = cdiv(wv, klg::DZP_BN);
-    int n_uv;
-    plan_dual(a.n_rt, a.n_vt, num_sms() / 2, a.vt_per_unit, n_uv, a_parts ? 8 : 64);
-    a.n_units = a.n_rt * n_uv;
-    a.a_part_base = n_ap;
-    n_ap += klg::DZP_CSPLIT * n_uv;   // one cross-term partial per unit and column slice
-    alignas(64) CUtensorMap mdz_out, mdz_out2;
-    if (!make_map(&mdz_out, dz, wv, n_rows, ld_dz, klg::DZP_STORE_COLS, 32, CU_TENSOR_MAP_SWIZZLE_64B) ||
-        (split && !make_map(&mdz_out2, dz + cols, wv, n_rows, ld_dz, klg::DZP_STORE_COLS, 32, CU_TENSOR_MAP_SWIZZLE_64B)))
-      return fail(KLG_ERR_CUDA, "tensor map (dz store)");
-    if (!split) mdz_out2 = mdz_out;
-    if ((rc = launch_dual_pair<klg::MODE_DZ>(mhs, mht, mw, mdz_out, mdz_out2, a, s, split))) return rc;
+    if (il) {
+      klg::DziArgs b{};
+      b.n_rows = (int)n_rows;
+      b.v_begin = (int)v0;
+      b.v_count = (int)wv;
+      b.n_rt = cdiv(n_rows, klg::DZI_ROWS);
+      b.n_vt = cdiv(wv, klg::DZI_BN);
+      int n_uv;
+      plan_dual(b.n_rt, b.n_vt, num_sms() / 2, b.vt_per_unit, n_uv, a_parts ? 8 : 64);
+      b.n_units = b.n_rt * n_uv;
+      b.n_kb = cdiv(hidden, klg::BK);
+      b.s_view = s_view;
+      b.scale_log2 = a.scale_log2;
+      b.lse = lse;
+      b.mask = mask;
+      b.count = count;
+      b.grad = grad;
+      b.inv_temp = inv_temp;
+      b.a_parts = a_parts;
+      b.a_part_base = n_ap;
+      n_ap += klg::DZI_CSPLIT * n_uv;   // one cross-term partial per unit and column half
+      alignas(64) CUtensorMap mdz_out;
+      if (!make_map(&mdz_out, dz, wv, n_rows, ld_dz, klg::DZI_STORE_COLS, 16))
+        return fail(KLG_ERR_CUDA, "tensor map (dz store)");
+      if ((rc = launch_dzi(mhi, mw256, mdz_out, b, s))) return rc;
+    } else {
+      a.v_begin = (int)v0;
+      a.v_count = (int)wv;
+      a.n_vt = cdiv(wv, klg::DZP_BN);
+      int n_uv;
+      plan_dual(a.n_rt, a.n_vt, num_sms() / 2, a.vt_per_unit, n_uv, a_parts ? 8 : 64);
+      a.n_units = a.n_rt * n_uv;
+      a.a_part_base = n_ap;
+      n_ap += klg::DZP_CSPLIT * n_uv;   // one cross-term partial per unit and column slice
+      alignas(64) CUtensorMap mdz_out, mdz_out2;
+      if (!make_map(&mdz_out, dz, wv, n_rows, ld_dz, klg::DZP_STORE_COLS, 32, CU_TENSOR_MAP_SWIZZLE_64B) ||
+          (split && !make_map(&mdz_out2, dz + cols, wv, n_rows, ld_dz, klg::DZP_STORE_COLS, 32, CU_TENSOR_MAP_SWIZZLE_64B)))
+        return fail(KLG_ERR_CUDA, "tensor map (dz store)");
+      if (!split) mdz_out2 = mdz_out;
+      if ((rc = launch_dual_pair<klg::MODE_DZ>(mhs, mht, mw, mdz_out, mdz_out2, a, s, split))) return rc;
+    }
     if (!d_hs && !d_w) continue;
     // one grouped launch per dZ plane: problem 0 = dW chunk (longer tiles first), problem 1 = dH += dZ W_chunk
     // dW's K (all rows) may be split in two, at the point that gives the shortest
@@ -909,8 +995,9 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
   return KLG_OK;
 }
 
-// Number of cross-term partial rows pass 2 writes for chunks of `cols` columns (transposed
-// kernel unless the dZ planes are split).
+// Cross-term partial rows pass 2 writes for chunks of `cols` columns, at most: the transposed
+// kernel's count when it runs, else the larger of the interleaved-view and row-major kernels'
+// (which of the two runs depends on the input pointers; run_pass2 reports the rows written).
 int pass2_parts(int64_t n_rows, int64_t hidden, int64_t vocab, int64_t cols, bool split = false) {
   int n_ap = 0;
   const int n_chunks = cdiv(vocab, cols);
@@ -922,7 +1009,12 @@ int pass2_parts(int64_t n_rows, int64_t hidden, int64_t vocab, int64_t cols, boo
     }
     int vpu, n_uv;
     plan_dual(cdiv(n_rows, 256), cdiv(wv, klg::DZP_BN), num_sms() / 2, vpu, n_uv, 8);
-    n_ap += klg::DZP_CSPLIT * n_uv;
+    int rows = klg::DZP_CSPLIT * n_uv;
+    if (!split && dzi_on()) {
+      plan_dual(cdiv(n_rows, klg::DZI_ROWS), cdiv(wv, klg::DZI_BN), num_sms() / 2, vpu, n_uv, 8);
+      rows = std::max(rows, klg::DZI_CSPLIT * n_uv);
+    }
+    n_ap += rows;
   }
   return n_ap;
 }
@@ -1078,7 +1170,7 @@ int fwd_bwd_core(const void* hs, const void* ht, const void* w, const uint8_t* m
   if ((rc = run_pass2(hs, ht, w, mask, lse, count, grad, n_rows, hidden, vocab, inv_temp, d_hs, d_w, dz,
                       L.cols, a_parts, &n_ap, s, planes == 2, chunk_events, n_events)))
     return rc;
-  if (n_ap != L.n_ap) return fail(KLG_ERR_ARG, "internal plan mismatch (cross-term partials)");
+  if (n_ap > L.n_ap) return fail(KLG_ERR_ARG, "internal plan mismatch (cross-term partials)");
   // per-row KL in 256-row blocks (block sums reuse the pass-1 partial area), then the loss
   const int nb = cdiv(n_rows, 256);
   float* block_sums = lse_parts;
@@ -1327,7 +1419,7 @@ int klg_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
   if ((rc = run_pass2(hs, ht, w, mask, lse, count, grad, n_rows, hidden, vocab, inv_temp, d_hs, d_w, dz, L.cols,
                       a_parts, &n_ap, s)))
     return rc;
-  if (n_ap != L.n_ap) return fail(KLG_ERR_ARG, "internal plan mismatch (cross-term partials)");
+  if (n_ap > L.n_ap) return fail(KLG_ERR_ARG, "internal plan mismatch (cross-term partials)");
   const int slot = trace_pre(s);
   cudaError_t e = launch_k(klg::cross_sum_kernel, dim3(cdiv(n_rows, 256)), dim3(256), 0, s, 1, a_parts, n_ap,
                            (int)n_rows, cross);
@@ -1653,6 +1745,54 @@ struct AttnPlan {
   int64_t ws_bytes;
 };
 
+// Largest cluster size (8, 4 or 2; else 1) whose CTAs of block_attn_kernel can all be resident
+// on the current device at once (cudaOccupancyMaxActiveClusters >= 1), memoised per device;
+// 8, the portable maximum, when the device cannot be queried (no device bound yet).
+int attn_max_cluster() {
+  static std::mutex mu;
+  static std::map<int, int> memo;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 8;
+  }
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = memo.find(dev);
+    if (it != memo.end()) return it->second;
+  }
+  if (set_smem(klg::block_attn_kernel, klg::ATT_SMEM) != cudaSuccess) {
+    cudaGetLastError();
+    return 8;
+  }
+  int best = 1;
+  for (int c = 8; c >= 2; c >>= 1) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(c);
+    cfg.blockDim = dim3(klg::ATT_THREADS);
+    cfg.dynamicSmemBytes = klg::ATT_SMEM;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = c;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, klg::block_attn_kernel, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      return 8;
+    }
+    if (n >= 1) {
+      best = c;
+      break;
+    }
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  memo[dev] = best;
+  return best;
+}
+
 int attn_plan(int64_t B, int64_t H, int64_t Hkv, int64_t Ld, int64_t K, int64_t ar_len, int64_t head_dim,
               AttnPlan& P) {
   if (B < 1 || H < 1 || Hkv < 1 || Ld < 1 || K < 1 || ar_len < 1)
@@ -1676,9 +1816,9 @@ int attn_plan(int64_t B, int64_t H, int64_t Hkv, int64_t Ld, int64_t K, int64_t 
   a.n_units = a.B * a.Hkv * a.n_hg * a.nb;
   const int n_ar = cdiv(ar_len, klg::ATT_BN);
   // few units (decode): split the AR keys over a cluster of up to 8 CTAs (the portable
-  // cluster size), aiming at about two CTAs per SM
+  // cluster size, or the largest that fits on the device), aiming at about two CTAs per SM
   int splits = cdiv(2 * num_sms(), a.n_units);
-  splits = std::max(1, std::min(std::min(splits, n_ar), 8));
+  splits = std::max(1, std::min(std::min(splits, n_ar), attn_max_cluster()));
   a.tps = cdiv(n_ar, splits);
   a.splits = cdiv(n_ar, a.tps);
   a.stall_split = -1;

@@ -1,0 +1,324 @@
+// Pass-2 dZ kernel with the two views interleaved along the MMA's M side (training path),
+// sm_100a.
+//
+// The row-major dZ kernel (dual_pair_kernel<MODE_DZ>) runs one MMA per view: each CTA loads
+// 128 student rows, 128 teacher rows and 64 W rows per k-block -- 40 KB per 512 MMA cycles,
+// which the TMA ring cannot keep up with (its tensor pipe idles ~17 % of the time waiting on
+// operands).  Here a CTA's 128 MMA rows are 64 token rows x 2 views, interleaved (MMA row 2r
+// and 2r + 1 are token r's student and teacher rows, in address order of the two tensors), and
+// one N = 256 MMA covers both views: a k-block costs 16 KB of rows plus 16 KB of W (128 rows)
+// per 512 MMA cycles, and two TMA copies instead of three.
+//
+// The interleave comes from one 3-D tensor map over both tensors -- {H, view, row} with the
+// view stride the distance between the two base pointers and the row stride 2H bytes -- whose
+// {64, 2, 64} box lands in shared memory as 128 rows of 64 bf16 in (row, view) order.  TMA
+// reads only the two tensors' own rows: every coordinate stays inside {H, 2, N}, and rows past
+// N are zero-filled.
+//
+// Epilogue: thread l of a TMEM lane quarter holds token row l / 2's logits of one view; the
+// lane pair (2r, 2r + 1) swaps half of a 32-column chunk with one shuffle per value, so each
+// thread ends up with both views for 16 columns and forms dZ = coef (q - p) for them.  Each warp
+// writes a 16-row x 64-column dZ block per TMA store (two 2 KB staging buffers, 128-byte swizzle)
+// and keeps its rows' KL cross term sum_v p_v (u_t - u_s), summed over the lane pair at the end
+// of a unit.
+#pragma once
+#include "klg_kernels.cuh"
+
+namespace klg {
+
+constexpr int DZI_BN = 256;                          // vocab columns per pair tile (128 W rows per CTA)
+constexpr int DZI_ROWS = 128;                        // token rows per pair tile (64 per CTA, both views)
+constexpr int DZI_A_BYTES = TILE_128x64;             // 64 token rows x 2 views x 64 (16 KB)
+constexpr int DZI_B_BYTES = (DZI_BN / 2) * BK * 2;   // 128 W rows x 64 (16 KB)
+constexpr int DZI_STAGE_BYTES = DZI_A_BYTES + DZI_B_BYTES;
+constexpr int DZI_EPI_WARPS = 8;                     // lane quarter x 128-column half
+constexpr int DZI_CSPLIT = 2;                        // cross-term partial rows per unit (column halves)
+constexpr int DZI_PW = EPI_WARP0 + DZI_EPI_WARPS;    // first extra producer warp
+#ifndef KLG_DZI_PROD
+#define KLG_DZI_PROD 2
+#endif
+constexpr int DZI_PROD = KLG_DZI_PROD;               // producer warps: warp 0 and DZI_PROD - 1 after the epilogue
+constexpr int DZI_THREADS = 32 * (DZI_PW + DZI_PROD - 1);
+constexpr int DZI_STG_BYTES = 2 * 16 * 128;          // per warp: 2 buffers x (16 token rows x 64 bf16)
+constexpr int DZI_STORE_COLS = 64;                   // columns per TMA store box (16 rows high)
+constexpr int DZI_FIXED = 1024 + DZI_EPI_WARPS * DZI_STG_BYTES + 256;
+constexpr int DZI_STAGES_RAW = (227 * 1024 - DZI_FIXED) / DZI_STAGE_BYTES;
+constexpr int DZI_STAGES = DZI_STAGES_RAW > 8 ? 8 : DZI_STAGES_RAW;
+constexpr int DZI_SMEM = DZI_FIXED + DZI_STAGES * DZI_STAGE_BYTES;
+static_assert(DZI_SMEM <= 227 * 1024, "dzi shared memory");
+
+struct DziArgs {
+  int n_rows;        // N token rows
+  int v_begin;       // first W row of this chunk
+  int v_count;       // W rows in the chunk
+  int n_rt;          // ceil(N / 128): pair row tiles
+  int n_vt;          // ceil(v_count / 256): vocab tiles
+  int vt_per_unit;   // vocab tiles per work unit
+  int n_units;       // n_rt * ceil(n_vt / vt_per_unit)
+  int n_kb;          // ceil(H / 64)
+  int s_view;        // view index (0 or 1) of the student rows in the interleaved map
+  float scale_log2;  // log2(e) / T
+  const float* lse;      // [2][N] log2-domain log-sum-exp (student, teacher)
+  const uint8_t* mask;   // [N]
+  const float* count;    // device scalar: number of valid rows (global)
+  const float* grad;     // device scalar: upstream gradient, or nullptr for 1
+  float inv_temp;
+  float* a_parts;        // optional [.][N]: cross-term partial rows a_part_base + uv * DZI_CSPLIT + half
+  int a_part_base;
+};
+
+// Units are numbered row-tile-major (the pairs running at the same time share a few row tiles
+// in L2 while each sweeps its own vocabulary range).
+__device__ __forceinline__ void dzi_unit(const DziArgs& a, int u, int& rt, int& uv, int& vt0, int& vt1) {
+  const int n_uv = (a.n_vt + a.vt_per_unit - 1) / a.vt_per_unit;
+  rt = u / n_uv;
+  uv = u - rt * n_uv;
+  vt0 = uv * a.vt_per_unit;
+  vt1 = min(vt0 + a.vt_per_unit, a.n_vt);
+}
+
+__global__ void __launch_bounds__(DZI_THREADS, 1)
+dzi_pair_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__ CUtensorMap map_w,
+                const __grid_constant__ CUtensorMap map_out, const DziArgs a) {
+  constexpr int STAGES = DZI_STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t stg0 = sbase + STAGES * DZI_STAGE_BYTES;   // 1024-aligned
+  const uint32_t bar0 = stg0 + DZI_EPI_WARPS * DZI_STG_BYTES;
+  const uint32_t full0 = bar0;
+  const uint32_t empty0 = bar0 + 8u * STAGES;
+  const uint32_t tfull0 = bar0 + 16u * STAGES;
+  const uint32_t tempty0 = tfull0 + 16u;
+  const uint32_t done_bar = tempty0 + 16u;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int cid = blockIdx.x >> 1;
+  const int n_clusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full0 + 8u * s, 2);
+      mbar_init(empty0 + 8u * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull0 + 8u * b, 1);
+      mbar_init(tempty0 + 8u * b, 2 * DZI_EPI_WARPS);
+    }
+    mbar_init(done_bar, 1);
+    fence_mbar_init();
+    tma_prefetch(&map_h);
+    tma_prefetch(&map_w);
+    tma_prefetch(&map_out);
+  }
+  if (warp == 1) tmem_alloc_pair(smem_u32(&tmem_slot), DUAL_TMEM_COLS);
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  pdl_enter();   // inputs of this launch are complete from here on
+  volatile int* abort_p = &abort_flag;
+  const uint32_t lead_full0 = mapa_shared(full0, 0);
+  const uint32_t lead_tempty0 = mapa_shared(tempty0, 0);
+  const uint32_t peer_empty0 = mapa_shared(empty0, 1);
+  const uint32_t peer_tfull0 = mapa_shared(tfull0, 1);
+
+  if (warp == 0 || warp >= DZI_PW) {
+    // ------------------------------------------------------------ TMA producers (both CTAs, whole warp)
+    // stage s belongs to producer s % DZI_PROD
+    const int prod = warp == 0 ? 0 : warp - DZI_PW + 1;
+    int stage = 0;
+    uint32_t phase = 0;
+    long long issued = 0;
+    bool ok = true;
+    for (int u = cid; ok && u < a.n_units; u += n_clusters) {
+      int rt, uv, vt0, vt1;
+      dzi_unit(a, u, rt, uv, vt0, vt1);
+      const int row0 = rt * DZI_ROWS + (int)rank * (DZI_ROWS / 2);
+      for (int vt = vt0; ok && vt < vt1; ++vt) {
+        const int wrow = a.v_begin + vt * DZI_BN + (int)rank * (DZI_BN / 2);
+        for (int kb = 0; kb < a.n_kb; ++kb) {
+          if (stage % DZI_PROD == prod) {
+            if (!warp_wait(empty0 + 8u * stage, phase ^ 1, abort_p, KLG_STATUS_TIMEOUT_PRODUCER)) { ok = false; break; }
+            if (elect_one()) {
+              const uint32_t sa = sbase + stage * DZI_STAGE_BYTES;
+              const uint32_t fb = lead_full0 + 8u * stage;
+              if (leader) mbar_arrive_expect_tx(full0 + 8u * stage, 2 * DZI_STAGE_BYTES);
+              tma_load_3d_pair(sa, &map_h, fb, kb * BK, 0, row0);
+              tma_load_2d_pair(sa + DZI_A_BYTES, &map_w, fb, kb * BK, wrow);
+              if (!leader) mbar_arrive_cluster(fb);
+            }
+            __syncwarp();
+          }
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+    if (leader && prod == 0) drain_loads<STAGES>(full0, stage, phase, issued);
+  } else if (warp == 1) {
+    if (leader) {
+      // ------------------------------------------------------------ pair MMA issuer (leader, whole warp)
+      constexpr uint32_t idesc = make_idesc_bf16(2 * BM, DZI_BN, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      int tcount = 0;
+      bool ok = true;
+      for (int u = cid; ok && u < a.n_units; u += n_clusters) {
+        int rt, uv, vt0, vt1;
+        dzi_unit(a, u, rt, uv, vt0, vt1);
+        for (int vt = vt0; ok && vt < vt1; ++vt, ++tcount) {
+          const int buf = tcount & 1;
+          const uint32_t tph = (tcount >> 1) & 1;
+          if (!warp_wait(tempty0 + 8u * buf, tph ^ 1, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d = tmem + buf * DZI_BN;
+          for (int kb = 0; kb < a.n_kb; ++kb) {
+            if (!warp_wait(full0 + 8u * stage, phase, abort_p, KLG_STATUS_TIMEOUT_MMA)) { ok = false; break; }
+            tc_fence_after();
+            if (elect_one()) {
+              const uint32_t sa = sbase + stage * DZI_STAGE_BYTES;
+#pragma unroll
+              for (int k = 0; k < BK / 16; ++k)
+                mma_bf16_pair(d, desc_kmajor(sa, k), desc_kmajor(sa + DZI_A_BYTES, k), idesc, (kb | k) != 0);
+              mma_commit_pair(empty0 + 8u * stage);
+              mma_commit_pair(peer_empty0 + 8u * stage);
+            }
+            __syncwarp();
+            if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          }
+          if (ok && elect_one()) {
+            mma_commit_pair(tfull0 + 8u * buf);
+            mma_commit_pair(peer_tfull0 + 8u * buf);
+          }
+          __syncwarp();
+        }
+      }
+      if (elect_one()) mma_commit_pair(done_bar);
+      __syncwarp();
+      mbar_wait_drain(done_bar, 0);
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue (both CTAs)
+    const int q = warp & 3;
+    const int hf = (warp - EPI_WARP0) >> 2;   // 128-column half of the tile
+    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(hf * (DZI_BN / 2));
+    const uint32_t stg = stg0 + (uint32_t)(warp - EPI_WARP0) * DZI_STG_BYTES;
+    const uint64_t pol = l2_evict_first_policy();   // dZ is streamed out once, read by the next kernel
+    const bool odd = (lane & 1) != 0;               // odd lanes take columns 16..31 of a chunk
+    const bool mine_s = (int)(lane & 1) == a.s_view;
+    const int sub = lane >> 1;                      // token row within the warp's 16
+    // 16-byte chunk k of 128-byte staging row r sits at chunk k ^ (r % 8) (128-byte swizzle)
+    const uint32_t rowoff = (uint32_t)sub * 128u;
+    const uint32_t swz = (uint32_t)(sub & 7);
+    int tcount = 0;
+    int sbuf = 0;
+    bool ok = true;
+    for (int u = cid; ok && u < a.n_units; u += n_clusters) {
+      int rt, uv, vt0, vt1;
+      dzi_unit(a, u, rt, uv, vt0, vt1);
+      const int y0 = rt * DZI_ROWS + (int)rank * (DZI_ROWS / 2) + q * 16;   // first token row of this warp
+      const int row = y0 + sub;
+      const bool row_ok = row < a.n_rows;
+      float Ls = 0.f, Lt = 0.f, coef = 0.f;
+      if (row_ok) {
+        Ls = a.lse[row];
+        Lt = a.lse[a.n_rows + row];
+        const float cnt = *a.count;
+        const float g = a.grad ? *a.grad : 1.0f;
+        coef = (a.mask[row] && cnt > 0.f) ? g / cnt * a.inv_temp : 0.f;
+      }
+      // e = 2^(u - L) of this lane's view ("me") and of the partner's ("ot"); dZ = coef (q - p)
+      const float L_me = mine_s ? Ls : Lt, L_ot = mine_s ? Lt : Ls;
+      const float c_me = mine_s ? coef : -coef;
+      const float sl2 = a.scale_log2;
+      float acc_me = 0.f, acc_ot = 0.f;   // sum e (z_me - z_ot) over valid columns, per view
+      for (int vt = vt0; ok && vt < vt1; ++vt, ++tcount) {
+        const int buf = tcount & 1;
+        const uint32_t tph = (tcount >> 1) & 1;
+        // warp-uniform outcome: the lanes exchange values by shuffles below
+        if (!warp_wait(tfull0 + 8u * buf, tph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t tbase = lane_addr + buf * DZI_BN;
+#pragma unroll 1
+        for (int cp = 0; cp < (DZI_BN / 2) / DZI_STORE_COLS; ++cp) {
+          const int x0 = vt * DZI_BN + hf * (DZI_BN / 2) + cp * DZI_STORE_COLS;   // chunk-relative column
+          if (x0 >= a.v_count) break;                                            // warp-uniform
+          // the staging buffer is free once the store issued from it two blocks ago has read it
+          if (lane == 0) bulk_wait_read1();
+          __syncwarp();
+          const uint32_t sb = stg + (uint32_t)sbuf * 2048u + rowoff;
+#pragma unroll
+          for (int c = 0; c < DZI_STORE_COLS / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld32_raw(tbase + cp * DZI_STORE_COLS + c * 32, v);
+            tmem_wait_ld_regs(v);
+            const int nvalid = a.v_count - (x0 + c * 32) - (odd ? 16 : 0);
+            float me[16], ot[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float lo = __uint_as_float(v[j]), hi = __uint_as_float(v[16 + j]);
+              ot[j] = __shfl_xor_sync(0xffffffffu, odd ? lo : hi, 1);
+              me[j] = odd ? hi : lo;
+            }
+            uint32_t pk[8];
+            if (coef == 0.f) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) pk[j] = 0u;
+            } else {
+              float am0 = 0.f, am1 = 0.f, ao0 = 0.f, ao1 = 0.f;
+#pragma unroll
+              for (int j = 0; j < 16; j += 2) {
+                const float em0 = ex2(fmaf(me[j], sl2, -L_me)), em1 = ex2(fmaf(me[j + 1], sl2, -L_me));
+                const float eo0 = ex2(fmaf(ot[j], sl2, -L_ot)), eo1 = ex2(fmaf(ot[j + 1], sl2, -L_ot));
+                pk[j / 2] = pack_bf16x2(c_me * (em0 - eo0), c_me * (em1 - eo1));
+                const float d0 = me[j] - ot[j], d1 = me[j + 1] - ot[j + 1];
+                const bool v0 = j < nvalid, v1 = j + 1 < nvalid;
+                am0 = fmaf(v0 ? em0 : 0.f, d0, am0);
+                am1 = fmaf(v1 ? em1 : 0.f, d1, am1);
+                ao0 = fmaf(v0 ? eo0 : 0.f, d0, ao0);
+                ao1 = fmaf(v1 ? eo1 : 0.f, d1, ao1);
+              }
+              acc_me += am0 + am1;
+              acc_ot += ao0 + ao1;
+            }
+            // this thread's 16 columns = 16-byte chunks k0, k0 + 1 of its staging row
+            const uint32_t k0 = (uint32_t)(c * 4 + (odd ? 2 : 0));
+            st_shared_v4(sb + ((k0 ^ swz) << 4), pk[0], pk[1], pk[2], pk[3]);
+            st_shared_v4(sb + (((k0 + 1) ^ swz) << 4), pk[4], pk[5], pk[6], pk[7]);
+          }
+          fence_async_shared();
+          __syncwarp();
+          if (lane == 0) {
+            if (y0 < a.n_rows) tma_store_2d_hint(&map_out, stg + (uint32_t)sbuf * 2048u, x0, y0, pol);
+            bulk_commit();
+          }
+          sbuf ^= 1;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (leader) mbar_arrive(tempty0 + 8u * buf);
+          else mbar_arrive_cluster(lead_tempty0 + 8u * buf);
+        }
+      }
+      // cross term p (z_t - z_s) = e_t (z_t - z_s): the student lane holds -acc_ot, the teacher lane acc_me
+      const float part = mine_s ? -acc_ot : acc_me;
+      const float cross = part + __shfl_xor_sync(0xffffffffu, part, 1);
+      if (ok && row_ok && !odd && a.a_parts)
+        a.a_parts[(size_t)(a.a_part_base + uv * DZI_CSPLIT + hf) * a.n_rows + row] = cross * sl2;
+    }
+    if (lane == 0) bulk_wait0();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem, DUAL_TMEM_COLS);
+}
+
+}  // namespace klg

@@ -1,11 +1,15 @@
-"""Both pass-2 dZ kernels against the oracle on the same problems.
+"""The three pass-2 dZ kernels against the oracle on the same problems.
 
-The library picks the transposed kernel (vocabulary on the MMA's M side, writing dZ^T) for
-H >= 1536 and the row-major dual-view kernel below that; KLG_DZT=1 / 0 forces either one.
-The choice is read once per process, so each variant runs in a child process.  Problems:
+The library runs the interleaved-view kernel (both views' rows alternating along the MMA's M
+side, read through one 3-D tensor map); KLG_DZT=1 selects the transposed kernel (vocabulary
+on the MMA's M side, writing dZ^T), KLG_DZI=0 the row-major dual-view kernel, and KLG_DZI=2 makes
+the interleaved kernel's tensor map a requirement (an error, not a fallback).  The choice is
+read once per process, so each variant runs in a child process.  Problems:
 ragged N and V (vocabulary chunks that are not multiples of the 256-row pair tile), H = 576
 (resident W in the transposed kernel), 1024 and 2048 (streamed W), T = 2 with a peaky
-teacher and masked rows, all-masked rows, and a backward chunk of 384 columns.  Tolerances
+teacher and masked rows, a backward chunk of 384 columns, both views in one buffer with the
+teacher at the lower address (the interleaved map's view order reversed), and the same tensor
+passed as both views (KL and gradients exactly 0; the interleaved kernel steps aside).  Tolerances
 as every GPU parity test: loss 1e-3 relative, gradients 2e-2 normalised max error and
 cosine >= 0.9999.
 """
@@ -45,13 +49,33 @@ for N, H, V, kw in cases:
 h_s, h_t, W, mask, T = problem(200, 576, 1500, seed=9)
 loss, dh, dw, *_ = run_oracle_np(h_s, h_t, W, mask, T)
 assert_close(run_ours(h_s, h_t, W, mask, T, workspace_bytes=4096 + 200 * 384 * 2), loss, dh, dw, "384-column chunks")
+
+from orthrus_training_test_b200 import ops
+from tests.gpu_helpers import GRAD_COS, GRAD_MAX_REL, LOSS_RTOL
+from oracle import klgemm_oracle as O
+dev = torch.device("cuda:0")
+# teacher rows at the lower address: one [2, N, H] buffer holding (h_t, h_s)
+h_s, h_t, W, mask, T = problem(259, 576, 1111, seed=11)
+loss, dh, dw, *_ = run_oracle_np(h_s, h_t, W, mask, T)
+buf = torch.stack([h_t, h_s]).to(torch.bfloat16).to(dev)
+out = ops.kl_fwd_bwd(buf[1], buf[0], W.to(torch.bfloat16).to(dev), mask.to(dev), T, need_dh=True, need_dw=True)
+torch.cuda.synchronize()
+assert abs(float(out[0]) - loss) <= LOSS_RTOL * abs(loss), (float(out[0]), loss)
+for name, ours, ref in (("dh", out[4], dh), ("dw", out[5], dw)):
+    mr, cos = O.grad_metrics(ours.double().cpu().numpy(), ref)
+    assert mr <= GRAD_MAX_REL and cos >= GRAD_COS, (name, mr, cos)
+# the same tensor as both views: KL = 0 and zero gradients, exactly
+x = h_s.to(torch.bfloat16).to(dev)
+out = ops.kl_fwd_bwd(x, x, W.to(torch.bfloat16).to(dev), mask.to(dev), T, need_dh=True, need_dw=True)
+torch.cuda.synchronize()
+assert float(out[0]) == 0.0 and not out[4].any() and not out[5].any(), float(out[0])
 print("ok")
 '''
 
 
-@pytest.mark.parametrize("force", ["0", "1"])
-def test_dz_kernel_variant_matches_oracle(force):
-    env = dict(os.environ, KLG_DZT=force)
+@pytest.mark.parametrize("dzt,dzi", [("0", "0"), ("0", "2"), ("1", "1")], ids=["row-major", "interleaved", "transposed"])
+def test_dz_kernel_variant_matches_oracle(dzt, dzi):
+    env = dict(os.environ, KLG_DZT=dzt, KLG_DZI=dzi)
     r = subprocess.run([sys.executable, "-c", CHILD, str(ROOT)], env=env, cwd=str(ROOT), capture_output=True,
                        text=True, timeout=900)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-3000:] + r.stderr[-3000:]
