@@ -375,22 +375,26 @@ inline int64_t round8(int64_t x) { return (x + 7) & ~int64_t(7); }
 
 // The interleaved-view dZ kernel (klg_dzi.cuh) replaces the row-major one on the bf16 path
 // wherever the transposed kernel is not used.  KLG_DZI=0 keeps the row-major kernel (A/B
-// timing); KLG_DZI=2 makes a rejected interleaved map an error instead of a fallback (tests).
+// timing); KLG_DZI=2 makes a rejected interleaved map an error instead of a fallback (tests);
+// KLG_DZI=3 uses the row-interleaved layout even where the 8-row-group one applies (tests).
 int dzi_mode() {
   static const int mode = [] {
     const char* v = std::getenv("KLG_DZI");
-    return v ? (v[0] == '0' ? 0 : v[0] == '2' ? 2 : 1) : 1;
+    return v ? (v[0] == '0' ? 0 : v[0] == '2' ? 2 : v[0] == '3' ? 3 : 1) : 1;
   }();
   return mode;
 }
 bool dzi_on() { return dzi_mode() > 0; }
 
-// Tensor map of both views interleaved along M: dims {H, 2 views, N rows} over the lower of the
-// two base pointers, strides {distance between the bases, 2H bytes}; a {64, 2, 64} box lands in
-// shared memory as 128 rows in (token row, view) order.  *s_view = the student's view index.
+// Tensor map of both views interleaved along M, over the lower of the two base pointers with
+// the distance between the bases as the view stride; *s_view = the student's view index.
+//  *lay = DZI_G8_S0 / _S1 (N % 8 == 0): dims {H, 8 rows, 2 views, N / 8 groups}, strides {2H
+//    bytes, gap, 16H bytes}; a {64, 8, 2, 8} box lands as 128 rows in (group, view, row) order.
+//  *lay = DZI_ROW: dims {H, 2 views, N rows}, strides {gap, 2H bytes}; a {64, 2, 64} box lands
+//    as 128 rows in (token row, view) order.
 // Fails (the caller keeps the row-major kernel) when both views are the same tensor or the
 // driver rejects the strides.
-bool dzi_map(CUtensorMap* m, const void* hs, const void* ht, int64_t n_rows, int64_t hidden, int* s_view) {
+bool dzi_map(CUtensorMap* m, const void* hs, const void* ht, int64_t n_rows, int64_t hidden, int* s_view, int* lay) {
   const uintptr_t ps = reinterpret_cast<uintptr_t>(hs), pt = reinterpret_cast<uintptr_t>(ht);
   if (ps == pt) return false;
   const uint64_t gap = ps < pt ? pt - ps : ps - pt;
@@ -398,18 +402,33 @@ bool dzi_map(CUtensorMap* m, const void* hs, const void* ht, int64_t n_rows, int
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   *s_view = ps < pt ? 0 : 1;
+  void* base = const_cast<void*>(ps < pt ? hs : ht);
+  const cuuint64_t rowb = (cuuint64_t)hidden * 2;
+  if (n_rows % 8 == 0 && dzi_mode() != 3) {
+    *lay = *s_view == 0 ? klg::DZI_G8_S0 : klg::DZI_G8_S1;
+    cuuint64_t dims[4] = {(cuuint64_t)hidden, 8, 2, (cuuint64_t)(n_rows / 8)};
+    cuuint64_t strides[3] = {rowb, gap, 8 * rowb};
+    cuuint32_t box[4] = {klg::BK, 8, 2, klg::DZI_ROWS / 16};
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  }
+  *lay = klg::DZI_ROW;
   cuuint64_t dims[3] = {(cuuint64_t)hidden, 2, (cuuint64_t)n_rows};
-  cuuint64_t strides[2] = {gap, (cuuint64_t)hidden * 2};
+  cuuint64_t strides[2] = {gap, rowb};
   cuuint32_t box[3] = {klg::BK, 2, klg::DZI_ROWS / 2};
   cuuint32_t es[3] = {1, 1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ps < pt ? hs : ht), dims, strides, box, es,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int launch_dzi(const CUtensorMap& mh, const CUtensorMap& mw, const CUtensorMap& mout, const klg::DziArgs& a,
+int launch_dzi(int lay, const CUtensorMap& mh, const CUtensorMap& mw, const CUtensorMap& mout, const klg::DziArgs& a,
                cudaStream_t s) {
-  auto k = klg::dzi_pair_kernel;
+  auto k = lay == klg::DZI_G8_S0 ? klg::dzi_pair_kernel<klg::DZI_G8_S0>
+                                 : lay == klg::DZI_G8_S1 ? klg::dzi_pair_kernel<klg::DZI_G8_S1>
+                                                         : klg::dzi_pair_kernel<klg::DZI_ROW>;
   cudaError_t e = set_smem(k, klg::DZI_SMEM);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dzi_pair_kernel)");
   const int pairs = a.n_units < num_sms() / 2 ? a.n_units : num_sms() / 2;
@@ -827,10 +846,10 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
   }
   // interleaved-view dZ kernel: both views through one 3-D map, W in 128-row halves
   alignas(64) CUtensorMap mhi, mw256;
-  int s_view = 0;
+  int s_view = 0, lay = klg::DZI_ROW;
   bool il = false;
   if (!split && !tr && dzi_on() && hs != ht) {
-    il = dzi_map(&mhi, hs, ht, n_rows, hidden, &s_view) &&
+    il = dzi_map(&mhi, hs, ht, n_rows, hidden, &s_view, &lay) &&
          make_map(&mw256, w, hidden, vocab, hidden, klg::BK, klg::DZI_BN / 2);
     if (!il && dzi_mode() == 2) return fail(KLG_ERR_CUDA, "interleaved-view tensor map rejected (KLG_DZI=2)");
   }
@@ -947,7 +966,7 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
       alignas(64) CUtensorMap mdz_out;
       if (!make_map(&mdz_out, dz, wv, n_rows, ld_dz, klg::DZI_STORE_COLS, 16))
         return fail(KLG_ERR_CUDA, "tensor map (dz store)");
-      if ((rc = launch_dzi(mhi, mw256, mdz_out, b, s))) return rc;
+      if ((rc = launch_dzi(lay, mhi, mw256, mdz_out, b, s))) return rc;
     } else {
       a.v_begin = (int)v0;
       a.v_count = (int)wv;

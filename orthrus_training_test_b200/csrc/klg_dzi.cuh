@@ -4,23 +4,29 @@
 // The row-major dZ kernel (dual_pair_kernel<MODE_DZ>) runs one MMA per view: each CTA loads
 // 128 student rows, 128 teacher rows and 64 W rows per k-block -- 40 KB per 512 MMA cycles,
 // which the TMA ring cannot keep up with (its tensor pipe idles ~17 % of the time waiting on
-// operands).  Here a CTA's 128 MMA rows are 64 token rows x 2 views, interleaved (MMA row 2r
-// and 2r + 1 are token r's student and teacher rows, in address order of the two tensors), and
-// one N = 256 MMA covers both views: a k-block costs 16 KB of rows plus 16 KB of W (128 rows)
-// per 512 MMA cycles, and two TMA copies instead of three.
+// operands).  Here a CTA's 128 MMA rows are 64 token rows x 2 views, interleaved, and one
+// N = 256 MMA covers both views: a k-block costs 16 KB of rows plus 16 KB of W (128 rows) per
+// 512 MMA cycles, and two TMA copies instead of three.
 //
-// The interleave comes from one 3-D tensor map over both tensors -- {H, view, row} with the
-// view stride the distance between the two base pointers and the row stride 2H bytes -- whose
-// {64, 2, 64} box lands in shared memory as 128 rows of 64 bf16 in (row, view) order.  TMA
-// reads only the two tensors' own rows: every coordinate stays inside {H, 2, N}, and rows past
-// N are zero-filled.
+// The interleave comes from one tensor map over both tensors whose view dimension has the
+// distance between the two base pointers as its stride (view 0 = the lower address).  TMA reads
+// only the two tensors' own rows: every coordinate stays inside the map's extents, and rows past
+// N are zero-filled.  Two layouts:
 //
-// Epilogue: thread l of a TMEM lane quarter holds token row l / 2's logits of one view; the
-// lane pair (2r, 2r + 1) swaps half of a 32-column chunk with one shuffle per value, so each
-// thread ends up with both views for 16 columns and forms dZ = coef (q - p) for them.  Each warp
-// writes a 16-row x 64-column dZ block per TMA store (two 2 KB staging buffers, 128-byte swizzle)
-// and keeps its rows' KL cross term sum_v p_v (u_t - u_s), summed over the lane pair at the end
-// of a unit.
+//  DZI_G8 (N % 8 == 0): a 4-D map {H, 8 rows, 2 views, N / 8 groups}, box {64, 8, 2, 8}: MMA row
+//    16 g + 8 v + r is row r of 8-row group g in view v.  A tcgen05.ld of shape 16x256b gives each
+//    thread lanes l and l + 8 of a 16-lane group -- one token row's logits in both views, two
+//    adjacent columns per 8 -- so the epilogue works on (student, teacher) pairs in registers, with
+//    packed fp32x2 arithmetic: per pair of columns 2 FMA2 for the exponent arguments, 4 ex2, 2 for
+//    dZ, 1 bf16x2 convert, 2 for the cross term.
+//  DZI_ROW (any N): a 3-D map {H, 2 views, N rows}, box {64, 2, 64}: MMA row 2 r + v.  With the
+//    32x32b TMEM shape each thread holds one view of one token row; the lane pair (2r, 2r + 1)
+//    swaps half of a 32-column chunk with one shuffle per value.
+//
+// Either way each warp writes a 16-row x 64-column dZ block per TMA store (two 2 KB staging
+// buffers, 128-byte swizzle) and keeps its rows' KL cross term sum_v p_v (u_t - u_s), summed over
+// the threads sharing a row at the end of a unit.  Rows whose mask is off (or a batch with no
+// valid row) get dZ = 0 without the arithmetic when no row of the warp's half needs it.
 #pragma once
 #include "klg_kernels.cuh"
 
@@ -47,6 +53,11 @@ constexpr int DZI_STAGES = DZI_STAGES_RAW > 8 ? 8 : DZI_STAGES_RAW;
 constexpr int DZI_SMEM = DZI_FIXED + DZI_STAGES * DZI_STAGE_BYTES;
 static_assert(DZI_SMEM <= 227 * 1024, "dzi shared memory");
 
+// layouts of the interleaved rows (template argument of dzi_pair_kernel)
+constexpr int DZI_ROW = 0;      // MMA row 2 r + v
+constexpr int DZI_G8_S0 = 1;    // MMA row 16 g + 8 v + r, the student rows are view 0
+constexpr int DZI_G8_S1 = 2;    // as DZI_G8_S0, the student rows are view 1
+
 struct DziArgs {
   int n_rows;        // N token rows
   int v_begin;       // first W row of this chunk
@@ -56,7 +67,7 @@ struct DziArgs {
   int vt_per_unit;   // vocab tiles per work unit
   int n_units;       // n_rt * ceil(n_vt / vt_per_unit)
   int n_kb;          // ceil(H / 64)
-  int s_view;        // view index (0 or 1) of the student rows in the interleaved map
+  int s_view;        // view index (0 or 1) of the student rows (DZI_ROW; the G8 layouts fix it)
   float scale_log2;  // log2(e) / T
   const float* lse;      // [2][N] log2-domain log-sum-exp (student, teacher)
   const uint8_t* mask;   // [N]
@@ -77,9 +88,60 @@ __device__ __forceinline__ void dzi_unit(const DziArgs& a, int u, int& rt, int& 
   vt1 = min(vt0 + a.vt_per_unit, a.n_vt);
 }
 
+// Per-row constants of the dZ epilogue.  live: the row takes part in the loss (mask set, count
+// > 0); coef = g / count / T for live rows, 0 otherwise.
+struct DziRow {
+  float Ls, Lt, coef;
+  bool live;
+};
+__device__ __forceinline__ DziRow dzi_row(const DziArgs& a, int row) {
+  DziRow r{0.f, 0.f, 0.f, false};
+  if (row < a.n_rows) {
+    r.Ls = a.lse[row];
+    r.Lt = a.lse[a.n_rows + row];
+    const float cnt = *a.count;
+    r.live = a.mask[row] && cnt > 0.f;
+    const float g = a.grad ? *a.grad : 1.0f;
+    r.coef = r.live ? g / cnt * a.inv_temp : 0.f;
+  }
+  return r;
+}
+
+// G8 epilogue on one 16x256b.x4 load (32 columns): r[4k + 2 SV .. +1] are the student's logits
+// at columns 8k + 2 tq + {0, 1}, the other two the teacher's.  pk[k] = bf16x2 dZ of those
+// columns; acc (packed pair) += p (z_t - z_s) over the columns below ncol (MASK) or all of them.
+template <int SV, bool MASK>
+__device__ __forceinline__ void dzi_g8_chunk(const uint32_t (&r)[16], uint64_t sl2, uint64_t nls, uint64_t nlt,
+                                             uint64_t coef, int col0, int ncol, uint32_t (&pk)[4], uint64_t& acc) {
+  const uint64_t neg1 = f2_pack(-1.f, -1.f);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint64_t zs = f2_pack(__uint_as_float(r[4 * k + 2 * SV]), __uint_as_float(r[4 * k + 2 * SV + 1]));
+    const uint64_t zt = f2_pack(__uint_as_float(r[4 * k + 2 - 2 * SV]), __uint_as_float(r[4 * k + 3 - 2 * SV]));
+    float as0, as1, at0, at1;
+    f2_unpack(f2_fma(zs, sl2, nls), as0, as1);
+    f2_unpack(f2_fma(zt, sl2, nlt), at0, at1);
+    const float q0 = ex2(as0), q1 = ex2(as1), p0 = ex2(at0), p1 = ex2(at1);
+    const uint64_t p = f2_pack(p0, p1);
+    float d0, d1;
+    f2_unpack(f2_mul(f2_fma(p, neg1, f2_pack(q0, q1)), coef), d0, d1);
+    pk[k] = pack_bf16x2(d0, d1);
+    const uint64_t dzt = f2_sub(zt, zs);
+    if (MASK) {
+      const int c = col0 + 8 * k;
+      acc = f2_fma(f2_pack(c < ncol ? p0 : 0.f, c + 1 < ncol ? p1 : 0.f), dzt, acc);
+    } else {
+      acc = f2_fma(p, dzt, acc);
+    }
+  }
+}
+
+template <int LAY>
 __global__ void __launch_bounds__(DZI_THREADS, 1)
 dzi_pair_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__ CUtensorMap map_w,
                 const __grid_constant__ CUtensorMap map_out, const DziArgs a) {
+  constexpr bool G8 = LAY != DZI_ROW;
+  constexpr int SV = LAY == DZI_G8_S1 ? 1 : 0;
   constexpr int STAGES = DZI_STAGES;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint32_t tmem_slot;
@@ -149,7 +211,8 @@ dzi_pair_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant
               const uint32_t sa = sbase + stage * DZI_STAGE_BYTES;
               const uint32_t fb = lead_full0 + 8u * stage;
               if (leader) mbar_arrive_expect_tx(full0 + 8u * stage, 2 * DZI_STAGE_BYTES);
-              tma_load_3d_pair(sa, &map_h, fb, kb * BK, 0, row0);
+              if (G8) tma_load_4d_pair(sa, &map_h, fb, kb * BK, 0, 0, row0 / 8);
+              else tma_load_3d_pair(sa, &map_h, fb, kb * BK, 0, row0);
               tma_load_2d_pair(sa + DZI_A_BYTES, &map_w, fb, kb * BK, wrow);
               if (!leader) mbar_arrive_cluster(fb);
             }
@@ -210,108 +273,186 @@ dzi_pair_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(hf * (DZI_BN / 2));
     const uint32_t stg = stg0 + (uint32_t)(warp - EPI_WARP0) * DZI_STG_BYTES;
     const uint64_t pol = l2_evict_first_policy();   // dZ is streamed out once, read by the next kernel
-    const bool odd = (lane & 1) != 0;               // odd lanes take columns 16..31 of a chunk
-    const bool mine_s = (int)(lane & 1) == a.s_view;
-    const int sub = lane >> 1;                      // token row within the warp's 16
-    // 16-byte chunk k of 128-byte staging row r sits at chunk k ^ (r % 8) (128-byte swizzle)
-    const uint32_t rowoff = (uint32_t)sub * 128u;
-    const uint32_t swz = (uint32_t)(sub & 7);
+    const float sl2f = a.scale_log2;
     int tcount = 0;
     int sbuf = 0;
     bool ok = true;
-    for (int u = cid; ok && u < a.n_units; u += n_clusters) {
-      int rt, uv, vt0, vt1;
-      dzi_unit(a, u, rt, uv, vt0, vt1);
-      const int y0 = rt * DZI_ROWS + (int)rank * (DZI_ROWS / 2) + q * 16;   // first token row of this warp
-      const int row = y0 + sub;
-      const bool row_ok = row < a.n_rows;
-      float Ls = 0.f, Lt = 0.f, coef = 0.f;
-      if (row_ok) {
-        Ls = a.lse[row];
-        Lt = a.lse[a.n_rows + row];
-        const float cnt = *a.count;
-        const float g = a.grad ? *a.grad : 1.0f;
-        coef = (a.mask[row] && cnt > 0.f) ? g / cnt * a.inv_temp : 0.f;
-      }
-      // e = 2^(u - L) of this lane's view ("me") and of the partner's ("ot"); dZ = coef (q - p)
-      const float L_me = mine_s ? Ls : Lt, L_ot = mine_s ? Lt : Ls;
-      const float c_me = mine_s ? coef : -coef;
-      const float sl2 = a.scale_log2;
-      float acc_me = 0.f, acc_ot = 0.f;   // sum e (z_me - z_ot) over valid columns, per view
-      for (int vt = vt0; ok && vt < vt1; ++vt, ++tcount) {
-        const int buf = tcount & 1;
-        const uint32_t tph = (tcount >> 1) & 1;
-        // warp-uniform outcome: the lanes exchange values by shuffles below
-        if (!warp_wait(tfull0 + 8u * buf, tph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t tbase = lane_addr + buf * DZI_BN;
+    if (G8) {
+      // thread (t4, tq) = (lane / 4, lane % 4): token rows y0 + t4 (16-lane group 0) and y0 + 8 + t4
+      // (group 1), columns 8k + 2 tq + {0, 1} of each 32; staging rows t4 and 8 + t4
+      const int t4 = lane >> 2, tq = lane & 3;
+      const uint64_t sl2 = f2_pack(sl2f, sl2f);
+      for (int u = cid; ok && u < a.n_units; u += n_clusters) {
+        int rt, uv, vt0, vt1;
+        dzi_unit(a, u, rt, uv, vt0, vt1);
+        const int y0 = rt * DZI_ROWS + (int)rank * (DZI_ROWS / 2) + q * 16;   // first token row of this warp
+        const DziRow rA = dzi_row(a, y0 + t4), rB = dzi_row(a, y0 + 8 + t4);
+        const bool anyA = __any_sync(0xffffffffu, rA.live), anyB = __any_sync(0xffffffffu, rB.live);
+        const uint64_t nlsA = f2_pack(-rA.Ls, -rA.Ls), nltA = f2_pack(-rA.Lt, -rA.Lt);
+        const uint64_t nlsB = f2_pack(-rB.Ls, -rB.Ls), nltB = f2_pack(-rB.Lt, -rB.Lt);
+        const uint64_t cfA = f2_pack(rA.coef, rA.coef), cfB = f2_pack(rB.coef, rB.coef);
+        uint64_t accA = 0, accB = 0;   // packed (0.f, 0.f)
+        for (int vt = vt0; ok && vt < vt1; ++vt, ++tcount) {
+          const int buf = tcount & 1;
+          const uint32_t tph = (tcount >> 1) & 1;
+          if (!warp_wait(tfull0 + 8u * buf, tph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t tbase = lane_addr + buf * DZI_BN;
 #pragma unroll 1
-        for (int cp = 0; cp < (DZI_BN / 2) / DZI_STORE_COLS; ++cp) {
-          const int x0 = vt * DZI_BN + hf * (DZI_BN / 2) + cp * DZI_STORE_COLS;   // chunk-relative column
-          if (x0 >= a.v_count) break;                                            // warp-uniform
-          // the staging buffer is free once the store issued from it two blocks ago has read it
-          if (lane == 0) bulk_wait_read1();
-          __syncwarp();
-          const uint32_t sb = stg + (uint32_t)sbuf * 2048u + rowoff;
+          for (int cp = 0; cp < (DZI_BN / 2) / DZI_STORE_COLS; ++cp) {
+            const int x0 = vt * DZI_BN + hf * (DZI_BN / 2) + cp * DZI_STORE_COLS;   // chunk-relative column
+            if (x0 >= a.v_count) break;                                            // warp-uniform
+            // the staging buffer is free once the store issued from it two blocks ago has read it
+            if (lane == 0) bulk_wait_read1();
+            __syncwarp();
+            const uint32_t sb = stg + (uint32_t)sbuf * 2048u;
 #pragma unroll
-          for (int c = 0; c < DZI_STORE_COLS / 32; ++c) {
-            uint32_t v[32];
-            tmem_ld32_raw(tbase + cp * DZI_STORE_COLS + c * 32, v);
-            tmem_wait_ld_regs(v);
-            const int nvalid = a.v_count - (x0 + c * 32) - (odd ? 16 : 0);
-            float me[16], ot[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const float lo = __uint_as_float(v[j]), hi = __uint_as_float(v[16 + j]);
-              ot[j] = __shfl_xor_sync(0xffffffffu, odd ? lo : hi, 1);
-              me[j] = odd ? hi : lo;
-            }
-            uint32_t pk[8];
-            if (coef == 0.f) {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) pk[j] = 0u;
-            } else {
-              float am0 = 0.f, am1 = 0.f, ao0 = 0.f, ao1 = 0.f;
-#pragma unroll
-              for (int j = 0; j < 16; j += 2) {
-                const float em0 = ex2(fmaf(me[j], sl2, -L_me)), em1 = ex2(fmaf(me[j + 1], sl2, -L_me));
-                const float eo0 = ex2(fmaf(ot[j], sl2, -L_ot)), eo1 = ex2(fmaf(ot[j + 1], sl2, -L_ot));
-                pk[j / 2] = pack_bf16x2(c_me * (em0 - eo0), c_me * (em1 - eo1));
-                const float d0 = me[j] - ot[j], d1 = me[j + 1] - ot[j + 1];
-                const bool v0 = j < nvalid, v1 = j + 1 < nvalid;
-                am0 = fmaf(v0 ? em0 : 0.f, d0, am0);
-                am1 = fmaf(v1 ? em1 : 0.f, d1, am1);
-                ao0 = fmaf(v0 ? eo0 : 0.f, d0, ao0);
-                ao1 = fmaf(v1 ? eo1 : 0.f, d1, ao1);
+            for (int c = 0; c < DZI_STORE_COLS / 32; ++c) {
+              const uint32_t col = tbase + cp * DZI_STORE_COLS + c * 32;
+              uint32_t ra[16], rb[16];
+              if (anyA) tmem_ld16x256b_x4(col, ra);
+              if (anyB) tmem_ld16x256b_x4(col + (16u << 16), rb);
+              if (anyA && anyB) tmem_wait_ld16(ra, rb);
+              else if (anyA) tmem_wait_ld16(ra);
+              else if (anyB) tmem_wait_ld16(rb);
+              const int col0 = x0 + c * 32 + 2 * tq;     // column of r[0] (chunk-relative)
+              const bool full = x0 + c * 32 + 32 <= a.v_count;
+              uint32_t pa[4] = {0u, 0u, 0u, 0u}, pb[4] = {0u, 0u, 0u, 0u};
+              if (anyA) {
+                if (full) dzi_g8_chunk<SV, false>(ra, sl2, nlsA, nltA, cfA, col0, a.v_count, pa, accA);
+                else dzi_g8_chunk<SV, true>(ra, sl2, nlsA, nltA, cfA, col0, a.v_count, pa, accA);
               }
-              acc_me += am0 + am1;
-              acc_ot += ao0 + ao1;
+              if (anyB) {
+                if (full) dzi_g8_chunk<SV, false>(rb, sl2, nlsB, nltB, cfB, col0, a.v_count, pb, accB);
+                else dzi_g8_chunk<SV, true>(rb, sl2, nlsB, nltB, cfB, col0, a.v_count, pb, accB);
+              }
+              // 16-byte chunk j of 128-byte staging row rr sits at j ^ (rr % 8); rows t4 and 8 + t4
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const uint32_t off = ((((uint32_t)(4 * c + k)) ^ (uint32_t)t4) << 4) + 4u * tq;
+                st_shared_b32(sb + (uint32_t)t4 * 128u + off, pa[k]);
+                st_shared_b32(sb + (uint32_t)(8 + t4) * 128u + off, pb[k]);
+              }
             }
-            // this thread's 16 columns = 16-byte chunks k0, k0 + 1 of its staging row
-            const uint32_t k0 = (uint32_t)(c * 4 + (odd ? 2 : 0));
-            st_shared_v4(sb + ((k0 ^ swz) << 4), pk[0], pk[1], pk[2], pk[3]);
-            st_shared_v4(sb + (((k0 + 1) ^ swz) << 4), pk[4], pk[5], pk[6], pk[7]);
+            fence_async_shared();
+            __syncwarp();
+            if (lane == 0) {
+              if (y0 < a.n_rows) tma_store_2d_hint(&map_out, sb, x0, y0, pol);
+              bulk_commit();
+            }
+            sbuf ^= 1;
           }
-          fence_async_shared();
+          tc_fence_before();
           __syncwarp();
           if (lane == 0) {
-            if (y0 < a.n_rows) tma_store_2d_hint(&map_out, stg + (uint32_t)sbuf * 2048u, x0, y0, pol);
-            bulk_commit();
+            if (leader) mbar_arrive(tempty0 + 8u * buf);
+            else mbar_arrive_cluster(lead_tempty0 + 8u * buf);
           }
-          sbuf ^= 1;
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) {
-          if (leader) mbar_arrive(tempty0 + 8u * buf);
-          else mbar_arrive_cluster(lead_tempty0 + 8u * buf);
+        // cross term of each row: the four threads of a row (tq = 0..3) and both packed lanes
+        float a0, a1, b0, b1;
+        f2_unpack(accA, a0, a1);
+        f2_unpack(accB, b0, b1);
+        float xa = a0 + a1, xb = b0 + b1;
+        xa += __shfl_xor_sync(0xffffffffu, xa, 1);
+        xb += __shfl_xor_sync(0xffffffffu, xb, 1);
+        xa += __shfl_xor_sync(0xffffffffu, xa, 2);
+        xb += __shfl_xor_sync(0xffffffffu, xb, 2);
+        if (ok && tq == 0 && a.a_parts) {
+          float* ap = a.a_parts + (size_t)(a.a_part_base + uv * DZI_CSPLIT + hf) * a.n_rows;
+          if (y0 + t4 < a.n_rows) ap[y0 + t4] = xa * sl2f;
+          if (y0 + 8 + t4 < a.n_rows) ap[y0 + 8 + t4] = xb * sl2f;
         }
       }
-      // cross term p (z_t - z_s) = e_t (z_t - z_s): the student lane holds -acc_ot, the teacher lane acc_me
-      const float part = mine_s ? -acc_ot : acc_me;
-      const float cross = part + __shfl_xor_sync(0xffffffffu, part, 1);
-      if (ok && row_ok && !odd && a.a_parts)
-        a.a_parts[(size_t)(a.a_part_base + uv * DZI_CSPLIT + hf) * a.n_rows + row] = cross * sl2;
+    } else {
+      const bool odd = (lane & 1) != 0;               // odd lanes take columns 16..31 of a chunk
+      const bool mine_s = (int)(lane & 1) == a.s_view;
+      const int sub = lane >> 1;                      // token row within the warp's 16
+      // 16-byte chunk k of 128-byte staging row r sits at chunk k ^ (r % 8) (128-byte swizzle)
+      const uint32_t rowoff = (uint32_t)sub * 128u;
+      const uint32_t swz = (uint32_t)(sub & 7);
+      for (int u = cid; ok && u < a.n_units; u += n_clusters) {
+        int rt, uv, vt0, vt1;
+        dzi_unit(a, u, rt, uv, vt0, vt1);
+        const int y0 = rt * DZI_ROWS + (int)rank * (DZI_ROWS / 2) + q * 16;   // first token row of this warp
+        const int row = y0 + sub;
+        const DziRow rr = dzi_row(a, row);
+        const bool any = __any_sync(0xffffffffu, rr.live);
+        // e = 2^(u - L) of this lane's view ("me") and of the partner's ("ot"); dZ = coef (q - p)
+        const float L_me = mine_s ? rr.Ls : rr.Lt, L_ot = mine_s ? rr.Lt : rr.Ls;
+        const float c_me = mine_s ? rr.coef : -rr.coef;
+        float acc_me = 0.f, acc_ot = 0.f;   // sum e (z_me - z_ot) over valid columns, per view
+        for (int vt = vt0; ok && vt < vt1; ++vt, ++tcount) {
+          const int buf = tcount & 1;
+          const uint32_t tph = (tcount >> 1) & 1;
+          // warp-uniform outcome: the lanes exchange values by shuffles below
+          if (!warp_wait(tfull0 + 8u * buf, tph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t tbase = lane_addr + buf * DZI_BN;
+#pragma unroll 1
+          for (int cp = 0; cp < (DZI_BN / 2) / DZI_STORE_COLS; ++cp) {
+            const int x0 = vt * DZI_BN + hf * (DZI_BN / 2) + cp * DZI_STORE_COLS;   // chunk-relative column
+            if (x0 >= a.v_count) break;                                            // warp-uniform
+            if (lane == 0) bulk_wait_read1();
+            __syncwarp();
+            const uint32_t sb = stg + (uint32_t)sbuf * 2048u + rowoff;
+#pragma unroll
+            for (int c = 0; c < DZI_STORE_COLS / 32; ++c) {
+              uint32_t pk[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+              if (any) {
+                uint32_t v[32];
+                tmem_ld32_raw(tbase + cp * DZI_STORE_COLS + c * 32, v);
+                tmem_wait_ld_regs(v);
+                const int nvalid = a.v_count - (x0 + c * 32) - (odd ? 16 : 0);
+                float me[16], ot[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const float lo = __uint_as_float(v[j]), hi = __uint_as_float(v[16 + j]);
+                  ot[j] = __shfl_xor_sync(0xffffffffu, odd ? lo : hi, 1);
+                  me[j] = odd ? hi : lo;
+                }
+                float am0 = 0.f, am1 = 0.f, ao0 = 0.f, ao1 = 0.f;
+#pragma unroll
+                for (int j = 0; j < 16; j += 2) {
+                  const float em0 = ex2(fmaf(me[j], sl2f, -L_me)), em1 = ex2(fmaf(me[j + 1], sl2f, -L_me));
+                  const float eo0 = ex2(fmaf(ot[j], sl2f, -L_ot)), eo1 = ex2(fmaf(ot[j + 1], sl2f, -L_ot));
+                  pk[j / 2] = pack_bf16x2(c_me * (em0 - eo0), c_me * (em1 - eo1));
+                  const float d0 = me[j] - ot[j], d1 = me[j + 1] - ot[j + 1];
+                  const bool v0 = j < nvalid, v1 = j + 1 < nvalid;
+                  am0 = fmaf(v0 ? em0 : 0.f, d0, am0);
+                  am1 = fmaf(v1 ? em1 : 0.f, d1, am1);
+                  ao0 = fmaf(v0 ? eo0 : 0.f, d0, ao0);
+                  ao1 = fmaf(v1 ? eo1 : 0.f, d1, ao1);
+                }
+                acc_me += am0 + am1;
+                acc_ot += ao0 + ao1;
+              }
+              // this thread's 16 columns = 16-byte chunks k0, k0 + 1 of its staging row
+              const uint32_t k0 = (uint32_t)(c * 4 + (odd ? 2 : 0));
+              st_shared_v4(sb + ((k0 ^ swz) << 4), pk[0], pk[1], pk[2], pk[3]);
+              st_shared_v4(sb + (((k0 + 1) ^ swz) << 4), pk[4], pk[5], pk[6], pk[7]);
+            }
+            fence_async_shared();
+            __syncwarp();
+            if (lane == 0) {
+              if (y0 < a.n_rows) tma_store_2d_hint(&map_out, stg + (uint32_t)sbuf * 2048u, x0, y0, pol);
+              bulk_commit();
+            }
+            sbuf ^= 1;
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if (leader) mbar_arrive(tempty0 + 8u * buf);
+            else mbar_arrive_cluster(lead_tempty0 + 8u * buf);
+          }
+        }
+        // cross term p (z_t - z_s) = e_t (z_t - z_s): the student lane holds -acc_ot, the teacher lane acc_me
+        const float part = mine_s ? -acc_ot : acc_me;
+        const float cross = part + __shfl_xor_sync(0xffffffffu, part, 1);
+        if (ok && row < a.n_rows && !odd && a.a_parts)
+          a.a_parts[(size_t)(a.a_part_base + uv * DZI_CSPLIT + hf) * a.n_rows + row] = cross * sl2f;
+      }
     }
     if (lane == 0) bulk_wait0();
   }

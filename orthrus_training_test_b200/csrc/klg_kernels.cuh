@@ -133,9 +133,10 @@ __device__ __forceinline__ void stats_chunk(const uint32_t (&bs)[32], const uint
 
 // One 32-column chunk of dZ = coef * (2^(u_s - L_s) - 2^(u_t - L_t)) as 16 bf16 pairs,
 // and acc += sum_{j < nvalid} p_j (z_t - z_s) (raw logits; scaled by log2(e)/T later).
+// Rows outside the loss (live = false: mask off, or no valid row at all) get zeros.
 __device__ __forceinline__ void dz_chunk(const uint32_t (&bs)[32], const uint32_t (&bt)[32], int nvalid, float sl2,
-                                         float Ls, float Lt, float coef, uint32_t (&pk)[16], float& acc) {
-  if (coef == 0.f) {
+                                         float Ls, float Lt, float coef, bool live, uint32_t (&pk)[16], float& acc) {
+  if (!live) {
 #pragma unroll
     for (int j = 0; j < 16; ++j) pk[j] = 0u;
     return;
@@ -1054,12 +1055,14 @@ dual_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_consta
       const int row = rt * 256 + (int)rank * 128 + q * 32 + lane;
       const bool row_ok = row < a.n_rows;
       float Ls = 0.f, Lt = 0.f, coef = 0.f, acc = 0.f;
+      bool live = false;
       if (row_ok) {
         Ls = a.lse[row];
         Lt = a.lse[a.n_rows + row];
         const float cnt = *a.count;
         const float g = a.grad ? *a.grad : 1.0f;
-        coef = (a.mask[row] && cnt > 0.f) ? g / cnt * a.inv_temp : 0.f;
+        live = a.mask[row] && cnt > 0.f;
+        coef = live ? g / cnt * a.inv_temp : 0.f;
       }
       for (int vt = vt0; ok && vt < vt1; ++vt, ++tcount) {
         const int buf = tcount & 1;
@@ -1097,7 +1100,7 @@ dual_pair_kernel(const __grid_constant__ CUtensorMap map_hs, const __grid_consta
             }
           } else if (nvalid > 0) {
             uint32_t pk[16];
-            dz_chunk(bs, bt, nvalid, a.scale_log2, Ls, Lt, coef, pk, acc);
+            dz_chunk(bs, bt, nvalid, a.scale_log2, Ls, Lt, coef, live, pk, acc);
             // staging is free once the previous chunk's store has read it
             if (lane == 0) bulk_wait_read0();
             __syncwarp();
