@@ -786,7 +786,8 @@ int klg_fwd(const void* hs, const void* ht, const void* w, const uint8_t* mask, 
 
 // Backward workspace: [KLG_BWD_HEADER bytes, reserved][dZ chunk N x C bf16].  The header also
 // bounds the chunk count (cdiv(V, C) <= KLG_BWD_HEADER / 4) and, in the fused layout, is
-// where the pass-1 partials start.
+// where the pass-1 partials start; the training step keeps its loss kernel's completion
+// counter in the header's first word.
 #define KLG_BWD_HEADER 4096
 
 int64_t klg_bwd_chunk_cols(int64_t n_rows, int64_t vocab, int64_t workspace_bytes) {
@@ -856,7 +857,7 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
   if (!make_map(&mw_mn, w, hidden, vocab, hidden, 32, klg::BK, CU_TENSOR_MAP_SWIZZLE_64B) ||
       !make_map(&mhs_mn, hs, hidden, n_rows, hidden, 32, klg::BK, CU_TENSOR_MAP_SWIZZLE_64B))
     return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed");
-  // fp32 outputs, accumulated by TMA reduce-add from zero
+  // fp32 outputs, written by TMA stores and reduce-adds
   alignas(64) CUtensorMap mdw, mdh;
   if ((d_w && !make_map(&mdw, d_w, hidden, vocab, hidden, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_DATA_TYPE_FLOAT32)) ||
@@ -865,14 +866,20 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
     return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed (outputs)");
   if (!d_w) mdw = mhs;   // unused placeholders
   if (!d_hs) mdh = mhs;
-  // zero the fp32 gradients (H % 8 == 0, so every buffer is a whole number of float4)
-  for (int z = 0; z < 2; ++z) {
-    float* buf = z ? d_hs : d_w;
-    if (!buf) continue;
-    const long long n4 = (z ? n_rows : vocab) * hidden / 4;
+  // The GEMMs store a tile's first addend and reduce-add the later ones: dH's first addend is
+  // chunk 0's (plane 0's), a dW row's is its chunk's -- unless dW's K is split in two, whose
+  // partial sums are reduce-added onto zero in either order.  So only dW of a shape with a K
+  // split is zeroed (H % 8 == 0: a whole number of float4).
+  bool dw_split = false;
+  for (int64_t v0 = 0; d_w && v0 < vocab && !split; v0 += cols) {
+    const int64_t wv = (vocab - v0) < cols ? (vocab - v0) : cols;
+    if (pick_dw_split((int)n_rows, (int)wv, (int)hidden, bn) > 0) dw_split = true;
+  }
+  if (dw_split) {
+    const long long n4 = vocab * hidden / 4;
     const int blocks = (int)std::min<long long>(cdiv(n4, 256), 4ll * num_sms());
     const int slot = trace_pre(s);
-    cudaError_t ze = launch_k(klg::zero_f32x4_kernel, dim3(blocks), dim3(256), 0, s, 1, reinterpret_cast<float4*>(buf), n4);
+    cudaError_t ze = launch_k(klg::zero_f32x4_kernel, dim3(blocks), dim3(256), 0, s, 1, reinterpret_cast<float4*>(d_w), n4);
     trace_post(slot, s, KLG_KIND_ZERO);
     if (ze != cudaSuccess) return cuda_fail(ze, "launch zero_f32x4_kernel");
     ++g_launches;
@@ -924,11 +931,11 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
       if (d_hs || d_w) {
         // problem 0: dW chunk = dZ^T h_s (A = dZ^T, K-major); problem 1: dH += dZ W_chunk (A = dZ^T read MN-major)
         klg::PairGemmArgs g{};
-        g.p[1] = gemm_problem(d_hs != nullptr, (int)n_rows, (int)hidden, (int)wv, bn, nullptr, (int)hidden, 1, 0,
-                              (int)v0, 1, 256, 0, 0);
+        g.p[1] = gemm_problem(d_hs != nullptr, (int)n_rows, (int)hidden, (int)wv, bn, nullptr, (int)hidden,
+                              v0 > 0 ? 1 : 0, 0, (int)v0, 1, 256, 0, 0);
         const int kb_split = pick_dw_split((int)n_rows, (int)wv, (int)hidden, bn);
-        g.p[0] = gemm_problem(d_w != nullptr, (int)wv, (int)hidden, (int)n_rows, bn, nullptr, (int)hidden, 1, 0, 0, 0,
-                              256, kb_split, (int)v0);
+        g.p[0] = gemm_problem(d_w != nullptr, (int)wv, (int)hidden, (int)n_rows, bn, nullptr, (int)hidden,
+                              kb_split > 0 ? 1 : 0, 0, 0, 0, 256, kb_split, (int)v0);
         g.n_tiles = g.p[0].n_tiles + g.p[1].n_tiles;
         alignas(64) CUtensorMap mdzt_k, mdzt_mn;
         if (!make_map(&mdzt_k, dz, n_rows, wv, ld_n, klg::BK, klg::BM) ||
@@ -998,6 +1005,8 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
     g.n_tiles = g.p[0].n_tiles + g.p[1].n_tiles;
     (void)ci;
     for (int plane = 0; plane < (split ? 2 : 1); ++plane) {
+      g.p[1].accumulate = (v0 > 0 || plane > 0) ? 1 : 0;        // dH: store chunk 0's plane 0
+      g.p[0].accumulate = (kb_split > 0 || plane > 0) ? 1 : 0;  // dW rows of this chunk: store plane 0
       const __nv_bfloat16* dzp = dz + plane * cols;
       alignas(64) CUtensorMap mdz_k, mdz_mn;
       if (!make_map(&mdz_k, dzp, wv, n_rows, ld_dz, klg::BK, klg::BM) ||
@@ -1098,7 +1107,8 @@ FwdBwdLayout fwd_bwd_layout(int64_t n_rows, int64_t hidden, int64_t vocab, int64
 // (partial records into lse_parts, n_lp of them), merged into the log-sum-exps `lse` [2][N]
 // and/or one merged record `rec` [2][2N].
 int run_pass1(const void* hs, const void* ht, const void* w, int64_t n_rows, int64_t hidden, int64_t vocab,
-              float inv_temp, float* lse_parts, int n_lp, float* lse, float* rec, cudaStream_t s) {
+              float inv_temp, float* lse_parts, int n_lp, float* lse, float* rec, cudaStream_t s,
+              const uint8_t* mask = nullptr, float* count = nullptr, unsigned* done = nullptr) {
   alignas(64) CUtensorMap mhs, mht, mw;
   if (!make_map(&mhs, hs, hidden, n_rows, hidden, klg::BK, klg::BM) ||
       !make_map(&mht, ht, hidden, n_rows, hidden, klg::BK, klg::BM) ||
@@ -1121,7 +1131,9 @@ int run_pass1(const void* hs, const void* ht, const void* w, int64_t n_rows, int
   if (rc) return rc;
   const int n2 = (int)(2 * n_rows);
   const int slot = trace_pre(s);
-  cudaError_t e = launch_k(klg::lse_merge_kernel, dim3(cdiv(n2, 256)), dim3(256), 0, s, 1, lse_parts, n_lp, n2, lse, rec);
+  const int extra = (count || done) ? 1 : 0;   // the block that counts the mask / clears *done
+  cudaError_t e = launch_k(klg::lse_merge_kernel, dim3(cdiv(n2, 256) + extra), dim3(256), 0, s, 1, lse_parts, n_lp,
+                           n2, lse, rec, mask, (int)n_rows, count, done);
   trace_post(slot, s, KLG_KIND_MERGE);
   if (e != cudaSuccess) return cuda_fail(e, "launch lse_merge_kernel");
   ++g_launches;
@@ -1179,10 +1191,13 @@ int fwd_bwd_core(const void* hs, const void* ht, const void* w, const uint8_t* m
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   float* lse_parts = reinterpret_cast<float*>(ws + L.lse_parts_off);
   float* a_parts = reinterpret_cast<float*>(ws + L.a_parts_off);
-  if (!count_given && (rc = klg_count_valid(mask, n_rows, count, s))) return rc;
+  unsigned* done = reinterpret_cast<unsigned*>(ws);   // first word of the reserved header: the loss kernel's counter
 
-  // pass 1: log-sum-exp of both views on CTA pairs
-  if ((rc = run_pass1(hs, ht, w, n_rows, hidden, vocab, inv_temp, lse_parts, L.n_lp, lse, nullptr, s))) return rc;
+  // pass 1: log-sum-exp of both views on CTA pairs; the merge launch also counts the mask
+  // (unless the caller gives the count) and clears the loss kernel's completion counter
+  if ((rc = run_pass1(hs, ht, w, n_rows, hidden, vocab, inv_temp, lse_parts, L.n_lp, lse, nullptr, s, mask,
+                      count_given ? nullptr : count, done)))
+    return rc;
   // pass 2: dZ chunks (+ KL cross-term partials) and the dW / dH GEMMs
   int n_ap = 0;
   __nv_bfloat16* dz = reinterpret_cast<__nv_bfloat16*>(ws + L.dz_off);
@@ -1190,19 +1205,15 @@ int fwd_bwd_core(const void* hs, const void* ht, const void* w, const uint8_t* m
                       L.cols, a_parts, &n_ap, s, planes == 2, chunk_events, n_events)))
     return rc;
   if (n_ap > L.n_ap) return fail(KLG_ERR_ARG, "internal plan mismatch (cross-term partials)");
-  // per-row KL in 256-row blocks (block sums reuse the pass-1 partial area), then the loss
+  // per-row KL in 256-row blocks (block sums reuse the pass-1 partial area); the last block
+  // to finish forms the loss
   const int nb = cdiv(n_rows, 256);
   float* block_sums = lse_parts;
-  int slot = trace_pre(s);
+  const int slot = trace_pre(s);
   cudaError_t e = launch_k(klg::row_kl_pair_kernel, dim3(nb), dim3(256), 0, s, 1, lse, a_parts, n_ap, mask,
-                           (int)n_rows, row_kl, block_sums);
+                           (int)n_rows, row_kl, block_sums, static_cast<const float*>(count), loss, done);
   trace_post(slot, s, KLG_KIND_FINALIZE);
   if (e != cudaSuccess) return cuda_fail(e, "launch row_kl_pair_kernel");
-  ++g_launches;
-  slot = trace_pre(s);
-  e = launch_k(klg::loss_from_sums_kernel, dim3(1), dim3(1024), 0, s, 1, block_sums, nb, count, loss);
-  trace_post(slot, s, KLG_KIND_FINALIZE);
-  if (e != cudaSuccess) return cuda_fail(e, "launch loss_from_sums_kernel");
   ++g_launches;
   return KLG_OK;
 }
@@ -1405,7 +1416,8 @@ int klg_lse_merge(const float* recs, int n_rec, int64_t n_rows, float* lse, void
   cudaStream_t s = (cudaStream_t)stream;
   const int slot = trace_pre(s);
   cudaError_t e = launch_k(klg::lse_merge_kernel, dim3(cdiv(n2, 256)), dim3(256), 0, s, 1, recs, n_rec, n2, lse,
-                           static_cast<float*>(nullptr));
+                           static_cast<float*>(nullptr), static_cast<const uint8_t*>(nullptr), 0,
+                           static_cast<float*>(nullptr), static_cast<unsigned*>(nullptr));
   trace_post(slot, s, KLG_KIND_MERGE);
   if (e != cudaSuccess) return cuda_fail(e, "launch lse_merge_kernel");
   ++g_launches;

@@ -1373,7 +1373,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_consta
   } else {
     // -------------------------------------------------------------- epilogue (both CTAs)
     // Each 32 x 32 fp32 block goes through a 128-byte-swizzled staging buffer and is added
-    // into C by a TMA reduce-add (the add happens at L2; C was zeroed before the launch).
+    // into C by a TMA reduce-add (the add happens at L2), or stored when the problem's
+    // accumulate flag is 0 (the tile's first and only addend in C).
     const int q = warp & 3;
     const int hh = (warp - EPI_WARP0) >> 2;          // column half when two warps share a quarter
     constexpr int PER = (BN / 32) / (EPI / 4);       // 32-column blocks per warp and tile
@@ -1410,7 +1411,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_consta
         fence_async_shared();
         __syncwarp();
         if (lane == 0) {
-          tma_reduce_add_2d(mc, stg + (uint32_t)sbuf * 4096u, col0, P.c_row0 + row_blk);
+          if (P.accumulate) tma_reduce_add_2d(mc, stg + (uint32_t)sbuf * 4096u, col0, P.c_row0 + row_blk);
+          else tma_store_2d(mc, stg + (uint32_t)sbuf * 4096u, col0, P.c_row0 + row_blk);
           bulk_commit();
         }
         sbuf = (sbuf + 1) % Cfg::STG_BUFS;
@@ -1519,9 +1521,32 @@ __global__ void finalize_kernel(const float* __restrict__ stats, const uint8_t* 
 // Merge of n_part (m, S) records parts[n_part][2][n2] (log2 units) per row i: lse[i] = the
 // log-sum-exp (when lse is set) and/or rec = the merged record [2][n2] (when rec is set; a
 // vocab shard's record, to be gathered with the other shards' and merged again).
+// With count or done set, the grid has one block more than the rows need: that block writes
+// *count = sum(mask[0..n_rows)) (fixed order) when count is set and clears *done (the loss
+// kernel's completion counter) when done is set.
 __global__ void lse_merge_kernel(const float* __restrict__ parts, int n_part, int n2, float* __restrict__ lse,
-                                 float* __restrict__ rec) {
+                                 float* __restrict__ rec, const uint8_t* __restrict__ mask, int n_rows,
+                                 float* __restrict__ count, unsigned* __restrict__ done) {
   pdl_enter();
+  if ((count || done) && blockIdx.x == gridDim.x - 1) {
+    __shared__ int part[32];
+    if (count) {
+      int c = 0;
+      for (int r = threadIdx.x; r < n_rows; r += blockDim.x) c += mask[r] != 0;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+      if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = c;
+      __syncthreads();
+      if (threadIdx.x < 32) {
+        c = (threadIdx.x < (blockDim.x >> 5)) ? part[threadIdx.x] : 0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+        if (threadIdx.x == 0) *count = (float)c;
+      }
+    }
+    if (done && threadIdx.x == 0) *done = 0u;
+    return;
+  }
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n2) return;
   const size_t st = (size_t)n2;
@@ -1873,13 +1898,16 @@ __global__ void __launch_bounds__(FILT_THREADS) filter_select_kernel(
 }
 
 // Training-path per-row KL: KL_i = ln2 * (sum_p a_parts[p][i] + L_s,i - L_t,i) for rows
-// carrying loss (0 elsewhere: the cross term is only formed for them).  Each block
-// writes the sum of its rows' masked KL to block_sums[blockIdx.x] (fixed order).
+// carrying loss (0 elsewhere).  Each block writes the sum of its rows' masked KL to
+// block_sums[blockIdx.x]; the block that finishes last (counted on *done, which starts at 0
+// and is left at 0) forms loss = sum(block_sums) / count in a fixed order (0 when count == 0).
 __global__ void row_kl_pair_kernel(const float* __restrict__ lse, const float* __restrict__ a_parts, int n_ap,
                                    const uint8_t* __restrict__ mask, int n, float* __restrict__ row_kl,
-                                   float* __restrict__ block_sums) {
+                                   float* __restrict__ block_sums, const float* __restrict__ count,
+                                   float* __restrict__ loss, unsigned* __restrict__ done) {
   pdl_enter();
   __shared__ float part[8];
+  __shared__ bool last;
   const float ln2 = 0.69314718055994530942f;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   float kl = 0.f;
@@ -1898,30 +1926,28 @@ __global__ void row_kl_pair_kernel(const float* __restrict__ lse, const float* _
     float t = 0.f;
     for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += part[w];
     block_sums[blockIdx.x] = t;
+    __threadfence();
+    last = atomicAdd(done, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  float tot = 0.f;
+  for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) tot += __ldcg(block_sums + b);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+  __syncthreads();   // part[] is reused
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = tot;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += part[w];
+    const float c = *count;
+    *loss = c > 0.f ? t / c : 0.f;
+    *done = 0u;
   }
 }
 
-// loss = sum(block_sums) / count (0 when count == 0); one block, fixed reduction order.
-__global__ void loss_from_sums_kernel(const float* __restrict__ block_sums, int n_blocks,
-                                      const float* __restrict__ count, float* __restrict__ loss) {
-  pdl_enter();
-  __shared__ float part[32];
-  float acc = 0.f;
-  for (int i = threadIdx.x; i < n_blocks; i += blockDim.x) acc += block_sums[i];
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    acc = (threadIdx.x < (blockDim.x >> 5)) ? part[threadIdx.x] : 0.f;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (threadIdx.x == 0) {
-      const float c = *count;
-      *loss = c > 0.f ? acc / c : 0.f;
-    }
-  }
-}
 
 // Self-test of the bounded wait: one warp waits on an mbarrier that nothing arrives on.
 // mbar_wait gives up after KLG_WAIT_CYCLES, sets KLG_STATUS_SELFTEST and returns false.
