@@ -24,7 +24,9 @@ dH is all-reduced; ``value`` then counts each row once.
 ``e2e``    the same metric through the public autograd API with the step's
            inputs copied host->device (pinned) and the loss read back each step;
            the copies run on a second stream, double-buffered, so step i+1's copy
-           overlaps step i's compute.
+           overlaps step i's compute; each step's loss lands in pinned host memory
+           and the host reads it during the next step (the last one before the
+           timed region ends).
 ``--impl reference`` times the CPU restatement of the reference's loss (its
            own op sequence in fp32 torch, all host threads) on a bounded row
            sample of the same workload.
@@ -882,27 +884,34 @@ def main():
 
         # Each step copies its own inputs from pinned host memory (double-buffered on a second
         # stream, so step i+1's copy overlaps step i's compute), runs the public API and reads
-        # the loss back to the host.  The L2 flush runs before each step's compute, inside the
-        # timed region.
+        # the loss back to the host: copied into pinned memory behind the step and read by the
+        # host once that copy has landed, during the next step (the host stays one step ahead
+        # instead of idling the GPU while it waits).  The L2 flush runs before each step's
+        # compute, inside the timed region.
         copy_stream = torch.cuda.Stream(device=dev)
         slots = [(torch.empty(hs_h.shape, dtype=hs_h.dtype, device=dev), torch.empty(ht_h.shape, dtype=ht_h.dtype, device=dev),
                   torch.empty(m_h.shape, dtype=m_h.dtype, device=dev)) for _ in range(2)]
         landed = [torch.cuda.Event() for _ in range(2)]
+        used = [torch.cuda.Event() for _ in range(2)]       # the step reading slot k has finished
+        loss_h = torch.zeros(2, dtype=torch.float32).pin_memory()
+        read = [torch.cuda.Event() for _ in range(2)]       # loss_h[k] holds that step's loss
 
-        def issue_copy(k):
+        def issue_copy(k, after_use):
             with torch.cuda.stream(copy_stream):
+                if after_use:
+                    copy_stream.wait_event(used[k])
                 for d_, h_ in zip(slots[k], (hs_h, ht_h, m_h)):
                     d_.copy_(h_, non_blocking=True)
                 landed[k].record(copy_stream)
 
         def run_e2e(n):
-            issue_copy(0)
+            issue_copy(0, False)
             out = 0.0
             for i in range(n):
                 k = i & 1
                 torch.cuda.current_stream().wait_event(landed[k])
                 if i + 1 < n:
-                    issue_copy(1 - k)   # slot 1-k's previous step ended with the host read below
+                    issue_copy(1 - k, i >= 1)   # slot 1-k is refilled once step i-1 has finished with it
                 flush.zero_()
                 hs_d = slots[k][0].detach().requires_grad_(True)
                 ht_d, m_d = slots[k][1], slots[k][2]
@@ -916,8 +925,14 @@ def main():
                     loss = ops.kl_gemm_loss(hs_d, ht_d, Wp, m_d, T)
                 loss.backward()
                 Wp.grad = None
-                out = float(loss.item())                 # device -> host read of the step's result
-            return out
+                used[k].record()
+                loss_h[k].copy_(loss.detach(), non_blocking=True)   # device -> host copy of the step's result
+                read[k].record()
+                if i >= 1:
+                    read[1 - k].synchronize()
+                    out = float(loss_h[1 - k])                        # host read of step i-1's loss
+            read[(n - 1) & 1].synchronize()
+            return float(loss_h[(n - 1) & 1])
 
         run_e2e(max(3, args.warmup))
         torch.cuda.synchronize()
@@ -934,7 +949,8 @@ def main():
         e2e = {"value": rows_total / (float(et.item()) / 1e3), "unit": "rows/s", "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": 4, "ms_per_step": float(et.item()) / args.steps,
                "copies": "pinned host -> device each step on a second stream, double-buffered (step i+1's copy "
-                         "overlaps step i); L2 flushed before each step inside the timed region",
+                         "overlaps step i); each step's loss copied to pinned host memory and read by the host "
+                         "during the next step; L2 flushed before each step inside the timed region",
                "api": ("vocab_sharded_kl_loss" if vocab_sharded else "row_sharded_kl_loss" if world > 1
                        else "kl_gemm_loss (KLGemmFn autograd)")}
 

@@ -350,6 +350,11 @@ int klg_token_logit(const void* h, const void* w, const int32_t* tokens, int64_t
 /* fp32 -> bf16 conversion (round to nearest even) for fp32 callers. */
 int klg_cast_f32_bf16(const float* in, void* out, int64_t n, void* stream);
 
+/* out[i] = in[i] * (*g) (g a device float, or NULL for 1), as bf16 (out_bf16 = 1, round to
+ * nearest even) or fp32, in one pass: the scaling of the saved dH / dW by the loss's upstream
+ * gradient (torch.autograd.Function backward).  in and out 16-byte aligned. */
+int klg_scale_cast(const float* in, const float* g, int64_t n, void* out, int out_bf16, void* stream);
+
 /* ---------------------------------------------------------------- timing
  * Per-launch timing for benchmarks (the reference's counterpart is the manual
  * synchronize + perf_counter breakdown of train.py:541-547 and 676-685).

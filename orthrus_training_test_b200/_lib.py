@@ -65,6 +65,7 @@ SIGNATURES = {
     "klg_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64,
                         c_int64, c_float, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
     "klg_cast_f32_bf16": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
+    "klg_scale_cast": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_int, c_void_p]),
     "klg_fwd_bwd_workspace_bytes": (c_int64, [c_int64, c_int64, c_int64]),
     "klg_fwd_bwd_chunk_cols": (c_int64, [c_int64, c_int64, c_int64, c_int64]),
     "klg_fwd_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_float, c_int, c_void_p,

@@ -2034,6 +2034,23 @@ int klg_cast_f32_bf16(const float* in, void* out, int64_t n, void* stream) {
   return KLG_OK;
 }
 
+int klg_scale_cast(const float* in, const float* g, int64_t n, void* out, int out_bf16, void* stream) {
+  if (!in || !out || n < 0) return fail(KLG_ERR_ARG, "bad arguments to klg_scale_cast");
+  if (!aligned16(in) || !aligned16(out)) return fail(KLG_ERR_ALIGN, "klg_scale_cast: in and out must be 16-byte aligned");
+  if (n == 0) return KLG_OK;
+  if (int rc = bind_device(in)) return rc;
+  long long blocks = (n / 4 + 255) / 256;
+  if (blocks < 1) blocks = 1;
+  if (blocks > 4ll * num_sms()) blocks = 4ll * num_sms();
+  const int slot = trace_pre((cudaStream_t)stream);
+  cudaError_t e = launch_k(klg::scale_cast_kernel, dim3((int)blocks), dim3(256), 0, (cudaStream_t)stream, 1, in, g,
+                           (long long)n, out, out_bf16);
+  trace_post(slot, (cudaStream_t)stream, KLG_KIND_CAST);
+  if (e != cudaSuccess) return cuda_fail(e, "launch scale_cast_kernel");
+  ++g_launches;
+  return KLG_OK;
+}
+
 int klg_trace_begin(int capacity) {
   if (capacity < 1 || capacity > (1 << 20)) return fail(KLG_ERR_ARG, "trace capacity out of range");
   std::lock_guard<std::mutex> lk(g_trace.mu);

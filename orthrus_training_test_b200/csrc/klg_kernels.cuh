@@ -2209,4 +2209,32 @@ __global__ void cast_f32_bf16_kernel(const float* __restrict__ in, __nv_bfloat16
   for (long long j = i; j < n; j += stride) out[j] = __float2bfloat16_rn(in[j]);
 }
 
+// out = in * s with s = *g (1 when g is null): the autograd backward's scaling of a saved fp32
+// gradient by the upstream gradient, written as bf16 (out_bf16) or fp32, in one pass.  n4 = n / 4
+// float4 groups (pointers 16-byte aligned), then the n % 4 tail.
+__global__ void scale_cast_kernel(const float* __restrict__ in, const float* __restrict__ g, long long n,
+                                  void* __restrict__ out, int out_bf16) {
+  pdl_enter();
+  const float sc = g ? *g : 1.0f;
+  const long long i0 = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const long long n4 = n >> 2;
+  const float4* in4 = reinterpret_cast<const float4*>(in);
+  for (long long j = i0; j < n4; j += stride) {
+    const float4 v = in4[j];
+    if (out_bf16) {
+      uint2 o;
+      o.x = pack_bf16x2(v.x * sc, v.y * sc);
+      o.y = pack_bf16x2(v.z * sc, v.w * sc);
+      reinterpret_cast<uint2*>(out)[j] = o;
+    } else {
+      reinterpret_cast<float4*>(out)[j] = make_float4(v.x * sc, v.y * sc, v.z * sc, v.w * sc);
+    }
+  }
+  for (long long j = 4 * n4 + i0; j < n; j += stride) {
+    if (out_bf16) reinterpret_cast<__nv_bfloat16*>(out)[j] = __float2bfloat16_rn(in[j] * sc);
+    else reinterpret_cast<float*>(out)[j] = in[j] * sc;
+  }
+}
+
 }  // namespace klg

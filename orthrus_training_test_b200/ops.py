@@ -57,6 +57,18 @@ def prepare_inputs(h_s: torch.Tensor, h_t: torch.Tensor, weight: torch.Tensor):
     return to_compute_dtype(h_s), to_compute_dtype(h_t), to_compute_dtype(weight)
 
 
+def scale_grad(x: torch.Tensor, g: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """``(x * g).to(dtype)`` for a saved fp32 gradient ``x`` and the upstream gradient ``g`` (a
+    device scalar), in one pass over ``x`` (``klg_scale_cast``) for bf16 and fp32 results.  Host
+    tensors (the sharding logic's CPU test engine) use torch ops."""
+    if dtype not in (torch.bfloat16, torch.float32) or not x.is_contiguous() or not x.is_cuda:
+        return (x * g.to(torch.float32)).to(dtype)
+    out = torch.empty(x.shape, dtype=dtype, device=x.device)
+    gs = g.detach().to(device=x.device, dtype=torch.float32).reshape(1).contiguous()
+    call("klg_scale_cast", _ptr(x), _ptr(gs), x.numel(), _ptr(out), int(dtype == torch.bfloat16), _stream(x.device))
+    return out
+
+
 def to_compute_dtype(x: torch.Tensor) -> torch.Tensor:
     """bf16, contiguous.  fp32 inputs are rounded to bf16 by the library's cast kernel."""
     x = x.detach()
@@ -354,9 +366,8 @@ class KLGemmFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g):
         dh, dw = ctx.saved_tensors
-        g = g.to(torch.float32)
-        return ((dh * g).to(ctx.dtypes[0]) if dh is not None else None, None,
-                (dw * g).to(ctx.dtypes[1]) if dw is not None else None, None, None, None)
+        return (scale_grad(dh, g, ctx.dtypes[0]) if dh is not None else None, None,
+                scale_grad(dw, g, ctx.dtypes[1]) if dw is not None else None, None, None, None)
 
 
 def kl_gemm_loss(h_s: torch.Tensor, h_t: torch.Tensor, weight: torch.Tensor, mask: torch.Tensor,
@@ -438,9 +449,8 @@ class PrenormKLGemmFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g):
         dx, dw = ctx.saved_tensors
-        g = g.to(torch.float32)
-        return ((dx * g).to(ctx.dtypes[0]) if dx is not None else None, None, None,
-                (dw * g).to(ctx.dtypes[1]) if dw is not None else None, None, None, None, None)
+        return (scale_grad(dx, g, ctx.dtypes[0]) if dx is not None else None, None, None,
+                scale_grad(dw, g, ctx.dtypes[1]) if dw is not None else None, None, None, None, None)
 
 
 def prenorm_kl_loss(x_s: torch.Tensor, x_t: torch.Tensor, norm_weight: torch.Tensor, weight: torch.Tensor,

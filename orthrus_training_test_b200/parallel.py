@@ -33,6 +33,11 @@ import torch
 import torch.distributed as dist
 
 
+def _scale_grad(x: torch.Tensor, g: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    from .ops import scale_grad
+    return scale_grad(x, g, dtype)
+
+
 class CudaEngine:
     """Per-device arithmetic through the CUDA library."""
 
@@ -160,8 +165,8 @@ class _RowShardedFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g):
         dh, dw = ctx.saved_tensors          # dW already summed over ranks
-        return ((dh * g).to(ctx.dtypes[0]) if dh is not None else None, None,
-                (dw * g).to(ctx.dtypes[1]) if dw is not None else None, None, None, None, None)
+        return (_scale_grad(dh, g, ctx.dtypes[0]) if dh is not None else None, None,
+                _scale_grad(dw, g, ctx.dtypes[1]) if dw is not None else None, None, None, None, None)
 
 
 def row_sharded_kl_loss(h_s: torch.Tensor, h_t: torch.Tensor, weight: torch.Tensor, mask: torch.Tensor,
@@ -215,8 +220,8 @@ class _VocabShardedFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g):
         dh, dw = ctx.saved_tensors
-        return ((dh * g).to(ctx.dtypes[0]) if dh is not None else None, None,
-                (dw * g).to(ctx.dtypes[1]) if dw is not None else None, None, None, None, None)
+        return (_scale_grad(dh, g, ctx.dtypes[0]) if dh is not None else None, None,
+                _scale_grad(dw, g, ctx.dtypes[1]) if dw is not None else None, None, None, None, None)
 
 
 def vocab_sharded_kl_loss(h_s: torch.Tensor, h_t: torch.Tensor, weight_shard: torch.Tensor, mask: torch.Tensor,

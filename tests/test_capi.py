@@ -67,6 +67,11 @@ def test_argument_validation_codes():
     assert L.klg_merge_stats(p, 0, 4, p, None) == _lib.KLG_ERR_ARG
     assert L.klg_count_valid(None, 4, p, None) == _lib.KLG_ERR_ARG
     assert L.klg_trace_begin(0) == _lib.KLG_ERR_ARG
+    # gradient scaling: null / negative size / misaligned buffers rejected before any device call
+    assert L.klg_scale_cast(None, None, 4, p, 1, None) == _lib.KLG_ERR_ARG
+    assert L.klg_scale_cast(p, None, -1, p, 1, None) == _lib.KLG_ERR_ARG
+    assert L.klg_scale_cast(odd, None, 4, p, 1, None) == _lib.KLG_ERR_ALIGN
+    assert L.klg_scale_cast(p, None, 0, p, 0, None) == 0
     # both outputs NULL: nothing to do, succeeds without touching the device
     assert L.klg_bwd(p, p, p, p, p, p, None, 4, 64, 4, 1.0, None, None, p, 1 << 16, None) == 0
     del keep

@@ -354,3 +354,19 @@ def test_fp32_path_golden(name):
     ref_dh = g["grad_diff_hidden"][np.arange(B)[:, None], dp].reshape(h_s.shape)
     _f32_close(float(loss), h_s.grad.double().cpu().numpy(), w.grad.double().cpu().numpy(), float(g["loss"]), ref_dh,
                g["grad_weight"], name)
+
+
+@pytest.mark.parametrize("n", [4, 37, 1 << 20])
+def test_scale_grad_matches_torch(n):
+    """The autograd backward's one-pass scaling (klg_scale_cast) gives exactly torch's
+    (x * g).to(dtype): one fp32 product, then round to nearest even for bf16."""
+    from orthrus_training_test_b200 import ops
+    dev = torch.device("cuda:0")
+    g = torch.Generator().manual_seed(n)
+    x = (torch.randn(n, generator=g) * 1e-3).to(dev)
+    for gv in (1.0, -0.37, 3.0e4):
+        gs = torch.tensor(gv, device=dev)
+        for dt in (torch.bfloat16, torch.float32):
+            ours = ops.scale_grad(x, gs, dt)
+            torch.cuda.synchronize()
+            assert ours.dtype == dt and torch.equal(ours, (x * gs).to(dt)), (n, gv, dt)
