@@ -679,10 +679,21 @@ int klg_selftest_wait_timeout(void* stream) {
 // vocab ranges per row, one partial record per unit and epilogue column slice.
 constexpr int kStatsMaxRanges = 8;
 
+// Vocab ranges of the forward statistics: planned on the interleaved kernel's units (128-row
+// pair tiles x 256-column vocab tiles; vpu vocab tiles per range) unless KLG_DZI=0 keeps the
+// row-major kernel's (256-row tiles x 128 columns).  Where the row-major kernel runs under the
+// interleaved plan it takes 2 * vpu of its 128-column tiles per range: the same number of ranges.
+void stats_plan(int64_t n_rows, int64_t vocab, int& vpu, int& n_uv) {
+  if (dzi_on())
+    plan_dual(cdiv(n_rows, klg::DZI_ROWS), cdiv(vocab, klg::DZI_BN), num_sms() / 2, vpu, n_uv, kStatsMaxRanges);
+  else
+    plan_dual(cdiv(n_rows, 256), cdiv(vocab, klg::DZP_BN), num_sms() / 2, vpu, n_uv, kStatsMaxRanges);
+}
+
 int klg_num_partials(int64_t n_rows, int64_t vocab, int* n_part) {
   if (!n_part || n_rows < 1 || vocab < 1) return fail(KLG_ERR_ARG, "bad arguments to klg_num_partials");
   int vpu, n_uv;
-  plan_dual(cdiv(n_rows, 256), cdiv(vocab, klg::DZP_BN), num_sms() / 2, vpu, n_uv, kStatsMaxRanges);
+  stats_plan(n_rows, vocab, vpu, n_uv);
   *n_part = n_uv * klg::DZP_CSPLIT;
   return KLG_OK;
 }
@@ -695,17 +706,53 @@ int klg_fwd_stats(const void* hs, const void* ht, const void* w, int64_t n_rows,
   if (n_part < klg::DZP_CSPLIT || n_part % klg::DZP_CSPLIT != 0 || n_part > kStatsMaxRanges * klg::DZP_CSPLIT)
     return fail(KLG_ERR_ARG, "n_part=%d is not a record count this kernel writes (use klg_num_partials)", n_part);
   if ((rc = bind_device(hs))) return rc;   // the exact plan below depends on the SM count of hs's device
+  int vpu, n_uv;
+  stats_plan(n_rows, vocab, vpu, n_uv);
+  if (n_part != n_uv * klg::DZP_CSPLIT)
+    return fail(KLG_ERR_ARG, "n_part=%d but this device plans %d (use klg_num_partials)", n_part, n_uv * klg::DZP_CSPLIT);
+  NvtxRange nvtx_range("klg_fwd_stats");
+  // interleaved-view statistics (8-row groups: N % 8 == 0, two distinct tensors)
+  if (dzi_on() && n_rows % 8 == 0 && hs != ht) {
+    alignas(64) CUtensorMap mhi, mw256;
+    int s_view = 0, lay = klg::DZI_ROW;
+    if (dzi_map(&mhi, hs, ht, n_rows, hidden, &s_view, &lay) && lay != klg::DZI_ROW &&
+        make_map(&mw256, w, hidden, vocab, hidden, klg::BK, klg::DZI_BN / 2)) {
+      klg::DziArgs b{};
+      b.n_rows = (int)n_rows;
+      b.v_begin = 0;
+      b.v_count = (int)vocab;
+      b.n_rt = cdiv(n_rows, klg::DZI_ROWS);
+      b.n_vt = cdiv(vocab, klg::DZI_BN);
+      b.vt_per_unit = vpu;
+      b.n_units = b.n_rt * n_uv;
+      b.n_kb = cdiv(hidden, klg::BK);
+      b.s_view = s_view;
+      b.scale_log2 = inv_temp * 1.4426950408889634f;
+      b.inv_temp = inv_temp;
+      b.partials = partials;
+      auto k = lay == klg::DZI_G8_S0 ? klg::dzi_pair_kernel<klg::DZI_G8_S0, klg::MODE_STATS>
+                                     : klg::dzi_pair_kernel<klg::DZI_G8_S1, klg::MODE_STATS>;
+      cudaError_t e = set_smem(k, klg::DZI_SMEM);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dzi_pair_kernel)");
+      const int pairs = b.n_units < num_sms() / 2 ? b.n_units : num_sms() / 2;
+      const int slot = trace_pre((cudaStream_t)stream);
+      e = launch_k(k, dim3(2 * pairs), dim3(klg::DZI_THREADS), klg::DZI_SMEM, (cudaStream_t)stream, 2, mhi, mw256, mw256,
+                   b);
+      trace_post(slot, (cudaStream_t)stream, KLG_KIND_STATS);
+      if (e != cudaSuccess) return cuda_fail(e, "launch dzi_pair_kernel (statistics)");
+      ++g_launches;
+      return KLG_OK;
+    }
+    if (dzi_mode() == 2 && lay != klg::DZI_ROW) return fail(KLG_ERR_CUDA, "interleaved-view tensor map rejected (KLG_DZI=2)");
+  }
   klg::DualArgs a{};
   a.n_rows = (int)n_rows;
   a.v_begin = 0;
   a.v_count = (int)vocab;
   a.n_rt = cdiv(n_rows, 256);
   a.n_vt = cdiv(vocab, klg::DZP_BN);
-  int n_uv;
-  plan_dual(a.n_rt, a.n_vt, num_sms() / 2, a.vt_per_unit, n_uv, kStatsMaxRanges);
-  if (n_part != n_uv * klg::DZP_CSPLIT)
-    return fail(KLG_ERR_ARG, "n_part=%d but this device plans %d (use klg_num_partials)", n_part, n_uv * klg::DZP_CSPLIT);
-  NvtxRange nvtx_range("klg_fwd_stats");
+  a.vt_per_unit = dzi_on() ? 2 * vpu : vpu;   // same vocab ranges as the plan
+  if (cdiv(a.n_vt, a.vt_per_unit) != n_uv) return fail(KLG_ERR_ARG, "internal plan mismatch (statistics ranges)");
   a.n_units = a.n_rt * n_uv;
   a.n_kb = cdiv(hidden, klg::BK);
   a.scale_log2 = inv_temp * 1.4426950408889634f;

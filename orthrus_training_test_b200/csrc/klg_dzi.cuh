@@ -76,6 +76,7 @@ struct DziArgs {
   float inv_temp;
   float* a_parts;        // optional [.][N]: cross-term partial rows a_part_base + uv * DZI_CSPLIT + half
   int a_part_base;
+  float* partials;       // MODE_STATS: [n_uv * DZI_CSPLIT][5][N] records (m_s, S_s, m_t, S_t, A), log2 units
 };
 
 // Units are numbered row-tile-major (the pairs running at the same time share a few row tiles
@@ -136,12 +137,86 @@ __device__ __forceinline__ void dzi_g8_chunk(const uint32_t (&r)[16], uint64_t s
   }
 }
 
-template <int LAY>
+// G8 statistics on one 16x256b.x4 load (32 columns, 8 per thread: columns col0 + 8k + {0, 1}):
+// the online (m_s, S_s, m_t, S_t, A) update of stats_chunk, A = sum 2^(u_t - m_t) (u_t - u_s),
+// with u = z * sl2; columns at or past ncol are left out (MASK).
+template <int SV, bool MASK>
+__device__ __forceinline__ void dzi_g8_stats(const uint32_t (&r)[16], uint64_t sl2, int col0, int ncol,
+                                             float (&st)[5]) {
+  float us[8], ut[8];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint64_t zs = f2_pack(__uint_as_float(r[4 * k + 2 * SV]), __uint_as_float(r[4 * k + 2 * SV + 1]));
+    const uint64_t zt = f2_pack(__uint_as_float(r[4 * k + 2 - 2 * SV]), __uint_as_float(r[4 * k + 3 - 2 * SV]));
+    f2_unpack(f2_mul(zs, sl2), us[2 * k], us[2 * k + 1]);
+    f2_unpack(f2_mul(zt, sl2), ut[2 * k], ut[2 * k + 1]);
+    if (MASK) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e)
+        if (col0 + 8 * k + e >= ncol) us[2 * k + e] = ut[2 * k + e] = -INFINITY;
+    }
+  }
+  float cms = us[0], cmt = ut[0];
+#pragma unroll
+  for (int j = 1; j < 8; ++j) {
+    cms = fmaxf(cms, us[j]);
+    cmt = fmaxf(cmt, ut[j]);
+  }
+  const float nms = fmaxf(st[0], cms), nmt = fmaxf(st[2], cmt);
+  const float rs = ex2(st[0] - nms), rt = ex2(st[2] - nmt);
+  const uint64_t ms2 = f2_pack(nms, nms), mt2 = f2_pack(nmt, nmt);
+  uint64_t ss = 0, stt = 0, aa = 0;   // packed (0.f, 0.f)
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint64_t u_s = f2_pack(us[2 * k], us[2 * k + 1]), u_t = f2_pack(ut[2 * k], ut[2 * k + 1]);
+    float a0, a1, b0, b1;
+    f2_unpack(f2_sub(u_s, ms2), a0, a1);
+    f2_unpack(f2_sub(u_t, mt2), b0, b1);
+    const uint64_t es = f2_pack(ex2(a0), ex2(a1)), et = f2_pack(ex2(b0), ex2(b1));
+    ss = f2_add(ss, es);
+    stt = f2_add(stt, et);
+    uint64_t d = f2_sub(u_t, u_s);
+    if (MASK) {   // left-out columns: e_t = 0 but u_t - u_s is NaN
+      float d0, d1;
+      f2_unpack(d, d0, d1);
+      d = f2_pack(col0 + 8 * k < ncol ? d0 : 0.f, col0 + 8 * k + 1 < ncol ? d1 : 0.f);
+    }
+    aa = f2_fma(et, d, aa);
+  }
+  float x0, x1;
+  f2_unpack(ss, x0, x1);
+  st[1] = fmaf(st[1], rs, x0 + x1);
+  f2_unpack(stt, x0, x1);
+  st[3] = fmaf(st[3], rt, x0 + x1);
+  f2_unpack(aa, x0, x1);
+  st[4] = fmaf(st[4], rt, x0 + x1);
+  st[0] = nms;
+  st[2] = nmt;
+}
+
+// Online merge of this thread's record with the one of lane ^ o (same row, other columns).
+__device__ __forceinline__ void dzi_stats_merge(float (&st)[5], int o) {
+  float q[5];
+#pragma unroll
+  for (int i = 0; i < 5; ++i) q[i] = __shfl_xor_sync(0xffffffffu, st[i], o);
+  const float ms = fmaxf(st[0], q[0]), mt = fmaxf(st[2], q[2]);
+  const float a = ex2(st[0] - ms), b = ex2(q[0] - ms), c = ex2(st[2] - mt), d = ex2(q[2] - mt);
+  st[1] = fmaf(st[1], a, q[1] * b);
+  st[3] = fmaf(st[3], c, q[3] * d);
+  st[4] = fmaf(st[4], c, q[4] * d);
+  st[0] = ms;
+  st[2] = mt;
+}
+
+// MODE_DZ: pass 2's dZ chunk and KL cross-term partials.  MODE_STATS (G8 layouts only): the
+// single-pass forward's per-unit records (m_s, S_s, m_t, S_t, A) for evaluation.
+template <int LAY, int MODE = MODE_DZ>
 __global__ void __launch_bounds__(DZI_THREADS, 1)
 dzi_pair_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant__ CUtensorMap map_w,
                 const __grid_constant__ CUtensorMap map_out, const DziArgs a) {
   constexpr bool G8 = LAY != DZI_ROW;
   constexpr int SV = LAY == DZI_G8_S1 ? 1 : 0;
+  static_assert(MODE == MODE_DZ || G8, "the statistics epilogue is built for the 8-row-group layouts");
   constexpr int STAGES = DZI_STAGES;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint32_t tmem_slot;
@@ -277,7 +352,61 @@ dzi_pair_kernel(const __grid_constant__ CUtensorMap map_h, const __grid_constant
     int tcount = 0;
     int sbuf = 0;
     bool ok = true;
-    if (G8) {
+    if (MODE == MODE_STATS) {
+      // thread (t4, tq): token rows y0 + t4 and y0 + 8 + t4, columns 8k + 2 tq + {0, 1} of each 32
+      const int t4 = lane >> 2, tq = lane & 3;
+      const uint64_t sl2 = f2_pack(sl2f, sl2f);
+      for (int u = cid; ok && u < a.n_units; u += n_clusters) {
+        int rt, uv, vt0, vt1;
+        dzi_unit(a, u, rt, uv, vt0, vt1);
+        const int y0 = rt * DZI_ROWS + (int)rank * (DZI_ROWS / 2) + q * 16;
+        float sa[5] = {NEG_BIG, 0.f, NEG_BIG, 0.f, 0.f}, sb[5] = {NEG_BIG, 0.f, NEG_BIG, 0.f, 0.f};
+        for (int vt = vt0; ok && vt < vt1; ++vt, ++tcount) {
+          const int buf = tcount & 1;
+          const uint32_t tph = (tcount >> 1) & 1;
+          if (!warp_wait(tfull0 + 8u * buf, tph, abort_p, KLG_STATUS_TIMEOUT_EPILOGUE)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t tbase = lane_addr + buf * DZI_BN;
+#pragma unroll 1
+          for (int c = 0; c < (DZI_BN / 2) / 32; ++c) {
+            const int x = vt * DZI_BN + hf * (DZI_BN / 2) + c * 32;   // first column of this chunk
+            if (x >= a.v_count) break;                               // warp-uniform
+            uint32_t ra[16], rb[16];
+            tmem_ld16x256b_x4(tbase + c * 32, ra);
+            tmem_ld16x256b_x4(tbase + c * 32 + (16u << 16), rb);
+            tmem_wait_ld16(ra, rb);
+            const int col0 = x + 2 * tq;
+            if (x + 32 <= a.v_count) {
+              dzi_g8_stats<SV, false>(ra, sl2, col0, a.v_count, sa);
+              dzi_g8_stats<SV, false>(rb, sl2, col0, a.v_count, sb);
+            } else {
+              dzi_g8_stats<SV, true>(ra, sl2, col0, a.v_count, sa);
+              dzi_g8_stats<SV, true>(rb, sl2, col0, a.v_count, sb);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if (leader) mbar_arrive(tempty0 + 8u * buf);
+            else mbar_arrive_cluster(lead_tempty0 + 8u * buf);
+          }
+        }
+        dzi_stats_merge(sa, 1);
+        dzi_stats_merge(sb, 1);
+        dzi_stats_merge(sa, 2);
+        dzi_stats_merge(sb, 2);
+        if (ok && tq == 0) {
+          float* pr = a.partials + (size_t)(uv * DZI_CSPLIT + hf) * 5 * a.n_rows;
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const int row = y0 + 8 * h2 + t4;
+            const float* v = h2 ? sb : sa;
+            if (row < a.n_rows)
+              for (int i = 0; i < 5; ++i) pr[(size_t)i * a.n_rows + row] = v[i];
+          }
+        }
+      }
+    } else if (G8) {
       // thread (t4, tq) = (lane / 4, lane % 4): token rows y0 + t4 (16-lane group 0) and y0 + 8 + t4
       // (group 1), columns 8k + 2 tq + {0, 1} of each 32; staging rows t4 and 8 + t4
       const int t4 = lane >> 2, tq = lane & 3;
