@@ -69,33 +69,41 @@ __device__ __forceinline__ void attn_unit(const AttnArgs& a, int u, int& b, int&
 __device__ __forceinline__ void attn_p_chunk(const uint32_t (&v)[32], int c, int nk, int kmax, bool open, float sl2,
                                              float ref, uint32_t prow, int r, float& tmax, float& sum) {
   uint32_t pk[16];   // P as bf16 pairs
-  float t0 = -INFINITY, t1 = -INFINITY, s0 = 0.f, s1 = 0.f;
+  float t0 = -INFINITY, t1 = -INFINITY;
+  uint64_t ss = 0;   // packed (s0, s1) = (0.f, 0.f): the even and odd keys' sums
+  const uint64_t sl2x2 = f2_pack(sl2, sl2), nref = f2_pack(-ref, -ref);
   if (open) {
 #pragma unroll
     for (int j = 0; j < 32; j += 2) {
       const float x0 = __uint_as_float(v[j]), x1 = __uint_as_float(v[j + 1]);
       t0 = fmaxf(t0, x0);
       t1 = fmaxf(t1, x1);
-      const float p0 = ex2(fmaf(x0, sl2, -ref)), p1 = ex2(fmaf(x1, sl2, -ref));
-      s0 += p0;
-      s1 += p1;
+      float a0, a1;
+      f2_unpack(f2_fma(f2_pack(x0, x1), sl2x2, nref), a0, a1);
+      const float p0 = ex2(a0), p1 = ex2(a1);
+      ss = f2_add(ss, f2_pack(p0, p1));
       pk[j >> 1] = pack_bf16x2(p0, p1);
     }
     tmax = fmaxf(tmax, fmaxf(t0, t1) * sl2);   // scale > 0 commutes with max
   } else {
 #pragma unroll
     for (int j = 0; j < 32; j += 2) {
-      const float x0 = c * 32 + j <= kmax ? __uint_as_float(v[j]) * sl2 : -INFINITY;
-      const float x1 = c * 32 + j + 1 <= kmax ? __uint_as_float(v[j + 1]) * sl2 : -INFINITY;
+      float x0, x1;
+      f2_unpack(f2_mul(f2_pack(__uint_as_float(v[j]), __uint_as_float(v[j + 1])), sl2x2), x0, x1);
+      x0 = c * 32 + j <= kmax ? x0 : -INFINITY;
+      x1 = c * 32 + j + 1 <= kmax ? x1 : -INFINITY;
       t0 = fmaxf(t0, x0);
       t1 = fmaxf(t1, x1);
-      const float p0 = ex2(x0 - ref), p1 = ex2(x1 - ref);
-      s0 += p0;
-      s1 += p1;
+      float a0, a1;
+      f2_unpack(f2_add(f2_pack(x0, x1), nref), a0, a1);
+      const float p0 = ex2(a0), p1 = ex2(a1);
+      ss = f2_add(ss, f2_pack(p0, p1));
       pk[j >> 1] = pack_bf16x2(p0, p1);
     }
     tmax = fmaxf(tmax, fmaxf(t0, t1));
   }
+  float s0, s1;
+  f2_unpack(ss, s0, s1);
   sum += s0 + s1;
 #pragma unroll
   for (int q8 = 0; q8 < 4; ++q8) {
@@ -725,15 +733,19 @@ block_attn_bwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_co
         tmem_ld32_raw(lrow + ATB_DP_COL + c32 * 32, pv);
         tmem_wait_ld_regs(sv, pv);
         uint32_t pp[16], dd[16];
+        const uint64_t sl2x2 = f2_pack(a.sl2, a.sl2), nlse = f2_pack(-lse2, -lse2), dd2 = f2_pack(D, D);
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
           const int key0 = c32 * 32 + j;             // key index within the tile
           const bool v0 = live && (self ? key0 < a.K : i * ATT_BN + key0 <= lim);
           const bool v1 = live && (self ? key0 + 1 < a.K : i * ATT_BN + key0 + 1 <= lim);
-          const float p0 = v0 ? ex2(fmaf(__uint_as_float(sv[j]), a.sl2, -lse2)) : 0.f;
-          const float p1 = v1 ? ex2(fmaf(__uint_as_float(sv[j + 1]), a.sl2, -lse2)) : 0.f;
-          const float d0 = p0 * (__uint_as_float(pv[j]) - D);
-          const float d1 = p1 * (__uint_as_float(pv[j + 1]) - D);
+          float e0, e1;   // packed fp32x2: the same roundings as the scalar form
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(sv[j]), __uint_as_float(sv[j + 1])), sl2x2, nlse), e0, e1);
+          const float p0 = v0 ? ex2(e0) : 0.f;
+          const float p1 = v1 ? ex2(e1) : 0.f;
+          const uint64_t p = f2_pack(p0, p1);
+          float d0, d1;
+          f2_unpack(f2_mul(p, f2_sub(f2_pack(__uint_as_float(pv[j]), __uint_as_float(pv[j + 1])), dd2)), d0, d1);
           pp[j / 2] = pack_bf16x2(p0, p1);
           dd[j / 2] = pack_bf16x2(d0, d1);
         }
