@@ -84,6 +84,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-overlap", action="store_true",
                     help="row sharding: one dW all-reduce after the step instead of per-chunk buckets overlapped")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="nccl",
+                    help="row sharding: dW all-reduced by NCCL, overlapped per chunk (nccl), or summed inside "
+                         "the step over NVLink peer memory (p2p)")
     ap.add_argument("--sm-reserve", type=int, default=0,
                     help="SMs left out of the persistent kernels' grids (room for NCCL beside them)")
     ap.add_argument("--sustained-seconds", type=float, default=2.5,
@@ -743,7 +746,16 @@ def main():
 
     # row sharding: dW is exchanged in vocab-chunk buckets, each all-reduced on a side stream as
     # soon as its chunk's GEMM is done (overlapping the chunks still computing)
-    overlap = world > 1 and not vocab_sharded and not prenorm and not args.no_overlap
+    # row sharding with --exchange p2p: dW summed over the ranks inside the step over NVLink peer
+    # memory (the GEMM stores each block of the partial into its owner's buffer)
+    xr = None
+    os.environ["KLG_XR"] = "1" if args.exchange == "p2p" else "0"   # the e2e leg below takes the same route
+    if world > 1 and not vocab_sharded and not prenorm and args.exchange == "p2p":
+        from orthrus_training_test_b200.parallel import CudaEngine
+        xr = CudaEngine().xr_exchange(None, hs, W)
+        if xr is None:
+            os.environ["KLG_XR"] = "0"   # the e2e leg below takes the same (NCCL) route
+    overlap = world > 1 and xr is None and not vocab_sharded and not prenorm and not args.no_overlap
     buckets = ops.chunk_bounds(N, H, V_work, fb_ws) if overlap else None
     chunk_evs = ops.new_chunk_events(len(buckets)) if overlap else None
     side = torch.cuda.Stream(device=dev) if overlap else None
@@ -757,6 +769,11 @@ def main():
         cnt = ops.count_valid(m)
         if world > 1:
             dist.all_reduce(cnt)
+        if xr is not None:
+            loss, dh, dw = ops.kl_fwd_bwd_xr(hs, ht, W, m, T, cnt, True, xr.world, xr.rank, xr.peer_buffers,
+                                             xr.next_epoch(), workspace_bytes=fb_ws)
+            dist.all_reduce(loss)
+            return loss
         loss, _, _, _, dh, dw = ops.kl_fwd_bwd(hs, ht, W, m, T, count=cnt, workspace_bytes=fb_ws,
                                                chunk_events=chunk_evs)
         if world > 1:
@@ -971,7 +988,8 @@ def main():
                        "vocab_per_gpu": V_work,
                        "temperature": T, "parallelism": (f"vocab-sharded x{world}" if vocab_sharded else
                                                          f"row-sharded dp{world}" if world > 1 else "single GPU"),
-                       "dw_exchange": ("per-chunk buckets overlapped on a side stream" if overlap else
+                       "dw_exchange": ("inside the step over NVLink peer memory (klg_fwd_bwd_xr)" if xr is not None
+                                       else "per-chunk buckets overlapped on a side stream" if overlap else
                                        "one all-reduce after the step" if world > 1 and not vocab_sharded else None),
                        "sm_reserve": args.sm_reserve,
                        "l2": "flushed between steps (256 MiB write)"},

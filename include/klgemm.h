@@ -60,6 +60,7 @@ int klg_device_status(int* status, int reset);
 #define KLG_STATUS_TIMEOUT_MMA 0x2        /* the MMA issuer waited out its bound on operands/TMEM  */
 #define KLG_STATUS_TIMEOUT_EPILOGUE 0x4   /* an epilogue warp waited out its bound on a tile       */
 #define KLG_STATUS_TIMEOUT_DRAIN 0x8      /* a final drain of copies / MMAs waited out its bound   */
+#define KLG_STATUS_TIMEOUT_PEER 0x10      /* a cross-rank exchange waited out its bound on a peer  */
 #define KLG_STATUS_SELFTEST 0x100         /* set by klg_selftest_wait_timeout                      */
 
 /* Test hook (no counterpart in the reference): launches one block that waits on an
@@ -178,6 +179,38 @@ int klg_fwd_bwd_events(const void* h_s, const void* h_t, const void* w, const ui
                        int64_t hidden, int64_t vocab, float inv_temp, int count_given, float* count, const float* grad,
                        float* loss, float* lse, float* row_kl, float* d_h_s, float* d_w, void* workspace,
                        int64_t workspace_bytes, void* const* chunk_events, int n_events, void* stream);
+
+/* Row-sharded training step with the dW exchange done over NVLink peer memory inside the step
+ * (no counterpart in the reference; replaces klg_fwd_bwd + an all-reduce of dW): the dW GEMM
+ * stores each 32-row block of this rank's partial dW into its owner's inbox (block b belongs to
+ * rank b % world), then the owners sum their blocks in a fixed rank order and every rank copies
+ * the sums into d_w, so d_w holds the sum over ranks on every rank when the stream reaches the
+ * end of the call.  peer_buffers[world]: every rank's exchange buffer (klg_xr_buffer_bytes bytes,
+ * zero-filled before the first call, addressable from this device: klg_xr_alloc / klg_xr_open),
+ * the same on all ranks; epoch: 1 on the first call, +1 per call, the same on all ranks (it
+ * orders the steps).  Every rank must make the call; a wait on a rank that does not arrive gives
+ * up after ~1 s with KLG_STATUS_TIMEOUT_PEER (d_w is then invalid).  world in [2, 8]; bf16 path;
+ * d_w required; loss and count as klg_fwd_bwd (count_given = 1 with the global count). */
+int64_t klg_xr_buffer_bytes(int64_t vocab, int64_t hidden, int world);
+int klg_fwd_bwd_xr(const void* h_s, const void* h_t, const void* w, const uint8_t* mask, int64_t n_rows,
+                   int64_t hidden, int64_t vocab, float inv_temp, int count_given, float* count, const float* grad,
+                   float* loss, float* lse, float* row_kl, float* d_h_s, float* d_w, void* workspace,
+                   int64_t workspace_bytes, int world, int rank, void* const* peer_buffers, uint32_t epoch,
+                   void* stream);
+
+/* Exchange buffers over CUDA IPC (plain peer mappings, no multicast object): klg_xr_alloc
+ * allocates and zero-fills `bytes` on `device` and writes its IPC handle (64 bytes) to
+ * `handle`; every other rank opens it with klg_xr_open (its own device current); klg_xr_close
+ * releases either (own = 1: the allocation, own = 0: a peer mapping). */
+int klg_xr_alloc(int device, int64_t bytes, void** ptr, void* handle);
+int klg_xr_open(int device, const void* handle, void** ptr);
+int klg_xr_close(void* ptr, int own);
+
+/* Test hook: the exchange's bounded wait on one GPU.  Runs the reduce step of the exchange on
+ * `buffer` (klg_xr_buffer_bytes(vocab, hidden, 2) bytes, zero-filled) as rank 0 of 2 waiting for
+ * an epoch no rank publishes: after ~1 s it sets KLG_STATUS_TIMEOUT_PEER and returns, the
+ * context stays usable. */
+int klg_selftest_xr_timeout(void* buffer, int64_t vocab, int64_t hidden, void* stream);
 
 /* Leaves n_sms SMs of every device out of the persistent kernels' grids (0 = use all; at most
  * 64; process-wide, for launches planned after the call), so that communication kernels -- an
@@ -373,6 +406,7 @@ int klg_scale_cast(const float* in, const float* g, int64_t n, void* out, int ou
 #define KLG_KIND_NORM 10     /* final RMSNorm of pre-norm rows, forward or backward       */
 #define KLG_KIND_ATTN 11     /* block-diffusion attention, forward                        */
 #define KLG_KIND_GATHER 12   /* row selection (gather) or its gradient scatter            */
+#define KLG_KIND_XR 13       /* cross-rank dW exchange: owners' reduce, then the gather   */
 int klg_trace_begin(int capacity);
 int klg_trace_end(int* kinds, float* ms, int capacity, int* n);
 

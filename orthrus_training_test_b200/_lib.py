@@ -6,7 +6,7 @@ loaded, :func:`lib` raises.  There is no CPU or pure-PyTorch path.
 from __future__ import annotations
 
 import ctypes
-from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_longlong, c_uint8, c_ulonglong, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_longlong, c_uint8, c_uint32, c_ulonglong, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libklgemm.so"
@@ -66,6 +66,14 @@ SIGNATURES = {
                         c_int64, c_float, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
     "klg_cast_f32_bf16": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
     "klg_scale_cast": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_int, c_void_p]),
+    "klg_xr_buffer_bytes": (c_int64, [c_int64, c_int64, c_int]),
+    "klg_fwd_bwd_xr": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_float, c_int,
+                               c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
+                               c_int, c_int, c_void_p, c_uint32, c_void_p]),
+    "klg_selftest_xr_timeout": (c_int, [c_void_p, c_int64, c_int64, c_void_p]),
+    "klg_xr_alloc": (c_int, [c_int, c_int64, POINTER(c_void_p), c_void_p]),
+    "klg_xr_open": (c_int, [c_int, c_void_p, POINTER(c_void_p)]),
+    "klg_xr_close": (c_int, [c_void_p, c_int]),
     "klg_fwd_bwd_workspace_bytes": (c_int64, [c_int64, c_int64, c_int64]),
     "klg_fwd_bwd_chunk_cols": (c_int64, [c_int64, c_int64, c_int64, c_int64]),
     "klg_fwd_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_float, c_int, c_void_p,
@@ -96,7 +104,7 @@ SIGNATURES = {
     "klg_trace_end": (c_int, [POINTER(c_int), POINTER(c_float), c_int, POINTER(c_int)]),
 }
 
-KIND_NAMES = {1: "stats", 2: "dz", 3: "gemm", 4: "merge", 5: "finalize", 6: "count", 7: "cast", 8: "zero", 9: "sample", 10: "norm", 11: "attn", 12: "gather"}
+KIND_NAMES = {1: "stats", 2: "dz", 3: "gemm", 4: "merge", 5: "finalize", 6: "count", 7: "cast", 8: "zero", 9: "sample", 10: "norm", 11: "attn", 12: "gather", 13: "xr"}
 
 _lib = None
 

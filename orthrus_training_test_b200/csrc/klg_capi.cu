@@ -26,6 +26,7 @@
 #include "klg_attn.cuh"
 #include "klg_dzt.cuh"
 #include "klg_dzi.cuh"
+#include "klg_xr.cuh"
 #include "klgemm.h"
 
 namespace {
@@ -535,7 +536,8 @@ void build_schedule(const klg::PairGemmArgs& g, int t_begin, int t_end, int pair
 
 template <int BN>
 int launch_gemm_pair_t(const CUtensorMap& a0, const CUtensorMap& b0, const CUtensorMap& a1, const CUtensorMap& b1,
-                       const CUtensorMap& c0, const CUtensorMap& c1, const klg::PairGemmArgs& g, cudaStream_t s) {
+                       const CUtensorMap& c0, const CUtensorMap& c1, const klg::PairGemmArgs& g, cudaStream_t s,
+                       const klg::XrMaps& xm) {
   using Cfg = klg::PairGemmCfg<BN>;
   auto k = klg::gemm_pair_kernel<BN>;
   cudaError_t e = set_smem(k, Cfg::SMEM);
@@ -547,7 +549,7 @@ int launch_gemm_pair_t(const CUtensorMap& a0, const CUtensorMap& b0, const CUten
     const int pairs = std::min(max_pairs, t1 - t0);
     build_schedule(g, t0, t1, pairs, sc);
     const int slot = trace_pre(s);
-    e = launch_k(k, dim3(2 * pairs), dim3(Cfg::THREADS), Cfg::SMEM, s, 2, a0, b0, a1, b1, c0, c1, g, sc);
+    e = launch_k(k, dim3(2 * pairs), dim3(Cfg::THREADS), Cfg::SMEM, s, 2, a0, b0, a1, b1, c0, c1, g, sc, xm);
     trace_post(slot, s, KLG_KIND_GEMM);
     if (e != cudaSuccess) return cuda_fail(e, "launch gemm_pair_kernel");
     ++g_launches;
@@ -556,11 +558,14 @@ int launch_gemm_pair_t(const CUtensorMap& a0, const CUtensorMap& b0, const CUten
 }
 
 int launch_gemm_pair(int bn, const CUtensorMap& a0, const CUtensorMap& b0, const CUtensorMap& a1, const CUtensorMap& b1,
-                     const CUtensorMap& c0, const CUtensorMap& c1, const klg::PairGemmArgs& g, cudaStream_t s) {
+                     const CUtensorMap& c0, const CUtensorMap& c1, const klg::PairGemmArgs& g, cudaStream_t s,
+                     const klg::XrMaps* xm = nullptr) {
+  static const klg::XrMaps none{};   // unused unless g.xr is set
+  const klg::XrMaps& m = xm ? *xm : none;
   switch (bn) {
-    case 128: return launch_gemm_pair_t<128>(a0, b0, a1, b1, c0, c1, g, s);
-    case 192: return launch_gemm_pair_t<192>(a0, b0, a1, b1, c0, c1, g, s);
-    default: return launch_gemm_pair_t<256>(a0, b0, a1, b1, c0, c1, g, s);
+    case 128: return launch_gemm_pair_t<128>(a0, b0, a1, b1, c0, c1, g, s, m);
+    case 192: return launch_gemm_pair_t<192>(a0, b0, a1, b1, c0, c1, g, s, m);
+    default: return launch_gemm_pair_t<256>(a0, b0, a1, b1, c0, c1, g, s, m);
   }
 }
 
@@ -877,7 +882,7 @@ namespace {
 int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask, const float* lse, const float* count,
               const float* grad, int64_t n_rows, int64_t hidden, int64_t vocab, float inv_temp, float* d_hs, float* d_w,
               __nv_bfloat16* dz, int64_t cols, float* a_parts, int* n_ap_out, cudaStream_t s, bool split = false,
-              void* const* chunk_events = nullptr, int n_events = 0) {
+              void* const* chunk_events = nullptr, int n_events = 0, const klg::XrArgs* xr = nullptr) {
   int rc;
   const bool tr = !split && dzt_on(hidden);           // dZ^T [cols][ld_n] from the transposed kernel
   const int64_t ld_n = round8(n_rows);
@@ -913,12 +918,19 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
     return fail(KLG_ERR_CUDA, "cuTensorMapEncodeTiled failed (outputs)");
   if (!d_w) mdw = mhs;   // unused placeholders
   if (!d_hs) mdh = mhs;
+  // the exchange's TMA stores: one map per rank over its inbox [2 * world * rows_per_owner][H]
+  alignas(64) klg::XrMaps xm{};
+  if (xr && xr->tma)
+    for (int p = 0; p < xr->world; ++p)
+      if (!make_map(&xm.m[p], xr->inbox[p], hidden, (uint64_t)2 * xr->world * xr->rows_per_owner, hidden, 32, 32,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_DATA_TYPE_FLOAT32))
+        return fail(KLG_ERR_CUDA, "tensor map (exchange inbox %d)", p);
   // The GEMMs store a tile's first addend and reduce-add the later ones: dH's first addend is
   // chunk 0's (plane 0's), a dW row's is its chunk's -- unless dW's K is split in two, whose
   // partial sums are reduce-added onto zero in either order.  So only dW of a shape with a K
   // split is zeroed (H % 8 == 0: a whole number of float4).
   bool dw_split = false;
-  for (int64_t v0 = 0; d_w && v0 < vocab && !split; v0 += cols) {
+  for (int64_t v0 = 0; d_w && !xr && v0 < vocab && !split; v0 += cols) {
     const int64_t wv = (vocab - v0) < cols ? (vocab - v0) : cols;
     if (pick_dw_split((int)n_rows, (int)wv, (int)hidden, bn) > 0) dw_split = true;
   }
@@ -984,11 +996,12 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
         g.p[0] = gemm_problem(d_w != nullptr, (int)wv, (int)hidden, (int)n_rows, bn, nullptr, (int)hidden,
                               kb_split > 0 ? 1 : 0, 0, 0, 0, 256, kb_split, (int)v0);
         g.n_tiles = g.p[0].n_tiles + g.p[1].n_tiles;
+        if (xr) g.xr = *xr;   // dW blocks go to their owners' inboxes (klg_xr.cuh)
         alignas(64) CUtensorMap mdzt_k, mdzt_mn;
         if (!make_map(&mdzt_k, dz, n_rows, wv, ld_n, klg::BK, klg::BM) ||
             !make_map(&mdzt_mn, dz, n_rows, wv, ld_n, 64, klg::BK))
           return fail(KLG_ERR_CUDA, "tensor map (dz^T operand)");
-        if ((rc = launch_gemm_pair(bn, mdzt_k, mhs_mn, mdzt_mn, mw_mn, mdw, mdh, g, s))) return rc;
+        if ((rc = launch_gemm_pair(bn, mdzt_k, mhs_mn, mdzt_mn, mw_mn, mdw, mdh, g, s, &xm))) return rc;
       }
       if (chunk_events && ci < n_events && chunk_events[ci]) {
         cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(chunk_events[ci]), s);
@@ -1050,6 +1063,7 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
     g.p[0] = gemm_problem(d_w != nullptr, (int)wv, (int)hidden, (int)n_rows, bn, nullptr, (int)hidden, 1, 0, 0, 1, 256,
                           kb_split, (int)v0);
     g.n_tiles = g.p[0].n_tiles + g.p[1].n_tiles;
+    if (xr) g.xr = *xr;   // dW blocks go to their owners' inboxes (klg_xr.cuh)
     (void)ci;
     for (int plane = 0; plane < (split ? 2 : 1); ++plane) {
       g.p[1].accumulate = (v0 > 0 || plane > 0) ? 1 : 0;        // dH: store chunk 0's plane 0
@@ -1059,7 +1073,7 @@ int run_pass2(const void* hs, const void* ht, const void* w, const uint8_t* mask
       if (!make_map(&mdz_k, dzp, wv, n_rows, ld_dz, klg::BK, klg::BM) ||
           !make_map(&mdz_mn, dzp, wv, n_rows, ld_dz, 64, klg::BK))
         return fail(KLG_ERR_CUDA, "tensor map (dz operand)");
-      if ((rc = launch_gemm_pair(bn, mdz_mn, mhs_mn, mdz_k, mw_mn, mdw, mdh, g, s))) return rc;
+      if ((rc = launch_gemm_pair(bn, mdz_mn, mhs_mn, mdz_k, mw_mn, mdw, mdh, g, s, &xm))) return rc;
     }
     if (chunk_events && ci < n_events && chunk_events[ci]) {
       cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(chunk_events[ci]), s);
@@ -1215,6 +1229,77 @@ int klg_bwd(const void* hs, const void* ht, const void* w, const uint8_t* mask, 
 
 namespace {
 
+// The exchange's stores from the dW GEMM: TMA tensor stores into the owners' inboxes (default),
+// or 16-byte stores from registers with KLG_XR_TMA=0 (A/B timing).
+bool xr_tma_on() {
+  static const bool on = [] {
+    const char* v = std::getenv("KLG_XR_TMA");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+// The two kernels that finish the cross-rank dW exchange (klg_xr.cuh).  Their blocks wait only
+// on other ranks' flags (block 0 publishes this rank's first), so a grid larger than what is
+// resident at once cannot deadlock; four blocks per SM keep enough loads in flight.
+int launch_xr(const klg::XrSync& x, cudaStream_t s) {
+  int slot = trace_pre(s);
+  cudaError_t e = launch_k(klg::xr_reduce_kernel, dim3(4 * num_sms()), dim3(256), 0, s, 1, x);
+  if (e == cudaSuccess) {
+    ++g_launches;
+    e = launch_k(klg::xr_wait_kernel, dim3(1), dim3(32), 0, s, 1, x);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "launch xr_reduce_kernel / xr_wait_kernel");
+  ++g_launches;
+  // the gather on the copy engines: owner p's summed rows hold its 32-row blocks b = p, p + W,
+  // ... back to back; each goes to rows 32 b of dW
+  const size_t blk = (size_t)32 * x.hidden * 4;
+  const int nb = cdiv(x.vocab, 32), tail = x.vocab - (nb - 1) * 32;   // rows of the last block
+  for (int p = 0; p < x.world && p < nb; ++p) {
+    const int own = (nb - 1 - p) / x.world + 1;                       // blocks of owner p
+    const bool last_mine = (nb - 1) % x.world == p;
+    const int full = own - ((last_mine && tail < 32) ? 1 : 0);
+    const char* src = reinterpret_cast<const char*>(x.final_peer[p]);
+    char* dst = reinterpret_cast<char*>(x.dw) + (size_t)p * blk;
+    if (full > 0 && (e = cudaMemcpy2DAsync(dst, blk * x.world, src, blk, blk, full, cudaMemcpyDeviceToDevice, s)) !=
+                        cudaSuccess)
+      return cuda_fail(e, "dW gather copy");
+    if (full < own &&
+        (e = cudaMemcpyAsync(dst + (size_t)full * blk * x.world, src + (size_t)full * blk,
+                             (size_t)tail * x.hidden * 4, cudaMemcpyDeviceToDevice, s)) != cudaSuccess)
+      return cuda_fail(e, "dW gather copy (last block)");
+  }
+  trace_post(slot, s, KLG_KIND_XR);
+  return KLG_OK;
+}
+
+// Per-rank exchange buffer: [inbox world x 2 x rows_per_owner x H][final rows_per_owner x H] fp32,
+// then the flags [2][XR_MAX_WORLD] u32 and the split records (256 bytes).
+int64_t xr_rows_per_owner(int64_t vocab, int world) { return (int64_t)cdiv(cdiv(vocab, 32), world) * 32; }
+
+klg::XrSync xr_sync(int64_t vocab, int64_t hidden, int world, int rank, void* const* bufs, uint32_t epoch, float* d_w) {
+  klg::XrSync x{};
+  x.world = world;
+  x.rank = rank;
+  x.rows_per_owner = (int)xr_rows_per_owner(vocab, world);
+  x.hidden = (int)hidden;
+  x.vocab = (int)vocab;
+  x.epoch = epoch;
+  const size_t inbox_f = (size_t)2 * world * x.rows_per_owner * hidden, final_f = (size_t)x.rows_per_owner * hidden;
+  for (int p = 0; p < world; ++p) {
+    float* base = static_cast<float*>(bufs[p]);
+    x.inbox_peer[p] = base;
+    x.final_peer[p] = base + inbox_f;
+    x.flags_peer[p] = reinterpret_cast<uint32_t*>(base + inbox_f + final_f);
+  }
+  float* mine = static_cast<float*>(bufs[rank]);
+  x.inbox = mine;
+  x.final_rows = mine + inbox_f;
+  x.flags = reinterpret_cast<uint32_t*>(mine + inbox_f + final_f);
+  x.dw = d_w;
+  return x;
+}
+
 // Workspace of the training step with `planes` bf16 planes of dZ (1, or 2 for the fp32-faithful path).
 int64_t fwd_bwd_ws(int64_t n_rows, int64_t hidden, int64_t vocab, int planes) {
   if (n_rows < 1 || vocab < 1) return -1;
@@ -1229,7 +1314,8 @@ int64_t fwd_bwd_ws(int64_t n_rows, int64_t hidden, int64_t vocab, int planes) {
 int fwd_bwd_core(const void* hs, const void* ht, const void* w, const uint8_t* mask, int64_t n_rows, int64_t hidden,
                  int64_t vocab, float inv_temp, int count_given, float* count, const float* grad, float* loss,
                  float* lse, float* row_kl, float* d_hs, float* d_w, void* workspace, int64_t workspace_bytes,
-                 cudaStream_t s, int planes, void* const* chunk_events = nullptr, int n_events = 0) {
+                 cudaStream_t s, int planes, void* const* chunk_events = nullptr, int n_events = 0,
+                 const klg::XrSync* xs = nullptr) {
   int rc;
   const FwdBwdLayout L = fwd_bwd_layout(n_rows, hidden, vocab, workspace_bytes, planes);
   if (L.cols < 0)
@@ -1248,8 +1334,16 @@ int fwd_bwd_core(const void* hs, const void* ht, const void* w, const uint8_t* m
   // pass 2: dZ chunks (+ KL cross-term partials) and the dW / dH GEMMs
   int n_ap = 0;
   __nv_bfloat16* dz = reinterpret_cast<__nv_bfloat16*>(ws + L.dz_off);
+  klg::XrArgs xa{};
+  if (xs) {
+    xa.world = xs->world;
+    xa.rank = xs->rank;
+    xa.rows_per_owner = xs->rows_per_owner;
+    xa.tma = xr_tma_on() ? 1 : 0;
+    for (int p = 0; p < xs->world; ++p) xa.inbox[p] = xs->inbox_peer[p];
+  }
   if ((rc = run_pass2(hs, ht, w, mask, lse, count, grad, n_rows, hidden, vocab, inv_temp, d_hs, d_w, dz,
-                      L.cols, a_parts, &n_ap, s, planes == 2, chunk_events, n_events)))
+                      L.cols, a_parts, &n_ap, s, planes == 2, chunk_events, n_events, xs ? &xa : nullptr)))
     return rc;
   if (n_ap > L.n_ap) return fail(KLG_ERR_ARG, "internal plan mismatch (cross-term partials)");
   // per-row KL in 256-row blocks (block sums reuse the pass-1 partial area); the last block
@@ -1262,6 +1356,7 @@ int fwd_bwd_core(const void* hs, const void* ht, const void* w, const uint8_t* m
   trace_post(slot, s, KLG_KIND_FINALIZE);
   if (e != cudaSuccess) return cuda_fail(e, "launch row_kl_pair_kernel");
   ++g_launches;
+  if (xs) return launch_xr(*xs, s);
   return KLG_OK;
 }
 
@@ -1362,6 +1457,88 @@ int klg_fwd_bwd_events(const void* hs, const void* ht, const void* w, const uint
   NvtxRange nvtx_range("klg_fwd_bwd_events");
   return fwd_bwd_core(hs, ht, w, mask, n_rows, hidden, vocab, inv_temp, count_given, count, grad, loss, lse, row_kl,
                       d_hs, d_w, workspace, workspace_bytes, (cudaStream_t)stream, 1, chunk_events, n_events);
+}
+
+int64_t klg_xr_buffer_bytes(int64_t vocab, int64_t hidden, int world) {
+  if (vocab < 1 || hidden < 8 || hidden % 8 != 0 || world < 2 || world > klg::XR_MAX_WORLD) return -1;
+  const int64_t rpo = xr_rows_per_owner(vocab, world);
+  return ((int64_t)2 * world + 1) * rpo * hidden * 4 + 256;   // flags and split records: 192 of 256 bytes
+}
+
+int klg_fwd_bwd_xr(const void* hs, const void* ht, const void* w, const uint8_t* mask, int64_t n_rows, int64_t hidden,
+                   int64_t vocab, float inv_temp, int count_given, float* count, const float* grad, float* loss,
+                   float* lse, float* row_kl, float* d_hs, float* d_w, void* workspace, int64_t workspace_bytes,
+                   int world, int rank, void* const* peer_buffers, uint32_t epoch, void* stream) {
+  int rc = check_problem(hs, ht, w, n_rows, hidden, vocab, inv_temp);
+  if (rc) return rc;
+  if (!mask || !count || !loss || !lse || !d_w) return fail(KLG_ERR_ARG, "null mask/count/loss/lse/d_w");
+  if (world < 2 || world > klg::XR_MAX_WORLD || rank < 0 || rank >= world || !peer_buffers)
+    return fail(KLG_ERR_ARG, "world %d / rank %d out of range or no peer buffers", world, rank);
+  for (int p = 0; p < world; ++p)
+    if (!peer_buffers[p] || !aligned16(peer_buffers[p])) return fail(KLG_ERR_ALIGN, "peer buffer %d null or misaligned", p);
+  if ((d_hs && !aligned16(d_hs)) || !aligned16(d_w)) return fail(KLG_ERR_ALIGN, "outputs must be 16-byte aligned");
+  if (!workspace || !aligned16(workspace)) return fail(KLG_ERR_WORKSPACE, "null or misaligned workspace");
+  if ((rc = bind_device(hs))) return rc;
+  NvtxRange nvtx_range("klg_fwd_bwd_xr");
+  klg::XrSync xs = xr_sync(vocab, hidden, world, rank, peer_buffers, epoch, d_w);
+  // which chunks split dW's K (the GEMM's plan): their rows carry a second half in slot 1
+  const FwdBwdLayout L = fwd_bwd_layout(n_rows, hidden, vocab, workspace_bytes);
+  if (L.cols > 0) {
+    const int bn = gemm_bn(hidden);
+    const int64_t last_start = (int64_t)(cdiv(vocab, L.cols) - 1) * L.cols;
+    xs.cols = (int)L.cols;
+    xs.last_start = (int)last_start;
+    xs.split_full = pick_dw_split((int)n_rows, (int)L.cols, (int)hidden, bn) > 0;
+    xs.split_last = pick_dw_split((int)n_rows, (int)(vocab - last_start), (int)hidden, bn) > 0;
+  }
+  return fwd_bwd_core(hs, ht, w, mask, n_rows, hidden, vocab, inv_temp, count_given, count, grad, loss, lse, row_kl,
+                      d_hs, d_w, workspace, workspace_bytes, (cudaStream_t)stream, 1, nullptr, 0, &xs);
+}
+
+int klg_xr_alloc(int device, int64_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes < 1) return fail(KLG_ERR_ARG, "bad arguments to klg_xr_alloc");
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice (klg_xr_alloc)");
+  void* p = nullptr;
+  if ((e = cudaMalloc(&p, (size_t)bytes)) != cudaSuccess) return cuda_fail(e, "cudaMalloc (exchange buffer)");
+  if ((e = cudaMemset(p, 0, (size_t)bytes)) != cudaSuccess ||
+      (e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), p)) != cudaSuccess ||
+      (e = cudaDeviceSynchronize()) != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "exchange buffer set-up");
+  }
+  *ptr = p;
+  return KLG_OK;
+}
+
+int klg_xr_open(int device, const void* handle, void** ptr) {
+  if (!ptr || !handle) return fail(KLG_ERR_ARG, "bad arguments to klg_xr_open");
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice (klg_xr_open)");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  if ((e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess)) != cudaSuccess)
+    return cuda_fail(e, "cudaIpcOpenMemHandle (peer exchange buffer)");
+  return KLG_OK;
+}
+
+int klg_xr_close(void* ptr, int own) {
+  if (!ptr) return KLG_OK;
+  cudaError_t e = own ? cudaFree(ptr) : cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? KLG_OK : cuda_fail(e, "exchange buffer release");
+}
+
+int klg_selftest_xr_timeout(void* buffer, int64_t vocab, int64_t hidden, void* stream) {
+  if (!buffer || !aligned16(buffer) || klg_xr_buffer_bytes(vocab, hidden, 2) < 0)
+    return fail(KLG_ERR_ARG, "bad arguments to klg_selftest_xr_timeout");
+  if (int rc = bind_device(buffer)) return rc;
+  void* bufs[2] = {buffer, buffer};
+  klg::XrSync x = xr_sync(vocab, hidden, 2, 0, bufs, 1u, nullptr);
+  x.stall = 1;
+  cudaError_t e = launch_k(klg::xr_reduce_kernel, dim3(1), dim3(256), 0, (cudaStream_t)stream, 1, x);
+  if (e != cudaSuccess) return cuda_fail(e, "launch xr_reduce_kernel (self-test)");
+  ++g_launches;
+  return KLG_OK;
 }
 
 // ---------------------------------------------------------------- fp32-faithful path

@@ -1163,9 +1163,27 @@ struct PairSchedule {
   uint32_t tile[PAIR_MAX_TILES];           // tile ids, grouped by pair
   uint16_t start[PAIR_MAX_CLUSTERS + 1];   // pair c runs tile[start[c] .. start[c+1])
 };
+// Cross-rank dW exchange (row sharding over NVLink, see klg_xr.cuh): problem 0's C tiles are
+// not written to C but stored, 32-row block by 32-row block, into the owning rank's inbox.
+// Block b of dW (rows 32b .. 32b + 31) belongs to rank b % world, at inbox row
+// (b / world) * 32 of slot (src rank, K half) -- [world][2][rows_per_owner][H] fp32 per rank.
+constexpr int XR_MAX_WORLD = 8;
+struct XrArgs {
+  int world;                        // 0: no cross-rank exchange
+  int rank;
+  int rows_per_owner;               // multiple of 32
+  int tma;                          // 1: TMA tensor stores through XrMaps; 0: 16-byte stores from registers
+  float* inbox[XR_MAX_WORLD];       // each rank's inbox base (peer pointers)
+};
+// Tensor maps of every rank's inbox, [2 * world * rows_per_owner][H] fp32, 32 x 32 boxes
+// (128-byte swizzle), for the TMA form of the exchange's stores.
+struct XrMaps {
+  CUtensorMap m[XR_MAX_WORLD];
+};
 struct PairGemmArgs {
   GemmProblem p[2];   // n_mt counts 256-row pair tiles
   int n_tiles;
+  XrArgs xr;
 };
 
 #ifndef KLG_GEMM_KPS
@@ -1222,7 +1240,8 @@ __global__ void __launch_bounds__(PairGemmCfg<BN>::THREADS, 1)
 gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_constant__ CUtensorMap map_b0,
                  const __grid_constant__ CUtensorMap map_a1, const __grid_constant__ CUtensorMap map_b1,
                  const __grid_constant__ CUtensorMap map_c0, const __grid_constant__ CUtensorMap map_c1,
-                 const PairGemmArgs g, const __grid_constant__ PairSchedule sched) {
+                 const PairGemmArgs g, const __grid_constant__ PairSchedule sched,
+                 const __grid_constant__ XrMaps xm) {
   using Cfg = PairGemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int EPI = Cfg::EPI_WARPS;
@@ -1398,6 +1417,32 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_consta
         tmem_wait_ld_regs(v);
         const int col0 = nt * BN + c * 32;
         if (row_blk >= P.M || col0 >= P.Ncol) continue;   // warp-uniform
+        const bool xr_blk = pi == 0 && g.xr.world > 0;
+        const int xr_vb = P.c_row0 + row_blk;            // first dW row of this 32-row block (multiple of 32)
+        const int xr_owner = xr_blk ? (xr_vb >> 5) % g.xr.world : 0;
+        const int xr_row = xr_blk ? (g.xr.rank * 2 + (kb0 > 0 ? 1 : 0)) * g.xr.rows_per_owner +
+                                        ((xr_vb >> 5) / g.xr.world) * 32
+                                  : 0;                   // inbox row of the block: slot (rank, K half), owner's row
+        if (xr_blk && !g.xr.tma) {
+          // dW block to its owner's inbox (plain 16-byte stores over NVLink, no atomics): rows
+          // past M are not written; the K half (split tiles) picks the slot
+          const int owner = xr_owner;
+          const int orow = ((xr_vb >> 5) / g.xr.world) * 32 + lane;
+          const int slot = g.xr.rank * 2 + (kb0 > 0 ? 1 : 0);
+          // columns past Ncol (H not a multiple of 32) are not written either: H % 8 == 0, so the
+          // block's valid columns are whole float4s
+          const int n4 = min(8, (P.Ncol - col0) >> 2);
+          if (row_blk + lane < P.M) {
+            float4* dst = reinterpret_cast<float4*>(g.xr.inbox[owner] +
+                                                    ((size_t)slot * g.xr.rows_per_owner + orow) * P.ldc + col0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              if (j < n4)
+                dst[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                     __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+          }
+          continue;
+        }
         if (lane == 0) {                                   // the buffer written STG_BUFS blocks ago is free
           if (Cfg::STG_BUFS == 2) bulk_wait_read1();
           else bulk_wait_read0();
@@ -1411,7 +1456,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a0, const __grid_consta
         fence_async_shared();
         __syncwarp();
         if (lane == 0) {
-          if (P.accumulate) tma_reduce_add_2d(mc, stg + (uint32_t)sbuf * 4096u, col0, P.c_row0 + row_blk);
+          if (xr_blk) tma_store_2d(&xm.m[xr_owner], stg + (uint32_t)sbuf * 4096u, col0, xr_row);   // owner's inbox
+          else if (P.accumulate) tma_reduce_add_2d(mc, stg + (uint32_t)sbuf * 4096u, col0, P.c_row0 + row_blk);
           else tma_store_2d(mc, stg + (uint32_t)sbuf * 4096u, col0, P.c_row0 + row_blk);
           bulk_commit();
         }

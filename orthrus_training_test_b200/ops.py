@@ -265,6 +265,33 @@ def kl_fwd_bwd(h_s, h_t, weight, mask, temperature: float = 1.0, count: Optional
     return loss, lse, cnt, row_kl, dh, dw
 
 
+def kl_fwd_bwd_xr(h_s, h_t, weight, mask, temperature: float, count: torch.Tensor, need_dh: bool, world: int,
+                  rank: int, peer_buffers, epoch: int, workspace_bytes: Optional[int] = None):
+    """Row-sharded training step whose dW is summed over the ranks inside the step, over NVLink
+    peer memory (``klg_fwd_bwd_xr``): ``peer_buffers`` is a ctypes array of every rank's exchange
+    buffer, ``epoch`` 1, 2, ... per call (the same on every rank), ``count`` the global count.
+    bf16 inputs.  Returns ``(loss of the local rows, dH_s fp32 or None, dW fp32 summed over ranks)``.
+    """
+    m = mask_u8(mask)
+    dev = _require_cuda(h_s, h_t, weight, m)
+    N, H = h_s.shape
+    V = weight.shape[0]
+    if h_t.shape != h_s.shape or weight.shape[1] != H or m.numel() != N:
+        raise ValueError(f"shape mismatch: h_s {tuple(h_s.shape)} h_t {tuple(h_t.shape)} "
+                         f"weight {tuple(weight.shape)} mask {tuple(m.shape)}")
+    if workspace_bytes is None:
+        workspace_bytes = int(_lib.lib().klg_fwd_bwd_workspace_bytes(N, H, V))
+    ws = torch.empty(int(workspace_bytes), dtype=torch.uint8, device=dev)
+    loss = torch.empty((), dtype=torch.float32, device=dev)
+    lse = torch.empty(2, N, dtype=torch.float32, device=dev)
+    dh = torch.empty(N, H, dtype=torch.float32, device=dev) if need_dh else None
+    dw = torch.empty(V, H, dtype=torch.float32, device=dev)
+    call("klg_fwd_bwd_xr", _ptr(h_s), _ptr(h_t), _ptr(weight), _ptr(m), N, H, V, 1.0 / float(temperature), 1,
+         _ptr(count), None, _ptr(loss), _ptr(lse), None, _ptr(dh), _ptr(dw), _ptr(ws), int(workspace_bytes),
+         int(world), int(rank), peer_buffers, ctypes.c_uint32(int(epoch) & 0xFFFFFFFF), _stream(dev))
+    return loss, dh, dw
+
+
 # ----------------------------------------------------------------- the training step in pieces
 
 def lse_record(h_s, h_t, weight, temperature: float = 1.0) -> torch.Tensor:

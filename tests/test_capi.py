@@ -72,6 +72,20 @@ def test_argument_validation_codes():
     assert L.klg_scale_cast(p, None, -1, p, 1, None) == _lib.KLG_ERR_ARG
     assert L.klg_scale_cast(odd, None, 4, p, 1, None) == _lib.KLG_ERR_ALIGN
     assert L.klg_scale_cast(p, None, 0, p, 0, None) == 0
+    # peer-memory dW exchange: buffer size and the argument checks made before any device call
+    assert L.klg_xr_buffer_bytes(49152, 576, 1) == -1 and L.klg_xr_buffer_bytes(49152, 576, 9) == -1
+    assert L.klg_xr_buffer_bytes(49152, 576, 4) == (2 * 4 + 1) * 12288 * 576 * 4 + 256
+    bufs = (ctypes.c_void_p * 2)(p, p)
+    assert L.klg_fwd_bwd_xr(p, p, p, p, 4, 64, 4, 1.0, 1, p, None, p, p, None, p, p, p, 1 << 16, 1, 0, bufs, 1,
+                            None) == _lib.KLG_ERR_ARG                                   # world < 2
+    assert L.klg_fwd_bwd_xr(p, p, p, p, 4, 64, 4, 1.0, 1, p, None, p, p, None, p, p, p, 1 << 16, 2, 2, bufs, 1,
+                            None) == _lib.KLG_ERR_ARG                                   # rank >= world
+    assert L.klg_fwd_bwd_xr(p, p, p, p, 4, 64, 4, 1.0, 1, p, None, p, p, None, p, None, p, 1 << 16, 2, 0, bufs, 1,
+                            None) == _lib.KLG_ERR_ARG                                   # no dW
+    odd_bufs = (ctypes.c_void_p * 2)(p, odd)
+    assert L.klg_fwd_bwd_xr(p, p, p, p, 4, 64, 4, 1.0, 1, p, None, p, p, None, p, p, p, 1 << 16, 2, 0, odd_bufs, 1,
+                            None) == _lib.KLG_ERR_ALIGN
+    assert L.klg_selftest_xr_timeout(None, 1000, 128, None) == _lib.KLG_ERR_ARG
     # both outputs NULL: nothing to do, succeeds without touching the device
     assert L.klg_bwd(p, p, p, p, p, p, None, 4, 64, 4, 1.0, None, None, p, 1 << 16, None) == 0
     del keep

@@ -88,3 +88,29 @@ def test_attention_split_timeout_reports_and_cluster_exits():
     ro, _ = O.block_attention_np(q.float().cpu().numpy(), ks.float().cpu().numpy(), vs.float().cpu().numpy(),
                                  ka.float().cpu().numpy(), va.float().cpu().numpy(), lim.cpu().numpy(), K)
     assert float((o.float().cpu() - torch.tensor(ro)).abs().max()) <= 3e-2
+
+
+def test_exchange_wait_on_a_missing_rank_times_out():
+    """The in-step dW exchange waits for every rank's epoch flag; a rank that never arrives
+    (here: an epoch nobody publishes, on one GPU, through the test hook) makes the wait give up
+    after its bound with KLG_STATUS_TIMEOUT_PEER instead of hanging, and the context stays usable."""
+    from orthrus_training_test_b200 import _lib, ops
+
+    KLG_STATUS_TIMEOUT_PEER = 0x10
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    V, H = 1000, 128
+    nbytes = int(_lib.lib().klg_xr_buffer_bytes(V, H, 2))
+    assert nbytes > 0
+    buf = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+    assert _lib.device_status(reset=True) == 0
+    t0 = time.perf_counter()
+    _lib.call("klg_selftest_xr_timeout", ops._ptr(buf), V, H, ops._stream(dev))
+    torch.cuda.synchronize()
+    waited = time.perf_counter() - t0
+    status = _lib.device_status(reset=True)
+    assert status == KLG_STATUS_TIMEOUT_PEER, hex(status)
+    assert 0.2 < waited < 30.0, waited
+    x = torch.ones(1 << 20, device=dev)
+    assert float(x.sum()) == float(1 << 20)         # the context still runs kernels
+    assert _lib.device_status(reset=True) == 0

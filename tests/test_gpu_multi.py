@@ -1,7 +1,9 @@
 """Row and vocab sharding on 2, 4 and 8 GPUs (one process per GPU, NCCL), through the CUDA
 library, against the fp32 oracle.
 
-Each rank runs the sharded loss on its slice; the loss and the assembled gradients must
+Each rank runs the sharded loss on its slice; row sharding three times, with dW all-reduced
+by NCCL ("row") or summed over the ranks inside the step over NVLink peer memory ("row_xr",
+bitwise the same dW in every step and on every rank).  The loss and the assembled gradients must
 match the fp32 torch oracle (the reference's op sequence, run on cuda:0 over the whole
 problem) within the tolerances every GPU parity test uses: loss 1e-3 relative, gradients
 2e-2 normalised max error and cosine similarity >= 0.9999.  Two problems: a small one with a
@@ -51,6 +53,9 @@ def _worker(rank, world, port, mode, name, out_q):
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
         os.environ["NCCL_NVLS_ENABLE"] = "0"
+        # "row": dW all-reduced by NCCL (the default); "row_xr": dW summed over the ranks inside
+        # the step over NVLink peer memory
+        os.environ["KLG_XR"] = "1" if mode == "row_xr" else "0"
         torch.cuda.set_device(rank)
         dev = torch.device("cuda", rank)
         dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
@@ -58,20 +63,35 @@ def _worker(rank, world, port, mode, name, out_q):
 
         h_s, h_t, W, mask, T = _problem(name)
         N, V = h_s.shape[0], W.shape[0]
-        if mode == "row":
+        row = mode.startswith("row")
+        dws = []
+        if row:
             lo, hi = shard_bounds(N, world, rank)
             hs = h_s[lo:hi].to(dev).requires_grad_(True)
             w = W.to(dev).requires_grad_(True)
-            loss = row_sharded_kl_loss(hs, h_t[lo:hi].to(dev), w, mask[lo:hi].to(dev), T)
+            # three steps: the exchange's epochs order consecutive steps; dW is the same every time
+            for _ in range(3):
+                hs.grad = None
+                w.grad = None
+                loss = row_sharded_kl_loss(hs, h_t[lo:hi].to(dev), w, mask[lo:hi].to(dev), T)
+                loss.backward()
+                dws.append(w.grad.detach().clone())
         else:
             lo, hi = shard_bounds(V, world, rank)
             hs = h_s.to(dev).requires_grad_(True)
             w = W[lo:hi].to(dev).requires_grad_(True)
             loss = vocab_sharded_kl_loss(hs, h_t.to(dev), w, mask.to(dev), T)
-        loss.backward()
+            loss.backward()
+        if row:
+            # bitwise the same dW in every step, and (all-gathered) on every rank
+            assert all(torch.equal(d, dws[0]) for d in dws[1:]), "dW changed between identical steps"
+            allw = [torch.empty_like(dws[0]) for _ in range(world)]
+            dist.all_gather(allw, dws[0])
+            if mode == "row_xr":
+                assert all(torch.equal(d, allw[0]) for d in allw[1:]), "dW differs between ranks"
         # the evaluation route (no gradients) on the same shards
         with torch.no_grad():
-            if mode == "row":
+            if row:
                 loss_eval = row_sharded_kl_loss(hs.detach(), h_t[lo:hi].to(dev), w.detach(), mask[lo:hi].to(dev), T)
             else:
                 loss_eval = vocab_sharded_kl_loss(hs.detach(), h_t.to(dev), w.detach(), mask.to(dev), T)
@@ -92,7 +112,7 @@ def _close(a, b, what):
 
 @pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("name", ["small", "c5"])
-@pytest.mark.parametrize("mode", ["row", "vocab"])
+@pytest.mark.parametrize("mode", ["row", "row_xr", "vocab"])
 def test_sharding_matches_oracle(mode, name, world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
@@ -116,7 +136,7 @@ def test_sharding_matches_oracle(mode, name, world):
     for _, loss, _, _, _, loss_eval in res:
         assert abs(loss - ref_loss) <= LOSS_RTOL * abs(ref_loss), (loss, ref_loss)
         assert abs(loss_eval - ref_loss) <= LOSS_RTOL * abs(ref_loss), (loss_eval, ref_loss)
-    if mode == "row":
+    if mode.startswith("row"):
         _close(torch.cat([r[3] for r in res]), ref_dh, "dH")
         for r in res:
             _close(r[4], ref_dw, "dW (all-reduced)")
