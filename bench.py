@@ -765,9 +765,11 @@ def main():
             return step_vocab()
         if prenorm:
             return step_prenorm()
-        # the training step: count (all-reduced across ranks) -> loss + dH + dW -> loss and dW all-reduced
-        cnt = ops.count_valid(m)
+        # the training step: count (all-reduced across ranks) -> loss + dH + dW -> loss and dW all-reduced;
+        # on one GPU the step counts the mask itself (inside its pass-1 merge), as the autograd op does
+        cnt = None
         if world > 1:
+            cnt = ops.count_valid(m)
             dist.all_reduce(cnt)
         if xr is not None:
             loss, dh, dw = ops.kl_fwd_bwd_xr(hs, ht, W, m, T, cnt, True, xr.world, xr.rank, xr.peer_buffers,
