@@ -6,10 +6,14 @@
 //
 //  lse_pair_kernel     training pass 1: per view, online (max, sum 2^(u - max)) per row
 //                      over all vocab tiles (row block resident for H <= 576).
-//  dual_pair_kernel    both views' logit tiles per (row pair tile, vocab tile):
+//  dual_pair_kernel    both views' logit tiles per (row pair tile, vocab tile), one MMA per
+//                      view (the row-major form; the interleaved-view kernel of
+//                      klg_dzi.cuh, one MMA for both views, is the default for both modes):
 //     <MODE_DZ>        training pass 2: dZ = g valid/count (q - p)/T as bf16 for one vocab
-//                      chunk, plus the KL cross term sum_v p (u_t - u_s) per unit;
-//     <MODE_STATS>     forward only: per unit the online (m_s, S_s, m_t, S_t, A) record.
+//                      chunk, plus the KL cross term sum_v p (u_t - u_s) per unit (the
+//                      fp32-faithful path's two dZ planes; bf16 with KLG_DZI=0);
+//     <MODE_STATS>     forward only: per unit the online (m_s, S_s, m_t, S_t, A) record
+//                      (N % 8 != 0 or KLG_DZI=0).
 //  gemm_pair_kernel    C (+)= A B over one backward chunk: dW_chunk = dZ^T h_s and
 //                      dH += dZ W_chunk in one launch (host-built longest-first schedule).
 //
