@@ -83,7 +83,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-overlap", action="store_true",
-                    help="row sharding: one dW all-reduce after the step instead of per-chunk buckets overlapped")
+                    help="row sharding: one dW all-reduce after the step instead of per-chunk buckets overlapped "
+                         "(the default from 8 ranks)")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="nccl",
                     help="row sharding: dW all-reduced by NCCL, overlapped per chunk (nccl), or summed inside "
                          "the step over NVLink peer memory (p2p)")
@@ -755,7 +756,9 @@ def main():
         xr = CudaEngine().xr_exchange(None, hs, W)
         if xr is None:
             os.environ["KLG_XR"] = "0"   # the e2e leg below takes the same (NCCL) route
-    overlap = world > 1 and xr is None and not vocab_sharded and not prenorm and not args.no_overlap
+    # per-chunk overlapped buckets up to 4 ranks (as row_sharded_kl_loss): at 8 ranks one
+    # all-reduce after the step measured faster
+    overlap = 1 < world < 8 and xr is None and not vocab_sharded and not prenorm and not args.no_overlap
     buckets = ops.chunk_bounds(N, H, V_work, fb_ws) if overlap else None
     chunk_evs = ops.new_chunk_events(len(buckets)) if overlap else None
     side = torch.cuda.Stream(device=dev) if overlap else None

@@ -12,7 +12,7 @@ H=576, V=49,152, ~25 % of rows valid, teacher x4, T=2, all-masked rows).
 Skipped when fewer GPUs than ranks are visible.  NVLS is off in every rank.
 """
 import os
-import socket
+import tempfile
 import traceback
 from datetime import timedelta
 
@@ -23,14 +23,6 @@ from oracle import klgemm_oracle as O
 from tests.gpu_helpers import GRAD_COS, GRAD_MAX_REL, LOSS_RTOL, run_oracle_torch_gpu
 
 pytestmark = pytest.mark.gpu
-
-
-def _free_port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    port = s.getsockname()[1]
-    s.close()
-    return port
 
 
 def _problem(name):
@@ -47,18 +39,18 @@ def _problem(name):
     return h_s, h_t, W, mask, 1.5
 
 
-def _worker(rank, world, port, mode, name, out_q):
+def _worker(rank, world, init_file, mode, name, out_q):
     try:
         import torch.distributed as dist
-        os.environ["MASTER_ADDR"] = "127.0.0.1"
-        os.environ["MASTER_PORT"] = str(port)
         os.environ["NCCL_NVLS_ENABLE"] = "0"
         # "row": dW all-reduced by NCCL (the default); "row_xr": dW summed over the ranks inside
         # the step over NVLink peer memory
         os.environ["KLG_XR"] = "1" if mode == "row_xr" else "0"
         torch.cuda.set_device(rank)
         dev = torch.device("cuda", rank)
-        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+        # rendezvous through a file: no TCP port to collide with a previous test's
+        dist.init_process_group("nccl", init_method=f"file://{init_file}", rank=rank, world_size=world,
+                                timeout=timedelta(seconds=60), device_id=dev)
         from orthrus_training_test_b200.parallel import row_sharded_kl_loss, shard_bounds, vocab_sharded_kl_loss
 
         h_s, h_t, W, mask, T = _problem(name)
@@ -123,8 +115,8 @@ def test_sharding_matches_oracle(mode, name, world):
     torch.cuda.synchronize()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, name, q)) for r in range(world)]
+    init_file = os.path.join(tempfile.mkdtemp(prefix="klg_multi_"), "rendezvous")
+    procs = [ctx.Process(target=_worker, args=(r, world, init_file, mode, name, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=600) for _ in range(world)]
