@@ -38,44 +38,120 @@ def _scale_grad(x: torch.Tensor, g: torch.Tensor, dtype: torch.dtype) -> torch.T
     return scale_grad(x, g, dtype)
 
 
+class _XrNative:
+    """The library calls behind the exchange buffers (``klg_xr_alloc`` / ``klg_xr_open`` /
+    ``klg_xr_close``).  Tests substitute a fake with the same three methods to run the set-up's
+    agreement logic on ``gloo`` ranks."""
+
+    def buffer_bytes(self, vocab: int, hidden: int, world: int) -> int:
+        from . import _lib
+        return int(_lib.lib().klg_xr_buffer_bytes(int(vocab), int(hidden), int(world)))
+
+    def alloc(self, device: int, nbytes: int):
+        """``(pointer, 64-byte IPC handle)`` of a new zero-filled buffer on ``device``."""
+        import ctypes
+
+        from . import _lib
+        own = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        _lib.call("klg_xr_alloc", device, nbytes, ctypes.byref(own), handle)
+        return own.value, handle.raw
+
+    def open(self, device: int, handle: bytes) -> int:
+        import ctypes
+
+        from . import _lib
+        q = ctypes.c_void_p()
+        _lib.call("klg_xr_open", device, ctypes.create_string_buffer(handle, 64), ctypes.byref(q))
+        return q.value
+
+    def close(self, ptr: int, own: bool) -> None:
+        import ctypes
+
+        from . import _lib
+        _lib.call("klg_xr_close", ctypes.c_void_p(ptr), int(bool(own)))
+
+    def synchronize(self, device: int) -> None:
+        torch.cuda.synchronize(device)
+
+
+class XrSetupError(RuntimeError):
+    """The exchange could not be set up on some rank; raised on every rank alike."""
+
+
 class _XrExchange:
     """One rank's buffer for the in-step dW exchange over NVLink (``klg_fwd_bwd_xr``) and its
     mappings of every other rank's: each rank allocates and zero-fills its own buffer
     (``klg_xr_alloc``), the CUDA IPC handles are all-gathered, and each rank opens the others'
-    (``klg_xr_open``: plain peer mappings).  All ranks meet at a barrier before the first step
-    pushes into the buffers.  The epoch counter orders the steps."""
+    (``klg_xr_open``: plain peer mappings).  The ranks agree on the outcome of each stage
+    before the next, so a failure on one rank makes every rank release what it holds and raise
+    :class:`XrSetupError` -- no rank goes on to a collective the others skip.  All ranks meet
+    at a barrier before the first step pushes into the buffers.  The epoch counter orders the
+    steps."""
 
-    def __init__(self, group, vocab: int, hidden: int, device: torch.device):
+    def __init__(self, group, vocab: int, hidden: int, device: torch.device, native=None):
         import ctypes
 
-        from . import _lib
-        lib = _lib.lib()
+        self.native = native if native is not None else _XrNative()
+        self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
-        nbytes = int(lib.klg_xr_buffer_bytes(int(vocab), int(hidden), self.world))
-        if nbytes < 0:
-            raise ValueError("no exchange buffer for this shape / world")
-        dev = device.index if device.index is not None else torch.cuda.current_device()
-        own = ctypes.c_void_p()
-        handle = ctypes.create_string_buffer(64)
-        _lib.call("klg_xr_alloc", dev, nbytes, ctypes.byref(own), handle)
-        self._own = own.value
-        handles = [None] * self.world
-        dist.all_gather_object(handles, handle.raw, group=group)
+        self._dev = device.index if device.index is not None else torch.cuda.current_device()
+        self._own = None
         self._peers = []
+        err = None
+        nbytes = self.native.buffer_bytes(vocab, hidden, self.world)
+        handle = None
+        if nbytes < 0:
+            err = "no exchange buffer for this shape / world"
+        else:
+            try:
+                self._own, handle = self.native.alloc(self._dev, nbytes)
+            except Exception as e:
+                err = f"rank {self.rank}: {e}"
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)          # every rank reaches this
+        if any(h is None for h in handles):
+            self._release(barrier=False)                              # nobody opened anything
+            raise XrSetupError(err or "exchange buffer allocation failed on another rank")
         ptrs = []
         for p in range(self.world):
             if p == self.rank:
                 ptrs.append(self._own)
                 continue
-            q = ctypes.c_void_p()
-            _lib.call("klg_xr_open", dev, ctypes.create_string_buffer(handles[p], 64), ctypes.byref(q))
-            self._peers.append(q.value)
-            ptrs.append(q.value)
+            try:
+                q = self.native.open(self._dev, handles[p])
+            except Exception as e:
+                err = f"rank {self.rank} opening rank {p}'s buffer: {e}"
+                break
+            self._peers.append(q)
+            ptrs.append(q)
+        oks = [None] * self.world
+        dist.all_gather_object(oks, err is None, group=group)
+        if not all(oks):
+            self._release(barrier=True)
+            raise XrSetupError(err or "exchange buffer mapping failed on another rank")
         self.peer_buffers = (ctypes.c_void_p * self.world)(*ptrs)
-        torch.cuda.synchronize(device)
+        self.native.synchronize(self._dev)
         dist.barrier(group=group)
         self.epoch = 0
+
+    def _release(self, barrier: bool) -> None:
+        # peer mappings first; with `barrier`, every rank has closed its mappings before any
+        # owner frees its buffer
+        for q in self._peers:
+            self.native.close(q, own=False)
+        self._peers = []
+        if barrier:
+            dist.barrier(group=self.group)
+        if self._own is not None:
+            self.native.close(self._own, own=True)
+            self._own = None
+
+    def close(self) -> None:
+        """Collective: every rank of the group calls it, with no step in flight."""
+        self.native.synchronize(self._dev)
+        self._release(barrier=True)
 
     def next_epoch(self) -> int:
         self.epoch += 1
@@ -154,7 +230,7 @@ class CudaEngine:
         if ex is None:
             try:
                 ex = _XrExchange(group, w.shape[0], w.shape[1], h_s.device)
-            except Exception as e:   # every rank fails alike: the set-up is collective
+            except XrSetupError as e:   # raised on every rank alike: the set-up agrees first
                 import warnings
                 warnings.warn(f"peer-memory dW exchange unavailable ({e}); using an NCCL all-reduce")
                 _XR_BROKEN.add(key)

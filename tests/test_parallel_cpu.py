@@ -149,3 +149,78 @@ def test_shard_bounds_cover_vocab():
         assert b[0][0] == 0 and b[-1][1] == V
         assert all(b[i][1] == b[i + 1][0] for i in range(P - 1))
         assert max(h - l for l, h in b) - min(h - l for l, h in b) <= 1
+
+
+class _FakeXrNative:
+    """Stands in for the exchange buffers' library calls: pointers are integers, a handle names
+    its owner, and one chosen stage can fail on one chosen rank."""
+
+    def __init__(self, rank, fail):
+        self.rank, self.fail = rank, fail
+        self.held = set()        # buffers allocated or mapped and not yet released
+
+    def buffer_bytes(self, vocab, hidden, world):
+        return 4096
+
+    def alloc(self, device, nbytes):
+        if self.fail == ("alloc", self.rank):
+            raise RuntimeError("cudaMalloc failed (fake)")
+        self.held.add(("own", self.rank))
+        return 1000 + self.rank, bytes([self.rank]) * 64
+
+    def open(self, device, handle):
+        if self.fail == ("open", self.rank):
+            raise RuntimeError("cudaIpcOpenMemHandle failed (fake)")
+        self.held.add(("peer", handle[0]))
+        return 2000 + handle[0]
+
+    def close(self, ptr, own):
+        self.held.discard(("own", ptr - 1000) if own else ("peer", ptr - 2000))
+
+    def synchronize(self, device):
+        pass
+
+
+def _xr_setup_worker(rank, world, port, fail, out_q):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
+        from orthrus_training_test_b200.parallel import XrSetupError, _XrExchange
+        native = _FakeXrNative(rank, fail)
+        try:
+            ex = _XrExchange(None, 1024, 64, torch.device("cuda", 0), native=native)
+            outcome = "ok"
+            held = sorted(native.held)
+            ex.close()
+        except XrSetupError:
+            outcome, held = "refused", None
+        dist.barrier()              # every rank is still in step with the others
+        out_q.put((rank, outcome, held, sorted(native.held)))
+        dist.destroy_process_group()
+    except Exception:
+        out_q.put((rank, "error", traceback.format_exc(), None))
+
+
+@pytest.mark.parametrize("fail", [None, ("alloc", 1), ("open", 0), ("open", 2)])
+def test_exchange_setup_agrees_across_ranks(fail):
+    """A failure to allocate or map an exchange buffer on one rank makes every rank refuse the
+    exchange (and fall back to the NCCL all-reduce) with nothing left allocated or mapped,
+    instead of one rank waiting in a collective that the others skip."""
+    world = 3
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_xr_setup_worker, args=(r, world, port, fail, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    errs = [r for r in res if r[1] == "error"]
+    assert not errs, errs[0][2]
+    assert {r[1] for r in res} == {"ok" if fail is None else "refused"}
+    for rank, outcome, held, left in res:
+        if outcome == "ok":   # its own buffer and a mapping of every other rank's
+            assert held == sorted([("own", rank)] + [("peer", p) for p in range(world) if p != rank])
+        assert left == []    # released after close() or the refusal
