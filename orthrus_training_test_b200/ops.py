@@ -1,11 +1,14 @@
 """PyTorch binding of the fused KL-GEMM distillation loss.
 
 ``KLGemmFn`` is the ``torch.autograd.Function`` that replaces the reference's
-loss arithmetic (``train.py:142-210``): its forward runs pass 1 (both views'
-logits over vocab tiles with online max / sum-exp / KL, never storing an
-``[N, V]`` tensor) and returns the scalar loss; its backward runs pass 2
-(recompute the logits chunk by chunk, form dZ, then dH_s = dZ W and
-dW = dZ^T h_s).  Saved for backward: the inputs and two log-sum-exps per row.
+loss arithmetic (``train.py:142-210``).  When a gradient will be needed its
+forward runs the whole training step: pass 1 (both views' logits over vocab
+tiles with an online max / sum-exp per row, never storing an ``[N, V]``
+tensor), then pass 2 (recompute the logits chunk by chunk, form dZ and the KL
+cross term, then dH_s = dZ W and dW = dZ^T h_s).  It saves the fp32 dH_s
+``[N, H]`` and dW ``[V, H]`` for an upstream gradient of 1, and its backward
+only scales them by the actual upstream gradient.  Without gradients the
+forward is the single-pass statistics kernel alone.
 
 Every function here calls the CUDA library; there is no CPU fallback.
 """
