@@ -166,3 +166,46 @@ def test_attention_argument_validation():
     assert L.klg_block_attn_fwd(*args(scale=0.0)) == _lib.KLG_ERR_ARG
     assert L.klg_block_attn_fwd(*args(wsb=8)) == _lib.KLG_ERR_WORKSPACE
     del keep
+
+
+_C_CALLER = r"""
+#include <stdio.h>
+#include <string.h>
+#include "klgemm.h"
+
+int main(void) {
+  char msg[256];
+  static float buf[64] __attribute__((aligned(16)));
+  if (klg_version() != KLG_VERSION) return 10;
+  /* null inputs: rejected before any device work */
+  if (klg_fwd_bwd(NULL, NULL, NULL, NULL, 16, 64, 16, 1.0f, 0, NULL, NULL, NULL, NULL, NULL, NULL, NULL, NULL, 0,
+                  NULL) != KLG_ERR_ARG) return 11;
+  if (klg_last_error(msg, (int)sizeof msg) != KLG_OK || strstr(msg, "null") == NULL) return 12;
+  /* hidden not a multiple of 8 */
+  if (klg_fwd_stats(buf, buf, buf, 4, 12, 4, 1.0f, buf, 1, NULL) != KLG_ERR_ALIGN) return 13;
+  printf("ok %d\n", klg_version());
+  return 0;
+}
+"""
+
+
+def test_plain_c_caller_builds_and_links(tmp_path):
+    """The header is plain C99 and C++, and a C program links against the library and gets
+    the documented status codes: the boundary needs no Python or torch."""
+    import shutil
+    import subprocess
+    gcc, gxx = shutil.which("gcc"), shutil.which("g++")
+    if gcc is None or gxx is None:
+        pytest.skip("no host C compiler")
+    _lib.lib()   # builds nothing; fails here if the library is missing
+    inc = ROOT / "include"
+    subprocess.run([gxx, "-fsyntax-only", "-Wall", "-Werror", "-x", "c++", str(inc / "klgemm.h")], check=True)
+    src = tmp_path / "caller.c"
+    src.write_text(_C_CALLER)
+    exe = tmp_path / "caller"
+    libdir = _lib.LIB_PATH.parent
+    subprocess.run([gcc, "-std=c99", "-Wall", "-Werror", "-I", str(inc), str(src), "-o", str(exe), f"-L{libdir}",
+                    "-lklgemm", f"-Wl,-rpath,{libdir}"], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, (out.returncode, out.stdout, out.stderr)
+    assert out.stdout.strip() == "ok 100"
