@@ -57,6 +57,31 @@ def select_rows(diff_hidden, ar_hidden_states, anchor_positions, K, target_ids, 
     return h_s, h_t, valid.reshape(-1)
 
 
+def _check_selection_shapes(diff_hidden, ar_hidden_states, anchor_positions, K, target_ids):
+    """``(B, P, H, L, B_blocks)`` of a row selection, or ValueError: every index the gather
+    kernel forms from these shapes stays inside its tensor (where train.py:156-164's torch
+    indexing would raise, this raises before anything reaches the device).  Anchor values
+    need no check: the teacher row is clamped to ``[0, L-1]``."""
+    if diff_hidden.dim() != 3 or ar_hidden_states.dim() != 3:
+        raise ValueError(f"expected diff_hidden [B, B_blocks*K, H] and ar_hidden_states [B, L, H], got "
+                         f"{tuple(diff_hidden.shape)} and {tuple(ar_hidden_states.shape)}")
+    B, P, H = diff_hidden.shape
+    L = ar_hidden_states.shape[1]
+    if ar_hidden_states.shape[0] != B or ar_hidden_states.shape[2] != H or L < 1:
+        raise ValueError(f"ar_hidden_states {tuple(ar_hidden_states.shape)} does not match diff_hidden "
+                         f"{tuple(diff_hidden.shape)} (same B and H, L >= 1)")
+    if K < 2:
+        raise ValueError(f"K={K}: a block needs an anchor and at least one diffusion position")
+    if anchor_positions.dim() != 2 or anchor_positions.shape[0] != B:
+        raise ValueError(f"anchor_positions must be [B={B}, B_blocks], got {tuple(anchor_positions.shape)}")
+    Bb = anchor_positions.shape[1]
+    if Bb < 1 or P != Bb * K:
+        raise ValueError(f"diff_hidden has {P} positions, expected B_blocks*K = {Bb * K}")
+    if target_ids.dim() != 2 or target_ids.shape[0] != B or target_ids.shape[1] < P:
+        raise ValueError(f"target_ids must be [B={B}, >= {P}], got {tuple(target_ids.shape)}")
+    return B, P, H, L, Bb
+
+
 class GatherRowsFn(torch.autograd.Function):
     """The row selection of train.py:124-139, 156-164 as one CUDA kernel.
 
@@ -70,16 +95,15 @@ class GatherRowsFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, diff_hidden, ar_hidden_states, anchor_positions, K, target_ids, pad_token_id):
+        B, P, H, L, Bb = _check_selection_shapes(diff_hidden, ar_hidden_states, anchor_positions, K, target_ids)
         dev = _require_cuda(diff_hidden, ar_hidden_states, anchor_positions, target_ids)
         diff = diff_hidden.detach().contiguous()
         ar = ar_hidden_states.detach().to(diff.dtype).contiguous()
-        B, P, H = diff.shape
-        Bb = anchor_positions.shape[1]
-        if P != Bb * K:
-            raise ValueError(f"diff_hidden has {P} positions, expected B_blocks*K = {Bb * K}")
         row_bytes = H * diff.element_size()
         anchors = anchor_positions.detach().to(torch.int64).contiguous()
-        targets = target_ids.detach().to(torch.int64).contiguous()
+        # the kernel reads target row b at b * P: positions past the diffusion positions
+        # (train.py:163 indexes only those) are dropped here
+        targets = target_ids.detach()[:, :P].to(torch.int64).contiguous()
         n = B * Bb * (K - 1)
         h_s = torch.empty(n, H, dtype=diff.dtype, device=dev)
         h_t = torch.empty(n, H, dtype=diff.dtype, device=dev)

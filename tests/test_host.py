@@ -61,3 +61,35 @@ def test_token_logprob_rejects_bad_shapes(h_shape, w_shape, n_tok, lse_shape):
     with pytest.raises(ValueError):
         token_logprob(torch.zeros(h_shape), torch.zeros(w_shape), torch.zeros(n_tok, dtype=torch.long),
                       torch.zeros(lse_shape))
+
+
+# (diff_hidden, ar_hidden_states, anchor_positions, K, target_ids) shapes; B=2, B_blocks=3, K=4, H=64
+@pytest.mark.parametrize("diff,ar,anc,K,tgt", [
+    ((2, 12, 64), (1, 20, 64), (2, 3), 4, (2, 12)),    # AR states of another batch size
+    ((2, 12, 64), (2, 20, 32), (2, 3), 4, (2, 12)),    # AR states of another hidden size
+    ((2, 12, 64), (2, 20, 64), (1, 3), 4, (2, 12)),    # anchors of another batch size
+    ((2, 12, 64), (2, 20, 64), (2, 3), 4, (2, 11)),    # too few target positions
+    ((2, 12, 64), (2, 20, 64), (2, 3), 4, (24,)),      # targets not [B, P]
+    ((2, 12, 64), (2, 20, 64), (2, 4), 4, (2, 12)),    # positions != B_blocks * K
+    ((2, 3, 64), (2, 20, 64), (2, 3), 1, (2, 3)),      # K = 1: no diffusion position
+    ((24, 64), (2, 20, 64), (2, 3), 4, (2, 12)),       # diff_hidden not 3-D
+])
+def test_row_gather_rejects_bad_shapes(diff, ar, anc, K, tgt):
+    """Every index the gather kernel forms stays inside its tensor: inconsistent shapes raise
+    on the host (where the reference's torch indexing would raise) before any device work."""
+    from orthrus_training_test_b200.loss import gather_rows
+    with pytest.raises(ValueError):
+        gather_rows(torch.zeros(diff), torch.zeros(ar), torch.zeros(anc, dtype=torch.long), K,
+                    torch.zeros(tgt, dtype=torch.long), 0)
+
+
+def test_row_gather_accepts_longer_targets():
+    """target_ids wider than the diffusion positions pass the shape check (only the first
+    B_blocks*K positions are read, as train.py:163 indexes them)."""
+    from orthrus_training_test_b200.loss import _check_selection_shapes
+    assert _check_selection_shapes(torch.zeros(2, 12, 64), torch.zeros(2, 20, 64), torch.zeros(2, 3), 4,
+                                   torch.zeros(2, 16)) == (2, 12, 64, 20, 3)
+    with pytest.raises(RuntimeError, match="CUDA"):   # consistent shapes reach the device check
+        from orthrus_training_test_b200.loss import gather_rows
+        gather_rows(torch.zeros(2, 12, 64), torch.zeros(2, 20, 64), torch.zeros(2, 3, dtype=torch.long), 4,
+                    torch.zeros(2, 12, dtype=torch.long), 0)
