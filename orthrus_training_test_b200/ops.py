@@ -43,6 +43,40 @@ def _require_cuda(*ts):
     return dev
 
 
+def _check_operands(h_s: torch.Tensor, h_t: torch.Tensor, weight: torch.Tensor, mask: Optional[torch.Tensor] = None,
+                    allow_f32: bool = True) -> Tuple[int, int, int]:
+    """``(N, H, V)`` of a consistent problem, or ValueError / TypeError before any device pointer
+    is formed: the kernels read ``N x H`` elements of each view, ``V x H`` of the weight and
+    ``N`` mask bytes, all dense and of one dtype (bf16, or fp32 where ``allow_f32``)."""
+    if h_s.dim() != 2 or weight.dim() != 2 or h_t.shape != h_s.shape or weight.shape[1] != h_s.shape[1]:
+        raise ValueError(f"expected h_s, h_t [N, H] and weight [V, H], got {tuple(h_s.shape)}, {tuple(h_t.shape)} "
+                         f"and {tuple(weight.shape)}")
+    N, H = h_s.shape
+    if mask is not None and mask.numel() != N:
+        raise ValueError(f"mask has {mask.numel()} elements, expected N={N}")
+    dtypes = (torch.bfloat16, torch.float32) if allow_f32 else (torch.bfloat16,)
+    if h_s.dtype not in dtypes or h_t.dtype != h_s.dtype or weight.dtype != h_s.dtype:
+        raise TypeError(f"h_s, h_t and weight must share one dtype of {dtypes}, got {h_s.dtype}, {h_t.dtype}, "
+                        f"{weight.dtype}")
+    if not (h_s.is_contiguous() and h_t.is_contiguous() and weight.is_contiguous()):
+        raise ValueError("h_s, h_t and weight must be contiguous")
+    return N, H, weight.shape[0]
+
+
+def _check_f32(name: str, t: Optional[torch.Tensor], shape: Tuple[int, ...]) -> None:
+    """A dense fp32 buffer of ``shape`` that a kernel reads or writes as such."""
+    if t is None:
+        return
+    if t.dtype != torch.float32 or tuple(t.shape) != tuple(shape) or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous fp32 tensor of shape {tuple(shape)}, got "
+                         f"{t.dtype} {tuple(t.shape)}{'' if t.is_contiguous() else ' (strided)'}")
+
+
+def _check_count(count: Optional[torch.Tensor]) -> None:
+    if count is not None and (count.dtype != torch.float32 or count.numel() != 1):
+        raise ValueError(f"count must be a one-element fp32 tensor, got {count.dtype} {tuple(count.shape)}")
+
+
 def to_fp32(x: torch.Tensor) -> torch.Tensor:
     """fp32, contiguous (bf16 inputs widen exactly): the operands of the fp32-faithful path."""
     x = x.detach()
@@ -111,9 +145,8 @@ def count_valid(mask: torch.Tensor) -> torch.Tensor:
 
 def fwd_stats(h_s: torch.Tensor, h_t: torch.Tensor, weight: torch.Tensor, temperature: float = 1.0) -> torch.Tensor:
     """Pass 1 partial records ``[n_part, 5, N]`` (log2 domain) over ``weight``'s rows."""
+    N, H, V = _check_operands(h_s, h_t, weight, allow_f32=False)
     dev = _require_cuda(h_s, h_t, weight)
-    N, H = h_s.shape
-    V = weight.shape[0]
     n_part = num_partials(N, V)
     parts = torch.empty(n_part, 5, N, dtype=torch.float32, device=dev)
     call("klg_fwd_stats", _ptr(h_s), _ptr(h_t), _ptr(weight), N, H, V, 1.0 / float(temperature), _ptr(parts), n_part,
@@ -123,6 +156,8 @@ def fwd_stats(h_s: torch.Tensor, h_t: torch.Tensor, weight: torch.Tensor, temper
 
 def merge_stats(parts: torch.Tensor) -> torch.Tensor:
     """Online-softmax merge ``[P, 5, N] -> [5, N]``."""
+    if parts.dim() != 3 or parts.shape[1] != 5 or parts.dtype != torch.float32:
+        raise ValueError(f"expected fp32 partial records [P, 5, N], got {parts.dtype} {tuple(parts.shape)}")
     parts = parts.contiguous()
     dev = _require_cuda(parts)
     P, _, N = parts.shape
@@ -135,8 +170,10 @@ def finalize(stats: torch.Tensor, mask: torch.Tensor, count: torch.Tensor,
              want_row_kl: bool = False) -> Tuple[torch.Tensor, torch.Tensor, Optional[torch.Tensor]]:
     """``(loss [] fp32, lse [2, N] log2 domain, row_kl [N] or None)``."""
     m = mask_u8(mask)
+    N = m.numel()
+    _check_f32("stats", stats, (5, N))
+    _check_count(count)
     dev = _require_cuda(stats, m, count)
-    N = stats.shape[1]
     loss = torch.empty((), dtype=torch.float32, device=dev)
     lse = torch.empty(2, N, dtype=torch.float32, device=dev)
     row_kl = torch.empty(N, dtype=torch.float32, device=dev) if want_row_kl else None
@@ -153,12 +190,9 @@ def kl_forward(h_s: torch.Tensor, h_t: torch.Tensor, weight: torch.Tensor, mask:
     Returns ``(loss, lse, count, row_kl)``.
     """
     m = mask_u8(mask)
+    N, H, V = _check_operands(h_s, h_t, weight, m)
+    _check_count(count)
     dev = _require_cuda(h_s, h_t, weight, m)
-    N, H = h_s.shape
-    V = weight.shape[0]
-    if h_t.shape != h_s.shape or weight.shape[1] != H or m.numel() != N:
-        raise ValueError(f"shape mismatch: h_s {tuple(h_s.shape)} h_t {tuple(h_t.shape)} "
-                         f"weight {tuple(weight.shape)} mask {tuple(m.shape)}")
     f32 = h_s.dtype == torch.float32
     ws_bytes = int(_lib.lib().klg_fwd_f32_workspace_bytes(N, H, V) if f32 else _lib.lib().klg_fwd_workspace_bytes(N, V))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
@@ -180,9 +214,10 @@ def kl_backward(h_s, h_t, weight, mask, lse, count, grad: Optional[torch.Tensor]
     ``workspace_bytes`` sizes the dZ chunk (default: the library's choice).
     """
     m = mask_u8(mask)
+    N, H, V = _check_operands(h_s, h_t, weight, m, allow_f32=False)
+    _check_f32("lse", lse, (2, N))
+    _check_count(count)
     dev = _require_cuda(h_s, h_t, weight, m, lse, count)
-    N, H = h_s.shape
-    V = weight.shape[0]
     if workspace_bytes is None:
         workspace_bytes = int(_lib.lib().klg_bwd_workspace_bytes(N, H, V))
     ws = torch.empty(int(workspace_bytes), dtype=torch.uint8, device=dev)
@@ -235,12 +270,9 @@ def kl_fwd_bwd(h_s, h_t, weight, mask, temperature: float = 1.0, count: Optional
     Returns ``(loss, lse, count, row_kl, dH_s fp32 or None, dW fp32 or None)``.
     """
     m = mask_u8(mask)
+    N, H, V = _check_operands(h_s, h_t, weight, m)
+    _check_count(count)
     dev = _require_cuda(h_s, h_t, weight, m)
-    N, H = h_s.shape
-    V = weight.shape[0]
-    if h_t.shape != h_s.shape or weight.shape[1] != H or m.numel() != N:
-        raise ValueError(f"shape mismatch: h_s {tuple(h_s.shape)} h_t {tuple(h_t.shape)} "
-                         f"weight {tuple(weight.shape)} mask {tuple(m.shape)}")
     f32 = h_s.dtype == torch.float32
     if workspace_bytes is None:
         workspace_bytes = int(_lib.lib().klg_fwd_bwd_f32_workspace_bytes(N, H, V) if f32
@@ -276,12 +308,9 @@ def kl_fwd_bwd_xr(h_s, h_t, weight, mask, temperature: float, count: torch.Tenso
     bf16 inputs.  Returns ``(loss of the local rows, dH_s fp32 or None, dW fp32 summed over ranks)``.
     """
     m = mask_u8(mask)
+    N, H, V = _check_operands(h_s, h_t, weight, m, allow_f32=False)
+    _check_count(count)
     dev = _require_cuda(h_s, h_t, weight, m)
-    N, H = h_s.shape
-    V = weight.shape[0]
-    if h_t.shape != h_s.shape or weight.shape[1] != H or m.numel() != N:
-        raise ValueError(f"shape mismatch: h_s {tuple(h_s.shape)} h_t {tuple(h_t.shape)} "
-                         f"weight {tuple(weight.shape)} mask {tuple(m.shape)}")
     if workspace_bytes is None:
         workspace_bytes = int(_lib.lib().klg_fwd_bwd_workspace_bytes(N, H, V))
     ws = torch.empty(int(workspace_bytes), dtype=torch.uint8, device=dev)
@@ -300,9 +329,8 @@ def kl_fwd_bwd_xr(h_s, h_t, weight, mask, temperature: float, count: torch.Tenso
 def lse_record(h_s, h_t, weight, temperature: float = 1.0) -> torch.Tensor:
     """Pass 1 over ``weight``'s rows: the merged ``(m, S)`` record ``[2, 2N]`` (log2 units;
     rows ``0..N-1`` student, ``N..2N-1`` teacher) -- one vocab shard's contribution."""
+    N, H, V = _check_operands(h_s, h_t, weight, allow_f32=False)
     dev = _require_cuda(h_s, h_t, weight)
-    N, H = h_s.shape
-    V = weight.shape[0]
     ws_bytes = int(_lib.lib().klg_lse_workspace_bytes(N, V))
     ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
     rec = torch.empty(2, 2 * N, dtype=torch.float32, device=dev)
@@ -313,6 +341,8 @@ def lse_record(h_s, h_t, weight, temperature: float = 1.0) -> torch.Tensor:
 
 def lse_merge(recs: torch.Tensor) -> torch.Tensor:
     """``[R, 2, 2N]`` records (e.g. gathered from R vocab shards) -> ``lse [2, N]`` (log2 units)."""
+    if recs.dim() != 3 or recs.shape[1] != 2 or recs.shape[2] % 2 != 0 or recs.dtype != torch.float32:
+        raise ValueError(f"expected fp32 records [R, 2, 2N], got {recs.dtype} {tuple(recs.shape)}")
     recs = recs.contiguous()
     dev = _require_cuda(recs)
     R, _, N2 = recs.shape
@@ -328,9 +358,11 @@ def pass2(h_s, h_t, weight, mask, lse, count, grad: Optional[torch.Tensor] = Non
     cross term (log2 units).  ``dh_out`` may supply the dH buffer (e.g. a view into a larger
     buffer that one all-reduce carries)."""
     m = mask_u8(mask)
+    N, H, V = _check_operands(h_s, h_t, weight, m, allow_f32=False)
+    _check_f32("lse", lse, (2, N))
+    _check_f32("dh_out", dh_out, (N, H))
+    _check_count(count)
     dev = _require_cuda(h_s, h_t, weight, m, lse, count)
-    N, H = h_s.shape
-    V = weight.shape[0]
     if workspace_bytes is None:
         workspace_bytes = int(_lib.lib().klg_pass2_workspace_bytes(N, H, V))
     ws = torch.empty(int(workspace_bytes), dtype=torch.uint8, device=dev)
@@ -348,8 +380,12 @@ def pass2(h_s, h_t, weight, mask, lse, count, grad: Optional[torch.Tensor] = Non
 def kl_loss(lse, cross, mask, count, want_row_kl: bool = False):
     """``(loss [] fp32, row_kl [N] or None)`` from complete cross terms."""
     m = mask_u8(mask)
-    dev = _require_cuda(lse, cross, m, count)
     N = m.numel()
+    _check_f32("lse", lse, (2, N))
+    if cross.dtype != torch.float32 or cross.numel() != N:
+        raise ValueError(f"cross must be fp32 with N={N} elements, got {cross.dtype} {tuple(cross.shape)}")
+    _check_count(count)
+    dev = _require_cuda(lse, cross, m, count)
     loss = torch.empty((), dtype=torch.float32, device=dev)
     row_kl = torch.empty(N, dtype=torch.float32, device=dev) if want_row_kl else None
     call("klg_kl_loss", _ptr(lse), _ptr(cross.contiguous()), _ptr(m), N, _ptr(count), _ptr(loss), _ptr(row_kl),

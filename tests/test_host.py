@@ -93,3 +93,58 @@ def test_row_gather_accepts_longer_targets():
         from orthrus_training_test_b200.loss import gather_rows
         gather_rows(torch.zeros(2, 12, 64), torch.zeros(2, 20, 64), torch.zeros(2, 3, dtype=torch.long), 4,
                     torch.zeros(2, 12, dtype=torch.long), 0)
+
+
+def _bf(*shape):
+    return torch.zeros(*shape, dtype=torch.bfloat16)
+
+
+@pytest.mark.parametrize("case", ["h_t rows", "weight H", "mask N", "mixed dtypes", "fp16", "strided h_s", "3-D"])
+def test_ops_reject_inconsistent_operands(case):
+    """The wrappers check shapes, dtypes and density on the host: the kernels read N x H per
+    view, V x H of the weight and N mask bytes of one dtype, so a mismatch would otherwise read
+    past a buffer on the device."""
+    from orthrus_training_test_b200 import ops
+    hs, ht, w, m = _bf(8, 64), _bf(8, 64), _bf(10, 64), torch.ones(8, dtype=torch.bool)
+    if case == "h_t rows":
+        ht = _bf(7, 64)
+    elif case == "weight H":
+        w = _bf(10, 32)
+    elif case == "mask N":
+        m = torch.ones(9, dtype=torch.bool)
+    elif case == "mixed dtypes":
+        hs, ht = hs.float(), ht.float()          # fp32 rows with a bf16 weight
+    elif case == "fp16":
+        hs, ht, w = hs.half(), ht.half(), w.half()
+    elif case == "strided h_s":
+        hs = _bf(8, 128)[:, ::2]
+    elif case == "3-D":
+        hs, ht = _bf(2, 4, 64), _bf(2, 4, 64)
+    with pytest.raises((ValueError, TypeError)):
+        ops.kl_fwd_bwd(hs, ht, w, m)
+    with pytest.raises((ValueError, TypeError)):
+        ops.kl_forward(hs, ht, w, m)
+
+
+def test_ops_pieces_check_their_buffers():
+    from orthrus_training_test_b200 import ops
+    hs, ht, w, m = _bf(8, 64), _bf(8, 64), _bf(10, 64), torch.ones(8, dtype=torch.bool)
+    lse, cnt = torch.zeros(2, 8), torch.ones(1)
+    with pytest.raises(TypeError):               # the vocab-shard pieces are bf16 only
+        ops.lse_record(hs.float(), ht.float(), w.float())
+    with pytest.raises(ValueError):              # lse of another row count
+        ops.pass2(hs, ht, w, m, torch.zeros(2, 7), cnt)
+    with pytest.raises(ValueError):              # dH buffer too small
+        ops.pass2(hs, ht, w, m, lse, cnt, dh_out=torch.zeros(8, 32))
+    with pytest.raises(ValueError):              # count not one fp32 element
+        ops.pass2(hs, ht, w, m, lse, torch.ones(2))
+    with pytest.raises(ValueError):              # cross term of another row count
+        ops.kl_loss(lse, torch.zeros(7), m, cnt)
+    with pytest.raises(ValueError):              # records not [R, 2, 2N]
+        ops.lse_merge(torch.zeros(2, 3, 16))
+    with pytest.raises(ValueError):              # partial records not [P, 5, N]
+        ops.merge_stats(torch.zeros(2, 4, 8))
+    with pytest.raises(ValueError):              # statistics of another row count
+        ops.finalize(torch.zeros(5, 7), m, cnt)
+    with pytest.raises(RuntimeError, match="CUDA"):   # consistent host tensors reach the device check
+        ops.pass2(hs, ht, w, m, lse, cnt)
