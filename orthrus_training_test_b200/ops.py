@@ -444,7 +444,10 @@ def kl_gemm_loss(h_s: torch.Tensor, h_t: torch.Tensor, weight: torch.Tensor, mas
 
 # ----------------------------------------------------------------- final RMSNorm prologue
 
-def _norm_input(x: torch.Tensor) -> Tuple[torch.Tensor, int]:
+def _norm_input(x: torch.Tensor, gamma: torch.Tensor) -> Tuple[torch.Tensor, int]:
+    # the norm kernels read H gamma entries and N x H elements of x
+    if x.dim() != 2 or gamma.numel() != x.shape[-1]:
+        raise ValueError(f"expected x [N, H] and gamma [H], got {tuple(x.shape)} and {tuple(gamma.shape)}")
     x = x.detach()
     _require_cuda(x)
     if x.dtype == torch.bfloat16:
@@ -462,7 +465,7 @@ def rmsnorm_rows(x: torch.Tensor, gamma: torch.Tensor, eps: float = 1e-5,
     rstd fp32 [N] or None)`` with ``y = gamma * bf16(x r)`` (bf16 x) or ``bf16(gamma * x r)``
     (fp32 x), ``r = 1 / sqrt(mean(x^2) + eps)``.
     """
-    xc, f32 = _norm_input(x)
+    xc, f32 = _norm_input(x, gamma)
     dev = xc.device
     N, H = xc.shape
     g = gamma.detach().to(device=dev, dtype=torch.float32).contiguous()
@@ -474,7 +477,11 @@ def rmsnorm_rows(x: torch.Tensor, gamma: torch.Tensor, eps: float = 1e-5,
 
 def rmsnorm_rows_backward(x: torch.Tensor, gamma: torch.Tensor, rstd: torch.Tensor, dy: torch.Tensor) -> torch.Tensor:
     """``dx`` fp32 ``[N, H]`` through the norm for ``dy`` fp32 ``[N, H]`` (weight frozen)."""
-    xc, f32 = _norm_input(x)
+    if tuple(dy.shape) != tuple(x.shape):
+        raise ValueError(f"dy must have x's shape {tuple(x.shape)}, got {tuple(dy.shape)}")
+    if x.dim() == 2:
+        _check_f32("rstd", rstd, (x.shape[0],))
+    xc, f32 = _norm_input(x, gamma)
     dev = xc.device
     N, H = xc.shape
     g = gamma.detach().to(device=dev, dtype=torch.float32).contiguous()

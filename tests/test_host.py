@@ -148,3 +148,18 @@ def test_ops_pieces_check_their_buffers():
         ops.finalize(torch.zeros(5, 7), m, cnt)
     with pytest.raises(RuntimeError, match="CUDA"):   # consistent host tensors reach the device check
         ops.pass2(hs, ht, w, m, lse, cnt)
+
+
+def test_norm_wrappers_check_shapes():
+    from orthrus_training_test_b200 import ops
+    x = torch.zeros(4, 64)
+    with pytest.raises(ValueError):              # gamma of another width
+        ops.rmsnorm_rows(x, torch.ones(32))
+    with pytest.raises(ValueError):              # rows not 2-D
+        ops.rmsnorm_rows(torch.zeros(2, 2, 64), torch.ones(64))
+    with pytest.raises(ValueError):              # dy of another shape
+        ops.rmsnorm_rows_backward(x, torch.ones(64), torch.ones(4), torch.zeros(4, 32))
+    with pytest.raises(ValueError):              # rstd of another row count
+        ops.rmsnorm_rows_backward(x, torch.ones(64), torch.ones(3), torch.zeros(4, 64))
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.rmsnorm_rows(x, torch.ones(64))
