@@ -209,3 +209,41 @@ def test_plain_c_caller_builds_and_links(tmp_path):
     out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     assert out.returncode == 0, (out.returncode, out.stdout, out.stderr)
     assert out.stdout.strip() == "ok 100"
+
+
+_NULL_CALLER = r"""
+import ctypes, json, sys
+sys.path.insert(0, sys.argv[1])
+from orthrus_training_test_b200 import _lib
+L = _lib.lib()
+out = {}
+for name in sys.argv[2:]:
+    res, args = _lib.SIGNATURES[name]
+    vals = [0.0 if a is ctypes.c_float else
+            0 if a in (ctypes.c_int, ctypes.c_int64, ctypes.c_longlong, ctypes.c_uint32, ctypes.c_ulonglong) else None
+            for a in args]
+    out[name] = getattr(L, name)(*vals)
+print(json.dumps(out))
+"""
+
+
+def test_every_entry_point_rejects_null_arguments():
+    """Every status-returning entry point, called with null pointers and zero sizes, answers
+    KLG_ERR_ARG from its own checks -- no dereference, no device work (run in a child process,
+    so that a crash would fail this test instead of the session)."""
+    import json
+    import subprocess
+    import sys
+    # not applicable: no pointer arguments (version, error text, SM reserve, trace start,
+    # split count), a release of nothing (klg_xr_close(NULL) is a no-op), a read of an empty
+    # trace, and the self-test whose one argument is a stream and which needs a GPU
+    exempt = {"klg_version", "klg_last_error", "klg_set_sm_reserve", "klg_trace_begin", "klg_block_attn_splits",
+              "klg_xr_close", "klg_trace_end", "klg_selftest_wait_timeout"}
+    names = [n for n, (res, _) in _lib.SIGNATURES.items() if res is ctypes.c_int and n not in exempt]
+    assert len(names) >= 30
+    out = subprocess.run([sys.executable, "-c", _NULL_CALLER, str(ROOT), *names], capture_output=True, text=True,
+                         timeout=300)
+    assert out.returncode == 0, out.stderr[-2000:]
+    rcs = json.loads(out.stdout.strip().splitlines()[-1])
+    bad = {n: rc for n, rc in rcs.items() if rc != _lib.KLG_ERR_ARG}
+    assert not bad, bad
