@@ -16,7 +16,7 @@
  *
  * Conventions
  *   - Inputs h_s, h_t [N, H] and W [V, H] are bf16, row-major, 16-byte aligned,
- *     H a multiple of 8.  (fp32 callers use the *_f32 entry points, which keep fp32
+ *     H a multiple of 8 and at least 64.  (fp32 callers use the *_f32 entry points, which keep fp32
  *     fidelity, or round with klg_cast_f32_bf16.)
  *   - mask [N] is uint8 (nonzero = row carries loss), the reference's
  *     target != pad_token_id (train.py:163-164).

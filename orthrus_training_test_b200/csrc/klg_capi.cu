@@ -635,6 +635,9 @@ int check_problem(const void* hs, const void* ht, const void* w, int64_t n_rows,
     return fail(KLG_ERR_ARG, "shape too large N=%lld H=%lld V=%lld", (long long)n_rows, (long long)hidden,
                 (long long)vocab);
   if (hidden % 8 != 0) return fail(KLG_ERR_ALIGN, "hidden=%lld must be a multiple of 8", (long long)hidden);
+  // the tensor-core kernels load 64-column k-blocks; hidden sizes below one k-block (narrower
+  // rows than the TMA box) are outside what they are built and tested for
+  if (hidden < 64) return fail(KLG_ERR_ARG, "hidden=%lld: the lm_head kernels need hidden >= 64", (long long)hidden);
   if (!aligned16(hs) || !aligned16(ht) || !aligned16(w)) return fail(KLG_ERR_ALIGN, "inputs must be 16-byte aligned");
   if (!(inv_temp > 0.f) || !std::isfinite(inv_temp)) return fail(KLG_ERR_ARG, "inv_temp must be finite and > 0");
   return KLG_OK;

@@ -47,6 +47,11 @@ def test_argument_validation_codes():
     _, odd = _buf(1 << 16, offset=4)
     # hidden not a multiple of 8 -> alignment error
     assert L.klg_fwd_stats(p, p, p, 4, 12, 4, 1.0, p, 1, None) == _lib.KLG_ERR_ALIGN
+    # hidden below one 64-column k-block -> rejected, on every lm_head entry point
+    assert L.klg_fwd_stats(p, p, p, 4, 56, 4, 1.0, p, 1, None) == _lib.KLG_ERR_ARG
+    assert "hidden >= 64" in _lib.last_error()
+    assert L.klg_fwd_bwd(p, p, p, p, 4, 32, 4, 1.0, 0, p, None, p, p, None, p, p, p, 1 << 16, None) == _lib.KLG_ERR_ARG
+    assert L.klg_lm_head_sample(p, p, 4, 8, 4, 1.0, 0, 0, p, p, p, p, 1 << 16, None) == _lib.KLG_ERR_ARG
     # misaligned input pointer
     assert L.klg_fwd_stats(odd, p, p, 4, 64, 4, 1.0, p, 1, None) == _lib.KLG_ERR_ALIGN
     # bad shapes / temperature
