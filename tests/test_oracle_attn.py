@@ -46,3 +46,31 @@ def test_block_attention_backward_oracle_matches_reference_mask():
     dq, dks, dvs = O.block_attention_bwd_np(*args, g["d_out"])
     for ours, ref in ((dq, g["dq"]), (dks, g["dk_self"]), (dvs, g["dv_self"])):
         np.testing.assert_allclose(ours, ref, rtol=1e-9, atol=1e-11)
+
+
+def test_block_attention_backward_matches_finite_differences():
+    """The closed-form backward is the derivative of the forward (float64 central differences
+    of sum(out * d_out)) for queries and the blocks' own keys and values, with GQA and limits
+    from none to past the cache end."""
+    rng = np.random.default_rng(3)
+    B, H, Hkv, K, Ld, D, AL = 1, 4, 2, 2, 6, 8, 5
+    q = rng.normal(size=(B, H, Ld, D))
+    ks, vs = rng.normal(size=(B, Hkv, Ld, D)), rng.normal(size=(B, Hkv, Ld, D))
+    ka, va = rng.normal(size=(B, Hkv, AL, D)), rng.normal(size=(B, Hkv, AL, D))
+    lim = np.array([[-1, 0, 2, 3, 4, 99]])
+    d_out = rng.normal(size=(B, H, Ld, D))
+    dq, dks, dvs = O.block_attention_bwd_np(q, ks, vs, ka, va, lim, K, d_out)
+    eps = 1e-6
+
+    def f(q_, ks_, vs_):
+        return float((O.block_attention_np(q_, ks_, vs_, ka, va, lim, K)[0] * d_out).sum())
+
+    for which, grad in (("q", dq), ("ks", dks), ("vs", dvs)):
+        for idx in [(0, 0, 0, 0), (0, 1, 3, 5), (0, 1, 5, 7), (0, 0, 2, 1)]:
+            args = {"q": q, "ks": ks, "vs": vs}
+            a = {k: v.copy() for k, v in args.items()}
+            b = {k: v.copy() for k, v in args.items()}
+            a[which][idx] += eps
+            b[which][idx] -= eps
+            fd = (f(a["q"], a["ks"], a["vs"]) - f(b["q"], b["ks"], b["vs"])) / (2 * eps)
+            assert abs(fd - grad[idx]) <= 1e-7 + 1e-6 * abs(grad[idx]), (which, idx, fd, grad[idx])
