@@ -75,7 +75,7 @@ def _check_selection_shapes(diff_hidden, ar_hidden_states, anchor_positions, K, 
     if anchor_positions.dim() != 2 or anchor_positions.shape[0] != B:
         raise ValueError(f"anchor_positions must be [B={B}, B_blocks], got {tuple(anchor_positions.shape)}")
     Bb = anchor_positions.shape[1]
-    if Bb < 1 or P != Bb * K:
+    if P != Bb * K:
         raise ValueError(f"diff_hidden has {P} positions, expected B_blocks*K = {Bb * K}")
     if target_ids.dim() != 2 or target_ids.shape[0] != B or target_ids.shape[1] < P:
         raise ValueError(f"target_ids must be [B={B}, >= {P}], got {tuple(target_ids.shape)}")
@@ -108,8 +108,9 @@ class GatherRowsFn(torch.autograd.Function):
         h_s = torch.empty(n, H, dtype=diff.dtype, device=dev)
         h_t = torch.empty(n, H, dtype=diff.dtype, device=dev)
         valid = torch.empty(n, dtype=torch.uint8, device=dev)
-        call("klg_gather_rows", _ptr(diff), _ptr(ar), _ptr(anchors), _ptr(targets), B, Bb, K, ar.shape[1], row_bytes,
-             int(pad_token_id), _ptr(h_s), _ptr(h_t), _ptr(valid), _stream(dev))
+        if n > 0:   # no blocks (or no sequences): nothing selected, as the reference's empty index tensors
+            call("klg_gather_rows", _ptr(diff), _ptr(ar), _ptr(anchors), _ptr(targets), B, Bb, K, ar.shape[1],
+                 row_bytes, int(pad_token_id), _ptr(h_s), _ptr(h_t), _ptr(valid), _stream(dev))
         ctx.meta = (B, Bb, K, H, diff.dtype, row_bytes)
         ctx.mark_non_differentiable(h_t, valid)
         return h_s, h_t, valid
@@ -119,7 +120,8 @@ class GatherRowsFn(torch.autograd.Function):
         B, Bb, K, H, dtype, row_bytes = ctx.meta
         g = g_hs.detach().to(dtype).contiguous()
         d_diff = torch.empty(B, Bb * K, H, dtype=dtype, device=g.device)
-        call("klg_scatter_rows_grad", _ptr(g), B, Bb, K, row_bytes, _ptr(d_diff), _stream(g.device))
+        if d_diff.numel() > 0:
+            call("klg_scatter_rows_grad", _ptr(g), B, Bb, K, row_bytes, _ptr(d_diff), _stream(g.device))
         return d_diff, None, None, None, None, None
 
 

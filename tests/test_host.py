@@ -83,6 +83,13 @@ def test_row_gather_rejects_bad_shapes(diff, ar, anc, K, tgt):
                     torch.zeros(tgt, dtype=torch.long), 0)
 
 
+def test_row_gather_accepts_no_blocks():
+    """Zero blocks pass the shape check (the reference returns a zero loss for them)."""
+    from orthrus_training_test_b200.loss import _check_selection_shapes
+    assert _check_selection_shapes(torch.zeros(2, 0, 64), torch.zeros(2, 20, 64), torch.zeros(2, 0), 4,
+                                   torch.zeros(2, 0)) == (2, 0, 64, 20, 0)
+
+
 def test_row_gather_accepts_longer_targets():
     """target_ids wider than the diffusion positions pass the shape check (only the first
     B_blocks*K positions are read, as train.py:163 indexes them)."""
